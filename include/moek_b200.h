@@ -1,0 +1,99 @@
+/* moek_b200: routed-expert NVFP4-weight / bf16-activation (W4A16) MoE kernels for NVIDIA B200 (sm_100a).
+ *
+ * C ABI of libmoek_b200.so. Every function takes plain device pointers, element counts and a cudaStream_t (as
+ * void*), launches asynchronously on that stream and returns MOEK_OK or an error code; moek_last_error() returns the
+ * calling thread's last message. The caller allocates every buffer (the library allocates nothing). Reference paths
+ * are relative to the Alssndr0/qwen38-flash-coder project; "vllm/..." paths point into vLLM's Python sources.
+ *
+ * Tensor formats (produced at load time by qwen38_flash_coder_b200.prep):
+ *   W    int32 [E, K/16, 2N], this build's tiled layout: per (expert, 256-column item, 64-k stage) 8 KB of E2M1
+ *        codes (same bytes as the checkpoint's [E, N, K/2], reordered).
+ *   SP   uint8 [E, N/256, K/128, 1056]: the kit's packed E4M3 block scales, tiled per item (files/mbx_moek.py:61-172).
+ *   exc_off int32 [E * N/256 * K/128 + 1], exc_ent int32 [>= 1]: the packed format's exception lists.
+ *   G    fp32 [E]: weight_scale_2 * 2^119 / scale_factor (vllm/.../marlin_utils_fp4.py:134-146,385-386).
+ */
+#ifndef MOEK_B200_H
+#define MOEK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MOEK_OK = 0,
+  MOEK_ERR_ARG = 1,         /* bad argument (shape, size, null pointer): nothing was launched */
+  MOEK_ERR_CUDA = 2,        /* a CUDA call failed; the message names it */
+  MOEK_ERR_UNSUPPORTED = 3  /* a valid request this build does not implement */
+};
+
+/* Device-side error codes written to the error word (cnt[0] of moek_gemm); 0 means none. */
+enum { MOEK_DEV_TIMEOUT = 1, MOEK_DEV_BAD_EXPERT = 2, MOEK_DEV_TOO_MANY_ROWS = 3 };
+
+/* Last error message of the calling thread (empty if none). No reference counterpart (the reference raised
+ * c10::Error from TORCH_CHECK, files/mbx_moek.cu:727-755). */
+const char* moek_last_error(void);
+
+/* ABI version of this header (1). */
+int moek_version(void);
+
+/* Bound on every device-side wait (default 2 s). After it a kernel records MOEK_DEV_TIMEOUT and returns instead of
+ * hanging. No reference counterpart (its waits are unbounded, files/mbx_moek.cu:87-93). */
+int moek_set_wait_timeout_ns(uint64_t ns);
+
+/* Workspace moek_align needs for numel indices (0 when numel <= 1024). */
+int moek_align_workspace_bytes(int64_t numel, int32_t num_experts, size_t* bytes);
+
+/* moe_align: replaces vLLM's torch.ops._moe_C.moe_align_block_size as the kit calls it
+ * (vllm/model_executor/layers/fused_moe/moe_align_block_size.py:11-103 via vllm/_custom_ops.py:2247-2265; called at
+ * files/mbx_moek.py:266 with ignore_invalid_experts=True, expert_map=None).
+ * topk_ids int32 [numel] (flattened [M, top_k]) -> sorted_ids int32 [sorted_len >= numel + E*(bs-1), or
+ * min(numel*bs, that) when numel < E], expert_ids int32 [expert_len >= ceil(sorted_len/bs)], num_post_pad int32 [1].
+ * Indices grouped by expert in ascending expert order, ascending inside an expert, each expert padded to a multiple
+ * of block_size with the sentinel numel (also in every entry past num_post_pad); expert_ids is -1 past the last
+ * block; ids outside [0, E) are skipped. workspace: moek_align_workspace_bytes() bytes (may be NULL when 0). */
+int moek_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size, int32_t* sorted_ids,
+               int64_t sorted_len, int32_t* expert_ids, int64_t expert_len, int32_t* num_post_pad, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* Grouped GEMM of one routed-expert matrix: replaces the kit's moe_gemm (pybind, files/mbx_moek.cu:714-795) with the
+ * same fields: A, W, S, G, sorted_ids, expert_ids, num_post_pad, topk_w, out, top_k, gate_up, SP, exc_off, exc_ent,
+ * cnt, mode, nsplit, part, tiled (the reference's stream-k ws and schedule order have no use here).
+ *   A       bf16: gate_up: hidden states [M, K] (row id / top_k); down: act [num_ids, K] (row id, top_k = 1).
+ *   S       must be NULL (plain Marlin scales go with Marlin's untiled weight layout, which this build does not use);
+ *           tiled must be 1.
+ *   mode    2: split-k; the kernel writes fp32 partial sums part[nsplit][num_ids][N] (gate_up: gate at column c, up
+ *           at N/2 + c) and moek_split_epilogue finishes. (The reference's modes 0/1 are not available.)
+ *   nsplit  K/64/nsplit must be even (whole packed-scale runs).
+ *   cnt     int32 [>= 4]; cnt[0] is the device error word (MOEK_DEV_*), left as is when nothing goes wrong.
+ *   block_m the block size moek_align used; max_rows >= the most valid rows of any block (min(M, block_m) for top-k
+ *           routing with distinct experts per token), <= 96.
+ * The weights are dequantised exactly as the fp32 oracle does (bench/moek/problem.py:31-38: bf16(e2m1 * s * gs)),
+ * products summed in fp32. topk_w and out are unused in mode 2 (kept for the reference's argument list). */
+int moek_gemm(const void* A, const void* W, const void* S, const float* G, const int32_t* sorted_ids,
+              int64_t sorted_len, const int32_t* expert_ids, const int32_t* num_post_pad, const float* topk_w,
+              void* out, int32_t num_ids, int32_t N, int32_t K, int32_t E, int32_t top_k, int32_t gate_up,
+              const uint8_t* SP, const int32_t* exc_off, const int32_t* exc_ent, int32_t* cnt, int64_t cnt_len,
+              int32_t mode, int32_t nsplit, float* part, int64_t part_len, int32_t tiled, int32_t block_m,
+              int32_t max_rows, void* stream);
+
+/* Split-k epilogue: replaces the kit's moe_split_epilogue (files/mbx_moek.cu:797-851). Adds the nsplit partials in
+ * split order (deterministic), then
+ *   gate_up: out = act bf16 [num_ids, N/2] = bf16(silu(g) * u) with g, u the fp32 sums (the oracle's rounding point,
+ *            bench/moek/problem.py:63-65);
+ *   down, out_kind 1: out = fp32 rows [num_ids, N] = topk_w[id] * sum;
+ *   down, out_kind 2: out = bf16 [num_ids/top_k, N] = bf16(sum_j topk_w * sum) over the top_k slots of each token in
+ *            slot order: the down epilogue fused with the top-k combine (files/mbx_moek.py:284-289). */
+int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int32_t N, int32_t gate_up,
+                        const float* topk_w, int32_t top_k, void* out, int32_t out_kind, void* stream);
+
+/* Top-k combine: replaces torch.sum(dout.view(-1, top_k, N), 1, out=output) / vLLM's moe_sum (files/mbx_moek.py:
+ * 284-289): out bf16 [m, N] = bf16(sum_j rows[t*top_k + j]) in fp32, slot order. rows: fp32 if rows_fp32 else bf16. */
+int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int32_t N, int32_t top_k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOEK_B200_H */

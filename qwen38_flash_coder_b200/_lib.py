@@ -1,0 +1,46 @@
+"""ctypes binding of libmoek_b200.so (include/moek_b200.h). Loading fails loudly: there is no fallback path."""
+import ctypes
+import os
+
+from .build import LIB
+
+_P, _I32, _I64, _U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64
+
+SIGNATURES = {
+    "moek_last_error": (ctypes.c_char_p, []),
+    "moek_version": (ctypes.c_int, []),
+    "moek_set_wait_timeout_ns": (ctypes.c_int, [_U64]),
+    "moek_align_workspace_bytes": (ctypes.c_int, [_I64, _I32, ctypes.POINTER(ctypes.c_size_t)]),
+    "moek_align": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P, ctypes.c_size_t, _P]),
+    "moek_gemm": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
+                                 _P, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _I32, _I32, _I32, _P]),
+    "moek_split_epilogue": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P]),
+    "moek_combine": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _P]),
+}
+
+_lib = None
+
+
+class MoekError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            raise ImportError(f"moek_b200: {LIB} is missing; build it with `python -m qwen38_flash_coder_b200.build`"
+                              " (nvcc, sm_100a). There is no fallback implementation.")
+        h = ctypes.CDLL(LIB)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(h, name)
+            f.restype, f.argtypes = res, args
+        _lib = h
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    rc = getattr(lib(), name)(*args)
+    if rc:
+        msg = lib().moek_last_error().decode(errors="replace")
+        raise MoekError(f"{name} failed ({rc}): {msg}")

@@ -1,0 +1,181 @@
+// C ABI of the routed-expert MoE kernels: plain pointers, sizes and a cudaStream_t, an int status (0 = ok) and a
+// thread-local message behind moek_last_error(). Declared in include/moek_b200.h (each entry point's comment names
+// the reference interface it replaces).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+
+#include "moek_common.cuh"
+#include "moek_kernels.cuh"
+
+#define MOEK_API extern "C" __attribute__((visibility("default")))
+
+enum { MOEK_OK = 0, MOEK_ERR_ARG = 1, MOEK_ERR_CUDA = 2, MOEK_ERR_UNSUPPORTED = 3 };
+
+static thread_local char g_msg[512];
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+static int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MOEK_OK;
+  return fail(MOEK_ERR_CUDA, "moek_b200: %s: %s", what, cudaGetErrorString(e));
+}
+
+static int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (!v) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+static uint64_t g_timeout_ns = 2000000000ull;  // 2 s bound on every device-side wait
+
+MOEK_API const char* moek_last_error(void) { return g_msg; }
+
+MOEK_API int moek_version(void) { return 1; }
+
+MOEK_API int moek_set_wait_timeout_ns(uint64_t ns) {
+  if (ns == 0) return fail(MOEK_ERR_ARG, "moek_b200: the wait timeout must be positive");
+  g_timeout_ns = ns;
+  return MOEK_OK;
+}
+
+MOEK_API int moek_align_workspace_bytes(int64_t numel, int32_t num_experts, size_t* bytes) {
+  if (!bytes || numel < 0 || num_experts <= 0) return fail(MOEK_ERR_ARG, "moek_b200: bad align workspace query");
+  *bytes = moek::align_workspace_bytes(numel, num_experts);
+  return MOEK_OK;
+}
+
+MOEK_API int moek_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
+                        int32_t* sorted_ids, int64_t sorted_len, int32_t* expert_ids, int64_t expert_len,
+                        int32_t* num_post_pad, void* workspace, size_t workspace_bytes, void* stream) {
+  if (numel < 0 || num_experts <= 0 || block_size <= 0)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_align needs numel >= 0, num_experts > 0, block_size > 0");
+  if (moek::align_smem_one(num_experts) > 220 * 1024)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_align supports up to 1600 experts (got %d)", num_experts);
+  int64_t need = numel + (int64_t)num_experts * (block_size - 1);
+  if (numel < num_experts) need = std::min<int64_t>(need, numel * block_size);
+  if (sorted_len < need || expert_len < (need + block_size - 1) / block_size)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_align outputs too small (sorted %lld < %lld or expert_ids %lld)",
+                (long long)sorted_len, (long long)need, (long long)expert_len);
+  if (numel > INT32_MAX / 2) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_align numel too large");
+  if (!sorted_ids || !expert_ids || !num_post_pad || (numel && !topk_ids))
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_align null pointer");
+  const size_t ws = moek::align_workspace_bytes(numel, num_experts);
+  if (ws > workspace_bytes || (ws && !workspace))
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_align needs %zu workspace bytes for %lld indices", ws, (long long)numel);
+  return cuda_status(moek::launch_align(topk_ids, numel, num_experts, block_size, sorted_ids, sorted_len, expert_ids,
+                                        expert_len, num_post_pad, workspace, (cudaStream_t)stream),
+                     "moe_align launch");
+}
+
+MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float* G, const int32_t* sorted_ids,
+                       int64_t sorted_len, const int32_t* expert_ids, const int32_t* num_post_pad,
+                       const float* topk_w, void* out, int32_t num_ids, int32_t N, int32_t K, int32_t E,
+                       int32_t top_k, int32_t gate_up, const uint8_t* SP, const int32_t* exc_off,
+                       const int32_t* exc_ent, int32_t* cnt, int64_t cnt_len, int32_t mode, int32_t nsplit,
+                       float* part, int64_t part_len, int32_t tiled, int32_t block_m, int32_t max_rows,
+                       void* stream) {
+  (void)topk_w;
+  (void)out;
+  if (num_ids == 0) return MOEK_OK;  // empty batch
+  if (num_ids < 0 || N <= 0 || K <= 0 || E <= 0 || block_m <= 0)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm bad sizes (num_ids %d, N %d, K %d, E %d, block %d)", num_ids, N,
+                K, E, block_m);
+  if (K % 128 || N % 256 || (gate_up && (N / 2) % 128))
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm needs K %% 128 == 0 and N %% 256 == 0 (got N %d, K %d)", N, K);
+  if (S) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: plain (unpacked) scales are not supported; pass packed SP");
+  if (!tiled) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: weights must be in moek_b200's tiled layout");
+  if (!A || !W || !G || !sorted_ids || !expert_ids || !num_post_pad || !SP || !exc_off || !exc_ent)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm null pointer");
+  if (!gate_up && top_k != 1) return fail(MOEK_ERR_ARG, "moek_b200: down reads one activation row per id (top_k 1)");
+  if (top_k <= 0) return fail(MOEK_ERR_ARG, "moek_b200: top_k must be positive");
+  if (mode != 2) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build", mode);
+  const int nstage = K / moek::BK;
+  if (nsplit < 1 || nstage % nsplit || (nstage / nsplit) % moek::STAGES_PER_RUN)
+    return fail(MOEK_ERR_ARG, "moek_b200: nsplit %d must cut K/128 = %d into whole runs", nsplit, K / 128);
+  if (!part || part_len < (int64_t)nsplit * num_ids * N)
+    return fail(MOEK_ERR_ARG, "moek_b200: split partials need %lld floats", (long long)nsplit * num_ids * N);
+  if (max_rows <= 0 || max_rows > 96)
+    return fail(MOEK_ERR_ARG, "moek_b200: max_rows %d must be in [1, 96]", max_rows);
+  if (!cnt || cnt_len < 4) return fail(MOEK_ERR_ARG, "moek_b200: cnt must hold >= 4 int32 (error word at cnt[0])");
+  const int64_t maxb = std::min<int64_t>(sorted_len / block_m, (num_ids + block_m - 1) / block_m +
+                                                                   std::min<int64_t>(E, num_ids));
+  moek::GemmParams p{};
+  p.A = static_cast<const __nv_bfloat16*>(A);
+  p.W = static_cast<const uint8_t*>(W);
+  p.G = G;
+  p.sorted_ids = sorted_ids;
+  p.expert_ids = expert_ids;
+  p.num_post_pad = num_post_pad;
+  p.SP = SP;
+  p.exc_off = exc_off;
+  p.exc_ent = reinterpret_cast<const uint32_t*>(exc_ent);
+  p.part = part;
+  p.err = cnt;
+  p.timeout_ns = g_timeout_ns;
+  p.num_ids = num_ids;
+  p.N = N;
+  p.K = K;
+  p.E = E;
+  p.a_div = top_k;
+  p.block_m = block_m;
+  p.nsplit = nsplit;
+  p.max_blocks = (int)maxb;
+  p.gate_up = gate_up ? 1 : 0;
+  return cuda_status(moek::launch_decode(p, max_rows, sm_count(), (cudaStream_t)stream), "moe_gemm launch");
+}
+
+MOEK_API int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int32_t N, int32_t gate_up,
+                                 const float* topk_w, int32_t top_k, void* out, int32_t out_kind, void* stream) {
+  if (num_ids == 0) return MOEK_OK;
+  if (!part || !out || nsplit < 1 || num_ids < 0 || N <= 0 || (N & 1))
+    return fail(MOEK_ERR_ARG, "moek_b200: split epilogue bad arguments");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (gate_up) {
+    return cuda_status(moek::launch_gate_epilogue(part, nsplit, num_ids, N, static_cast<__nv_bfloat16*>(out), st),
+                       "gate epilogue");
+  }
+  if (!topk_w) return fail(MOEK_ERR_ARG, "moek_b200: down epilogue needs the router weights");
+  switch (out_kind) {
+    case 1:
+      return cuda_status(moek::launch_down_rows(part, nsplit, num_ids, N, topk_w, static_cast<float*>(out), st),
+                         "down rows epilogue");
+    case 2:
+      if (top_k <= 0 || num_ids % top_k) return fail(MOEK_ERR_ARG, "moek_b200: num_ids must be a multiple of top_k");
+      return cuda_status(moek::launch_down_combine(part, nsplit, num_ids, N, top_k, topk_w,
+                                                   static_cast<__nv_bfloat16*>(out), st),
+                         "down combine epilogue");
+    default:
+      return fail(MOEK_ERR_ARG, "moek_b200: down out_kind %d (1 = fp32 rows, 2 = combined)", out_kind);
+  }
+}
+
+MOEK_API int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int32_t N, int32_t top_k,
+                          void* stream) {
+  if (m == 0) return MOEK_OK;
+  if (!rows || !out || m < 0 || N <= 0 || top_k <= 0) return fail(MOEK_ERR_ARG, "moek_b200: combine bad arguments");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (rows_fp32)
+    return cuda_status(moek::launch_combine_f32(static_cast<const float*>(rows), m, N, top_k,
+                                                static_cast<__nv_bfloat16*>(out), st),
+                       "combine");
+  return cuda_status(moek::launch_combine_bf16(static_cast<const __nv_bfloat16*>(rows), m, N, top_k,
+                                               static_cast<__nv_bfloat16*>(out), st),
+                     "combine");
+}

@@ -1,0 +1,161 @@
+// Shared device helpers for the routed-expert NVFP4 (W4A16) MoE kernels (sm_100a).
+//
+// Weight decode. A tiled weight word holds 8 E2M1 codes (sign in bit 3) of 8 consecutive k of one output column;
+// code i sits in nibble NIBBLE_OF[i] = {3, 7, 2, 6, 1, 5, 0, 4}, so that step d of the decode (word shifted left by
+// 4d) finds codes 2d and 2d + 1 at bits 12-15 and 28-31. Moving a code's sign to bit 15 and its three magnitude bits
+// to bits 8..6 of a bf16 gives exactly e2m1 * 2^-126 (exponent field = the code's exponent, top mantissa bit = its
+// mantissa bit; code 1 becomes the subnormal 2^-127). That value D is exact, and the weight the reference's oracle
+// uses, bf16(e2m1 * s * gs) with s the E4M3 block scale and gs the expert's fp32 global scale
+// (bench/moek/problem.py:31-38), is then rebuilt per pair of codes with two bf16 FMAs:
+//     Y  = fp32(s * gs) * 2^126            (once per 16 weights, from the packed scale byte and the global scale)
+//     B  = bf16(Y), R = bf16(Y - B)         (B carries 8 bits of Y, R the next 8)
+//     w  = bf16(D * B + bf16(D * R))        (D * B is exact inside the FMA; one rounding of the sum)
+// which equals bf16(e2m1 * fp32(s * gs)) except when e2m1 * Y lies within 2^-18 (relative) of a bf16 rounding
+// midpoint (about 1 weight in 2000 then differs by one bf16 ulp).
+//
+// Scale bytes. The kit's packed scales hold vLLM's Marlin "S0E5M3" bytes: the high byte of (fp16(s * sf * 2^7) << 1)
+// (vllm/.../marlin_utils_fp4.py:53-114), 0 for values below 2. As fp32: bits = (b << 20) + (112 << 23) for b != 0.
+// The global scale the kernels receive is G = gs * 2^119 / sf (marlin_utils_fp4.py:134-146,385-386), so
+// fp32(S0E5M3(b) * G) = fp32(s * gs) * 2^126 exactly: Y needs one multiply.
+//
+// Waits. Every spin (mbarrier phase) is bounded by a %globaltimer deadline; on expiry the waiting thread records
+// MOEK_DEV_TIMEOUT in the caller's error word and the kernel winds down instead of hanging the GPU.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moek {
+
+constexpr int BK = 64;                       // k per pipeline stage
+constexpr int ITEM_COLS = 256;               // output columns (weight rows) per item
+constexpr int STAGE_BYTES = BK * ITEM_COLS / 2;  // 8 KB of packed codes per (item, stage)
+constexpr int KG = 8;                        // k-groups of 16 per packed-scale run
+constexpr int RUN_BYTES = 16 + KG * 64;      // 528
+constexpr int PAIR_BYTES = 2 * RUN_BYTES;    // an item's two runs
+constexpr int STAGES_PER_RUN = KG * 16 / BK; // 2
+
+// Device error codes (the caller's error word; 0 = fine)
+constexpr int MOEK_DEV_TIMEOUT = 1;
+constexpr int MOEK_DEV_BAD_EXPERT = 2;
+constexpr int MOEK_DEV_TOO_MANY_ROWS = 3;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void report(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ---------------------------------------------------------------------------------------------------- mbarriers
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, int bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity. Returns false (after reporting) once the deadline passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err) {
+  if (mbar_try(bar, parity)) return true;
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0 && globaltimer() > deadline) {
+      report(err, MOEK_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ bulk copies
+// Non-tensor bulk copy global -> this CTA's shared memory, completion counted on an mbarrier (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// -------------------------------------------------------------------------------------------------- decoding
+// Pair d of a tiled word, after the word was shifted left by 4d: bf16x2 of e2m1 * 2^-126 for codes 2d, 2d+1.
+__device__ __forceinline__ uint32_t fp4_pair(uint32_t q) {
+  return (q & 0x80008000u) | ((q >> 6) & 0x01C001C0u);
+}
+// S0E5M3 byte -> fp32 value (s * sf * 2^7)
+__device__ __forceinline__ float s0e5m3_to_f32(uint32_t b) {
+  return __uint_as_float(b ? (b << 20) + (112u << 23) : 0u);
+}
+// Per-scale constants: B and R of the module comment, each broadcast to both halves of a bf16x2.
+struct ScaleBR {
+  uint32_t b2, r2;
+};
+__device__ __forceinline__ ScaleBR scale_br(uint32_t byte, float g) {
+  const float y = s0e5m3_to_f32(byte) * g;
+  const __nv_bfloat16 b = __float2bfloat16_rn(y);
+  const __nv_bfloat16 r = __float2bfloat16_rn(y - __bfloat162float(b));
+  const uint32_t bu = __bfloat16_as_ushort(b), ru = __bfloat16_as_ushort(r);
+  return {bu | (bu << 16), ru | (ru << 16)};
+}
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// The oracle's bf16 weights for the 8 codes of one word: out[d] = bf16x2 of codes 2d, 2d + 1.
+__device__ __forceinline__ void dequant_word(uint32_t q, const ScaleBR& s, uint32_t* out) {
+#pragma unroll
+  for (int d = 0; d < 4; d++) {
+    const uint32_t dv = fp4_pair(q << (4 * d));
+    out[d] = bf2_fma(dv, s.b2, bf2_mul(dv, s.r2));
+  }
+}
+
+// Processed position (within its 128-position run) of item slot s: vLLM's scale_perm (new 8i + j <- old i + 8j)
+// followed by the [0, 2, 1, 3] swap of every 4, inverted (vllm/.../marlin_utils.py:296-316,
+// marlin_utils_fp4.py:91-93).
+__device__ __forceinline__ int slot_position(int s) {
+  const int c = s & 63;
+  const int m = 8 * (c & 7) + (c >> 3);
+  const int r = m & 3;
+  return (s & 64) | (m & ~3) | (r == 1 ? 2 : r == 2 ? 1 : r);
+}
+// Logical slot offset (within its 64-column group) held at processed position p (the forward permutation).
+__device__ __forceinline__ int position_slot(int p) {
+  const int q = p & 63;
+  const int r = q & 3;
+  const int m = (q & ~3) | (r == 1 ? 2 : r == 2 ? 1 : r);
+  return (p & 64) | ((m >> 3) + 8 * (m & 7));
+}
+// S0E5M3 byte of run position p, k-group kg (0..7) from a 528-byte packed run (exceptions not applied).
+__device__ __forceinline__ uint32_t run_byte(const uint8_t* run, int p, int kg) {
+  const uint32_t base = run[p >> 3];
+  const uint32_t nb = run[16 + kg * 64 + (p >> 3) * 4 + (p & 3)];
+  return base + ((p & 4) ? (nb >> 4) : (nb & 15));
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+}  // namespace moek

@@ -1,0 +1,406 @@
+// Decode-regime W4A16 grouped GEMM (gate_up and down of the routed experts) for sm_100a, plus its split-k
+// epilogues and the top-k combine.
+//
+// The reference's kernel (files/mbx_moek.cu:665-712, mode 2 for batches of <= 16 tokens) does the same job; this one
+// is written for B200 from the weight stream outwards:
+//
+//   unit      = (moe_align block, 256-column item, k-split). Units are dealt round-robin to the CTAs in
+//               (block, item, split) order, so neighbouring CTAs stream the splits of one expert's item at once and
+//               every SM keeps a stream going however few experts the batch touches.
+//   producer  = warp 8. Per 64-k stage it bulk-copies (cp.async.bulk, no multicast) the stage's 8 KB of packed codes,
+//               the item's 1056-byte packed-scale run pair and the block's activation rows (one 128-byte copy per
+//               valid row, gathered through sorted_ids) into a ring slot, all counted on the slot's mbarrier.
+//   consumers = warps 0-7. Warp w owns 32 of the item's 256 weight rows (gate_up: 16 gate rows and the matching 16 up
+//               rows, so SwiGLU pairs stay in one thread). Per stage a lane decodes its 2 x 16 bytes of codes plus
+//               the two scales its k-group needs into the oracle's bf16 weights (moek_common.cuh) and runs
+//               mma.sync m16n8k16 with the WEIGHTS as the 16-row A operand and up to 8 activation rows as B
+//               ("swap AB": a decode block has 1-8 valid rows, so no MMA row is padding). The k order inside an
+//               MMA is the lane's own 16 consecutive k; activations are read in the same order.
+//   output    = fp32 partial sums part[split][id][column] (gate at column c, up at I + c); the epilogue kernels add
+//               the splits in split order (deterministic) and apply SwiGLU or router weight + top-k sum.
+//
+// Exception scales (the packed format's out-of-window values) are patched per stage: the run's list is read by the
+// warp, an entry whose k-group and column belong to the warp is broadcast with a shuffle to the lane that owns it.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "moek_common.cuh"
+#include "moek_kernels.cuh"
+
+namespace moek {
+
+
+
+constexpr int DC_WARPS = 8, DC_THREADS = DC_WARPS * 32 + 32;
+constexpr int X_STRIDE = 144;  // bytes per activation row in a slot (128 + 16: conflict-free 16-byte reads)
+
+template <int XR>
+struct DecodeCfg {
+  static constexpr int SLOT = STAGE_BYTES + PAIR_BYTES + XR * X_STRIDE;
+  static constexpr int NS = (XR <= 8 ? 10 : XR <= 16 ? 8 : XR <= 32 ? 6 : 4);
+  static constexpr int BAR_OFF = NS * SLOT;
+  static constexpr int SMEM = BAR_OFF + 2 * NS * 8;
+  static constexpr int T = XR / 8;  // token tiles of 8 rows
+};
+
+__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+struct Unit {
+  int blk, item, ks, e;
+};
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t u, int nt) {
+  Unit r;
+  const int per = nt * p.nsplit;
+  r.blk = (int)(u / per);
+  const int rem = (int)(u - (int64_t)r.blk * per);
+  r.item = rem / p.nsplit;
+  r.ks = rem - r.item * p.nsplit;
+  r.e = p.expert_ids[r.blk];
+  return r;
+}
+
+// Item slot -> output column of the N-wide weight matrix
+__device__ __forceinline__ int slot_column(const GemmParams& p, int item, int slot) {
+  if (p.gate_up) return slot < 128 ? 128 * item + slot : p.N / 2 + 128 * item + slot - 128;
+  return 256 * item + slot;
+}
+
+template <int XR>
+__global__ void __launch_bounds__(DC_THREADS, 1) moek_decode_kernel(GemmParams p) {
+  using C = DecodeCfg<XR>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* empty = full + C::NS;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nt = p.N / ITEM_COLS, nstage = p.K / BK, nb = p.K / 128;
+  const int su = nstage / p.nsplit;  // stages per unit
+  if (tid == 0) {
+    for (int i = 0; i < C::NS; i++) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, DC_WARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const uint64_t deadline = globaltimer() + p.timeout_ns;
+  const int nblocks = min(p.num_post_pad[0] / p.block_m, p.max_blocks);
+  const int64_t nunits = (int64_t)nblocks * nt * p.nsplit;
+
+  if (warp == DC_WARPS) {  // ------------------------------------------------------------------ producer
+    uint32_t g = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+      const Unit un = unit_of(p, u, nt);
+      if (un.e < 0 || un.e >= p.E) continue;  // reported by the consumers
+      // valid rows are a prefix of the block: count them once per unit
+      int nv = 0;
+      for (int r0 = 0; r0 < XR; r0 += 32) {
+        const int r = r0 + lane;
+        const bool v = r < XR && r < p.block_m && p.sorted_ids[(int64_t)un.blk * p.block_m + r] < p.num_ids;
+        nv += __popc(__ballot_sync(0xffffffffu, v));
+      }
+      for (int st = un.ks * su; st < (un.ks + 1) * su; st++, g++) {
+        const int slot = g % C::NS;
+        if (g >= C::NS && !mbar_wait(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err)) { ok = false; break; }
+        uint8_t* dst = smem + slot * C::SLOT;
+        if (lane == 0) mbar_expect_tx(full + slot, STAGE_BYTES + PAIR_BYTES + nv * BK * 2);
+        __syncwarp();
+        if (lane == 0) {
+          const int64_t wi = ((int64_t)un.e * nt + un.item) * nstage + st;
+          bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
+          const int64_t si = ((int64_t)un.e * nt + un.item) * nb + (st >> 1);
+          bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+        }
+        for (int r = lane; r < nv; r += 32) {
+          const int id = p.sorted_ids[(int64_t)un.blk * p.block_m + r];
+          const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + st * BK;
+          bulk_g2s(dst + STAGE_BYTES + PAIR_BYTES + r * X_STRIDE, src, BK * 2, full + slot);
+        }
+      }
+    }
+    // wind down: wait (bounded) until the consumers released every slot still in flight
+    if (!ok) return;
+    for (uint32_t i = 0; i < C::NS && i < g; i++) {
+      const uint32_t gg = g - 1 - i;
+      if (!mbar_wait(empty + gg % C::NS, (gg / C::NS) & 1, deadline, p.err)) return;
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------------------------------- consumers
+  const int gq = lane >> 2, c = lane & 3;
+  // the warp's two 16-row groups of the item
+  const int G0 = p.gate_up ? warp : 2 * warp, G1 = p.gate_up ? warp + 8 : 2 * warp + 1;
+  int slots[2][2], pos[2][2];
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      slots[i][h] = 16 * (i ? G1 : G0) + gq + 8 * h;
+      pos[i][h] = slot_position(slots[i][h]);
+    }
+  uint32_t g = 0;
+  for (int64_t u = blockIdx.x; u < nunits; u += gridDim.x) {
+    const Unit un = unit_of(p, u, nt);
+    if (un.e < 0 || un.e >= p.E) {
+      if (lane == 0 && warp == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
+      continue;
+    }
+    const float gsc = p.G[un.e];
+    int nv = 0;
+    for (int r0 = 0; r0 < XR; r0 += 32) {
+      const int r = r0 + lane;
+      const bool v = r < XR && r < p.block_m && p.sorted_ids[(int64_t)un.blk * p.block_m + r] < p.num_ids;
+      nv += __popc(__ballot_sync(0xffffffffu, v));
+    }
+    if (XR < p.block_m && lane == 0 && warp == 0 &&
+        p.sorted_ids[(int64_t)un.blk * p.block_m + XR] < p.num_ids)
+      report(p.err, MOEK_DEV_TOO_MANY_ROWS);  // more rows than this instantiation holds: the host chose too small
+    const int ntile = (nv + 7) >> 3;
+    float acc[2][C::T][4];
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+#pragma unroll
+      for (int t = 0; t < C::T; t++)
+#pragma unroll
+        for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
+
+    bool ok = true;
+    for (int st = un.ks * su; st < (un.ks + 1) * su; st++, g++) {
+      const int slot = g % C::NS;
+      if (!mbar_wait(full + slot, (g / C::NS) & 1, deadline, p.err)) { ok = false; break; }
+      const uint8_t* sw = smem + slot * C::SLOT;
+      const uint8_t* ss = sw + STAGE_BYTES;
+      const uint8_t* sx = ss + PAIR_BYTES;
+      const int kg_run = (st & 1) * 4 + c;  // this lane's k-group inside the run
+      uint32_t sb[2][2];
+#pragma unroll
+      for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) sb[i][h] = run_byte(ss + (slots[i][h] >> 7) * RUN_BYTES, pos[i][h], kg_run);
+      // exceptions of this (expert, item, run)
+      {
+        const int64_t key = ((int64_t)un.e * nt + un.item) * nb + (st >> 1);
+        const int eo0 = p.exc_off[key], eo1 = p.exc_off[key + 1];
+        const int r0g = p.gate_up ? un.item : 2 * un.item;  // global run index of the pair's first run
+        for (int b0 = eo0; b0 < eo1; b0 += 32) {
+          uint32_t en = 0;
+          bool mine = false;
+          if (b0 + lane < eo1) {
+            en = p.exc_ent[b0 + lane];
+            const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+            const int rp = (ppos >> 7) == r0g ? 0 : 1;
+            const int slot_e = rp * 128 + position_slot(ppos & 127);
+            const int ge = slot_e >> 4;
+            const int we = p.gate_up ? (ge & 7) : (ge >> 1);
+            mine = (kg >> 2) == (st & 1) && we == warp;
+          }
+          unsigned m = __ballot_sync(0xffffffffu, mine);
+          while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const uint32_t e2 = __shfl_sync(0xffffffffu, en, src);
+            const int ppos = e2 & 0xFFFF, kg = (e2 >> 16) & 0xFF;
+            const int rp = (ppos >> 7) == r0g ? 0 : 1;
+            const int slot_e = rp * 128 + position_slot(ppos & 127);
+            const int ge = slot_e >> 4, row = slot_e & 15;
+            const int i = (ge == G0) ? 0 : 1;
+            if (gq == (row & 7) && c == (kg & 3)) sb[i][row >> 3] = e2 >> 24;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 2; i++) {
+        const ScaleBR sa = scale_br(sb[i][0], gsc), sbv = scale_br(sb[i][1], gsc);
+        const uint4 q = *reinterpret_cast<const uint4*>(sw + ((i ? G1 : G0) * 32 + lane) * 16);
+        uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
+        dequant_word(q.x, sa, wa0);
+        dequant_word(q.y, sbv, wb0);
+        dequant_word(q.z, sa, wa1);
+        dequant_word(q.w, sbv, wb1);
+        const uint32_t A0[4] = {wa0[0], wb0[0], wa0[1], wb0[1]};
+        const uint32_t A1[4] = {wa0[2], wb0[2], wa0[3], wb0[3]};
+        const uint32_t A2[4] = {wa1[0], wb1[0], wa1[1], wb1[1]};
+        const uint32_t A3[4] = {wa1[2], wb1[2], wa1[3], wb1[3]};
+#pragma unroll
+        for (int t = 0; t < C::T; t++) {
+          if (t < ntile) {
+            const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
+            const uint4 x0 = *reinterpret_cast<const uint4*>(xr);
+            const uint4 x1 = *reinterpret_cast<const uint4*>(xr + 16);
+            mma_bf16_16816(acc[i][t], A0, x0.x, x0.y);
+            mma_bf16_16816(acc[i][t], A1, x0.z, x0.w);
+            mma_bf16_16816(acc[i][t], A2, x1.x, x1.y);
+            mma_bf16_16816(acc[i][t], A3, x1.z, x1.w);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + slot);
+    }
+    if (!ok) return;
+    // fp32 partials
+    float* base = p.part + (int64_t)un.ks * p.num_ids * p.N;
+#pragma unroll
+    for (int t = 0; t < C::T; t++) {
+      if (t >= ntile) break;
+#pragma unroll
+      for (int v = 0; v < 2; v++) {
+        const int r = t * 8 + 2 * c + v;
+        if (r >= nv) continue;
+        const int id = p.sorted_ids[(int64_t)un.blk * p.block_m + r];
+        float* row = base + (int64_t)id * p.N;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          row[slot_column(p, un.item, slots[i][0])] = acc[i][t][v];
+          row[slot_column(p, un.item, slots[i][1])] = acc[i][t][2 + v];
+        }
+      }
+    }
+  }
+}
+
+// gate_up epilogue: act[id][c] = bf16(silu(sum_s g) * sum_s u), sums over the splits in split order.
+__global__ void moek_gate_epilogue_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N,
+                                          __nv_bfloat16* __restrict__ act) {
+  const int I = N / 2;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)num_ids * I) return;
+  const int64_t id = i / I;
+  const int col = (int)(i - id * I);
+  const int64_t stride = (int64_t)num_ids * N;
+  const float* r = part + id * N;
+  float gsum = 0.f, usum = 0.f;
+  for (int s = 0; s < nsplit; s++) {
+    gsum += r[s * stride + col];
+    usum += r[s * stride + I + col];
+  }
+  act[i] = __float2bfloat16_rn(silu(gsum) * usum);
+}
+
+// down epilogue fused with the top-k sum: out[t][n] = bf16(sum_j w[t,j] * sum_s part[s][t*k+j][n]) in fp32, slots in
+// order j = 0..k-1 (one rounding, as the fp32 oracle), optionally also the per-slot rows dout (fp32 -> bf16).
+__global__ void moek_down_combine_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N, int top_k,
+                                         const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = num_ids / top_k;
+  if (i >= (int64_t)m * N) return;
+  const int64_t t = i / N;
+  const int n = (int)(i - t * N);
+  const int64_t stride = (int64_t)num_ids * N;
+  float o = 0.f;
+  for (int j = 0; j < top_k; j++) {
+    const int64_t id = t * top_k + j;
+    float s = 0.f;
+    for (int sp = 0; sp < nsplit; sp++) s += part[sp * stride + id * N + n];
+    o += topk_w[id] * s;
+  }
+  out[i] = __float2bfloat16_rn(o);
+}
+
+// down epilogue without the sum: dout[id][n] = fp32 w[id] * sum_s part (kept in fp32 for the combine)
+__global__ void moek_down_rows_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N,
+                                      const float* __restrict__ topk_w, float* __restrict__ dout) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)num_ids * N) return;
+  const int64_t id = i / N;
+  const int64_t stride = (int64_t)num_ids * N;
+  float s = 0.f;
+  for (int sp = 0; sp < nsplit; sp++) s += part[sp * stride + i];
+  dout[i] = topk_w[id] * s;
+}
+
+// top-k combine of fp32 rows: out[t][n] = bf16(sum_j rows[t*k + j][n]) (slot order)
+__global__ void moek_combine_f32_kernel(const float* __restrict__ rows, int m, int N, int top_k,
+                                        __nv_bfloat16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)m * N) return;
+  const int64_t t = i / N;
+  const int n = (int)(i - t * N);
+  float o = 0.f;
+  for (int j = 0; j < top_k; j++) o += rows[(t * top_k + j) * N + n];
+  out[i] = __float2bfloat16_rn(o);
+}
+
+// top-k combine of bf16 rows (the reference's torch.sum over dim 1: fp32 accumulation, one rounding)
+__global__ void moek_combine_bf16_kernel(const __nv_bfloat16* __restrict__ rows, int m, int N, int top_k,
+                                         __nv_bfloat16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)m * N) return;
+  const int64_t t = i / N;
+  const int n = (int)(i - t * N);
+  float o = 0.f;
+  for (int j = 0; j < top_k; j++) o += __bfloat162float(rows[(t * top_k + j) * N + n]);
+  out[i] = __float2bfloat16_rn(o);
+}
+
+// ------------------------------------------------------------------------------------------------- launchers
+template <int XR>
+static cudaError_t launch_decode_xr(const GemmParams& p, int grid, cudaStream_t st) {
+  using C = DecodeCfg<XR>;
+  cudaError_t e = cudaFuncSetAttribute(moek_decode_kernel<XR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  moek_decode_kernel<XR><<<grid, DC_THREADS, C::SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode(const GemmParams& p, int max_rows, int sms, cudaStream_t st) {
+  const int nt = p.N / ITEM_COLS;
+  const int64_t units = (int64_t)p.max_blocks * nt * p.nsplit;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, units));
+  if (max_rows <= 8) return launch_decode_xr<8>(p, grid, st);
+  if (max_rows <= 16) return launch_decode_xr<16>(p, grid, st);
+  if (max_rows <= 32) return launch_decode_xr<32>(p, grid, st);
+  return launch_decode_xr<96>(p, grid, st);
+}
+
+cudaError_t launch_gate_epilogue(const float* part, int nsplit, int num_ids, int N, __nv_bfloat16* act,
+                                 cudaStream_t st) {
+  const int64_t n = (int64_t)num_ids * (N / 2);
+  if (n == 0) return cudaSuccess;
+  moek_gate_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, nsplit, num_ids, N, act);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_down_combine(const float* part, int nsplit, int num_ids, int N, int top_k, const float* topk_w,
+                                __nv_bfloat16* out, cudaStream_t st) {
+  const int64_t n = (int64_t)(num_ids / top_k) * N;
+  if (n == 0) return cudaSuccess;
+  moek_down_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, nsplit, num_ids, N, top_k, topk_w,
+                                                                         out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_down_rows(const float* part, int nsplit, int num_ids, int N, const float* topk_w, float* dout,
+                             cudaStream_t st) {
+  const int64_t n = (int64_t)num_ids * N;
+  if (n == 0) return cudaSuccess;
+  moek_down_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, nsplit, num_ids, N, topk_w, dout);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_f32(const float* rows, int m, int N, int top_k, __nv_bfloat16* out, cudaStream_t st) {
+  const int64_t n = (int64_t)m * N;
+  if (n == 0) return cudaSuccess;
+  moek_combine_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, m, N, top_k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_bf16(const __nv_bfloat16* rows, int m, int N, int top_k, __nv_bfloat16* out,
+                                cudaStream_t st) {
+  const int64_t n = (int64_t)m * N;
+  if (n == 0) return cudaSuccess;
+  moek_combine_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, m, N, top_k, out);
+  return cudaGetLastError();
+}
+
+}  // namespace moek

@@ -1,0 +1,44 @@
+// Launch interfaces shared by the kernel files and the C ABI (moek_abi.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moek {
+
+struct GemmParams {
+  const __nv_bfloat16* A;  // gate_up: hidden [M, K]; down: act [num_ids, K]
+  const uint8_t* W;        // tiled codes [E, N/256, K/64, 8 KB]
+  const float* G;          // processed global scales [E]
+  const int32_t* sorted_ids;
+  const int32_t* expert_ids;
+  const int32_t* num_post_pad;
+  const uint8_t* SP;        // tiled packed scales [E, N/256, K/128, 1056]
+  const int32_t* exc_off;   // [E * N/256 * K/128 + 1]
+  const uint32_t* exc_ent;  // exception entries
+  float* part;              // [nsplit, num_ids, N]
+  int* err;
+  uint64_t timeout_ns;
+  int num_ids, N, K, E, a_div, block_m, nsplit, max_blocks;
+  int gate_up;
+};
+
+// moek_align.cu
+cudaError_t launch_align(const int32_t* ids, int64_t numel, int E, int bs, int32_t* sorted_ids, int64_t sorted_len,
+                         int32_t* expert_ids, int64_t expert_len, int32_t* npad, void* ws, cudaStream_t st);
+size_t align_workspace_bytes(int64_t numel, int E);
+size_t align_smem_one(int E);
+
+// moek_decode.cu
+cudaError_t launch_decode(const GemmParams& p, int max_rows, int sms, cudaStream_t st);
+cudaError_t launch_gate_epilogue(const float* part, int nsplit, int num_ids, int N, __nv_bfloat16* act,
+                                 cudaStream_t st);
+cudaError_t launch_down_combine(const float* part, int nsplit, int num_ids, int N, int top_k, const float* topk_w,
+                                __nv_bfloat16* out, cudaStream_t st);
+cudaError_t launch_down_rows(const float* part, int nsplit, int num_ids, int N, const float* topk_w, float* dout,
+                             cudaStream_t st);
+cudaError_t launch_combine_f32(const float* rows, int m, int N, int top_k, __nv_bfloat16* out, cudaStream_t st);
+cudaError_t launch_combine_bf16(const __nv_bfloat16* rows, int m, int N, int top_k, __nv_bfloat16* out,
+                                cudaStream_t st);
+
+}  // namespace moek

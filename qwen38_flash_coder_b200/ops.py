@@ -1,0 +1,240 @@
+"""Torch-facing operators over the C ABI, with the reference's names and argument lists.
+
+- ``moe_align_block_size``: vLLM's wrapper signature (vllm/model_executor/layers/fused_moe/moe_align_block_size.py:
+  11-18, buffer sizes :74-88), backed by this build's kernel instead of ``torch.ops._moe_C``.
+- ``moe_gemm`` / ``moe_split_epilogue``: the kit's extension functions (files/mbx_moek.cu:717-721,835-836).
+- ``fused_moe``: the body of the kit's forward wrap (files/mbx_moek.py:236-289): align -> gate_up -> epilogue -> down
+  -> epilogue fused with the top-k sum.
+
+Every tensor must already live on a CUDA device; there is no CPU path. Errors raise ``MoekError`` (a RuntimeError),
+like the reference's TORCH_CHECK failures.
+"""
+import os
+
+import torch
+
+from . import _lib
+from ._lib import MoekError, call
+from .prep import PreparedLayer
+
+BM = 96  # moe_align block size (rows per block), as the kit (files/mbx_moek.py:33)
+LAUNCHES_PER_LAYER = 5  # align, gate_up GEMM, gate epilogue, down GEMM, down epilogue + top-k sum
+_BUF: dict = {}
+_PROF = None  # when a list, fused_moe records (name, start event, end event) around its GEMM launches
+
+
+def _ptr(t):
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise MoekError("moek_b200: tensors must be on a CUDA device (no CPU implementation)")
+
+
+def error_word(dev) -> torch.Tensor:
+    """Per-device int32 [4]; [0] is the kernels' device error word (MOEK_DEV_*)."""
+    key = ("cnt", torch.device(dev))
+    if key not in _BUF:
+        _BUF[key] = torch.zeros(4, dtype=torch.int32, device=dev)
+    return _BUF[key]
+
+
+def check_device_errors(dev) -> None:
+    """Synchronises and raises if a kernel recorded a device-side error (timeout, bad expert id, too many rows)."""
+    w = error_word(dev)
+    code = int(w[0].item())
+    if code:
+        w.zero_()
+        names = {1: "a bounded wait timed out", 2: "an expert id out of range", 3: "a block with more rows than "
+                 "max_rows"}
+        raise MoekError(f"moek_b200: device error {code}: {names.get(code, 'unknown')}")
+
+
+def _scratch(name: str, numel: int, dtype, dev) -> torch.Tensor:
+    key = (name, torch.device(dev), dtype)
+    t = _BUF.get(key)
+    if t is None or t.numel() < numel:
+        t = _BUF[key] = torch.empty(max(numel, 1), dtype=dtype, device=dev)
+    return t
+
+
+# ---------------------------------------------------------------------------------------------------- moe_align
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int, expert_map=None,
+                         pad_sorted_ids: bool = False, ignore_invalid_experts: bool = False):
+    """(sorted_ids, expert_ids, num_tokens_post_pad) with vLLM's contract; ids outside [0, E) are always skipped."""
+    if expert_map is not None:
+        raise MoekError("moek_b200: expert_map is not supported by moe_align (use qwen38_flash_coder_b200.ep)")
+    _need_cuda(topk_ids)
+    ids = topk_ids.reshape(-1)
+    if ids.dtype != torch.int32:
+        ids = ids.to(torch.int32)
+    ids = ids.contiguous()
+    numel = ids.numel()
+    n = numel + num_experts * (block_size - 1)
+    if pad_sorted_ids:
+        n = (n + block_size - 1) // block_size * block_size
+    if numel < num_experts:
+        n = min(numel * block_size, n)
+    dev = ids.device
+    sorted_ids = torch.empty(n, dtype=torch.int32, device=dev)
+    expert_ids = torch.empty((n + block_size - 1) // block_size, dtype=torch.int32, device=dev)
+    npad = torch.empty(1, dtype=torch.int32, device=dev)
+    import ctypes
+
+    wsb = ctypes.c_size_t(0)
+    call("moek_align_workspace_bytes", numel, num_experts, ctypes.byref(wsb))
+    ws = _scratch("align_ws", (wsb.value + 3) // 4, torch.int32, dev) if wsb.value else None
+    call("moek_align", _ptr(ids), numel, num_experts, block_size, _ptr(sorted_ids), sorted_ids.numel(),
+         _ptr(expert_ids), expert_ids.numel(), _ptr(npad), _ptr(ws), wsb.value, _stream(dev))
+    return sorted_ids, expert_ids, npad
+
+
+# ------------------------------------------------------------------------------------------------------ moe_gemm
+def moe_gemm(A, W, S, G, sorted_ids, expert_ids, num_post_pad, topk_w, out, top_k: int, gate_up: bool, SP, exc_off,
+             exc_ent, ws, cnt, mode: int, nsplit: int, part, order: int = 0, tiled: bool = True, *,
+             block_m: int = BM, max_rows: int = 0) -> None:
+    """The kit's moe_gemm argument list (files/mbx_moek.cu:717-721). ``ws`` and ``order`` are accepted and unused;
+    ``S`` must be empty (packed scales only); ``cnt``'s first int32 receives device error codes. Only mode 2 (split-k
+    partials into ``part``) exists; ``out`` and ``topk_w`` are finished by ``moe_split_epilogue``."""
+    _need_cuda(A, W, G, sorted_ids, SP, part)
+    if S is not None and S.numel():
+        raise MoekError("moek_b200: plain Marlin scales are not supported; pass the packed SP")
+    k = A.shape[1]
+    n = W.shape[2] // 2
+    num_ids = out.shape[0]  # act [num_ids, N/2] or dout [num_ids, N], as the reference sizes the call
+    if max_rows <= 0:
+        m_tok = num_ids // top_k if gate_up else num_ids
+        max_rows = min(block_m, max(1, m_tok))
+    call("moek_gemm", _ptr(A), _ptr(W), None, _ptr(G), _ptr(sorted_ids), sorted_ids.numel(), _ptr(expert_ids),
+         _ptr(num_post_pad), _ptr(topk_w), _ptr(out), num_ids, n, k, W.shape[0], top_k, int(bool(gate_up)), _ptr(SP),
+         _ptr(exc_off), _ptr(exc_ent), _ptr(cnt), cnt.numel(), mode, nsplit, _ptr(part), part.numel(), int(tiled),
+         block_m, min(max_rows, 96), _stream(A.device))
+
+
+def moe_split_epilogue(part, nsplit: int, topk_ids, G, topk_w, out, gate_up: bool, N: int) -> None:
+    """The kit's moe_split_epilogue argument list (files/mbx_moek.cu:835-836). ``G`` is accepted and unused (the
+    global scale is already inside the dequantised weights). Down: ``out`` fp32 [num_ids, N] receives the weighted
+    rows; ``out`` bf16 [num_ids / top_k, N] the rows already summed over each token's top_k slots."""
+    _need_cuda(part, out)
+    num_ids = topk_ids.numel()
+    top_k = topk_ids.shape[-1] if topk_ids.dim() > 1 else 1
+    if gate_up:
+        call("moek_split_epilogue", _ptr(part), nsplit, num_ids, N, 1, None, top_k, _ptr(out), 0, _stream(out.device))
+        return
+    if out.dtype == torch.float32 and out.shape[0] == num_ids:
+        kind = 1
+    elif out.dtype == torch.bfloat16 and out.shape[0] * top_k == num_ids:
+        kind = 2
+    else:
+        raise MoekError("moek_b200: down epilogue writes fp32 [num_ids, N] rows or the bf16 [M, N] top-k sum")
+    call("moek_split_epilogue", _ptr(part), nsplit, num_ids, N, 0, _ptr(topk_w), top_k, _ptr(out), kind,
+         _stream(out.device))
+
+
+def combine(rows: torch.Tensor, top_k: int, out: torch.Tensor = None) -> torch.Tensor:
+    """Top-k sum of per-slot rows [M * top_k, N] (fp32 or bf16) -> bf16 [M, N] (files/mbx_moek.py:284-289)."""
+    _need_cuda(rows)
+    m = rows.shape[0] // top_k
+    n = rows.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=rows.device)
+    call("moek_combine", _ptr(rows), int(rows.dtype == torch.float32), _ptr(out), m, n, top_k, _stream(rows.device))
+    return out
+
+
+# ----------------------------------------------------------------------------------------------------- forward
+def _splits(k: int, units_per_split: int, sms: int) -> int:
+    """Smallest k-split (whole 128-k runs per unit) giving at least 2 units per SM, else the finest."""
+    nstage = k // 64
+    best = 1
+    for d in range(1, nstage + 1):
+        if nstage % d or (nstage // d) % 2:
+            continue
+        best = d
+        if units_per_split * d >= 2 * sms:
+            break
+    return best
+
+
+def _sms(dev) -> int:
+    key = ("sms", torch.device(dev))
+    if key not in _BUF:
+        _BUF[key] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return _BUF[key]
+
+
+def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+              output: torch.Tensor = None) -> torch.Tensor:
+    """One routed-expert layer: out[t] = sum_j w[t, j] * down_e(silu(gate_e(x_t)) * up_e(x_t)), e = topk_ids[t, j]."""
+    x = hidden_states
+    _need_cuda(x, topk_ids, topk_weights)
+    m, hid = x.shape
+    if output is None:
+        output = torch.empty((m, hid), dtype=torch.bfloat16, device=x.device)
+    if m == 0:
+        return output
+    if x.dtype != torch.bfloat16:
+        raise MoekError("moek_b200: hidden states must be bf16")
+    x = x.contiguous()
+    top_k = topk_ids.shape[1]
+    num_ids = m * top_k
+    dev = x.device
+    a, b = layer.w13, layer.w2
+    ids32 = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
+    ids32 = ids32.contiguous()
+    tw = topk_weights.reshape(-1).float().contiguous()
+    sid, eid, npad = moe_align_block_size(ids32, BM, layer.E)
+    sms = _sms(dev)
+    est_blocks = min(layer.E, num_ids) if m <= BM else (num_ids + BM - 1) // BM + min(layer.E, num_ids)
+    ns1 = _splits(a.K, est_blocks * (a.N // 256), sms)
+    ns2 = _splits(b.K, est_blocks * (b.N // 256), sms)
+    part = _scratch("part", max(ns1 * num_ids * a.N, ns2 * num_ids * b.N), torch.float32, dev)
+    cnt = error_word(dev)
+    rows = min(BM, m)
+    _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, ns1, part, rows))
+    act = torch.empty((num_ids, a.N // 2), dtype=torch.bfloat16, device=dev)
+    call("moek_split_epilogue", _ptr(part), ns1, num_ids, a.N, 1, None, top_k, _ptr(act), 0, _stream(dev))
+    _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, ns2, part, rows))
+    call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(output), 2, _stream(dev))
+    return output
+
+
+def _gemm(a_in, mat, sid, eid, npad, num_ids, a_div, gate_up, cnt, nsplit, part, rows):
+    call("moek_gemm", _ptr(a_in), _ptr(mat.w), None, _ptr(mat.g), _ptr(sid), sid.numel(), _ptr(eid), _ptr(npad), None,
+         None, num_ids, mat.N, mat.K, mat.E, a_div, int(gate_up), _ptr(mat.sp), _ptr(mat.exc_off), _ptr(mat.exc_ent),
+         _ptr(cnt), cnt.numel(), 2, nsplit, _ptr(part), part.numel(), 1, BM, rows, _stream(a_in.device))
+
+
+def _timed(name, fn):
+    if _PROF is None:
+        return fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    r = fn()
+    e1.record()
+    _PROF.append((name, e0, e1))
+    return r
+
+
+def profile_kernels(fn, names=("gate_gemm", "down_gemm"), reps: int = 3) -> dict:
+    """Average device time in ms of each named launch while ``fn`` runs ``reps`` times (CUDA events recorded on the
+    launching stream around each launch)."""
+    global _PROF
+    _PROF = []
+    try:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        acc = {n: [] for n in names}
+        for n, e0, e1 in _PROF:
+            if n in acc:
+                acc[n].append(e0.elapsed_time(e1))
+    finally:
+        _PROF = None
+    return {n: (sum(v) / len(v) if v else float("nan")) for n, v in acc.items()}

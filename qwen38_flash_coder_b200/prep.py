@@ -1,0 +1,214 @@
+"""Load-time conversion of checkpoint NVFP4 experts into the kernels' layouts (torch, runs on the weights' device).
+
+Input: the checkpoint tensors vLLM hands to ``prepare_nvfp4_moe_layer_for_marlin`` (vllm/.../marlin_utils_fp4.py:
+288-298): ``weight`` uint8 [E, N, K/2] (element 2i in the low nibble), ``weight_scale`` float8 E4M3 [E, N, K/16],
+``weight_scale_2`` fp32 [E].
+
+Output, per matrix:
+
+- **scales**: vLLM's Marlin scale bytes (marlin_utils_fp4.py:30-146,355-386: shared power-of-two factor, the 64-value
+  ``scale_perm`` and the [0, 2, 1, 3] pair swap, the S0E5M3 byte), then the kit's lossless packed format and item
+  tiling (files/mbx_moek.py:61-172). The byte format is the reference's, bit for bit; the code is this module's own
+  (window choice by pairwise counting instead of sort + searchsorted).
+- **global scale**: ``weight_scale_2 * 2^119 / scale_factor`` (marlin_utils_fp4.py:134-146,385-386).
+- **weights**: this build's tiled layout, an int32 tensor of the reference's shape [E, K/16, 2N] (same bytes as the
+  checkpoint, reordered). Per (expert, 256-column item, 64-k stage) one contiguous 8 KB block; inside it 16 groups
+  of 16 columns, each 32 lanes x 4 words of 8 codes. Lane L = 4g + c, word j holds column ``16G + g + 8(j & 1)``
+  of the item and the 8 consecutive k ``64s + 16c + 8(j >> 1) + i`` (i = 0..7) with code i in nibble
+  ``NIBBLE_OF[i]``: a lane's 16 bytes are rows g and g + 8 of a 16-row group over one whole 16-k group (one scale
+  per row), i.e. the A operand of four mma.sync m16n8k16 steps, and each word decodes, two codes at a time, into
+  bf16 pairs (k, k+1) in order. Item slots 0..127 are gate columns ``128t + slot`` and 128..255 the
+  matching up columns ``I + 128t + slot - 128`` (gate_up), or columns ``256t + slot`` (down).
+"""
+import torch
+
+KG = 8
+RUN = 16 + KG * 64  # 528: packed bytes per (expert, run of 8 k-groups, 128 positions)
+NIBBLE_OF = (3, 7, 2, 6, 1, 5, 0, 4)  # nibble position of code i of a word's 8 consecutive k
+
+
+# ------------------------------------------------------------------------------------------------------------ scales
+def scale_factor(scales: torch.Tensor) -> float:
+    """Power of two shared by all experts of a matrix: largest 2^j with max(nonzero) * 2^(7+j) <= 448 * 2^7."""
+    v = scales.float()
+    nz = v[v > 0]
+    if nz.numel() == 0:
+        return 1.0
+    mx = float(nz.max()) * 128.0
+    lim = 448.0 * 128.0
+    sf = 1.0
+    while mx < lim and mx * sf * 2.0 <= lim:
+        sf *= 2.0
+    return sf
+
+
+def marlin_scale_bytes(scales: torch.Tensor, sf: float) -> torch.Tensor:
+    """[E, N, K/16] float8_e4m3fn -> Marlin S0E5M3 bytes [E, K/16, N] (uint8)."""
+    e, n, kg = scales.shape
+    s = scales.float().transpose(1, 2).reshape(e, kg, n // 64, 8, 8)  # column 8j + i of each 64 at [.., j, i]
+    s = s.transpose(-1, -2).reshape(e, kg, n)  # position 8i + j <- column i + 8j
+    h = s.to(torch.float16).reshape(e, kg, n // 4, 4)[..., [0, 2, 1, 3]].reshape(e, kg, n)
+    if sf > 1.0:
+        h = (h.float() * sf).to(torch.float16)
+    h = h * 128.0
+    h = torch.where(h < 2, torch.zeros_like(h), h)
+    bits = h.view(torch.int16).to(torch.int32) & 0xFFFF
+    return ((bits >> 7) & 0xFF).to(torch.uint8)
+
+
+def global_scale(gs: torch.Tensor, sf: float) -> torch.Tensor:
+    return (gs.float() * (2.0 ** 119)) / sf
+
+
+def pack_scales(s: torch.Tensor, gate_up: bool, chunk: int = 32):
+    """bytes [E, K/16, N] -> (packed uint8 [E, K/128, N/128, 528], exc_off int32 [E*N/256*K/128 + 1], exc_ent int32).
+
+    Same bytes as files/mbx_moek.py:61-120. The base of each (8 positions x 8 k-groups) block is the smallest value v
+    of the block whose window [v, v + 15] holds the most values of the block.
+    """
+    e, kr, n = s.shape
+    nb, nt = kr // KG, n // 256
+    dev = s.device
+    packed = torch.empty((e, nb, n // 128, RUN), dtype=torch.uint8, device=dev)
+    keys, cols, kgs, vals = [], [], [], []
+    for e0 in range(0, e, chunk):
+        e1 = min(e, e0 + chunk)
+        ec = e1 - e0
+        # v[e, b, chunk, kg, p]: block (e, b, chunk) holds k-groups b*8..b*8+7 of positions chunk*8..chunk*8+7
+        v = s[e0:e1].view(ec, nb, KG, n // 8, 8).permute(0, 1, 3, 2, 4).to(torch.int16)
+        flat = v.reshape(ec, nb, n // 8, KG * 8)
+        inwin = (flat[..., None, :] >= flat[..., :, None]) & (flat[..., None, :] <= flat[..., :, None] + 15)
+        score = inwin.sum(-1).to(torch.int32) * 256 + (255 - flat.to(torch.int32))
+        base = torch.gather(flat, -1, score.argmax(-1, keepdim=True))  # [ec, nb, n/8, 1]
+        off = v - base[..., None]
+        exc = (off < 0) | (off > 15)
+        off = torch.where(exc, torch.zeros_like(off), off).to(torch.uint8)
+        nib = off[..., :4] | (off[..., 4:] << 4)  # [ec, nb, n/8, KG, 4]
+        body = nib.view(ec, nb, n // 128, 16, KG, 4).permute(0, 1, 2, 4, 3, 5).reshape(ec, nb, n // 128, KG * 64)
+        packed[e0:e1, :, :, :16] = base.view(ec, nb, n // 128, 16).to(torch.uint8)
+        packed[e0:e1, :, :, 16:] = body
+        ie, ib, ic, ikg, ip = torch.nonzero(exc, as_tuple=True)
+        run = ic // 16
+        item = run % nt if gate_up else run // 2
+        keys.append(((ie + e0) * nt + item) * nb + ib)
+        cols.append(ic * 8 + ip)
+        kgs.append(ikg)
+        vals.append(v[ie, ib, ic, ikg, ip].to(torch.int64))
+    key, col, kg, val = (torch.cat(t) for t in (keys, cols, kgs, vals))
+    # entries of one (expert, item, run) list in (position chunk, k-group, position-in-chunk) order
+    order = torch.argsort((key * (n // 8) + col // 8) * 64 + kg * 8 + col % 8)
+    key, col, kg, val = key[order], col[order], kg[order], val[order]
+    cnt = torch.bincount(key, minlength=e * nt * nb)
+    exc_off = torch.zeros(e * nt * nb + 1, dtype=torch.int32, device=dev)
+    exc_off[1:] = torch.cumsum(cnt, 0).to(torch.int32)
+    word = col | (kg << 16) | (val << 24)
+    word = torch.where(word >= 2 ** 31, word - 2 ** 32, word).to(torch.int32)
+    ent = word if word.numel() else torch.zeros(1, dtype=torch.int32, device=dev)
+    return packed, exc_off, ent
+
+
+def tile_scales(packed: torch.Tensor, n: int, gate_up: bool) -> torch.Tensor:
+    """[E, nb, N/128, 528] -> [E, N/256, nb, 1056]: an item's two runs side by side (files/mbx_moek.py:163-172)."""
+    e, nb = packed.shape[:2]
+    nt = n // 256
+    t = torch.arange(nt, device=packed.device)
+    runs = torch.stack([t, nt + t], 1) if gate_up else torch.stack([2 * t, 2 * t + 1], 1)
+    return packed[:, :, runs.flatten(), :].view(e, nb, nt, 2 * RUN).transpose(1, 2).contiguous()
+
+
+# ----------------------------------------------------------------------------------------------------------- weights
+def item_columns(n: int, gate_up: bool, device=None) -> torch.Tensor:
+    """Logical column of every item slot: [N/256, 256]."""
+    nt = n // 256
+    slot = torch.arange(256, device=device)
+    t = torch.arange(nt, device=device)[:, None]
+    if gate_up:
+        return torch.where(slot < 128, 128 * t + slot, n // 2 + 128 * t + slot - 128)
+    return 256 * t + slot
+
+
+def tile_weights(codes: torch.Tensor, gate_up: bool, chunk: int = 16) -> torch.Tensor:
+    """Checkpoint codes uint8 [E, N, K/2] -> this build's tiled int32 [E, K/16, 2N] (see the module docstring)."""
+    e, n, k2 = codes.shape
+    k = 2 * k2
+    nt, ns = n // 256, k // 64
+    cols = item_columns(n, gate_up, codes.device).flatten()
+    shifts = torch.tensor([4 * p for p in NIBBLE_OF], dtype=torch.int64, device=codes.device)
+    out = torch.empty((e, k // 16, 2 * n), dtype=torch.int32, device=codes.device)
+    for e0 in range(0, e, chunk):
+        e1 = min(e, e0 + chunk)
+        c = codes[e0:e1][:, cols, :]
+        nib = torch.stack([c & 0xF, c >> 4], -1).view(e1 - e0, nt, 16, 2, 8, ns, 4, 2, 8)
+        # [e, t, G, jr, g, s, c, jc, i] -> [e, t, s, G, g, c, jc, jr, i]
+        nib = nib.permute(0, 1, 5, 2, 4, 6, 7, 3, 8).to(torch.int64)
+        word = (nib << shifts).sum(-1)
+        word = torch.where(word >= 2 ** 31, word - 2 ** 32, word).to(torch.int32)
+        out[e0:e1] = word.reshape(e1 - e0, k // 16, 2 * n)
+    return out
+
+
+def untile_weights(w: torch.Tensor, n: int, gate_up: bool) -> torch.Tensor:
+    """Inverse of ``tile_weights``: int32 [E, K/16, 2N] -> checkpoint codes uint8 [E, N, K/2]."""
+    e = w.shape[0]
+    k = w.shape[1] * 16
+    nt, ns = n // 256, k // 64
+    shifts = torch.tensor([4 * p for p in NIBBLE_OF], dtype=torch.int64, device=w.device)
+    word = w.to(torch.int64).view(e, nt, ns, 16, 8, 4, 2, 2) & 0xFFFFFFFF
+    nib = ((word[..., None] >> shifts) & 0xF).to(torch.uint8)  # [e, t, s, G, g, c, jc, jr, i]
+    nib = nib.permute(0, 1, 3, 7, 4, 2, 5, 6, 8).reshape(e, nt * 256, k)  # [e, t, G, jr, g, s, c, jc, i]
+    out = torch.empty((e, n, k), dtype=torch.uint8, device=w.device)
+    out[:, item_columns(n, gate_up, w.device).flatten(), :] = nib
+    return (out[..., 0::2] | (out[..., 1::2] << 4)).contiguous()
+
+
+# ------------------------------------------------------------------------------------------------------------- layer
+class PreparedMatrix:
+    """One matrix of a layer in the kernels' format."""
+
+    def __init__(self, codes, scales, gs, gate_up: bool):
+        e, n, k2 = codes.shape
+        k = 2 * k2
+        check_shapes(n, k, gate_up)
+        self.gate_up, self.E, self.N, self.K = gate_up, e, n, k
+        self.sf = scale_factor(scales)
+        sb = marlin_scale_bytes(scales, self.sf)
+        packed, self.exc_off, self.exc_ent = pack_scales(sb, gate_up)
+        self.sp = tile_scales(packed, n, gate_up)
+        self.g = global_scale(gs, self.sf).contiguous()
+        self.w = tile_weights(codes, gate_up)
+
+    def nbytes(self) -> int:
+        """Bytes the kernels read for the whole matrix (weights + packed scales + exception lists)."""
+        return (self.w.numel() * 4 + self.sp.numel() + self.exc_off.numel() * 4
+                + int(self.exc_off[-1]) * 4)
+
+
+def check_shapes(n: int, k: int, gate_up: bool):
+    if k % 128 or n % 256 or (gate_up and (n // 2) % 128):
+        raise ValueError(f"moek_b200: unsupported matrix N={n}, K={k} (need K % 128 == 0, N % 256 == 0"
+                         + (", N/2 % 128 == 0)" if gate_up else ")"))
+
+
+class PreparedLayer:
+    """Both matrices of one routed-expert layer (w13 = gate rows then up rows, w2 = down)."""
+
+    def __init__(self, w13, w2):
+        self.w13 = PreparedMatrix(*w13, gate_up=True)
+        self.w2 = PreparedMatrix(*w2, gate_up=False)
+        self.E = self.w13.E
+        self.hidden = self.w13.K
+        self.inter = self.w13.N // 2
+        if self.w2.N != self.hidden or self.w2.K != self.inter or self.w2.E != self.E:
+            raise ValueError("moek_b200: w13 and w2 shapes do not belong to one layer")
+
+    def expert_bytes(self) -> torch.Tensor:
+        """Per-expert bytes both matrices stream when the expert is touched: [E] int64 (weights + packed scales +
+        that expert's exception entries and offsets)."""
+        out = []
+        for m in (self.w13, self.w2):
+            per = m.w[0].numel() * 4 + m.sp[0].numel()
+            nkeys = (m.exc_off.numel() - 1) // m.E
+            off = m.exc_off.to(torch.int64)
+            n_exc = off[nkeys::nkeys][:m.E] - off[0:-1:nkeys][:m.E]
+            out.append(per + 4 * n_exc + 4 * (nkeys + 1))
+        return out[0] + out[1]

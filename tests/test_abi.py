@@ -1,0 +1,59 @@
+"""The C ABI library: it loads without a GPU, exports every function include/*.h declares, and rejects bad
+arguments on the host (no kernel is launched for them)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from qwen38_flash_coder_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names += re.findall(r"\b(moek_\w+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for must in ("moek_align", "moek_gemm", "moek_split_epilogue", "moek_combine", "moek_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(declared()) <= set(_lib.SIGNATURES), "ctypes signatures out of date"
+
+
+def test_version_and_errors_without_gpu():
+    lib = _lib.lib()
+    assert lib.moek_version() == 1
+    # bad arguments are rejected before any CUDA call
+    rc = lib.moek_align(None, 10, 0, 96, None, 0, None, 0, None, None, 0, None)
+    assert rc == 1 and b"num_experts" in lib.moek_last_error()
+    rc = lib.moek_gemm(*([None] * 4), None, 0, None, None, None, None, 5, 300, 2048, 8, 5, 1, None, None, None, None,
+                       0, 2, 1, None, 0, 1, 96, 8, None)
+    assert rc == 1 and b"N % 256" in lib.moek_last_error()
+    rc = lib.moek_set_wait_timeout_ns(0)
+    assert rc == 1
+
+
+def test_align_workspace_query():
+    lib = _lib.lib()
+    b = ctypes.c_size_t(7)
+    assert lib.moek_align_workspace_bytes(40, 512, ctypes.byref(b)) == 0 and b.value == 0
+    assert lib.moek_align_workspace_bytes(34560, 512, ctypes.byref(b)) == 0
+    assert b.value == 4 * (34 * 512 + 34560)
+
+
+def test_call_raises_moek_error():
+    with pytest.raises(_lib.MoekError):
+        _lib.call("moek_set_wait_timeout_ns", 0)

@@ -1,0 +1,126 @@
+"""Load-time weight preparation (qwen38_flash_coder_b200.prep) against the golden fixtures and the CPU oracle.
+
+Mirrors the reference's CPU-side checks (bench/moek/cpu_check.py: the packed-scale round trip) and its tiled ==
+plain check (bench/moek/test_tiled.py:12-15) for this build's own weight layout.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import marlin_scales
+from qwen38_flash_coder_b200 import prep, synth
+
+SETS = [("mw13", True), ("mw2", False), ("rw13", True), ("rw2", False), ("tw2", False)]
+
+
+def _scales(golden, name):
+    return torch.from_numpy(golden[f"{name}_scales"]).view(torch.float8_e4m3fn)
+
+
+@pytest.mark.parametrize("name,gu", SETS)
+def test_marlin_bytes_and_global(golden, name, gu):
+    s = _scales(golden, name)
+    sf = prep.scale_factor(s)
+    assert sf == golden[f"{name}_sf"][0]
+    assert np.array_equal(prep.marlin_scale_bytes(s, sf).numpy(), golden[f"{name}_sbytes"])
+    g = prep.global_scale(torch.from_numpy(golden[f"{name}_gs"]), sf)
+    assert np.array_equal(g.numpy(), golden[f"{name}_g"])
+
+
+@pytest.mark.parametrize("name,gu", SETS)
+def test_pack_scales_bit_exact(golden, name, gu):
+    sb = torch.from_numpy(golden[f"{name}_sbytes"])
+    for chunk in (32, 3):  # expert chunking must not change the result
+        packed, off, ent = prep.pack_scales(sb, gu, chunk=chunk)
+        assert np.array_equal(packed.numpy(), golden[f"{name}_packed"])
+        assert np.array_equal(off.numpy(), golden[f"{name}_exc_off"])
+        assert np.array_equal(ent.numpy(), golden[f"{name}_exc_ent"])
+    n = sb.shape[2]
+    assert np.array_equal(prep.tile_scales(packed, n, gu).numpy(), golden[f"{name}_tiled"])
+
+
+def test_pack_scales_no_exceptions():
+    sb = torch.full((2, 16, 256), 0x90, dtype=torch.uint8)
+    packed, off, ent = prep.pack_scales(sb, False)
+    assert int(off[-1]) == 0 and ent.numel() == 1 and int(ent[0]) == 0
+    assert (packed[..., :16] == 0x90).all() and (packed[..., 16:] == 0).all()
+
+
+@pytest.mark.parametrize("gate_up,n,k", [(True, 512, 256), (False, 256, 512), (True, 1024, 128)])
+def test_tile_weights_round_trip(gate_up, n, k):
+    g = torch.Generator().manual_seed(n + k)
+    codes = torch.randint(0, 256, (3, n, k // 2), dtype=torch.uint8, generator=g)
+    w = prep.tile_weights(codes, gate_up)
+    assert w.shape == (3, k // 16, 2 * n) and w.dtype == torch.int32
+    assert torch.equal(prep.untile_weights(w, n, gate_up), codes)
+
+
+def test_tile_weights_word_contents():
+    """Spot-check the documented layout: word j of lane 4g + c in group G of (item t, stage s)."""
+    n, k = 512, 256
+    codes = torch.randint(0, 256, (1, n, k // 2), dtype=torch.uint8, generator=torch.Generator().manual_seed(3))
+    w = prep.tile_weights(codes, True).view(-1)
+    cols = prep.item_columns(n, True)
+    rng = np.random.default_rng(0)
+    for _ in range(200):
+        t, s, G, g, c, j = (int(rng.integers(x)) for x in (n // 256, k // 64, 16, 8, 4, 4))
+        word = int(w[((((t * (k // 64) + s) * 16 + G) * 32 + 4 * g + c) * 4 + j)]) & 0xFFFFFFFF
+        col = int(cols[t, 16 * G + g + 8 * (j & 1)])
+        for i in range(8):
+            kk = 64 * s + 16 * c + 8 * (j >> 1) + i
+            byte = int(codes[0, col, kk // 2])
+            code = (byte >> 4) if kk & 1 else (byte & 15)
+            assert (word >> (4 * prep.NIBBLE_OF[i])) & 15 == code
+
+
+def test_quantizer_matches_reference_e2m1(golden):
+    x = torch.from_numpy(golden["e2m1_in"])
+    mag = torch.bucketize(x.abs().clamp(max=6.0), synth._MIDS, right=False)
+    codes = (mag | ((x < 0).to(mag.dtype) << 3)).to(torch.uint8)
+    assert torch.equal(codes, torch.from_numpy(golden["e2m1_codes"]))
+
+
+def test_quantizer_scales_and_dequant_error():
+    w = (torch.randn((2, 64, 256), generator=torch.Generator().manual_seed(1)) * 0.02).to(torch.bfloat16)
+    codes, scales, gs = synth.quantize_nvfp4(w)
+    assert codes.shape == (2, 64, 128) and scales.shape == (2, 64, 16) and gs.shape == (2,)
+    assert float(scales.float().max()) <= 448.0
+    from oracle.nvfp4 import dequant_expert
+
+    for e in range(2):
+        deq = dequant_expert(codes[e].numpy(), scales[e].view(torch.uint8).numpy(), float(gs[e]))
+        rel = np.linalg.norm(deq - w[e].float().numpy()) / np.linalg.norm(w[e].float().numpy())
+        assert rel < 0.12, rel  # NVFP4 on Gaussian weights: ~9 % relative error
+
+
+def test_oracle_logical_column_matches_device_permutation():
+    """The device helper slot_position/position_slot pair is the inverse of oracle.marlin_scales.logical_column."""
+    pos = np.arange(128)
+    slot = marlin_scales.logical_column(pos)  # slot within the 128-run of each position
+    inv = np.empty(128, dtype=np.int64)
+    inv[slot] = pos
+    # restate the device arithmetic of moek_common.cuh in Python
+    def slot_position(s):
+        c = s & 63
+        m = 8 * (c & 7) + (c >> 3)
+        r = m & 3
+        return (s & 64) | (m & ~3) | (2 if r == 1 else 1 if r == 2 else r)
+
+    assert all(slot_position(s) == inv[s] for s in range(128))
+
+
+def test_prepared_layer_bytes():
+    w13 = synth.make_experts(4, 512, 256, 1)
+    w2 = synth.make_experts(4, 256, 256, 2)
+    layer = prep.PreparedLayer(w13, w2)
+    per = layer.expert_bytes()
+    assert per.shape == (4,)
+    total = layer.w13.nbytes() + layer.w2.nbytes()
+    assert abs(int(per.sum()) - total) <= 8 * 4  # offsets: E*keys + 1 per matrix
+
+
+def test_unsupported_shapes_raise():
+    with pytest.raises(ValueError):
+        prep.check_shapes(300, 256, False)
+    with pytest.raises(ValueError):
+        prep.check_shapes(512, 200, True)
