@@ -97,9 +97,28 @@ def kit_semantics(x, topk_ids, topk_w, w13, w2, return_act=False):
     return (out, act, dout) if return_act else out
 
 
+def half_ulp_bf16(r: torch.Tensor) -> torch.Tensor:
+    """Half a bf16 ulp at each value of r: the largest error a correctly rounded bf16 copy of r can have."""
+    a = r.float().abs().clamp_min(2.0 ** -126)
+    e = torch.floor(torch.log2(a))
+    return torch.pow(2.0, e - 8)
+
+
 def check(out: torch.Tensor, ref: torch.Tensor):
-    """(rel-L2, max-abs / rms) of ``out`` against ``ref``: the parity gate is rel <= 5e-3 and ratio <= 2e-2."""
+    """(rel-L2, max-abs / rms, net max-abs / rms) of a bf16 ``out`` against the fp32 ``ref``.
+
+    The parity gate is rel-L2 <= 5e-3 and net <= 2e-2, where net = max(|out - ref| - half_ulp_bf16(ref)) / rms: the
+    max-abs bound applied beyond the rounding of the output to bf16 itself. Without that allowance the bound is
+    tighter than half an ulp at the largest outputs (a bf16 copy of the oracle itself measures up to ~1.9e-2 at
+    M=700), so it would reject a correctly rounded result of the oracle."""
     o, r = out.float(), ref.float()
     rel = float((o - r).norm() / r.norm().clamp_min(1e-30))
     rms = float(r.pow(2).mean().sqrt().clamp_min(1e-30))
-    return rel, float((o - r).abs().max()) / rms
+    d = (o - r).abs()
+    net = float((d - half_ulp_bf16(r)).clamp_min(0).max()) if d.numel() else 0.0
+    return rel, float(d.max()) / rms if d.numel() else 0.0, net / rms
+
+
+def within_gate(out: torch.Tensor, ref: torch.Tensor, rel_gate=5e-3, max_gate=2e-2):
+    rel, raw, net = check(out, ref)
+    return rel <= rel_gate and net <= max_gate, (rel, raw, net)

@@ -74,7 +74,7 @@ MOEK_API int moek_align(const int32_t* topk_ids, int64_t numel, int32_t num_expe
     return fail(MOEK_ERR_ARG, "moek_b200: moe_align outputs too small (sorted %lld < %lld or expert_ids %lld)",
                 (long long)sorted_len, (long long)need, (long long)expert_len);
   if (numel > INT32_MAX / 2) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_align numel too large");
-  if (!sorted_ids || !expert_ids || !num_post_pad || (numel && !topk_ids))
+  if ((sorted_len && !sorted_ids) || (expert_len && !expert_ids) || !num_post_pad || (numel && !topk_ids))
     return fail(MOEK_ERR_ARG, "moek_b200: moe_align null pointer");
   const size_t ws = moek::align_workspace_bytes(numel, num_experts);
   if (ws > workspace_bytes || (ws && !workspace))

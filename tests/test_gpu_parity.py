@@ -14,7 +14,7 @@ from qwen38_flash_coder_b200 import ops, prep, synth
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-REL, MAXABS = 5e-3, 2e-2
+REL, MAXABS = 5e-3, 2e-2  # rel-L2, and max-abs / rms beyond the bf16 rounding of the output (oracle.moe_ref.check)
 
 
 def _np(t):
@@ -41,9 +41,9 @@ def _run_and_check(w13, w2, x, ids, wts, rel_gate=REL, max_gate=MAXABS):
     ops.check_device_errors(x.device)
     c13, c2, cids = _compact(w13, w2, ids)
     ref = moe_ref.reference(x.cpu(), cids, _np(wts), c13, c2)
-    rel, mx = moe_ref.check(out.cpu(), ref)
+    ok, stats = moe_ref.within_gate(out.cpu(), ref, rel_gate, max_gate)
     assert torch.isfinite(out).all()
-    assert rel <= rel_gate and mx <= max_gate, (rel, mx)
+    assert ok, stats
     return out, layer
 
 
@@ -88,8 +88,8 @@ def test_layer_matches_reference_golden(golden):
     wts = torch.from_numpy(golden["moe_wts"]).to(DEV)
     out = ops.fused_moe(x, prep.PreparedLayer(w13, w2), wts, ids)
     ops.check_device_errors(DEV)
-    rel, mx = moe_ref.check(out.cpu(), torch.from_numpy(golden["moe_out"]))
-    assert rel <= REL and mx <= MAXABS, (rel, mx)
+    ok, stats = moe_ref.within_gate(out.cpu(), torch.from_numpy(golden["moe_out"]))
+    assert ok, stats
 
 
 def test_config1_cpu_reference_case():

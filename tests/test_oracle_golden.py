@@ -68,7 +68,7 @@ def test_moe_reference_matches_problem_reference(golden):
     w2 = (golden["mw2_codes"], golden["mw2_scales"], golden["mw2_gs"])
     out = moe_ref.reference(x, golden["moe_ids"], golden["moe_wts"], w13, w2)
     ref = torch.from_numpy(golden["moe_out"])
-    rel, _ = moe_ref.check(out, ref)
+    rel, _, _ = moe_ref.check(out, ref)
     assert rel < 1e-5, rel
 
 
@@ -80,11 +80,19 @@ def test_rounding_points(golden):
     w2 = (golden["mw2_codes"], golden["mw2_scales"], golden["mw2_gs"])
     ref = torch.from_numpy(golden["moe_out"])
     kit = moe_ref.kit_semantics(x, golden["moe_ids"], golden["moe_wts"], w13, w2)
-    rel, _ = moe_ref.check(kit, ref)
+    rel, _, _ = moe_ref.check(kit, ref)
     assert rel <= 1e-2, rel
     mine = moe_ref.reference(x, golden["moe_ids"], golden["moe_wts"], w13, w2).to(torch.bfloat16)
-    rel, mx = moe_ref.check(mine, ref)
-    assert rel <= 5e-3 and mx <= 2e-2, (rel, mx)
+    ok, stats = moe_ref.within_gate(mine, ref)
+    assert ok and stats[2] == 0.0, stats  # a correctly rounded oracle has no error beyond half an ulp
+
+
+def test_gate_net_of_output_rounding():
+    r = torch.tensor([1.0, 3.0, 7.9, -6.0, 0.01])
+    assert moe_ref.check(r.to(torch.bfloat16), r)[2] == 0.0
+    bad = r.clone()
+    bad[2] += 1.0
+    assert moe_ref.check(bad, r)[2] > 0.2
 
 
 def test_align_docstring_example(golden):
