@@ -148,6 +148,41 @@ def cpu_baseline(layers, xs, routes, budget_s=12.0):
                       f"torch-CPU oracle (oracle/moe_ref.py), {tot:.1f} s of compute"}
 
 
+def make_graph(fn, warmup):
+    """Warm up on a side stream, then capture one call of fn in a CUDA graph."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(max(3, warmup)):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def timed(fn, steps, barrier):
+    """ms per call of fn over ``steps`` calls: barrier + synchronize on both sides, CUDA events on the stream."""
+    import torch
+
+    fn()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    return e0.elapsed_time(e1) / steps
+
+
 def main():
     a = parse()
     import torch
@@ -191,22 +226,11 @@ def main():
         if world > 1:
             torch.distributed.barrier()
 
-    for _ in range(max(3, a.warmup)):
-        step()
-    torch.cuda.synchronize()
+    graph = make_graph(step, a.warmup)
     ops.check_device_errors(dev)
     clocks = Clocks(local)
-    barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(a.steps):
-        step()
-    ev1.record()
-    torch.cuda.synchronize()
-    barrier()
+    ms = timed(graph.replay, a.steps, barrier)
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1) / a.steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -218,27 +242,34 @@ def main():
         total_bytes = step_bytes
     value = total_bytes / (ms / 1e3) / 1e9
 
-    # --- roofline of the dominant kernel (the gate_up grouped GEMM), CUDA events on its launching stream
-    gk = ops.profile_kernels(lambda: step(), names=("gate_gemm", "down_gemm"))
+    # --- roofline of the dominant kernel (the gate_up grouped GEMM): a graph of the step's gate_up launches alone,
+    # CUDA events on the stream that replays it
+    rec = ops.record_launches(step)
+    kern_us = {}
+    for name in ("gate_gemm", "down_gemm"):
+        fns = [f for n, f in rec if n == name]
+        g = make_graph(lambda: [f() for f in fns], 2)
+        kern_us[name] = timed(g.replay, a.steps, barrier) * 1e3 / len(fns)
+        del g
     gb = sum(gate_bytes(layers[l][2], routes[l][0], m) for l in range(nl)) / nl
     peaks = {}
     pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pp):
         peaks = json.load(open(pp))
     peak = peaks.get("hbm_gbs", 6650.0)
-    g_avg_ms = gk["gate_gemm"]
-    achieved = gb / (g_avg_ms / 1e3) / 1e9
+    achieved = gb / (kern_us["gate_gemm"] / 1e6) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         traffic = json.load(open(tp)).get(f"gate_gemm_{a.workload}")
     roof = {"kernel": "moek_decode_kernel (gate_up)", "bound": "hbm", "achieved": round(achieved, 1),
-            "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": traffic,
-            "bytes_per_launch": int(gb), "avg_launch_us": round(g_avg_ms * 1e3, 2),
-            "down_gemm_avg_us": round(gk["down_gemm"] * 1e3, 2)}
+            "peak": peak, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
+            else "fallback 6650", "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+            "bytes_per_launch": int(gb), "avg_launch_us": round(kern_us["gate_gemm"], 2),
+            "down_gemm_avg_us": round(kern_us["down_gemm"], 2)}
 
-    # --- e2e: public API, inputs from pinned host memory, outputs read back, inside the timed region
+    # --- e2e: the public API (fused_moe) with each step's inputs copied from pinned host memory and its outputs
+    # read back, all inside the timed region (one CUDA graph per step, as vLLM runs decode)
     hx = [x.cpu().pin_memory() for x in xs]
     hid = [r[0].cpu().pin_memory() for r in routes]
     hw = [r[1].cpu().pin_memory() for r in routes]
@@ -255,16 +286,8 @@ def main():
             ops.fused_moe(dx[l], layers[l][2], dw[l], did[l], output=outs[l])
             hout[l].copy_(outs[l], non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    barrier()
-    torch.cuda.synchronize()
-    ev0.record()
-    for _ in range(a.steps):
-        e2e_step()
-    ev1.record()
-    torch.cuda.synchronize()
-    ems = ev0.elapsed_time(ev1) / a.steps
+    eg = make_graph(e2e_step, 2)
+    ems = timed(eg.replay, a.steps, barrier)
     if world > 1:
         t = torch.tensor([ems], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -272,7 +295,8 @@ def main():
     h2d = sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4 for x, r, w in zip(hx, hid, hw))
     d2h = sum(o.numel() * 2 for o in hout)
     e2e = {"value": round(total_bytes / (ems / 1e3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 4)}
+           "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 4), "api": "ops.fused_moe, CUDA graph per step"}
+    eager_ms = timed(step, max(2, a.steps // 4), barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -292,6 +316,7 @@ def main():
             "touched_experts_per_layer": round(sum(t for _, t in per_layer) / nl, 1),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": ops.LAUNCHES_PER_LAYER * nl * a.steps,
+            "eager_ms_per_step": round(eager_ms, 4),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -65,19 +65,27 @@ int moek_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int3
  *   S       must be NULL (plain Marlin scales go with Marlin's untiled weight layout, which this build does not use);
  *           tiled must be 1.
  *   mode    2: split-k; the kernel writes fp32 partial sums part[nsplit][num_ids][N] (gate_up: gate at column c, up
- *           at N/2 + c) and moek_split_epilogue finishes. (The reference's modes 0/1 are not available.)
- *   nsplit  K/64/nsplit must be even (whole packed-scale runs).
- *   cnt     int32 [>= 4]; cnt[0] is the device error word (MOEK_DEV_*), left as is when nothing goes wrong.
+ *           at N/2 + c) and moek_split_epilogue finishes (the reference's mode 2).
+ *           3: the epilogue is fused. nsplit 1: gate_up writes act bf16 [num_ids, N/2] = bf16(silu(g) * u) to out;
+ *           down writes fp32 rows topk_w[id] * sum to part [num_ids, N] (finish with moek_combine). nsplit > 1:
+ *           the unit that completes an item (arrival counters in cnt[1..]) adds the partials in split order;
+ *           gate_up writes act to out, down writes out bf16 [num_ids/combine_k, N] = the top-k sum over each
+ *           token's combine_k slots (slots whose topk_ids entry is outside [0, E) are left out).
+ *           (The reference's modes 0/1, its atomic item counter and stream-k, are not available.)
+ *   nsplit  K/64/nsplit must be even (whole packed-scale runs), K/128/nsplit <= 32.
+ *   cnt     int32, zero-filled before the first call; cnt[0] is the device error word (MOEK_DEV_*), cnt[1..] the
+ *           split counters (mode 3, nsplit > 1: gate_up 1 + blocks * N/256, down 1 + N/256 entries), which every
+ *           completed launch leaves at zero.
  *   block_m the block size moek_align used; max_rows >= the most valid rows of any block (min(M, block_m) for top-k
  *           routing with distinct experts per token), <= 96.
  * The weights are dequantised exactly as the fp32 oracle does (bench/moek/problem.py:31-38: bf16(e2m1 * s * gs)),
- * products summed in fp32. topk_w and out are unused in mode 2 (kept for the reference's argument list). */
+ * products summed in fp32. topk_w, out, topk_ids and combine_k are unused in mode 2. */
 int moek_gemm(const void* A, const void* W, const void* S, const float* G, const int32_t* sorted_ids,
               int64_t sorted_len, const int32_t* expert_ids, const int32_t* num_post_pad, const float* topk_w,
               void* out, int32_t num_ids, int32_t N, int32_t K, int32_t E, int32_t top_k, int32_t gate_up,
               const uint8_t* SP, const int32_t* exc_off, const int32_t* exc_ent, int32_t* cnt, int64_t cnt_len,
               int32_t mode, int32_t nsplit, float* part, int64_t part_len, int32_t tiled, int32_t block_m,
-              int32_t max_rows, void* stream);
+              int32_t max_rows, const int32_t* topk_ids, int32_t combine_k, void* stream);
 
 /* Split-k epilogue: replaces the kit's moe_split_epilogue (files/mbx_moek.cu:797-851). Adds the nsplit partials in
  * split order (deterministic), then

@@ -90,9 +90,7 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
                        int32_t top_k, int32_t gate_up, const uint8_t* SP, const int32_t* exc_off,
                        const int32_t* exc_ent, int32_t* cnt, int64_t cnt_len, int32_t mode, int32_t nsplit,
                        float* part, int64_t part_len, int32_t tiled, int32_t block_m, int32_t max_rows,
-                       void* stream) {
-  (void)topk_w;
-  (void)out;
+                       const int32_t* topk_ids, int32_t combine_k, void* stream) {
   if (num_ids == 0) return MOEK_OK;  // empty batch
   if (num_ids < 0 || N <= 0 || K <= 0 || E <= 0 || block_m <= 0)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm bad sizes (num_ids %d, N %d, K %d, E %d, block %d)", num_ids, N,
@@ -105,17 +103,29 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
     return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm null pointer");
   if (!gate_up && top_k != 1) return fail(MOEK_ERR_ARG, "moek_b200: down reads one activation row per id (top_k 1)");
   if (top_k <= 0) return fail(MOEK_ERR_ARG, "moek_b200: top_k must be positive");
-  if (mode != 2) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build", mode);
+  if (mode != 2 && mode != 3)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (2 or 3)", mode);
   const int nstage = K / moek::BK;
   if (nsplit < 1 || nstage % nsplit || (nstage / nsplit) % moek::STAGES_PER_RUN)
     return fail(MOEK_ERR_ARG, "moek_b200: nsplit %d must cut K/128 = %d into whole runs", nsplit, K / 128);
-  if (!part || part_len < (int64_t)nsplit * num_ids * N)
-    return fail(MOEK_ERR_ARG, "moek_b200: split partials need %lld floats", (long long)nsplit * num_ids * N);
+  if (K / 128 / nsplit > 32)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: at most 32 packed-scale runs (4096 k) per split (K %d, nsplit %d)",
+                K, nsplit);
+  const bool fused = mode == 3, direct = fused && nsplit == 1;
+  const int64_t part_need = direct ? (gate_up ? 0 : (int64_t)num_ids * N) : (int64_t)nsplit * num_ids * N;
+  if (part_need && (!part || part_len < part_need))
+    return fail(MOEK_ERR_ARG, "moek_b200: part needs %lld floats", (long long)part_need);
   if (max_rows <= 0 || max_rows > 96)
     return fail(MOEK_ERR_ARG, "moek_b200: max_rows %d must be in [1, 96]", max_rows);
-  if (!cnt || cnt_len < 4) return fail(MOEK_ERR_ARG, "moek_b200: cnt must hold >= 4 int32 (error word at cnt[0])");
   const int64_t maxb = std::min<int64_t>(sorted_len / block_m, (num_ids + block_m - 1) / block_m +
                                                                    std::min<int64_t>(E, num_ids));
+  const int64_t cnt_need = fused && !direct ? 1 + (gate_up ? maxb * (N / 256) : N / 256) : 1;
+  if (!cnt || cnt_len < std::max<int64_t>(4, cnt_need))
+    return fail(MOEK_ERR_ARG, "moek_b200: cnt needs %lld int32 (error word + split counters, zero-filled)",
+                (long long)std::max<int64_t>(4, cnt_need));
+  if (fused && gate_up && !out) return fail(MOEK_ERR_ARG, "moek_b200: mode 3 gate_up writes act to out");
+  if (fused && !gate_up && (!topk_w || (!direct && (!out || !topk_ids || combine_k <= 0 || num_ids % combine_k))))
+    return fail(MOEK_ERR_ARG, "moek_b200: mode 3 down needs topk_w (and out, topk_ids, combine_k when split)");
   moek::GemmParams p{};
   p.A = static_cast<const __nv_bfloat16*>(A);
   p.W = static_cast<const uint8_t*>(W);
@@ -128,6 +138,12 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
   p.exc_ent = reinterpret_cast<const uint32_t*>(exc_ent);
   p.part = part;
   p.err = cnt;
+  p.counters = cnt + 1;
+  p.topk_ids = topk_ids;
+  p.topk_w = topk_w;
+  p.out = out;
+  p.mode = mode;
+  p.combine_k = combine_k;
   p.timeout_ns = g_timeout_ns;
   p.num_ids = num_ids;
   p.N = N;

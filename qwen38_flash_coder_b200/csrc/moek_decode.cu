@@ -36,14 +36,32 @@ namespace moek {
 
 constexpr int DC_WARPS = 8, DC_THREADS = DC_WARPS * 32 + 32;
 constexpr int X_STRIDE = 144;  // bytes per activation row in a slot (128 + 16: conflict-free 16-byte reads)
+constexpr int MAXU = 64;       // units per metadata round
+constexpr int MAXRUN = 32;     // packed-scale runs per unit (K / 128 / nsplit)
+constexpr int EXC_POOL = 1024; // exception entries cached in shared memory per round
+
+// Per-unit metadata, gathered by the producer warp once per round (MAXU units) so that no consumer waits on a global
+// load inside the stage loop.
+struct UnitMeta {
+  int blk, item, ks, e, nv, flags;  // flags: 1 = exception list read from global, 2 = block has more rows than XR
+  float g;                           // the expert's global scale
+  int exc_g0;                        // global index of the unit's first exception entry
+  int exc_s0;                        // shared-pool index of the unit's first entry (flags & 1 == 0)
+  int run_off[MAXRUN + 1];           // entry offsets, relative to the first, at each run boundary
+};
 
 template <int XR>
 struct DecodeCfg {
   static constexpr int SLOT = STAGE_BYTES + PAIR_BYTES + XR * X_STRIDE;
-  static constexpr int NS = (XR <= 8 ? 10 : XR <= 16 ? 8 : XR <= 32 ? 6 : 4);
-  static constexpr int BAR_OFF = NS * SLOT;
-  static constexpr int SMEM = BAR_OFF + 2 * NS * 8;
+  static constexpr int NS = XR <= 8 ? 8 : XR <= 16 ? 6 : XR <= 32 ? 5 : 4;
+  static constexpr int META_OFF = NS * SLOT;
+  static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
+  static constexpr int POOL_OFF = IDS_OFF + MAXU * XR * 4;
+  static constexpr int RED_OFF = POOL_OFF + EXC_POOL * 4;
+  static constexpr int BAR_OFF = RED_OFF + 16;
+  static constexpr int SMEM = BAR_OFF + (2 * NS + 2) * 8;
   static constexpr int T = XR / 8;  // token tiles of 8 rows
+  static constexpr int MINB = XR <= 32 ? 2 : 1;
 };
 
 __device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -53,20 +71,16 @@ __device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-
-struct Unit {
-  int blk, item, ks, e;
-};
-__device__ __forceinline__ Unit unit_of(const GemmParams& p, int64_t u, int nt) {
-  Unit r;
-  const int per = nt * p.nsplit;
-  r.blk = (int)(u / per);
-  const int rem = (int)(u - (int64_t)r.blk * per);
-  r.item = rem / p.nsplit;
-  r.ks = rem - r.item * p.nsplit;
-  r.e = p.expert_ids[r.blk];
-  return r;
+// Bounded wait honouring the CTA-wide abort flag: once any thread of the CTA gave up, every later wait fails at once,
+// so all warps keep their control flow (and the named barriers) in step and the kernel ends.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err,
+                                              volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (mbar_wait(bar, parity, deadline, err)) return true;
+  *abort_flag = 1;
+  return false;
 }
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(DC_WARPS * 32) : "memory"); }
 
 // Item slot -> output column of the N-wide weight matrix
 __device__ __forceinline__ int slot_column(const GemmParams& p, int item, int slot) {
@@ -75,70 +89,125 @@ __device__ __forceinline__ int slot_column(const GemmParams& p, int item, int sl
 }
 
 template <int XR>
-__global__ void __launch_bounds__(DC_THREADS, 1) moek_decode_kernel(GemmParams p) {
+__global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_kernel(GemmParams p) {
   using C = DecodeCfg<XR>;
   extern __shared__ __align__(128) uint8_t smem[];
+  UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);
+  int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);
+  uint32_t* pool = reinterpret_cast<uint32_t*>(smem + C::POOL_OFF);
+  volatile int* red = reinterpret_cast<volatile int*>(smem + C::RED_OFF);  // [0] last-arriver flag, [1] abort
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::NS;
+  uint64_t* mfull = empty + C::NS;  // a round's metadata is published (32 producer lanes arrive)
+  uint64_t* mempty = mfull + 1;     // a round's units are all consumed (one arrive per consumer warp)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nt = p.N / ITEM_COLS, nstage = p.K / BK, nb = p.K / 128;
-  const int su = nstage / p.nsplit;  // stages per unit
+  const int su = nstage / p.nsplit, nruns = su / 2;
   if (tid == 0) {
+    red[1] = 0;
     for (int i = 0; i < C::NS; i++) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, DC_WARPS);
     }
+    mbar_init(mfull, 32);
+    mbar_init(mempty, DC_WARPS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int nblocks = min(p.num_post_pad[0] / p.block_m, p.max_blocks);
   const int64_t nunits = (int64_t)nblocks * nt * p.nsplit;
+  const int n_mine = nunits > blockIdx.x ? (int)((nunits - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  const int rounds = (n_mine + MAXU - 1) / MAXU;
 
   if (warp == DC_WARPS) {  // ------------------------------------------------------------------ producer
     uint32_t g = 0;
-    bool ok = true;
-    for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
-      const Unit un = unit_of(p, u, nt);
-      if (un.e < 0 || un.e >= p.E) continue;  // reported by the consumers
-      // valid rows are a prefix of the block: count them once per unit
-      int nv = 0;
-      for (int r0 = 0; r0 < XR; r0 += 32) {
-        const int r = r0 + lane;
-        const bool v = r < XR && r < p.block_m && p.sorted_ids[(int64_t)un.blk * p.block_m + r] < p.num_ids;
-        nv += __popc(__ballot_sync(0xffffffffu, v));
-      }
-      for (int st = un.ks * su; st < (un.ks + 1) * su; st++, g++) {
-        const int slot = g % C::NS;
-        if (g >= C::NS && !mbar_wait(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err)) { ok = false; break; }
-        uint8_t* dst = smem + slot * C::SLOT;
-        if (lane == 0) mbar_expect_tx(full + slot, STAGE_BYTES + PAIR_BYTES + nv * BK * 2);
-        __syncwarp();
-        if (lane == 0) {
-          const int64_t wi = ((int64_t)un.e * nt + un.item) * nstage + st;
-          bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
-          const int64_t si = ((int64_t)un.e * nt + un.item) * nb + (st >> 1);
-          bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+    for (int r = 0; r < rounds; r++) {
+      const int u0 = r * MAXU, nu = min(MAXU, n_mine - u0);
+      if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, red + 1)) return;
+      // units, experts, row ids (valid rows are a prefix of a block)
+      for (int i = lane; i < nu; i += 32) {
+        const int64_t u = blockIdx.x + (int64_t)(u0 + i) * gridDim.x;
+        const int per = nt * p.nsplit;
+        UnitMeta& m = meta[i];
+        m.blk = (int)(u / per);
+        const int rem = (int)(u - (int64_t)m.blk * per);
+        m.item = rem / p.nsplit;
+        m.ks = rem - m.item * p.nsplit;
+        m.e = p.expert_ids[m.blk];
+        const int lim = min(XR, p.block_m);
+        const int64_t row0 = (int64_t)m.blk * p.block_m;
+        int nv = 0;
+        for (int rr = 0; rr < lim; rr++) {
+          const int id = p.sorted_ids[row0 + rr];
+          mids[i * XR + rr] = id;
+          nv += id < p.num_ids;
         }
-        for (int r = lane; r < nv; r += 32) {
-          const int id = p.sorted_ids[(int64_t)un.blk * p.block_m + r];
-          const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + st * BK;
-          bulk_g2s(dst + STAGE_BYTES + PAIR_BYTES + r * X_STRIDE, src, BK * 2, full + slot);
+        m.nv = nv;
+        m.flags = (lim < p.block_m && p.sorted_ids[row0 + lim] < p.num_ids) ? 2 : 0;
+      }
+      __syncwarp();
+      // global scales and exception-list bounds
+      for (int i = lane; i < nu; i += 32) {
+        UnitMeta& m = meta[i];
+        const bool valid = m.e >= 0 && m.e < p.E;
+        m.g = valid ? p.G[m.e] : 0.f;
+        const int64_t key0 = ((int64_t)(valid ? m.e : 0) * nt + m.item) * nb + (int64_t)m.ks * nruns;
+        const int o0 = valid ? p.exc_off[key0] : 0;
+        m.exc_g0 = o0;
+        for (int j = 0; j <= nruns; j++) m.run_off[j] = valid ? p.exc_off[key0 + j] - o0 : 0;
+      }
+      __syncwarp();
+      if (lane == 0) {  // pool places; a unit whose list does not fit reads it from global memory
+        int used = 0;
+        for (int i = 0; i < nu; i++) {
+          const int n = meta[i].run_off[nruns];
+          if (used + n <= EXC_POOL) {
+            meta[i].exc_s0 = used;
+            used += n;
+          } else {
+            meta[i].flags |= 1;
+          }
         }
       }
-    }
-    // wind down: wait (bounded) until the consumers released every slot still in flight
-    if (!ok) return;
-    for (uint32_t i = 0; i < C::NS && i < g; i++) {
-      const uint32_t gg = g - 1 - i;
-      if (!mbar_wait(empty + gg % C::NS, (gg / C::NS) & 1, deadline, p.err)) return;
+      __syncwarp();
+      for (int i = 0; i < nu; i++) {
+        if (meta[i].flags & 1) continue;
+        const int n = meta[i].run_off[nruns], s0 = meta[i].exc_s0, g0 = meta[i].exc_g0;
+        for (int j = lane; j < n; j += 32) pool[s0 + j] = p.exc_ent[g0 + j];
+      }
+      __syncwarp();
+      mbar_arrive(mfull);
+      // stream the round's stages
+      for (int i = 0; i < nu; i++) {
+        const int e = meta[i].e, item = meta[i].item, ks = meta[i].ks, nv = meta[i].nv;
+        if (e < 0 || e >= p.E) continue;
+        for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
+          const int slot = g % C::NS;
+          if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, red + 1)) return;
+          uint8_t* dst = smem + slot * C::SLOT;
+          if (lane == 0) mbar_expect_tx(full + slot, STAGE_BYTES + PAIR_BYTES + nv * BK * 2);
+          __syncwarp();
+          if (lane == 0) {
+            const int64_t wi = ((int64_t)e * nt + item) * nstage + st;
+            bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
+            const int64_t si = ((int64_t)e * nt + item) * nb + (st >> 1);
+            bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+          }
+          for (int rr = lane; rr < nv; rr += 32) {
+            const int id = mids[i * XR + rr];
+            const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + st * BK;
+            bulk_g2s(dst + STAGE_BYTES + PAIR_BYTES + rr * X_STRIDE, src, BK * 2, full + slot);
+          }
+        }
+      }
     }
     return;
   }
 
   // -------------------------------------------------------------------------------------------- consumers
   const int gq = lane >> 2, c = lane & 3;
-  // the warp's two 16-row groups of the item
+  // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
   const int G0 = p.gate_up ? warp : 2 * warp, G1 = p.gate_up ? warp + 8 : 2 * warp + 1;
   int slots[2][2], pos[2][2];
 #pragma unroll
@@ -148,124 +217,193 @@ __global__ void __launch_bounds__(DC_THREADS, 1) moek_decode_kernel(GemmParams p
       slots[i][h] = 16 * (i ? G1 : G0) + gq + 8 * h;
       pos[i][h] = slot_position(slots[i][h]);
     }
+  const int I = p.N / 2;
   uint32_t g = 0;
-  for (int64_t u = blockIdx.x; u < nunits; u += gridDim.x) {
-    const Unit un = unit_of(p, u, nt);
-    if (un.e < 0 || un.e >= p.E) {
-      if (lane == 0 && warp == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
-      continue;
-    }
-    const float gsc = p.G[un.e];
-    int nv = 0;
-    for (int r0 = 0; r0 < XR; r0 += 32) {
-      const int r = r0 + lane;
-      const bool v = r < XR && r < p.block_m && p.sorted_ids[(int64_t)un.blk * p.block_m + r] < p.num_ids;
-      nv += __popc(__ballot_sync(0xffffffffu, v));
-    }
-    if (XR < p.block_m && lane == 0 && warp == 0 &&
-        p.sorted_ids[(int64_t)un.blk * p.block_m + XR] < p.num_ids)
-      report(p.err, MOEK_DEV_TOO_MANY_ROWS);  // more rows than this instantiation holds: the host chose too small
-    const int ntile = (nv + 7) >> 3;
-    float acc[2][C::T][4];
-#pragma unroll
-    for (int i = 0; i < 2; i++)
-#pragma unroll
-      for (int t = 0; t < C::T; t++)
-#pragma unroll
-        for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
-
-    bool ok = true;
-    for (int st = un.ks * su; st < (un.ks + 1) * su; st++, g++) {
-      const int slot = g % C::NS;
-      if (!mbar_wait(full + slot, (g / C::NS) & 1, deadline, p.err)) { ok = false; break; }
-      const uint8_t* sw = smem + slot * C::SLOT;
-      const uint8_t* ss = sw + STAGE_BYTES;
-      const uint8_t* sx = ss + PAIR_BYTES;
-      const int kg_run = (st & 1) * 4 + c;  // this lane's k-group inside the run
-      uint32_t sb[2][2];
+  for (int r = 0; r < rounds; r++) {
+    const int nu = min(MAXU, n_mine - r * MAXU);
+    wait_or_abort(mfull, r & 1, deadline, p.err, red + 1);
+    consumer_sync();  // one decision for all consumer warps
+    const bool have_meta = !red[1];
+    for (int ui = 0; ui < nu; ui++) {
+      const UnitMeta& m = meta[ui];
+      if (!have_meta) break;  // aborted: nothing was published (uniform across the consumer warps)
+      const int e = m.e, item = m.item, ks = m.ks, nv = m.nv, blk = m.blk, flags = m.flags;
+      const int* ids = mids + ui * XR;
+      if (e < 0 || e >= p.E) {
+        if (tid == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
+        continue;
+      }
+      if ((flags & 2) && tid == 0) report(p.err, MOEK_DEV_TOO_MANY_ROWS);
+      const float gsc = m.g;
+      const uint32_t* exc = (flags & 1) ? p.exc_ent + m.exc_g0 : pool + m.exc_s0;
+      const int ntile = (nv + 7) >> 3;
+      const int r0g = p.gate_up ? item : 2 * item;  // global run index of the pair's first run
+      float acc[2][C::T][4];
 #pragma unroll
       for (int i = 0; i < 2; i++)
 #pragma unroll
-        for (int h = 0; h < 2; h++) sb[i][h] = run_byte(ss + (slots[i][h] >> 7) * RUN_BYTES, pos[i][h], kg_run);
-      // exceptions of this (expert, item, run)
-      {
-        const int64_t key = ((int64_t)un.e * nt + un.item) * nb + (st >> 1);
-        const int eo0 = p.exc_off[key], eo1 = p.exc_off[key + 1];
-        const int r0g = p.gate_up ? un.item : 2 * un.item;  // global run index of the pair's first run
-        for (int b0 = eo0; b0 < eo1; b0 += 32) {
-          uint32_t en = 0;
-          bool mine = false;
-          if (b0 + lane < eo1) {
-            en = p.exc_ent[b0 + lane];
-            const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-            const int rp = (ppos >> 7) == r0g ? 0 : 1;
-            const int slot_e = rp * 128 + position_slot(ppos & 127);
-            const int ge = slot_e >> 4;
-            const int we = p.gate_up ? (ge & 7) : (ge >> 1);
-            mine = (kg >> 2) == (st & 1) && we == warp;
-          }
-          unsigned m = __ballot_sync(0xffffffffu, mine);
-          while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const uint32_t e2 = __shfl_sync(0xffffffffu, en, src);
-            const int ppos = e2 & 0xFFFF, kg = (e2 >> 16) & 0xFF;
-            const int rp = (ppos >> 7) == r0g ? 0 : 1;
-            const int slot_e = rp * 128 + position_slot(ppos & 127);
-            const int ge = slot_e >> 4, row = slot_e & 15;
-            const int i = (ge == G0) ? 0 : 1;
-            if (gq == (row & 7) && c == (kg & 3)) sb[i][row >> 3] = e2 >> 24;
-          }
-        }
-      }
+        for (int t = 0; t < C::T; t++)
 #pragma unroll
-      for (int i = 0; i < 2; i++) {
-        const ScaleBR sa = scale_br(sb[i][0], gsc), sbv = scale_br(sb[i][1], gsc);
-        const uint4 q = *reinterpret_cast<const uint4*>(sw + ((i ? G1 : G0) * 32 + lane) * 16);
-        uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
-        dequant_word(q.x, sa, wa0);
-        dequant_word(q.y, sbv, wb0);
-        dequant_word(q.z, sa, wa1);
-        dequant_word(q.w, sbv, wb1);
-        const uint32_t A0[4] = {wa0[0], wb0[0], wa0[1], wb0[1]};
-        const uint32_t A1[4] = {wa0[2], wb0[2], wa0[3], wb0[3]};
-        const uint32_t A2[4] = {wa1[0], wb1[0], wa1[1], wb1[1]};
-        const uint32_t A3[4] = {wa1[2], wb1[2], wa1[3], wb1[3]};
+          for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
+
+      for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
+        const int slot = g % C::NS;
+        if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, red + 1)) continue;  // skip, stay in step
+        const uint8_t* sw = smem + slot * C::SLOT;
+        const uint8_t* ss = sw + STAGE_BYTES;
+        const uint8_t* sx = ss + PAIR_BYTES;
+        const int kg_run = (st & 1) * 4 + c;  // this lane's k-group inside the run
+        uint32_t sb[2][2];
 #pragma unroll
-        for (int t = 0; t < C::T; t++) {
-          if (t < ntile) {
-            const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
-            const uint4 x0 = *reinterpret_cast<const uint4*>(xr);
-            const uint4 x1 = *reinterpret_cast<const uint4*>(xr + 16);
-            mma_bf16_16816(acc[i][t], A0, x0.x, x0.y);
-            mma_bf16_16816(acc[i][t], A1, x0.z, x0.w);
-            mma_bf16_16816(acc[i][t], A2, x1.x, x1.y);
-            mma_bf16_16816(acc[i][t], A3, x1.z, x1.w);
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+          for (int h = 0; h < 2; h++) sb[i][h] = run_byte(ss + (slots[i][h] >> 7) * RUN_BYTES, pos[i][h], kg_run);
+        {  // exceptions of this run that fall in this stage and in this warp's rows
+          const int rr = (st - ks * su) >> 1;
+          const int eo0 = m.run_off[rr], eo1 = m.run_off[rr + 1];
+          for (int b0 = eo0; b0 < eo1; b0 += 32) {
+            uint32_t en = 0;
+            bool mine = false;
+            if (b0 + lane < eo1) {
+              en = exc[b0 + lane];
+              const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+              const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
+              const int ge = slot_e >> 4;
+              mine = (kg >> 2) == (st & 1) && (p.gate_up ? (ge & 7) : (ge >> 1)) == warp;
+            }
+            unsigned msk = __ballot_sync(0xffffffffu, mine);
+            while (msk) {
+              const int src = __ffs(msk) - 1;
+              msk &= msk - 1;
+              const uint32_t e2 = __shfl_sync(0xffffffffu, en, src);
+              const int ppos = e2 & 0xFFFF, kg = (e2 >> 16) & 0xFF;
+              const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
+              const int ge = slot_e >> 4, row = slot_e & 15;
+              if (gq == (row & 7) && c == (kg & 3)) sb[ge == G0 ? 0 : 1][row >> 3] = e2 >> 24;
+            }
           }
         }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + slot);
-    }
-    if (!ok) return;
-    // fp32 partials
-    float* base = p.part + (int64_t)un.ks * p.num_ids * p.N;
-#pragma unroll
-    for (int t = 0; t < C::T; t++) {
-      if (t >= ntile) break;
-#pragma unroll
-      for (int v = 0; v < 2; v++) {
-        const int r = t * 8 + 2 * c + v;
-        if (r >= nv) continue;
-        const int id = p.sorted_ids[(int64_t)un.blk * p.block_m + r];
-        float* row = base + (int64_t)id * p.N;
 #pragma unroll
         for (int i = 0; i < 2; i++) {
-          row[slot_column(p, un.item, slots[i][0])] = acc[i][t][v];
-          row[slot_column(p, un.item, slots[i][1])] = acc[i][t][2 + v];
+          const ScaleBR sa = scale_br(sb[i][0], gsc), sbv = scale_br(sb[i][1], gsc);
+          const uint4 q = *reinterpret_cast<const uint4*>(sw + ((i ? G1 : G0) * 32 + lane) * 16);
+          uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
+          dequant_word(q.x, sa, wa0);
+          dequant_word(q.y, sbv, wb0);
+          dequant_word(q.z, sa, wa1);
+          dequant_word(q.w, sbv, wb1);
+          const uint32_t A0[4] = {wa0[0], wb0[0], wa0[1], wb0[1]};
+          const uint32_t A1[4] = {wa0[2], wb0[2], wa0[3], wb0[3]};
+          const uint32_t A2[4] = {wa1[0], wb1[0], wa1[1], wb1[1]};
+          const uint32_t A3[4] = {wa1[2], wb1[2], wa1[3], wb1[3]};
+#pragma unroll
+          for (int t = 0; t < C::T; t++) {
+            if (t < ntile) {
+              const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
+              const uint4 x0 = *reinterpret_cast<const uint4*>(xr);
+              const uint4 x1 = *reinterpret_cast<const uint4*>(xr + 16);
+              mma_bf16_16816(acc[i][t], A0, x0.x, x0.y);
+              mma_bf16_16816(acc[i][t], A1, x0.z, x0.w);
+              mma_bf16_16816(acc[i][t], A2, x1.x, x1.y);
+              mma_bf16_16816(acc[i][t], A3, x1.z, x1.w);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+      }
+
+      // ---------------------------------------------------------------------------------------- epilogue
+      // acc[i][t][2h + v] = weight row slots[i][h] x block row 8t + 2c + v
+      if (p.mode == 3 && p.nsplit == 1) {
+#pragma unroll
+        for (int t = 0; t < C::T; t++) {
+          if (t >= ntile) break;
+#pragma unroll
+          for (int v = 0; v < 2; v++) {
+            const int row = t * 8 + 2 * c + v;
+            if (row >= nv) continue;
+            const int id = ids[row];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              if (p.gate_up) {  // gate slot and up slot + 128 share the column
+                const int col = 128 * item + slots[0][h];
+                static_cast<__nv_bfloat16*>(p.out)[(int64_t)id * I + col] =
+                    __float2bfloat16_rn(silu(acc[0][t][2 * h + v]) * acc[1][t][2 * h + v]);
+              } else {
+                const float w = p.topk_w[id];
+#pragma unroll
+                for (int i = 0; i < 2; i++)
+                  p.part[(int64_t)id * p.N + slot_column(p, item, slots[i][h])] = w * acc[i][t][2 * h + v];
+              }
+            }
+          }
+        }
+        continue;
+      }
+      float* base = p.part + (int64_t)ks * p.num_ids * p.N;
+#pragma unroll
+      for (int t = 0; t < C::T; t++) {
+        if (t >= ntile) break;
+#pragma unroll
+        for (int v = 0; v < 2; v++) {
+          const int row = t * 8 + 2 * c + v;
+          if (row >= nv) continue;
+          float* prow = base + (int64_t)ids[row] * p.N;
+#pragma unroll
+          for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) prow[slot_column(p, item, slots[i][h])] = acc[i][t][2 * h + v];
         }
       }
+      if (p.mode != 3) continue;
+      // split-k: the unit that completes an item adds the partials in split order (deterministic)
+      __threadfence();
+      consumer_sync();
+      if (tid == 0) {
+        int* ctr = p.gate_up ? p.counters + (int64_t)blk * nt + item : p.counters + item;
+        const int total = p.gate_up ? p.nsplit : nblocks * p.nsplit;
+        const int old = atomicAdd(ctr, 1);
+        const int last = old == total - 1;
+        if (last) *ctr = 0;  // every contribution is in: ready for the next launch
+        *red = last;
+      }
+      consumer_sync();
+      if (*red) {
+        __threadfence();
+        const int64_t stride = (int64_t)p.num_ids * p.N;
+        if (p.gate_up) {
+          for (int idx = tid; idx < nv * 128; idx += DC_WARPS * 32) {
+            const int row = idx >> 7, col = 128 * item + (idx & 127);
+            const float* pr = p.part + (int64_t)ids[row] * p.N;
+            float gs = 0.f, us = 0.f;
+            for (int s = 0; s < p.nsplit; s++) {
+              gs += __ldcg(pr + s * stride + col);
+              us += __ldcg(pr + s * stride + I + col);
+            }
+            static_cast<__nv_bfloat16*>(p.out)[(int64_t)ids[row] * I + col] = __float2bfloat16_rn(silu(gs) * us);
+          }
+        } else {
+          const int mtok = p.num_ids / p.combine_k;
+          for (int idx = tid; idx < mtok * 256; idx += DC_WARPS * 32) {
+            const int t = idx >> 8, col = 256 * item + (idx & 255);
+            float o = 0.f;
+            for (int j = 0; j < p.combine_k; j++) {
+              const int id = t * p.combine_k + j;
+              const int ej = p.topk_ids[id];
+              if (ej < 0 || ej >= p.E) continue;
+              float sum = 0.f;
+              for (int s = 0; s < p.nsplit; s++) sum += __ldcg(p.part + s * stride + (int64_t)id * p.N + col);
+              o += p.topk_w[id] * sum;
+            }
+            static_cast<__nv_bfloat16*>(p.out)[(int64_t)t * p.N + col] = __float2bfloat16_rn(o);
+          }
+        }
+      }
+      consumer_sync();
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(mempty);
   }
 }
 
@@ -356,7 +494,8 @@ static cudaError_t launch_decode_xr(const GemmParams& p, int grid, cudaStream_t 
 cudaError_t launch_decode(const GemmParams& p, int max_rows, int sms, cudaStream_t st) {
   const int nt = p.N / ITEM_COLS;
   const int64_t units = (int64_t)p.max_blocks * nt * p.nsplit;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, units));
+  const int per_sm = max_rows <= 32 ? 2 : 1;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)per_sm * sms, units));
   if (max_rows <= 8) return launch_decode_xr<8>(p, grid, st);
   if (max_rows <= 16) return launch_decode_xr<16>(p, grid, st);
   if (max_rows <= 32) return launch_decode_xr<32>(p, grid, st);

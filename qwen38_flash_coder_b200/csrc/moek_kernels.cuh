@@ -16,11 +16,15 @@ struct GemmParams {
   const uint8_t* SP;        // tiled packed scales [E, N/256, K/128, 1056]
   const int32_t* exc_off;   // [E * N/256 * K/128 + 1]
   const uint32_t* exc_ent;  // exception entries
-  float* part;              // [nsplit, num_ids, N]
-  int* err;
+  float* part;              // mode 2 / split: [nsplit, num_ids, N] fp32 partials; down, nsplit 1: fp32 rows
+  int* err;                 // device error word (cnt[0])
+  int* counters;            // split-k arrival counters (cnt[1..]), zero between launches
+  const int32_t* topk_ids;  // mode 3 down combine: [num_ids] (slots whose expert is invalid are left out)
+  const float* topk_w;      // [num_ids] router weights (down)
+  void* out;                // mode 3: gate_up -> act bf16 [num_ids, N/2]; down (split) -> bf16 [M, N] top-k sums
   uint64_t timeout_ns;
   int num_ids, N, K, E, a_div, block_m, nsplit, max_blocks;
-  int gate_up;
+  int gate_up, mode, combine_k;
 };
 
 // moek_align.cu

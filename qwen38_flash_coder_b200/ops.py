@@ -18,9 +18,9 @@ from ._lib import MoekError, call
 from .prep import PreparedLayer
 
 BM = 96  # moe_align block size (rows per block), as the kit (files/mbx_moek.py:33)
-LAUNCHES_PER_LAYER = 5  # align, gate_up GEMM, gate epilogue, down GEMM, down epilogue + top-k sum
+LAUNCHES_PER_LAYER = 3  # decode: align, gate_up GEMM (+SwiGLU), down GEMM (+router weight, top-k sum)
 _BUF: dict = {}
-_PROF = None  # when a list, fused_moe records (name, start event, end event) around its GEMM launches
+_PROF = None  # when a list, fused_moe appends (name, launch closure) for each of its GEMM launches
 
 
 def _ptr(t):
@@ -38,10 +38,11 @@ def _need_cuda(*ts):
 
 
 def error_word(dev) -> torch.Tensor:
-    """Per-device int32 [4]; [0] is the kernels' device error word (MOEK_DEV_*)."""
+    """Per-device int32 [65536], zero-filled (the size of the kit's cnt buffer, files/mbx_moek.py:179): [0] is the
+    kernels' device error word (MOEK_DEV_*), [1..] the split-k arrival counters, which every launch leaves at 0."""
     key = ("cnt", torch.device(dev))
     if key not in _BUF:
-        _BUF[key] = torch.zeros(4, dtype=torch.int32, device=dev)
+        _BUF[key] = torch.zeros(1 << 16, dtype=torch.int32, device=dev)
     return _BUF[key]
 
 
@@ -50,7 +51,7 @@ def check_device_errors(dev) -> None:
     w = error_word(dev)
     code = int(w[0].item())
     if code:
-        w.zero_()
+        w.zero_()  # an aborted launch may also have left split counters behind
         names = {1: "a bounded wait timed out", 2: "an expert id out of range", 3: "a block with more rows than "
                  "max_rows"}
         raise MoekError(f"moek_b200: device error {code}: {names.get(code, 'unknown')}")
@@ -114,7 +115,7 @@ def moe_gemm(A, W, S, G, sorted_ids, expert_ids, num_post_pad, topk_w, out, top_
     call("moek_gemm", _ptr(A), _ptr(W), None, _ptr(G), _ptr(sorted_ids), sorted_ids.numel(), _ptr(expert_ids),
          _ptr(num_post_pad), _ptr(topk_w), _ptr(out), num_ids, n, k, W.shape[0], top_k, int(bool(gate_up)), _ptr(SP),
          _ptr(exc_off), _ptr(exc_ent), _ptr(cnt), cnt.numel(), mode, nsplit, _ptr(part), part.numel(), int(tiled),
-         block_m, min(max_rows, 96), _stream(A.device))
+         block_m, min(max_rows, 96), None, 0, _stream(A.device))
 
 
 def moe_split_epilogue(part, nsplit: int, topk_ids, G, topk_w, out, gate_up: bool, N: int) -> None:
@@ -149,15 +150,18 @@ def combine(rows: torch.Tensor, top_k: int, out: torch.Tensor = None) -> torch.T
 
 
 # ----------------------------------------------------------------------------------------------------- forward
-def _splits(k: int, units_per_split: int, sms: int) -> int:
-    """Smallest k-split (whole 128-k runs per unit) giving at least 2 units per SM, else the finest."""
+DECODE_MAX_M = int(os.environ.get("MOEK_B200_DECODE_MAX_M", "64"))  # split-k with fused epilogues up to this M
+
+
+def _splits(k: int, units_per_split: int, target: int) -> int:
+    """Smallest k-split (whole 128-k runs per unit) giving at least ``target`` units, else the finest."""
     nstage = k // 64
     best = 1
     for d in range(1, nstage + 1):
         if nstage % d or (nstage // d) % 2:
             continue
         best = d
-        if units_per_split * d >= 2 * sms:
+        if units_per_split * d >= target:
             break
     return best
 
@@ -187,54 +191,52 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
     dev = x.device
     a, b = layer.w13, layer.w2
     ids32 = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
-    ids32 = ids32.contiguous()
+    ids32 = ids32.reshape(-1).contiguous()
     tw = topk_weights.reshape(-1).float().contiguous()
     sid, eid, npad = moe_align_block_size(ids32, BM, layer.E)
-    sms = _sms(dev)
-    est_blocks = min(layer.E, num_ids) if m <= BM else (num_ids + BM - 1) // BM + min(layer.E, num_ids)
-    ns1 = _splits(a.K, est_blocks * (a.N // 256), sms)
-    ns2 = _splits(b.K, est_blocks * (b.N // 256), sms)
-    part = _scratch("part", max(ns1 * num_ids * a.N, ns2 * num_ids * b.N), torch.float32, dev)
     cnt = error_word(dev)
     rows = min(BM, m)
-    _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, ns1, part, rows))
     act = torch.empty((num_ids, a.N // 2), dtype=torch.bfloat16, device=dev)
-    call("moek_split_epilogue", _ptr(part), ns1, num_ids, a.N, 1, None, top_k, _ptr(act), 0, _stream(dev))
-    _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, ns2, part, rows))
-    call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(output), 2, _stream(dev))
+    if m <= DECODE_MAX_M:
+        grid = (2 if rows <= 32 else 1) * _sms(dev)
+        blocks = min(layer.E, num_ids)
+        ns1 = _splits(a.K, blocks * (a.N // 256), 4 * grid)
+        ns2 = max(2, _splits(b.K, blocks * (b.N // 256), 4 * grid))
+        part = _scratch("part", max(ns1 * num_ids * a.N, ns2 * num_ids * b.N), torch.float32, dev)
+        _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, ns1, part, rows, act,
+                                          tw, ids32, top_k))
+        _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, ns2, part, rows, output,
+                                          tw, ids32, top_k))
+        return output
+    part = _scratch("part", num_ids * b.N, torch.float32, dev)
+    _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, 1, part, rows, act, tw, ids32,
+                                      top_k))
+    _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, 1, part, rows, None, tw, ids32,
+                                      top_k))
+    call("moek_combine", _ptr(part), 1, _ptr(output), m, b.N, top_k, _stream(dev))
     return output
 
 
-def _gemm(a_in, mat, sid, eid, npad, num_ids, a_div, gate_up, cnt, nsplit, part, rows):
-    call("moek_gemm", _ptr(a_in), _ptr(mat.w), None, _ptr(mat.g), _ptr(sid), sid.numel(), _ptr(eid), _ptr(npad), None,
-         None, num_ids, mat.N, mat.K, mat.E, a_div, int(gate_up), _ptr(mat.sp), _ptr(mat.exc_off), _ptr(mat.exc_ent),
-         _ptr(cnt), cnt.numel(), 2, nsplit, _ptr(part), part.numel(), 1, BM, rows, _stream(a_in.device))
+def _gemm(a_in, mat, sid, eid, npad, num_ids, a_div, gate_up, cnt, nsplit, part, rows, out, tw, ids32, combine_k):
+    call("moek_gemm", _ptr(a_in), _ptr(mat.w), None, _ptr(mat.g), _ptr(sid), sid.numel(), _ptr(eid), _ptr(npad),
+         _ptr(tw), _ptr(out), num_ids, mat.N, mat.K, mat.E, a_div, int(gate_up), _ptr(mat.sp), _ptr(mat.exc_off),
+         _ptr(mat.exc_ent), _ptr(cnt), cnt.numel(), 3, nsplit, _ptr(part), part.numel(), 1, BM, rows, _ptr(ids32),
+         combine_k, _stream(a_in.device))
 
 
 def _timed(name, fn):
-    if _PROF is None:
-        return fn()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    r = fn()
-    e1.record()
-    _PROF.append((name, e0, e1))
-    return r
+    if _PROF is not None:
+        _PROF.append((name, fn))
+    return fn()
 
 
-def profile_kernels(fn, names=("gate_gemm", "down_gemm"), reps: int = 3) -> dict:
-    """Average device time in ms of each named launch while ``fn`` runs ``reps`` times (CUDA events recorded on the
-    launching stream around each launch)."""
+def record_launches(fn) -> list:
+    """Run ``fn`` once and return the (name, closure) of every GEMM launch fused_moe made: replaying a closure
+    re-launches that kernel with the same arguments (bench.py times the GEMMs alone this way)."""
     global _PROF
     _PROF = []
     try:
-        for _ in range(reps):
-            fn()
-        torch.cuda.synchronize()
-        acc = {n: [] for n in names}
-        for n, e0, e1 in _PROF:
-            if n in acc:
-                acc[n].append(e0.elapsed_time(e1))
+        fn()
+        return list(_PROF)
     finally:
         _PROF = None
-    return {n: (sum(v) / len(v) if v else float("nan")) for n, v in acc.items()}

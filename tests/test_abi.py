@@ -40,7 +40,7 @@ def test_version_and_errors_without_gpu():
     rc = lib.moek_align(None, 10, 0, 96, None, 0, None, 0, None, None, 0, None)
     assert rc == 1 and b"num_experts" in lib.moek_last_error()
     rc = lib.moek_gemm(*([None] * 4), None, 0, None, None, None, None, 5, 300, 2048, 8, 5, 1, None, None, None, None,
-                       0, 2, 1, None, 0, 1, 96, 8, None)
+                       0, 2, 1, None, 0, 1, 96, 8, None, 0, None)
     assert rc == 1 and b"N % 256" in lib.moek_last_error()
     rc = lib.moek_set_wait_timeout_ns(0)
     assert rc == 1
