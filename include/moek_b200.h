@@ -58,6 +58,19 @@ int moek_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int3
                int64_t sorted_len, int32_t* expert_ids, int64_t expert_len, int32_t* num_post_pad, void* workspace,
                size_t workspace_bytes, void* stream);
 
+/* moe_align without a workspace argument, for callers that cannot allocate device memory on the path that calls
+ * it (a host runtime with a fixed memory plan, or a foreign-language binding that only passes the tensors it already
+ * owns). No counterpart in the reference. Same outputs as moek_align. Limits: numel <= 65536, num_experts <= 1024;
+ * larger calls are rejected with MOEK_ERR_ARG (use moek_align with a workspace). The scratch it needs for more than
+ * 1024 indices is a fixed 512 KiB array inside the library, held on every GPU that loads the library until the
+ * process exits, and shared by all calls on that GPU: calls that overlap on the GPU (two streams at once) race on
+ * it, so serialise them. It keeps the last call's contents, and nothing in it needs to start at zero (every call
+ * writes what it reads). The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * caches it; make that first call before any stream capture on that device. */
+int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
+                       int32_t* sorted_ids, int64_t sorted_len, int32_t* expert_ids, int64_t expert_len,
+                       int32_t* num_post_pad, void* stream);
+
 /* Grouped GEMM of one routed-expert matrix: replaces the kit's moe_gemm (pybind, files/mbx_moek.cu:714-795) with the
  * same fields: A, W, S, G, sorted_ids, expert_ids, num_post_pad, topk_w, out, top_k, gate_up, SP, exc_off, exc_ent,
  * cnt, mode, nsplit, part, tiled (the reference's stream-k ws and schedule order have no use here).

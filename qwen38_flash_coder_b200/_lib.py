@@ -12,6 +12,7 @@ SIGNATURES = {
     "moek_set_wait_timeout_ns": (ctypes.c_int, [_U64]),
     "moek_align_workspace_bytes": (ctypes.c_int, [_I64, _I32, ctypes.POINTER(ctypes.c_size_t)]),
     "moek_align": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P, ctypes.c_size_t, _P]),
+    "moek_align_noalloc": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P]),
     "moek_gemm": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32,
                                  _P, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _I32, _I32, _I32, _P, _I32, _P]),
     "moek_split_epilogue": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P]),

@@ -26,6 +26,16 @@ static int fail(int code, const char* fmt, ...) {
   va_end(ap);
   return code;
 }
+namespace moek {
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace moek
+
 static int cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return MOEK_OK;
   return fail(MOEK_ERR_CUDA, "moek_b200: %s: %s", what, cudaGetErrorString(e));

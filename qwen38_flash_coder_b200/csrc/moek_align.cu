@@ -10,6 +10,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
 
@@ -186,3 +189,63 @@ cudaError_t launch_align(const int32_t* ids, int64_t numel, int E, int bs, int32
 }
 
 }  // namespace moek
+
+// ------------------------------------------------------------------------------------------ allocation-free variant
+// moek_align_noalloc: the same sort-and-pad as moek_align, for callers that cannot hand the library any scratch
+// buffer because they may not allocate device memory on the path that calls it (a host runtime that owns a fixed
+// memory plan, or a binding that only passes the tensors it already holds). The multi-tile path's scratch (per-tile
+// expert counts and per-index ranks) lives instead in the fixed array below, which every GPU that loads this library
+// keeps until the process exits.
+namespace moek {
+constexpr int64_t NOALLOC_MAX_NUMEL = 65536;  // flattened (token, slot) indices per call
+constexpr int NOALLOC_MAX_EXPERTS = 1024;
+constexpr int64_t NOALLOC_MAX_TILES = NOALLOC_MAX_NUMEL / AT;
+constexpr int64_t NOALLOC_INTS = NOALLOC_MAX_TILES * NOALLOC_MAX_EXPERTS + NOALLOC_MAX_NUMEL;  // 512 KiB
+static __device__ __align__(256) int32_t g_align_scratch[NOALLOC_INTS];
+
+// Device address of g_align_scratch on the current device. In host code the symbol's name is only a host-side
+// stand-in, so the address is looked up once per device (with that device current) and cached.
+static cudaError_t noalloc_scratch(int32_t** out) {
+  static std::mutex mu;
+  static int32_t* ptr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_align_scratch);
+    if (e != cudaSuccess) return e;
+    ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = ptr[dev];
+  return cudaSuccess;
+}
+}  // namespace moek
+
+extern "C" __attribute__((visibility("default"))) int moek_align_noalloc(
+    const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size, int32_t* sorted_ids,
+    int64_t sorted_len, int32_t* expert_ids, int64_t expert_len, int32_t* num_post_pad, void* stream) {
+  using namespace moek;
+  if (numel < 0 || numel > NOALLOC_MAX_NUMEL || num_experts <= 0 || num_experts > NOALLOC_MAX_EXPERTS ||
+      block_size <= 0)
+    return set_error(1, "moek_b200: moe_align_noalloc takes 0..%lld indices, 1..%d experts and block_size > 0 "
+                        "(got %lld, %d, %d); use moek_align with a workspace for larger calls",
+                     (long long)NOALLOC_MAX_NUMEL, NOALLOC_MAX_EXPERTS, (long long)numel, num_experts, block_size);
+  int64_t need = numel + (int64_t)num_experts * (block_size - 1);
+  if (numel < num_experts) need = std::min<int64_t>(need, numel * block_size);
+  if (sorted_len < need || expert_len < (need + block_size - 1) / block_size)
+    return set_error(1, "moek_b200: moe_align_noalloc outputs too small (sorted %lld < %lld or expert_ids %lld)",
+                     (long long)sorted_len, (long long)need, (long long)expert_len);
+  if ((sorted_len && !sorted_ids) || (expert_len && !expert_ids) || !num_post_pad || (numel && !topk_ids))
+    return set_error(1, "moek_b200: moe_align_noalloc null pointer");
+  int32_t* scratch = nullptr;
+  cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess)
+    return set_error(2, "moek_b200: moe_align_noalloc scratch lookup: %s", cudaGetErrorString(e));
+  e = launch_align(topk_ids, numel, num_experts, block_size, sorted_ids, sorted_len, expert_ids, expert_len,
+                   num_post_pad, scratch, (cudaStream_t)stream);
+  if (e != cudaSuccess) return set_error(2, "moek_b200: moe_align_noalloc launch: %s", cudaGetErrorString(e));
+  return 0;
+}

@@ -27,6 +27,9 @@ struct GemmParams {
   int gate_up, mode, combine_k;
 };
 
+// moek_abi.cu: record the calling thread's error message (read back by moek_last_error) and return code
+int set_error(int code, const char* fmt, ...);
+
 // moek_align.cu
 cudaError_t launch_align(const int32_t* ids, int64_t numel, int E, int bs, int32_t* sorted_ids, int64_t sorted_len,
                          int32_t* expert_ids, int64_t expert_len, int32_t* npad, void* ws, cudaStream_t st);
