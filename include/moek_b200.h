@@ -81,13 +81,16 @@ int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_exper
  *           at N/2 + c) and moek_split_epilogue finishes (the reference's mode 2).
  *           3: the epilogue is fused. nsplit 1: gate_up writes act bf16 [num_ids, N/2] = bf16(silu(g) * u) to out;
  *           down writes fp32 rows topk_w[id] * sum to part [num_ids, N] (finish with moek_combine). nsplit > 1:
- *           the unit that completes an item (arrival counters in cnt[1..]) adds the partials in split order;
- *           gate_up writes act to out, down writes out bf16 [num_ids/combine_k, N] = the top-k sum over each
- *           token's combine_k slots (slots whose topk_ids entry is outside [0, E) are left out).
+ *           the warp whose arrival completes a (block, item) (counters in cnt[1..]) adds the partials in split
+ *           order; gate_up writes act to out; down writes fp32 rows topk_w * sum to part after the partials
+ *           (part holds (nsplit + 1) * num_ids * N floats) and the arrival that completes a token's valid slots
+ *           writes out bf16 [num_ids/combine_k, N] = their sum in slot order (slots whose topk_ids entry is outside
+ *           [0, E) are left out).
  *           (The reference's modes 0/1, its atomic item counter and stream-k, are not available.)
  *   nsplit  K/64/nsplit must be even (whole packed-scale runs), K/128/nsplit <= 32.
  *   cnt     int32, zero-filled before the first call; cnt[0] is the device error word (MOEK_DEV_*), cnt[1..] the
- *           split counters (mode 3, nsplit > 1: gate_up 1 + blocks * N/256, down 1 + N/256 entries), which every
+ *           split counters (mode 3, nsplit > 1: 1 + max_blocks * N/256 entries, down + (num_ids/combine_k) * N/256,
+ *           max_blocks = min(sorted_len / block_m, ceil(num_ids / block_m) + min(E, num_ids))), which every
  *           completed launch leaves at zero.
  *   block_m the block size moek_align used; max_rows >= the most valid rows of any block (min(M, block_m) for top-k
  *           routing with distinct experts per token), <= 96.

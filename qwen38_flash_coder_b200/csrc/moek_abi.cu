@@ -122,14 +122,16 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
     return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: at most 32 packed-scale runs (4096 k) per split (K %d, nsplit %d)",
                 K, nsplit);
   const bool fused = mode == 3, direct = fused && nsplit == 1;
-  const int64_t part_need = direct ? (gate_up ? 0 : (int64_t)num_ids * N) : (int64_t)nsplit * num_ids * N;
+  const int64_t part_need = direct ? (gate_up ? 0 : (int64_t)num_ids * N)
+                                   : (int64_t)(nsplit + (fused && !gate_up ? 1 : 0)) * num_ids * N;
   if (part_need && (!part || part_len < part_need))
     return fail(MOEK_ERR_ARG, "moek_b200: part needs %lld floats", (long long)part_need);
   if (max_rows <= 0 || max_rows > 96)
     return fail(MOEK_ERR_ARG, "moek_b200: max_rows %d must be in [1, 96]", max_rows);
   const int64_t maxb = std::min<int64_t>(sorted_len / block_m, (num_ids + block_m - 1) / block_m +
                                                                    std::min<int64_t>(E, num_ids));
-  const int64_t cnt_need = fused && !direct ? 1 + (gate_up ? maxb * (N / 256) : N / 256) : 1;
+  const int64_t mtok = combine_k > 0 ? num_ids / combine_k : 0;
+  const int64_t cnt_need = fused && !direct ? 1 + maxb * (N / 256) + (gate_up ? 0 : mtok * (N / 256)) : 1;
   if (!cnt || cnt_len < std::max<int64_t>(4, cnt_need))
     return fail(MOEK_ERR_ARG, "moek_b200: cnt needs %lld int32 (error word + split counters, zero-filled)",
                 (long long)std::max<int64_t>(4, cnt_need));

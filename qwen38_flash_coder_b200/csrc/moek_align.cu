@@ -48,49 +48,107 @@ __device__ __forceinline__ void tile_ranks(const int32_t* ids, int64_t numel, in
   r_out = e >= 0 ? tab[w * E + e] + rw : 0;
 }
 
-// One CTA: numel <= AT.
+// Block-wide exclusive scan of one int per thread (AT threads); returns the exclusive prefix, *total the sum.
+__device__ __forceinline__ int block_scan(int v, int* wsum, int* total) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) wsum[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int s = wsum[lane];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, d);
+      if (lane >= d) s += y;
+    }
+    wsum[lane] = s;  // inclusive over warps
+  }
+  __syncthreads();
+  const int before = (w ? wsum[w - 1] : 0) + x - v;
+  *total = wsum[31];
+  __syncthreads();  // wsum may be reused by the caller's next scan
+  return before;
+}
+
+// One CTA: numel <= AT. Keys (expert << 11 | index) sorted in shared memory (bitonic), so equal experts come out in
+// ascending index order; then group starts, padded offsets by a block scan, and the scatter.
 __global__ void __launch_bounds__(AT) align_one_kernel(const int32_t* __restrict__ ids, int numel, int E, int bs,
                                                         int32_t* __restrict__ sorted_ids, int sorted_len,
                                                         int32_t* __restrict__ expert_ids, int expert_len,
                                                         int32_t* __restrict__ npad) {
-  extern __shared__ int sm[];
-  int* tab = sm;            // [32][E]
-  int* tot = tab + 32 * E;  // [E]
-  int* off = tot + E;       // [E + 1] padded offsets
-  int e, r;
-  tile_ranks(ids, numel, 0, E, tab, tot, e, r);
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ uint32_t key[AT];
+  __shared__ int gstart[AT + 1], goff[AT + 1], wsum[32];
   const int t = threadIdx.x;
-  if (t == 0) {  // serial scan over experts: E is small (<= a few thousand)
-    int s = 0;
-    for (int x = 0; x < E; x++) {
-      off[x] = s;
-      s += (tot[x] + bs - 1) / bs * bs;
-    }
-    off[E] = s;
-    npad[0] = s;
+  int n2 = 32;
+  while (n2 < numel) n2 <<= 1;
+  if (t < n2) {
+    const int e = t < numel ? ids[t] : -1;
+    key[t] = (e >= 0 && e < E) ? ((uint32_t)e << 11) | (uint32_t)t : 0xFFFFFFFFu;
   }
   __syncthreads();
-  const int total = off[E];
-  for (int j = t; j < sorted_len; j += AT) sorted_ids[j] = numel;
-  for (int b = t; b < expert_len; b += AT) {
-    int x = -1;
-    if (b * bs < total) {  // the expert whose padded range holds block b
-      int lo = 0, hi = E - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (off[mid] <= b * bs) lo = mid; else hi = mid - 1;
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (t < n2) {
+        const int q = t ^ j;
+        if (q > t) {
+          const uint32_t a = key[t], b = key[q];
+          const bool up = (t & k) == 0;
+          if ((a > b) == up) {
+            key[t] = b;
+            key[q] = a;
+          }
+        }
       }
-      x = lo;
+      __syncthreads();
     }
-    expert_ids[b] = x;
   }
+  // valid keys form a prefix; a group starts where the expert changes
+  const uint32_t kt = t < n2 ? key[t] : 0xFFFFFFFFu;
+  const bool valid = kt != 0xFFFFFFFFu;
+  const bool head = valid && (t == 0 || (key[t - 1] >> 11) != (kt >> 11));
+  int ngroups;
+  const int gidx = block_scan(head ? 1 : 0, wsum, &ngroups);
+  if (head) gstart[gidx] = t;
+  int nvalid;
+  block_scan(valid ? 1 : 0, wsum, &nvalid);
+  if (t == 0) gstart[ngroups] = nvalid;
   __syncthreads();
-  if (e >= 0) sorted_ids[off[e] + r] = t;
+  int padded = 0;
+  if (t < ngroups) padded = (gstart[t + 1] - gstart[t] + bs - 1) / bs * bs;
+  int total;
+  const int off = block_scan(padded, wsum, &total);
+  if (t < ngroups) goff[t] = off;
+  if (t == 0) npad[0] = total;
+  for (int j = t; j < sorted_len; j += AT) sorted_ids[j] = numel;
+  for (int b = t; b < expert_len; b += AT) expert_ids[b] = -1;
+  __syncthreads();
+  if (t < ngroups) {
+    const int e = (int)(key[gstart[t]] >> 11);
+    for (int b = goff[t] / bs; b < (goff[t] + padded) / bs; b++) expert_ids[b] = e;
+  }
+  if (valid) {
+    // the group of sorted position t: the last group start <= t
+    int lo = 0, hi = ngroups - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (gstart[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    sorted_ids[goff[lo] + t - gstart[lo]] = (int32_t)(kt & 2047u);
+  }
 }
 
 // Multi-tile pass 1: per-tile expert counts [ntiles][E] and every index's in-tile rank.
 __global__ void __launch_bounds__(AT) align_count_kernel(const int32_t* __restrict__ ids, int64_t numel, int E,
                                                           int32_t* __restrict__ counts, int32_t* __restrict__ ranks) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];
   int* tab = sm;
   int* tot = tab + 32 * E;
@@ -106,6 +164,8 @@ __global__ void __launch_bounds__(AT) align_offsets_kernel(int32_t* __restrict__
                                                             int numel, int32_t* __restrict__ sorted_ids,
                                                             int64_t sorted_len, int32_t* __restrict__ expert_ids,
                                                             int expert_len, int32_t* __restrict__ npad) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int sm[];
   int* off = sm;  // [E + 1]
   const int t = threadIdx.x;
@@ -119,15 +179,21 @@ __global__ void __launch_bounds__(AT) align_offsets_kernel(int32_t* __restrict__
     off[x] = s;
   }
   __syncthreads();
-  if (t == 0) {
-    int s = 0;
-    for (int x = 0; x < E; x++) {
-      const int c = off[x];
-      off[x] = s;
-      s += (c + bs - 1) / bs * bs;
+  {  // padded expert offsets: block scans over chunks of AT experts
+    __shared__ int wsum[32];
+    int carry = 0;
+    for (int x0 = 0; x0 < E; x0 += AT) {
+      const int x = x0 + t;
+      const int c = x < E ? off[x] : 0;
+      int tot;
+      const int before = block_scan((c + bs - 1) / bs * bs, wsum, &tot);
+      if (x < E) off[x] = carry + before;
+      carry += tot;
     }
-    off[E] = s;
-    npad[0] = s;
+    if (t == 0) {
+      off[E] = carry;
+      npad[0] = carry;
+    }
   }
   __syncthreads();
   for (int x = t; x < E; x += AT)
@@ -153,6 +219,8 @@ __global__ void __launch_bounds__(AT) align_scatter_kernel(const int32_t* __rest
                                                             const int32_t* __restrict__ starts,
                                                             const int32_t* __restrict__ ranks,
                                                             int32_t* __restrict__ sorted_ids) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * AT + threadIdx.x;
   if (i >= numel) return;
   const int e = ids[i];
@@ -160,7 +228,7 @@ __global__ void __launch_bounds__(AT) align_scatter_kernel(const int32_t* __rest
   sorted_ids[starts[(int64_t)blockIdx.x * E + e] + ranks[i]] = (int32_t)i;
 }
 
-size_t align_smem_one(int E) { return sizeof(int) * (33 * (size_t)E + E + 1); }
+size_t align_smem_one(int E) { return sizeof(int) * (33 * (size_t)E + 1); }  // largest dynamic smem (count pass)
 size_t align_workspace_bytes(int64_t numel, int E) {
   const int64_t ntiles = (numel + AT - 1) / AT;
   return ntiles <= 1 ? 0 : sizeof(int32_t) * (size_t)(ntiles * E + numel);
@@ -170,10 +238,9 @@ cudaError_t launch_align(const int32_t* ids, int64_t numel, int E, int bs, int32
                          int32_t* expert_ids, int64_t expert_len, int32_t* npad, void* ws, cudaStream_t st) {
   const int64_t ntiles = (numel + AT - 1) / AT;
   if (ntiles <= 1) {
-    const size_t smem = align_smem_one(E);
-    cudaFuncSetAttribute(align_one_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    align_one_kernel<<<1, AT, smem, st>>>(ids, (int)numel, E, bs, sorted_ids, (int)sorted_len, expert_ids,
-                                          (int)expert_len, npad);
+    cudaError_t e = launch_pdl(align_one_kernel, dim3(1), dim3(AT), 0, st, ids, (int)numel, E, bs, sorted_ids,
+                               (int)sorted_len, expert_ids, (int)expert_len, npad);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
   int32_t* counts = static_cast<int32_t*>(ws);

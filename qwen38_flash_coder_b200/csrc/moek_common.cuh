@@ -52,6 +52,12 @@ __device__ __forceinline__ void report(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Programmatic dependent launch: wait until the grid this one depends on has completed and its memory is visible
+// (a no-op when the launch did not ask for programmatic serialisation), and let the next grid in the stream start
+// launching (its CTAs stop at their own pdl_wait until this grid completes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------------------------------- mbarriers
 __device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

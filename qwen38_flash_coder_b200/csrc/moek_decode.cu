@@ -34,13 +34,16 @@ namespace moek {
 
 
 
-constexpr int DC_WARPS = 8, DC_THREADS = DC_WARPS * 32 + 32;
-constexpr int X_STRIDE = 144;  // bytes per activation row in a slot (128 + 16: conflict-free 16-byte reads)
-constexpr int MAXU = 64;       // units per metadata round
-constexpr int MAXRUN = 32;     // packed-scale runs per unit (K / 128 / nsplit)
-constexpr int EXC_POOL = 1024; // exception entries cached in shared memory per round
+constexpr int DC_WARPS = 8;                      // consumer warps
+constexpr int DC_THREADS = DC_WARPS * 32 + 64;    // + the bulk-copy producer warp + the scale warp
+constexpr int X_STRIDE = 144;   // bytes per activation row in a slot (128 + 16: conflict-free 16-byte reads)
+constexpr int SC_STRIDE = 264;  // words per k-group row of a slot's scale table (256 + 8: conflict-free reads)
+constexpr int SC_BYTES = 4 * SC_STRIDE * 4;
+constexpr int MAXU = 64;        // units per metadata round
+constexpr int MAXRUN = 32;      // packed-scale runs per unit (K / 128 / nsplit)
+constexpr int EXC_POOL = 1024;  // exception entries cached in shared memory per round
 
-// Per-unit metadata, gathered by the producer warp once per round (MAXU units) so that no consumer waits on a global
+// Per-unit metadata, gathered by the producer warp once per round (MAXU units) so that no thread waits on a global
 // load inside the stage loop.
 struct UnitMeta {
   int blk, item, ks, e, nv, flags;  // flags: 1 = exception list read from global, 2 = block has more rows than XR
@@ -50,16 +53,21 @@ struct UnitMeta {
   int run_off[MAXRUN + 1];           // entry offsets, relative to the first, at each run boundary
 };
 
+// Ring slot: [8 KB codes][1056 B packed-scale run pair][XR activation rows][scale table: 4 k-groups x 256 rows of
+// (bf16 B | bf16 R << 16), written by the scale warp].
 template <int XR>
 struct DecodeCfg {
-  static constexpr int SLOT = STAGE_BYTES + PAIR_BYTES + XR * X_STRIDE;
-  static constexpr int NS = XR <= 8 ? 8 : XR <= 16 ? 6 : XR <= 32 ? 5 : 4;
+  static constexpr int X_OFF = STAGE_BYTES + PAIR_BYTES;
+  static constexpr int SC_OFF = X_OFF + XR * X_STRIDE;
+  static constexpr int SLOT = SC_OFF + SC_BYTES;
+  static constexpr int NS = XR <= 8 ? 6 : XR <= 32 ? (XR <= 16 ? 5 : 4) : 4;
   static constexpr int META_OFF = NS * SLOT;
   static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
   static constexpr int POOL_OFF = IDS_OFF + MAXU * XR * 4;
-  static constexpr int RED_OFF = POOL_OFF + EXC_POOL * 4;
+  static constexpr int LUT_OFF = POOL_OFF + EXC_POOL * 4;
+  static constexpr int RED_OFF = LUT_OFF + 256 * 4;
   static constexpr int BAR_OFF = RED_OFF + 16;
-  static constexpr int SMEM = BAR_OFF + (2 * NS + 2) * 8;
+  static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
   static constexpr int T = XR / 8;  // token tiles of 8 rows
   static constexpr int MINB = XR <= 32 ? 2 : 1;
 };
@@ -80,7 +88,24 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, ui
   *abort_flag = 1;
   return false;
 }
+__device__ __forceinline__ int atom_add_acq_rel(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(DC_WARPS * 32) : "memory"); }
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %1, %2;" : "=r"(r) : "r"(a), "r"(sel));
+  return r;
+}
+// (bf16 B | bf16 R << 16) for a scale byte and the expert's global scale (see moek_common.cuh)
+__device__ __forceinline__ uint32_t scale_word(uint32_t byte, float g) {
+  const float y = s0e5m3_to_f32(byte) * g;
+  const __nv_bfloat16 b = __float2bfloat16_rn(y);
+  const __nv_bfloat16 r = __float2bfloat16_rn(y - __bfloat162float(b));
+  return (uint32_t)__bfloat16_as_ushort(b) | ((uint32_t)__bfloat16_as_ushort(r) << 16);
+}
 
 // Item slot -> output column of the N-wide weight matrix
 __device__ __forceinline__ int slot_column(const GemmParams& p, int item, int slot) {
@@ -95,11 +120,13 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
   UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);
   int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);
   uint32_t* pool = reinterpret_cast<uint32_t*>(smem + C::POOL_OFF);
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::LUT_OFF);
   volatile int* red = reinterpret_cast<volatile int*>(smem + C::RED_OFF);  // [0] last-arriver flag, [1] abort
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::NS;
-  uint64_t* mfull = empty + C::NS;  // a round's metadata is published (32 producer lanes arrive)
-  uint64_t* mempty = mfull + 1;     // a round's units are all consumed (one arrive per consumer warp)
+  uint64_t* scaled = empty + C::NS;   // the scale warp filled the slot's scale table (32 arrivals)
+  uint64_t* mfull = scaled + C::NS;   // a round's metadata is published (32 producer lanes arrive)
+  uint64_t* mempty = mfull + 1;       // a round's units are all consumed (consumer warps + the scale warp)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nt = p.N / ITEM_COLS, nstage = p.K / BK, nb = p.K / 128;
   const int su = nstage / p.nsplit, nruns = su / 2;
@@ -108,23 +135,27 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
     for (int i = 0; i < C::NS; i++) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, DC_WARPS);
+      mbar_init(scaled + i, 32);
     }
     mbar_init(mfull, 32);
-    mbar_init(mempty, DC_WARPS);
+    mbar_init(mempty, DC_WARPS + 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  pdl_wait();  // sorted_ids / expert_ids / activations come from the previous kernel
+  pdl_launch_dependents();
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int nblocks = min(p.num_post_pad[0] / p.block_m, p.max_blocks);
   const int64_t nunits = (int64_t)nblocks * nt * p.nsplit;
   const int n_mine = nunits > blockIdx.x ? (int)((nunits - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
   const int rounds = (n_mine + MAXU - 1) / MAXU;
+  volatile int* abort_flag = red + 1;
 
   if (warp == DC_WARPS) {  // ------------------------------------------------------------------ producer
     uint32_t g = 0;
     for (int r = 0; r < rounds; r++) {
       const int u0 = r * MAXU, nu = min(MAXU, n_mine - u0);
-      if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, red + 1)) return;
+      if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, abort_flag)) return;
       // units, experts, row ids (valid rows are a prefix of a block)
       for (int i = lane; i < nu; i += 32) {
         const int64_t u = blockIdx.x + (int64_t)(u0 + i) * gridDim.x;
@@ -147,6 +178,41 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         m.flags = (lim < p.block_m && p.sorted_ids[row0 + lim] < p.num_ids) ? 2 : 0;
       }
       __syncwarp();
+      // stream: the first NS stages go out now (they need only the expert and the rows), the rest after the
+      // scale and exception metadata is published
+      int ci = 0, cst = -1;  // cursor: unit index and stage of the next copy
+      auto issue = [&](int limit) -> bool {
+        int issued = 0;
+        for (; ci < nu; ci++) {
+          const int e = meta[ci].e, item = meta[ci].item, ks = meta[ci].ks, nv = meta[ci].nv;
+          if (e < 0 || e >= p.E) continue;
+          if (cst < 0) cst = ks * su;
+          for (; cst < (ks + 1) * su; cst++, g++) {
+            if (issued == limit) return true;
+            const int slot = g % C::NS;
+            if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag))
+              return false;
+            uint8_t* dst = smem + slot * C::SLOT;
+            if (lane == 0) mbar_expect_tx(full + slot, STAGE_BYTES + PAIR_BYTES + nv * BK * 2);
+            __syncwarp();
+            if (lane == 0) {
+              const int64_t wi = ((int64_t)e * nt + item) * nstage + cst;
+              bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
+              const int64_t si = ((int64_t)e * nt + item) * nb + (cst >> 1);
+              bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+            }
+            for (int rr = lane; rr < nv; rr += 32) {
+              const int id = mids[ci * XR + rr];
+              const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + cst * BK;
+              bulk_g2s(dst + C::X_OFF + rr * X_STRIDE, src, BK * 2, full + slot);
+            }
+            issued++;
+          }
+          cst = -1;
+        }
+        return true;
+      };
+      if (!issue(r == 0 ? C::NS : 0)) return;
       // global scales and exception-list bounds
       for (int i = lane; i < nu; i += 32) {
         UnitMeta& m = meta[i];
@@ -171,36 +237,74 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         }
       }
       __syncwarp();
-      for (int i = 0; i < nu; i++) {
+      for (int i = lane; i < nu; i += 32) {  // each lane copies its own units' lists: loads in parallel
         if (meta[i].flags & 1) continue;
         const int n = meta[i].run_off[nruns], s0 = meta[i].exc_s0, g0 = meta[i].exc_g0;
-        for (int j = lane; j < n; j += 32) pool[s0 + j] = p.exc_ent[g0 + j];
+        for (int j = 0; j < n; j++) pool[s0 + j] = p.exc_ent[g0 + j];
       }
       __syncwarp();
       mbar_arrive(mfull);
-      // stream the round's stages
-      for (int i = 0; i < nu; i++) {
-        const int e = meta[i].e, item = meta[i].item, ks = meta[i].ks, nv = meta[i].nv;
+      if (!issue(1 << 30)) return;
+    }
+    return;
+  }
+
+  if (warp == DC_WARPS + 1) {  // ------------------------------------------------------------- scale warp
+    // Per stage: the 4 k-groups x 256 rows of scale bytes (base + 4-bit offset, then the unit's exception entries)
+    // -> (B | R) words through a per-unit table of all 256 byte values. Lane L decodes chunk L % 16 (8 positions) of
+    // run L / 16 of the item's run pair.
+    uint32_t g = 0;
+    const int run = lane >> 4, ch = lane & 15;
+    for (int r = 0; r < rounds; r++) {
+      const int nu = min(MAXU, n_mine - r * MAXU);
+      if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) return;
+      for (int ui = 0; ui < nu; ui++) {
+        const UnitMeta& m = meta[ui];
+        const int e = m.e, item = m.item, ks = m.ks, flags = m.flags;
         if (e < 0 || e >= p.E) continue;
+        const float gsc = m.g;
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; j++) lut[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
+        __syncwarp();
+        const uint32_t* exc = (flags & 1) ? p.exc_ent + m.exc_g0 : pool + m.exc_s0;
+        const int r0g = p.gate_up ? item : 2 * item;  // global run index of the pair's first run
         for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
           const int slot = g % C::NS;
-          if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, red + 1)) return;
-          uint8_t* dst = smem + slot * C::SLOT;
-          if (lane == 0) mbar_expect_tx(full + slot, STAGE_BYTES + PAIR_BYTES + nv * BK * 2);
+          if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, abort_flag)) return;
+          const uint8_t* runp = smem + slot * C::SLOT + STAGE_BYTES + run * RUN_BYTES;
+          uint32_t* sc = reinterpret_cast<uint32_t*>(smem + slot * C::SLOT + C::SC_OFF);
+          const uint32_t b4 = runp[ch] * 0x01010101u;  // the chunk's base, in every byte
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++) {
+            const int kg = (st & 1) * 4 + kk;
+            const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kg * 64 + ch * 4);
+            const uint32_t lo = (q & 0x0F0F0F0Fu) + b4;         // positions 8ch + 0..3
+            const uint32_t hi = ((q >> 4) & 0x0F0F0F0Fu) + b4;  // positions 8ch + 4..7
+            uint32_t* row = sc + kk * SC_STRIDE + run * 128;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const uint32_t byte = ((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF;
+              row[position_slot(8 * ch + i)] = lut[byte];
+            }
+          }
           __syncwarp();
-          if (lane == 0) {
-            const int64_t wi = ((int64_t)e * nt + item) * nstage + st;
-            bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
-            const int64_t si = ((int64_t)e * nt + item) * nb + (st >> 1);
-            bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+          // exception entries of this run that fall in this stage: overwrite their rows
+          const int rr = (st - ks * su) >> 1;
+          const int eo0 = m.run_off[rr], eo1 = m.run_off[rr + 1];
+          for (int j = eo0 + lane; j < eo1; j += 32) {
+            const uint32_t en = exc[j];
+            const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+            if ((kg >> 2) != (st & 1)) continue;
+            const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
+            sc[(kg & 3) * SC_STRIDE + slot_e] = lut[en >> 24];
           }
-          for (int rr = lane; rr < nv; rr += 32) {
-            const int id = mids[i * XR + rr];
-            const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + st * BK;
-            bulk_g2s(dst + STAGE_BYTES + PAIR_BYTES + rr * X_STRIDE, src, BK * 2, full + slot);
-          }
+          __syncwarp();
+          mbar_arrive(scaled + slot);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mempty);
     }
     return;
   }
@@ -209,24 +313,17 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
   const int gq = lane >> 2, c = lane & 3;
   // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
   const int G0 = p.gate_up ? warp : 2 * warp, G1 = p.gate_up ? warp + 8 : 2 * warp + 1;
-  int slots[2][2], pos[2][2];
-#pragma unroll
-  for (int i = 0; i < 2; i++)
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      slots[i][h] = 16 * (i ? G1 : G0) + gq + 8 * h;
-      pos[i][h] = slot_position(slots[i][h]);
-    }
+  const int slot00 = 16 * G0 + gq, slot10 = 16 * G1 + gq;  // rows (g) of the two groups; g + 8 follows
   const int I = p.N / 2;
   uint32_t g = 0;
   for (int r = 0; r < rounds; r++) {
     const int nu = min(MAXU, n_mine - r * MAXU);
-    wait_or_abort(mfull, r & 1, deadline, p.err, red + 1);
+    wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag);
     consumer_sync();  // one decision for all consumer warps
-    const bool have_meta = !red[1];
+    const bool have_meta = !*abort_flag;
     for (int ui = 0; ui < nu; ui++) {
-      const UnitMeta& m = meta[ui];
       if (!have_meta) break;  // aborted: nothing was published (uniform across the consumer warps)
+      const UnitMeta& m = meta[ui];
       const int e = m.e, item = m.item, ks = m.ks, nv = m.nv, blk = m.blk, flags = m.flags;
       const int* ids = mids + ui * XR;
       if (e < 0 || e >= p.E) {
@@ -234,10 +331,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         continue;
       }
       if ((flags & 2) && tid == 0) report(p.err, MOEK_DEV_TOO_MANY_ROWS);
-      const float gsc = m.g;
-      const uint32_t* exc = (flags & 1) ? p.exc_ent + m.exc_g0 : pool + m.exc_s0;
       const int ntile = (nv + 7) >> 3;
-      const int r0g = p.gate_up ? item : 2 * item;  // global run index of the pair's first run
       float acc[2][C::T][4];
 #pragma unroll
       for (int i = 0; i < 2; i++)
@@ -248,44 +342,18 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
 
       for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
         const int slot = g % C::NS;
-        if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, red + 1)) continue;  // skip, stay in step
+        const uint32_t par = (g / C::NS) & 1;
+        if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag) ||
+            !wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag))
+          continue;  // aborted: skip, stay in step
         const uint8_t* sw = smem + slot * C::SLOT;
-        const uint8_t* ss = sw + STAGE_BYTES;
-        const uint8_t* sx = ss + PAIR_BYTES;
-        const int kg_run = (st & 1) * 4 + c;  // this lane's k-group inside the run
-        uint32_t sb[2][2];
-#pragma unroll
-        for (int i = 0; i < 2; i++)
-#pragma unroll
-          for (int h = 0; h < 2; h++) sb[i][h] = run_byte(ss + (slots[i][h] >> 7) * RUN_BYTES, pos[i][h], kg_run);
-        {  // exceptions of this run that fall in this stage and in this warp's rows
-          const int rr = (st - ks * su) >> 1;
-          const int eo0 = m.run_off[rr], eo1 = m.run_off[rr + 1];
-          for (int b0 = eo0; b0 < eo1; b0 += 32) {
-            uint32_t en = 0;
-            bool mine = false;
-            if (b0 + lane < eo1) {
-              en = exc[b0 + lane];
-              const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-              const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
-              const int ge = slot_e >> 4;
-              mine = (kg >> 2) == (st & 1) && (p.gate_up ? (ge & 7) : (ge >> 1)) == warp;
-            }
-            unsigned msk = __ballot_sync(0xffffffffu, mine);
-            while (msk) {
-              const int src = __ffs(msk) - 1;
-              msk &= msk - 1;
-              const uint32_t e2 = __shfl_sync(0xffffffffu, en, src);
-              const int ppos = e2 & 0xFFFF, kg = (e2 >> 16) & 0xFF;
-              const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
-              const int ge = slot_e >> 4, row = slot_e & 15;
-              if (gq == (row & 7) && c == (kg & 3)) sb[ge == G0 ? 0 : 1][row >> 3] = e2 >> 24;
-            }
-          }
-        }
+        const uint8_t* sx = sw + C::X_OFF;
+        const uint32_t* sc = reinterpret_cast<const uint32_t*>(sw + C::SC_OFF) + c * SC_STRIDE;
+        const uint32_t s0a = sc[slot00], s0b = sc[slot00 + 8], s1a = sc[slot10], s1b = sc[slot10 + 8];
 #pragma unroll
         for (int i = 0; i < 2; i++) {
-          const ScaleBR sa = scale_br(sb[i][0], gsc), sbv = scale_br(sb[i][1], gsc);
+          const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;
+          const ScaleBR sa{prmt(wa, 0x1010), prmt(wa, 0x3232)}, sbv{prmt(wb, 0x1010), prmt(wb, 0x3232)};
           const uint4 q = *reinterpret_cast<const uint4*>(sw + ((i ? G1 : G0) * 32 + lane) * 16);
           uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
           dequant_word(q.x, sa, wa0);
@@ -314,7 +382,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
       }
 
       // ---------------------------------------------------------------------------------------- epilogue
-      // acc[i][t][2h + v] = weight row slots[i][h] x block row 8t + 2c + v
+      // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
       if (p.mode == 3 && p.nsplit == 1) {
 #pragma unroll
         for (int t = 0; t < C::T; t++) {
@@ -326,15 +394,14 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
             const int id = ids[row];
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-              if (p.gate_up) {  // gate slot and up slot + 128 share the column
-                const int col = 128 * item + slots[0][h];
+              if (p.gate_up) {  // gate row and up row + 128 share the column
+                const int col = 128 * item + slot00 + 8 * h;
                 static_cast<__nv_bfloat16*>(p.out)[(int64_t)id * I + col] =
                     __float2bfloat16_rn(silu(acc[0][t][2 * h + v]) * acc[1][t][2 * h + v]);
               } else {
                 const float w = p.topk_w[id];
-#pragma unroll
-                for (int i = 0; i < 2; i++)
-                  p.part[(int64_t)id * p.N + slot_column(p, item, slots[i][h])] = w * acc[i][t][2 * h + v];
+                p.part[(int64_t)id * p.N + slot_column(p, item, slot00 + 8 * h)] = w * acc[0][t][2 * h + v];
+                p.part[(int64_t)id * p.N + slot_column(p, item, slot10 + 8 * h)] = w * acc[1][t][2 * h + v];
               }
             }
           }
@@ -351,56 +418,86 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
           if (row >= nv) continue;
           float* prow = base + (int64_t)ids[row] * p.N;
 #pragma unroll
-          for (int i = 0; i < 2; i++)
-#pragma unroll
-            for (int h = 0; h < 2; h++) prow[slot_column(p, item, slots[i][h])] = acc[i][t][2 * h + v];
+          for (int h = 0; h < 2; h++) {
+            prow[slot_column(p, item, slot00 + 8 * h)] = acc[0][t][2 * h + v];
+            prow[slot_column(p, item, slot10 + 8 * h)] = acc[1][t][2 * h + v];
+          }
         }
       }
       if (p.mode != 3) continue;
-      // split-k: the unit that completes an item adds the partials in split order (deterministic)
+      // split-k completion, per warp (no CTA barrier): the warp whose arrival completes the (block, item) adds the
+      // partials of every split in split order (deterministic) and finishes the item's rows.
       __threadfence();
-      consumer_sync();
-      if (tid == 0) {
-        int* ctr = p.gate_up ? p.counters + (int64_t)blk * nt + item : p.counters + item;
-        const int total = p.gate_up ? p.nsplit : nblocks * p.nsplit;
-        const int old = atomicAdd(ctr, 1);
-        const int last = old == total - 1;
-        if (last) *ctr = 0;  // every contribution is in: ready for the next launch
-        *red = last;
-      }
-      consumer_sync();
-      if (*red) {
-        __threadfence();
-        const int64_t stride = (int64_t)p.num_ids * p.N;
-        if (p.gate_up) {
-          for (int idx = tid; idx < nv * 128; idx += DC_WARPS * 32) {
-            const int row = idx >> 7, col = 128 * item + (idx & 127);
-            const float* pr = p.part + (int64_t)ids[row] * p.N;
+      __syncwarp();
+      int old = 0;
+      if (lane == 0) old = atom_add_acq_rel(p.counters + (int64_t)blk * nt + item, 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old != DC_WARPS * p.nsplit - 1) continue;
+      if (lane == 0) p.counters[(int64_t)blk * nt + item] = 0;  // every arrival is in: ready for the next launch
+      __threadfence();
+      const int64_t stride = (int64_t)p.num_ids * p.N;
+      if (p.gate_up) {
+        for (int row = 0; row < nv; row++) {
+          const int id = ids[row];
+          const float* pr = p.part + (int64_t)id * p.N;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int col = 128 * item + lane + 32 * j;
             float gs = 0.f, us = 0.f;
-            for (int s = 0; s < p.nsplit; s++) {
-              gs += __ldcg(pr + s * stride + col);
-              us += __ldcg(pr + s * stride + I + col);
+            for (int s2 = 0; s2 < p.nsplit; s2++) {
+              gs += __ldcg(pr + s2 * stride + col);
+              us += __ldcg(pr + s2 * stride + I + col);
             }
-            static_cast<__nv_bfloat16*>(p.out)[(int64_t)ids[row] * I + col] = __float2bfloat16_rn(silu(gs) * us);
-          }
-        } else {
-          const int mtok = p.num_ids / p.combine_k;
-          for (int idx = tid; idx < mtok * 256; idx += DC_WARPS * 32) {
-            const int t = idx >> 8, col = 256 * item + (idx & 255);
-            float o = 0.f;
-            for (int j = 0; j < p.combine_k; j++) {
-              const int id = t * p.combine_k + j;
-              const int ej = p.topk_ids[id];
-              if (ej < 0 || ej >= p.E) continue;
-              float sum = 0.f;
-              for (int s = 0; s < p.nsplit; s++) sum += __ldcg(p.part + s * stride + (int64_t)id * p.N + col);
-              o += p.topk_w[id] * sum;
-            }
-            static_cast<__nv_bfloat16*>(p.out)[(int64_t)t * p.N + col] = __float2bfloat16_rn(o);
+            static_cast<__nv_bfloat16*>(p.out)[(int64_t)id * I + col] = __float2bfloat16_rn(silu(gs) * us);
           }
         }
+        continue;
       }
-      consumer_sync();
+      // down: weighted fp32 rows of this (block, item) into the row buffer after the partials
+      float* rows_f32 = p.part + (int64_t)p.nsplit * stride;
+      for (int row = 0; row < nv; row++) {
+        const int id = ids[row];
+        const float w = p.topk_w[id];
+        const float* pr = p.part + (int64_t)id * p.N;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int col = 256 * item + lane + 32 * j;
+          float sum = 0.f;
+          for (int s2 = 0; s2 < p.nsplit; s2++) sum += __ldcg(pr + s2 * stride + col);
+          rows_f32[(int64_t)id * p.N + col] = w * sum;
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      // each row's token: the arrival that completes the token's valid slots for this item adds them (slot order)
+      int* tok_ctr = p.counters + (int64_t)p.max_blocks * nt;
+      for (int row = 0; row < nv; row++) {
+        const int tk = ids[row] / p.combine_k;
+        int nslots = 0;
+        if (lane < p.combine_k) {
+          const int ej = p.topk_ids[tk * p.combine_k + lane];
+          nslots = ej >= 0 && ej < p.E;
+        }
+        nslots = __popc(__ballot_sync(0xffffffffu, nslots != 0));
+        int o2 = 0;
+        if (lane == 0) o2 = atom_add_acq_rel(tok_ctr + (int64_t)tk * nt + item, 1);
+        o2 = __shfl_sync(0xffffffffu, o2, 0);
+        if (o2 != nslots - 1) continue;
+        if (lane == 0) tok_ctr[(int64_t)tk * nt + item] = 0;
+        __threadfence();
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int col = 256 * item + lane + 32 * j;
+          float o = 0.f;
+          for (int sl = 0; sl < p.combine_k; sl++) {
+            const int id = tk * p.combine_k + sl;
+            const int ej = p.topk_ids[id];
+            if (ej < 0 || ej >= p.E) continue;
+            o += __ldcg(rows_f32 + (int64_t)id * p.N + col);
+          }
+          static_cast<__nv_bfloat16*>(p.out)[(int64_t)tk * p.N + col] = __float2bfloat16_rn(o);
+        }
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(mempty);
@@ -410,6 +507,8 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
 // gate_up epilogue: act[id][c] = bf16(silu(sum_s g) * sum_s u), sums over the splits in split order.
 __global__ void moek_gate_epilogue_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N,
                                           __nv_bfloat16* __restrict__ act) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int I = N / 2;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)num_ids * I) return;
@@ -429,6 +528,8 @@ __global__ void moek_gate_epilogue_kernel(const float* __restrict__ part, int ns
 // order j = 0..k-1 (one rounding, as the fp32 oracle), optionally also the per-slot rows dout (fp32 -> bf16).
 __global__ void moek_down_combine_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N, int top_k,
                                          const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int m = num_ids / top_k;
   if (i >= (int64_t)m * N) return;
@@ -448,6 +549,8 @@ __global__ void moek_down_combine_kernel(const float* __restrict__ part, int nsp
 // down epilogue without the sum: dout[id][n] = fp32 w[id] * sum_s part (kept in fp32 for the combine)
 __global__ void moek_down_rows_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N,
                                       const float* __restrict__ topk_w, float* __restrict__ dout) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)num_ids * N) return;
   const int64_t id = i / N;
@@ -460,6 +563,8 @@ __global__ void moek_down_rows_kernel(const float* __restrict__ part, int nsplit
 // top-k combine of fp32 rows: out[t][n] = bf16(sum_j rows[t*k + j][n]) (slot order)
 __global__ void moek_combine_f32_kernel(const float* __restrict__ rows, int m, int N, int top_k,
                                         __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)m * N) return;
   const int64_t t = i / N;
@@ -472,6 +577,8 @@ __global__ void moek_combine_f32_kernel(const float* __restrict__ rows, int m, i
 // top-k combine of bf16 rows (the reference's torch.sum over dim 1: fp32 accumulation, one rounding)
 __global__ void moek_combine_bf16_kernel(const __nv_bfloat16* __restrict__ rows, int m, int N, int top_k,
                                          __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)m * N) return;
   const int64_t t = i / N;
@@ -487,7 +594,8 @@ static cudaError_t launch_decode_xr(const GemmParams& p, int grid, cudaStream_t 
   using C = DecodeCfg<XR>;
   cudaError_t e = cudaFuncSetAttribute(moek_decode_kernel<XR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  moek_decode_kernel<XR><<<grid, DC_THREADS, C::SMEM, st>>>(p);
+  e = launch_pdl(moek_decode_kernel<XR>, dim3(grid), dim3(DC_THREADS), C::SMEM, st, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -506,7 +614,9 @@ cudaError_t launch_gate_epilogue(const float* part, int nsplit, int num_ids, int
                                  cudaStream_t st) {
   const int64_t n = (int64_t)num_ids * (N / 2);
   if (n == 0) return cudaSuccess;
-  moek_gate_epilogue_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, nsplit, num_ids, N, act);
+  cudaError_t e = launch_pdl(moek_gate_epilogue_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, part,
+                             nsplit, num_ids, N, act);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -514,8 +624,9 @@ cudaError_t launch_down_combine(const float* part, int nsplit, int num_ids, int 
                                 __nv_bfloat16* out, cudaStream_t st) {
   const int64_t n = (int64_t)(num_ids / top_k) * N;
   if (n == 0) return cudaSuccess;
-  moek_down_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, nsplit, num_ids, N, top_k, topk_w,
-                                                                         out);
+  cudaError_t e = launch_pdl(moek_down_combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, part,
+                             nsplit, num_ids, N, top_k, topk_w, out);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

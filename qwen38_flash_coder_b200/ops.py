@@ -18,7 +18,7 @@ from ._lib import MoekError, call
 from .prep import PreparedLayer
 
 BM = 96  # moe_align block size (rows per block), as the kit (files/mbx_moek.py:33)
-LAUNCHES_PER_LAYER = 3  # decode: align, gate_up GEMM (+SwiGLU), down GEMM (+router weight, top-k sum)
+LAUNCHES_PER_LAYER = 5  # decode: align, gate_up GEMM, SwiGLU epilogue, down GEMM, router weight + top-k sum
 _BUF: dict = {}
 _PROF = None  # when a list, fused_moe appends (name, launch closure) for each of its GEMM launches
 
@@ -198,15 +198,20 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
     rows = min(BM, m)
     act = torch.empty((num_ids, a.N // 2), dtype=torch.bfloat16, device=dev)
     if m <= DECODE_MAX_M:
+        # split-k with fp32 partials (no cross-CTA synchronisation in the GEMMs), finished by two small
+        # deterministic epilogue kernels: SwiGLU -> act, and router weight + top-k sum -> output
         grid = (2 if rows <= 32 else 1) * _sms(dev)
         blocks = min(layer.E, num_ids)
         ns1 = _splits(a.K, blocks * (a.N // 256), 4 * grid)
-        ns2 = max(2, _splits(b.K, blocks * (b.N // 256), 4 * grid))
+        ns2 = _splits(b.K, blocks * (b.N // 256), 4 * grid)
         part = _scratch("part", max(ns1 * num_ids * a.N, ns2 * num_ids * b.N), torch.float32, dev)
-        _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, ns1, part, rows, act,
-                                          tw, ids32, top_k))
-        _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, ns2, part, rows, output,
-                                          tw, ids32, top_k))
+        st = _stream(dev)
+        _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, ns1, part, rows, None,
+                                          None, None, 0, mode=2))
+        call("moek_split_epilogue", _ptr(part), ns1, num_ids, a.N, 1, None, top_k, _ptr(act), 0, st)
+        _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, ns2, part, rows, None,
+                                          None, None, 0, mode=2))
+        call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(output), 2, st)
         return output
     part = _scratch("part", num_ids * b.N, torch.float32, dev)
     _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, 1, part, rows, act, tw, ids32,
@@ -217,10 +222,11 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
     return output
 
 
-def _gemm(a_in, mat, sid, eid, npad, num_ids, a_div, gate_up, cnt, nsplit, part, rows, out, tw, ids32, combine_k):
+def _gemm(a_in, mat, sid, eid, npad, num_ids, a_div, gate_up, cnt, nsplit, part, rows, out, tw, ids32, combine_k,
+          mode=3):
     call("moek_gemm", _ptr(a_in), _ptr(mat.w), None, _ptr(mat.g), _ptr(sid), sid.numel(), _ptr(eid), _ptr(npad),
          _ptr(tw), _ptr(out), num_ids, mat.N, mat.K, mat.E, a_div, int(gate_up), _ptr(mat.sp), _ptr(mat.exc_off),
-         _ptr(mat.exc_ent), _ptr(cnt), cnt.numel(), 3, nsplit, _ptr(part), part.numel(), 1, BM, rows, _ptr(ids32),
+         _ptr(mat.exc_ent), _ptr(cnt), cnt.numel(), mode, nsplit, _ptr(part), part.numel(), 1, BM, rows, _ptr(ids32),
          combine_k, _stream(a_in.device))
 
 
