@@ -37,8 +37,9 @@ namespace moek {
 constexpr int DC_WARPS = 8;                      // consumer warps
 constexpr int DC_THREADS = DC_WARPS * 32 + 64;    // + the bulk-copy producer warp + the scale warp
 constexpr int X_STRIDE = 144;   // bytes per activation row in a slot (128 + 16: conflict-free 16-byte reads)
-constexpr int SC_STRIDE = 264;  // words per k-group row of a slot's scale table (256 + 8: conflict-free reads)
-constexpr int SC_BYTES = 4 * SC_STRIDE * 4;
+constexpr int SC_STRIDE = 288;  // bytes per k-group row of a slot's scale-byte table (256 + 32: conflict-free reads)
+constexpr int SC_BYTES = 4 * SC_STRIDE;
+constexpr int NLUT = 4;         // per-unit (B | R) tables in flight (the scale warp runs at most 3 units ahead)
 constexpr int MAXU = 64;        // units per metadata round
 constexpr int MAXRUN = 32;      // packed-scale runs per unit (K / 128 / nsplit)
 constexpr int EXC_POOL = 1024;  // exception entries cached in shared memory per round
@@ -53,19 +54,20 @@ struct UnitMeta {
   int run_off[MAXRUN + 1];           // entry offsets, relative to the first, at each run boundary
 };
 
-// Ring slot: [8 KB codes][1056 B packed-scale run pair][XR activation rows][scale table: 4 k-groups x 256 rows of
-// (bf16 B | bf16 R << 16), written by the scale warp].
+// Ring slot: [8 KB codes][1056 B packed-scale run pair][XR activation rows][scale bytes: 4 k-groups x 256 rows,
+// exceptions applied, written by the scale warp]. Per unit the scale warp also fills one of NLUT tables mapping every
+// byte value to (bf16 B | bf16 R << 16) for the unit's expert.
 template <int XR>
 struct DecodeCfg {
   static constexpr int X_OFF = STAGE_BYTES + PAIR_BYTES;
   static constexpr int SC_OFF = X_OFF + XR * X_STRIDE;
   static constexpr int SLOT = SC_OFF + SC_BYTES;
-  static constexpr int NS = XR <= 8 ? 6 : XR <= 32 ? (XR <= 16 ? 5 : 4) : 4;
+  static constexpr int NS = XR <= 8 ? 7 : XR <= 32 ? (XR <= 16 ? 6 : 5) : 4;
   static constexpr int META_OFF = NS * SLOT;
   static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
   static constexpr int POOL_OFF = IDS_OFF + MAXU * XR * 4;
   static constexpr int LUT_OFF = POOL_OFF + EXC_POOL * 4;
-  static constexpr int RED_OFF = LUT_OFF + 256 * 4;
+  static constexpr int RED_OFF = LUT_OFF + NLUT * 256 * 4;
   static constexpr int BAR_OFF = RED_OFF + 16;
   static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
   static constexpr int T = XR / 8;  // token tiles of 8 rows
@@ -251,10 +253,13 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
 
   if (warp == DC_WARPS + 1) {  // ------------------------------------------------------------- scale warp
     // Per stage: the 4 k-groups x 256 rows of scale bytes (base + 4-bit offset, then the unit's exception entries)
-    // -> (B | R) words through a per-unit table of all 256 byte values. Lane L decodes chunk L % 16 (8 positions) of
-    // run L / 16 of the item's run pair.
-    uint32_t g = 0;
+    // into the slot's byte table; per unit: the (B | R) table of all 256 byte values for the unit's expert. Lane L
+    // decodes chunk L % 16 (8 positions) of run L / 16 of the item's run pair.
+    uint32_t g = 0, k = 0;
     const int run = lane >> 4, ch = lane & 15;
+    int dst[8];  // the rows (item slots) of the lane's 8 positions
+#pragma unroll
+    for (int i = 0; i < 8; i++) dst[i] = run * 128 + position_slot(8 * ch + i);
     for (int r = 0; r < rounds; r++) {
       const int nu = min(MAXU, n_mine - r * MAXU);
       if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) return;
@@ -263,17 +268,17 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         const int e = m.e, item = m.item, ks = m.ks, flags = m.flags;
         if (e < 0 || e >= p.E) continue;
         const float gsc = m.g;
-        __syncwarp();
+        uint32_t* lt = lut + (k % NLUT) * 256;
 #pragma unroll
-        for (int j = 0; j < 8; j++) lut[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
-        __syncwarp();
+        for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
+        k++;
         const uint32_t* exc = (flags & 1) ? p.exc_ent + m.exc_g0 : pool + m.exc_s0;
         const int r0g = p.gate_up ? item : 2 * item;  // global run index of the pair's first run
         for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
           const int slot = g % C::NS;
           if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, abort_flag)) return;
           const uint8_t* runp = smem + slot * C::SLOT + STAGE_BYTES + run * RUN_BYTES;
-          uint32_t* sc = reinterpret_cast<uint32_t*>(smem + slot * C::SLOT + C::SC_OFF);
+          uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF;
           const uint32_t b4 = runp[ch] * 0x01010101u;  // the chunk's base, in every byte
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
@@ -281,15 +286,12 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
             const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kg * 64 + ch * 4);
             const uint32_t lo = (q & 0x0F0F0F0Fu) + b4;         // positions 8ch + 0..3
             const uint32_t hi = ((q >> 4) & 0x0F0F0F0Fu) + b4;  // positions 8ch + 4..7
-            uint32_t* row = sc + kk * SC_STRIDE + run * 128;
+            uint8_t* row = sc + kk * SC_STRIDE;
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-              const uint32_t byte = ((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF;
-              row[position_slot(8 * ch + i)] = lut[byte];
-            }
+            for (int i = 0; i < 8; i++) row[dst[i]] = (uint8_t)(((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF);
           }
           __syncwarp();
-          // exception entries of this run that fall in this stage: overwrite their rows
+          // exception entries of this run that fall in this stage: overwrite their bytes
           const int rr = (st - ks * su) >> 1;
           const int eo0 = m.run_off[rr], eo1 = m.run_off[rr + 1];
           for (int j = eo0 + lane; j < eo1; j += 32) {
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
             const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
             if ((kg >> 2) != (st & 1)) continue;
             const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
-            sc[(kg & 3) * SC_STRIDE + slot_e] = lut[en >> 24];
+            sc[(kg & 3) * SC_STRIDE + slot_e] = (uint8_t)(en >> 24);
           }
           __syncwarp();
           mbar_arrive(scaled + slot);
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
   const int G0 = p.gate_up ? warp : 2 * warp, G1 = p.gate_up ? warp + 8 : 2 * warp + 1;
   const int slot00 = 16 * G0 + gq, slot10 = 16 * G1 + gq;  // rows (g) of the two groups; g + 8 follows
   const int I = p.N / 2;
-  uint32_t g = 0;
+  uint32_t g = 0, k = 0;
   for (int r = 0; r < rounds; r++) {
     const int nu = min(MAXU, n_mine - r * MAXU);
     wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag);
@@ -331,6 +333,8 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         continue;
       }
       if ((flags & 2) && tid == 0) report(p.err, MOEK_DEV_TOO_MANY_ROWS);
+      const uint32_t* lt = lut + (k % NLUT) * 256;  // filled by the scale warp before the unit's first stage
+      k++;
       const int ntile = (nv + 7) >> 3;
       float acc[2][C::T][4];
 #pragma unroll
@@ -348,8 +352,8 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
           continue;  // aborted: skip, stay in step
         const uint8_t* sw = smem + slot * C::SLOT;
         const uint8_t* sx = sw + C::X_OFF;
-        const uint32_t* sc = reinterpret_cast<const uint32_t*>(sw + C::SC_OFF) + c * SC_STRIDE;
-        const uint32_t s0a = sc[slot00], s0b = sc[slot00 + 8], s1a = sc[slot10], s1b = sc[slot10 + 8];
+        const uint8_t* sc = sw + C::SC_OFF + c * SC_STRIDE;
+        const uint32_t s0a = lt[sc[slot00]], s0b = lt[sc[slot00 + 8]], s1a = lt[sc[slot10]], s1b = lt[sc[slot10 + 8]];
 #pragma unroll
         for (int i = 0; i < 2; i++) {
           const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;

@@ -153,16 +153,18 @@ def combine(rows: torch.Tensor, top_k: int, out: torch.Tensor = None) -> torch.T
 DECODE_MAX_M = int(os.environ.get("MOEK_B200_DECODE_MAX_M", "64"))  # split-k with fused epilogues up to this M
 
 
-def _splits(k: int, units_per_split: int, target: int) -> int:
-    """Smallest k-split (whole 128-k runs per unit) giving at least ``target`` units, else the finest."""
+def _splits(k: int, units_per_split: int, grid: int) -> int:
+    """k-split (whole 128-k runs per unit) that balances units over the grid best: the split whose busiest CTA has the
+    least work (in stages), preferring fewer splits on ties."""
     nstage = k // 64
-    best = 1
+    best, best_cost = 1, None
     for d in range(1, nstage + 1):
         if nstage % d or (nstage // d) % 2:
             continue
-        best = d
-        if units_per_split * d >= target:
-            break
+        units = units_per_split * d
+        cost = -(-units // grid) * (nstage // d)  # stages of the busiest CTA
+        if best_cost is None or cost < best_cost:
+            best, best_cost = d, cost
     return best
 
 
@@ -202,8 +204,8 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
         # deterministic epilogue kernels: SwiGLU -> act, and router weight + top-k sum -> output
         grid = (2 if rows <= 32 else 1) * _sms(dev)
         blocks = min(layer.E, num_ids)
-        ns1 = _splits(a.K, blocks * (a.N // 256), 4 * grid)
-        ns2 = _splits(b.K, blocks * (b.N // 256), 4 * grid)
+        ns1 = _splits(a.K, blocks * (a.N // 256), grid)
+        ns2 = _splits(b.K, blocks * (b.N // 256), grid)
         part = _scratch("part", max(ns1 * num_ids * a.N, ns2 * num_ids * b.N), torch.float32, dev)
         st = _stream(dev)
         _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, ns1, part, rows, None,
