@@ -48,9 +48,10 @@ __device__ __forceinline__ void tile_ranks(const int32_t* ids, int64_t numel, in
   r_out = e >= 0 ? tab[w * E + e] + rw : 0;
 }
 
-// Block-wide exclusive scan of one int per thread (AT threads); returns the exclusive prefix, *total the sum.
+// Block-wide exclusive scan of one int per thread (any multiple of 32 threads up to 1024); returns the exclusive
+// prefix, *total the block's sum.
 __device__ __forceinline__ int block_scan(int v, int* wsum, int* total) {
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
   int x = v;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
@@ -60,23 +61,24 @@ __device__ __forceinline__ int block_scan(int v, int* wsum, int* total) {
   if (lane == 31) wsum[w] = x;
   __syncthreads();
   if (w == 0) {
-    int s = wsum[lane];
+    int s = lane < nw ? wsum[lane] : 0;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, s, d);
       if (lane >= d) s += y;
     }
-    wsum[lane] = s;  // inclusive over warps
+    if (lane < nw) wsum[lane] = s;  // inclusive over warps
   }
   __syncthreads();
   const int before = (w ? wsum[w - 1] : 0) + x - v;
-  *total = wsum[31];
+  *total = wsum[nw - 1];
   __syncthreads();  // wsum may be reused by the caller's next scan
   return before;
 }
 
-// One CTA: numel <= AT. Keys (expert << 11 | index) sorted in shared memory (bitonic), so equal experts come out in
-// ascending index order; then group starts, padded offsets by a block scan, and the scatter.
+// One CTA of n2 threads (n2 = numel rounded up to a power of two, at least 64, at most AT): keys
+// (expert << 11 | index) sorted in shared memory (bitonic), so equal experts come out in ascending index order; then
+// group starts, padded offsets by a block scan, and the scatter.
 __global__ void __launch_bounds__(AT) align_one_kernel(const int32_t* __restrict__ ids, int numel, int E, int bs,
                                                         int32_t* __restrict__ sorted_ids, int sorted_len,
                                                         int32_t* __restrict__ expert_ids, int expert_len,
@@ -86,8 +88,7 @@ __global__ void __launch_bounds__(AT) align_one_kernel(const int32_t* __restrict
   __shared__ uint32_t key[AT];
   __shared__ int gstart[AT + 1], goff[AT + 1], wsum[32];
   const int t = threadIdx.x;
-  int n2 = 32;
-  while (n2 < numel) n2 <<= 1;
+  const int n2 = blockDim.x;
   if (t < n2) {
     const int e = t < numel ? ids[t] : -1;
     key[t] = (e >= 0 && e < E) ? ((uint32_t)e << 11) | (uint32_t)t : 0xFFFFFFFFu;
@@ -126,8 +127,8 @@ __global__ void __launch_bounds__(AT) align_one_kernel(const int32_t* __restrict
   const int off = block_scan(padded, wsum, &total);
   if (t < ngroups) goff[t] = off;
   if (t == 0) npad[0] = total;
-  for (int j = t; j < sorted_len; j += AT) sorted_ids[j] = numel;
-  for (int b = t; b < expert_len; b += AT) expert_ids[b] = -1;
+  for (int j = t; j < sorted_len; j += blockDim.x) sorted_ids[j] = numel;
+  for (int b = t; b < expert_len; b += blockDim.x) expert_ids[b] = -1;
   __syncthreads();
   if (t < ngroups) {
     const int e = (int)(key[gstart[t]] >> 11);
@@ -238,7 +239,9 @@ cudaError_t launch_align(const int32_t* ids, int64_t numel, int E, int bs, int32
                          int32_t* expert_ids, int64_t expert_len, int32_t* npad, void* ws, cudaStream_t st) {
   const int64_t ntiles = (numel + AT - 1) / AT;
   if (ntiles <= 1) {
-    cudaError_t e = launch_pdl(align_one_kernel, dim3(1), dim3(AT), 0, st, ids, (int)numel, E, bs, sorted_ids,
+    int n2 = 64;
+    while (n2 < numel) n2 <<= 1;
+    cudaError_t e = launch_pdl(align_one_kernel, dim3(1), dim3(n2), 0, st, ids, (int)numel, E, bs, sorted_ids,
                                (int)sorted_len, expert_ids, (int)expert_len, npad);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();

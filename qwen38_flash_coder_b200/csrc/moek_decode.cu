@@ -508,6 +508,21 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
   }
 }
 
+// Sum of the nsplit partials at p[0], p[stride], ... in split order, with all loads issued before the adds (the
+// partials are independent loads; the order of the fp32 additions is fixed, so the result is deterministic).
+__device__ __forceinline__ float split_sum(const float* __restrict__ p, int64_t stride, int nsplit) {
+  float acc = 0.f;
+  for (int s0 = 0; s0 < nsplit; s0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = s0 + j < nsplit ? __ldcg(p + (s0 + j) * stride) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (s0 + j < nsplit) acc += v[j];
+  }
+  return acc;
+}
+
 // gate_up epilogue: act[id][c] = bf16(silu(sum_s g) * sum_s u), sums over the splits in split order.
 __global__ void moek_gate_epilogue_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N,
                                           __nv_bfloat16* __restrict__ act) {
@@ -520,16 +535,13 @@ __global__ void moek_gate_epilogue_kernel(const float* __restrict__ part, int ns
   const int col = (int)(i - id * I);
   const int64_t stride = (int64_t)num_ids * N;
   const float* r = part + id * N;
-  float gsum = 0.f, usum = 0.f;
-  for (int s = 0; s < nsplit; s++) {
-    gsum += r[s * stride + col];
-    usum += r[s * stride + I + col];
-  }
+  const float gsum = split_sum(r + col, stride, nsplit);
+  const float usum = split_sum(r + I + col, stride, nsplit);
   act[i] = __float2bfloat16_rn(silu(gsum) * usum);
 }
 
 // down epilogue fused with the top-k sum: out[t][n] = bf16(sum_j w[t,j] * sum_s part[s][t*k+j][n]) in fp32, slots in
-// order j = 0..k-1 (one rounding, as the fp32 oracle), optionally also the per-slot rows dout (fp32 -> bf16).
+// order j = 0..k-1 (one rounding, as the fp32 oracle).
 __global__ void moek_down_combine_kernel(const float* __restrict__ part, int nsplit, int num_ids, int N, int top_k,
                                          const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
@@ -541,11 +553,14 @@ __global__ void moek_down_combine_kernel(const float* __restrict__ part, int nsp
   const int n = (int)(i - t * N);
   const int64_t stride = (int64_t)num_ids * N;
   float o = 0.f;
-  for (int j = 0; j < top_k; j++) {
-    const int64_t id = t * top_k + j;
-    float s = 0.f;
-    for (int sp = 0; sp < nsplit; sp++) s += part[sp * stride + id * N + n];
-    o += topk_w[id] * s;
+  for (int j0 = 0; j0 < top_k; j0 += 8) {
+    float sums[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      sums[j] = j0 + j < top_k ? split_sum(part + (t * top_k + j0 + j) * N + n, stride, nsplit) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (j0 + j < top_k) o += topk_w[t * top_k + j0 + j] * sums[j];
   }
   out[i] = __float2bfloat16_rn(o);
 }
