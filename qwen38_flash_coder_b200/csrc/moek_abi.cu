@@ -113,8 +113,45 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
     return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm null pointer");
   if (!gate_up && top_k != 1) return fail(MOEK_ERR_ARG, "moek_b200: down reads one activation row per id (top_k 1)");
   if (top_k <= 0) return fail(MOEK_ERR_ARG, "moek_b200: top_k must be positive");
-  if (mode != 2 && mode != 3)
-    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (2 or 3)", mode);
+  if (mode != 0 && mode != 2 && mode != 3)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (0, 2 or 3)", mode);
+  if (mode == 0) {  // tcgen05 path: whole K per unit, direct epilogue
+    if (K / 128 > 32) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: mode 0 supports K <= 4096 (got %d)", K);
+    if (block_m > moek::prefill_block_m())
+      return fail(MOEK_ERR_ARG, "moek_b200: mode 0 takes moe_align blocks of <= %d rows (got %d)",
+                  moek::prefill_block_m(), block_m);
+    if (gate_up ? !out : (!topk_w || !part || part_len < (int64_t)num_ids * N))
+      return fail(MOEK_ERR_ARG, "moek_b200: mode 0 gate_up writes act to out; down writes fp32 rows to part "
+                                "(num_ids * N floats) and needs topk_w");
+    if (!cnt || cnt_len < 1) return fail(MOEK_ERR_ARG, "moek_b200: cnt[0] is the device error word");
+    moek::GemmParams p{};
+    p.A = static_cast<const __nv_bfloat16*>(A);
+    p.W = static_cast<const uint8_t*>(W);
+    p.G = G;
+    p.sorted_ids = sorted_ids;
+    p.expert_ids = expert_ids;
+    p.num_post_pad = num_post_pad;
+    p.SP = SP;
+    p.exc_off = exc_off;
+    p.exc_ent = reinterpret_cast<const uint32_t*>(exc_ent);
+    p.part = part;
+    p.err = cnt;
+    p.topk_w = topk_w;
+    p.out = out;
+    p.timeout_ns = g_timeout_ns;
+    p.num_ids = num_ids;
+    p.N = N;
+    p.K = K;
+    p.E = E;
+    p.a_div = top_k;
+    p.block_m = block_m;
+    p.nsplit = 1;
+    p.max_blocks = (int)std::min<int64_t>(sorted_len / block_m,
+                                          (num_ids + block_m - 1) / block_m + std::min<int64_t>(E, num_ids));
+    p.gate_up = gate_up ? 1 : 0;
+    p.mode = 0;
+    return cuda_status(moek::launch_prefill(p, sm_count(), (cudaStream_t)stream), "moe_gemm (tcgen05) launch");
+  }
   const int nstage = K / moek::BK;
   if (nsplit < 1 || nstage % nsplit || (nstage / nsplit) % moek::STAGES_PER_RUN)
     return fail(MOEK_ERR_ARG, "moek_b200: nsplit %d must cut K/128 = %d into whole runs", nsplit, K / 128);

@@ -164,4 +164,17 @@ __device__ __forceinline__ uint32_t run_byte(const uint8_t* run, int p, int kg) 
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
+__device__ __forceinline__ uint32_t prmt_b(uint32_t a, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %1, %2;" : "=r"(r) : "r"(a), "r"(sel));
+  return r;
+}
+// (bf16 B | bf16 R << 16) for a scale byte and the expert's global scale G (the B / R split described above)
+__device__ __forceinline__ uint32_t scale_word(uint32_t byte, float g) {
+  const float y = s0e5m3_to_f32(byte) * g;
+  const __nv_bfloat16 b = __float2bfloat16_rn(y);
+  const __nv_bfloat16 r = __float2bfloat16_rn(y - __bfloat162float(b));
+  return (uint32_t)__bfloat16_as_ushort(b) | ((uint32_t)__bfloat16_as_ushort(r) << 16);
+}
+
 }  // namespace moek

@@ -96,18 +96,6 @@ __device__ __forceinline__ int atom_add_acq_rel(int* addr, int v) {
   return old;
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(DC_WARPS * 32) : "memory"); }
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %1, %2;" : "=r"(r) : "r"(a), "r"(sel));
-  return r;
-}
-// (bf16 B | bf16 R << 16) for a scale byte and the expert's global scale (see moek_common.cuh)
-__device__ __forceinline__ uint32_t scale_word(uint32_t byte, float g) {
-  const float y = s0e5m3_to_f32(byte) * g;
-  const __nv_bfloat16 b = __float2bfloat16_rn(y);
-  const __nv_bfloat16 r = __float2bfloat16_rn(y - __bfloat162float(b));
-  return (uint32_t)__bfloat16_as_ushort(b) | ((uint32_t)__bfloat16_as_ushort(r) << 16);
-}
 
 // Item slot -> output column of the N-wide weight matrix
 __device__ __forceinline__ int slot_column(const GemmParams& p, int item, int slot) {
@@ -357,7 +345,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
 #pragma unroll
         for (int i = 0; i < 2; i++) {
           const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;
-          const ScaleBR sa{prmt(wa, 0x1010), prmt(wa, 0x3232)}, sbv{prmt(wb, 0x1010), prmt(wb, 0x3232)};
+          const ScaleBR sa{prmt_b(wa, 0x1010), prmt_b(wa, 0x3232)}, sbv{prmt_b(wb, 0x1010), prmt_b(wb, 0x3232)};
           const uint4 q = *reinterpret_cast<const uint4*>(sw + ((i ? G1 : G0) * 32 + lane) * 16);
           uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
           dequant_word(q.x, sa, wa0);

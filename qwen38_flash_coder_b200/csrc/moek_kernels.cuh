@@ -56,6 +56,10 @@ cudaError_t launch_align(const int32_t* ids, int64_t numel, int E, int bs, int32
 size_t align_workspace_bytes(int64_t numel, int E);
 size_t align_smem_one(int E);
 
+// moek_prefill.cu: tcgen05 grouped GEMM for large batches (blocks of <= prefill_block_m() rows)
+int prefill_block_m();
+cudaError_t launch_prefill(const GemmParams& p, int sms, cudaStream_t st);
+
 // moek_decode.cu
 cudaError_t launch_decode(const GemmParams& p, int max_rows, int sms, cudaStream_t st);
 cudaError_t launch_gate_epilogue(const float* part, int nsplit, int num_ids, int N, __nv_bfloat16* act,

@@ -17,7 +17,8 @@ from . import _lib
 from ._lib import MoekError, call
 from .prep import PreparedLayer
 
-BM = 96  # moe_align block size (rows per block), as the kit (files/mbx_moek.py:33)
+BM = 96  # moe_align block size (rows per block) of the decode path, as the kit (files/mbx_moek.py:33)
+BM_PREFILL = 128  # block size of the tcgen05 path (the MMA's N, at most)
 LAUNCHES_PER_LAYER = 5  # decode: align, gate_up GEMM, SwiGLU epilogue, down GEMM, router weight + top-k sum
 _BUF: dict = {}
 _PROF = None  # when a list, fused_moe appends (name, launch closure) for each of its GEMM launches
@@ -195,11 +196,11 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
     ids32 = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
     ids32 = ids32.reshape(-1).contiguous()
     tw = topk_weights.reshape(-1).float().contiguous()
-    sid, eid, npad = moe_align_block_size(ids32, BM, layer.E)
     cnt = error_word(dev)
     rows = min(BM, m)
     act = torch.empty((num_ids, a.N // 2), dtype=torch.bfloat16, device=dev)
     if m <= DECODE_MAX_M:
+        sid, eid, npad = moe_align_block_size(ids32, BM, layer.E)
         # split-k with fp32 partials (no cross-CTA synchronisation in the GEMMs), finished by two small
         # deterministic epilogue kernels: SwiGLU -> act, and router weight + top-k sum -> output
         grid = (2 if rows <= 32 else 1) * _sms(dev)
@@ -215,21 +216,25 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
                                           None, None, 0, mode=2))
         call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(output), 2, st)
         return output
+    # prefill: tcgen05 GEMMs over moe_align blocks of <= 128 rows (the MMA's N), SwiGLU and router weight in their
+    # epilogues, the top-k sum of the fp32 rows in one more kernel
+    sid, eid, npad = moe_align_block_size(ids32, BM_PREFILL, layer.E)
     part = _scratch("part", num_ids * b.N, torch.float32, dev)
     _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, 1, part, rows, act, tw, ids32,
-                                      top_k))
+                                      top_k, mode=0, block_m=BM_PREFILL))
     _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, 1, part, rows, None, tw, ids32,
-                                      top_k))
+                                      top_k, mode=0, block_m=BM_PREFILL))
     call("moek_combine", _ptr(part), 1, _ptr(output), m, b.N, top_k, _stream(dev))
     return output
 
 
 def _gemm(a_in, mat, sid, eid, npad, num_ids, a_div, gate_up, cnt, nsplit, part, rows, out, tw, ids32, combine_k,
-          mode=3):
+          mode=3, block_m=None):
+    block_m = block_m or BM
     call("moek_gemm", _ptr(a_in), _ptr(mat.w), None, _ptr(mat.g), _ptr(sid), sid.numel(), _ptr(eid), _ptr(npad),
          _ptr(tw), _ptr(out), num_ids, mat.N, mat.K, mat.E, a_div, int(gate_up), _ptr(mat.sp), _ptr(mat.exc_off),
-         _ptr(mat.exc_ent), _ptr(cnt), cnt.numel(), mode, nsplit, _ptr(part), part.numel(), 1, BM, rows, _ptr(ids32),
-         combine_k, _stream(a_in.device))
+         _ptr(mat.exc_ent), _ptr(cnt), cnt.numel(), mode, nsplit, _ptr(part), part.numel(), 1, block_m, rows,
+         _ptr(ids32), combine_k, _stream(a_in.device))
 
 
 def _timed(name, fn):

@@ -108,12 +108,36 @@ def test_decode_sizes_512_experts(m, route, seed):
     _run_and_check(w13, w2, x, ids, wts)
 
 
-@pytest.mark.parametrize("m,e", [(200, 64), (700, 512)])
-def test_larger_batches(m, e):
+@pytest.mark.parametrize("m,e,route", [(65, 64, "u"), (200, 64, "z"), (700, 512, "z"), (2000, 64, "u")])
+def test_prefill_path(m, e, route):
+    """Batches above the decode threshold run the tcgen05 kernels (moe_align blocks of 128 rows)."""
     w13, w2 = synth.make_layer(e, 2048, 512, 7, device=DEV)
     x = synth.activations(m, 2048, 7, device=DEV)
-    ids, wts = synth.route_zipf(m, e, 5, 7, device=DEV)
+    ids, wts = (synth.route_softmax if route == "u" else synth.route_zipf)(m, e, 5, 7, device=DEV)
     _run_and_check(w13, w2, x, ids, wts)
+
+
+@pytest.mark.parametrize("route", ["u", "z"])
+def test_prefill_config4_full_size(route):
+    """M=6912, 512 experts, uniform and Zipf(1.1) routing, against the oracle on every row."""
+    w13, w2 = synth.make_layer(512, 2048, 512, 21, device=DEV)
+    x = synth.activations(6912, 2048, 21, device=DEV)
+    ids, wts = (synth.route_softmax if route == "u" else synth.route_zipf)(6912, 512, 5, 21, device=DEV)
+    _run_and_check(w13, w2, x, ids, wts)
+
+
+def test_decode_and_prefill_paths_agree(monkeypatch):
+    """The same 64-token batch through the split-k mma.sync path and the tcgen05 path."""
+    w13, w2 = synth.make_layer(64, 2048, 512, 13, device=DEV)
+    layer = prep.PreparedLayer(w13, w2)
+    x = synth.activations(64, 2048, 13, device=DEV)
+    ids, wts = synth.route_zipf(64, 64, 5, 13, device=DEV)
+    a = ops.fused_moe(x, layer, wts, ids)
+    monkeypatch.setattr(ops, "DECODE_MAX_M", 0)
+    b = ops.fused_moe(x, layer, wts, ids)
+    ops.check_device_errors(DEV)
+    rel = float((a.float() - b.float()).norm() / b.float().norm())
+    assert rel < 2e-3, rel
 
 
 def test_bitwise_repeat():
