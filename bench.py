@@ -1,18 +1,28 @@
 """Benchmark of the routed-expert NVFP4 (W4A16) MoE layer on B200.
 
-Default workload (the one the headline metric is quoted on): a decode verify step, M = 8 tokens per
-GPU, 512 experts, hidden 2048, expert intermediate 512, top-5, uniform routing (softmax of N(0,1) logits -> top-5 ->
-renormalise); 48 layers with independent seeded NVFP4 weights (bf16 N(0, 0.02) quantised, 857 MB per layer, 41 GB
-in HBM). A step runs the 48 layers back to back; the weights the 48 layers touch (~3 GB) far exceed the 126 MB L2, so
-every layer streams its experts from HBM (the rotation is the L2 flush). Other workloads: --workload decode32
-(config 3: M=32, Zipf(1.1)), --workload prefill (config 4: M=6912, one layer per step, 48 rotating layers).
+Workloads (the reference's configs; synthetic seeded data of those shapes):
 
-value = algorithmic HBM bytes per second over all GPUs (touched experts' packed weights + packed scales + exception
-lists + x + output + routing, SURVEY 8(d) formula); e2e = the same metric through the public API with the step's
-inputs copied from pinned host memory and the outputs read back inside the timed region.
+- decode8  (config 2, the headline): a decode verify step, M = 8 tokens per GPU, uniform routing (softmax of N(0,1)
+           logits -> top-5 -> renormalise);
+- decode32 (config 3): M = 32 tokens (4 streams x 8), Zipf(1.1) routing over a seeded permutation of the experts;
+- prefill  (config 4): M = 6912 tokens, uniform routing (``--workload prefill_zipf``: the Zipf variant).
 
---impl reference times the reference's CPU restatement (the fp32 dequantise-then-matmul oracle of
-bench/moek/problem.py:51-67, oracle/moe_ref.py) on the host cores, same metric and unit, a bounded sample per step.
+Every workload runs on the same 48 layers of 512 experts (hidden 2048, expert intermediate 512, top-5) with
+independent seeded NVFP4 weights (bf16 N(0, 0.02) quantised; 857 MB per layer, 41 GB in HBM). A step runs the 48
+layers back to back through ``ops.fused_moe``, replayed as one CUDA graph; the weights the 48 layers touch exceed the
+126 MB L2, so each layer streams its experts from HBM (the layer rotation is the L2 flush).
+
+Units: decode = algorithmic HBM GB/s (touched experts' packed codes + packed scales + exception lists + x + output +
+routing); prefill = algorithmic TFLOP/s (2 * M * 5 * 3 * 2048 * 512, real rows only). ``value`` is the chosen
+workload's (``--workload``, default decode8); by default the other two are measured as well and reported under
+``workloads``. ``e2e`` = the same metric through the public API with each step's inputs copied from pinned host
+memory and its outputs read back inside the timed region. ``roofline`` = the gate_up GEMM launches replayed alone
+(CUDA events on the replaying stream) against MEASURED_PEAKS.json.
+
+``--impl reference`` times the reference's CPU path (the fp32 dequantise-then-matmul oracle of
+bench/moek/problem.py:51-67, restated in oracle/moe_ref.py) on the host cores, same metric and unit.
+Multi-GPU (torchrun, N > 1): every rank runs the workload on its own GPU with its own tokens (independent replicas,
+weak scaling); value = the sum of the ranks' algorithmic bytes (or FLOPs) over the slowest rank's time.
 """
 import argparse
 import json
@@ -28,6 +38,14 @@ sys.path.insert(0, ROOT)
 
 METRIC = "routed-MoE layer µs & HBM GB/s (M=8,32); TFLOP/s (M=6912); 1/2/4/8 GPU"
 H, I, E, TOPK = 2048, 512, 512, 5
+FLOPS_PER_ROW = 2 * 3 * H * I  # gate + up + down per (token, slot) row
+
+WORKLOADS = {
+    "decode8": dict(m=8, route="uniform", unit="GB/s", desc="decode verify M=8 (1 stream x block 8), uniform routing"),
+    "decode32": dict(m=32, route="zipf", unit="GB/s", desc="multi-stream decode M=32 (4 x 8), Zipf(1.1) routing"),
+    "prefill": dict(m=6912, route="uniform", unit="TFLOP/s", desc="prefill chunk M=6912, uniform routing"),
+    "prefill_zipf": dict(m=6912, route="zipf", unit="TFLOP/s", desc="prefill chunk M=6912, Zipf(1.1) routing"),
+}
 
 
 def parse():
@@ -36,18 +54,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode8", choices=["decode8", "decode32", "prefill"])
+    ap.add_argument("--workload", default="decode8", choices=list(WORKLOADS))
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", action="store_true", help="measure the chosen workload only")
     return ap.parse_args()
-
-
-def workload(name):
-    if name == "decode8":
-        return dict(m=8, route="uniform", desc="decode verify M=8 (1 stream x block 8), uniform routing")
-    if name == "decode32":
-        return dict(m=32, route="zipf", desc="multi-stream decode M=32 (4 x 8), Zipf(1.1) routing")
-    return dict(m=6912, route="uniform", desc="prefill chunk M=6912, uniform routing")
 
 
 def route(m, seed, kind, device):
@@ -58,7 +69,7 @@ def route(m, seed, kind, device):
     return synth.route_softmax(m, E, TOPK, seed, device=device)
 
 
-def layer_bytes(layer, ids, m):
+def touched_bytes(layer, ids, m):
     """Algorithmic bytes of one layer call: touched experts' streamed bytes + x + out + routing."""
     import torch
 
@@ -68,6 +79,7 @@ def layer_bytes(layer, ids, m):
 
 
 def gate_bytes(layer, ids, m):
+    """Algorithmic bytes of one gate_up GEMM launch: touched experts' w13 codes, packed scales, exceptions, and x."""
     import torch
 
     touched = torch.unique(ids.long()).cpu()
@@ -87,11 +99,10 @@ class Clocks:
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
-        self.index = index
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
@@ -101,7 +112,7 @@ class Clocks:
         self.p.terminate()
         self.p.wait(timeout=10)
         self.f.seek(0)
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, power = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.f.read().splitlines():
             c = [x.strip() for x in line.split(",")]
@@ -110,6 +121,7 @@ class Clocks:
             try:
                 sm.append(float(c[1].split()[0]))
                 mx = float(c[2].split()[0])
+                power.append(float(c[3].split()[0]))
             except ValueError:
                 continue
             for n, v in zip(names, c[5:9]):
@@ -117,35 +129,7 @@ class Clocks:
                     reasons.add(n)
         os.unlink(self.f.name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
-                "reasons": sorted(reasons)}
-
-
-def cpu_baseline(layers, xs, routes, budget_s=12.0):
-    """The oracle (fp32 dequantise-then-matmul, torch CPU, all host threads) on whole layers until ~budget_s of
-    compute; copying the touched experts to the host is not timed."""
-    import torch
-
-    from oracle import moe_ref
-
-    torch.set_num_threads(os.cpu_count())
-    done_bytes, tot, n = 0, 0.0, 0
-    while n < len(layers) and (tot < budget_s or n == 0):
-        (w13, w2, layer), x, (ids, wts) = layers[n], xs[n], routes[n]
-        touched = torch.unique(ids.long())
-        remap = torch.full((E,), -1, dtype=torch.long, device=ids.device)
-        remap[touched] = torch.arange(touched.numel(), device=ids.device)
-        cpu = lambda mm: (mm[0][touched].cpu().numpy(), mm[1][touched].view(torch.uint8).cpu().numpy(),
-                          mm[2][touched].cpu().numpy())
-        c13, c2, cid = cpu(w13), cpu(w2), remap[ids.long()].cpu().numpy()
-        xc, wc = x.cpu(), wts.cpu().numpy()
-        t1 = time.perf_counter()
-        moe_ref.reference(xc, cid, wc, c13, c2)
-        tot += time.perf_counter() - t1
-        done_bytes += layer_bytes(layer, ids, x.shape[0])[0]
-        n += 1
-    return {"value": round(done_bytes / tot / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n} layer(s) of the same workload (M={xs[0].shape[0]}, touched experts only), "
-                      f"torch-CPU oracle (oracle/moe_ref.py), {tot:.1f} s of compute"}
+                "power_w_max": max(power) if power else None, "reasons": sorted(reasons)}
 
 
 def make_graph(fn, warmup):
@@ -183,6 +167,152 @@ def timed(fn, steps, barrier):
     return e0.elapsed_time(e1) / steps
 
 
+def over_ranks(v, world, dev, op="max"):
+    """The max (or sum) of a per-rank number over all ranks."""
+    import torch
+
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX if op == "max" else torch.distributed.ReduceOp.SUM)
+    return float(t)
+
+
+def cpu_baseline(layers, name, budget_s=12.0):
+    """The oracle (fp32 dequantise-then-matmul, torch CPU, all host threads) on a bounded sample of the workload:
+    whole decode layers, or the first 256 tokens of prefill layers; copying the touched experts to the host is not
+    timed. Same unit as the workload."""
+    import torch
+
+    from oracle import moe_ref
+
+    torch.set_num_threads(os.cpu_count())
+    wl = WORKLOADS[name]
+    sample_m = min(wl["m"], 256)
+    amount, tot, n = 0.0, 0.0, 0
+    while n < len(layers) and (tot < budget_s or n == 0):
+        w13, w2 = layers[n]["ckpt"]
+        x = layers[n]["x"][name][:sample_m]
+        ids, wts = (t[:sample_m] for t in layers[n]["route"][name])
+        touched = torch.unique(ids.long())
+        remap = torch.full((E,), -1, dtype=torch.long, device=ids.device)
+        remap[touched] = torch.arange(touched.numel(), device=ids.device)
+        cpu = lambda mm: (mm[0][touched].cpu().numpy(), mm[1][touched].view(torch.uint8).cpu().numpy(),
+                          mm[2][touched].cpu().numpy())
+        c13, c2, cid = cpu(w13), cpu(w2), remap[ids.long()].cpu().numpy()
+        xc, wc = x.cpu(), wts.cpu().numpy()
+        t1 = time.perf_counter()
+        moe_ref.reference(xc, cid, wc, c13, c2)
+        tot += time.perf_counter() - t1
+        if wl["unit"] == "GB/s":
+            amount += touched_bytes(layers[n]["prep"], ids, sample_m)[0] / 1e9
+        else:
+            amount += sample_m * TOPK * FLOPS_PER_ROW / 1e12
+        n += 1
+    return {"value": round(amount / tot, 6), "unit": wl["unit"], "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} layer(s) x {sample_m} tokens of this workload (touched experts only), torch-CPU oracle "
+                      f"(oracle/moe_ref.py), {tot:.1f} s of compute"}
+
+
+def measure(name, layers, a, dev, world, barrier, headline):
+    """One workload over all layers: device step time, value, the gate_up roofline and, for the headline, e2e."""
+    import torch
+
+    from qwen38_flash_coder_b200 import ops
+
+    wl = WORKLOADS[name]
+    m, nl = wl["m"], len(layers)
+    outs = [torch.empty((m, H), dtype=torch.bfloat16, device=dev) for _ in range(nl)]
+
+    def step():
+        for l in range(nl):
+            ids, wts = layers[l]["route"][name]
+            ops.fused_moe(layers[l]["x"][name], layers[l]["prep"], wts, ids, output=outs[l])
+
+    graph = make_graph(step, a.warmup)
+    ops.check_device_errors(dev)
+    clocks = Clocks(dev.index)
+    ms = timed(graph.replay, a.steps, barrier)
+    clk = clocks.stop()
+    if wl["unit"] == "GB/s":
+        amount = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] for L in layers) / 1e9
+    else:
+        amount = nl * m * TOPK * FLOPS_PER_ROW / 1e12
+    ms = over_ranks(ms, world, dev)
+    amount = over_ranks(amount, world, dev, op="sum")
+    value = amount / (ms / 1e3)
+
+    # roofline of the dominant kernel: the step's gate_up GEMM launches alone, replayed as a graph
+    rec = ops.record_launches(step)
+    kern_us = {}
+    for kname in ("gate_gemm", "down_gemm"):
+        fns = [f for n, f in rec if n == kname]
+        g = make_graph(lambda: [f() for f in fns], 2)
+        kern_us[kname] = over_ranks(timed(g.replay, a.steps, barrier) * 1e3 / len(fns), world, dev)
+        del g
+    peaks = {}
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        peaks = json.load(open(pp))
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(f"gate_gemm_{name}")
+    if wl["unit"] == "GB/s":
+        gb = sum(gate_bytes(L["prep"], L["route"][name][0], m) for L in layers) / nl
+        peak = peaks.get("hbm_gbs", 6650.0)
+        achieved = gb / (kern_us["gate_gemm"] / 1e6) / 1e9
+        roof = {"kernel": "moek_decode_kernel (gate_up, split-k)", "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": peak, "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
+                else "of fallback", "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                "bytes_per_launch": int(gb)}
+    else:
+        flops = m * TOPK * 2 * H * 2 * I  # gate + up rows of real tokens
+        peak = peaks.get("bf16_tflops_sustained", 1400.0)
+        achieved = flops / (kern_us["gate_gemm"] / 1e6) / 1e12
+        roof = {"kernel": "moek_prefill_kernel (gate_up, tcgen05)", "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": peak, "peak_source": "of measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
+                if "bf16_tflops_sustained" in peaks else "of fallback", "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "flops_per_launch": flops}
+    roof["avg_launch_us"] = round(kern_us["gate_gemm"], 2)
+    roof["down_gemm_avg_us"] = round(kern_us["down_gemm"], 2)
+    res = {"workload": wl["desc"], "value": round(value, 3), "unit": wl["unit"], "ms_per_step": round(ms, 4),
+           "us_per_layer": round(ms * 1e3 / nl, 2), "roofline": roof, "clocks": clk,
+           "gpu_launches_per_step": ops.launches_per_layer(m, TOPK) * nl}
+    if wl["unit"] == "GB/s":
+        res["touched_experts_per_layer"] = round(
+            sum(touched_bytes(L["prep"], L["route"][name][0], m)[1] for L in layers) / nl, 1)
+    if headline:
+        # e2e: the public API with each step's inputs copied from pinned host memory and its outputs read back
+        hx = [L["x"][name].cpu().pin_memory() for L in layers]
+        hid = [L["route"][name][0].cpu().pin_memory() for L in layers]
+        hw = [L["route"][name][1].cpu().pin_memory() for L in layers]
+        hout = [torch.empty((m, H), dtype=torch.bfloat16).pin_memory() for _ in range(nl)]
+        dx = [torch.empty_like(L["x"][name]) for L in layers]
+        did = [torch.empty_like(L["route"][name][0]) for L in layers]
+        dw = [torch.empty_like(L["route"][name][1]) for L in layers]
+
+        def e2e_step():
+            for l in range(nl):
+                dx[l].copy_(hx[l], non_blocking=True)
+                did[l].copy_(hid[l], non_blocking=True)
+                dw[l].copy_(hw[l], non_blocking=True)
+                ops.fused_moe(dx[l], layers[l]["prep"], dw[l], did[l], output=outs[l])
+                hout[l].copy_(outs[l], non_blocking=True)
+
+        eg = make_graph(e2e_step, 2)
+        ems = over_ranks(timed(eg.replay, a.steps, barrier), world, dev)
+        del eg
+        res["e2e"] = {"value": round(amount / (ems / 1e3), 3), "unit": wl["unit"],
+                      "h2d_bytes_per_step": sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4
+                                                for x, r, w in zip(hx, hid, hw)),
+                      "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
+                      "api": "ops.fused_moe with host copies, one CUDA graph per step"}
+        res["eager_ms_per_step"] = round(over_ranks(timed(step, max(2, a.steps // 4), barrier), world, dev), 4)
+    del graph
+    return res
+
+
 def main():
     a = parse()
     import torch
@@ -190,9 +320,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    wl = workload(a.workload)
     if a.impl == "reference":
-        return reference_arm(a, wl, rank, world)
+        return reference_arm(a, rank, world)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -201,140 +330,68 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    from qwen38_flash_coder_b200 import ops, prep, synth
+    from qwen38_flash_coder_b200 import prep, synth
 
-    m = wl["m"]
-    nl = a.layers
-    layers, xs, routes = [], [], []
-    for l in range(nl):
-        seed = 1000 * rank + l
+    names = [a.workload] + ([] if a.only else [n for n in ("decode8", "decode32", "prefill") if n != a.workload])
+    layers = []
+    for l in range(a.layers):
         w13, w2 = synth.make_layer(E, H, I, l, device=dev)
-        keep = l < 3  # checkpoint tensors only for the layers the CPU baseline may sample
-        layers.append((w13 if keep else None, w2 if keep else None, prep.PreparedLayer(w13, w2)))
+        # checkpoint tensors are kept only for the layers the CPU baseline may sample
+        L = {"prep": prep.PreparedLayer(w13, w2), "ckpt": (w13, w2) if l < 3 else None, "x": {}, "route": {}}
         del w13, w2
-        xs.append(synth.activations(m, H, seed, device=dev))
-        routes.append(route(m, seed, wl["route"], dev))
-    outs = [torch.empty((m, H), dtype=torch.bfloat16, device=dev) for _ in range(nl)]
-    per_layer = [layer_bytes(layers[l][2], routes[l][0], m) for l in range(nl)]
-    step_bytes = sum(b for b, _ in per_layer)
-
-    def step():
-        for l in range(nl):
-            ops.fused_moe(xs[l], layers[l][2], routes[l][1], routes[l][0], output=outs[l])
+        for j, n in enumerate(names):
+            seed = 100000 * rank + 100 * l + j
+            L["x"][n] = synth.activations(WORKLOADS[n]["m"], H, seed, device=dev)
+            L["route"][n] = route(WORKLOADS[n]["m"], seed, WORKLOADS[n]["route"], dev)
+        layers.append(L)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
 
-    graph = make_graph(step, a.warmup)
-    ops.check_device_errors(dev)
-    clocks = Clocks(local)
-    ms = timed(graph.replay, a.steps, barrier)
-    clk = clocks.stop()
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t)
-        sb = torch.tensor([step_bytes], dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(sb)
-        total_bytes = float(sb)
-    else:
-        total_bytes = step_bytes
-    value = total_bytes / (ms / 1e3) / 1e9
-
-    # --- roofline of the dominant kernel (the gate_up grouped GEMM): a graph of the step's gate_up launches alone,
-    # CUDA events on the stream that replays it
-    rec = ops.record_launches(step)
-    kern_us = {}
-    for name in ("gate_gemm", "down_gemm"):
-        fns = [f for n, f in rec if n == name]
-        g = make_graph(lambda: [f() for f in fns], 2)
-        kern_us[name] = timed(g.replay, a.steps, barrier) * 1e3 / len(fns)
-        del g
-    gb = sum(gate_bytes(layers[l][2], routes[l][0], m) for l in range(nl)) / nl
-    peaks = {}
-    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(pp):
-        peaks = json.load(open(pp))
-    peak = peaks.get("hbm_gbs", 6650.0)
-    achieved = gb / (kern_us["gate_gemm"] / 1e6) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        traffic = json.load(open(tp)).get(f"gate_gemm_{a.workload}")
-    roof = {"kernel": "moek_decode_kernel (gate_up)", "bound": "hbm", "achieved": round(achieved, 1),
-            "peak": peak, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
-            else "fallback 6650", "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-            "bytes_per_launch": int(gb), "avg_launch_us": round(kern_us["gate_gemm"], 2),
-            "down_gemm_avg_us": round(kern_us["down_gemm"], 2)}
-
-    # --- e2e: the public API (fused_moe) with each step's inputs copied from pinned host memory and its outputs
-    # read back, all inside the timed region (one CUDA graph per step, as vLLM runs decode)
-    hx = [x.cpu().pin_memory() for x in xs]
-    hid = [r[0].cpu().pin_memory() for r in routes]
-    hw = [r[1].cpu().pin_memory() for r in routes]
-    hout = [torch.empty((m, H), dtype=torch.bfloat16).pin_memory() for _ in range(nl)]
-    dx = [torch.empty_like(x) for x in xs]
-    did = [torch.empty_like(r[0]) for r in routes]
-    dw = [torch.empty_like(r[1]) for r in routes]
-
-    def e2e_step():
-        for l in range(nl):
-            dx[l].copy_(hx[l], non_blocking=True)
-            did[l].copy_(hid[l], non_blocking=True)
-            dw[l].copy_(hw[l], non_blocking=True)
-            ops.fused_moe(dx[l], layers[l][2], dw[l], did[l], output=outs[l])
-            hout[l].copy_(outs[l], non_blocking=True)
-
-    eg = make_graph(e2e_step, 2)
-    ems = timed(eg.replay, a.steps, barrier)
-    if world > 1:
-        t = torch.tensor([ems], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ems = float(t)
-    h2d = sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4 for x, r, w in zip(hx, hid, hw))
-    d2h = sum(o.numel() * 2 for o in hout)
-    e2e = {"value": round(total_bytes / (ems / 1e3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 4), "api": "ops.fused_moe, CUDA graph per step"}
-    eager_ms = timed(step, max(2, a.steps // 4), barrier)
-
+    results = {n: measure(n, layers, a, dev, world, barrier, headline=(n == a.workload)) for n in names}
+    head = results.pop(a.workload)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline(layers[:3], xs[:3], routes[:3])
+        cpu = cpu_baseline(layers[:3], a.workload)
     if world > 1:
         torch.distributed.barrier()
     if rank == 0:
+        wl = WORKLOADS[a.workload]
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
-            "warmup": max(3, a.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": wl["desc"], "layers_per_step": nl, "experts": E, "hidden": H, "inter": I,
-                       "top_k": TOPK, "tokens_per_gpu": m, "weights": "NVFP4 (E2M1 + E4M3/16 + fp32), bf16 acts",
-                       "l2": f"{nl} distinct layers per step (~{step_bytes / 1e9:.1f} GB touched) > 126 MB L2",
+            "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": wl["desc"], "layers_per_step": a.layers, "experts": E, "hidden": H, "inter": I,
+                       "top_k": TOPK, "tokens_per_gpu": wl["m"],
+                       "weights": "NVFP4 (E2M1 + E4M3/16 + fp32 global), bf16 activations",
+                       "l2": f"{a.layers} distinct layers per step rotate; touched weights >> 126 MB L2",
                        "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"},
-            "us_per_layer": round(ms * 1e3 / nl, 2),
-            "touched_experts_per_layer": round(sum(t for _, t in per_layer) / nl, 1),
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-            "gpu_launches": ops.LAUNCHES_PER_LAYER * nl * a.steps,
-            "eager_ms_per_step": round(eager_ms, 4),
+            "us_per_layer": head["us_per_layer"], "roofline": head["roofline"], "cpu_baseline": cpu,
+            "e2e": head["e2e"], "clocks": head["clocks"],
+            "gpu_launches": head["gpu_launches_per_step"] * a.steps,
+            "eager_ms_per_step": head["eager_ms_per_step"],
+            "workloads": results,
         }
+        if "touched_experts_per_layer" in head:
+            line["touched_experts_per_layer"] = head["touched_experts_per_layer"]
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
 
 
-def reference_arm(a, wl, rank, world):
-    """The reference's fp32 CPU oracle on the host cores (rank 0 only)."""
+def reference_arm(a, rank, world):
+    """The reference's fp32 CPU oracle on the host cores (rank 0 only), a bounded sample of the workload per step."""
     if rank != 0:
         return
     import torch
 
-    from qwen38_flash_coder_b200 import prep, synth
     from oracle import moe_ref
+    from qwen38_flash_coder_b200 import prep, synth
 
     torch.set_num_threads(os.cpu_count())
-    m = wl["m"]
-    # a bounded sample of the same workload: one layer's touched experts (CPU-generated weights)
+    wl = WORKLOADS[a.workload]
+    m = min(wl["m"], 256)
     ids, wts = route(m, 0, wl["route"], "cpu")
     touched = torch.unique(ids.long())
     remap = torch.full((E,), -1, dtype=torch.long)
@@ -344,8 +401,10 @@ def reference_arm(a, wl, rank, world):
     w2 = synth.make_experts(nt, H, I, 1)
     to_np = lambda mm: (mm[0].numpy(), mm[1].view(torch.uint8).numpy(), mm[2].numpy())
     c13, c2 = to_np(w13), to_np(w2)
-    layer = prep.PreparedLayer(w13, w2)
-    nbytes = int(layer.expert_bytes().sum()) + m * H * 4 + m * TOPK * 8
+    if wl["unit"] == "GB/s":
+        amount = (int(prep.PreparedLayer(w13, w2).expert_bytes().sum()) + m * H * 4 + m * TOPK * 8) / 1e9
+    else:
+        amount = m * TOPK * FLOPS_PER_ROW / 1e12
     x = synth.activations(m, H, 0)
     cid = remap[ids.long()].numpy()
     times = []
@@ -355,15 +414,16 @@ def reference_arm(a, wl, rank, world):
         if i >= a.warmup:
             times.append(time.perf_counter() - t0)
     s = statistics.median(times)
-    v = nbytes / s / 1e9
+    v = amount / s
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC, "value": round(v, 6), "unit": wl["unit"], "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(s * 1e3, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": wl["desc"], "experts": E, "hidden": H, "inter": I, "top_k": TOPK, "tokens": m},
-        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"one layer (M={m}, {nt} touched experts) per step, fp32 dequantise-then-matmul"},
-        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+        "cpu_baseline": {"value": round(v, 6), "unit": wl["unit"], "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"one layer of {m} tokens ({nt} touched experts) per step, the fp32 "
+                                   "dequantise-then-matmul oracle (oracle/moe_ref.py), all host threads"},
+        "e2e": {"value": round(v, 6), "unit": wl["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
         flush=True)
 
 

@@ -11,8 +11,9 @@
 //               the item's 1056-byte packed-scale run pair and the block's activation rows (one 128-byte copy per
 //               valid row, gathered through sorted_ids) into a ring slot, all counted on the slot's mbarrier.
 //   consumers = warps 0-7. Warp w owns 32 of the item's 256 weight rows (gate_up: 16 gate rows and the matching 16 up
-//               rows, so SwiGLU pairs stay in one thread). Per stage a lane decodes its 2 x 16 bytes of codes plus
-//               the two scales its k-group needs into the oracle's bf16 weights (moek_common.cuh) and runs
+//               rows, so SwiGLU pairs stay in one thread). Per stage a lane (4g + c) decodes 4 x 8 bytes of codes
+//               (k-group c of rows g and g + 8 of its two 16-row groups) plus the scales its k-group needs into the
+//               oracle's bf16 weights (moek_common.cuh) and runs
 //               mma.sync m16n8k16 with the WEIGHTS as the 16-row A operand and up to 8 activation rows as B
 //               ("swap AB": a decode block has 1-8 valid rows, so no MMA row is padding). The k order inside an
 //               MMA is the lane's own 16 consecutive k; activations are read in the same order.
@@ -304,6 +305,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
   // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
   const int G0 = p.gate_up ? warp : 2 * warp, G1 = p.gate_up ? warp + 8 : 2 * warp + 1;
   const int slot00 = 16 * G0 + gq, slot10 = 16 * G1 + gq;  // rows (g) of the two groups; g + 8 follows
+  const int w_off = ((((c >> 1) ^ (gq >> 2)) & 1) << 4) | ((c & 1) << 3);  // byte of k-group c in a 32-byte row
   const int I = p.N / 2;
   uint32_t g = 0, k = 0;
   for (int r = 0; r < rounds; r++) {
@@ -346,12 +348,14 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         for (int i = 0; i < 2; i++) {
           const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;
           const ScaleBR sa{prmt_b(wa, 0x1010), prmt_b(wa, 0x3232)}, sbv{prmt_b(wb, 0x1010), prmt_b(wb, 0x3232)};
-          const uint4 q = *reinterpret_cast<const uint4*>(sw + ((i ? G1 : G0) * 32 + lane) * 16);
+          // k-group c of rows g and g + 8 of the group: 8 bytes of each 32-byte row (halves swizzled by row bit 2)
+          const uint8_t* wr = sw + (16 * (i ? G1 : G0) + gq) * 32 + w_off;
+          const uint2 qa = *reinterpret_cast<const uint2*>(wr), qb = *reinterpret_cast<const uint2*>(wr + 8 * 32);
           uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
-          dequant_word(q.x, sa, wa0);
-          dequant_word(q.y, sbv, wb0);
-          dequant_word(q.z, sa, wa1);
-          dequant_word(q.w, sbv, wb1);
+          dequant_word(qa.x, sa, wa0);
+          dequant_word(qb.x, sbv, wb0);
+          dequant_word(qa.y, sa, wa1);
+          dequant_word(qb.y, sbv, wb1);
           const uint32_t A0[4] = {wa0[0], wb0[0], wa0[1], wb0[1]};
           const uint32_t A1[4] = {wa0[2], wb0[2], wa0[3], wb0[3]};
           const uint32_t A2[4] = {wa1[0], wb1[0], wa1[1], wb1[1]};

@@ -1,29 +1,40 @@
-// Prefill-regime W4A16 grouped GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators), sm_100a.
+// Prefill-regime W4A16 grouped GEMM on the 5th-generation tensor cores (tcgen05, TMEM operands), sm_100a.
 //
 // Same work as the decode kernel (moek_decode.cu) but for large batches, where every expert has tens to thousands of
-// rows and the layer is at the tensor-core / HBM ridge. The weights are the MMA's M side ("swap AB"): an item's 256
-// weight rows are two M=128 halves, the block's token rows are the N side (N = valid rows rounded up to 16, <= 128),
-// so ragged experts cost no padded MMA rows beyond that rounding.
+// rows and the layer sits at the tensor-core ridge. The weights are the MMA's M side ("swap AB"): an item's 256
+// weight rows are two M = 128 halves; the block's token rows are the N side (N = valid rows rounded up to 16,
+// <= 128), so ragged experts cost no padded MMA rows beyond that rounding.
+//
+// The dequantised weights never touch shared memory: each dequant thread owns one weight row, turns its 64 codes of
+// a stage into the oracle's bf16 weights in registers and writes them straight into tensor memory
+// (tcgen05.st 32x32b), and the MMA reads A from TMEM (tcgen05.mma ... [d], [a], b_desc): shared memory only carries
+// the packed codes, the packed scales and the activation tiles.
 //
 //   unit      = (moe_align block of <= 128 rows, 256-row item); units dealt round-robin to one persistent CTA per SM.
 //   producer  = warp 0: per 64-k stage, bulk-copies (cp.async.bulk, no multicast) the 8 KB of packed codes and the
 //               1056-byte packed-scale run pair into a ring slot (mbarrier complete_tx).
-//   MMA       = warp 1 (one elected lane): per stage 2 halves x 4 k16 steps of tcgen05.mma.cta_group::1.kind::f16
-//               (bf16 x bf16 -> fp32), A and B from shared memory through K-major SWIZZLE_128B descriptors, D in TMEM;
-//               tcgen05.commit releases the stage and, after a unit's last stage, hands the accumulator to the
-//               epilogue. Two accumulator buffers (2 x 2 halves x 128 columns = all 512 TMEM columns) let the next
-//               unit's MMAs run while the epilogue drains the previous one. Warp 1 also allocates and frees TMEM.
-//   dequant   = warps 2-9: per stage, the scale bytes of the 4 k-groups x 256 rows (base + 4-bit offset, then the
-//               unit's exception entries), then the oracle's bf16 weights (moek_common.cuh: bf16(e2m1 * s * gs))
-//               written as two 128 x 64 K-major tiles in the 128-byte swizzle (16-byte chunk c of row r at c ^ (r % 8)),
-//               and the block's activation rows gathered with cp.async into the same swizzled layout;
-//               fence.proxy.async then makes the generic-proxy writes visible to the tensor core.
-//   epilogue  = warps 10-13 (TMEM lane quarter = warp % 4): tcgen05.ld 32 columns at a time; gate_up writes
+//   MMA       = warp 1 (one lane): per stage 2 halves x 4 k16 steps of tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16
+//               -> fp32), A from a TMEM ring slot, B from a shared-memory K-major SWIZZLE_128B tile, D in TMEM.
+//               tcgen05.commit releases the A and B slots and, after a unit's last stage, hands D to the epilogue.
+//               Warp 1 also allocates and frees the 512 TMEM columns: D = columns 0-255 (two halves x 128),
+//               A ring = columns 256-511 (4 slots x two halves x 32 columns of bf16 pairs).
+//   loader    = warp 2: the block's activation rows gathered by TMA (cp.async.bulk.tensor tile::gather4, no
+//               multicast: 4 rows of 64 k per instruction, one instruction per lane) into the 128-byte-swizzled B tile
+//               of the stage; rows past the block's valid ones read out of bounds and arrive as zeros.
+//   scales    = warp 3: per unit the (B | R) table of the expert's scale bytes (moek_common.cuh) and the unit's
+//               exception lists; per stage the scale byte of each of the 256 rows x 4 k-groups (base + 4-bit offset,
+//               then the exceptions), one 32-bit word per row.
+//   dequant   = warps 4-11: warp 4 + 4h + q owns rows 128h + 32q .. +31 of the item (TMEM lane quarter q = warp % 4);
+//               per stage a thread reads its row's 32 bytes of codes and its scale word, and stores 32 columns of
+//               bf16 pairs into the A slot.
+//   epilogue  = warps 12-15 (lane quarter = warp % 4): tcgen05.ld 32 columns at a time; gate_up writes
 //               act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves 0 and 1), down writes
 //               the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
 //
 // Every wait is bounded (%globaltimer); on expiry the CTA raises an abort flag, every role skips its remaining work
 // in step, and TMEM is freed before the kernel returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -36,37 +47,50 @@
 namespace moek {
 namespace pf {
 
-constexpr int BMP = 128;           // rows per moe_align block (the MMA's N, at most)
-constexpr int NST = 3;             // ring stages
-constexpr int NDQ = 8;             // dequant warps
-constexpr int NEPI = 4;            // epilogue warps
-constexpr int THREADS = (2 + NDQ + NEPI) * 32;
-constexpr int DQ0 = 2, EPI0 = 2 + NDQ;  // first dequant warp, first epilogue warp
-constexpr int A_BYTES = 2 * 128 * 128;  // two 128-row x 64-k bf16 tiles
-constexpr int B_BYTES = BMP * 128;      // up to 128 token rows x 64 k bf16
-constexpr int SCB_STRIDE = 288;         // scale-byte row per k-group (256 + 32)
-constexpr int A_OFF = 0, B_OFF = A_OFF + A_BYTES, W_OFF = B_OFF + B_BYTES, S_OFF = W_OFF + STAGE_BYTES,
-              SCB_OFF = S_OFF + PAIR_BYTES, STAGE_END = SCB_OFF + 4 * SCB_STRIDE;
-constexpr int STAGE_STRIDE = (STAGE_END + 1023) / 1024 * 1024;  // tiles stay 1024-byte aligned
-constexpr int EXC_CAP = 2048;           // exception entries of one unit cached in shared memory
-constexpr int RING_END = NST * STAGE_STRIDE;
-constexpr int LUT_OFF = RING_END;                     // 2 x 256 (B | R) words (units alternate)
-constexpr int EXC_OFF = LUT_OFF + 2 * 256 * 4;        // 2 x EXC_CAP entries
-constexpr int RUNOFF_OFF = EXC_OFF + 2 * EXC_CAP * 4; // 2 x 33 run offsets
-constexpr int MISC_OFF = RUNOFF_OFF + 2 * 33 * 4;     // tmem base, abort flag
+constexpr int BMP = 128;  // rows per moe_align block (the MMA's N, at most)
+constexpr int NW = 4;     // shared-memory ring of packed codes + packed scales + scale words
+constexpr int NB = 4;     // shared-memory ring of activation tiles
+constexpr int NA = 4;     // TMEM ring of dequantised weight tiles
+constexpr int NDQ = 8;    // dequant warps
+constexpr int NEPI = 4;   // epilogue warps
+constexpr int W_PROD = 0, W_MMA = 1, W_LOAD = 2, W_SCALE = 3, DQ0 = 4, EPI0 = DQ0 + NDQ;
+constexpr int THREADS = (EPI0 + NEPI) * 32;
+constexpr int D_COLS = 256, A_COL0 = 256, A_SLOT_COLS = 64;  // TMEM columns
+
+constexpr int B_BYTES = BMP * 128;  // up to 128 token rows x 64 k bf16, 128-byte swizzled rows
+constexpr int B_OFF = 0;
+constexpr int TBL_BYTES = ITEM_COLS * 4;  // one scale word (4 k-groups) per row
+constexpr int W_SLOT = STAGE_BYTES + PAIR_BYTES + TBL_BYTES;
+constexpr int W_OFF = B_OFF + NB * B_BYTES;
+constexpr int S_REL = STAGE_BYTES, TBL_REL = STAGE_BYTES + PAIR_BYTES;
+constexpr int EXC_CAP = 2048;  // exception entries of one unit cached in shared memory
+constexpr int LUT_OFF = W_OFF + NW * W_SLOT;                     // 2 x 256 (B | R) words (units alternate)
+constexpr int EXC_OFF = LUT_OFF + 2 * 256 * 4;                   // EXC_CAP entries (scale warp only)
+constexpr int RUNOFF_OFF = EXC_OFF + EXC_CAP * 4;                // 33 run offsets (scale warp only)
+constexpr int IDS_OFF = (RUNOFF_OFF + 33 * 4 + 15) / 16 * 16;    // 128 activation rows (loader only)
+constexpr int MISC_OFF = IDS_OFF + BMP * 4;                      // tmem base, abort flag
 constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
-constexpr int NBARS = 4 * NST + 4;
-constexpr int SMEM = BAR_OFF + NBARS * 8 + 1024;      // + slack to align the base to 1024
+constexpr int NBARS = 3 * NW + 2 * NB + 2 * NA + 2 + 2;
+constexpr int SMEM_USED = BAR_OFF + NBARS * 8;
+// + slack to align the base to 1024; at least 116 KB so that two CTAs never share an SM (each holds all 512 columns)
+constexpr int SMEM = std::max(SMEM_USED + 1024, 116 * 1024);
+static_assert(B_BYTES % 1024 == 0 && W_OFF % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
+static_assert(W_SLOT % 16 == 0 && S_REL % 16 == 0, "bulk copies need 16-byte alignment");
+static_assert(A_COL0 == D_COLS && A_COL0 + NA * A_SLOT_COLS <= 512, "D and the A ring share the 512 TMEM columns");
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void dq_sync() { asm volatile("bar.sync 2, %0;" ::"n"(NDQ * 32) : "memory"); }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+// TMA gather of 4 rows of a 2-D tensor (box: 64 bf16 x 1 row, 128-byte swizzle) into 512 bytes of shared memory;
+// completion counted on an mbarrier. No multicast.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int x, int4 rows, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(rows.x), "r"(rows.y), "r"(rows.z), "r"(rows.w),
+      "r"(smem_u32(bar))
+      : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // K-major, 128-byte swizzle UMMA shared-memory descriptor of a tile whose 128-byte rows are contiguous and whose
 // 8-row groups are 1024 bytes apart (SBO); LBO is unused for swizzled K-major layouts (1); version 1 (sm_100).
@@ -83,17 +107,29 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
 __device__ __forceinline__ uint32_t idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D[tmem] (+)= A[tmem] x B[smem]: A is 128 lanes (rows) x 8 columns of bf16 pairs (k 2c, 2c + 1 in column c).
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n.reg .pred p;\n"
       "setp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
@@ -109,9 +145,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
 
 struct Bars {
-  uint64_t *wfull, *wempty, *afull, *aempty, *accfull, *accempty;
+  uint64_t *wfull, *wempty, *sfull, *bfull, *bempty, *afull, *aempty, *accfull, *accempty, *lutempty;
 };
 
 __device__ __forceinline__ bool wait_ab(uint64_t* bar, uint32_t par, uint64_t deadline, int* err, volatile int* ab) {
@@ -120,9 +161,14 @@ __device__ __forceinline__ bool wait_ab(uint64_t* bar, uint32_t par, uint64_t de
   *ab = 1;
   return false;
 }
+// Warp-uniform bounded wait: every role is a whole warp and some of them go on to warp-wide instructions, so the
+// lanes agree on the outcome (a lane that saw the deadline pass makes the whole warp give up).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t par, uint64_t deadline, int* err, volatile int* ab) {
+  return __all_sync(0xffffffffu, wait_ab(bar, par, deadline, err, ab));
+}
 
 struct UnitInfo {
-  int blk, item, e, nv;
+  int blk, item, e;
 };
 __device__ __forceinline__ UnitInfo unit_info(const GemmParams& p, int64_t u, int nt) {
   UnitInfo r;
@@ -132,34 +178,50 @@ __device__ __forceinline__ UnitInfo unit_info(const GemmParams& p, int64_t u, in
   return r;
 }
 
-__global__ void __launch_bounds__(THREADS, 1) moek_prefill_kernel(GemmParams p) {
+__global__ void __launch_bounds__(THREADS, 1)
+    moek_prefill_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap_a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
-  const Bars B{bars, bars + NST, bars + 2 * NST, bars + 3 * NST, bars + 4 * NST, bars + 4 * NST + 2};
+  Bars B;
+  B.wfull = bars;
+  B.wempty = B.wfull + NW;
+  B.sfull = B.wempty + NW;
+  B.bfull = B.sfull + NW;
+  B.bempty = B.bfull + NB;
+  B.afull = B.bempty + NB;
+  B.aempty = B.afull + NA;
+  B.accfull = B.aempty + NA;
+  B.accempty = B.accfull + 1;
+  B.lutempty = B.accempty + 1;
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem + LUT_OFF);
-  uint32_t* excs = reinterpret_cast<uint32_t*>(smem + EXC_OFF);
-  int* runoffs = reinterpret_cast<int*>(smem + RUNOFF_OFF);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + MISC_OFF + 4);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nt = p.N / ITEM_COLS, nstage = p.K / BK, nb = p.K / 128, nruns = nb;
+  const int nt = p.N / ITEM_COLS, nstage = p.K / BK, nb = p.K / 128;
 
   if (tid == 0) {
     *abort_flag = 0;
-    for (int i = 0; i < NST; i++) {
+    for (int i = 0; i < NW; i++) {
       mbar_init(B.wfull + i, 1);
       mbar_init(B.wempty + i, NDQ);
+      mbar_init(B.sfull + i, 1);
+    }
+    for (int i = 0; i < NB; i++) {
+      mbar_init(B.bfull + i, 1);
+      mbar_init(B.bempty + i, 1);
+    }
+    for (int i = 0; i < NA; i++) {
       mbar_init(B.afull + i, NDQ);
       mbar_init(B.aempty + i, 1);
     }
-    for (int i = 0; i < 2; i++) {
-      mbar_init(B.accfull + i, 1);
-      mbar_init(B.accempty + i, NEPI);
-    }
+    mbar_init(B.accfull, 1);
+    mbar_init(B.accempty, NEPI);
+    mbar_init(B.lutempty, NDQ);
+    mbar_init(B.lutempty + 1, NDQ);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // TMEM: all 512 columns (2 accumulator buffers x 2 halves x 128 columns)
+  if (warp == W_MMA) {  // TMEM: all 512 columns (D, then the A ring)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
                      smem_u32((const void*)tmem_slot))
                  : "memory");
@@ -175,26 +237,26 @@ __global__ void __launch_bounds__(THREADS, 1) moek_prefill_kernel(GemmParams p) 
   const int nblocks = min(p.num_post_pad[0] / p.block_m, p.max_blocks);
   const int64_t nunits = (int64_t)nblocks * nt;
 
-  if (warp == 0) {  // --------------------------------------------------------------------------- producer
+  if (warp == W_PROD) {  // ---------------------------------------------------------------------- producer
     uint32_t g = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
       if (ui.e < 0 || ui.e >= p.E) continue;
       for (int st = 0; st < nstage; st++, g++) {
-        const int s = g % NST;
-        if (g >= NST && !wait_ab(B.wempty + s, ((g / NST) - 1) & 1, deadline, p.err, abort_flag)) break;
+        const int s = g % NW;
+        if (g >= NW && !wait_warp(B.wempty + s, ((g / NW) - 1) & 1, deadline, p.err, abort_flag)) break;
         if (lane == 0) {
-          uint8_t* dst = smem + s * STAGE_STRIDE;
+          uint8_t* dst = smem + W_OFF + s * W_SLOT;
           mbar_expect_tx(B.wfull + s, STAGE_BYTES + PAIR_BYTES);
           const int64_t wi = ((int64_t)ui.e * nt + ui.item) * nstage + st;
-          bulk_g2s(dst + W_OFF, p.W + wi * STAGE_BYTES, STAGE_BYTES, B.wfull + s);
+          bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, B.wfull + s);
           const int64_t si = ((int64_t)ui.e * nt + ui.item) * nb + (st >> 1);
-          bulk_g2s(dst + S_OFF, p.SP + si * PAIR_BYTES, PAIR_BYTES, B.wfull + s);
+          bulk_g2s(dst + S_REL, p.SP + si * PAIR_BYTES, PAIR_BYTES, B.wfull + s);
         }
         __syncwarp();
       }
     }
-  } else if (warp == 1) {  // ------------------------------------------------------------------------ MMA
+  } else if (warp == W_MMA) {  // ---------------------------------------------------------------------- MMA
     uint32_t g = 0, un = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
@@ -205,153 +267,187 @@ __global__ void __launch_bounds__(THREADS, 1) moek_prefill_kernel(GemmParams p) 
         nv += __popc(__ballot_sync(0xffffffffu, r < p.block_m &&
                                                     p.sorted_ids[(int64_t)ui.blk * p.block_m + r] < p.num_ids));
       }
-      const int n = max(16, (nv + 15) & ~15);
-      const uint32_t idesc = idesc_bf16(n);
-      const int buf = un & 1;
-      if (un >= 2 && !wait_ab(B.accempty + buf, ((un >> 1) - 1) & 1, deadline, p.err, abort_flag)) break;
+      const uint32_t idesc = idesc_bf16(max(16, (nv + 15) & ~15));
+      if (un >= 1 && !wait_warp(B.accempty, (un - 1) & 1, deadline, p.err, abort_flag)) break;
       tc_fence_after();
       bool ok = true;
       for (int st = 0; st < nstage; st++, g++) {
-        const int s = g % NST;
-        if (!wait_ab(B.afull + s, (g / NST) & 1, deadline, p.err, abort_flag)) {
+        const int a = g % NA, b = g % NB;
+        if (!wait_warp(B.afull + a, (g / NA) & 1, deadline, p.err, abort_flag) ||
+            !wait_warp(B.bfull + b, (g / NB) & 1, deadline, p.err, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a0 = smem_u32(smem + s * STAGE_STRIDE + A_OFF), b0 = smem_u32(smem + s * STAGE_STRIDE + B_OFF);
+          const uint32_t b0 = smem_u32(smem + B_OFF + b * B_BYTES);
+          const uint32_t a0 = tmem + A_COL0 + a * A_SLOT_COLS;
 #pragma unroll
           for (int ks = 0; ks < 4; ks++) {
             const uint64_t bd = umma_desc_k_sw128(b0 + 32 * ks);
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-              const uint64_t ad = umma_desc_k_sw128(a0 + h * (128 * 128) + 32 * ks);
-              umma_bf16(tmem + buf * 256 + h * 128, ad, bd, idesc, (st > 0 || ks > 0) ? 1u : 0u);
-            }
+            for (int h = 0; h < 2; h++)
+              umma_ts(tmem + h * 128, a0 + h * 32 + ks * 8, bd, idesc, (st > 0 || ks > 0) ? 1u : 0u);
           }
-          umma_commit(B.aempty + s);  // the stage's tiles may be overwritten once these MMAs completed
-          if (st == nstage - 1) umma_commit(B.accfull + buf);
+          umma_commit(B.aempty + a);  // the A and B slots may be refilled once these MMAs completed
+          umma_commit(B.bempty + b);
+          if (st == nstage - 1) umma_commit(B.accfull);
         }
         __syncwarp();
       }
       if (!ok) break;
       un++;
     }
-  } else if (warp < EPI0) {  // ------------------------------------------------------------------- dequant
-    const int dw = warp - DQ0, dt = tid - DQ0 * 32;  // dequant warp 0..7, thread 0..255
-    const int gq = lane >> 2, c = lane & 3;
-    // scale-byte decode: thread dt < 128 owns chunk (dt & 15) of run (dt >> 4) & 1 for k-group kk = dt >> 5
-    const int s_kk = dt >> 5, s_run = (dt >> 4) & 1, s_ch = dt & 15;
-    int s_dst[8];
+  } else if (warp == W_LOAD) {  // ------------------------------------------------------------- activation loader
+    int* rowc = reinterpret_cast<int*>(smem + IDS_OFF);
+    const int rows_a = p.num_ids / p.a_div;  // rows of A; a coordinate of rows_a reads zeros
+    uint32_t g = 0;
+    for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
+      const UnitInfo ui = unit_info(p, u, nt);
+      if (ui.e < 0 || ui.e >= p.E) continue;
+      const int64_t row0 = (int64_t)ui.blk * p.block_m;
+      __syncwarp();  // the previous unit's gathers were issued from these rows
+      int nv = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++) s_dst[i] = s_run * 128 + position_slot(8 * s_ch + i);
+      for (int j = 0; j < BMP / 32; j++) {
+        const int r = lane + 32 * j;
+        const int id = r < p.block_m ? p.sorted_ids[row0 + r] : p.num_ids;
+        const bool valid = id < p.num_ids;
+        rowc[r] = valid ? id / p.a_div : rows_a;
+        nv += __popc(__ballot_sync(0xffffffffu, valid));
+      }
+      __syncwarp();
+      const int ng = (nv + 3) >> 2;  // gathers of 4 rows; the block's valid rows come first
+      bool ok = true;
+      for (int st = 0; st < nstage; st++, g++) {
+        const int b = g % NB;
+        if (g >= NB && !wait_warp(B.bempty + b, ((g / NB) - 1) & 1, deadline, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_expect_tx(B.bfull + b, ng * 4 * 128);
+        __syncwarp();
+        if (lane < ng)
+          tma_gather4(smem + B_OFF + b * B_BYTES + lane * 512, &tmap_a, st * BK,
+                      *reinterpret_cast<const int4*>(rowc + 4 * lane), B.bfull + b);
+      }
+      if (!ok) break;
+    }
+  } else if (warp == W_SCALE) {  // ------------------------------------------------------------------ scale words
+    uint32_t* excs = reinterpret_cast<uint32_t*>(smem + EXC_OFF);
+    int* ro = reinterpret_cast<int*>(smem + RUNOFF_OFF);
+    const int run = lane >> 4, chk = lane & 15;  // this lane's 8 positions: run `run`, positions 8 chk .. 8 chk + 7
+    int rows[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) rows[i] = run * 128 + position_slot(8 * chk + i);
     uint32_t g = 0, un = 0;
-    // no abort test in the loop header: the dequant warps share a named barrier, so they all run every unit and
-    // stage; after an abort every wait fails at once and the work is skipped
+    for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
+      const UnitInfo ui = unit_info(p, u, nt);
+      if (ui.e < 0 || ui.e >= p.E) continue;
+      const int lb = un & 1;
+      const int64_t key0 = ((int64_t)ui.e * nt + ui.item) * nb;
+      const int o0 = p.exc_off[key0];
+      __syncwarp();  // the previous unit's exception lists are no longer read
+      for (int j = lane; j <= nb; j += 32) ro[j] = p.exc_off[key0 + j] - o0;
+      __syncwarp();
+      const int nexc = ro[nb];
+      const bool exc_smem = nexc <= EXC_CAP;
+      if (exc_smem)
+        for (int j = lane; j < nexc; j += 32) excs[j] = p.exc_ent[o0 + j];
+      const uint32_t* exl = exc_smem ? excs : p.exc_ent + o0;
+      const int r0g = p.gate_up ? ui.item : 2 * ui.item;
+      // the (B | R) table of this expert, once the dequant warps finished the unit that used this buffer last
+      if (un >= 2 && !wait_warp(B.lutempty + lb, ((un >> 1) - 1) & 1, deadline, p.err, abort_flag)) break;
+      const float gsc = p.G[ui.e];
+#pragma unroll
+      for (int j = 0; j < 8; j++) lut[lb * 256 + lane + 32 * j] = scale_word(lane + 32 * j, gsc);
+      __syncwarp();
+      bool ok = true;
+      for (int st = 0; st < nstage; st++, g++) {
+        const int s = g % NW;
+        if (!wait_warp(B.wfull + s, (g / NW) & 1, deadline, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* slot = smem + W_OFF + s * W_SLOT;
+        uint32_t* tbl = reinterpret_cast<uint32_t*>(slot + TBL_REL);
+        const uint8_t* runp = slot + S_REL + run * RUN_BYTES;
+        const uint32_t b4 = runp[chk] * 0x01010101u;
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const int kg = (st & 1) * 4 + kk;
+          const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kg * 64 + chk * 4);
+          lo[kk] = (q & 0x0F0F0F0Fu) + b4;         // positions 8 chk + 0..3
+          hi[kk] = ((q >> 4) & 0x0F0F0F0Fu) + b4;  // positions 8 chk + 4..7
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const uint32_t* src = i < 4 ? lo : hi;
+          const uint32_t bi = i & 3, sel = bi | ((bi + 4) << 4);
+          tbl[rows[i]] = prmt(prmt(src[0], src[1], sel), prmt(src[2], src[3], sel), 0x5410);
+        }
+        __syncwarp();
+        const int rn = st >> 1;
+        for (int j = ro[rn] + lane; j < ro[rn + 1]; j += 32) {
+          const uint32_t en = exl[j];
+          const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+          if ((kg >> 2) != (st & 1)) continue;
+          const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
+          reinterpret_cast<uint8_t*>(tbl)[row * 4 + (kg & 3)] = (uint8_t)(en >> 24);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(B.sfull + s);
+      }
+      if (!ok) break;
+      un++;
+    }
+  } else if (warp < EPI0) {  // ------------------------------------------------------------------- dequant
+    const int dw = warp - DQ0, h = dw >> 2, q = warp & 3;
+    const int row = 128 * h + 32 * q + lane;  // this thread's weight row within the item
+    const int sw = ((row >> 2) & 1) << 4;     // byte offset of the row's first 16-byte half (swizzle)
+    const uint32_t t_row = tmem + ((uint32_t)(32 * q) << 16) + A_COL0 + 32 * h;
+    uint32_t g = 0, un = 0;
     for (int64_t u = blockIdx.x; u < nunits; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
       if (ui.e < 0 || ui.e >= p.E) {
-        if (dt == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
+        if (dw == 0 && lane == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
         continue;
       }
-      const int lb = un & 1;
-      uint32_t* lt = lut + lb * 256;
-      uint32_t* ex = excs + lb * EXC_CAP;
-      int* ro = runoffs + lb * 33;
-      const int64_t row0 = (int64_t)ui.blk * p.block_m;
-      // per unit: the (B | R) table for this expert, the exception lists of the item, the valid rows
-      const float gsc = p.G[ui.e];
-      lt[dt] = scale_word(dt, gsc);
-      const int64_t key0 = ((int64_t)ui.e * nt + ui.item) * nb;
-      const int o0 = p.exc_off[key0];
-      if (dt <= nruns) ro[dt] = p.exc_off[key0 + dt] - o0;
-      dq_sync();
-      const int nexc = ro[nruns];
-      const bool exc_smem = nexc <= EXC_CAP;
-      if (exc_smem)
-        for (int j = dt; j < nexc; j += NDQ * 32) ex[j] = p.exc_ent[o0 + j];
-      const uint32_t* exl = exc_smem ? ex : p.exc_ent + o0;
-      int my_id[4];
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int r = (dt >> 3) + 32 * j;  // the rows this thread copies (8 16-byte chunks per row)
-        my_id[j] = r < p.block_m ? p.sorted_ids[row0 + r] : p.num_ids;
-      }
-      dq_sync();
-      const int r0g = p.gate_up ? ui.item : 2 * ui.item;
+      const uint32_t* lt = lut + (un & 1) * 256;
       for (int st = 0; st < nstage; st++, g++) {
-        const int s = g % NST;
-        uint8_t* sb = smem + s * STAGE_STRIDE;
-        const bool have_w = wait_ab(B.wfull + s, (g / NST) & 1, deadline, p.err, abort_flag);
-        const bool free_a = g < NST || wait_ab(B.aempty + s, ((g / NST) - 1) & 1, deadline, p.err, abort_flag);
-        const bool live = have_w && free_a && !*abort_flag;
-        // 1. activation rows of this stage into the swizzled B tile (cp.async, 16 bytes each)
+        const int s = g % NW, a = g % NA;
+        const bool have_w = wait_warp(B.wfull + s, (g / NW) & 1, deadline, p.err, abort_flag) &&
+                            wait_warp(B.sfull + s, (g / NW) & 1, deadline, p.err, abort_flag);
+        const bool free_a = g < NA || wait_warp(B.aempty + a, ((g / NA) - 1) & 1, deadline, p.err, abort_flag);
+        // warp-uniform: tcgen05.st is a warp-wide instruction
+        const bool live = __all_sync(0xffffffffu, have_w && free_a && !*abort_flag);
         if (live) {
-          const uint32_t bbase = smem_u32(sb + B_OFF);
-          const int ch = dt & 7;
+          tc_fence_after();
+          const uint8_t* slot = smem + W_OFF + s * W_SLOT;
+          const uint4 c0 = *reinterpret_cast<const uint4*>(slot + row * 32 + sw);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(slot + row * 32 + (sw ^ 16));
+          const uint32_t sc = reinterpret_cast<const uint32_t*>(slot + TBL_REL)[row];
+          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          uint32_t v[32];
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            const int r = (dt >> 3) + 32 * j;
-            const int id = my_id[j];
-            if (id < p.num_ids) {
-              const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + st * BK + ch * 8;
-              cp_async16(bbase + r * 128 + ((ch ^ (r & 7)) << 4), src);
-            }
+          for (int kk = 0; kk < 4; kk++) {
+            const uint32_t lw = lt[(sc >> (8 * kk)) & 0xFF];
+            const ScaleBR sbr{prmt_b(lw, 0x1010), prmt_b(lw, 0x3232)};
+            dequant_word(words[2 * kk], sbr, v + 8 * kk);
+            dequant_word(words[2 * kk + 1], sbr, v + 8 * kk + 4);
           }
+          tmem_st32(t_row + a * A_SLOT_COLS, v);
         }
-        // 2. scale bytes of the stage (4 k-groups x 256 rows), then the exceptions that fall in it
-        uint8_t* scb = sb + SCB_OFF;
-        if (live && dt < 128) {
-          const uint8_t* runp = sb + S_OFF + s_run * RUN_BYTES;
-          const uint32_t b4 = runp[s_ch] * 0x01010101u;
-          const int kg = (st & 1) * 4 + s_kk;
-          const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kg * 64 + s_ch * 4);
-          const uint32_t lo = (q & 0x0F0F0F0Fu) + b4, hi = ((q >> 4) & 0x0F0F0F0Fu) + b4;
-          uint8_t* row = scb + s_kk * SCB_STRIDE;
-#pragma unroll
-          for (int i = 0; i < 8; i++) row[s_dst[i]] = (uint8_t)(((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF);
-        }
-        dq_sync();
-        if (live) {
-          const int rr = st >> 1;
-          for (int j = ro[rr] + dt; j < ro[rr + 1]; j += NDQ * 32) {
-            const uint32_t en = exl[j];
-            const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-            if ((kg >> 2) != (st & 1)) continue;
-            const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
-            scb[(kg & 3) * SCB_STRIDE + slot_e] = (uint8_t)(en >> 24);
-          }
-        }
-        dq_sync();
-        // 3. the oracle's bf16 weights of this warp's two 16-row groups (one per half) into the A tiles
-        if (live) {
-          const uint8_t* scr = scb + c * SCB_STRIDE;
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            const int G = h * 8 + dw;
-            const uint4 q = *reinterpret_cast<const uint4*>(sb + W_OFF + (G * 32 + lane) * 16);
-            const int rA = 16 * dw + gq, rB = rA + 8;  // rows within the half
-            const uint32_t wa = lt[scr[h * 128 + rA]], wb = lt[scr[h * 128 + rB]];
-            const ScaleBR sa{prmt_b(wa, 0x1010), prmt_b(wa, 0x3232)}, sbv{prmt_b(wb, 0x1010), prmt_b(wb, 0x3232)};
-            uint8_t* at = sb + A_OFF + h * (128 * 128);
-            const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const int r = (j & 1) ? rB : rA, chunk = 2 * c + (j >> 1);
-              uint32_t o[4];
-              dequant_word(words[j], (j & 1) ? sbv : sa, o);
-              *reinterpret_cast<uint4*>(at + r * 128 + ((chunk ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-            }
-          }
-        }
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0 && have_w) mbar_arrive(B.wempty + s);  // packed codes and scales consumed
-        cp_async_wait_all();
-        fence_async_smem();  // generic-proxy writes (st.shared, cp.async) -> visible to the tensor core
-        __syncwarp();
-        if (lane == 0) mbar_arrive(B.afull + s);
-        dq_sync();  // the scale-byte table of this slot is rewritten next time round
+        if (lane == 0) {
+          if (have_w) mbar_arrive(B.wempty + s);  // packed codes and scale words consumed
+          mbar_arrive(B.afull + a);
+        }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B.lutempty + (un & 1));
       un++;
     }
   } else {  // ------------------------------------------------------------------------------------ epilogue
@@ -372,10 +468,9 @@ __global__ void __launch_bounds__(THREADS, 1) moek_prefill_kernel(GemmParams p) 
         nv += __popc(__ballot_sync(0xffffffffu, ids[j] < p.num_ids));
         wts[j] = (!p.gate_up && ids[j] < p.num_ids) ? p.topk_w[ids[j]] : 0.f;
       }
-      const int buf = un & 1;
-      if (!wait_ab(B.accfull + buf, (un >> 1) & 1, deadline, p.err, abort_flag)) break;
+      if (!wait_warp(B.accfull, un & 1, deadline, p.err, abort_flag)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + buf * 256;
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
       const int row = 32 * q + lane;  // weight row within the half
       for (int c0 = 0; c0 < nv; c0 += 32) {
         float v0[32], v1[32];
@@ -399,14 +494,14 @@ __global__ void __launch_bounds__(THREADS, 1) moek_prefill_kernel(GemmParams p) 
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(B.accempty + buf);
+      if (lane == 0) mbar_arrive(B.accempty);
       un++;
     }
   }
   // ------------------------------------------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == W_MMA) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
   }
@@ -416,13 +511,37 @@ __global__ void __launch_bounds__(THREADS, 1) moek_prefill_kernel(GemmParams p) 
 
 int prefill_block_m() { return pf::BMP; }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver library).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
 cudaError_t launch_prefill(const GemmParams& p, int sms, cudaStream_t st) {
   const int nt = p.N / ITEM_COLS;
   const int64_t units = (int64_t)p.max_blocks * nt;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sms, units));
+  // A as a 2-D bf16 tensor [rows, K] (K contiguous), read 64 k x 1 row per gathered row, 128-byte swizzle
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return cudaErrorNotSupported;
+  CUtensorMap tmap;
+  const cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)std::max(1, p.num_ids / p.a_div)};
+  const cuuint64_t strides[1] = {(cuuint64_t)p.K * 2};
+  const cuuint32_t box[2] = {BK, 1}, estr[2] = {1, 1};
+  if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(p.A), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(pf::moek_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
   if (e != cudaSuccess) return e;
-  e = launch_pdl(pf::moek_prefill_kernel, dim3(grid), dim3(pf::THREADS), pf::SMEM, st, p);
+  e = launch_pdl(pf::moek_prefill_kernel, dim3(grid), dim3(pf::THREADS), pf::SMEM, st, p, tmap);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -154,6 +154,15 @@ def combine(rows: torch.Tensor, top_k: int, out: torch.Tensor = None) -> torch.T
 DECODE_MAX_M = int(os.environ.get("MOEK_B200_DECODE_MAX_M", "64"))  # split-k with fused epilogues up to this M
 
 
+def launches_per_layer(m: int, top_k: int) -> int:
+    """Kernels of this library one fused_moe call launches: decode = align, gate_up GEMM, SwiGLU epilogue, down GEMM,
+    router-weight + top-k epilogue; prefill = align (one kernel up to 1024 indices, else count/offsets/scatter),
+    gate_up GEMM, down GEMM, top-k combine."""
+    if m <= DECODE_MAX_M:
+        return LAUNCHES_PER_LAYER
+    return (1 if m * top_k <= 1024 else 3) + 3
+
+
 def _splits(k: int, units_per_split: int, grid: int) -> int:
     """k-split (whole 128-k runs per unit) that balances units over the grid best: the split whose busiest CTA has the
     least work (in stages), preferring fewer splits on ties."""

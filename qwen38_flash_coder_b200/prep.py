@@ -12,13 +12,14 @@ Output, per matrix:
   (window choice by pairwise counting instead of sort + searchsorted).
 - **global scale**: ``weight_scale_2 * 2^119 / scale_factor`` (marlin_utils_fp4.py:134-146,385-386).
 - **weights**: this build's tiled layout, an int32 tensor of the reference's shape [E, K/16, 2N] (same bytes as the
-  checkpoint, reordered). Per (expert, 256-column item, 64-k stage) one contiguous 8 KB block; inside it 16 groups
-  of 16 columns, each 32 lanes x 4 words of 8 codes. Lane L = 4g + c, word j holds column ``16G + g + 8(j & 1)``
-  of the item and the 8 consecutive k ``64s + 16c + 8(j >> 1) + i`` (i = 0..7) with code i in nibble
-  ``NIBBLE_OF[i]``: a lane's 16 bytes are rows g and g + 8 of a 16-row group over one whole 16-k group (one scale
-  per row), i.e. the A operand of four mma.sync m16n8k16 steps, and each word decodes, two codes at a time, into
-  bf16 pairs (k, k+1) in order. Item slots 0..127 are gate columns ``128t + slot`` and 128..255 the
-  matching up columns ``I + 128t + slot - 128`` (gate_up), or columns ``256t + slot`` (down).
+  checkpoint, reordered). Per (expert, 256-row item, 64-k stage) one contiguous 8 KB block of 256 rows x 32 bytes:
+  row r holds the item's row r over the stage's 64 k as 8 words, word w = the 8 consecutive k ``64s + 8w + i``
+  (i = 0..7) with code i in nibble ``NIBBLE_OF[i]``, so words 2c and 2c + 1 are k-group c (one scale) and each word
+  decodes, two codes at a time, into bf16 pairs (k, k+1) in order. The row's two 16-byte halves are swapped when
+  bit 2 of r is set, so that 8 threads reading 16 bytes of 8 consecutive rows, or 32 lanes reading 8 bytes
+  (k-group c of rows g and g + 8, the A operand of mma.sync m16n8k16), hit distinct shared-memory banks. Item rows
+  0..127 are gate rows ``128t + r`` and 128..255 the matching up rows ``I + 128t + r - 128`` (gate_up), or rows
+  ``256t + r`` (down).
 """
 import torch
 
@@ -127,6 +128,11 @@ def item_columns(n: int, gate_up: bool, device=None) -> torch.Tensor:
     return 256 * t + slot
 
 
+def _swizzle_rows(device) -> torch.Tensor:
+    """Rows of a stage block whose two 16-byte halves are swapped (bit 2 of the row index set)."""
+    return ((torch.arange(256, device=device) >> 2) & 1).bool()
+
+
 def tile_weights(codes: torch.Tensor, gate_up: bool, chunk: int = 16) -> torch.Tensor:
     """Checkpoint codes uint8 [E, N, K/2] -> this build's tiled int32 [E, K/16, 2N] (see the module docstring)."""
     e, n, k2 = codes.shape
@@ -134,14 +140,15 @@ def tile_weights(codes: torch.Tensor, gate_up: bool, chunk: int = 16) -> torch.T
     nt, ns = n // 256, k // 64
     cols = item_columns(n, gate_up, codes.device).flatten()
     shifts = torch.tensor([4 * p for p in NIBBLE_OF], dtype=torch.int64, device=codes.device)
+    swap = _swizzle_rows(codes.device)
     out = torch.empty((e, k // 16, 2 * n), dtype=torch.int32, device=codes.device)
     for e0 in range(0, e, chunk):
         e1 = min(e, e0 + chunk)
         c = codes[e0:e1][:, cols, :]
-        nib = torch.stack([c & 0xF, c >> 4], -1).view(e1 - e0, nt, 16, 2, 8, ns, 4, 2, 8)
-        # [e, t, G, jr, g, s, c, jc, i] -> [e, t, s, G, g, c, jc, jr, i]
-        nib = nib.permute(0, 1, 5, 2, 4, 6, 7, 3, 8).to(torch.int64)
-        word = (nib << shifts).sum(-1)
+        nib = torch.stack([c & 0xF, c >> 4], -1).view(e1 - e0, nt, 256, ns, 8, 8)  # [e, t, r, s, w, i]
+        word = (nib.permute(0, 1, 3, 2, 4, 5).to(torch.int64) << shifts).sum(-1)  # [e, t, s, r, w]
+        word = word.view(e1 - e0, nt, ns, 256, 2, 4)
+        word[:, :, :, swap] = word[:, :, :, swap].flip(-2)
         word = torch.where(word >= 2 ** 31, word - 2 ** 32, word).to(torch.int32)
         out[e0:e1] = word.reshape(e1 - e0, k // 16, 2 * n)
     return out
@@ -153,9 +160,11 @@ def untile_weights(w: torch.Tensor, n: int, gate_up: bool) -> torch.Tensor:
     k = w.shape[1] * 16
     nt, ns = n // 256, k // 64
     shifts = torch.tensor([4 * p for p in NIBBLE_OF], dtype=torch.int64, device=w.device)
-    word = w.to(torch.int64).view(e, nt, ns, 16, 8, 4, 2, 2) & 0xFFFFFFFF
-    nib = ((word[..., None] >> shifts) & 0xF).to(torch.uint8)  # [e, t, s, G, g, c, jc, jr, i]
-    nib = nib.permute(0, 1, 3, 7, 4, 2, 5, 6, 8).reshape(e, nt * 256, k)  # [e, t, G, jr, g, s, c, jc, i]
+    word = (w.to(torch.int64) & 0xFFFFFFFF).view(e, nt, ns, 256, 2, 4).clone()
+    swap = _swizzle_rows(w.device)
+    word[:, :, :, swap] = word[:, :, :, swap].flip(-2)
+    nib = ((word.view(e, nt, ns, 256, 8)[..., None] >> shifts) & 0xF).to(torch.uint8)  # [e, t, s, r, w, i]
+    nib = nib.permute(0, 1, 3, 2, 4, 5).reshape(e, nt * 256, k)
     out = torch.empty((e, n, k), dtype=torch.uint8, device=w.device)
     out[:, item_columns(n, gate_up, w.device).flatten(), :] = nib
     return (out[..., 0::2] | (out[..., 1::2] << 4)).contiguous()

@@ -56,18 +56,19 @@ def test_tile_weights_round_trip(gate_up, n, k):
 
 
 def test_tile_weights_word_contents():
-    """Spot-check the documented layout: word j of lane 4g + c in group G of (item t, stage s)."""
+    """Spot-check the documented layout: word w of row r in the block of (item t, stage s), halves swizzled."""
     n, k = 512, 256
     codes = torch.randint(0, 256, (1, n, k // 2), dtype=torch.uint8, generator=torch.Generator().manual_seed(3))
     w = prep.tile_weights(codes, True).view(-1)
     cols = prep.item_columns(n, True)
     rng = np.random.default_rng(0)
-    for _ in range(200):
-        t, s, G, g, c, j = (int(rng.integers(x)) for x in (n // 256, k // 64, 16, 8, 4, 4))
-        word = int(w[((((t * (k // 64) + s) * 16 + G) * 32 + 4 * g + c) * 4 + j)]) & 0xFFFFFFFF
-        col = int(cols[t, 16 * G + g + 8 * (j & 1)])
+    for _ in range(300):
+        t, s, r, wd = (int(rng.integers(x)) for x in (n // 256, k // 64, 256, 8))
+        pos = (((wd >> 2) ^ ((r >> 2) & 1)) << 2) | (wd & 3)
+        word = int(w[((t * (k // 64) + s) * 256 + r) * 8 + pos]) & 0xFFFFFFFF
+        col = int(cols[t, r])
         for i in range(8):
-            kk = 64 * s + 16 * c + 8 * (j >> 1) + i
+            kk = 64 * s + 8 * wd + i
             byte = int(codes[0, col, kk // 2])
             code = (byte >> 4) if kk & 1 else (byte & 15)
             assert (word >> (4 * prep.NIBBLE_OF[i])) & 15 == code
