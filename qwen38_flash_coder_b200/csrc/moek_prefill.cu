@@ -16,8 +16,10 @@
 //   MMA       = warp 1 (one lane): per stage 2 halves x 4 k16 steps of tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16
 //               -> fp32), A from a TMEM ring slot, B from a shared-memory K-major SWIZZLE_128B tile, D in TMEM.
 //               tcgen05.commit releases the A and B slots and, after a unit's last stage, hands D to the epilogue.
-//               Warp 1 also allocates and frees the 512 TMEM columns: D = columns 0-255 (two halves x 128),
-//               A ring = columns 256-511 (4 slots x two halves x 32 columns of bf16 pairs).
+//               Warp 1 also allocates and frees the 512 TMEM columns: D = columns 0-319 (four accumulators of <= 80
+//               columns for blocks of <= 80 padded rows, else two of <= 128), A ring = columns 320-511 (3 slots x two
+//               halves x 32 columns of bf16 pairs). An MMA costs about the same for any N <= 256 and chained MMAs
+//               into one accumulator wait on each other, so more independent accumulators means more MMAs in flight.
 //   loader    = warp 2: the block's activation rows gathered by TMA (cp.async.bulk.tensor tile::gather4, no
 //               multicast: 4 rows of 64 k per instruction, one instruction per lane) into the 128-byte-swizzled B tile
 //               of the stage; rows past the block's valid ones read out of bounds and arrive as zeros.
@@ -50,12 +52,15 @@ namespace pf {
 constexpr int BMP = 128;  // rows per moe_align block (the MMA's N, at most)
 constexpr int NW = 4;     // shared-memory ring of packed codes + packed scales + scale words
 constexpr int NB = 4;     // shared-memory ring of activation tiles
-constexpr int NA = 4;     // TMEM ring of dequantised weight tiles
+constexpr int NA = 3;     // TMEM ring of dequantised weight tiles
 constexpr int NDQ = 8;    // dequant warps
 constexpr int NEPI = 4;   // epilogue warps
 constexpr int W_PROD = 0, W_MMA = 1, W_LOAD = 2, W_SCALE = 3, DQ0 = 4, EPI0 = DQ0 + NDQ;
 constexpr int THREADS = (EPI0 + NEPI) * 32;
-constexpr int D_COLS = 256, A_COL0 = 256, A_SLOT_COLS = 64;  // TMEM columns
+// TMEM columns. D: a block of N <= QUAD_N padded rows keeps four accumulators (half h, k16-step parity p at column
+// (2h + p) * QUAD_N), so four independent MMA chains are in flight; larger blocks keep two (half h at column 128h).
+// The A ring follows.
+constexpr int QUAD_N = 80, D_COLS = 4 * QUAD_N, A_COL0 = D_COLS, A_SLOT_COLS = 64;
 
 constexpr int B_BYTES = BMP * 128;  // up to 128 token rows x 64 k bf16, 128-byte swizzled rows
 constexpr int B_OFF = 0;
@@ -76,7 +81,7 @@ constexpr int SMEM_USED = BAR_OFF + NBARS * 8;
 constexpr int SMEM = std::max(SMEM_USED + 1024, 116 * 1024);
 static_assert(B_BYTES % 1024 == 0 && W_OFF % 1024 == 0, "swizzled tiles stay 1024-byte aligned");
 static_assert(W_SLOT % 16 == 0 && S_REL % 16 == 0, "bulk copies need 16-byte alignment");
-static_assert(A_COL0 == D_COLS && A_COL0 + NA * A_SLOT_COLS <= 512, "D and the A ring share the 512 TMEM columns");
+static_assert(A_COL0 >= 256 && A_COL0 + NA * A_SLOT_COLS <= 512, "D and the A ring share the 512 TMEM columns");
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -131,20 +136,43 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
+// 16-column loads (32 lanes x 16 columns each) issued together, then one wait.
+#define MOEK_LD16(T, X)                                                                                              \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];" \
+               : "=r"(X[0]), "=r"(X[1]), "=r"(X[2]), "=r"(X[3]), "=r"(X[4]), "=r"(X[5]), "=r"(X[6]), "=r"(X[7]),       \
+                 "=r"(X[8]), "=r"(X[9]), "=r"(X[10]), "=r"(X[11]), "=r"(X[12]), "=r"(X[13]), "=r"(X[14]), "=r"(X[15])  \
+               : "r"(T))
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  uint32_t r[16], q[16];
+  MOEK_LD16(ta, r);
+  MOEK_LD16(tb, q);
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; i++) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(q[i]);
+  }
 }
+__device__ __forceinline__ void tmem_ld16x4(uint32_t ta, uint32_t tb, uint32_t tc, uint32_t td, float* va, float* vb,
+                                            float* vc, float* vd) {
+  uint32_t r[16], q[16], x[16], y[16];
+  MOEK_LD16(ta, r);
+  MOEK_LD16(tb, q);
+  MOEK_LD16(tc, x);
+  MOEK_LD16(td, y);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(q[i]);
+    vc[i] = __uint_as_float(x[i]);
+    vd[i] = __uint_as_float(y[i]);
+  }
+}
+#undef MOEK_LD16
+// SiLU with the hardware exponent and the approximate divide (a few fp32 ulps; the product is rounded to bf16 next).
+// x -> -inf gives x * 0 = -0, the limit.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
@@ -261,13 +289,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
       if (ui.e < 0 || ui.e >= p.E) continue;
-      int nv = 0;
-      for (int r0 = 0; r0 < BMP; r0 += 32) {
-        const int r = r0 + lane;
-        nv += __popc(__ballot_sync(0xffffffffu, r < p.block_m &&
-                                                    p.sorted_ids[(int64_t)ui.blk * p.block_m + r] < p.num_ids));
+      int ids[BMP / 32], nv = 0;
+#pragma unroll
+      for (int j = 0; j < BMP / 32; j++) {  // all loads first, then the ballots
+        const int r = lane + 32 * j;
+        ids[j] = r < p.block_m ? p.sorted_ids[(int64_t)ui.blk * p.block_m + r] : p.num_ids;
       }
-      const uint32_t idesc = idesc_bf16(max(16, (nv + 15) & ~15));
+#pragma unroll
+      for (int j = 0; j < BMP / 32; j++) nv += __popc(__ballot_sync(0xffffffffu, ids[j] < p.num_ids));
+      const int nalloc = max(16, (nv + 15) & ~15);
+      const uint32_t idesc = idesc_bf16(nalloc);
+      const bool quad = nalloc <= QUAD_N;
       if (un >= 1 && !wait_warp(B.accempty, (un - 1) & 1, deadline, p.err, abort_flag)) break;
       tc_fence_after();
       bool ok = true;
@@ -286,8 +318,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int ks = 0; ks < 4; ks++) {
             const uint64_t bd = umma_desc_k_sw128(b0 + 32 * ks);
 #pragma unroll
-            for (int h = 0; h < 2; h++)
-              umma_ts(tmem + h * 128, a0 + h * 32 + ks * 8, bd, idesc, (st > 0 || ks > 0) ? 1u : 0u);
+            for (int h = 0; h < 2; h++) {
+              const uint32_t d = quad ? (2 * h + (ks & 1)) * QUAD_N : h * 128;
+              umma_ts(tmem + d, a0 + h * 32 + ks * 8, bd, idesc, (st > 0 || ks >= (quad ? 2 : 1)) ? 1u : 0u);
+            }
           }
           umma_commit(B.aempty + a);  // the A and B slots may be refilled once these MMAs completed
           umma_commit(B.bempty + b);
@@ -312,10 +346,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < BMP / 32; j++) {
         const int r = lane + 32 * j;
         const int id = r < p.block_m ? p.sorted_ids[row0 + r] : p.num_ids;
-        const bool valid = id < p.num_ids;
-        rowc[r] = valid ? id / p.a_div : rows_a;
-        nv += __popc(__ballot_sync(0xffffffffu, valid));
+        rowc[r] = id < p.num_ids ? id / p.a_div : rows_a;
       }
+#pragma unroll
+      for (int j = 0; j < BMP / 32; j++) nv += __popc(__ballot_sync(0xffffffffu, rowc[lane + 32 * j] < rows_a));
       __syncwarp();
       const int ng = (nv + 3) >> 2;  // gathers of 4 rows; the block's valid rows come first
       bool ok = true;
@@ -472,20 +506,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
       const int row = 32 * q + lane;  // weight row within the half
-      for (int c0 = 0; c0 < nv; c0 += 32) {
-        float v0[32], v1[32];
-        tmem_ld32(tbase + c0, v0);
-        tmem_ld32(tbase + 128 + c0, v1);
-        const int jj = c0 >> 5;
+      const bool quad = max(16, (nv + 15) & ~15) <= QUAD_N;
+      for (int c0 = 0; c0 < nv; c0 += 16) {
+        float v0[16], v1[16];
+        if (quad) {  // sum the two k-parity accumulators of each half
+          float g1[16], u1[16];
+          tmem_ld16x4(tbase + c0, tbase + QUAD_N + c0, tbase + 2 * QUAD_N + c0, tbase + 3 * QUAD_N + c0, v0, g1, v1,
+                      u1);
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+          for (int j = 0; j < 16; j++) {
+            v0[j] += g1[j];
+            v1[j] += u1[j];
+          }
+        } else {
+          tmem_ld16x2(tbase + c0, tbase + 128 + c0, v0, v1);
+        }
+        const int jj = c0 >> 5, l0 = c0 & 16;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
           if (c0 + j >= nv) break;
-          const int id = __shfl_sync(0xffffffffu, ids[jj], j);
+          const int id = __shfl_sync(0xffffffffu, ids[jj], l0 + j);
           if (p.gate_up) {
             static_cast<__nv_bfloat16*>(p.out)[(int64_t)id * I + 128 * ui.item + row] =
-                __float2bfloat16_rn(silu(v0[j]) * v1[j]);
+                __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
           } else {
-            const float w = __shfl_sync(0xffffffffu, wts[jj], j);
+            const float w = __shfl_sync(0xffffffffu, wts[jj], l0 + j);
             float* orow = p.part + (int64_t)id * p.N + 256 * ui.item;
             orow[row] = w * v0[j];
             orow[128 + row] = w * v1[j];
