@@ -21,8 +21,13 @@ memory and its outputs read back inside the timed region. ``roofline`` = the gat
 
 ``--impl reference`` times the reference's CPU path (the fp32 dequantise-then-matmul oracle of
 bench/moek/problem.py:51-67, restated in oracle/moe_ref.py) on the host cores, same metric and unit.
-Multi-GPU (torchrun, N > 1): every rank runs the workload on its own GPU with its own tokens (independent replicas,
-weak scaling); value = the sum of the ranks' algorithmic bytes (or FLOPs) over the slowest rank's time.
+Multi-GPU (torchrun, N > 1): the expert-parallel stack (the reference's config 5). The 512 experts of every layer are
+split contiguously over the ranks (each GPU holds 1/N of the 41 GB), each rank brings its own tokens (weak scaling),
+and ``ep.ep_moe`` moves them with NCCL all-to-all: decode M=8 per GPU (the headline, same metric as N=1) and M=64
+Zipf with the fixed-capacity exchange, prefill M=6912 Zipf with exact counts. value = the bytes of the experts the
+step touched (each streamed once, by its owner) plus every rank's x / output / routing (or the FLOPs of all ranks'
+rows) over the slowest rank's time (CUDA events, max over ranks). The roofline is the local gate_up GEMM on the rows
+one step delivered.
 """
 import argparse
 import json
@@ -330,6 +335,10 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        try:
+            return ep_main(a, rank, world, dev)
+        finally:
+            dist.destroy_process_group()
     from qwen38_flash_coder_b200 import prep, synth
 
     names = [a.workload] + ([] if a.only else [n for n in ("decode8", "decode32", "prefill") if n != a.workload])
@@ -378,6 +387,166 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+EP_WORKLOADS = {
+    "decode8": dict(m=8, route="uniform", unit="GB/s", capacity=True,
+                    desc="EP decode verify, M=8 tokens per GPU, uniform routing, fixed-capacity exchange"),
+    "decode64": dict(m=64, route="zipf", unit="GB/s", capacity=True,
+                     desc="EP decode, M=64 tokens per GPU (8 streams x 8), Zipf(1.1), fixed-capacity exchange"),
+    "prefill": dict(m=6912, route="zipf", unit="TFLOP/s", capacity=False,
+                    desc="EP prefill chunk, M=6912 tokens per GPU, Zipf(1.1), all-to-allv exchange"),
+}
+
+
+def ep_main(a, rank, world, dev):
+    """N > 1: the expert-parallel stack (experts split contiguously over the ranks, tokens per rank, NCCL
+    all-to-all dispatch and combine). Weak scaling: every rank brings its own M tokens per layer."""
+    import torch
+    import torch.distributed as dist
+
+    from qwen38_flash_coder_b200 import ep, ops, synth
+
+    names = ["decode8"] if a.only else ["decode8", "decode64", "prefill"]
+    layers, touched_bytes_all = [], []
+    for l in range(a.layers):
+        w13, w2 = synth.make_layer(E, H, I, l, device=dev)
+        L = ep.EPLayer(ep.shard_checkpoint(w13, E, world, rank), ep.shard_checkpoint(w2, E, world, rank), E, world,
+                       rank)
+        del w13, w2
+        entry = {"layer": L, "x": {}, "route": {}}
+        for j, n in enumerate(names):
+            seed = 100000 * rank + 100 * l + j
+            m = EP_WORKLOADS[n]["m"]
+            entry["x"][n] = synth.activations(m, H, seed, device=dev)
+            entry["route"][n] = route(m, seed, EP_WORKLOADS[n]["route"], dev)
+        layers.append(entry)
+    torch.cuda.empty_cache()
+
+    def barrier():
+        dist.barrier()
+
+    def local_touched_bytes(entry, name):
+        """Bytes of this rank's experts that any rank's tokens touch in this layer (each streamed once by its
+        owner), plus this rank's x, output and routing."""
+        L = entry["layer"]
+        ids = entry["route"][name][0].to(torch.int32)
+        allids = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(allids, ids)
+        g = torch.cat([t.reshape(-1) for t in allids]).long()
+        loc = g[(g >= L.lo) & (g < L.hi)] - L.lo
+        touched = torch.unique(loc)
+        m = ids.shape[0]
+        return int(L.prep.expert_bytes().to(dev)[touched].sum()) + m * H * 2 * 2 + m * TOPK * 8
+
+    results = {}
+    for name in names:
+        wl = EP_WORKLOADS[name]
+        m = wl["m"]
+
+        def step(be=None, name=name, wl=wl):
+            for e in layers:
+                ids, wts = e["route"][name]
+                ep.ep_moe(e["x"][name], e["layer"], wts, ids, backend=be, capacity=wl["capacity"])
+
+        for _ in range(max(3, a.warmup)):
+            step()
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        clocks = Clocks(dev.index)
+        ms = over_ranks(timed(step, a.steps, barrier), world, dev)
+        clk = clocks.stop()
+        if wl["unit"] == "GB/s":
+            amount = over_ranks(sum(local_touched_bytes(e, name) for e in layers) / 1e9, world, dev, op="sum")
+        else:
+            amount = world * len(layers) * m * TOPK * FLOPS_PER_ROW / 1e12
+        res = {"workload": wl["desc"], "value": round(amount / (ms / 1e3), 3), "unit": wl["unit"],
+               "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / len(layers), 2), "clocks": clk}
+        # the local expert GEMMs on the rows one step delivered: gate_up launches replayed alone (this rank)
+        rec = []
+        step(ep.CudaBackend(record=rec))
+        torch.cuda.synchronize()
+        be = ep.CudaBackend()
+        launches = ops.record_launches(lambda: [be.local(xr, mr, e["layer"], TOPK) for (xr, mr), e in zip(rec, layers)])
+        gates = [f for n, f in launches if n == "gate_gemm"]
+        roof = None
+        if gates:
+            g = make_graph(lambda: [f() for f in gates], 2)
+            gus = timed(g.replay, a.steps, lambda: None) * 1e3 / len(gates)
+            del g
+            gus = over_ranks(gus, world, dev)
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+                os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+            if wl["unit"] == "GB/s":
+                gb = []
+                for (xr, mr), e in zip(rec, layers):
+                    lid = mr[:, :TOPK]
+                    valid = lid[(lid >= 0) & (lid < e["layer"].local_experts)]
+                    if valid.numel():
+                        gb.append(gate_bytes(e["layer"].prep, valid, int(xr.shape[0])))
+                gbpl = sum(gb) / max(1, len(gb))
+                peak = peaks.get("hbm_gbs", 6650.0)
+                ach = gbpl / (gus / 1e6) / 1e9
+                roof = {"kernel": "moek_decode_kernel (gate_up of the local experts on the received rows)",
+                        "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+                        "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
+                        else "of fallback", "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
+                        "bytes_per_launch": int(gbpl), "avg_launch_us": round(gus, 2), "rank": "max over ranks"}
+            else:
+                rows = sum(int(((mr[:, :TOPK] >= 0) & (mr[:, :TOPK] < e["layer"].local_experts)).sum())
+                           for (xr, mr), e in zip(rec, layers)) / len(layers)
+                flops = rows * 2 * H * 2 * I
+                peak = peaks.get("bf16_tflops_sustained", 1400.0)
+                ach = flops / (gus / 1e6) / 1e12
+                roof = {"kernel": "moek_prefill_kernel (gate_up of the local experts on the received rows)",
+                        "bound": "tensor", "achieved": round(ach, 1), "peak": peak,
+                        "peak_source": "of measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
+                        if "bf16_tflops_sustained" in peaks else "of fallback", "unit": "TFLOP/s",
+                        "frac": round(ach / peak, 4), "traffic": None, "flops_per_launch": int(flops),
+                        "avg_launch_us": round(gus, 2), "rank": "this rank's gate launches, max over ranks"}
+        res["roofline"] = roof
+        del rec
+        per_layer = 4 + (ops.LAUNCHES_PER_LAYER if m <= ops.DECODE_MAX_M else 5)  # plan, pack, partial, unpack
+        res["gpu_launches_per_step"] = per_layer * len(layers)
+        if name == names[0]:
+            # e2e: inputs copied from pinned host memory and the outputs read back, every layer, every step
+            hx = [e["x"][name].cpu().pin_memory() for e in layers]
+            hid = [e["route"][name][0].cpu().pin_memory() for e in layers]
+            hw = [e["route"][name][1].cpu().pin_memory() for e in layers]
+            hout = [torch.empty((m, H), dtype=torch.bfloat16).pin_memory() for _ in layers]
+
+            def e2e_step():
+                for l, e in enumerate(layers):
+                    dx = hx[l].to(dev, non_blocking=True)
+                    did = hid[l].to(dev, non_blocking=True)
+                    dw = hw[l].to(dev, non_blocking=True)
+                    o = ep.ep_moe(dx, e["layer"], dw, did, capacity=wl["capacity"])
+                    hout[l].copy_(o, non_blocking=True)
+
+            e2e_step()
+            ems = over_ranks(timed(e2e_step, a.steps, barrier), world, dev)
+            res["e2e"] = {"value": round(amount / (ems / 1e3), 3), "unit": wl["unit"],
+                          "h2d_bytes_per_step": sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4
+                                                    for x, r, w in zip(hx, hid, hw)),
+                          "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
+                          "api": "ep.ep_moe with host copies (per rank; value over all ranks)"}
+        results[name] = res
+    head = results.pop(names[0])
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": EP_WORKLOADS[names[0]]["desc"], "layers_per_step": a.layers, "experts": E,
+                       "hidden": H, "inter": I, "top_k": TOPK, "tokens_per_gpu": EP_WORKLOADS[names[0]]["m"],
+                       "weights": "NVFP4 (E2M1 + E4M3/16 + fp32 global), bf16 activations",
+                       "l2": f"{a.layers} distinct layers per step rotate; touched weights >> 126 MB L2",
+                       "parallelism": f"ep{world}: experts split contiguously, tokens per rank, NCCL all-to-all"},
+            "us_per_layer": head["us_per_layer"], "roofline": head["roofline"], "cpu_baseline": None,
+            "e2e": head["e2e"], "clocks": head["clocks"],
+            "gpu_launches": head["gpu_launches_per_step"] * a.steps, "workloads": results,
+        }
+        print(json.dumps(line), flush=True)
 
 
 def reference_arm(a, rank, world):

@@ -117,6 +117,33 @@ int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int3
  * 284-289): out bf16 [m, N] = bf16(sum_j rows[t*top_k + j]) in fp32, slot order. rows: fp32 if rows_fp32 else bf16. */
 int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int32_t N, int32_t top_k, void* stream);
 
+/* ---- Expert parallelism. The reference has none (its hook rejects expert_map, files/mbx_moek.py:248-255); these
+ * are the dispatch / combine steps around the same GEMMs when the experts are split contiguously over `world` ranks
+ * (rank d owns [d * E/world, (d + 1) * E/world)). The all-to-all transfers are the caller's (NCCL). */
+
+/* Dispatch plan: for tokens t < M and ranks d < world, pos[t * world + d] = position of token t in rank d's send
+ * segment (tokens with at least one of their top_k experts on d, ascending t), else -1; counts[d] = rows for d;
+ * offsets[0..world] = exclusive prefix of counts. Ids outside [0, num_experts) go nowhere. */
+int moek_ep_plan(const int32_t* topk_ids, int32_t M, int32_t top_k, int32_t num_experts, int32_t world,
+                 int32_t* pos, int32_t* counts, int32_t* offsets, void* stream);
+
+/* Packs the send buffer: send_x bf16 [offsets[world], H] (row offsets[d] + pos[t*world + d] = x[t]) and send_meta
+ * int32 [offsets[world], 2 * top_k] (the slots' expert ids local to d, -1 for slots owned elsewhere, then the router
+ * weights as fp32 bits, 0 for slots owned elsewhere). */
+int moek_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* pos,
+                 const int32_t* offsets, int32_t M, int32_t H, int32_t top_k, int32_t num_experts, int32_t world,
+                 void* send_x, int32_t* send_meta, void* stream);
+
+/* Receiving side, after the down GEMM wrote fp32 rows (router weight applied) for the R received rows' slots:
+ * out fp32 [R, N] = sum over slots j with 0 <= meta[r][j] < local_experts, slot order, of rows[r * top_k + j]. */
+int moek_ep_partial(const float* rows, const int32_t* meta, int32_t local_experts, int32_t R, int32_t N,
+                    int32_t top_k, float* out, void* stream);
+
+/* Source side, after the partial rows came back (back fp32 [offsets[world], H], same order as the send buffer):
+ * out bf16 [M, H] = bf16(sum over d = 0..world-1 with pos >= 0 of back[offsets[d] + pos[t*world + d]]). */
+int moek_ep_unpack(const float* back, const int32_t* pos, const int32_t* offsets, int32_t M, int32_t H,
+                   int32_t world, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,25 +44,42 @@ def _groups(topk_ids: np.ndarray):
         yield int(e), torch.from_numpy(rows.astype(np.int64))
 
 
+def slot_rows(x, topk_ids, topk_w, w13, w2) -> torch.Tensor:
+    """fp32 rows [M * k, H] of bench/moek/problem.py:51-67's per-slot terms: row t * k + j = w[t, j] *
+    (bf16(silu(h_gate) * h_up) @ W2_e^T) with h = x_t @ W13_e^T, e = topk_ids[t, j]; slots whose id is outside the
+    expert range of the given weights stay zero (a routed slot that belongs to another shard)."""
+    m, hid = x.shape
+    k = topk_ids.shape[1]
+    n_exp = w13[0].shape[0]
+    inter = w13[0].shape[1] // 2
+    xf = x.float()
+    wf = torch.as_tensor(np.asarray(topk_w, dtype=np.float32)).reshape(-1)
+    ids = np.asarray(topk_ids).reshape(-1).astype(np.int64)
+    y = torch.zeros((m * k, hid), dtype=torch.float32)
+    valid = (ids >= 0) & (ids < n_exp)
+    sel = np.nonzero(valid)[0]
+    if sel.size == 0:
+        return y
+    for e, rows in _groups(ids[sel][:, None]):
+        rows = torch.from_numpy(sel[rows.numpy()].astype(np.int64))
+        a = _bf16(_expert_values(w13[0], w13[1], e) * float(np.float32(w13[2][e])))
+        b = _bf16(_expert_values(w2[0], w2[1], e) * float(np.float32(w2[2][e])))
+        h = xf[rows // k] @ a.T
+        h = _bf16(torch.nn.functional.silu(h[:, :inter]) * h[:, inter:])
+        y[rows] = wf[rows][:, None] * (h @ b.T)
+    return y
+
+
 def reference(x, topk_ids, topk_w, w13, w2) -> torch.Tensor:
-    """fp32 output [M, H] of bench/moek/problem.py:51-67's ``reference`` for all rows.
+    """fp32 output [M, H] of bench/moek/problem.py:51-67's ``reference`` for all rows: the slot rows summed in slot
+    order.
 
     x: bf16 [M, H] tensor; topk_ids: int [M, k]; topk_w: fp32 [M, k];
     w13 = (codes uint8 [E, 2I, H/2], scale bits uint8 [E, 2I, H/16], gs fp32 [E]); w2 likewise [E, H, I/2] ...
     """
     m, hid = x.shape
     k = topk_ids.shape[1]
-    inter = w13[0].shape[1] // 2
-    xf = x.float()
-    wf = torch.as_tensor(np.asarray(topk_w, dtype=np.float32)).reshape(-1)
-    y = torch.zeros((m * k, hid), dtype=torch.float32)
-    for e, rows in _groups(topk_ids):
-        a = _bf16(_expert_values(w13[0], w13[1], e) * float(np.float32(w13[2][e])))
-        b = _bf16(_expert_values(w2[0], w2[1], e) * float(np.float32(w2[2][e])))
-        h = xf[rows // k] @ a.T
-        h = _bf16(torch.nn.functional.silu(h[:, :inter]) * h[:, inter:])
-        y[rows] = wf[rows][:, None] * (h @ b.T)
-    y = y.view(m, k, hid)
+    y = slot_rows(x, topk_ids, topk_w, w13, w2).view(m, k, hid)
     out = torch.zeros((m, hid), dtype=torch.float32)
     for j in range(k):
         out += y[:, j]

@@ -244,3 +244,56 @@ MOEK_API int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_
                                                static_cast<__nv_bfloat16*>(out), st),
                      "combine");
 }
+
+// ------------------------------------------------------------------------------------------- expert parallel
+static int ep_world_ok(int32_t E, int32_t world) {
+  if (world < 1 || world > moek::EP_MAX_WORLD)
+    return fail(MOEK_ERR_ARG, "moek_b200: EP world size %d outside [1, %d]", world, moek::EP_MAX_WORLD);
+  if (E <= 0 || E % world) return fail(MOEK_ERR_ARG, "moek_b200: %d experts do not split evenly over %d ranks", E, world);
+  return MOEK_OK;
+}
+
+MOEK_API int moek_ep_plan(const int32_t* topk_ids, int32_t M, int32_t top_k, int32_t num_experts, int32_t world,
+                          int32_t* pos, int32_t* counts, int32_t* offsets, void* stream) {
+  if (int rc = ep_world_ok(num_experts, world)) return rc;
+  if (M < 0 || top_k <= 0 || !counts || !offsets || (M > 0 && (!topk_ids || !pos)))
+    return fail(MOEK_ERR_ARG, "moek_b200: ep_plan bad arguments");
+  return cuda_status(moek::launch_ep_plan(topk_ids, M, top_k, num_experts, world, pos, counts, offsets,
+                                          (cudaStream_t)stream),
+                     "ep_plan");
+}
+
+MOEK_API int moek_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* pos,
+                          const int32_t* offsets, int32_t M, int32_t H, int32_t top_k, int32_t num_experts,
+                          int32_t world, void* send_x, int32_t* send_meta, void* stream) {
+  if (int rc = ep_world_ok(num_experts, world)) return rc;
+  if (M == 0) return MOEK_OK;
+  if (M < 0 || H <= 0 || H % 8 || top_k <= 0 || top_k > 256 || !x || !topk_ids || !topk_w || !pos || !offsets ||
+      !send_x || !send_meta)
+    return fail(MOEK_ERR_ARG, "moek_b200: ep_pack bad arguments (H must be a multiple of 8)");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(send_x) % 16)
+    return fail(MOEK_ERR_ARG, "moek_b200: ep_pack rows must be 16-byte aligned");
+  return cuda_status(moek::launch_ep_pack(static_cast<const __nv_bfloat16*>(x), topk_ids, topk_w, pos, offsets, M, H,
+                                          top_k, num_experts, world, static_cast<__nv_bfloat16*>(send_x), send_meta,
+                                          (cudaStream_t)stream),
+                     "ep_pack");
+}
+
+MOEK_API int moek_ep_partial(const float* rows, const int32_t* meta, int32_t local_experts, int32_t R, int32_t N,
+                             int32_t top_k, float* out, void* stream) {
+  if (R == 0) return MOEK_OK;
+  if (R < 0 || N <= 0 || top_k <= 0 || local_experts <= 0 || !rows || !meta || !out)
+    return fail(MOEK_ERR_ARG, "moek_b200: ep_partial bad arguments");
+  return cuda_status(moek::launch_ep_partial(rows, meta, local_experts, R, N, top_k, out, (cudaStream_t)stream),
+                     "ep_partial");
+}
+
+MOEK_API int moek_ep_unpack(const float* back, const int32_t* pos, const int32_t* offsets, int32_t M, int32_t H,
+                            int32_t world, void* out, void* stream) {
+  if (M == 0) return MOEK_OK;
+  if (M < 0 || H <= 0 || world < 1 || world > moek::EP_MAX_WORLD || !pos || !offsets || !out)
+    return fail(MOEK_ERR_ARG, "moek_b200: ep_unpack bad arguments");
+  return cuda_status(moek::launch_ep_unpack(back, pos, offsets, M, H, world, static_cast<__nv_bfloat16*>(out),
+                                            (cudaStream_t)stream),
+                     "ep_unpack");
+}

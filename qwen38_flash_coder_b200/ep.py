@@ -1,0 +1,161 @@
+"""Expert parallelism: the routed experts split over the ranks of a process group, tokens exchanged with NCCL.
+
+The reference runs on one GPU and rejects vLLM's ``expert_map`` (files/mbx_moek.py:248-255). This module adds the
+expert-parallel form of the same layer for 2/4/8 GPUs of one node, one process per GPU:
+
+- **sharding**: the E experts are split contiguously, rank d owns [d * E / world, (d + 1) * E / world) and holds
+  only those experts' prepared weights (``EPLayer``); every rank keeps its own tokens (data-parallel tokens,
+  expert-parallel weights);
+- **dispatch**: ``moek_ep_plan`` places every token in the send segment of each rank owning one of its top-k
+  experts (ascending token order), an int32 all-to-all exchanges the row counts, ``moek_ep_pack`` copies the rows and
+  their slot metadata (local expert ids, -1 for slots owned elsewhere, and router weights), and two all-to-allv
+  (``torch.distributed.all_to_all_single`` on NCCL) move rows and metadata;
+- **local experts**: the received rows go through the same align / gate_up / SwiGLU / down kernels
+  (``ops.moe_rows``), and ``moek_ep_partial`` sums each row's local slots in fp32;
+- **combine**: an all-to-allv returns the fp32 partial rows and ``moek_ep_unpack`` adds them in rank order and
+  rounds once to bf16, so the result differs from the one-GPU layer only by the order of fp32 additions.
+
+With exact row counts (the default) the counts cross to the host between the count exchange and the row exchange
+(the receive buffers are sized from them), so one EP layer call synchronises its stream once; the fixed-capacity
+mode (``capacity=True``, for decode batches) reserves M rows per destination instead and never synchronises.
+
+Failure handling is the process group's: create it with a short ``timeout``; a rank that fails or never arrives
+makes the others' next collective raise instead of hanging (tested with gloo ranks on the CPU). The backend is
+pluggable so that the orchestration can be tested on CPU ranks against the oracle (``tests/test_ep_cpu.py``); the
+default backend is the CUDA kernels, and there is no CPU fallback in it.
+"""
+import torch
+import torch.distributed as dist
+
+from . import ops, prep
+from ._lib import MoekError, call
+
+
+def owned_experts(num_experts: int, world: int, rank: int):
+    """[lo, hi) of the experts rank ``rank`` owns."""
+    if num_experts % world:
+        raise MoekError(f"moek_b200: {num_experts} experts do not split evenly over {world} ranks")
+    per = num_experts // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_checkpoint(mat, num_experts: int, world: int, rank: int):
+    """The local slice of a checkpoint matrix (codes, scales, global scales), each indexed by expert first."""
+    lo, hi = owned_experts(num_experts, world, rank)
+    return tuple(t[lo:hi] for t in mat)
+
+
+class EPLayer:
+    """The experts of one layer owned by this rank, prepared for the kernels, plus the global geometry."""
+
+    def __init__(self, w13_local, w2_local, num_experts: int, world: int, rank: int, ckpt: bool = False):
+        lo, hi = owned_experts(num_experts, world, rank)
+        if w13_local[0].shape[0] != hi - lo or w2_local[0].shape[0] != hi - lo:
+            raise MoekError("moek_b200: the local checkpoint slice does not match the rank's expert range")
+        self.num_experts, self.world, self.rank, self.lo, self.hi = num_experts, world, rank, lo, hi
+        self.prep = prep.PreparedLayer(w13_local, w2_local) if w13_local[0].is_cuda else None
+        self.ckpt = (w13_local, w2_local) if ckpt or self.prep is None else None
+        self.hidden = w2_local[0].shape[1]
+
+    @property
+    def local_experts(self) -> int:
+        return self.hi - self.lo
+
+
+class CudaBackend:
+    """The build's kernels (C ABI) for the index work, the row copies and the local experts. With ``record`` a list,
+    every received batch (rows, slot metadata) is appended to it."""
+
+    def __init__(self, record=None):
+        self.record = record
+
+    def plan(self, ids32, num_experts, world):
+        m, k = ids32.shape
+        dev = ids32.device
+        pos = torch.empty((m, world), dtype=torch.int32, device=dev)
+        counts = torch.empty(world, dtype=torch.int32, device=dev)
+        offsets = torch.empty(world + 1, dtype=torch.int32, device=dev)
+        call("moek_ep_plan", ops._ptr(ids32), m, k, num_experts, world, ops._ptr(pos), ops._ptr(counts),
+             ops._ptr(offsets), ops._stream(dev))
+        return pos, counts, offsets
+
+    def pack(self, x, ids32, w, pos, offsets, num_experts, world, rows, fill=False):
+        m, hid = x.shape
+        k = ids32.shape[1]
+        send_x = torch.empty((rows, hid), dtype=torch.bfloat16, device=x.device)
+        meta = torch.empty((rows, 2 * k), dtype=torch.int32, device=x.device)
+        if fill:  # rows no token fills keep invalid slots (and zero weights)
+            meta[:, :k].fill_(-1)
+            meta[:, k:].zero_()
+        call("moek_ep_pack", ops._ptr(x), ops._ptr(ids32), ops._ptr(w), ops._ptr(pos), ops._ptr(offsets), m, hid, k,
+             num_experts, world, ops._ptr(send_x), ops._ptr(meta), ops._stream(x.device))
+        return send_x, meta
+
+    def local(self, x_recv, meta, layer: EPLayer, k):
+        if self.record is not None:
+            self.record.append((x_recv, meta))
+        r, hid = x_recv.shape
+        out = torch.empty((r, hid), dtype=torch.float32, device=x_recv.device)
+        if r == 0:
+            return out
+        ids = meta[:, :k].contiguous()
+        w = meta[:, k:].contiguous().view(torch.float32)
+        rows = ops.moe_rows(x_recv, layer.prep, w, ids)
+        call("moek_ep_partial", ops._ptr(rows), ops._ptr(meta), layer.local_experts, r, hid, k, ops._ptr(out),
+             ops._stream(x_recv.device))
+        return out
+
+    def unpack(self, back, pos, offsets, m, world):
+        hid = back.shape[1]
+        out = torch.empty((m, hid), dtype=torch.bfloat16, device=pos.device)
+        call("moek_ep_unpack", ops._ptr(back), ops._ptr(pos), ops._ptr(offsets), m, hid, world, ops._ptr(out),
+             ops._stream(pos.device))
+        return out
+
+
+def ep_moe(hidden_states: torch.Tensor, layer: EPLayer, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+           group=None, backend=None, capacity: bool = False) -> torch.Tensor:
+    """This rank's tokens through the expert-parallel layer: bf16 [M, H], the same result as ``ops.fused_moe`` on
+    one GPU holding all experts (up to the order of fp32 additions). ``topk_ids`` are global expert ids.
+
+    ``capacity=False``: all-to-allv with exact row counts (the counts cross to the host once per call).
+    ``capacity=True``: every rank reserves M rows for every destination (M = this call's token count, the same on
+    all ranks), so the exchange has fixed sizes and no host synchronisation; unused rows carry invalid slot ids and
+    are skipped by the kernels. Suited to decode batches, where the rows are few and the latency matters.
+
+    Every rank of ``group`` must call this for the same layer with the same mode (the collectives pair up in call
+    order)."""
+    be = backend or CudaBackend()
+    world = dist.get_world_size(group)
+    if world != layer.world:
+        raise MoekError(f"moek_b200: layer sharded for {layer.world} ranks, process group has {world}")
+    x = hidden_states.contiguous()
+    m, hid = x.shape
+    k = topk_ids.shape[1]
+    ids32 = topk_ids.to(torch.int32).contiguous()
+    w = topk_weights.float().contiguous()
+    pos, counts, offsets = be.plan(ids32, layer.num_experts, world)
+    if capacity:
+        offsets = torch.arange(world + 1, dtype=torch.int32, device=pos.device) * m
+        rows = world * m
+        send_x, send_meta = be.pack(x, ids32, w, pos, offsets, layer.num_experts, world, rows, fill=True)
+        recv_x, recv_meta = torch.empty_like(send_x), torch.empty_like(send_meta)
+        dist.all_to_all_single(recv_x, send_x, group=group)
+        dist.all_to_all_single(recv_meta, send_meta, group=group)
+        partial = be.local(recv_x, recv_meta, layer, k)
+        back = torch.empty_like(partial)
+        dist.all_to_all_single(back, partial, group=group)
+        return be.unpack(back, pos, offsets, m, world)
+    recv_counts = torch.empty_like(counts)
+    dist.all_to_all_single(recv_counts, counts, group=group)
+    send = [int(c) for c in counts.tolist()]
+    recv = [int(c) for c in recv_counts.tolist()]
+    send_x, send_meta = be.pack(x, ids32, w, pos, offsets, layer.num_experts, world, sum(send))
+    recv_x = torch.empty((sum(recv), hid), dtype=send_x.dtype, device=send_x.device)
+    recv_meta = torch.empty((sum(recv), 2 * k), dtype=torch.int32, device=send_meta.device)
+    dist.all_to_all_single(recv_x, send_x, recv, send, group=group)
+    dist.all_to_all_single(recv_meta, send_meta, recv, send, group=group)
+    partial = be.local(recv_x, recv_meta, layer, k)
+    back = torch.empty((sum(send), hid), dtype=torch.float32, device=partial.device)
+    dist.all_to_all_single(back, partial, send, recv, group=group)
+    return be.unpack(back, pos, offsets, m, world)

@@ -195,9 +195,31 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
         output = torch.empty((m, hid), dtype=torch.bfloat16, device=x.device)
     if m == 0:
         return output
+    _layer_call(x, layer, topk_weights, topk_ids, output, None)
+    return output
+
+
+def moe_rows(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: torch.Tensor,
+             topk_ids: torch.Tensor) -> torch.Tensor:
+    """The same layer without the top-k sum: fp32 rows [M * top_k, H], row t * top_k + j = w[t, j] *
+    down_e(silu(gate_e(x_t)) * up_e(x_t)) for e = topk_ids[t, j] in [0, E). Rows of slots whose expert is outside
+    [0, E) are not computed and hold arbitrary values (the expert-parallel partial sum leaves them out)."""
+    x = hidden_states
+    _need_cuda(x, topk_ids, topk_weights)
+    m, hid = x.shape
+    top_k = topk_ids.shape[1]
+    if m == 0:
+        return torch.empty((0, hid), dtype=torch.float32, device=x.device)
+    return _layer_call(x, layer, topk_weights, topk_ids, None, top_k)
+
+
+def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
+    """Align + gate_up + SwiGLU + down. ``output`` bf16 [M, H] gets the top-k sums; with ``rows_k`` set instead,
+    the fp32 weighted rows [M * top_k, H] are returned."""
     if x.dtype != torch.bfloat16:
         raise MoekError("moek_b200: hidden states must be bf16")
     x = x.contiguous()
+    m = x.shape[0]
     top_k = topk_ids.shape[1]
     num_ids = m * top_k
     dev = x.device
@@ -223,16 +245,23 @@ def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: t
         call("moek_split_epilogue", _ptr(part), ns1, num_ids, a.N, 1, None, top_k, _ptr(act), 0, st)
         _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, ns2, part, rows, None,
                                           None, None, 0, mode=2))
-        call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(output), 2, st)
-        return output
+        if rows_k is None:
+            call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(output), 2, st)
+            return output
+        dout = torch.empty((num_ids, b.N), dtype=torch.float32, device=dev)
+        call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(dout), 1, st)
+        return dout
     # prefill: tcgen05 GEMMs over moe_align blocks of <= 128 rows (the MMA's N), SwiGLU and router weight in their
     # epilogues, the top-k sum of the fp32 rows in one more kernel
     sid, eid, npad = moe_align_block_size(ids32, BM_PREFILL, layer.E)
-    part = _scratch("part", num_ids * b.N, torch.float32, dev)
+    part = _scratch("part", num_ids * b.N, torch.float32, dev) if rows_k is None else \
+        torch.empty((num_ids, b.N), dtype=torch.float32, device=dev)
     _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, 1, part, rows, act, tw, ids32,
                                       top_k, mode=0, block_m=BM_PREFILL))
     _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, 1, part, rows, None, tw, ids32,
                                       top_k, mode=0, block_m=BM_PREFILL))
+    if rows_k is not None:
+        return part
     call("moek_combine", _ptr(part), 1, _ptr(output), m, b.N, top_k, _stream(dev))
     return output
 
