@@ -45,6 +45,10 @@ METRIC = "routed-MoE layer µs & HBM GB/s (M=8,32); TFLOP/s (M=6912); 1/2/4/8 GP
 H, I, E, TOPK = 2048, 512, 512, 5
 FLOPS_PER_ROW = 2 * 3 * H * I  # gate + up + down per (token, slot) row
 
+# DRAM bytes (read + write) of one gate_up launch, from one ncu --set full capture each:
+# profiles/moek_decode_kernel_decode8.md (layer 0 of the seeded layers) and profiles/moek_prefill_kernel_prefill6912.md
+TRAFFIC = {"decode8": 42_990_336, "prefill": 695_317_952}
+
 WORKLOADS = {
     "decode8": dict(m=8, route="uniform", unit="GB/s", desc="decode verify M=8 (1 stream x block 8), uniform routing"),
     "decode32": dict(m=32, route="zipf", unit="GB/s", desc="multi-stream decode M=32 (4 x 8), Zipf(1.1) routing"),
@@ -259,10 +263,7 @@ def measure(name, layers, a, dev, world, barrier, headline):
     pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pp):
         peaks = json.load(open(pp))
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        traffic = json.load(open(tp)).get(f"gate_gemm_{name}")
+    traffic = TRAFFIC.get(name)
     if wl["unit"] == "GB/s":
         gb = sum(gate_bytes(L["prep"], L["route"][name][0], m) for L in layers) / nl
         peak = peaks.get("hbm_gbs", 6650.0)
