@@ -454,21 +454,36 @@ def ep_main(a, rank, world, dev):
             step()
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
+        run, how = step, "eager (exact-count exchange synchronises the host every layer)"
+        if wl["capacity"]:  # no host synchronisation: the whole step, NCCL included, as one CUDA graph
+            graph, err = None, None
+            try:
+                graph = make_graph(step, 1)
+            except Exception as exc:  # every rank must take the same path: agree before timing
+                err = f"{type(exc).__name__}: {str(exc)[:120]}"
+            ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if int(ok) == 1:
+                run, how = graph.replay, "one CUDA graph per step (NCCL all-to-alls captured)"
+            else:
+                how = f"eager (graph capture failed on a rank: {err})"
         clocks = Clocks(dev.index)
-        ms = over_ranks(timed(step, a.steps, barrier), world, dev)
+        ms = over_ranks(timed(run, a.steps, barrier), world, dev)
         clk = clocks.stop()
         if wl["unit"] == "GB/s":
             amount = over_ranks(sum(local_touched_bytes(e, name) for e in layers) / 1e9, world, dev, op="sum")
         else:
             amount = world * len(layers) * m * TOPK * FLOPS_PER_ROW / 1e12
         res = {"workload": wl["desc"], "value": round(amount / (ms / 1e3), 3), "unit": wl["unit"],
-               "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / len(layers), 2), "clocks": clk}
+               "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / len(layers), 2), "clocks": clk,
+               "launch": how}
         # the local expert GEMMs on the rows one step delivered: gate_up launches replayed alone (this rank)
         rec = []
         step(ep.CudaBackend(record=rec))
         torch.cuda.synchronize()
         be = ep.CudaBackend()
-        launches = ops.record_launches(lambda: [be.local(xr, mr, e["layer"], TOPK) for (xr, mr), e in zip(rec, layers)])
+        launches = ops.record_launches(lambda: [be.local(xr, mr, e["layer"], TOPK, ms)
+                                                for (xr, mr, ms), e in zip(rec, layers)])
         gates = [f for n, f in launches if n == "gate_gemm"]
         roof = None
         if gates:
@@ -480,7 +495,7 @@ def ep_main(a, rank, world, dev):
                 os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
             if wl["unit"] == "GB/s":
                 gb = []
-                for (xr, mr), e in zip(rec, layers):
+                for (xr, mr, _), e in zip(rec, layers):
                     lid = mr[:, :TOPK]
                     valid = lid[(lid >= 0) & (lid < e["layer"].local_experts)]
                     if valid.numel():
@@ -495,7 +510,7 @@ def ep_main(a, rank, world, dev):
                         "bytes_per_launch": int(gbpl), "avg_launch_us": round(gus, 2), "rank": "max over ranks"}
             else:
                 rows = sum(int(((mr[:, :TOPK] >= 0) & (mr[:, :TOPK] < e["layer"].local_experts)).sum())
-                           for (xr, mr), e in zip(rec, layers)) / len(layers)
+                           for (xr, mr, _), e in zip(rec, layers)) / len(layers)
                 flops = rows * 2 * H * 2 * I
                 peak = peaks.get("bf16_tflops_sustained", 1400.0)
                 ach = flops / (gus / 1e6) / 1e12
@@ -545,7 +560,7 @@ def ep_main(a, rank, world, dev):
                        "parallelism": f"ep{world}: experts split contiguously, tokens per rank, NCCL all-to-all"},
             "us_per_layer": head["us_per_layer"], "roofline": head["roofline"], "cpu_baseline": None,
             "e2e": head["e2e"], "clocks": head["clocks"],
-            "gpu_launches": head["gpu_launches_per_step"] * a.steps, "workloads": results,
+            "gpu_launches": head["gpu_launches_per_step"] * a.steps, "launch": head["launch"], "workloads": results,
         }
         print(json.dumps(line), flush=True)
 

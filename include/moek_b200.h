@@ -127,17 +127,21 @@ int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int3
 int moek_ep_plan(const int32_t* topk_ids, int32_t M, int32_t top_k, int32_t num_experts, int32_t world,
                  int32_t* pos, int32_t* counts, int32_t* offsets, void* stream);
 
-/* Packs the send buffer: send_x bf16 [offsets[world], H] (row offsets[d] + pos[t*world + d] = x[t]) and send_meta
- * int32 [offsets[world], 2 * top_k] (the slots' expert ids local to d, -1 for slots owned elsewhere, then the router
- * weights as fp32 bits, 0 for slots owned elsewhere). */
+/* Packs the send buffer: rows bf16 at send_x + row * x_stride (x_stride >= H elements, a multiple of 8; row
+ * offsets[d] + pos[t*world + d] = x[t]) and slot metadata int32 at send_meta + row * meta_stride (meta_stride >=
+ * 2 * top_k: the slots' expert ids local to d, -1 for slots owned elsewhere, then the router weights as fp32 bits, 0
+ * for slots owned elsewhere). Rows and metadata may share one buffer (meta inside each row's tail). With fill != 0
+ * the rows offsets[d] + counts[d] .. offsets[d + 1] of each segment (a fixed-capacity layout) get ids -1. */
 int moek_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* pos,
-                 const int32_t* offsets, int32_t M, int32_t H, int32_t top_k, int32_t num_experts, int32_t world,
-                 void* send_x, int32_t* send_meta, void* stream);
+                 const int32_t* offsets, const int32_t* counts, int32_t fill, int32_t M, int32_t H, int32_t top_k,
+                 int32_t num_experts, int32_t world, void* send_x, int64_t x_stride, int32_t* send_meta,
+                 int64_t meta_stride, void* stream);
 
 /* Receiving side, after the down GEMM wrote fp32 rows (router weight applied) for the R received rows' slots:
- * out fp32 [R, N] = sum over slots j with 0 <= meta[r][j] < local_experts, slot order, of rows[r * top_k + j]. */
-int moek_ep_partial(const float* rows, const int32_t* meta, int32_t local_experts, int32_t R, int32_t N,
-                    int32_t top_k, float* out, void* stream);
+ * out fp32 [R, N] = sum over slots j with 0 <= meta[r * meta_stride + j] < local_experts, slot order, of
+ * rows[r * top_k + j]. */
+int moek_ep_partial(const float* rows, const int32_t* meta, int64_t meta_stride, int32_t local_experts, int32_t R,
+                    int32_t N, int32_t top_k, float* out, void* stream);
 
 /* Source side, after the partial rows came back (back fp32 [offsets[world], H], same order as the send buffer):
  * out bf16 [M, H] = bf16(sum over d = 0..world-1 with pos >= 0 of back[offsets[d] + pos[t*world + d]]). */

@@ -18,8 +18,9 @@ SIGNATURES = {
     "moek_split_epilogue": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P]),
     "moek_combine": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _P]),
     "moek_ep_plan": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
-    "moek_ep_pack": (ctypes.c_int, [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P]),
-    "moek_ep_partial": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _I32, _P, _P]),
+    "moek_ep_pack": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64,
+                                    _P]),
+    "moek_ep_partial": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "moek_ep_unpack": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _P, _P]),
 }
 

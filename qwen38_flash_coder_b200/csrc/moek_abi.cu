@@ -264,27 +264,32 @@ MOEK_API int moek_ep_plan(const int32_t* topk_ids, int32_t M, int32_t top_k, int
 }
 
 MOEK_API int moek_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* pos,
-                          const int32_t* offsets, int32_t M, int32_t H, int32_t top_k, int32_t num_experts,
-                          int32_t world, void* send_x, int32_t* send_meta, void* stream) {
+                          const int32_t* offsets, const int32_t* counts, int32_t fill, int32_t M, int32_t H,
+                          int32_t top_k, int32_t num_experts, int32_t world, void* send_x, int64_t x_stride,
+                          int32_t* send_meta, int64_t meta_stride, void* stream) {
   if (int rc = ep_world_ok(num_experts, world)) return rc;
-  if (M == 0) return MOEK_OK;
-  if (M < 0 || H <= 0 || H % 8 || top_k <= 0 || top_k > 256 || !x || !topk_ids || !topk_w || !pos || !offsets ||
-      !send_x || !send_meta)
-    return fail(MOEK_ERR_ARG, "moek_b200: ep_pack bad arguments (H must be a multiple of 8)");
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(send_x) % 16)
+  if (M == 0 && !fill) return MOEK_OK;
+  if (M < 0 || H <= 0 || H % 8 || top_k <= 0 || top_k > 256 || !pos || !offsets || !send_x || !send_meta ||
+      x_stride < H || x_stride % 8 || meta_stride < 2 * top_k || (M > 0 && (!x || !topk_ids || !topk_w)) ||
+      (fill && !counts))
+    return fail(MOEK_ERR_ARG, "moek_b200: ep_pack bad arguments (H and the row stride must be multiples of 8)");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(send_x) % 16 ||
+      reinterpret_cast<uintptr_t>(send_meta) % 4)
     return fail(MOEK_ERR_ARG, "moek_b200: ep_pack rows must be 16-byte aligned");
-  return cuda_status(moek::launch_ep_pack(static_cast<const __nv_bfloat16*>(x), topk_ids, topk_w, pos, offsets, M, H,
-                                          top_k, num_experts, world, static_cast<__nv_bfloat16*>(send_x), send_meta,
+  return cuda_status(moek::launch_ep_pack(static_cast<const __nv_bfloat16*>(x), topk_ids, topk_w, pos, offsets, counts,
+                                          fill ? 1 : 0, M, H, top_k, num_experts, world,
+                                          static_cast<__nv_bfloat16*>(send_x), x_stride, send_meta, meta_stride,
                                           (cudaStream_t)stream),
                      "ep_pack");
 }
 
-MOEK_API int moek_ep_partial(const float* rows, const int32_t* meta, int32_t local_experts, int32_t R, int32_t N,
-                             int32_t top_k, float* out, void* stream) {
+MOEK_API int moek_ep_partial(const float* rows, const int32_t* meta, int64_t meta_stride, int32_t local_experts,
+                             int32_t R, int32_t N, int32_t top_k, float* out, void* stream) {
   if (R == 0) return MOEK_OK;
-  if (R < 0 || N <= 0 || top_k <= 0 || local_experts <= 0 || !rows || !meta || !out)
+  if (R < 0 || N <= 0 || top_k <= 0 || local_experts <= 0 || !rows || !meta || !out || meta_stride < top_k)
     return fail(MOEK_ERR_ARG, "moek_b200: ep_partial bad arguments");
-  return cuda_status(moek::launch_ep_partial(rows, meta, local_experts, R, N, top_k, out, (cudaStream_t)stream),
+  return cuda_status(moek::launch_ep_partial(rows, meta, meta_stride, local_experts, R, N, top_k, out,
+                                             (cudaStream_t)stream),
                      "ep_partial");
 }
 

@@ -11,7 +11,9 @@
 //   ep_plan     one CTA: for every destination rank, the position of each token in that rank's send segment
 //               (ascending token order, -1 when nothing goes there), the per-rank row counts and their offsets.
 //   ep_pack     one CTA per token: the token's bf16 row into each destination segment (16-byte vector copies) and
-//               the slot metadata (k local ids, then k router weights as fp32 bits).
+//               the slot metadata (k local ids, then k router weights as fp32 bits), at caller-given row strides so
+//               that rows and metadata can share one buffer (one all-to-all); with `fill`, one more CTA per
+//               destination marks the segment's unused rows (fixed-capacity exchange) as having no valid slot.
 //   ep_partial  out[r][n] = sum over the row's local slots j (slot order) of rows[r * k + j][n], fp32.
 //   ep_unpack   out[t][n] = bf16(sum over ranks d in order of back[offset[d] + pos[t][d]][n]).
 #include <cuda_bf16.h>
@@ -78,34 +80,44 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) ep_plan_kernel(const int32_t*
 
 __global__ void ep_pack_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids,
                                const float* __restrict__ topk_w, const int32_t* __restrict__ pos,
-                               const int32_t* __restrict__ offsets, int H16, int k, int E, int world,
-                               uint4* __restrict__ send_x, int32_t* __restrict__ send_meta) {
-  const int t = blockIdx.x;
+                               const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts, int M,
+                               int H16, int k, int E, int world, uint4* __restrict__ send_x, int64_t xs16,
+                               int32_t* __restrict__ send_meta, int64_t ms) {
   const int per = E / world;
+  if (blockIdx.x >= M) {  // fill: the rows of destination d's segment that no token uses get invalid slots
+    const int d = blockIdx.x - M;
+    for (int64_t row = (int64_t)offsets[d] + counts[d] + threadIdx.x; row < offsets[d + 1]; row += blockDim.x)
+      for (int j = 0; j < k; j++) {
+        send_meta[row * ms + j] = -1;
+        send_meta[row * ms + k + j] = 0;
+      }
+    return;
+  }
+  const int t = blockIdx.x;
   for (int d = 0; d < world; d++) {
     const int p = pos[(int64_t)t * world + d];
     if (p < 0) continue;
     const int64_t row = (int64_t)offsets[d] + p;
-    for (int c = threadIdx.x; c < H16; c += blockDim.x) send_x[row * H16 + c] = x[(int64_t)t * H16 + c];
+    for (int c = threadIdx.x; c < H16; c += blockDim.x) send_x[row * xs16 + c] = x[(int64_t)t * H16 + c];
     if (threadIdx.x < k) {
       const int j = threadIdx.x;
       const int e = ids[(int64_t)t * k + j];
       const bool mine = e >= 0 && e < E && e / per == d;
-      send_meta[row * 2 * k + j] = mine ? e - d * per : -1;
-      send_meta[row * 2 * k + k + j] = __float_as_int(mine ? topk_w[(int64_t)t * k + j] : 0.f);
+      send_meta[row * ms + j] = mine ? e - d * per : -1;
+      send_meta[row * ms + k + j] = __float_as_int(mine ? topk_w[(int64_t)t * k + j] : 0.f);
     }
   }
 }
 
-__global__ void ep_partial_kernel(const float* __restrict__ rows, const int32_t* __restrict__ meta, int E_local,
-                                  int R, int N, int k, float* __restrict__ out) {
+__global__ void ep_partial_kernel(const float* __restrict__ rows, const int32_t* __restrict__ meta, int64_t ms,
+                                  int E_local, int R, int N, int k, float* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)R * N) return;
   const int64_t r = i / N;
   const int n = (int)(i - r * N);
   float o = 0.f;
   for (int j = 0; j < k; j++) {
-    const int e = meta[r * 2 * k + j];
+    const int e = meta[r * ms + j];
     if (e >= 0 && e < E_local) o += rows[(r * k + j) * N + n];
   }
   out[i] = o;
@@ -133,19 +145,22 @@ cudaError_t launch_ep_plan(const int32_t* ids, int M, int k, int E, int world, i
 }
 
 cudaError_t launch_ep_pack(const __nv_bfloat16* x, const int32_t* ids, const float* topk_w, const int32_t* pos,
-                           const int32_t* offsets, int M, int H, int k, int E, int world, __nv_bfloat16* send_x,
-                           int32_t* send_meta, cudaStream_t st) {
-  if (M == 0) return cudaSuccess;
-  ep_pack_kernel<<<M, 256, 0, st>>>(reinterpret_cast<const uint4*>(x), ids, topk_w, pos, offsets, H / 8, k, E, world,
-                                    reinterpret_cast<uint4*>(send_x), send_meta);
+                           const int32_t* offsets, const int32_t* counts, int fill, int M, int H, int k, int E,
+                           int world, __nv_bfloat16* send_x, int64_t x_stride, int32_t* send_meta,
+                           int64_t meta_stride, cudaStream_t st) {
+  const int grid = M + (fill ? world : 0);
+  if (grid == 0) return cudaSuccess;
+  ep_pack_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(x), ids, topk_w, pos, offsets, counts, M, H / 8,
+                                       k, E, world, reinterpret_cast<uint4*>(send_x), x_stride / 8, send_meta,
+                                       meta_stride);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_partial(const float* rows, const int32_t* meta, int E_local, int R, int N, int k, float* out,
-                              cudaStream_t st) {
+cudaError_t launch_ep_partial(const float* rows, const int32_t* meta, int64_t meta_stride, int E_local, int R, int N,
+                              int k, float* out, cudaStream_t st) {
   const int64_t n = (int64_t)R * N;
   if (n == 0) return cudaSuccess;
-  ep_partial_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, meta, E_local, R, N, k, out);
+  ep_partial_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, meta, meta_stride, E_local, R, N, k, out);
   return cudaGetLastError();
 }
 

@@ -77,10 +77,11 @@ constexpr int EP_MAX_WORLD = 32;
 cudaError_t launch_ep_plan(const int32_t* ids, int M, int k, int E, int world, int32_t* pos, int32_t* counts,
                            int32_t* offsets, cudaStream_t st);
 cudaError_t launch_ep_pack(const __nv_bfloat16* x, const int32_t* ids, const float* topk_w, const int32_t* pos,
-                           const int32_t* offsets, int M, int H, int k, int E, int world, __nv_bfloat16* send_x,
-                           int32_t* send_meta, cudaStream_t st);
-cudaError_t launch_ep_partial(const float* rows, const int32_t* meta, int E_local, int R, int N, int k, float* out,
-                              cudaStream_t st);
+                           const int32_t* offsets, const int32_t* counts, int fill, int M, int H, int k, int E,
+                           int world, __nv_bfloat16* send_x, int64_t x_stride, int32_t* send_meta,
+                           int64_t meta_stride, cudaStream_t st);
+cudaError_t launch_ep_partial(const float* rows, const int32_t* meta, int64_t meta_stride, int E_local, int R, int N,
+                              int k, float* out, cudaStream_t st);
 cudaError_t launch_ep_unpack(const float* back, const int32_t* pos, const int32_t* offsets, int M, int H, int world,
                              __nv_bfloat16* out, cudaStream_t st);
 

@@ -64,7 +64,7 @@ class EPLayer:
 
 class CudaBackend:
     """The build's kernels (C ABI) for the index work, the row copies and the local experts. With ``record`` a list,
-    every received batch (rows, slot metadata) is appended to it."""
+    every received batch (rows, slot metadata, metadata row stride in int32) is appended to it."""
 
     def __init__(self, record=None):
         self.record = record
@@ -79,31 +79,47 @@ class CudaBackend:
              ops._ptr(offsets), ops._stream(dev))
         return pos, counts, offsets
 
-    def pack(self, x, ids32, w, pos, offsets, num_experts, world, rows, fill=False):
+    def pack(self, x, ids32, w, pos, offsets, num_experts, world, rows, counts=None, merged=False):
+        """Send rows and slot metadata. merged=False: (rows bf16 [rows, H], meta int32 [rows, 2k]); merged=True: one
+        bf16 buffer [rows, H + mc] with each row's metadata in its last mc columns (one all-to-all moves both), and
+        the rows no token uses (fixed-capacity segments, given ``counts``) marked as having no valid slot."""
         m, hid = x.shape
         k = ids32.shape[1]
-        send_x = torch.empty((rows, hid), dtype=torch.bfloat16, device=x.device)
-        meta = torch.empty((rows, 2 * k), dtype=torch.int32, device=x.device)
-        if fill:  # rows no token fills keep invalid slots (and zero weights)
-            meta[:, :k].fill_(-1)
-            meta[:, k:].zero_()
-        call("moek_ep_pack", ops._ptr(x), ops._ptr(ids32), ops._ptr(w), ops._ptr(pos), ops._ptr(offsets), m, hid, k,
-             num_experts, world, ops._ptr(send_x), ops._ptr(meta), ops._stream(x.device))
+        dev = x.device
+        if merged:
+            mc = meta_columns(k)
+            buf = torch.empty((rows, hid + mc), dtype=torch.bfloat16, device=dev)
+            call("moek_ep_pack", ops._ptr(x), ops._ptr(ids32), ops._ptr(w), ops._ptr(pos), ops._ptr(offsets),
+                 ops._ptr(counts), 1, m, hid, k, num_experts, world, buf.data_ptr(), hid + mc,
+                 buf.data_ptr() + 2 * hid, (hid + mc) // 2, ops._stream(dev))
+            return buf
+        send_x = torch.empty((rows, hid), dtype=torch.bfloat16, device=dev)
+        meta = torch.empty((rows, 2 * k), dtype=torch.int32, device=dev)
+        call("moek_ep_pack", ops._ptr(x), ops._ptr(ids32), ops._ptr(w), ops._ptr(pos), ops._ptr(offsets), None, 0, m,
+             hid, k, num_experts, world, ops._ptr(send_x), hid, ops._ptr(meta), 2 * k, ops._stream(dev))
         return send_x, meta
 
-    def local(self, x_recv, meta, layer: EPLayer, k):
+    def local(self, x_recv, meta, layer: EPLayer, k, meta_stride=None):
+        """fp32 partial rows [R, H] of the received rows' local slots. ``meta`` int32 rows (stride ``meta_stride``
+        int32, default 2k)."""
         if self.record is not None:
-            self.record.append((x_recv, meta))
+            self.record.append((x_recv, meta, meta_stride or 2 * k))
         r, hid = x_recv.shape
         out = torch.empty((r, hid), dtype=torch.float32, device=x_recv.device)
         if r == 0:
             return out
         ids = meta[:, :k].contiguous()
-        w = meta[:, k:].contiguous().view(torch.float32)
+        w = meta[:, k:2 * k].contiguous().view(torch.float32)
         rows = ops.moe_rows(x_recv, layer.prep, w, ids)
-        call("moek_ep_partial", ops._ptr(rows), ops._ptr(meta), layer.local_experts, r, hid, k, ops._ptr(out),
-             ops._stream(x_recv.device))
+        call("moek_ep_partial", ops._ptr(rows), meta.data_ptr(), meta_stride or 2 * k, layer.local_experts, r, hid,
+             k, ops._ptr(out), ops._stream(x_recv.device))
         return out
+
+    def local_merged(self, recv, layer: EPLayer, k):
+        """``local`` on a merged receive buffer [R, H + mc] (rows, then each row's metadata)."""
+        hid = layer.hidden
+        meta = recv[:, hid:].view(torch.int32)
+        return self.local(recv[:, :hid].contiguous(), meta, layer, k, meta_stride=recv.shape[1] // 2)
 
     def unpack(self, back, pos, offsets, m, world):
         hid = back.shape[1]
@@ -111,6 +127,15 @@ class CudaBackend:
         call("moek_ep_unpack", ops._ptr(back), ops._ptr(pos), ops._ptr(offsets), m, hid, world, ops._ptr(out),
              ops._stream(pos.device))
         return out
+
+
+def meta_columns(top_k: int) -> int:
+    """bf16 columns that hold a row's 2 * top_k int32 of slot metadata in a merged send buffer (a multiple of 8, so
+    rows stay 16-byte aligned)."""
+    return (4 * top_k + 7) // 8 * 8
+
+
+_OFFSETS: dict = {}
 
 
 def ep_moe(hidden_states: torch.Tensor, layer: EPLayer, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
@@ -136,13 +161,23 @@ def ep_moe(hidden_states: torch.Tensor, layer: EPLayer, topk_weights: torch.Tens
     w = topk_weights.float().contiguous()
     pos, counts, offsets = be.plan(ids32, layer.num_experts, world)
     if capacity:
-        offsets = torch.arange(world + 1, dtype=torch.int32, device=pos.device) * m
-        rows = world * m
-        send_x, send_meta = be.pack(x, ids32, w, pos, offsets, layer.num_experts, world, rows, fill=True)
-        recv_x, recv_meta = torch.empty_like(send_x), torch.empty_like(send_meta)
-        dist.all_to_all_single(recv_x, send_x, group=group)
-        dist.all_to_all_single(recv_meta, send_meta, group=group)
-        partial = be.local(recv_x, recv_meta, layer, k)
+        key = (m, world, pos.device)
+        offsets = _OFFSETS.get(key)
+        if offsets is None:
+            offsets = _OFFSETS[key] = torch.arange(world + 1, dtype=torch.int32, device=pos.device) * m
+        if hasattr(be, "local_merged"):  # rows and metadata in one buffer: one all-to-all each way
+            send = be.pack(x, ids32, w, pos, offsets, layer.num_experts, world, world * m, counts=counts,
+                           merged=True)
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=group)
+            partial = be.local_merged(recv, layer, k)
+        else:
+            send_x, send_meta = be.pack(x, ids32, w, pos, offsets, layer.num_experts, world, world * m,
+                                        counts=counts, fill=True)
+            recv_x, recv_meta = torch.empty_like(send_x), torch.empty_like(send_meta)
+            dist.all_to_all_single(recv_x, send_x, group=group)
+            dist.all_to_all_single(recv_meta, send_meta, group=group)
+            partial = be.local(recv_x, recv_meta, layer, k)
         back = torch.empty_like(partial)
         dist.all_to_all_single(back, partial, group=group)
         return be.unpack(back, pos, offsets, m, world)

@@ -48,7 +48,7 @@ class OracleBackend:
         self._pos = pos
         return torch.from_numpy(pos), torch.from_numpy(counts), torch.from_numpy(offsets)
 
-    def pack(self, x, ids32, w, pos, offsets, num_experts, world, rows, fill=False):
+    def pack(self, x, ids32, w, pos, offsets, num_experts, world, rows, counts=None, fill=False):
         sx, meta = oep.pack(x, ids32.numpy(), w.numpy(), pos.numpy(), offsets.numpy(), num_experts, world)
         assert sx.shape[0] == rows
         return sx, meta

@@ -50,14 +50,25 @@ def test_ep_kernels_match_oracle(world, m):
     from qwen38_flash_coder_b200 import ops
     from qwen38_flash_coder_b200._lib import call
 
-    call("moek_ep_partial", ops._ptr(rows.to(DEV)) if R else None, ops._ptr(meta), el, R, H, k, ops._ptr(out),
-         ops._stream(DEV))
+    call("moek_ep_partial", ops._ptr(rows.to(DEV)) if R else None, ops._ptr(meta), 2 * k, el, R, H, k,
+         ops._ptr(out), ops._stream(DEV))
     exp = torch.zeros((R, H))
     lid = rmeta[:, :k]
     for j in range(k):
         valid = ((lid[:, j] >= 0) & (lid[:, j] < el))[:, None]
         exp += torch.where(valid, rows.view(R, k, H)[:, j], torch.zeros(()))
     assert torch.equal(out.cpu(), exp)
+    # merged fixed-capacity layout: segment d = rows [d*m, (d+1)*m), metadata in each row's tail, unused rows marked
+    cap_off = torch.arange(world + 1, dtype=torch.int32, device=DEV) * m
+    buf = be.pack(x.to(DEV), ids.to(DEV), w.to(DEV), pos, cap_off, E, world, world * m, counts=counts, merged=True)
+    mc = ep.meta_columns(k)
+    bx, bm = buf[:, :H].cpu(), buf[:, H:].contiguous().view(torch.int32).cpu()[:, :2 * k]
+    for d in range(world):
+        n = int(rcounts[d])
+        assert torch.equal(bx[d * m:d * m + n], rsx[roff[d]:roff[d] + n])
+        assert torch.equal(bm[d * m:d * m + n], rmeta[roff[d]:roff[d] + n])
+        assert (bm[d * m + n:(d + 1) * m, :k] == -1).all() and (bm[d * m + n:(d + 1) * m, k:] == 0).all()
+    assert buf.shape[1] == H + mc
     # unpack: returned partials added in rank order, one bf16 rounding
     back = torch.randn((R, H), generator=g)
     res = be.unpack(back.to(DEV), pos, offsets, m, world)
