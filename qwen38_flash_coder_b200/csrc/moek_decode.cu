@@ -186,16 +186,21 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
             uint8_t* dst = smem + slot * C::SLOT;
             if (lane == 0) mbar_expect_tx(full + slot, STAGE_BYTES + PAIR_BYTES + nv * BK * 2);
             __syncwarp();
-            if (lane == 0) {
-              const int64_t wi = ((int64_t)e * nt + item) * nstage + cst;
-              bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
-              const int64_t si = ((int64_t)e * nt + item) * nb + (cst >> 1);
-              bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
-            }
-            for (int rr = lane; rr < nv; rr += 32) {
-              const int id = mids[ci * XR + rr];
-              const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + cst * BK;
-              bulk_g2s(dst + C::X_OFF + rr * X_STRIDE, src, BK * 2, full + slot);
+            // every copy of the stage from its own lane in one instruction (a bulk copy's issue latency is paid once
+            // per instruction, not once per copy): lane 0 the codes, lane 1 the scale pair, lanes 2.. the rows
+            for (int c = lane; c < 2 + nv; c += 32) {
+              if (c == 0) {
+                const int64_t wi = ((int64_t)e * nt + item) * nstage + cst;
+                bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, full + slot);
+              } else if (c == 1) {
+                const int64_t si = ((int64_t)e * nt + item) * nb + (cst >> 1);
+                bulk_g2s(dst + STAGE_BYTES, p.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+              } else {
+                const int rr = c - 2;
+                const int id = mids[ci * XR + rr];
+                const __nv_bfloat16* src = p.A + (int64_t)(id / p.a_div) * p.K + cst * BK;
+                bulk_g2s(dst + C::X_OFF + rr * X_STRIDE, src, BK * 2, full + slot);
+              }
             }
             issued++;
           }
