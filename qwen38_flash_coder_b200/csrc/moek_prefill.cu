@@ -13,23 +13,28 @@
 //   unit      = (moe_align block of <= 128 rows, 256-row item); units dealt round-robin to one persistent CTA per SM.
 //   producer  = warp 0: per 64-k stage, bulk-copies (cp.async.bulk, no multicast) the 8 KB of packed codes and the
 //               1056-byte packed-scale run pair into a ring slot (mbarrier complete_tx).
-//   MMA       = warp 1 (one lane): per stage 2 halves x 4 k16 steps of tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16
-//               -> fp32), A from a TMEM ring slot, B from a shared-memory K-major SWIZZLE_128B tile, D in TMEM.
-//               tcgen05.commit releases the A and B slots and, after a unit's last stage, hands D to the epilogue.
+//   MMA       = warps 1-4 (one lane each): per stage 2 halves x 4 k16 steps of tcgen05.mma.cta_group::1.kind::f16
+//               (bf16 x bf16 -> fp32), A from a TMEM ring slot, B from a shared-memory K-major SWIZZLE_128B tile, D in
+//               TMEM. Warp 1 + 2h + p issues the MMAs of accumulator (half h, k16 parity p) (with two accumulators,
+//               warp 1 + 2h issues half h's): one thread's tcgen05.mma issue is latency-bound, so four issuing warps
+//               keep four times as many in flight. Each warp's tcgen05.commit releases the A and B slots (four
+//               arrivals) and, after a unit's last stage, hands D to the epilogue.
 //               Warp 1 also allocates and frees the 512 TMEM columns: D = columns 0-319 (four accumulators of <= 80
 //               columns for blocks of <= 80 padded rows, else two of <= 128), A ring = columns 320-511 (3 slots x two
 //               halves x 32 columns of bf16 pairs). An MMA costs about the same for any N <= 256 and chained MMAs
 //               into one accumulator wait on each other, so more independent accumulators means more MMAs in flight.
-//   loader    = warp 2: the block's activation rows gathered by TMA (cp.async.bulk.tensor tile::gather4, no
-//               multicast: 4 rows of 64 k per instruction, one instruction per lane) into the 128-byte-swizzled B tile
-//               of the stage; rows past the block's valid ones read out of bounds and arrive as zeros.
-//   scales    = warp 3: per unit the (B | R) table of the expert's scale bytes (moek_common.cuh) and the unit's
+//   loaders   = warps 5-6: the block's activation rows gathered by TMA (cp.async.bulk.tensor tile::gather4, no
+//               multicast: 4 rows of 64 k per instruction, one instruction per lane, the two warps taking alternate
+//               gathers) into the 128-byte-swizzled B tile of the stage; rows past the block's valid ones read out of
+//               bounds and arrive as zeros.
+//   scales    = warp 7: per unit the (B | R) table of the expert's scale bytes (moek_common.cuh) and the unit's
 //               exception lists; per stage the scale byte of each of the 256 rows x 4 k-groups (base + 4-bit offset,
 //               then the exceptions), one 32-bit word per row.
-//   dequant   = warps 4-11: warp 4 + 4h + q owns rows 128h + 32q .. +31 of the item (TMEM lane quarter q = warp % 4);
+//   dequant   = warps 8-15: warp 8 + 4h + i owns rows 128h + 32q .. +31 of the item, q = warp % 4 (its TMEM lane
+//               quarter);
 //               per stage a thread reads its row's 32 bytes of codes and its scale word, and stores 32 columns of
 //               bf16 pairs into the A slot.
-//   epilogue  = warps 12-15 (lane quarter = warp % 4): tcgen05.ld 32 columns at a time; gate_up writes
+//   epilogue  = warps 16-19 (lane quarter = warp % 4): tcgen05.ld 32 columns at a time; gate_up writes
 //               act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves 0 and 1), down writes
 //               the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
 //
@@ -55,7 +60,10 @@ constexpr int NB = 4;     // shared-memory ring of activation tiles
 constexpr int NA = 3;     // TMEM ring of dequantised weight tiles
 constexpr int NDQ = 8;    // dequant warps
 constexpr int NEPI = 4;   // epilogue warps
-constexpr int W_PROD = 0, W_MMA = 1, W_LOAD = 2, W_SCALE = 3, DQ0 = 4, EPI0 = DQ0 + NDQ;
+constexpr int NMMA = 4;   // MMA-issuing warps: one per accumulator (half h, k16-step parity p) = warp W_MMA + 2h + p
+constexpr int NLOAD = 2;  // activation-gather warps (a TMA issue is latency-bound per thread: two warps, twice the rate)
+constexpr int W_PROD = 0, W_MMA = 1, W_LOAD = W_MMA + NMMA, W_SCALE = W_LOAD + NLOAD, DQ0 = W_SCALE + 1,
+              EPI0 = DQ0 + NDQ;
 constexpr int THREADS = (EPI0 + NEPI) * 32;
 // TMEM columns. D: a block of N <= QUAD_N padded rows keeps four accumulators (half h, k16-step parity p at column
 // (2h + p) * QUAD_N), so four independent MMA chains are in flight; larger blocks keep two (half h at column 128h).
@@ -72,8 +80,8 @@ constexpr int EXC_CAP = 2048;  // exception entries of one unit cached in shared
 constexpr int LUT_OFF = W_OFF + NW * W_SLOT;                     // 2 x 256 (B | R) words (units alternate)
 constexpr int EXC_OFF = LUT_OFF + 2 * 256 * 4;                   // EXC_CAP entries (scale warp only)
 constexpr int RUNOFF_OFF = EXC_OFF + EXC_CAP * 4;                // 33 run offsets (scale warp only)
-constexpr int IDS_OFF = (RUNOFF_OFF + 33 * 4 + 15) / 16 * 16;    // 128 activation rows (loader only)
-constexpr int MISC_OFF = IDS_OFF + BMP * 4;                      // tmem base, abort flag
+constexpr int IDS_OFF = (RUNOFF_OFF + 33 * 4 + 15) / 16 * 16;    // 128 activation rows per loader warp
+constexpr int MISC_OFF = IDS_OFF + 2 * BMP * 4;                  // tmem base, abort flag
 constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
 constexpr int NBARS = 3 * NW + 2 * NB + 2 * NA + 2 + 2;
 constexpr int SMEM_USED = BAR_OFF + NBARS * 8;
@@ -237,13 +245,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < NB; i++) {
       mbar_init(B.bfull + i, 1);
-      mbar_init(B.bempty + i, 1);
+      mbar_init(B.bempty + i, NMMA);  // every MMA warp commits
     }
     for (int i = 0; i < NA; i++) {
       mbar_init(B.afull + i, NDQ);
-      mbar_init(B.aempty + i, 1);
+      mbar_init(B.aempty + i, NMMA);
     }
-    mbar_init(B.accfull, 1);
+    mbar_init(B.accfull, NMMA);
     mbar_init(B.accempty, NEPI);
     mbar_init(B.lutempty, NDQ);
     mbar_init(B.lutempty + 1, NDQ);
@@ -284,7 +292,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
       }
     }
-  } else if (warp == W_MMA) {  // ---------------------------------------------------------------------- MMA
+  } else if (warp >= W_MMA && warp < W_MMA + NMMA) {  // ------------------------------------------------ MMA
+    const int mh = (warp - W_MMA) >> 1, mp = (warp - W_MMA) & 1;  // this warp's accumulator
     uint32_t g = 0, un = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
@@ -316,12 +325,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t a0 = tmem + A_COL0 + a * A_SLOT_COLS;
 #pragma unroll
           for (int ks = 0; ks < 4; ks++) {
+            // four accumulators (half h, parity ks & 1): this warp's; two (half h): warp p = 0 of each half
+            if (quad ? (ks & 1) != mp : mp != 0) continue;
             const uint64_t bd = umma_desc_k_sw128(b0 + 32 * ks);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-              const uint32_t d = quad ? (2 * h + (ks & 1)) * QUAD_N : h * 128;
-              umma_ts(tmem + d, a0 + h * 32 + ks * 8, bd, idesc, (st > 0 || ks >= (quad ? 2 : 1)) ? 1u : 0u);
-            }
+            const uint32_t d = quad ? (2 * mh + mp) * QUAD_N : mh * 128;
+            umma_ts(tmem + d, a0 + mh * 32 + ks * 8, bd, idesc, (st > 0 || ks >= (quad ? 2 : 1)) ? 1u : 0u);
           }
           umma_commit(B.aempty + a);  // the A and B slots may be refilled once these MMAs completed
           umma_commit(B.bempty + b);
@@ -332,8 +340,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
       un++;
     }
-  } else if (warp == W_LOAD) {  // ------------------------------------------------------------- activation loader
-    int* rowc = reinterpret_cast<int*>(smem + IDS_OFF);
+  } else if (warp >= W_LOAD && warp < W_LOAD + NLOAD) {  // --------------------------------------- activation loaders
+    int* rowc = reinterpret_cast<int*>(smem + IDS_OFF) + (warp - W_LOAD) * BMP;  // each loader warp its own copy
+    const int lw = warp - W_LOAD;                // gathers lw, lw + NLOAD, ... of a stage are this warp's
     const int rows_a = p.num_ids / p.a_div;  // rows of A; a coordinate of rows_a reads zeros
     uint32_t g = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
@@ -359,11 +368,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        if (lane == 0) mbar_expect_tx(B.bfull + b, ng * 4 * 128);
+        // the first loader's arrival carries the stage's byte count; the other's copies may complete before it
+        // (the phase cannot end before that arrival)
+        if (lw == 0 && lane == 0) mbar_expect_tx(B.bfull + b, ng * 4 * 128);
         __syncwarp();
-        if (lane < ng)
-          tma_gather4(smem + B_OFF + b * B_BYTES + lane * 512, &tmap_a, st * BK,
-                      *reinterpret_cast<const int4*>(rowc + 4 * lane), B.bfull + b);
+        const int j = lane * NLOAD + lw;  // this lane's gather of the stage
+        if (j < ng)
+          tma_gather4(smem + B_OFF + b * B_BYTES + j * 512, &tmap_a, st * BK,
+                      *reinterpret_cast<const int4*>(rowc + 4 * j), B.bfull + b);
       }
       if (!ok) break;
     }
