@@ -45,13 +45,16 @@ constexpr int MAXU = 64;        // units per metadata round
 constexpr int MAXRUN = 32;      // packed-scale runs per unit (K / 128 / nsplit)
 constexpr int EXC_POOL = 1024;  // exception entries cached in shared memory per round
 
-// Per-unit metadata, gathered by the producer warp once per round (MAXU units) so that no thread waits on a global
-// load inside the stage loop.
+// Per-unit metadata, gathered once per round (MAXU units) so that no thread waits on a global load inside the stage
+// loop. The producer fills the first group (units, experts, rows) and publishes it with mfull; the scale warp, the
+// only reader of the second group (global scale, exception lists), fills it itself afterwards, so that those
+// dependent loads overlap the producer's streaming instead of delaying it.
 struct UnitMeta {
-  int blk, item, ks, e, nv, flags;  // flags: 1 = exception list read from global, 2 = block has more rows than XR
+  int blk, item, ks, e, nv, flags;  // flags: 2 = block has more rows than XR
   float g;                           // the expert's global scale
+  int from_global;                   // 1 = the exception list is read from global memory (did not fit the pool)
   int exc_g0;                        // global index of the unit's first exception entry
-  int exc_s0;                        // shared-pool index of the unit's first entry (flags & 1 == 0)
+  int exc_s0;                        // shared-pool index of the unit's first entry (from_global == 0)
   int run_off[MAXRUN + 1];           // entry offsets, relative to the first, at each run boundary
 };
 
@@ -169,8 +172,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         m.flags = (lim < p.block_m && p.sorted_ids[row0 + lim] < p.num_ids) ? 2 : 0;
       }
       __syncwarp();
-      // stream: the first NS stages go out now (they need only the expert and the rows), the rest after the
-      // scale and exception metadata is published
+      // stream: the copies need only the expert and the rows
       int ci = 0, cst = -1;  // cursor: unit index and stage of the next copy
       auto issue = [&](int limit) -> bool {
         int issued = 0;
@@ -208,38 +210,7 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
         }
         return true;
       };
-      if (!issue(r == 0 ? C::NS : 0)) return;
-      // global scales and exception-list bounds
-      for (int i = lane; i < nu; i += 32) {
-        UnitMeta& m = meta[i];
-        const bool valid = m.e >= 0 && m.e < p.E;
-        m.g = valid ? p.G[m.e] : 0.f;
-        const int64_t key0 = ((int64_t)(valid ? m.e : 0) * nt + m.item) * nb + (int64_t)m.ks * nruns;
-        const int o0 = valid ? p.exc_off[key0] : 0;
-        m.exc_g0 = o0;
-        for (int j = 0; j <= nruns; j++) m.run_off[j] = valid ? p.exc_off[key0 + j] - o0 : 0;
-      }
-      __syncwarp();
-      if (lane == 0) {  // pool places; a unit whose list does not fit reads it from global memory
-        int used = 0;
-        for (int i = 0; i < nu; i++) {
-          const int n = meta[i].run_off[nruns];
-          if (used + n <= EXC_POOL) {
-            meta[i].exc_s0 = used;
-            used += n;
-          } else {
-            meta[i].flags |= 1;
-          }
-        }
-      }
-      __syncwarp();
-      for (int i = lane; i < nu; i += 32) {  // each lane copies its own units' lists: loads in parallel
-        if (meta[i].flags & 1) continue;
-        const int n = meta[i].run_off[nruns], s0 = meta[i].exc_s0, g0 = meta[i].exc_g0;
-        for (int j = 0; j < n; j++) pool[s0 + j] = p.exc_ent[g0 + j];
-      }
-      __syncwarp();
-      mbar_arrive(mfull);
+      mbar_arrive(mfull);  // ids, rows and experts published: consumers and the scale warp may start
       if (!issue(1 << 30)) return;
     }
     return;
@@ -257,16 +228,45 @@ __global__ void __launch_bounds__(DC_THREADS, DecodeCfg<XR>::MINB) moek_decode_k
     for (int r = 0; r < rounds; r++) {
       const int nu = min(MAXU, n_mine - r * MAXU);
       if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) return;
+      // the round's global scales and exception-list bounds (one unit per lane), then the lists into the pool
+      for (int i = lane; i < nu; i += 32) {
+        UnitMeta& m = meta[i];
+        const bool valid = m.e >= 0 && m.e < p.E;
+        m.g = valid ? p.G[m.e] : 0.f;
+        const int64_t key0 = ((int64_t)(valid ? m.e : 0) * nt + m.item) * nb + (int64_t)m.ks * nruns;
+        const int o0 = valid ? p.exc_off[key0] : 0;
+        m.exc_g0 = o0;
+        for (int j = 0; j <= nruns; j++) m.run_off[j] = valid ? p.exc_off[key0 + j] - o0 : 0;
+      }
+      __syncwarp();
+      if (lane == 0) {  // pool places; a unit whose list does not fit reads it from global memory
+        int used = 0;
+        for (int i = 0; i < nu; i++) {
+          const int n = meta[i].run_off[nruns];
+          meta[i].from_global = used + n > EXC_POOL;
+          if (!meta[i].from_global) {
+            meta[i].exc_s0 = used;
+            used += n;
+          }
+        }
+      }
+      __syncwarp();
+      for (int i = lane; i < nu; i += 32) {  // each lane copies its own units' lists: loads in parallel
+        if (meta[i].from_global) continue;
+        const int n = meta[i].run_off[nruns], s0 = meta[i].exc_s0, g0 = meta[i].exc_g0;
+        for (int j = 0; j < n; j++) pool[s0 + j] = p.exc_ent[g0 + j];
+      }
+      __syncwarp();
       for (int ui = 0; ui < nu; ui++) {
         const UnitMeta& m = meta[ui];
-        const int e = m.e, item = m.item, ks = m.ks, flags = m.flags;
+        const int e = m.e, item = m.item, ks = m.ks;
         if (e < 0 || e >= p.E) continue;
         const float gsc = m.g;
         uint32_t* lt = lut + (k % NLUT) * 256;
 #pragma unroll
         for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
         k++;
-        const uint32_t* exc = (flags & 1) ? p.exc_ent + m.exc_g0 : pool + m.exc_s0;
+        const uint32_t* exc = m.from_global ? p.exc_ent + m.exc_g0 : pool + m.exc_s0;
         const int r0g = p.gate_up ? item : 2 * item;  // global run index of the pair's first run
         for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
           const int slot = g % C::NS;
