@@ -77,7 +77,12 @@ int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_exper
  *   A       bf16: gate_up: hidden states [M, K] (row id / top_k); down: act [num_ids, K] (row id, top_k = 1).
  *   S       must be NULL (plain Marlin scales go with Marlin's untiled weight layout, which this build does not use);
  *           tiled must be 1.
- *   mode    2: split-k; the kernel writes fp32 partial sums part[nsplit][num_ids][N] (gate_up: gate at column c, up
+ *   mode    0: the tcgen05 path for large batches (block_m <= 128, K <= 4096, nsplit 1): gate_up writes act bf16
+ *           [num_ids, N/2] = bf16(silu(g) * u) to out; down writes the fp32 rows topk_w[id] * sum to part
+ *           [num_ids, N] (finish with moek_combine).
+ *           1: as 0, but act is kept in moe_align's sorted order: gate_up writes act row sorted position (out holds
+ *           sorted_len rows) and down reads A by sorted position, one 128-row tile per stage instead of a gather.
+ *           2: split-k; the kernel writes fp32 partial sums part[nsplit][num_ids][N] (gate_up: gate at column c, up
  *           at N/2 + c) and moek_split_epilogue finishes (the reference's mode 2).
  *           3: the epilogue is fused. nsplit 1: gate_up writes act bf16 [num_ids, N/2] = bf16(silu(g) * u) to out;
  *           down writes fp32 rows topk_w[id] * sum to part [num_ids, N] (finish with moek_combine). nsplit > 1:
@@ -86,7 +91,7 @@ int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_exper
  *           (part holds (nsplit + 1) * num_ids * N floats) and the arrival that completes a token's valid slots
  *           writes out bf16 [num_ids/combine_k, N] = their sum in slot order (slots whose topk_ids entry is outside
  *           [0, E) are left out).
- *           (The reference's modes 0/1, its atomic item counter and stream-k, are not available.)
+ *           (The reference's own modes 0/1, its atomic item counter and stream-k, are not available.)
  *   nsplit  K/64/nsplit must be even (whole packed-scale runs), K/128/nsplit <= 32.
  *   cnt     int32, zero-filled before the first call; cnt[0] is the device error word (MOEK_DEV_*), cnt[1..] the
  *           split counters (mode 3, nsplit > 1: 1 + max_blocks * N/256 entries, down + (num_ids/combine_k) * N/256,

@@ -113,9 +113,9 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
     return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm null pointer");
   if (!gate_up && top_k != 1) return fail(MOEK_ERR_ARG, "moek_b200: down reads one activation row per id (top_k 1)");
   if (top_k <= 0) return fail(MOEK_ERR_ARG, "moek_b200: top_k must be positive");
-  if (mode != 0 && mode != 2 && mode != 3)
-    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (0, 2 or 3)", mode);
-  if (mode == 0) {  // tcgen05 path: whole K per unit, direct epilogue
+  if (mode < 0 || mode > 3)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (0-3)", mode);
+  if (mode <= 1) {  // tcgen05 path: whole K per unit, direct epilogue; mode 1: act rows in moe_align's sorted order
     if (K / 128 > 32) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: mode 0 supports K <= 4096 (got %d)", K);
     if (block_m > moek::prefill_block_m())
       return fail(MOEK_ERR_ARG, "moek_b200: mode 0 takes moe_align blocks of <= %d rows (got %d)",
@@ -149,7 +149,9 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
     p.max_blocks = (int)std::min<int64_t>(sorted_len / block_m,
                                           (num_ids + block_m - 1) / block_m + std::min<int64_t>(E, num_ids));
     p.gate_up = gate_up ? 1 : 0;
-    p.mode = 0;
+    p.mode = mode;
+    // mode 1 down reads A (act) by sorted position: sorted_len rows; otherwise A rows are tokens (num_ids / top_k)
+    p.a_rows = (mode == 1 && !gate_up) ? (int)sorted_len : std::max(1, num_ids / top_k);
     return cuda_status(moek::launch_prefill(p, sm_count(), (cudaStream_t)stream), "moe_gemm (tcgen05) launch");
   }
   const int nstage = K / moek::BK;

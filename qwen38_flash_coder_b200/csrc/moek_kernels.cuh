@@ -44,6 +44,7 @@ struct GemmParams {
   void* out;                // mode 3: gate_up -> act bf16 [num_ids, N/2]; down (split) -> bf16 [M, N] top-k sums
   uint64_t timeout_ns;
   int num_ids, N, K, E, a_div, block_m, nsplit, max_blocks;
+  int a_rows;  // tcgen05 path: rows of A (x: num_ids / a_div; mode 1 down: the sorted act rows)
   int gate_up, mode, combine_k;
 };
 

@@ -34,9 +34,11 @@
 //               quarter);
 //               per stage a thread reads its row's 32 bytes of codes and its scale word, and stores 32 columns of
 //               bf16 pairs into the A slot.
-//   epilogue  = warps 16-19 (lane quarter = warp % 4): tcgen05.ld 32 columns at a time; gate_up writes
+//   epilogue  = warps 16-19 (lane quarter = warp % 4): tcgen05.ld 16 columns at a time; gate_up writes
 //               act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves 0 and 1), down writes
 //               the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
+//   mode 1    = gate_up writes act at the row's position in moe_align's sorted order instead of its id, so that the
+//               down GEMM loads a block's rows as one 128-row TMA tile per stage instead of gathering them.
 //
 // Every wait is bounded (%globaltimer); on expiry the CTA raises an abort flag, every role skips its remaining work
 // in step, and TMEM is freed before the kernel returns.
@@ -102,6 +104,16 @@ __device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, i
       "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(rows.x), "r"(rows.y), "r"(rows.z), "r"(rows.w),
       "r"(smem_u32(bar))
+      : "memory");
+}
+
+// TMA load of a 2-D tile (box: 64 bf16 x 128 rows, 128-byte swizzle) into shared memory, completion on an mbarrier.
+// No multicast.
+__device__ __forceinline__ void tma_tile2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -343,7 +355,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp >= W_LOAD && warp < W_LOAD + NLOAD) {  // --------------------------------------- activation loaders
     int* rowc = reinterpret_cast<int*>(smem + IDS_OFF) + (warp - W_LOAD) * BMP;  // each loader warp its own copy
     const int lw = warp - W_LOAD;                // gathers lw, lw + NLOAD, ... of a stage are this warp's
-    const int rows_a = p.num_ids / p.a_div;  // rows of A; a coordinate of rows_a reads zeros
+    const int rows_a = p.a_rows;  // rows of A; a coordinate of rows_a reads zeros
+    const bool tile_rows = p.mode == 1 && !p.gate_up;  // act in sorted order: the block's rows are contiguous
     uint32_t g = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
@@ -370,6 +383,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         // the first loader's arrival carries the stage's byte count; the other's copies may complete before it
         // (the phase cannot end before that arrival)
+        if (tile_rows) {  // one TMA for the block's 128 rows (rows past the block's valid ones are not read)
+          if (lw == 0 && lane == 0) {
+            mbar_expect_tx(B.bfull + b, BMP * 128);
+            tma_tile2d(smem + B_OFF + b * B_BYTES, &tmap_a, st * BK, (int)row0, B.bfull + b);
+          }
+          __syncwarp();
+          continue;
+        }
         if (lw == 0 && lane == 0) mbar_expect_tx(B.bfull + b, ng * 4 * 128);
         __syncwarp();
         const int j = lane * NLOAD + lw;  // this lane's gather of the stage
@@ -538,8 +559,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < 16; j++) {
           if (c0 + j >= nv) break;
           const int id = __shfl_sync(0xffffffffu, ids[jj], l0 + j);
-          if (p.gate_up) {
-            static_cast<__nv_bfloat16*>(p.out)[(int64_t)id * I + 128 * ui.item + row] =
+          if (p.gate_up) {  // mode 1: act row = the row's sorted position, else its id
+            const int64_t arow = p.mode == 1 ? row0 + c0 + j : (int64_t)id;
+            static_cast<__nv_bfloat16*>(p.out)[arow * I + 128 * ui.item + row] =
                 __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
           } else {
             const float w = __shfl_sync(0xffffffffu, wts[jj], l0 + j);
@@ -589,9 +611,10 @@ cudaError_t launch_prefill(const GemmParams& p, int sms, cudaStream_t st) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
   CUtensorMap tmap;
-  const cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)std::max(1, p.num_ids / p.a_div)};
+  const cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)std::max(1, p.a_rows)};
   const cuuint64_t strides[1] = {(cuuint64_t)p.K * 2};
-  const cuuint32_t box[2] = {BK, 1}, estr[2] = {1, 1};
+  // gathered rows: a 1-row box (tile::gather4); mode 1 down: the block's 128 consecutive rows in one box
+  const cuuint32_t box[2] = {BK, (p.mode == 1 && !p.gate_up) ? (cuuint32_t)pf::BMP : 1u}, estr[2] = {1, 1};
   if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(p.A), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)

@@ -256,10 +256,13 @@ def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
     sid, eid, npad = moe_align_block_size(ids32, BM_PREFILL, layer.E)
     part = _scratch("part", num_ids * b.N, torch.float32, dev) if rows_k is None else \
         torch.empty((num_ids, b.N), dtype=torch.float32, device=dev)
+    # mode 1: act rows in moe_align's sorted order (row = position in sorted_ids), so the down GEMM reads each block's
+    # rows as one tile instead of gathering them
+    act = torch.empty((sid.numel(), a.N // 2), dtype=torch.bfloat16, device=dev)
     _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, 1, part, rows, act, tw, ids32,
-                                      top_k, mode=0, block_m=BM_PREFILL))
+                                      top_k, mode=1, block_m=BM_PREFILL))
     _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, 1, part, rows, None, tw, ids32,
-                                      top_k, mode=0, block_m=BM_PREFILL))
+                                      top_k, mode=1, block_m=BM_PREFILL))
     if rows_k is not None:
         return part
     call("moek_combine", _ptr(part), 1, _ptr(output), m, b.N, top_k, _stream(dev))
