@@ -45,9 +45,9 @@ METRIC = "routed-MoE layer µs & HBM GB/s (M=8,32); TFLOP/s (M=6912); 1/2/4/8 GP
 H, I, E, TOPK = 2048, 512, 512, 5
 FLOPS_PER_ROW = 2 * 3 * H * I  # gate + up + down per (token, slot) row
 
-# DRAM bytes (read + write) of one gate_up launch, from one ncu --set full capture each:
-# profiles/moek_decode_kernel_decode8.md (layer 0 of the seeded layers) and profiles/moek_prefill_kernel_prefill6912.md
-TRAFFIC = {"decode8": 42_990_336, "prefill": 695_317_952}
+# DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu --set full capture each:
+# profiles/moek_prefill_kernel_prefill6912.md (gate_up launch); the whole-layer decode kernel has none yet
+TRAFFIC = {"prefill": 695_317_952}
 
 WORKLOADS = {
     "decode8": dict(m=8, route="uniform", unit="GB/s", desc="decode verify M=8 (1 stream x block 8), uniform routing"),
@@ -254,8 +254,10 @@ def measure(name, layers, a, dev, world, barrier, headline):
     # roofline of the dominant kernel: the step's gate_up GEMM launches alone, replayed as a graph
     rec = ops.record_launches(step)
     kern_us = {}
-    for kname in ("gate_gemm", "down_gemm"):
+    for kname in ("layer", "gate_gemm", "down_gemm"):
         fns = [f for n, f in rec if n == kname]
+        if not fns:
+            continue
         g = make_graph(lambda: [f() for f in fns], 2)
         kern_us[kname] = over_ranks(timed(g.replay, a.steps, barrier) * 1e3 / len(fns), world, dev)
         del g
@@ -264,14 +266,15 @@ def measure(name, layers, a, dev, world, barrier, headline):
     if os.path.exists(pp):
         peaks = json.load(open(pp))
     traffic = TRAFFIC.get(name)
-    if wl["unit"] == "GB/s":
-        gb = sum(gate_bytes(L["prep"], L["route"][name][0], m) for L in layers) / nl
+    if wl["unit"] == "GB/s":  # the whole-layer kernel: every touched expert's gate_up and down bytes, x, out
+        gb = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] for L in layers) / nl
         peak = peaks.get("hbm_gbs", 6650.0)
-        achieved = gb / (kern_us["gate_gemm"] / 1e6) / 1e9
-        roof = {"kernel": "moek_decode_kernel (gate_up, split-k)", "bound": "hbm", "achieved": round(achieved, 1),
-                "peak": peak, "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
-                else "of fallback", "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                "bytes_per_launch": int(gb)}
+        achieved = gb / (kern_us["layer"] / 1e6) / 1e9
+        roof = {"kernel": "moek_layer_kernel (whole decode layer, one launch)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": peak,
+                "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic, "bytes_per_launch": int(gb),
+                "avg_launch_us": round(kern_us["layer"], 2)}
     else:
         flops = m * TOPK * 2 * H * 2 * I  # gate + up rows of real tokens
         peak = peaks.get("bf16_tflops_sustained", 1400.0)
@@ -280,8 +283,9 @@ def measure(name, layers, a, dev, world, barrier, headline):
                 "peak": peak, "peak_source": "of measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
                 if "bf16_tflops_sustained" in peaks else "of fallback", "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "flops_per_launch": flops}
-    roof["avg_launch_us"] = round(kern_us["gate_gemm"], 2)
-    roof["down_gemm_avg_us"] = round(kern_us["down_gemm"], 2)
+    if "gate_gemm" in kern_us:
+        roof["avg_launch_us"] = round(kern_us["gate_gemm"], 2)
+        roof["down_gemm_avg_us"] = round(kern_us["down_gemm"], 2)
     res = {"workload": wl["desc"], "value": round(value, 3), "unit": wl["unit"], "ms_per_step": round(ms, 4),
            "us_per_layer": round(ms * 1e3 / nl, 2), "roofline": roof, "clocks": clk,
            "gpu_launches_per_step": ops.launches_per_layer(m, TOPK) * nl}

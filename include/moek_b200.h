@@ -122,6 +122,37 @@ int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int3
  * 284-289): out bf16 [m, N] = bf16(sum_j rows[t*top_k + j]) in fp32, slot order. rows: fp32 if rows_fp32 else bf16. */
 int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int32_t N, int32_t top_k, void* stream);
 
+/* ---- Whole decode layer in one launch. Replaces, for decode batches, the sequence the kit's forward wrap runs
+ * (files/mbx_moek.py:236-289: moe_align, gate_up moe_gemm, split epilogue, down moe_gemm, split epilogue + top-k sum)
+ * with one persistent kernel: routing in shared memory, gate_up + SwiGLU, down x router weight and the top-k sum,
+ * the down units waiting (bounded) on the gate_up units that produce their act columns. */
+
+/* int32 count of the persistent state for (num_experts, H, I): counters and ready stamps. Zero it once before the
+ * first call; every completed call leaves it valid for the next one of the same geometry (after a device error,
+ * zero it again). Calls that share a state buffer must be ordered (one stream). */
+int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n);
+
+/* Scratch bytes of one call: act, k-split partials and the fp32 slot rows (rows_out != 0: the caller's out_rows
+ * receives the rows and no top-k sum is formed). Contents need not be preserved between calls. */
+int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t nsplit_gate,
+                               int32_t nsplit_down, int32_t rows_out, size_t* bytes);
+
+/* out bf16 [M, H] = bf16(sum over valid slots j in order of topk_w[t, j] * down_e(bf16(silu(g) * u))) with
+ * (g, u) = gate_up_e(x[t]) in fp32, e = topk_ids[t, j] in [0, E) (other ids are not routed; a token with none gets
+ * zeros), the weights dequantised as the oracle does (bf16(e2m1 * s * gs)). With out = NULL and out_rows set, the
+ * fp32 rows [M * top_k, H] = topk_w * down_e(...) are written instead (rows of unrouted slots are left as they were).
+ *   x       bf16 [M, H]; M <= 96 and M * top_k <= 512 (decode batches; larger ones take the moek_gemm path).
+ *   w13/sp13/g13/exc_off13/exc_ent13  gate_up in the tiled formats above (N = 2I, K = H); w2.. likewise (N = H,
+ *           K = I). H % 256 == 0, I % 128 == 0, both <= 4096.
+ *   nsplit_gate, nsplit_down  k-splits per 256-row item; (K/64/nsplit) even.
+ *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
+int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
+                   const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13, const float* g13,
+                   const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2, const uint8_t* sp2,
+                   const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                   int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state, int64_t state_ints,
+                   int32_t* err, void* out, float* out_rows, void* stream);
+
 /* ---- Expert parallelism. The reference has none (its hook rejects expert_map, files/mbx_moek.py:248-255); these
  * are the dispatch / combine steps around the same GEMMs when the experts are split contiguously over `world` ranks
  * (rank d owns [d * E/world, (d + 1) * E/world)). The all-to-all transfers are the caller's (NCCL). */

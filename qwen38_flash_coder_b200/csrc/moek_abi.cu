@@ -208,6 +208,118 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
   return cuda_status(moek::launch_decode(p, max_rows, sm_count(), (cudaStream_t)stream), "moe_gemm launch");
 }
 
+// ------------------------------------------------------------------------------------- whole decode layer
+// Persistent int32 state of moek_moe_layer: [epoch, done, cnt1, rcnt, ready, cnt2, tok]. The layout depends only on
+// (E, H, I), so one zeroed state buffer serves every call of that geometry.
+struct LayerLayout {
+  int64_t cnt1, rcnt, ready, cnt2, tok, total;
+};
+static LayerLayout layer_layout(int32_t E, int32_t H, int32_t I) {
+  const int64_t nbmax = std::min<int64_t>(E, moek::LAYER_MAXIDS), nt1 = 2 * (int64_t)I / 256, nt2 = H / 256;
+  LayerLayout l;
+  l.cnt1 = 2;
+  l.rcnt = l.cnt1 + nbmax * nt1 * 8;
+  l.ready = l.rcnt + nbmax * nt1;
+  l.cnt2 = l.ready + nbmax * nt1;
+  l.tok = l.cnt2 + nbmax * nt2 * 8;
+  l.total = l.tok + (int64_t)moek::LAYER_MAXIDS * nt2 * 8;
+  return l;
+}
+static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, int32_t ns1, int32_t ns2, bool rows) {
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return up(num_ids * I * 2) + (ns1 > 1 ? up((int64_t)ns1 * num_ids * 2 * I * 4) : 0) +
+         (ns2 > 1 ? up((int64_t)ns2 * num_ids * H * 4) : 0) + (rows ? up(num_ids * (int64_t)H * 4) : 0);
+}
+
+MOEK_API int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n) {
+  if (!n || num_experts <= 0 || H <= 0 || I <= 0) return fail(MOEK_ERR_ARG, "moek_b200: bad layer state query");
+  *n = layer_layout(num_experts, H, I).total;
+  return MOEK_OK;
+}
+
+MOEK_API int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t nsplit_gate,
+                                        int32_t nsplit_down, int32_t rows_out, size_t* bytes) {
+  if (!bytes || M < 0 || top_k <= 0 || H <= 0 || I <= 0 || nsplit_gate < 1 || nsplit_down < 1)
+    return fail(MOEK_ERR_ARG, "moek_b200: bad layer workspace query");
+  *bytes = (size_t)layer_ws_bytes((int64_t)M * top_k, H, I, nsplit_gate, nsplit_down, !rows_out);
+  return MOEK_OK;
+}
+
+MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
+                            const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13,
+                            const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
+                            const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
+                            int32_t nsplit_gate, int32_t nsplit_down, void* workspace, size_t workspace_bytes,
+                            int32_t* state, int64_t state_ints, int32_t* err, void* out, float* out_rows,
+                            void* stream) {
+  if (M == 0) return MOEK_OK;
+  if (M < 0 || top_k <= 0 || top_k > 32 || E <= 0 || H <= 0 || I <= 0)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer bad sizes (M %d, top_k %d, E %d, H %d, I %d)", M, top_k, E, H, I);
+  const int64_t num_ids = (int64_t)M * top_k;
+  if (num_ids > moek::LAYER_MAXIDS || M > 96)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_layer serves decode batches of <= 96 tokens and <= %d slots "
+                                      "(got M %d, top_k %d)", moek::LAYER_MAXIDS, M, top_k);
+  if (H % 256 || I % 128 || H / 128 > 32 || I / 128 > 32)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer needs H %% 256 == 0, I %% 128 == 0, H and I <= 4096 (H %d, I %d)",
+                H, I);
+  const int nst1 = H / 128, nst2 = I / 128;  // the kernel's stages: one 128-k packed-scale run pair each
+  if (nsplit_gate < 1 || nst1 % nsplit_gate || nsplit_down < 1 || nst2 % nsplit_down)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer k-splits (%d, %d) must cut H/128 = %d and I/128 = %d into whole "
+                              "runs", nsplit_gate, nsplit_down, H / 128, I / 128);
+  if (!x || !topk_ids || !topk_w || !w13 || !sp13 || !g13 || !exc_off13 || !exc_ent13 || !w2 || !sp2 || !g2 ||
+      !exc_off2 || !exc_ent2 || !state || !err || (!out && !out_rows))
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer null pointer");
+  if (out && out_rows) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer writes either out (bf16 sums) or out_rows");
+  const LayerLayout lay = layer_layout(E, H, I);
+  if (state_ints < lay.total)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer state needs %lld int32 (zeroed once)", (long long)lay.total);
+  const int64_t ws = layer_ws_bytes(num_ids, H, I, nsplit_gate, nsplit_down, out != nullptr);
+  if ((int64_t)workspace_bytes < ws || !workspace)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer needs %lld workspace bytes", (long long)ws);
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* wp = static_cast<uint8_t*>(workspace);
+  moek::LayerParams p{};
+  p.act = reinterpret_cast<__nv_bfloat16*>(wp);
+  wp += up(num_ids * I * 2);
+  if (nsplit_gate > 1) {
+    p.part1 = reinterpret_cast<float*>(wp);
+    wp += up((int64_t)nsplit_gate * num_ids * 2 * I * 4);
+  }
+  if (nsplit_down > 1) {
+    p.part2 = reinterpret_cast<float*>(wp);
+    wp += up((int64_t)nsplit_down * num_ids * H * 4);
+  }
+  if (out) p.rows = reinterpret_cast<float*>(wp);
+  const moek::LayerMat m1{static_cast<const uint8_t*>(w13), sp13, g13, exc_off13,
+                          reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1, nsplit_gate};
+  const moek::LayerMat m2{static_cast<const uint8_t*>(w2), sp2, g2, exc_off2,
+                          reinterpret_cast<const uint32_t*>(exc_ent2), H, I, H / 256, nst2, nsplit_down};
+  p.m[0] = m1;
+  p.m[1] = m2;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ids = topk_ids;
+  p.tw = topk_w;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_rows = out_rows;
+  p.ctr = state;
+  p.err = err;
+  p.timeout_ns = g_timeout_ns;
+  p.M = M;
+  p.top_k = top_k;
+  p.num_ids = (int)num_ids;
+  p.E = E;
+  p.H = H;
+  p.I = I;
+  p.off_epoch = 0;
+  p.off_done = 1;
+  p.off_cnt1 = (int)lay.cnt1;
+  p.off_rcnt = (int)lay.rcnt;
+  p.off_ready = (int)lay.ready;
+  p.off_cnt2 = (int)lay.cnt2;
+  p.off_tok = (int)lay.tok;
+  return cuda_status(moek::launch_layer(p, M, sm_count(), (cudaStream_t)stream), "moe_layer launch");
+}
+
 MOEK_API int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int32_t N, int32_t gate_up,
                                  const float* topk_w, int32_t top_k, void* out, int32_t out_kind, void* stream) {
   if (num_ids == 0) return MOEK_OK;

@@ -48,6 +48,35 @@ struct GemmParams {
   int gate_up, mode, combine_k;
 };
 
+// moek_layer.cu: the whole decode-regime layer in one persistent kernel
+constexpr int LAYER_MAXIDS = 512;  // routed slots (tokens x top_k) per call
+struct LayerMat {                  // one weight matrix in this build's layout (gate_up: N = 2I, K = H; down: N = H, K = I)
+  const uint8_t* W;
+  const uint8_t* SP;
+  const float* G;
+  const int32_t* exc_off;
+  const uint32_t* exc_ent;
+  int N, K, nt, nstage, nsplit;  // nt = N / 256 items, nstage = K / 128, nsplit = k-splits per item
+};
+struct LayerParams {
+  LayerMat m[2];  // 0 = gate_up, 1 = down
+  const __nv_bfloat16* x;  // [M, H]
+  const int32_t* ids;      // [M * top_k] expert per slot (outside [0, E): not routed)
+  const float* tw;         // [M * top_k] router weights
+  __nv_bfloat16* act;      // workspace [num_ids, I]
+  float* part1;            // workspace [nsplit_gate, num_ids, 2I] (nsplit_gate > 1)
+  float* part2;            // workspace [nsplit_down, num_ids, H] (nsplit_down > 1)
+  float* rows;             // workspace [num_ids, H]: weighted fp32 slot rows before the top-k sum
+  float* out_rows;         // caller's fp32 rows [num_ids, H] instead of the top-k sum (or null)
+  __nv_bfloat16* out;      // caller's bf16 [M, H] top-k sums (or null)
+  int* ctr;                // persistent int32 state: counters and ready stamps (zeroed once)
+  int* err;                // device error word
+  uint64_t timeout_ns;
+  int M, top_k, num_ids, E, H, I;
+  int off_cnt1, off_rcnt, off_ready, off_cnt2, off_tok, off_epoch, off_done;  // int offsets into ctr
+};
+cudaError_t launch_layer(const LayerParams& p, int max_rows, int sms, cudaStream_t st);
+
 // moek_abi.cu: record the calling thread's error message (read back by moek_last_error) and return code
 int set_error(int code, const char* fmt, ...);
 

@@ -1,0 +1,698 @@
+// The whole decode-regime routed-expert layer in one persistent kernel, sm_100a: routing, gate_up GEMM + SwiGLU,
+// down GEMM x router weight and the top-k sum, with no launch between the steps.
+//
+// The layer's data is small next to the latencies of a launch: a decode batch touches ~40 experts (about 60 MB of
+// packed weights), which one B200 streams in ~10 us, while a launch boundary costs a few microseconds of pipeline
+// drain and refill. So the steps that the reference runs as separate kernels (files/mbx_moek.py:252-289: moe_align,
+// the gate_up GEMM, SwiGLU, the down GEMM, the top-k sum) run here inside one grid of persistent CTAs (two per SM)
+// that stream the two weight matrices back to back:
+//
+//   routing   every CTA sorts the batch's (expert, slot) keys in shared memory at start-up: blocks = the distinct
+//             valid experts in ascending order, each with its slots in ascending order (moe_align's order,
+//             files/mbx_moek.cu:32-140); no global workspace and no separate launch.
+//   units     gate_up units (block, 256-row item, k-split) and then down units (block, item, k-split), dealt
+//             round-robin over the CTAs in that order: a CTA runs its gate_up units first, and the CTAs that got
+//             fewer of those start streaming down weights early.
+//   producer  warp 8: per 64-k stage, the 8 KB of packed codes (lane 0) and the 1056-byte packed-scale run pair
+//             (lane 1) by bulk copy (cp.async.bulk, no multicast) into a ring slot. It never waits on another CTA:
+//             the weights of every unit are known once the routing is.
+//   act warp  warp 9: the stage's activation rows. gate_up: the tokens' hidden rows by bulk copy; down: the act rows
+//             of the block, once the gate_up item that produced those act columns is complete in every CTA (a
+//             per-(block, item) ready stamp, acquire-loaded with a bounded wait), by plain loads into the slot.
+//   scales    warp 10: per stage the scale byte of each row x k-group (base + 4-bit offset, then the exceptions),
+//             per unit the (B | R) table of the expert (moek_common.cuh), as in moek_decode.cu.
+//   consumers warps 0-7: the swap-AB mma.sync m16n8k16 of moek_decode.cu (weights = the 16-row A operand, up to 8
+//             tokens = B), fp32 accumulators per unit.
+//   finishing gate_up: with one k-split the lane holds gate and up of the same column and writes
+//             act = bf16(silu(gate) * up); with more, fp32 partials go to the workspace and the warp whose arrival
+//             completes (block, item, warp) adds them in split order. Each warp's completion counts towards the
+//             (block, item) ready stamp. down: partials likewise, then the router weight: fp32 row w * sum; the
+//             arrival that completes a token's valid slots for (item, warp) adds the token's rows in slot order and
+//             rounds once to bf16 (the fp32 oracle's order, bench/moek/problem.py:51-67).
+//
+// Counters reset themselves (the completing arrival zeroes its counter); ready stamps carry a launch epoch, so the
+// workspace is zeroed once at allocation and never between launches. Every wait is bounded (%globaltimer); a CTA
+// whose wait expires records MOEK_DEV_TIMEOUT and winds down; the workspace must then be zeroed again.
+//
+// Co-residency: a down unit may wait on a gate_up unit of any CTA, and every CTA runs all of its gate_up units
+// before any down unit, so the grid makes progress whenever all its CTAs are resident at once: the launcher sizes
+// the grid to the occupancy the kernel reaches (cudaOccupancyMaxActiveBlocksPerMultiprocessor x SMs).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "moek_common.cuh"
+#include "moek_kernels.cuh"
+
+namespace moek {
+namespace dl {
+
+constexpr int NCW = 8;  // consumer warps
+constexpr int W_PROD = NCW, W_ACT = NCW + 1, W_SCALE = NCW + 2;
+constexpr int THREADS = (NCW + 3) * 32;
+constexpr int LBK = 2 * BK;                  // k per pipeline stage: one packed-scale run pair
+constexpr int LSTAGE = 2 * STAGE_BYTES;      // 16 KB of packed codes per (item, stage): one bulk copy
+constexpr int X_STRIDE = LBK * 2 + 16;       // bytes per activation row in a slot (+16: conflict-free reads)
+constexpr int SC_STRIDE = 288;               // bytes per k-group row of a slot's scale-byte table
+constexpr int SC_BYTES = KG * SC_STRIDE;     // the stage's 8 k-groups
+constexpr int NLUT = 8;         // per-unit (B | R) tables in flight (the scale warp runs at most 4 units ahead)
+constexpr int MAXU = 32;        // units per metadata round
+constexpr int MAXRUN = 32;      // packed-scale runs per unit
+constexpr int EXC_POOL = 1024;  // exception entries cached per round
+
+struct UnitMeta {
+  int ph, blk, item, ks, e, nv, flags;  // ph: 0 = gate_up, 1 = down; flags: 2 = block has more rows than XR
+  float g;
+  int from_global, exc_g0, exc_s0;
+  int run_off[MAXRUN + 1];
+};
+
+template <int XR>
+struct Cfg {
+  static constexpr int X_OFF = LSTAGE + PAIR_BYTES;
+  static constexpr int SC_OFF = X_OFF + XR * X_STRIDE;
+  static constexpr int SLOT = SC_OFF + SC_BYTES;
+  static constexpr int NS = XR <= 8 ? 4 : XR <= 16 ? 3 : XR <= 32 ? 2 : 3;  // two CTAs per SM up to XR = 32
+  static constexpr int META_OFF = NS * SLOT;
+  static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
+  static constexpr int POOL_OFF = IDS_OFF + MAXU * XR * 4;
+  static constexpr int LUT_OFF = POOL_OFF + EXC_POOL * 4;
+  static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 4;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
+  static constexpr int MISC_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;
+  static constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
+  static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
+  static constexpr int T = XR / 8;
+  static constexpr int MINB = XR <= 32 ? 2 : 1;
+  static_assert(2 * LAYER_MAXIDS * 4 <= SLOT, "routing scratch fits in ring slot 0");
+};
+
+__device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err,
+                                              volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (mbar_wait(bar, parity, deadline, err)) return true;
+  *abort_flag = 1;
+  return false;
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
+
+// Bounded wait (every lane) until the stamp reads `want`; the acquire orders the lane's later loads after it.
+__device__ __forceinline__ bool wait_stamp(const int* stamp, int want, uint64_t deadline, int* err,
+                                           volatile int* abort_flag) {
+  for (uint32_t i = 0;; i++) {
+    if (*abort_flag) return false;
+    if (ld_acquire(stamp) == want) return true;
+    if ((i & 63) == 63 && globaltimer() > deadline) {
+      report(err, MOEK_DEV_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void decode_unit(const LayerParams& p, int64_t u, int64_t U1, int& ph, int& blk, int& item,
+                                            int& ks) {
+  ph = u >= U1 ? 1 : 0;
+  const LayerMat& m = p.m[ph];
+  const int64_t v = ph ? u - U1 : u;
+  const int per = m.nt * m.nsplit;
+  blk = (int)(v / per);
+  const int rem = (int)(v - (int64_t)blk * per);
+  item = rem / m.nsplit;
+  ks = rem - item * m.nsplit;
+}
+
+template <int XR>
+__global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(LayerParams p) {
+  using C = Cfg<XR>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);
+  int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);
+  uint32_t* pool = reinterpret_cast<uint32_t*>(smem + C::POOL_OFF);
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::LUT_OFF);
+  int* srow = reinterpret_cast<int*>(smem + C::ROUTE_OFF);
+  int* bexp = srow + LAYER_MAXIDS;
+  int* bstart = bexp + LAYER_MAXIDS;
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);  // [0] blocks, [1] valid slots, [2] abort
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* empty = full + C::NS;
+  uint64_t* scaled = empty + C::NS;
+  uint64_t* mfull = scaled + C::NS;
+  uint64_t* mempty = mfull + 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  volatile int* abort_flag = misc + 2;
+
+  if (tid == 0) {
+    misc[1] = 0;
+    misc[2] = 0;
+    for (int i = 0; i < C::NS; i++) {
+      mbar_init(full + i, 2);  // the producer's and the act warp's arrivals (each with its byte count)
+      mbar_init(empty + i, NCW);
+      mbar_init(scaled + i, 32);
+    }
+    mbar_init(mfull, 32);
+    mbar_init(mempty, NCW + 2);  // consumers, scale warp, act warp
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  pdl_wait();  // x, routing and weights of the previous kernels; the workspace of the previous launch
+  pdl_launch_dependents();
+  const uint64_t deadline = globaltimer() + p.timeout_ns;
+  const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
+  const int n = p.num_ids, k = p.top_k;
+
+  // ------------------------------------------------------------------------------------------------- routing
+  {
+    uint32_t* key = reinterpret_cast<uint32_t*>(smem);  // scratch in ring slot 0: nothing is copied there yet
+    uint32_t* skey = key + LAYER_MAXIDS;
+    for (int i = tid; i < n; i += THREADS) {
+      const int e = p.ids[i];
+      const bool v = e >= 0 && e < p.E;
+      key[i] = v ? ((uint32_t)e << 9) | (uint32_t)i : 0xFFFFFFFFu;
+      if (v) atomicAdd(const_cast<int*>(misc + 1), 1);
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += THREADS) {  // rank of each valid key among all keys (they are distinct)
+      const uint32_t ki = key[i];
+      if (ki == 0xFFFFFFFFu) continue;
+      int r = 0;
+      for (int j = 0; j < n; j++) r += key[j] < ki;
+      skey[r] = ki;
+    }
+    __syncthreads();
+    const int nvalid = misc[1];
+    if (warp == 0) {  // blocks: a block starts where the expert changes
+      int base = 0;
+      for (int p0 = 0; p0 < nvalid; p0 += 32) {
+        const int pos = p0 + lane;
+        uint32_t kv = 0;
+        bool head = false;
+        if (pos < nvalid) {
+          kv = skey[pos];
+          head = pos == 0 || (skey[pos - 1] >> 9) != (kv >> 9);
+          srow[pos] = (int)(kv & 511u);
+        }
+        const uint32_t hb = __ballot_sync(0xffffffffu, head);
+        if (head) {
+          const int bi = base + __popc(hb & ((1u << lane) - 1u));
+          bstart[bi] = pos;
+          bexp[bi] = (int)(kv >> 9);
+        }
+        base += __popc(hb);
+      }
+      if (lane == 0) {
+        bstart[base] = nvalid;
+        misc[0] = base;
+      }
+    }
+    __syncthreads();
+  }
+  const int nblk = misc[0];
+
+  // tokens with no valid slot get a zero output row (nothing else writes them)
+  if (blockIdx.x == 0 && p.out && warp < NCW) {
+    for (int t = warp; t < p.M; t += NCW) {
+      const int e = lane < k ? p.ids[t * k + lane] : -1;
+      if (__any_sync(0xffffffffu, e >= 0 && e < p.E)) continue;
+      for (int c = lane; c < p.H; c += 32) p.out[(int64_t)t * p.H + c] = __float2bfloat16_rn(0.f);
+    }
+  }
+
+  const int64_t U1 = (int64_t)nblk * p.m[0].nt * p.m[0].nsplit;
+  const int64_t U = U1 + (int64_t)nblk * p.m[1].nt * p.m[1].nsplit;
+  const int n_mine = U > blockIdx.x ? (int)((U - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  const int rounds = (n_mine + MAXU - 1) / MAXU;
+
+  if (warp == W_PROD) {  // ------------------------------------------------------------------------- producer
+    uint32_t g = 0;
+    bool ok = true;
+    for (int r = 0; r < rounds && ok; r++) {
+      const int u0 = r * MAXU, nu = min(MAXU, n_mine - u0);
+      if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, abort_flag)) break;
+      for (int i = lane; i < nu; i += 32) {
+        UnitMeta& m = meta[i];
+        decode_unit(p, blockIdx.x + (int64_t)(u0 + i) * gridDim.x, U1, m.ph, m.blk, m.item, m.ks);
+        m.e = bexp[m.blk];
+        const int b0 = bstart[m.blk], cnt = bstart[m.blk + 1] - b0;
+        m.nv = min(cnt, XR);
+        m.flags = cnt > XR ? 2 : 0;
+        for (int rr = 0; rr < m.nv; rr++) mids[i * XR + rr] = srow[b0 + rr];
+      }
+      __syncwarp();
+      mbar_arrive(mfull);  // units, experts and rows published
+      for (int ci = 0; ci < nu && ok; ci++) {
+        const LayerMat& mt = p.m[meta[ci].ph];
+        const int e = meta[ci].e, item = meta[ci].item, ks = meta[ci].ks;
+        const int su = mt.nstage / mt.nsplit;
+        for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
+          const int slot = g % C::NS;
+          if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + slot * C::SLOT;
+          if (lane == 0) mbar_expect_tx(full + slot, LSTAGE + PAIR_BYTES);
+          __syncwarp();
+          if (lane == 0) {  // the two consecutive 64-k blocks of the stage
+            const int64_t wi = (((int64_t)e * mt.nt + item) * mt.nstage + st) * 2;
+            bulk_g2s(dst, mt.W + wi * STAGE_BYTES, LSTAGE, full + slot);
+          } else if (lane == 1) {
+            const int64_t si = ((int64_t)e * mt.nt + item) * mt.nstage + st;
+            bulk_g2s(dst + LSTAGE, mt.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
+          }
+          __syncwarp();
+        }
+      }
+    }
+  } else if (warp == W_ACT) {  // ----------------------------------------------------------------------- act warp
+    uint32_t g = 0;
+    bool ok = true;
+    for (int r = 0; r < rounds && ok; r++) {
+      const int nu = min(MAXU, n_mine - r * MAXU);
+      if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
+      for (int ci = 0; ci < nu && ok; ci++) {
+        const UnitMeta& m = meta[ci];
+        const LayerMat& mt = p.m[m.ph];
+        const int su = mt.nstage / mt.nsplit, nv = m.nv;
+        const int* ids = mids + ci * XR;
+        int ready_item = -1;
+        for (int st = m.ks * su; st < (m.ks + 1) * su; st++, g++) {
+          const int slot = g % C::NS;
+          if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* xs = smem + slot * C::SLOT + C::X_OFF;
+          if (m.ph == 0) {  // hidden rows of the block's tokens, 64 k each, by bulk copy
+            if (lane == 0) mbar_expect_tx(full + slot, nv * LBK * 2);
+            __syncwarp();
+            for (int rr = lane; rr < nv; rr += 32)
+              bulk_g2s(xs + rr * X_STRIDE, p.x + (int64_t)(ids[rr] / k) * p.H + st * LBK, LBK * 2, full + slot);
+          } else {  // act rows: columns [128 st, 128 st + 128) are gate_up item st's (ITEM_COLS / 2 act columns)
+            const int need = st;
+            if (need != ready_item) {
+              if (!wait_stamp(p.ctr + p.off_ready + m.blk * p.m[0].nt + need, epoch + 1, deadline, p.err,
+                              abort_flag)) {
+                ok = false;
+              }
+              ok = __all_sync(0xffffffffu, ok);
+              if (!ok) break;
+              ready_item = need;
+            }
+            for (int idx = lane; idx < nv * 16; idx += 32) {
+              const int rr = idx >> 4, c = idx & 15;
+              const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.act + (int64_t)ids[rr] * p.I + st * LBK) + c);
+              *reinterpret_cast<uint4*>(xs + rr * X_STRIDE + c * 16) = v;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full + slot);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mempty);
+    }
+  } else if (warp == W_SCALE) {  // -------------------------------------------------------------------- scale warp
+    uint32_t g = 0, kq = 0;
+    const int run = lane >> 4, ch = lane & 15;
+    int dst[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) dst[i] = run * 128 + position_slot(8 * ch + i);
+    bool ok = true;
+    for (int r = 0; r < rounds && ok; r++) {
+      const int nu = min(MAXU, n_mine - r * MAXU);
+      if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
+      for (int i = lane; i < nu; i += 32) {
+        UnitMeta& m = meta[i];
+        const LayerMat& mt = p.m[m.ph];
+        const int nb = mt.nstage, nruns = nb / mt.nsplit;
+        const bool valid = m.e >= 0 && m.e < p.E;
+        m.g = valid ? mt.G[m.e] : 0.f;
+        const int64_t key0 = ((int64_t)(valid ? m.e : 0) * mt.nt + m.item) * nb + (int64_t)m.ks * nruns;
+        const int o0 = valid ? mt.exc_off[key0] : 0;
+        m.exc_g0 = o0;
+        for (int j = 0; j <= nruns; j++) m.run_off[j] = valid ? mt.exc_off[key0 + j] - o0 : 0;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        int used = 0;
+        for (int i = 0; i < nu; i++) {
+          const LayerMat& mt = p.m[meta[i].ph];
+          const int nruns = mt.nstage / mt.nsplit;
+          const int cnt = meta[i].run_off[nruns];
+          meta[i].from_global = used + cnt > EXC_POOL;
+          if (!meta[i].from_global) {
+            meta[i].exc_s0 = used;
+            used += cnt;
+          }
+        }
+      }
+      __syncwarp();
+      for (int i = lane; i < nu; i += 32) {
+        if (meta[i].from_global) continue;
+        const LayerMat& mt = p.m[meta[i].ph];
+        const int nruns = mt.nstage / mt.nsplit;
+        const int cnt = meta[i].run_off[nruns], s0 = meta[i].exc_s0, g0 = meta[i].exc_g0;
+        for (int j = 0; j < cnt; j++) pool[s0 + j] = mt.exc_ent[g0 + j];
+      }
+      __syncwarp();
+      for (int ui = 0; ui < nu && ok; ui++) {
+        const UnitMeta& m = meta[ui];
+        const LayerMat& mt = p.m[m.ph];
+        const int su = mt.nstage / mt.nsplit;
+        uint32_t* lt = lut + (kq % NLUT) * 256;
+#pragma unroll
+        for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, m.g);
+        kq++;
+        const uint32_t* exc = m.from_global ? mt.exc_ent + m.exc_g0 : pool + m.exc_s0;
+        const int r0g = m.ph == 0 ? m.item : 2 * m.item;  // global run index of the pair's first run
+        for (int st = m.ks * su; st < (m.ks + 1) * su; st++, g++) {
+          const int slot = g % C::NS;
+          if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint8_t* runp = smem + slot * C::SLOT + LSTAGE + run * RUN_BYTES;
+          uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF;
+          const uint32_t b4 = runp[ch] * 0x01010101u;
+#pragma unroll
+          for (int kk = 0; kk < KG; kk++) {
+            const int kg = kk;
+            const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kg * 64 + ch * 4);
+            const uint32_t lo = (q & 0x0F0F0F0Fu) + b4;
+            const uint32_t hi = ((q >> 4) & 0x0F0F0F0Fu) + b4;
+            uint8_t* row = sc + kk * SC_STRIDE;
+#pragma unroll
+            for (int i = 0; i < 8; i++) row[dst[i]] = (uint8_t)(((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF);
+          }
+          __syncwarp();
+          const int rr = st - m.ks * su;  // the unit's run (pair) of this stage
+          const int eo0 = m.run_off[rr], eo1 = m.run_off[rr + 1];
+          for (int j = eo0 + lane; j < eo1; j += 32) {
+            const uint32_t en = exc[j];
+            const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+            const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
+            sc[kg * SC_STRIDE + slot_e] = (uint8_t)(en >> 24);
+          }
+          __syncwarp();
+          mbar_arrive(scaled + slot);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mempty);
+    }
+  } else {  // ------------------------------------------------------------------------------------------ consumers
+    const int gq = lane >> 2, c = lane & 3;
+    const int w_off = ((((c >> 1) ^ (gq >> 2)) & 1) << 4) | ((c & 1) << 3);  // k-group c's bytes in a 32-byte row
+    const int I = p.I, H = p.H;
+    uint32_t g = 0, kq = 0;
+    for (int r = 0; r < rounds; r++) {
+      const int nu = min(MAXU, n_mine - r * MAXU);
+      wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag);
+      consumer_sync();
+      const bool have_meta = !*abort_flag;
+      for (int ui = 0; ui < nu && have_meta; ui++) {
+        const UnitMeta& m = meta[ui];
+        const LayerMat& mt = p.m[m.ph];
+        const int ph = m.ph, item = m.item, ks = m.ks, nv = m.nv, blk = m.blk;
+        const int su = mt.nstage / mt.nsplit;
+        const int* ids = mids + ui * XR;
+        if ((m.flags & 2) && tid == 0) report(p.err, MOEK_DEV_TOO_MANY_ROWS);
+        // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
+        const int G0 = ph == 0 ? warp : 2 * warp, G1 = ph == 0 ? warp + 8 : 2 * warp + 1;
+        const int slot00 = 16 * G0 + gq, slot10 = 16 * G1 + gq;
+        const uint32_t* lt = lut + (kq % NLUT) * 256;
+        kq++;
+        const int ntile = (nv + 7) >> 3;
+        float acc[2][C::T][4];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+          for (int t = 0; t < C::T; t++)
+#pragma unroll
+            for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
+        bool ok = true;
+        for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
+          const int slot = g % C::NS;
+          const uint32_t par = (g / C::NS) & 1;
+          if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag) ||
+              !wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
+            ok = false;
+            continue;  // stay in step with the other roles' counters
+          }
+#pragma unroll 1
+          for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
+          const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
+          const uint8_t* sx = smem + slot * C::SLOT + C::X_OFF + hf * BK * 2;
+          const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + (4 * hf + c) * SC_STRIDE;
+          const uint32_t s0a = lt[sc[slot00]], s0b = lt[sc[slot00 + 8]], s1a = lt[sc[slot10]],
+                         s1b = lt[sc[slot10 + 8]];
+#pragma unroll
+          for (int i = 0; i < 2; i++) {
+            const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;
+            const ScaleBR sa{prmt_b(wa, 0x1010), prmt_b(wa, 0x3232)}, sbv{prmt_b(wb, 0x1010), prmt_b(wb, 0x3232)};
+            const uint8_t* wr = sw + (16 * (i ? G1 : G0) + gq) * 32 + w_off;
+            const uint2 qa = *reinterpret_cast<const uint2*>(wr), qb = *reinterpret_cast<const uint2*>(wr + 8 * 32);
+            uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
+            dequant_word(qa.x, sa, wa0);
+            dequant_word(qb.x, sbv, wb0);
+            dequant_word(qa.y, sa, wa1);
+            dequant_word(qb.y, sbv, wb1);
+            const uint32_t A0[4] = {wa0[0], wb0[0], wa0[1], wb0[1]};
+            const uint32_t A1[4] = {wa0[2], wb0[2], wa0[3], wb0[3]};
+            const uint32_t A2[4] = {wa1[0], wb1[0], wa1[1], wb1[1]};
+            const uint32_t A3[4] = {wa1[2], wb1[2], wa1[3], wb1[3]};
+#pragma unroll
+            for (int t = 0; t < C::T; t++) {
+              if (t < ntile) {
+                const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
+                const uint4 x0 = *reinterpret_cast<const uint4*>(xr);
+                const uint4 x1 = *reinterpret_cast<const uint4*>(xr + 16);
+                mma_16816(acc[i][t], A0, x0.x, x0.y);
+                mma_16816(acc[i][t], A1, x0.z, x0.w);
+                mma_16816(acc[i][t], A2, x1.x, x1.y);
+                mma_16816(acc[i][t], A3, x1.z, x1.w);
+              }
+            }
+          }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty + slot);
+        }
+        ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+        if (!ok) continue;
+
+        // ------------------------------------------------------------------------------------------ finishing
+        // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
+        const int N = mt.N;
+        if (ph == 0) {
+          const int nt1 = mt.nt;
+          bool complete = mt.nsplit == 1;
+          if (complete) {  // gate row and up row + 128 share the column: act straight from the accumulators
+#pragma unroll
+            for (int t = 0; t < C::T; t++) {
+              if (t >= ntile) break;
+#pragma unroll
+              for (int v = 0; v < 2; v++) {
+                const int row = t * 8 + 2 * c + v;
+                if (row >= nv) continue;
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+                  p.act[(int64_t)ids[row] * I + 128 * item + slot00 + 8 * h] =
+                      __float2bfloat16_rn(silu(acc[0][t][2 * h + v]) * acc[1][t][2 * h + v]);
+              }
+            }
+          } else {
+            float* base = p.part1 + (int64_t)ks * n * N;
+#pragma unroll
+            for (int t = 0; t < C::T; t++) {
+              if (t >= ntile) break;
+#pragma unroll
+              for (int v = 0; v < 2; v++) {
+                const int row = t * 8 + 2 * c + v;
+                if (row >= nv) continue;
+                float* prow = base + (int64_t)ids[row] * N;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                  prow[128 * item + slot00 + 8 * h] = acc[0][t][2 * h + v];
+                  prow[I + 128 * item + slot00 + 8 * h] = acc[1][t][2 * h + v];
+                }
+              }
+            }
+            __threadfence();
+            __syncwarp();
+            int old = 0;
+            int* cn = p.ctr + p.off_cnt1 + ((int64_t)blk * nt1 + item) * NCW + warp;
+            if (lane == 0) old = atomicAdd(cn, 1);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            complete = old == mt.nsplit - 1;
+            if (complete) {  // every split of (block, item, warp) is in: add them in split order
+              if (lane == 0) *cn = 0;
+              __threadfence();
+              for (int idx = lane; idx < nv * 16; idx += 32) {
+                const int row = idx >> 4, col = 128 * item + 16 * warp + (idx & 15);
+                const float* pr = p.part1 + (int64_t)ids[row] * N;
+                float gs = 0.f, us = 0.f;
+                for (int s2 = 0; s2 < mt.nsplit; s2++) {
+                  gs += __ldcg(pr + (int64_t)s2 * n * N + col);
+                  us += __ldcg(pr + (int64_t)s2 * n * N + I + col);
+                }
+                p.act[(int64_t)ids[row] * I + col] = __float2bfloat16_rn(silu(gs) * us);
+              }
+            }
+          }
+          if (complete) {  // this warp's act columns of (block, item) are written: count towards the ready stamp
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+              int* rc = p.ctr + p.off_rcnt + (int64_t)blk * nt1 + item;
+              if (atomicAdd(rc, 1) == NCW - 1) {
+                *rc = 0;
+                __threadfence();
+                st_release(p.ctr + p.off_ready + (int64_t)blk * nt1 + item, epoch + 1);
+              }
+            }
+          }
+          continue;
+        }
+        // down: weighted fp32 rows of (block, item), then the token sums
+        const int nt2 = mt.nt;
+        float* rows = p.out_rows ? p.out_rows : p.rows;
+        bool complete = mt.nsplit == 1;
+        if (complete) {
+#pragma unroll
+          for (int t = 0; t < C::T; t++) {
+            if (t >= ntile) break;
+#pragma unroll
+            for (int v = 0; v < 2; v++) {
+              const int row = t * 8 + 2 * c + v;
+              if (row >= nv) continue;
+              const int id = ids[row];
+              const float w = p.tw[id];
+#pragma unroll
+              for (int h = 0; h < 2; h++) {
+                rows[(int64_t)id * H + 256 * item + slot00 + 8 * h] = w * acc[0][t][2 * h + v];
+                rows[(int64_t)id * H + 256 * item + slot10 + 8 * h] = w * acc[1][t][2 * h + v];
+              }
+            }
+          }
+        } else {
+          float* base = p.part2 + (int64_t)ks * n * N;
+#pragma unroll
+          for (int t = 0; t < C::T; t++) {
+            if (t >= ntile) break;
+#pragma unroll
+            for (int v = 0; v < 2; v++) {
+              const int row = t * 8 + 2 * c + v;
+              if (row >= nv) continue;
+              float* prow = base + (int64_t)ids[row] * N + 256 * item;
+#pragma unroll
+              for (int h = 0; h < 2; h++) {
+                prow[slot00 + 8 * h] = acc[0][t][2 * h + v];
+                prow[slot10 + 8 * h] = acc[1][t][2 * h + v];
+              }
+            }
+          }
+          __threadfence();
+          __syncwarp();
+          int old = 0;
+          int* cn = p.ctr + p.off_cnt2 + ((int64_t)blk * nt2 + item) * NCW + warp;
+          if (lane == 0) old = atomicAdd(cn, 1);
+          old = __shfl_sync(0xffffffffu, old, 0);
+          complete = old == mt.nsplit - 1;
+          if (complete) {
+            if (lane == 0) *cn = 0;
+            __threadfence();
+            const int col = 256 * item + 32 * warp + lane;  // the warp's 32 output columns: one per lane
+            for (int row = 0; row < nv; row++) {
+              const int id = ids[row];
+              const float* pr = p.part2 + (int64_t)id * N + col;
+              float s = 0.f;
+              for (int s2 = 0; s2 < mt.nsplit; s2++) s += __ldcg(pr + (int64_t)s2 * n * N);
+              rows[(int64_t)id * H + col] = p.tw[id] * s;
+            }
+          }
+        }
+        if (!complete || p.out_rows) continue;
+        __threadfence();
+        __syncwarp();
+        // each row's token: the arrival that completes the token's valid slots for (item, warp) adds them in order
+        const int col = 256 * item + 32 * warp + lane;
+        for (int row = 0; row < nv; row++) {
+          const int tk = ids[row] / k;
+          const int ej = lane < k ? p.ids[tk * k + lane] : -1;
+          const int nslots = __popc(__ballot_sync(0xffffffffu, ej >= 0 && ej < p.E));
+          int o2 = 0;
+          int* tc = p.ctr + p.off_tok + ((int64_t)tk * nt2 + item) * NCW + warp;
+          if (lane == 0) o2 = atomicAdd(tc, 1);
+          o2 = __shfl_sync(0xffffffffu, o2, 0);
+          if (o2 != nslots - 1) continue;
+          if (lane == 0) *tc = 0;
+          __threadfence();
+          float o = 0.f;
+          for (int sl = 0; sl < k; sl++) {
+            const int ejs = p.ids[tk * k + sl];
+            if (ejs < 0 || ejs >= p.E) continue;
+            o += __ldcg(rows + (int64_t)(tk * k + sl) * H + col);
+          }
+          p.out[(int64_t)tk * H + col] = __float2bfloat16_rn(o);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mempty);
+    }
+  }
+
+  // ------------------------------------------------------------------------------------------------ teardown
+  __syncthreads();
+  if (tid == 0) {  // the last CTA to finish advances the launch epoch of the ready stamps
+    __threadfence();
+    if (atomicAdd(p.ctr + p.off_done, 1) == (int)gridDim.x - 1) {
+      p.ctr[p.off_done] = 0;
+      __threadfence();
+      atomicAdd(p.ctr + p.off_epoch, 1);
+    }
+  }
+}
+
+template <int XR>
+static cudaError_t launch_xr(const LayerParams& p, int sms, cudaStream_t st) {
+  using C = Cfg<XR>;
+  cudaError_t e = cudaFuncSetAttribute(moek_layer_kernel<XR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  int occ = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moek_layer_kernel<XR>, THREADS, C::SMEM);
+  if (e != cudaSuccess) return e;
+  if (occ < 1) return cudaErrorLaunchOutOfResources;
+  const int grid = std::min(occ, C::MINB) * sms;  // every CTA resident at once (down units wait on gate_up units)
+  e = launch_pdl(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace dl
+
+cudaError_t launch_layer(const LayerParams& p, int max_rows, int sms, cudaStream_t st) {
+  if (max_rows <= 8) return dl::launch_xr<8>(p, sms, st);
+  if (max_rows <= 16) return dl::launch_xr<16>(p, sms, st);
+  if (max_rows <= 32) return dl::launch_xr<32>(p, sms, st);
+  return dl::launch_xr<96>(p, sms, st);
+}
+
+}  // namespace moek

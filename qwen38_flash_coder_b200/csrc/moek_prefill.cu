@@ -11,8 +11,9 @@
 // the packed codes, the packed scales and the activation tiles.
 //
 //   unit      = (moe_align block of <= 128 rows, 256-row item); units dealt round-robin to one persistent CTA per SM.
-//   producer  = warp 0: per 64-k stage, bulk-copies (cp.async.bulk, no multicast) the 8 KB of packed codes and the
-//               1056-byte packed-scale run pair into a ring slot (mbarrier complete_tx).
+//   producer  = warp 0: per 64-k stage, bulk-copies (cp.async.bulk, no multicast) the 8 KB of packed codes (lane 0)
+//               and the 1056-byte packed-scale run pair (lane 1, same instruction) into a ring slot (mbarrier
+//               complete_tx).
 //   MMA       = warps 1-4 (one lane each): per stage 2 halves x 4 k16 steps of tcgen05.mma.cta_group::1.kind::f16
 //               (bf16 x bf16 -> fp32), A from a TMEM ring slot, B from a shared-memory K-major SWIZZLE_128B tile, D in
 //               TMEM. Warp 1 + 2h + p issues the MMAs of accumulator (half h, k16 parity p) (with two accumulators,
@@ -30,11 +31,12 @@
 //   scales    = warp 7: per unit the (B | R) table of the expert's scale bytes (moek_common.cuh) and the unit's
 //               exception lists; per stage the scale byte of each of the 256 rows x 4 k-groups (base + 4-bit offset,
 //               then the exceptions), one 32-bit word per row.
-//   dequant   = warps 8-15: warp 8 + 4h + i owns rows 128h + 32q .. +31 of the item, q = warp % 4 (its TMEM lane
-//               quarter);
-//               per stage a thread reads its row's 32 bytes of codes and its scale word, and stores 32 columns of
-//               bf16 pairs into the A slot.
-//   epilogue  = warps 16-19 (lane quarter = warp % 4): tcgen05.ld 16 columns at a time; gate_up writes
+//   dequant   = warps 8-23, two groups of eight taking alternate stages (a stage's dequant is a chain of shared-
+//               memory loads, table lookups, bf16 FMAs and a tcgen05.st + wait, so two stages in flight hide half
+//               of its latency): warp 8 + 8s + 4h + i owns rows 128h + 32q .. +31 of the item, q = warp % 4 (its TMEM
+//               lane quarter); per stage a thread reads its row's 32 bytes of codes and its scale word, and stores
+//               32 columns of bf16 pairs into the A slot.
+//   epilogue  = warps 24-27 (lane quarter = warp % 4): tcgen05.ld 8 columns at a time; gate_up writes
 //               act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves 0 and 1), down writes
 //               the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
 //   mode 1    = gate_up writes act at the row's position in moe_align's sorted order instead of its id, so that the
@@ -60,7 +62,7 @@ constexpr int BMP = 128;  // rows per moe_align block (the MMA's N, at most)
 constexpr int NW = 4;     // shared-memory ring of packed codes + packed scales + scale words
 constexpr int NB = 4;     // shared-memory ring of activation tiles
 constexpr int NA = 3;     // TMEM ring of dequantised weight tiles
-constexpr int NDQ = 8;    // dequant warps
+constexpr int NDQ = 16;   // dequant warps: two groups of 8 taking alternate stages
 constexpr int NEPI = 4;   // epilogue warps
 constexpr int NMMA = 4;   // MMA-issuing warps: one per accumulator (half h, k16-step parity p) = warp W_MMA + 2h + p
 constexpr int NLOAD = 2;  // activation-gather warps (a TMA issue is latency-bound per thread: two warps, twice the rate)
@@ -156,40 +158,39 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-// 16-column loads (32 lanes x 16 columns each) issued together, then one wait.
-#define MOEK_LD16(T, X)                                                                                              \
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];" \
-               : "=r"(X[0]), "=r"(X[1]), "=r"(X[2]), "=r"(X[3]), "=r"(X[4]), "=r"(X[5]), "=r"(X[6]), "=r"(X[7]),       \
-                 "=r"(X[8]), "=r"(X[9]), "=r"(X[10]), "=r"(X[11]), "=r"(X[12]), "=r"(X[13]), "=r"(X[14]), "=r"(X[15])  \
+// 8-column loads (32 lanes x 8 columns each) issued together, then one wait.
+#define MOEK_LD8(T, X)                                                                                   \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"                  \
+               : "=r"(X[0]), "=r"(X[1]), "=r"(X[2]), "=r"(X[3]), "=r"(X[4]), "=r"(X[5]), "=r"(X[6]), "=r"(X[7]) \
                : "r"(T))
-__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
-  uint32_t r[16], q[16];
-  MOEK_LD16(ta, r);
-  MOEK_LD16(tb, q);
+__device__ __forceinline__ void tmem_ld8x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  uint32_t r[8], q[8];
+  MOEK_LD8(ta, r);
+  MOEK_LD8(tb, q);
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; i++) {
+  for (int i = 0; i < 8; i++) {
     va[i] = __uint_as_float(r[i]);
     vb[i] = __uint_as_float(q[i]);
   }
 }
-__device__ __forceinline__ void tmem_ld16x4(uint32_t ta, uint32_t tb, uint32_t tc, uint32_t td, float* va, float* vb,
-                                            float* vc, float* vd) {
-  uint32_t r[16], q[16], x[16], y[16];
-  MOEK_LD16(ta, r);
-  MOEK_LD16(tb, q);
-  MOEK_LD16(tc, x);
-  MOEK_LD16(td, y);
+__device__ __forceinline__ void tmem_ld8x4(uint32_t ta, uint32_t tb, uint32_t tc, uint32_t td, float* va, float* vb,
+                                           float* vc, float* vd) {
+  uint32_t r[8], q[8], x[8], y[8];
+  MOEK_LD8(ta, r);
+  MOEK_LD8(tb, q);
+  MOEK_LD8(tc, x);
+  MOEK_LD8(td, y);
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; i++) {
+  for (int i = 0; i < 8; i++) {
     va[i] = __uint_as_float(r[i]);
     vb[i] = __uint_as_float(q[i]);
     vc[i] = __uint_as_float(x[i]);
     vd[i] = __uint_as_float(y[i]);
   }
 }
-#undef MOEK_LD16
+#undef MOEK_LD8
 // SiLU with the hardware exponent and the approximate divide (a few fp32 ulps; the product is rounded to bf16 next).
 // x -> -inf gives x * 0 = -0, the limit.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     *abort_flag = 0;
     for (int i = 0; i < NW; i++) {
       mbar_init(B.wfull + i, 1);
-      mbar_init(B.wempty + i, NDQ);
+      mbar_init(B.wempty + i, NDQ / 2);
       mbar_init(B.sfull + i, 1);
     }
     for (int i = 0; i < NB; i++) {
@@ -260,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(B.bempty + i, NMMA);  // every MMA warp commits
     }
     for (int i = 0; i < NA; i++) {
-      mbar_init(B.afull + i, NDQ);
+      mbar_init(B.afull + i, NDQ / 2);
       mbar_init(B.aempty + i, NMMA);
     }
     mbar_init(B.accfull, NMMA);
@@ -287,17 +288,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == W_PROD) {  // ---------------------------------------------------------------------- producer
     uint32_t g = 0;
-    for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < nunits && ok && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
       if (ui.e < 0 || ui.e >= p.E) continue;
       for (int st = 0; st < nstage; st++, g++) {
         const int s = g % NW;
-        if (g >= NW && !wait_warp(B.wempty + s, ((g / NW) - 1) & 1, deadline, p.err, abort_flag)) break;
+        if (g >= NW && !wait_warp(B.wempty + s, ((g / NW) - 1) & 1, deadline, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = smem + W_OFF + s * W_SLOT;
+        if (lane == 0) mbar_expect_tx(B.wfull + s, STAGE_BYTES + PAIR_BYTES);
+        __syncwarp();
+        // the codes from lane 0 and the scale pair from lane 1, in one instruction
         if (lane == 0) {
-          uint8_t* dst = smem + W_OFF + s * W_SLOT;
-          mbar_expect_tx(B.wfull + s, STAGE_BYTES + PAIR_BYTES);
           const int64_t wi = ((int64_t)ui.e * nt + ui.item) * nstage + st;
           bulk_g2s(dst, p.W + wi * STAGE_BYTES, STAGE_BYTES, B.wfull + s);
+        } else if (lane == 1) {
           const int64_t si = ((int64_t)ui.e * nt + ui.item) * nb + (st >> 1);
           bulk_g2s(dst + S_REL, p.SP + si * PAIR_BYTES, PAIR_BYTES, B.wfull + s);
         }
@@ -470,7 +478,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       un++;
     }
   } else if (warp < EPI0) {  // ------------------------------------------------------------------- dequant
-    const int dw = warp - DQ0, h = dw >> 2, q = warp & 3;
+    const int dw = warp - DQ0, h = (dw >> 2) & 1, grp = dw >> 3, q = warp & 3;
     const int row = 128 * h + 32 * q + lane;  // this thread's weight row within the item
     const int sw = ((row >> 2) & 1) << 4;     // byte offset of the row's first 16-byte half (swizzle)
     const uint32_t t_row = tmem + ((uint32_t)(32 * q) << 16) + A_COL0 + 32 * h;
@@ -483,6 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const uint32_t* lt = lut + (un & 1) * 256;
       for (int st = 0; st < nstage; st++, g++) {
+        if ((int)(g & 1) != grp) continue;  // the other group's stage
         const int s = g % NW, a = g % NA;
         const bool have_w = wait_warp(B.wfull + s, (g / NW) & 1, deadline, p.err, abort_flag) &&
                             wait_warp(B.sfull + s, (g / NW) & 1, deadline, p.err, abort_flag);
@@ -540,23 +549,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
       const int row = 32 * q + lane;  // weight row within the half
       const bool quad = max(16, (nv + 15) & ~15) <= QUAD_N;
-      for (int c0 = 0; c0 < nv; c0 += 16) {
-        float v0[16], v1[16];
+      for (int c0 = 0; c0 < nv; c0 += 8) {
+        float v0[8], v1[8];
         if (quad) {  // sum the two k-parity accumulators of each half
-          float g1[16], u1[16];
-          tmem_ld16x4(tbase + c0, tbase + QUAD_N + c0, tbase + 2 * QUAD_N + c0, tbase + 3 * QUAD_N + c0, v0, g1, v1,
-                      u1);
+          float g1[8], u1[8];
+          tmem_ld8x4(tbase + c0, tbase + QUAD_N + c0, tbase + 2 * QUAD_N + c0, tbase + 3 * QUAD_N + c0, v0, g1, v1, u1);
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
+          for (int j = 0; j < 8; j++) {
             v0[j] += g1[j];
             v1[j] += u1[j];
           }
         } else {
-          tmem_ld16x2(tbase + c0, tbase + 128 + c0, v0, v1);
+          tmem_ld8x2(tbase + c0, tbase + 128 + c0, v0, v1);
         }
-        const int jj = c0 >> 5, l0 = c0 & 16;
+        const int jj = c0 >> 5, l0 = c0 & 24;
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < 8; j++) {
           if (c0 + j >= nv) break;
           const int id = __shfl_sync(0xffffffffu, ids[jj], l0 + j);
           if (p.gate_up) {  // mode 1: act row = the row's sorted position, else its id

@@ -19,7 +19,7 @@ from .prep import PreparedLayer
 
 BM = 96  # moe_align block size (rows per block) of the decode path, as the kit (files/mbx_moek.py:33)
 BM_PREFILL = 128  # block size of the tcgen05 path (the MMA's N, at most)
-LAUNCHES_PER_LAYER = 5  # decode: align, gate_up GEMM, SwiGLU epilogue, down GEMM, router weight + top-k sum
+LAUNCHES_PER_LAYER = 1  # decode: the whole layer (routing, gate_up + SwiGLU, down, top-k sum) is one kernel
 _BUF: dict = {}
 _PROF = None  # when a list, fused_moe appends (name, launch closure) for each of its GEMM launches
 
@@ -53,6 +53,9 @@ def check_device_errors(dev) -> None:
     code = int(w[0].item())
     if code:
         w.zero_()  # an aborted launch may also have left split counters behind
+        for key, t in _BUF.items():  # and the whole-layer kernel's counters and ready stamps
+            if key[0] == "layer_state" and key[1] == torch.device(dev):
+                t.zero_()
         names = {1: "a bounded wait timed out", 2: "an expert id out of range", 3: "a block with more rows than "
                  "max_rows"}
         raise MoekError(f"moek_b200: device error {code}: {names.get(code, 'unknown')}")
@@ -155,12 +158,60 @@ DECODE_MAX_M = int(os.environ.get("MOEK_B200_DECODE_MAX_M", "64"))  # split-k wi
 
 
 def launches_per_layer(m: int, top_k: int) -> int:
-    """Kernels of this library one fused_moe call launches: decode = align, gate_up GEMM, SwiGLU epilogue, down GEMM,
-    router-weight + top-k epilogue; prefill = align (one kernel up to 1024 indices, else count/offsets/scatter),
-    gate_up GEMM, down GEMM, top-k combine."""
-    if m <= DECODE_MAX_M:
+    """Kernels of this library one fused_moe call launches: decode = one (moek_moe_layer); prefill = align (one
+    kernel up to 1024 indices, else count/offsets/scatter), gate_up GEMM, down GEMM, top-k combine."""
+    if _decode_path(m, top_k):
         return LAUNCHES_PER_LAYER
     return (1 if m * top_k <= 1024 else 3) + 3
+
+
+LAYER_MAXIDS = 512  # routed slots per whole-layer call (moek_layer.cu)
+
+
+def _decode_path(m: int, top_k: int) -> bool:
+    return m <= min(DECODE_MAX_M, 96) and m * top_k <= LAYER_MAXIDS
+
+
+def _layer_splits(hidden: int, inter: int):
+    """k-splits of the whole-layer kernel's gate_up (K = hidden) and down (K = inter) units: 2 and 1 where they cut
+    K into whole 128-k runs (measured best at M = 8 and 32 on B200: every further split costs a partial round trip
+    and an arrival; MOEK_B200_LAYER_SPLITS="g,d" overrides)."""
+    env = os.environ.get("MOEK_B200_LAYER_SPLITS")
+    if env:
+        g, d = (int(v) for v in env.split(","))
+        return g, d
+    pick = lambda k, want: max(d for d in range(1, want + 1) if (k // 128) % d == 0)
+    return pick(hidden, 2), pick(inter, 1)
+
+
+def _layer_state(dev, E: int, hidden: int, inter: int) -> torch.Tensor:
+    """Persistent zero-initialised int32 state of the whole-layer kernel (counters and ready stamps) for one layer
+    geometry on one device; calls in one stream share it (concurrent calls on other streams would race)."""
+    import ctypes
+
+    key = ("layer_state", torch.device(dev), E, hidden, inter)
+    if key not in _BUF:
+        n = ctypes.c_int64(0)
+        call("moek_layer_state_ints", E, hidden, inter, ctypes.byref(n))
+        _BUF[key] = torch.zeros(n.value, dtype=torch.int32, device=dev)
+    return _BUF[key]
+
+
+def _layer_kernel(x, layer, tw, ids32, m, top_k, output, rows):
+    import ctypes
+
+    a, b = layer.w13, layer.w2
+    hidden, inter = a.K, b.K
+    dev = x.device
+    ns1, ns2 = _layer_splits(hidden, inter)
+    wsb = ctypes.c_size_t(0)
+    call("moek_layer_workspace_bytes", m, top_k, hidden, inter, ns1, ns2, int(rows is not None), ctypes.byref(wsb))
+    ws = _scratch("layer_ws", wsb.value, torch.uint8, dev)
+    st = _layer_state(dev, layer.E, hidden, inter)
+    call("moek_moe_layer", _ptr(x), m, hidden, inter, layer.E, _ptr(ids32), _ptr(tw), top_k, _ptr(a.w), _ptr(a.sp),
+         _ptr(a.g), _ptr(a.exc_off), _ptr(a.exc_ent), _ptr(b.w), _ptr(b.sp), _ptr(b.g), _ptr(b.exc_off),
+         _ptr(b.exc_ent), ns1, ns2, _ptr(ws), ws.numel(), _ptr(st), st.numel(), _ptr(error_word(dev)),
+         _ptr(output), _ptr(rows), _stream(dev))
 
 
 def _splits(k: int, units_per_split: int, grid: int) -> int:
@@ -229,8 +280,15 @@ def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
     tw = topk_weights.reshape(-1).float().contiguous()
     cnt = error_word(dev)
     rows = min(BM, m)
+    if _decode_path(m, top_k) and os.environ.get("MOEK_B200_DECODE_PATH", "layer") == "layer":
+        # the whole layer in one persistent kernel: routing, gate_up + SwiGLU, down x router weight, top-k sum
+        out_rows = None if rows_k is None else torch.empty((num_ids, b.N), dtype=torch.float32, device=dev)
+        _timed("layer", lambda: _layer_kernel(x, layer, tw, ids32, m, top_k, output if rows_k is None else None,
+                                              out_rows))
+        return output if rows_k is None else out_rows
     act = torch.empty((num_ids, a.N // 2), dtype=torch.bfloat16, device=dev)
     if m <= DECODE_MAX_M:
+        # split-k GEMM launches (moek_gemm mode 2) and their two epilogue kernels (MOEK_B200_DECODE_PATH=split)
         sid, eid, npad = moe_align_block_size(ids32, BM, layer.E)
         # split-k with fp32 partials (no cross-CTA synchronisation in the GEMMs), finished by two small
         # deterministic epilogue kernels: SwiGLU -> act, and router weight + top-k sum -> output
