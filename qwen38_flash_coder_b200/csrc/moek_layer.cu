@@ -55,18 +55,12 @@ constexpr int THREADS = (NCW + 3) * 32;
 constexpr int LBK = 2 * BK;                  // k per pipeline stage: one packed-scale run pair
 constexpr int LSTAGE = 2 * STAGE_BYTES;      // 16 KB of packed codes per (item, stage): one bulk copy
 constexpr int X_STRIDE = LBK * 2 + 16;       // bytes per activation row in a slot (+16: conflict-free reads)
-constexpr int SC_STRIDE = 288;               // bytes per k-group row of a slot's scale-byte table
-constexpr int SC_BYTES = KG * SC_STRIDE;     // the stage's 8 k-groups
+constexpr int SC_BYTES = ITEM_COLS * KG;     // scale table of a stage: one byte per (weight row, k-group)
 constexpr int NLUT = 8;         // per-unit (B | R) tables in flight (the scale warp runs at most 4 units ahead)
 constexpr int MAXU = 32;        // units per metadata round
-constexpr int MAXRUN = 32;      // packed-scale runs per unit
-constexpr int EXC_POOL = 1024;  // exception entries cached per round
 
 struct UnitMeta {
   int ph, blk, item, ks, e, nv, flags;  // ph: 0 = gate_up, 1 = down; flags: 2 = block has more rows than XR
-  float g;
-  int from_global, exc_g0, exc_s0;
-  int run_off[MAXRUN + 1];
 };
 
 template <int XR>
@@ -74,11 +68,10 @@ struct Cfg {
   static constexpr int X_OFF = LSTAGE + PAIR_BYTES;
   static constexpr int SC_OFF = X_OFF + XR * X_STRIDE;
   static constexpr int SLOT = SC_OFF + SC_BYTES;
-  static constexpr int NS = XR <= 8 ? 4 : XR <= 16 ? 3 : XR <= 32 ? 2 : 3;  // two CTAs per SM up to XR = 32
+  static constexpr int NS = XR <= 16 ? 4 : 3;  // two CTAs per SM up to XR = 32
   static constexpr int META_OFF = NS * SLOT;
   static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
-  static constexpr int POOL_OFF = IDS_OFF + MAXU * XR * 4;
-  static constexpr int LUT_OFF = POOL_OFF + EXC_POOL * 4;
+  static constexpr int LUT_OFF = IDS_OFF + MAXU * XR * 4;
   static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 4;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
   static constexpr int MISC_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;
   static constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
@@ -109,6 +102,11 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
 
@@ -144,7 +142,6 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   extern __shared__ __align__(128) uint8_t smem[];
   UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);
   int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);
-  uint32_t* pool = reinterpret_cast<uint32_t*>(smem + C::POOL_OFF);
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::LUT_OFF);
   int* srow = reinterpret_cast<int*>(smem + C::ROUTE_OFF);
   int* bexp = srow + LAYER_MAXIDS;
@@ -329,58 +326,45 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       if (lane == 0) mbar_arrive(mempty);
     }
   } else if (warp == W_SCALE) {  // -------------------------------------------------------------------- scale warp
+    // Per unit: the expert's global scale and the unit's exception offsets (lane j: run j's first entry) and entries
+    // (up to 64 held in registers, two per lane), loaded by all lanes at once and one unit ahead, so that no stage
+    // waits on a chain of global loads. Per stage: the slot's scale table, one 8-byte row per weight row (byte kg =
+    // k-group kg), then the run's exceptions. Lane L decodes chunk L % 16 (8 positions) of run L / 16 of the pair.
     uint32_t g = 0, kq = 0;
     const int run = lane >> 4, ch = lane & 15;
-    int dst[8];
+    int dst[8];  // the rows (item slots) of the lane's 8 positions
 #pragma unroll
     for (int i = 0; i < 8; i++) dst[i] = run * 128 + position_slot(8 * ch + i);
     bool ok = true;
     for (int r = 0; r < rounds && ok; r++) {
       const int nu = min(MAXU, n_mine - r * MAXU);
       if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
-      for (int i = lane; i < nu; i += 32) {
-        UnitMeta& m = meta[i];
+      int ro_n = 0, end_n = 0;
+      float g_n = 0.f;
+      auto fetch = [&](int ui) {  // loads only; consumed one unit later
+        const UnitMeta& m = meta[ui];
         const LayerMat& mt = p.m[m.ph];
-        const int nb = mt.nstage, nruns = nb / mt.nsplit;
-        const bool valid = m.e >= 0 && m.e < p.E;
-        m.g = valid ? mt.G[m.e] : 0.f;
-        const int64_t key0 = ((int64_t)(valid ? m.e : 0) * mt.nt + m.item) * nb + (int64_t)m.ks * nruns;
-        const int o0 = valid ? mt.exc_off[key0] : 0;
-        m.exc_g0 = o0;
-        for (int j = 0; j <= nruns; j++) m.run_off[j] = valid ? mt.exc_off[key0 + j] - o0 : 0;
-      }
-      __syncwarp();
-      if (lane == 0) {
-        int used = 0;
-        for (int i = 0; i < nu; i++) {
-          const LayerMat& mt = p.m[meta[i].ph];
-          const int nruns = mt.nstage / mt.nsplit;
-          const int cnt = meta[i].run_off[nruns];
-          meta[i].from_global = used + cnt > EXC_POOL;
-          if (!meta[i].from_global) {
-            meta[i].exc_s0 = used;
-            used += cnt;
-          }
-        }
-      }
-      __syncwarp();
-      for (int i = lane; i < nu; i += 32) {
-        if (meta[i].from_global) continue;
-        const LayerMat& mt = p.m[meta[i].ph];
         const int nruns = mt.nstage / mt.nsplit;
-        const int cnt = meta[i].run_off[nruns], s0 = meta[i].exc_s0, g0 = meta[i].exc_g0;
-        for (int j = 0; j < cnt; j++) pool[s0 + j] = mt.exc_ent[g0 + j];
-      }
-      __syncwarp();
+        const int64_t key0 = ((int64_t)m.e * mt.nt + m.item) * mt.nstage + (int64_t)m.ks * nruns;
+        ro_n = lane < nruns ? mt.exc_off[key0 + lane] : 0;
+        end_n = mt.exc_off[key0 + nruns];
+        g_n = mt.G[m.e];
+      };
+      if (nu > 0) fetch(0);
       for (int ui = 0; ui < nu && ok; ui++) {
         const UnitMeta& m = meta[ui];
         const LayerMat& mt = p.m[m.ph];
         const int su = mt.nstage / mt.nsplit;
+        const int o0 = __shfl_sync(0xffffffffu, ro_n, 0);
+        const int ro = ro_n - o0, cnt = end_n - o0;
+        const float gsc = g_n;
+        const uint32_t* eg = mt.exc_ent + o0;
+        const uint32_t ex0 = lane < cnt ? eg[lane] : 0u, ex1 = lane + 32 < cnt ? eg[lane + 32] : 0u;
+        if (ui + 1 < nu) fetch(ui + 1);
         uint32_t* lt = lut + (kq % NLUT) * 256;
 #pragma unroll
-        for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, m.g);
+        for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
         kq++;
-        const uint32_t* exc = m.from_global ? mt.exc_ent + m.exc_g0 : pool + m.exc_s0;
         const int r0g = m.ph == 0 ? m.item : 2 * m.item;  // global run index of the pair's first run
         for (int st = m.ks * su; st < (m.ks + 1) * su; st++, g++) {
           const int slot = g % C::NS;
@@ -389,27 +373,37 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             break;
           }
           const uint8_t* runp = smem + slot * C::SLOT + LSTAGE + run * RUN_BYTES;
-          uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF;
+          uint8_t* tb = smem + slot * C::SLOT + C::SC_OFF;
           const uint32_t b4 = runp[ch] * 0x01010101u;
+          uint32_t lo[KG], hi[KG];  // k-group kk's bytes of positions 8 ch + 0..3 and + 4..7
 #pragma unroll
           for (int kk = 0; kk < KG; kk++) {
-            const int kg = kk;
-            const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kg * 64 + ch * 4);
-            const uint32_t lo = (q & 0x0F0F0F0Fu) + b4;
-            const uint32_t hi = ((q >> 4) & 0x0F0F0F0Fu) + b4;
-            uint8_t* row = sc + kk * SC_STRIDE;
+            const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kk * 64 + ch * 4);
+            lo[kk] = (q & 0x0F0F0F0Fu) + b4;
+            hi[kk] = ((q >> 4) & 0x0F0F0F0Fu) + b4;
+          }
 #pragma unroll
-            for (int i = 0; i < 8; i++) row[dst[i]] = (uint8_t)(((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF);
+          for (int i = 0; i < 8; i++) {
+            const uint32_t* src = i < 4 ? lo : hi;
+            const uint32_t bi = i & 3, sel = bi | ((bi + 4) << 4);
+            uint2 row;
+            row.x = prmt2(prmt2(src[0], src[1], sel), prmt2(src[2], src[3], sel), 0x5410);
+            row.y = prmt2(prmt2(src[4], src[5], sel), prmt2(src[6], src[7], sel), 0x5410);
+            *reinterpret_cast<uint2*>(tb + dst[i] * 8) = row;
           }
           __syncwarp();
-          const int rr = st - m.ks * su;  // the unit's run (pair) of this stage
-          const int eo0 = m.run_off[rr], eo1 = m.run_off[rr + 1];
-          for (int j = eo0 + lane; j < eo1; j += 32) {
-            const uint32_t en = exc[j];
+          // this stage's run: entries [eo0, eo1) of the unit's list overwrite their bytes
+          const int rr = st - m.ks * su;
+          const int eo0 = __shfl_sync(0xffffffffu, ro, rr);
+          const int eo1 = rr + 1 < su ? __shfl_sync(0xffffffffu, ro, rr + 1) : cnt;
+          auto patch = [&](uint32_t en) {
             const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-            const int slot_e = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
-            sc[kg * SC_STRIDE + slot_e] = (uint8_t)(en >> 24);
-          }
+            const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
+            tb[row * 8 + kg] = (uint8_t)(en >> 24);
+          };
+          if (lane >= eo0 && lane < eo1) patch(ex0);
+          if (lane + 32 >= eo0 && lane + 32 < eo1) patch(ex1);
+          for (int j = max(eo0, 64) + lane; j < eo1; j += 32) patch(eg[j]);  // long lists: the rest from memory
           __syncwarp();
           mbar_arrive(scaled + slot);
         }
@@ -456,13 +450,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             ok = false;
             continue;  // stay in step with the other roles' counters
           }
-#pragma unroll 1
+#pragma unroll
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
           const uint8_t* sx = smem + slot * C::SLOT + C::X_OFF + hf * BK * 2;
-          const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + (4 * hf + c) * SC_STRIDE;
-          const uint32_t s0a = lt[sc[slot00]], s0b = lt[sc[slot00 + 8]], s1a = lt[sc[slot10]],
-                         s1b = lt[sc[slot10 + 8]];
+          const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + 4 * hf + c;  // byte (k-group) of each row
+          const uint32_t s0a = lt[sc[slot00 * 8]], s0b = lt[sc[(slot00 + 8) * 8]], s1a = lt[sc[slot10 * 8]],
+                         s1b = lt[sc[(slot10 + 8) * 8]];
 #pragma unroll
           for (int i = 0; i < 2; i++) {
             const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;
