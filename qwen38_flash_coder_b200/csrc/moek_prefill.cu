@@ -36,9 +36,10 @@
 //               of its latency): warp 8 + 8s + 4h + i owns rows 128h + 32q .. +31 of the item, q = warp % 4 (its TMEM
 //               lane quarter); per stage a thread reads its row's 32 bytes of codes and its scale word, and stores
 //               32 columns of bf16 pairs into the A slot.
-//   epilogue  = warps 24-27 (lane quarter = warp % 4): tcgen05.ld 8 columns at a time; gate_up writes
-//               act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves 0 and 1), down writes
-//               the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
+//   epilogue  = warps 24-31 (lane quarter = warp % 4; two warps per quarter take alternate 8-column chunks, so the
+//               accumulator is drained twice as fast and the next unit's MMAs wait less): tcgen05.ld 8 columns at a
+//               time; gate_up writes act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves
+//               0 and 1), down writes the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
 //   mode 1    = gate_up writes act at the row's position in moe_align's sorted order instead of its id, so that the
 //               down GEMM loads a block's rows as one 128-row TMA tile per stage instead of gathering them.
 //
@@ -63,7 +64,7 @@ constexpr int NW = 4;     // shared-memory ring of packed codes + packed scales 
 constexpr int NB = 4;     // shared-memory ring of activation tiles
 constexpr int NA = 3;     // TMEM ring of dequantised weight tiles
 constexpr int NDQ = 16;   // dequant warps: two groups of 8 taking alternate stages
-constexpr int NEPI = 4;   // epilogue warps
+constexpr int NEPI = 8;   // epilogue warps: two per TMEM lane quarter, taking alternate 8-column chunks
 constexpr int NMMA = 4;   // MMA-issuing warps: one per accumulator (half h, k16-step parity p) = warp W_MMA + 2h + p
 constexpr int NLOAD = 2;  // activation-gather warps (a TMA issue is latency-bound per thread: two warps, twice the rate)
 constexpr int W_PROD = 0, W_MMA = 1, W_LOAD = W_MMA + NMMA, W_SCALE = W_LOAD + NLOAD, DQ0 = W_SCALE + 1,
@@ -528,6 +529,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {  // ------------------------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int part = (warp - EPI0) >> 2;  // this warp's chunks: c0 = 8 part (mod 16)
     const int I = p.N / 2;
     uint32_t un = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
@@ -549,7 +551,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
       const int row = 32 * q + lane;  // weight row within the half
       const bool quad = max(16, (nv + 15) & ~15) <= QUAD_N;
-      for (int c0 = 0; c0 < nv; c0 += 8) {
+      for (int c0 = 8 * part; c0 < nv; c0 += 16) {
         float v0[8], v1[8];
         if (quad) {  // sum the two k-parity accumulators of each half
           float g1[8], u1[8];
