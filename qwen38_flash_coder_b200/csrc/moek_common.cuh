@@ -1,11 +1,12 @@
 // Shared device helpers for the routed-expert NVFP4 (W4A16) MoE kernels (sm_100a).
 //
-// Weight decode. A tiled weight word holds 8 E2M1 codes (sign in bit 3) of 8 consecutive k of one output column;
-// code i sits in nibble NIBBLE_OF[i] = {3, 7, 2, 6, 1, 5, 0, 4}, so that step d of the decode (word shifted left by
-// 4d) finds codes 2d and 2d + 1 at bits 12-15 and 28-31. Moving a code's sign to bit 15 and its three magnitude bits
-// to bits 8..6 of a bf16 gives exactly e2m1 * 2^-126 (exponent field = the code's exponent, top mantissa bit = its
-// mantissa bit; code 1 becomes the subnormal 2^-127). That value D is exact, and the weight the reference's oracle
-// uses, bf16(e2m1 * s * gs) with s the E4M3 block scale and gs the expert's fp32 global scale
+// Weight decode. A tiled weight word holds 8 E2M1 codes (sign = bit 3) of 8 consecutive k of one output column,
+// bit-scattered at load time (prep.CODE_BITS) so that the bf16 pairs come out with few integer ops: codes 0 and 1
+// already have their signs at bits 15 / 31 and their three magnitude bits at 8..6 / 24..22, codes 2-3 and 4-5 sit 3
+// and 6 bits lower (one shift each), codes 6-7 use the remaining bits (three shifts). A code's sign at bit 15 and its
+// three magnitude bits at 8..6 of a bf16 give exactly e2m1 * 2^-126 (exponent field = the code's exponent, top
+// mantissa bit = its mantissa bit; code 1 becomes the subnormal 2^-127). That value D is exact, and the weight the
+// reference's oracle uses, bf16(e2m1 * s * gs) with s the E4M3 block scale and gs the expert's fp32 global scale
 // (bench/moek/problem.py:31-38), is then rebuilt per pair of codes with two bf16 FMAs:
 //     Y  = fp32(s * gs) * 2^126            (once per 16 weights, from the packed scale byte and the global scale)
 //     B  = bf16(Y), R = bf16(Y - B)         (B carries 8 bits of Y, R the next 8)
@@ -101,9 +102,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 
 // -------------------------------------------------------------------------------------------------- decoding
-// Pair d of a tiled word, after the word was shifted left by 4d: bf16x2 of e2m1 * 2^-126 for codes 2d, 2d+1.
-__device__ __forceinline__ uint32_t fp4_pair(uint32_t q) {
-  return (q & 0x80008000u) | ((q >> 6) & 0x01C001C0u);
+// The four pairs of a tiled word as bf16x2 of e2m1 * 2^-126: pair d = codes 2d, 2d + 1 (prep.CODE_BITS).
+__device__ __forceinline__ void fp4_pairs(uint32_t q, uint32_t* d) {
+  constexpr uint32_t P = 0x81C081C0u;  // sign and magnitude bits of a bf16 pair
+  d[0] = q & P;
+  d[1] = (q << 3) & P;
+  d[2] = (q << 6) & P;
+  d[3] = ((q >> 6) & 0x01800180u) | ((q >> 4) & 0x00400040u) | ((q << 4) & 0x80008000u);
 }
 // S0E5M3 byte -> fp32 value (s * sf * 2^7)
 __device__ __forceinline__ float s0e5m3_to_f32(uint32_t b) {
@@ -132,11 +137,10 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
 }
 // The oracle's bf16 weights for the 8 codes of one word: out[d] = bf16x2 of codes 2d, 2d + 1.
 __device__ __forceinline__ void dequant_word(uint32_t q, const ScaleBR& s, uint32_t* out) {
+  uint32_t dv[4];
+  fp4_pairs(q, dv);
 #pragma unroll
-  for (int d = 0; d < 4; d++) {
-    const uint32_t dv = fp4_pair(q << (4 * d));
-    out[d] = bf2_fma(dv, s.b2, bf2_mul(dv, s.r2));
-  }
+  for (int d = 0; d < 4; d++) out[d] = bf2_fma(dv[d], s.b2, bf2_mul(dv[d], s.r2));
 }
 
 // Processed position (within its 128-position run) of item slot s: vLLM's scale_perm (new 8i + j <- old i + 8j)

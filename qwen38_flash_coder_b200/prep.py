@@ -14,8 +14,11 @@ Output, per matrix:
 - **weights**: this build's tiled layout, an int32 tensor of the reference's shape [E, K/16, 2N] (same bytes as the
   checkpoint, reordered). Per (expert, 256-row item, 64-k stage) one contiguous 8 KB block of 256 rows x 32 bytes:
   row r holds the item's row r over the stage's 64 k as 8 words, word w = the 8 consecutive k ``64s + 8w + i``
-  (i = 0..7) with code i in nibble ``NIBBLE_OF[i]``, so words 2c and 2c + 1 are k-group c (one scale) and each word
-  decodes, two codes at a time, into bf16 pairs (k, k+1) in order. The row's two 16-byte halves are swapped when
+  (i = 0..7), so words 2c and 2c + 1 are k-group c (one scale). Inside a word the 4 bits of code i (m, e0, e1, sign
+  = bits 0..3 of the E2M1 code) sit at bit positions ``CODE_BITS[i]``: codes 0 and 1 exactly where a bf16 pair wants
+  them (sign at 15 / 31, e1 e0 m at 8..6 / 24..22, which makes the pair e2m1 * 2^-126), codes 2-3 and 4-5 three and
+  six bits lower, codes 6-7 in the bits left over; the decode of a word into its four bf16 pairs (k, k+1) is then
+  one mask, two shift-and-masks and one three-part gather (moek_common.cuh). The row's two 16-byte halves are swapped when
   bit 2 of r is set, so that 8 threads reading 16 bytes of 8 consecutive rows, or 32 lanes reading 8 bytes
   (k-group c of rows g and g + 8, the A operand of mma.sync m16n8k16), hit distinct shared-memory banks. Item rows
   0..127 are gate rows ``128t + r`` and 128..255 the matching up rows ``I + 128t + r - 128`` (gate_up), or rows
@@ -25,7 +28,18 @@ import torch
 
 KG = 8
 RUN = 16 + KG * 64  # 528: packed bytes per (expert, run of 8 k-groups, 128 positions)
-NIBBLE_OF = (3, 7, 2, 6, 1, 5, 0, 4)  # nibble position of code i of a word's 8 consecutive k
+# bit positions (m, e0, e1, sign) of code i of a word's 8 consecutive k
+CODE_BITS = ((6, 7, 8, 15), (22, 23, 24, 31), (3, 4, 5, 12), (19, 20, 21, 28), (0, 1, 2, 9), (16, 17, 18, 25),
+             (10, 13, 14, 11), (26, 29, 30, 27))
+
+
+def _spread_table(device) -> torch.Tensor:
+    """int64 [8, 16]: the word bits of code i with value v."""
+    t = torch.zeros((8, 16), dtype=torch.int64)
+    for i, bits in enumerate(CODE_BITS):
+        for v in range(16):
+            t[i, v] = sum(((v >> b) & 1) << pos for b, pos in enumerate(bits))
+    return t.to(device)
 
 
 # ------------------------------------------------------------------------------------------------------------ scales
@@ -139,14 +153,15 @@ def tile_weights(codes: torch.Tensor, gate_up: bool, chunk: int = 16) -> torch.T
     k = 2 * k2
     nt, ns = n // 256, k // 64
     cols = item_columns(n, gate_up, codes.device).flatten()
-    shifts = torch.tensor([4 * p for p in NIBBLE_OF], dtype=torch.int64, device=codes.device)
+    spread = _spread_table(codes.device)
+    slot_i = torch.arange(8, device=codes.device)
     swap = _swizzle_rows(codes.device)
     out = torch.empty((e, k // 16, 2 * n), dtype=torch.int32, device=codes.device)
     for e0 in range(0, e, chunk):
         e1 = min(e, e0 + chunk)
         c = codes[e0:e1][:, cols, :]
         nib = torch.stack([c & 0xF, c >> 4], -1).view(e1 - e0, nt, 256, ns, 8, 8)  # [e, t, r, s, w, i]
-        word = (nib.permute(0, 1, 3, 2, 4, 5).to(torch.int64) << shifts).sum(-1)  # [e, t, s, r, w]
+        word = spread[slot_i, nib.permute(0, 1, 3, 2, 4, 5).long()].sum(-1)  # [e, t, s, r, w]
         word = word.view(e1 - e0, nt, ns, 256, 2, 4)
         word[:, :, :, swap] = word[:, :, :, swap].flip(-2)
         word = torch.where(word >= 2 ** 31, word - 2 ** 32, word).to(torch.int32)
@@ -159,11 +174,12 @@ def untile_weights(w: torch.Tensor, n: int, gate_up: bool) -> torch.Tensor:
     e = w.shape[0]
     k = w.shape[1] * 16
     nt, ns = n // 256, k // 64
-    shifts = torch.tensor([4 * p for p in NIBBLE_OF], dtype=torch.int64, device=w.device)
+    pos = torch.tensor(CODE_BITS, dtype=torch.int64, device=w.device)  # [8 codes, 4 bits]
     word = (w.to(torch.int64) & 0xFFFFFFFF).view(e, nt, ns, 256, 2, 4).clone()
     swap = _swizzle_rows(w.device)
     word[:, :, :, swap] = word[:, :, :, swap].flip(-2)
-    nib = ((word.view(e, nt, ns, 256, 8)[..., None] >> shifts) & 0xF).to(torch.uint8)  # [e, t, s, r, w, i]
+    bits = (word.view(e, nt, ns, 256, 8)[..., None, None] >> pos) & 1  # [e, t, s, r, w, i, b]
+    nib = (bits << torch.arange(4, device=w.device)).sum(-1).to(torch.uint8)  # [e, t, s, r, w, i]
     nib = nib.permute(0, 1, 3, 2, 4, 5).reshape(e, nt * 256, k)
     out = torch.empty((e, n, k), dtype=torch.uint8, device=w.device)
     out[:, item_columns(n, gate_up, w.device).flatten(), :] = nib

@@ -71,7 +71,7 @@ def test_tile_weights_word_contents():
             kk = 64 * s + 8 * wd + i
             byte = int(codes[0, col, kk // 2])
             code = (byte >> 4) if kk & 1 else (byte & 15)
-            assert (word >> (4 * prep.NIBBLE_OF[i])) & 15 == code
+            assert sum(((word >> bp) & 1) << b for b, bp in enumerate(prep.CODE_BITS[i])) == code
 
 
 def test_quantizer_matches_reference_e2m1(golden):
