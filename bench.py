@@ -45,9 +45,9 @@ METRIC = "routed-MoE layer µs & HBM GB/s (M=8,32); TFLOP/s (M=6912); 1/2/4/8 GP
 H, I, E, TOPK = 2048, 512, 512, 5
 FLOPS_PER_ROW = 2 * 3 * H * I  # gate + up + down per (token, slot) row
 
-# DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu --set full capture each:
-# profiles/moek_prefill_kernel_prefill6912.md (gate_up launch); the whole-layer decode kernel has none yet
-TRAFFIC = {"prefill": 695_317_952}
+# DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu --set full capture each (layer 0):
+# profiles/moek_layer_kernel_decode8.md and profiles/moek_prefill_kernel_prefill6912.md (gate_up launch)
+TRAFFIC = {"decode8": 64_508_928, "prefill": 696_396_544}
 
 WORKLOADS = {
     "decode8": dict(m=8, route="uniform", unit="GB/s", desc="decode verify M=8 (1 stream x block 8), uniform routing"),
