@@ -60,8 +60,8 @@ namespace moek {
 namespace pf {
 
 constexpr int BMP = 128;  // rows per moe_align block (the MMA's N, at most)
-constexpr int NW = 4;     // shared-memory ring of packed codes + packed scales + scale words
-constexpr int NB = 4;     // shared-memory ring of activation tiles
+constexpr int NW = 6;     // shared-memory ring of packed codes + packed scales + scale words
+constexpr int NB = 6;     // shared-memory ring of activation tiles
 constexpr int NA = 3;     // TMEM ring of dequantised weight tiles
 constexpr int NDQ = 16;   // dequant warps: two groups of 8 taking alternate stages
 constexpr int NEPI = 8;   // epilogue warps: two per TMEM lane quarter, taking alternate 8-column chunks
@@ -86,7 +86,7 @@ constexpr int LUT_OFF = W_OFF + NW * W_SLOT;                     // 2 x 256 (B |
 constexpr int EXC_OFF = LUT_OFF + 2 * 256 * 4;                   // EXC_CAP entries (scale warp only)
 constexpr int RUNOFF_OFF = EXC_OFF + EXC_CAP * 4;                // 33 run offsets (scale warp only)
 constexpr int IDS_OFF = (RUNOFF_OFF + 33 * 4 + 15) / 16 * 16;    // 128 activation rows per loader warp
-constexpr int MISC_OFF = IDS_OFF + 2 * BMP * 4;                  // tmem base, abort flag
+constexpr int MISC_OFF = IDS_OFF + NLOAD * BMP * 4;              // tmem base, abort flag
 constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
 constexpr int NBARS = 3 * NW + 2 * NB + 2 * NA + 2 + 2;
 constexpr int SMEM_USED = BAR_OFF + NBARS * 8;
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {  // ------------------------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int part = (warp - EPI0) >> 2;  // this warp's chunks: c0 = 8 part (mod 16)
+    const int part = (warp - EPI0) >> 2;  // this warp's chunks: c0 = 8 part (mod 8 NEPI / 4)
     const int I = p.N / 2;
     uint32_t un = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
       const int row = 32 * q + lane;  // weight row within the half
       const bool quad = max(16, (nv + 15) & ~15) <= QUAD_N;
-      for (int c0 = 8 * part; c0 < nv; c0 += 16) {
+      for (int c0 = 8 * part; c0 < nv; c0 += 8 * (NEPI / 4)) {
         float v0[8], v1[8];
         if (quad) {  // sum the two k-parity accumulators of each half
           float g1[8], u1[8];

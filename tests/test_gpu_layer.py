@@ -22,12 +22,13 @@ def _oracle(w13, w2, x, ids, wts):
 
 
 @pytest.mark.parametrize("splits", ["1,1", "4,2", "16,4", "2,1", "8,2"])
-@pytest.mark.parametrize("m,route", [(1, "u"), (8, "u"), (13, "z"), (32, "z")])
-def test_layer_kernel_vs_oracle(monkeypatch, splits, m, route):
+@pytest.mark.parametrize("m,route,e", [(1, "u", 64), (8, "u", 64), (13, "z", 64), (32, "z", 64), (2, "u", 8),
+                                       (64, "z", 512)])
+def test_layer_kernel_vs_oracle(monkeypatch, splits, m, route, e):
     monkeypatch.setenv("MOEK_B200_LAYER_SPLITS", splits)
-    w13, w2 = synth.make_layer(64, 2048, 512, m, device=DEV)
+    w13, w2 = synth.make_layer(e, 2048, 512, m, device=DEV)
     x = synth.activations(m, 2048, m, device=DEV)
-    ids, wts = (synth.route_softmax if route == "u" else synth.route_zipf)(m, 64, 5, m, device=DEV)
+    ids, wts = (synth.route_softmax if route == "u" else synth.route_zipf)(m, e, 5, m, device=DEV)
     out = ops.fused_moe(x, prep.PreparedLayer(w13, w2), wts, ids)
     ops.check_device_errors(DEV)
     ok, stats = moe_ref.within_gate(out.cpu(), _oracle(w13, w2, x, ids, wts))
