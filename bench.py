@@ -101,44 +101,85 @@ def gate_bytes(layer, ids, m):
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region (started before, stopped after)."""
+    """SM clock, power and clock-event reasons sampled during the timed region: NVML every ~2 ms from a thread
+    (timed regions of a few milliseconds still get samples), nvidia-smi every 100 ms if NVML is not available."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, index):
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+    def __init__(self, dev):
+        import threading
+
+        self.samples, self.h, self.p = [], None, None
+        self.done = threading.Event()
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
-                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(dev).uuid)
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(dev.index)
+            self.nv = pynvml
+            self.mx = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception:
+            self.h = None
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            try:
+                self.p = subprocess.Popen(["nvidia-smi", f"--id={dev.index}", f"--query-gpu={q}", "--format=csv,noheader",
+                                           "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+            except OSError:
+                self.p = None
+
+    def _run(self):
+        nv = self.nv
+        while not self.done.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.samples.append((sm, rs, pw))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def stop(self):
+        if self.h is not None:
+            self.done.set()
+            self.t.join(timeout=5)
+            sm = [x[0] for x in self.samples]
+            reasons = sorted({n for _, rs, _ in self.samples for n, bit in self.REASONS.items() if rs & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.mx, "samples": len(sm),
+                    "power_w_max": max((x[2] for x in self.samples), default=None), "reasons": reasons,
+                    "source": "nvml"}
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
         self.p.wait(timeout=10)
         self.f.seek(0)
         sm, mx, reasons, power = [], None, set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.f.read().splitlines():
             c = [x.strip() for x in line.split(",")]
-            if len(c) < 9:
+            if len(c) < 7:
                 continue
             try:
-                sm.append(float(c[1].split()[0]))
-                mx = float(c[2].split()[0])
-                power.append(float(c[3].split()[0]))
+                sm.append(float(c[0].split()[0]))
+                mx = float(c[1].split()[0])
+                power.append(float(c[2].split()[0]))
             except ValueError:
                 continue
-            for n, v in zip(names, c[5:9]):
+            for n, v in zip(list(self.REASONS), c[3:7]):
                 if "Active" in v and "Not" not in v:
                     reasons.add(n)
         os.unlink(self.f.name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
-                "power_w_max": max(power) if power else None, "reasons": sorted(reasons)}
+                "power_w_max": max(power) if power else None, "reasons": sorted(reasons), "source": "nvidia-smi"}
 
 
 def make_graph(fn, warmup):
@@ -240,7 +281,7 @@ def measure(name, layers, a, dev, world, barrier, headline):
 
     graph = make_graph(step, a.warmup)
     ops.check_device_errors(dev)
-    clocks = Clocks(dev.index)
+    clocks = Clocks(dev)
     ms = timed(graph.replay, a.steps, barrier)
     clk = clocks.stop()
     if wl["unit"] == "GB/s":
@@ -471,7 +512,7 @@ def ep_main(a, rank, world, dev):
                 run, how = graph.replay, "one CUDA graph per step (NCCL all-to-alls captured)"
             else:
                 how = f"eager (graph capture failed on a rank: {err})"
-        clocks = Clocks(dev.index)
+        clocks = Clocks(dev)
         ms = over_ranks(timed(run, a.steps, barrier), world, dev)
         clk = clocks.stop()
         if wl["unit"] == "GB/s":
@@ -481,20 +522,24 @@ def ep_main(a, rank, world, dev):
         res = {"workload": wl["desc"], "value": round(amount / (ms / 1e3), 3), "unit": wl["unit"],
                "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / len(layers), 2), "clocks": clk,
                "launch": how}
-        # the local expert GEMMs on the rows one step delivered: gate_up launches replayed alone (this rank)
+        # the local kernels on the rows one step delivered, replayed alone (this rank): the whole-layer kernel when
+        # the received batch is a decode batch, else the tcgen05 gate_up GEMM
         rec = []
         step(ep.CudaBackend(record=rec))
         torch.cuda.synchronize()
         be = ep.CudaBackend()
         launches = ops.record_launches(lambda: [be.local(xr, mr, e["layer"], TOPK, ms)
                                                 for (xr, mr, ms), e in zip(rec, layers)])
-        gates = [f for n, f in launches if n == "gate_gemm"]
-        roof = None
-        if gates:
-            g = make_graph(lambda: [f() for f in gates], 2)
-            gus = timed(g.replay, a.steps, lambda: None) * 1e3 / len(gates)
+        kind = "layer" if any(n == "layer" for n, _ in launches) else "gate_gemm"
+        fns = [f for n, f in launches if n == kind]
+        kus = 0.0
+        if fns:
+            g = make_graph(lambda: [f() for f in fns], 2)
+            kus = timed(g.replay, a.steps, lambda: None) * 1e3 / len(fns)
             del g
-            gus = over_ranks(gus, world, dev)
+        kus = over_ranks(kus, world, dev)  # every rank takes part, whatever it launched
+        roof = None
+        if fns and kus > 0:
             peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
                 os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
             if wl["unit"] == "GB/s":
@@ -503,27 +548,30 @@ def ep_main(a, rank, world, dev):
                     lid = mr[:, :TOPK]
                     valid = lid[(lid >= 0) & (lid < e["layer"].local_experts)]
                     if valid.numel():
-                        gb.append(gate_bytes(e["layer"].prep, valid, int(xr.shape[0])))
+                        r = int(xr.shape[0])
+                        gb.append(touched_bytes(e["layer"].prep, valid, r)[0] if kind == "layer"
+                                  else gate_bytes(e["layer"].prep, valid, r))
                 gbpl = sum(gb) / max(1, len(gb))
                 peak = peaks.get("hbm_gbs", 6650.0)
-                ach = gbpl / (gus / 1e6) / 1e9
-                roof = {"kernel": "moek_decode_kernel (gate_up of the local experts on the received rows)",
+                ach = gbpl / (kus / 1e6) / 1e9
+                roof = {"kernel": "moek_layer_kernel (the local experts' whole layer on the received rows)"
+                        if kind == "layer" else "moek_prefill_kernel (gate_up of the local experts on the received rows)",
                         "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
                         "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
                         else "of fallback", "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
-                        "bytes_per_launch": int(gbpl), "avg_launch_us": round(gus, 2), "rank": "max over ranks"}
+                        "bytes_per_launch": int(gbpl), "avg_launch_us": round(kus, 2), "rank": "max over ranks"}
             else:
                 rows = sum(int(((mr[:, :TOPK] >= 0) & (mr[:, :TOPK] < e["layer"].local_experts)).sum())
                            for (xr, mr, _), e in zip(rec, layers)) / len(layers)
                 flops = rows * 2 * H * 2 * I
                 peak = peaks.get("bf16_tflops_sustained", 1400.0)
-                ach = flops / (gus / 1e6) / 1e12
+                ach = flops / (kus / 1e6) / 1e12
                 roof = {"kernel": "moek_prefill_kernel (gate_up of the local experts on the received rows)",
                         "bound": "tensor", "achieved": round(ach, 1), "peak": peak,
                         "peak_source": "of measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
                         if "bf16_tflops_sustained" in peaks else "of fallback", "unit": "TFLOP/s",
                         "frac": round(ach / peak, 4), "traffic": None, "flops_per_launch": int(flops),
-                        "avg_launch_us": round(gus, 2), "rank": "this rank's gate launches, max over ranks"}
+                        "avg_launch_us": round(kus, 2), "rank": "this rank's gate launches, max over ranks"}
         res["roofline"] = roof
         del rec
         per_layer = 4 + (ops.LAUNCHES_PER_LAYER if m <= ops.DECODE_MAX_M else 5)  # plan, pack, partial, unpack
