@@ -122,6 +122,16 @@ int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int3
  * 284-289): out bf16 [m, N] = bf16(sum_j rows[t*top_k + j]) in fp32, slot order. rows: fp32 if rows_fp32 else bf16. */
 int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int32_t N, int32_t top_k, void* stream);
 
+/* ---- Router. Replaces vLLM's fused_topk with scoring "softmax" (vllm/.../router/fused_topk_router.py:69-108, the
+ * topk_softmax op), the gating step in front of the layer (vllm/.../models/qwen3_next.py:158-165): per token t,
+ * p = softmax(logits[t]) in fp32, the top_k largest p (the lowest expert index among equal p, largest first) into
+ * topk_ids[t, :] and their p into topk_weights[t, :], divided by their sum when renormalize != 0; when
+ * token_expert_indices is not NULL it receives j * M + t for slot j. logits: fp32, or bf16 when logits_bf16 != 0,
+ * [M, E] row-major; E <= 1024, top_k <= 32. */
+int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M, int32_t E, int32_t top_k,
+                     int32_t renormalize, int32_t* topk_ids, float* topk_weights, int32_t* token_expert_indices,
+                     void* stream);
+
 /* ---- Whole decode layer in one launch. Replaces, for decode batches, the sequence the kit's forward wrap runs
  * (files/mbx_moek.py:236-289: moe_align, gate_up moe_gemm, split epilogue, down moe_gemm, split epilogue + top-k sum)
  * with one persistent kernel: routing in shared memory, gate_up + SwiGLU, down x router weight and the top-k sum,

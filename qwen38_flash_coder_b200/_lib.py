@@ -17,6 +17,7 @@ SIGNATURES = {
                                  _P, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _I32, _I32, _I32, _P, _I32, _P]),
     "moek_split_epilogue": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P]),
     "moek_combine": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _P]),
+    "moek_router_topk": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "moek_layer_state_ints": (ctypes.c_int, [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_int64)]),
     "moek_layer_workspace_bytes": (ctypes.c_int, [_I32] * 7 + [ctypes.POINTER(ctypes.c_size_t)]),
     "moek_moe_layer": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _I32] + [_P] * 10 + [_I32, _I32, _P,

@@ -6,7 +6,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmoek_b200.so")
-SOURCES = ["moek_abi.cu", "moek_align.cu", "moek_decode.cu", "moek_layer.cu", "moek_prefill.cu", "moek_ep.cu"]
+SOURCES = ["moek_abi.cu", "moek_align.cu", "moek_decode.cu", "moek_layer.cu", "moek_prefill.cu", "moek_ep.cu", "moek_router.cu"]
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17", "-shared",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden"]
 

@@ -208,6 +208,19 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
   return cuda_status(moek::launch_decode(p, max_rows, sm_count(), (cudaStream_t)stream), "moe_gemm launch");
 }
 
+// --------------------------------------------------------------------------------------------------- router
+MOEK_API int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M, int32_t E, int32_t top_k,
+                              int32_t renormalize, int32_t* topk_ids, float* topk_weights,
+                              int32_t* token_expert_indices, void* stream) {
+  if (M < 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > 32 || top_k > E)
+    return fail(MOEK_ERR_ARG, "moek_b200: router needs 0 < top_k <= min(32, E) and E <= 1024 (M %d, E %d, top_k %d)",
+                M, E, top_k);
+  if (M && (!logits || !topk_ids || !topk_weights)) return fail(MOEK_ERR_ARG, "moek_b200: router null pointer");
+  return cuda_status(moek::launch_router_topk(logits, logits_bf16 ? 1 : 0, M, E, top_k, renormalize ? 1 : 0,
+                                              topk_ids, topk_weights, token_expert_indices, (cudaStream_t)stream),
+                     "router launch");
+}
+
 // ------------------------------------------------------------------------------------- whole decode layer
 // Persistent int32 state of moek_moe_layer: [epoch, done, cnt1, rcnt, ready, cnt2, tok]. The layout depends only on
 // (E, H, I), so one zeroed state buffer serves every call of that geometry.

@@ -77,6 +77,10 @@ struct LayerParams {
 };
 cudaError_t launch_layer(const LayerParams& p, int max_rows, int sms, cudaStream_t st);
 
+// moek_router.cu: softmax -> top-k -> optional renormalisation (dtype 0 = fp32 logits, 1 = bf16)
+cudaError_t launch_router_topk(const void* logits, int dtype, int M, int E, int k, int renorm, int32_t* ids,
+                               float* weights, int32_t* tok_idx, cudaStream_t st);
+
 // moek_abi.cu: record the calling thread's error message (read back by moek_last_error) and return code
 int set_error(int code, const char* fmt, ...);
 

@@ -153,6 +153,45 @@ def combine(rows: torch.Tensor, top_k: int, out: torch.Tensor = None) -> torch.T
     return out
 
 
+# ------------------------------------------------------------------------------------------------------ router
+def fused_topk(hidden_states: torch.Tensor, gating_output: torch.Tensor, topk: int, renormalize: bool,
+               indices_type=None, scoring_func: str = "softmax"):
+    """vLLM's ``fused_topk`` (vllm/.../router/fused_topk_router.py:69-108) on this build's router kernel:
+    (topk_weights fp32 [M, k], topk_ids int32 (or ``indices_type``) [M, k], token_expert_indices int32 [M, k])."""
+    if scoring_func != "softmax":
+        raise MoekError(f"moek_b200: router scoring {scoring_func!r} is not supported (softmax only)")
+    if hidden_states.shape[0] != gating_output.shape[0]:
+        raise MoekError("moek_b200: number of tokens mismatch between hidden states and router logits")
+    w, ids, tei = router_topk(gating_output, topk, renormalize, with_indices=True)
+    if indices_type is not None and indices_type != torch.int32:
+        ids = ids.to(indices_type)
+    return w, ids, tei
+
+
+def router_topk(logits: torch.Tensor, top_k: int, renormalize: bool = True, with_indices: bool = False):
+    """softmax -> top-k -> renormalise on the GPU: (weights fp32 [M, k], ids int32 [M, k][, token_expert_indices])."""
+    _need_cuda(logits)
+    if logits.dtype not in (torch.float32, torch.bfloat16):
+        logits = logits.float()
+    logits = logits.contiguous()
+    m, e = logits.shape
+    dev = logits.device
+    ids = torch.empty((m, top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((m, top_k), dtype=torch.float32, device=dev)
+    tei = torch.empty((m, top_k), dtype=torch.int32, device=dev) if with_indices else None
+    call("moek_router_topk", _ptr(logits), int(logits.dtype == torch.bfloat16), m, e, top_k, int(renormalize),
+         _ptr(ids), _ptr(w), _ptr(tei), _stream(dev))
+    return (w, ids, tei) if with_indices else (w, ids)
+
+
+def fused_moe_from_logits(hidden_states: torch.Tensor, layer: PreparedLayer, router_logits: torch.Tensor,
+                          top_k: int, renormalize: bool = True, output: torch.Tensor = None) -> torch.Tensor:
+    """Router + routed-expert layer: ``fused_moe`` on the router kernel's ids and weights (two launches, the second
+    ordered behind the first by programmatic dependent launch)."""
+    w, ids = router_topk(router_logits, top_k, renormalize)
+    return fused_moe(hidden_states, layer, w, ids, output=output)
+
+
 # ----------------------------------------------------------------------------------------------------- forward
 DECODE_MAX_M = int(os.environ.get("MOEK_B200_DECODE_MAX_M", "64"))  # split-k with fused epilogues up to this M
 
