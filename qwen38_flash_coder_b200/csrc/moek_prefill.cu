@@ -29,8 +29,8 @@
 //               gathers) into the 128-byte-swizzled B tile of the stage; rows past the block's valid ones read out of
 //               bounds and arrive as zeros.
 //   scales    = warp 7: per unit the (B | R) table of the expert's scale bytes (moek_common.cuh) and the unit's
-//               exception lists; per stage the scale byte of each of the 256 rows x 4 k-groups (base + 4-bit offset,
-//               then the exceptions), one 32-bit word per row.
+//               exception lists (held in registers, loaded one unit ahead); per stage the scale byte of each of the
+//               256 rows x 4 k-groups (base + 4-bit offset, then the exceptions), one 32-bit word per row.
 //   dequant   = warps 8-23, two groups of eight taking alternate stages (a stage's dequant is a chain of shared-
 //               memory loads, table lookups, bf16 FMAs and a tcgen05.st + wait, so two stages in flight hide half
 //               of its latency): warp 8 + 8s + 4h + i owns rows 128h + 32q .. +31 of the item, q = warp % 4 (its TMEM
@@ -81,11 +81,8 @@ constexpr int TBL_BYTES = ITEM_COLS * 4;  // one scale word (4 k-groups) per row
 constexpr int W_SLOT = STAGE_BYTES + PAIR_BYTES + TBL_BYTES;
 constexpr int W_OFF = B_OFF + NB * B_BYTES;
 constexpr int S_REL = STAGE_BYTES, TBL_REL = STAGE_BYTES + PAIR_BYTES;
-constexpr int EXC_CAP = 2048;  // exception entries of one unit cached in shared memory
 constexpr int LUT_OFF = W_OFF + NW * W_SLOT;                     // 2 x 256 (B | R) words (units alternate)
-constexpr int EXC_OFF = LUT_OFF + 2 * 256 * 4;                   // EXC_CAP entries (scale warp only)
-constexpr int RUNOFF_OFF = EXC_OFF + EXC_CAP * 4;                // 33 run offsets (scale warp only)
-constexpr int IDS_OFF = (RUNOFF_OFF + 33 * 4 + 15) / 16 * 16;    // 128 activation rows per loader warp
+constexpr int IDS_OFF = LUT_OFF + 2 * 256 * 4;                   // 128 activation rows per loader warp
 constexpr int MISC_OFF = IDS_OFF + NLOAD * BMP * 4;              // tmem base, abort flag
 constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
 constexpr int NBARS = 3 * NW + 2 * NB + 2 * NA + 2 + 2;
@@ -290,8 +287,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == W_PROD) {  // ---------------------------------------------------------------------- producer
     uint32_t g = 0;
     bool ok = true;
+    UnitInfo nx = blockIdx.x < nunits ? unit_info(p, blockIdx.x, nt) : UnitInfo{0, 0, -1};  // one unit ahead
     for (int64_t u = blockIdx.x; u < nunits && ok && !*abort_flag; u += gridDim.x) {
-      const UnitInfo ui = unit_info(p, u, nt);
+      const UnitInfo ui = nx;
+      if (u + gridDim.x < nunits) nx = unit_info(p, u + gridDim.x, nt);
       if (ui.e < 0 || ui.e >= p.E) continue;
       for (int st = 0; st < nstage; st++, g++) {
         const int s = g % NW;
@@ -410,31 +409,45 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
     }
   } else if (warp == W_SCALE) {  // ------------------------------------------------------------------ scale words
-    uint32_t* excs = reinterpret_cast<uint32_t*>(smem + EXC_OFF);
-    int* ro = reinterpret_cast<int*>(smem + RUNOFF_OFF);
+    // Per unit: the expert's global scale, the unit's run offsets (lane j: run j's first exception entry) and up to 64
+    // exception entries, held in registers and loaded one unit ahead, so that no unit starts behind a chain of
+    // dependent global loads. Per stage: the 4 k-group scale bytes of each row as one word, then the exceptions.
     const int run = lane >> 4, chk = lane & 15;  // this lane's 8 positions: run `run`, positions 8 chk .. 8 chk + 7
     int rows[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) rows[i] = run * 128 + position_slot(8 * chk + i);
+    auto next_valid = [&](int64_t u2) -> int64_t {
+      for (; u2 < nunits; u2 += gridDim.x) {
+        const int e = unit_info(p, u2, nt).e;
+        if (e >= 0 && e < p.E) break;
+      }
+      return u2;
+    };
+    int ro_n = 0, end_n = 0;
+    float g_n = 0.f;
+    auto fetch = [&](int64_t u2) {  // loads only: consumed when the unit starts
+      const UnitInfo v = unit_info(p, u2, nt);
+      const int64_t key0 = ((int64_t)v.e * nt + v.item) * nb;
+      ro_n = lane < nb ? p.exc_off[key0 + lane] : 0;
+      end_n = p.exc_off[key0 + nb];
+      g_n = p.G[v.e];
+    };
     uint32_t g = 0, un = 0;
-    for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
+    int64_t u = next_valid(blockIdx.x);
+    if (u < nunits) fetch(u);
+    while (u < nunits && !*abort_flag) {
       const UnitInfo ui = unit_info(p, u, nt);
-      if (ui.e < 0 || ui.e >= p.E) continue;
       const int lb = un & 1;
-      const int64_t key0 = ((int64_t)ui.e * nt + ui.item) * nb;
-      const int o0 = p.exc_off[key0];
-      __syncwarp();  // the previous unit's exception lists are no longer read
-      for (int j = lane; j <= nb; j += 32) ro[j] = p.exc_off[key0 + j] - o0;
-      __syncwarp();
-      const int nexc = ro[nb];
-      const bool exc_smem = nexc <= EXC_CAP;
-      if (exc_smem)
-        for (int j = lane; j < nexc; j += 32) excs[j] = p.exc_ent[o0 + j];
-      const uint32_t* exl = exc_smem ? excs : p.exc_ent + o0;
+      const int o0 = __shfl_sync(0xffffffffu, ro_n, 0);
+      const int ro = ro_n - o0, cnt = end_n - o0;
+      const float gsc = g_n;
+      const uint32_t* eg = p.exc_ent + o0;
+      const uint32_t ex0 = lane < cnt ? eg[lane] : 0u, ex1 = lane + 32 < cnt ? eg[lane + 32] : 0u;
+      const int64_t u_next = next_valid(u + gridDim.x);
+      if (u_next < nunits) fetch(u_next);
       const int r0g = p.gate_up ? ui.item : 2 * ui.item;
       // the (B | R) table of this expert, once the dequant warps finished the unit that used this buffer last
       if (un >= 2 && !wait_warp(B.lutempty + lb, ((un >> 1) - 1) & 1, deadline, p.err, abort_flag)) break;
-      const float gsc = p.G[ui.e];
 #pragma unroll
       for (int j = 0; j < 8; j++) lut[lb * 256 + lane + 32 * j] = scale_word(lane + 32 * j, gsc);
       __syncwarp();
@@ -464,19 +477,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           tbl[rows[i]] = prmt(prmt(src[0], src[1], sel), prmt(src[2], src[3], sel), 0x5410);
         }
         __syncwarp();
+        // exceptions of this stage's run (rn) whose k-group falls in this stage's half overwrite their bytes
         const int rn = st >> 1;
-        for (int j = ro[rn] + lane; j < ro[rn + 1]; j += 32) {
-          const uint32_t en = exl[j];
+        const int eo0 = __shfl_sync(0xffffffffu, ro, rn);
+        const int eo1 = rn + 1 < nb ? __shfl_sync(0xffffffffu, ro, rn + 1) : cnt;
+        auto patch = [&](uint32_t en) {
           const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-          if ((kg >> 2) != (st & 1)) continue;
+          if ((kg >> 2) != (st & 1)) return;
           const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
           reinterpret_cast<uint8_t*>(tbl)[row * 4 + (kg & 3)] = (uint8_t)(en >> 24);
-        }
+        };
+        if (lane >= eo0 && lane < eo1) patch(ex0);
+        if (lane + 32 >= eo0 && lane + 32 < eo1) patch(ex1);
+        for (int j = max(eo0, 64) + lane; j < eo1; j += 32) patch(eg[j]);  // long lists: the rest from memory
         __syncwarp();
         if (lane == 0) mbar_arrive(B.sfull + s);
       }
       if (!ok) break;
       un++;
+      u = u_next;
     }
   } else if (warp < EPI0) {  // ------------------------------------------------------------------- dequant
     const int dw = warp - DQ0, h = (dw >> 2) & 1, grp = dw >> 3, q = warp & 3;
@@ -484,9 +503,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int sw = ((row >> 2) & 1) << 4;     // byte offset of the row's first 16-byte half (swizzle)
     const uint32_t t_row = tmem + ((uint32_t)(32 * q) << 16) + A_COL0 + 32 * h;
     uint32_t g = 0, un = 0;
+    // the next unit's expert is loaded one unit ahead (only its validity is needed here)
+    int e_next = blockIdx.x < nunits ? unit_info(p, blockIdx.x, nt).e : -1;
     for (int64_t u = blockIdx.x; u < nunits; u += gridDim.x) {
-      const UnitInfo ui = unit_info(p, u, nt);
-      if (ui.e < 0 || ui.e >= p.E) {
+      const int e = e_next;
+      e_next = u + gridDim.x < nunits ? unit_info(p, u + gridDim.x, nt).e : -1;
+      if (e < 0 || e >= p.E) {
         if (dw == 0 && lane == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
         continue;
       }
