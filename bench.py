@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", action="store_true", help="measure the chosen workload only")
+    ap.add_argument("--ep-exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1, fixed-capacity workloads: exchange over peer memory or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -490,10 +492,14 @@ def ep_main(a, rank, world, dev):
         wl = EP_WORKLOADS[name]
         m = wl["m"]
 
-        def step(be=None, name=name, wl=wl):
+        # fixed-capacity workloads exchange over peer memory (CUDA IPC blocks, this build's kernels) unless asked
+        # for NCCL; exact-count workloads use NCCL all-to-allv
+        px = ep.PeerExchange(None, m, H, TOPK, dev) if wl["capacity"] and a.ep_exchange == "peer" else None
+
+        def step(be=None, name=name, wl=wl, px=px):
             for e in layers:
                 ids, wts = e["route"][name]
-                ep.ep_moe(e["x"][name], e["layer"], wts, ids, backend=be, capacity=wl["capacity"])
+                ep.ep_moe(e["x"][name], e["layer"], wts, ids, backend=be, capacity=wl["capacity"], peer=px)
 
         for _ in range(max(3, a.warmup)):
             step()
@@ -554,7 +560,8 @@ def ep_main(a, rank, world, dev):
                 gbpl = sum(gb) / max(1, len(gb))
                 peak = peaks.get("hbm_gbs", 6650.0)
                 ach = gbpl / (kus / 1e6) / 1e9
-                roof = {"kernel": "moek_layer_kernel (the local experts' whole layer on the received rows)"
+                roof = {"kernel": "moek_layer_kernel (the local experts' whole layer on the received rows; timed "
+                                  "alone, writing the fp32 rows locally)"
                         if kind == "layer" else "moek_prefill_kernel (gate_up of the local experts on the received rows)",
                         "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
                         "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks
@@ -574,7 +581,12 @@ def ep_main(a, rank, world, dev):
                         "avg_launch_us": round(kus, 2), "rank": "this rank's gate launches, max over ranks"}
         res["roofline"] = roof
         del rec
-        per_layer = 4 + (ops.LAUNCHES_PER_LAYER if m <= ops.DECODE_MAX_M else 5)  # plan, pack, partial, unpack
+        rows_local = world * m if wl["capacity"] else m  # received rows per rank (exact counts: about m)
+        local = ops.launches_per_layer(rows_local, TOPK) - (0 if ops._decode_path(rows_local, TOPK) else 1)
+        if px is not None and ops.layer_p2p_fits(rows_local, TOPK):
+            per_layer = 3  # dispatch, the whole-layer kernel on the receive segments, unpack
+        else:  # plan + pack or dispatch + wait, the local layer's kernels (no top-k sum), partial or combine, unpack
+            per_layer = 4 + local
         res["gpu_launches_per_step"] = per_layer * len(layers)
         if name == names[0]:
             # e2e: inputs copied from pinned host memory and the outputs read back, every layer, every step
@@ -588,7 +600,7 @@ def ep_main(a, rank, world, dev):
                     dx = hx[l].to(dev, non_blocking=True)
                     did = hid[l].to(dev, non_blocking=True)
                     dw = hw[l].to(dev, non_blocking=True)
-                    o = ep.ep_moe(dx, e["layer"], dw, did, capacity=wl["capacity"])
+                    o = ep.ep_moe(dx, e["layer"], dw, did, capacity=wl["capacity"], peer=px)
                     hout[l].copy_(o, non_blocking=True)
 
             e2e_step()
@@ -598,6 +610,11 @@ def ep_main(a, rank, world, dev):
                                                     for x, r, w in zip(hx, hid, hw)),
                           "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
                           "api": "ep.ep_moe with host copies (per rank; value over all ranks)"}
+        fused = px is not None and ops.layer_p2p_fits(rows_local, TOPK)
+        res["exchange"] = ("peer memory (CUDA IPC; " + ("dispatch, whole-layer kernel returning the partials, unpack)"
+                           if fused else "dispatch / combine kernels)") if px is not None else "NCCL")
+        if px is not None:
+            px.close()
         results[name] = res
     head = results.pop(names[0])
     if rank == 0:
@@ -609,7 +626,8 @@ def ep_main(a, rank, world, dev):
                        "hidden": H, "inter": I, "top_k": TOPK, "tokens_per_gpu": EP_WORKLOADS[names[0]]["m"],
                        "weights": "NVFP4 (E2M1 + E4M3/16 + fp32 global), bf16 activations",
                        "l2": f"{a.layers} distinct layers per step rotate; touched weights >> 126 MB L2",
-                       "parallelism": f"ep{world}: experts split contiguously, tokens per rank, NCCL all-to-all"},
+                       "parallelism": f"ep{world}: experts split contiguously, tokens per rank, "
+                                      f"{head['exchange']} exchange"},
             "us_per_layer": head["us_per_layer"], "roofline": head["roofline"], "cpu_baseline": None,
             "e2e": head["e2e"], "clocks": head["clocks"],
             "gpu_launches": head["gpu_launches_per_step"] * a.steps, "launch": head["launch"], "workloads": results,

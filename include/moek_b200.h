@@ -2,7 +2,8 @@
  *
  * C ABI of libmoek_b200.so. Every function takes plain device pointers, element counts and a cudaStream_t (as
  * void*), launches asynchronously on that stream and returns MOEK_OK or an error code; moek_last_error() returns the
- * calling thread's last message. The caller allocates every buffer (the library allocates nothing). Reference paths
+ * calling thread's last message. The caller allocates every buffer (the library allocates nothing except through
+ * moek_ipc_malloc, the expert-parallel exchange block that must be a whole allocation to be shared). Reference paths
  * are relative to the Alssndr0/qwen38-flash-coder project; "vllm/..." paths point into vLLM's Python sources.
  *
  * Tensor formats (produced at load time by qwen38_flash_coder_b200.prep):
@@ -151,11 +152,16 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  * (g, u) = gate_up_e(x[t]) in fp32, e = topk_ids[t, j] in [0, E) (other ids are not routed; a token with none gets
  * zeros), the weights dequantised as the oracle does (bf16(e2m1 * s * gs)). With out = NULL and out_rows set, the
  * fp32 rows [M * top_k, H] = topk_w * down_e(...) are written instead (rows of unrouted slots are left as they were).
- *   x       bf16 [M, H]; M <= 96 and M * top_k <= 512 (decode batches; larger ones take the moek_gemm path).
+ *   x       bf16 [M, H]; M * top_k <= 512 (decode batches; larger ones take the moek_gemm path).
  *   w13/sp13/g13/exc_off13/exc_ent13  gate_up in the tiled formats above (N = 2I, K = H); w2.. likewise (N = H,
  *           K = I). H % 256 == 0, I % 128 == 0, both <= 4096.
  *   nsplit_gate, nsplit_down  k-splits per 256-row item; (K/64/nsplit) even.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
+/* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: the batch's size up to 16, else 32).
+ * An expert with more routed slots than that is cut into several blocks, its weights streamed once per block.
+ * Process-wide; a tuning knob with no effect on the results. */
+int moek_set_layer_block_rows(int32_t rows);
+
 int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
                    const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13, const float* g13,
                    const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2, const uint8_t* sp2,
@@ -193,6 +199,47 @@ int moek_ep_partial(const float* rows, const int32_t* meta, int64_t meta_stride,
  * out bf16 [M, H] = bf16(sum over d = 0..world-1 with pos >= 0 of back[offsets[d] + pos[t*world + d]]). */
 int moek_ep_unpack(const float* back, const int32_t* pos, const int32_t* offsets, int32_t M, int32_t H,
                    int32_t world, void* out, void* stream);
+
+/* ---- Expert parallelism over peer memory (the fixed-capacity decode exchange without a collective library; no
+ * counterpart in the reference, like the rest of EP). Each rank allocates one exchange block of moek_ep_p2p_layout's
+ * total bytes with moek_ipc_malloc (zeroed; a whole cudaMalloc allocation, so that CUDA IPC can share it), shares it
+ * with moek_ipc_handle / moek_ipc_open, and passes `peer`, a device array of every rank's block base (its own
+ * included). With R = world * mcap rows (segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent),
+ * moek_ep_p2p_layout gives the byte offsets of: received rows bf16 [R, H], their local expert ids int32 [R, top_k]
+ * (-1: slot owned elsewhere, or unused row), router weights fp32 [R, top_k], returned partials fp32 [R, H], flags
+ * int32 [2 world], arrival counters int32 [2 world], and the total. Per layer call, on one stream, every rank runs:
+ *   moek_ep_dispatch_p2p (plans the token order itself, writes pos [M, world] for the unpack, and copies rows, ids
+ *   and weights straight into the owners' receive segments), then either
+ *     moek_moe_layer_p2p (R * top_k <= 512: the whole-layer kernel waits for the receive flags itself and writes
+ *     each row's fp32 partial straight into its sender's back segment), or
+ *     moek_ep_wait(own flags), the local layer on the receive rows (fp32 slot rows), moek_ep_combine_p2p,
+ *   then moek_ep_unpack_p2p (waits for every rank's partials, sums them in rank order, rounds once to bf16).
+ * The flags hand each segment over and back and leave themselves ready for the next call, so the sequence can be
+ * captured in a CUDA graph. Waits are bounded (moek_set_wait_timeout_ns) and record MOEK_DEV_TIMEOUT in err.
+ * mcap <= 1024 tokens per rank and call. */
+int moek_ipc_malloc(size_t bytes, void** ptr);
+int moek_ipc_free(void* ptr);
+int moek_ipc_handle(void* ptr, void* handle64);
+int moek_ipc_open(const void* handle64, void** ptr);
+int moek_ipc_close(void* ptr);
+/* offsets7: x, ids, w, back, flags, counters, total (bytes). */
+int moek_ep_p2p_layout(int32_t world, int32_t mcap, int32_t H, int32_t top_k, int64_t* offsets7);
+int moek_ep_dispatch_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H, int32_t top_k,
+                         const void* x, const int32_t* topk_ids, const float* topk_w, int32_t M, int32_t num_experts,
+                         int32_t* pos, int32_t* err, void* stream);
+int moek_ep_wait(const int32_t* flags, int32_t world, int32_t* err, void* stream);
+int moek_ep_combine_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H, int32_t top_k,
+                        const float* rows, int32_t local_experts, int32_t* err, void* stream);
+int moek_ep_unpack_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H, int32_t top_k,
+                       const int32_t* pos, int32_t M, void* out, int32_t* err, void* stream);
+/* The whole-layer kernel on this rank's receive segments (own = this rank's block), the same arguments as
+ * moek_moe_layer otherwise; its rows' fp32 partials go straight to the senders' back segments. */
+int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap, int32_t H,
+                       int32_t I, int32_t local_experts, int32_t top_k, const void* w13, const uint8_t* sp13,
+                       const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
+                       const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
+                       int32_t nsplit_gate, int32_t nsplit_down, void* workspace, size_t workspace_bytes,
+                       int32_t* state, int64_t state_ints, int32_t* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -10,6 +10,7 @@ SIGNATURES = {
     "moek_last_error": (ctypes.c_char_p, []),
     "moek_version": (ctypes.c_int, []),
     "moek_set_wait_timeout_ns": (ctypes.c_int, [_U64]),
+    "moek_set_layer_block_rows": (ctypes.c_int, [_I32]),
     "moek_align_workspace_bytes": (ctypes.c_int, [_I64, _I32, ctypes.POINTER(ctypes.c_size_t)]),
     "moek_align": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P, ctypes.c_size_t, _P]),
     "moek_align_noalloc": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P]),
@@ -27,6 +28,18 @@ SIGNATURES = {
                                     _P]),
     "moek_ep_partial": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "moek_ep_unpack": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _P, _P]),
+    "moek_ipc_malloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "moek_ipc_free": (ctypes.c_int, [_P]),
+    "moek_ipc_handle": (ctypes.c_int, [_P, _P]),
+    "moek_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "moek_ipc_close": (ctypes.c_int, [_P]),
+    "moek_ep_p2p_layout": (ctypes.c_int, [_I32] * 4 + [_P]),
+    "moek_ep_dispatch_p2p": (ctypes.c_int, [_P] + [_I32] * 5 + [_P] * 3 + [_I32, _I32, _P, _P, _P]),
+    "moek_ep_wait": (ctypes.c_int, [_P, _I32, _P, _P]),
+    "moek_ep_combine_p2p": (ctypes.c_int, [_P] + [_I32] * 5 + [_P, _I32, _P, _P]),
+    "moek_ep_unpack_p2p": (ctypes.c_int, [_P] + [_I32] * 5 + [_P, _I32, _P, _P, _P]),
+    "moek_moe_layer_p2p": (ctypes.c_int, [_P, _P] + [_I32] * 7 + [_P] * 10 + [_I32, _I32, _P, ctypes.c_size_t, _P,
+                                                                              _I64, _P, _P]),
 }
 
 _lib = None

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdarg>
+#include <cstring>
 
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
@@ -222,15 +223,16 @@ MOEK_API int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M
 }
 
 // ------------------------------------------------------------------------------------- whole decode layer
-// Persistent int32 state of moek_moe_layer: [epoch, done, cnt1, rcnt, ready, cnt2, tok]. The layout depends only on
-// (E, H, I), so one zeroed state buffer serves every call of that geometry.
+// Persistent int32 state of moek_moe_layer: [epoch, done, ep, cnt1, rcnt, ready, cnt2, tok]. The layout depends only
+// on (E, H, I), so one zeroed state buffer serves every call of that geometry.
 struct LayerLayout {
   int64_t cnt1, rcnt, ready, cnt2, tok, total;
 };
 static LayerLayout layer_layout(int32_t E, int32_t H, int32_t I) {
-  const int64_t nbmax = std::min<int64_t>(E, moek::LAYER_MAXIDS), nt1 = 2 * (int64_t)I / 256, nt2 = H / 256;
+  // blocks: at most one per routed slot (an expert with more slots than a block takes spans several)
+  const int64_t nbmax = moek::LAYER_MAXIDS, nt1 = 2 * (int64_t)I / 256, nt2 = H / 256;
   LayerLayout l;
-  l.cnt1 = 2;
+  l.cnt1 = 3;
   l.rcnt = l.cnt1 + nbmax * nt1 * 8;
   l.ready = l.rcnt + nbmax * nt1;
   l.cnt2 = l.ready + nbmax * nt1;
@@ -258,20 +260,33 @@ MOEK_API int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int
   return MOEK_OK;
 }
 
-MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
-                            const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13,
-                            const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
-                            const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
-                            int32_t nsplit_gate, int32_t nsplit_down, void* workspace, size_t workspace_bytes,
-                            int32_t* state, int64_t state_ints, int32_t* err, void* out, float* out_rows,
-                            void* stream) {
-  if (M == 0) return MOEK_OK;
+// Rows per block of the whole-layer kernel (8, 16 or 32): the batch's size up to 16, else 32, unless set.
+static int g_layer_rows = 0;
+MOEK_API int moek_set_layer_block_rows(int32_t rows) {
+  if (rows != 0 && rows != 8 && rows != 16 && rows != 32)
+    return fail(MOEK_ERR_ARG, "moek_b200: layer block rows must be 8, 16, 32 or 0 (automatic), got %d", rows);
+  g_layer_rows = rows;
+  return MOEK_OK;
+}
+static int layer_block_rows(int M) {
+  if (g_layer_rows) return g_layer_rows;
+  return M <= 8 ? 8 : M <= 16 ? 16 : 32;
+}
+
+// Checks and parameters shared by moek_moe_layer and moek_moe_layer_p2p (rows_ws: the fp32 slot rows live in the
+// workspace, i.e. the caller does not take them).
+static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t H, int32_t I, int32_t E,
+                        const int32_t* topk_ids, const float* topk_w, int32_t top_k, const void* w13,
+                        const uint8_t* sp13, const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13,
+                        const void* w2, const uint8_t* sp2, const float* g2, const int32_t* exc_off2,
+                        const int32_t* exc_ent2, int32_t nsplit_gate, int32_t nsplit_down, void* workspace,
+                        size_t workspace_bytes, int32_t* state, int64_t state_ints, int32_t* err, bool rows_ws) {
   if (M < 0 || top_k <= 0 || top_k > 32 || E <= 0 || H <= 0 || I <= 0)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer bad sizes (M %d, top_k %d, E %d, H %d, I %d)", M, top_k, E, H, I);
   const int64_t num_ids = (int64_t)M * top_k;
-  if (num_ids > moek::LAYER_MAXIDS || M > 96)
-    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_layer serves decode batches of <= 96 tokens and <= %d slots "
-                                      "(got M %d, top_k %d)", moek::LAYER_MAXIDS, M, top_k);
+  if (num_ids > moek::LAYER_MAXIDS)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_layer serves decode batches of <= %d routed slots (got M %d, "
+                                      "top_k %d)", moek::LAYER_MAXIDS, M, top_k);
   if (H % 256 || I % 128 || H / 128 > 32 || I / 128 > 32)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer needs H %% 256 == 0, I %% 128 == 0, H and I <= 4096 (H %d, I %d)",
                 H, I);
@@ -280,18 +295,17 @@ MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int3
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer k-splits (%d, %d) must cut H/128 = %d and I/128 = %d into whole "
                               "runs", nsplit_gate, nsplit_down, H / 128, I / 128);
   if (!x || !topk_ids || !topk_w || !w13 || !sp13 || !g13 || !exc_off13 || !exc_ent13 || !w2 || !sp2 || !g2 ||
-      !exc_off2 || !exc_ent2 || !state || !err || (!out && !out_rows))
+      !exc_off2 || !exc_ent2 || !state || !err)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer null pointer");
-  if (out && out_rows) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer writes either out (bf16 sums) or out_rows");
   const LayerLayout lay = layer_layout(E, H, I);
   if (state_ints < lay.total)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer state needs %lld int32 (zeroed once)", (long long)lay.total);
-  const int64_t ws = layer_ws_bytes(num_ids, H, I, nsplit_gate, nsplit_down, out != nullptr);
+  const int64_t ws = layer_ws_bytes(num_ids, H, I, nsplit_gate, nsplit_down, rows_ws);
   if ((int64_t)workspace_bytes < ws || !workspace)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer needs %lld workspace bytes", (long long)ws);
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
   uint8_t* wp = static_cast<uint8_t*>(workspace);
-  moek::LayerParams p{};
+  p = moek::LayerParams{};
   p.act = reinterpret_cast<__nv_bfloat16*>(wp);
   wp += up(num_ids * I * 2);
   if (nsplit_gate > 1) {
@@ -302,7 +316,7 @@ MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int3
     p.part2 = reinterpret_cast<float*>(wp);
     wp += up((int64_t)nsplit_down * num_ids * H * 4);
   }
-  if (out) p.rows = reinterpret_cast<float*>(wp);
+  if (rows_ws) p.rows = reinterpret_cast<float*>(wp);
   const moek::LayerMat m1{static_cast<const uint8_t*>(w13), sp13, g13, exc_off13,
                           reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1, nsplit_gate};
   const moek::LayerMat m2{static_cast<const uint8_t*>(w2), sp2, g2, exc_off2,
@@ -312,8 +326,6 @@ MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int3
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.ids = topk_ids;
   p.tw = topk_w;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.out_rows = out_rows;
   p.ctr = state;
   p.err = err;
   p.timeout_ns = g_timeout_ns;
@@ -325,12 +337,146 @@ MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int3
   p.I = I;
   p.off_epoch = 0;
   p.off_done = 1;
+  p.off_ep = 2;
   p.off_cnt1 = (int)lay.cnt1;
   p.off_rcnt = (int)lay.rcnt;
   p.off_ready = (int)lay.ready;
   p.off_cnt2 = (int)lay.cnt2;
   p.off_tok = (int)lay.tok;
-  return cuda_status(moek::launch_layer(p, M, sm_count(), (cudaStream_t)stream), "moe_layer launch");
+  return MOEK_OK;
+}
+
+MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
+                            const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13,
+                            const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
+                            const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
+                            int32_t nsplit_gate, int32_t nsplit_down, void* workspace, size_t workspace_bytes,
+                            int32_t* state, int64_t state_ints, int32_t* err, void* out, float* out_rows,
+                            void* stream) {
+  if (M == 0) return MOEK_OK;
+  moek::LayerParams p;
+  if (int rc = layer_params(p, x, M, H, I, E, topk_ids, topk_w, top_k, w13, sp13, g13, exc_off13, exc_ent13, w2, sp2,
+                            g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down, workspace, workspace_bytes, state,
+                            state_ints, err, out != nullptr))
+    return rc;
+  if (!out && !out_rows) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer null pointer");
+  if (out && out_rows) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer writes either out (bf16 sums) or out_rows");
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_rows = out_rows;
+  return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), (cudaStream_t)stream),
+                     "moe_layer launch");
+}
+
+// ------------------------------------------------------------------------- EP peer-memory exchange (fixed capacity)
+MOEK_API int moek_ipc_malloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(MOEK_ERR_ARG, "moek_b200: ipc_malloc needs a size and an output pointer");
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  return cuda_status(e, "ipc_malloc");
+}
+MOEK_API int moek_ipc_free(void* ptr) { return cuda_status(cudaFree(ptr), "ipc_free"); }
+MOEK_API int moek_ipc_handle(void* ptr, void* handle64) {
+  if (!ptr || !handle64) return fail(MOEK_ERR_ARG, "moek_b200: ipc_handle null pointer");
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e == cudaSuccess) memcpy(handle64, &h, sizeof(h));
+  return cuda_status(e, "ipc_handle");
+}
+MOEK_API int moek_ipc_open(const void* handle64, void** ptr) {
+  if (!ptr || !handle64) return fail(MOEK_ERR_ARG, "moek_b200: ipc_open null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "ipc_open");
+}
+MOEK_API int moek_ipc_close(void* ptr) { return cuda_status(cudaIpcCloseMemHandle(ptr), "ipc_close"); }
+
+static int p2p_args(moek::P2PArgs& a, const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H,
+                    int32_t k, int32_t* err) {
+  if (!peer || !err || world < 1 || world > moek::EP_MAX_WORLD || rank < 0 || rank >= world || mcap < 0 ||
+      mcap > moek::EP_P2P_MAXM || H <= 0 || H % 8 || k <= 0 || k > 32)
+    return fail(MOEK_ERR_ARG, "moek_b200: EP peer exchange bad arguments (world %d, rank %d, mcap %d, H %d, k %d)",
+                world, rank, mcap, H, k);
+  a = moek::P2PArgs{peer, moek::p2p_layout(world, mcap, H, k), world, rank, mcap, H, k, err, g_timeout_ns};
+  return MOEK_OK;
+}
+
+MOEK_API int moek_ep_p2p_layout(int32_t world, int32_t mcap, int32_t H, int32_t top_k, int64_t* offsets7) {
+  if (!offsets7 || world < 1 || world > moek::EP_MAX_WORLD || mcap < 0 || mcap > moek::EP_P2P_MAXM || H <= 0 ||
+      H % 8 || top_k <= 0 || top_k > 32)
+    return fail(MOEK_ERR_ARG, "moek_b200: EP peer exchange layout bad arguments (world %d, mcap %d, H %d, k %d)",
+                world, mcap, H, top_k);
+  const moek::P2PLayout l = moek::p2p_layout(world, mcap, H, top_k);
+  const int64_t v[7] = {l.x, l.ids, l.w, l.back, l.flags, l.ctr, l.total};
+  memcpy(offsets7, v, sizeof(v));
+  return MOEK_OK;
+}
+
+MOEK_API int moek_ep_dispatch_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H,
+                                  int32_t top_k, const void* x, const int32_t* topk_ids, const float* topk_w, int32_t M,
+                                  int32_t num_experts, int32_t* pos, int32_t* err, void* stream) {
+  moek::P2PArgs a;
+  if (int rc = p2p_args(a, peer, world, rank, mcap, H, top_k, err)) return rc;
+  if (M < 0 || M > mcap || num_experts <= 0 || num_experts % world || (M && (!x || !topk_ids || !topk_w || !pos)))
+    return fail(MOEK_ERR_ARG, "moek_b200: EP dispatch needs 0 <= M <= mcap and experts split evenly (M %d, E %d)", M,
+                num_experts);
+  return cuda_status(moek::launch_ep_dispatch_p2p(a, static_cast<const __nv_bfloat16*>(x), topk_ids, topk_w, M,
+                                                  num_experts, pos, (cudaStream_t)stream),
+                     "ep dispatch launch");
+}
+
+MOEK_API int moek_ep_wait(const int32_t* flags, int32_t world, int32_t* err, void* stream) {
+  if (!flags || !err || world < 1 || world > moek::EP_MAX_WORLD)
+    return fail(MOEK_ERR_ARG, "moek_b200: EP wait bad arguments");
+  return cuda_status(moek::launch_ep_wait(flags, world, err, g_timeout_ns, (cudaStream_t)stream), "ep wait launch");
+}
+
+MOEK_API int moek_ep_combine_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H,
+                                 int32_t top_k, const float* rows, int32_t local_experts, int32_t* err, void* stream) {
+  moek::P2PArgs a;
+  if (int rc = p2p_args(a, peer, world, rank, mcap, H, top_k, err)) return rc;
+  if ((mcap && !rows) || local_experts <= 0) return fail(MOEK_ERR_ARG, "moek_b200: EP combine bad arguments");
+  return cuda_status(moek::launch_ep_combine_p2p(a, rows, local_experts, (cudaStream_t)stream), "ep combine launch");
+}
+
+MOEK_API int moek_ep_unpack_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H,
+                                int32_t top_k, const int32_t* pos, int32_t M, void* out, int32_t* err, void* stream) {
+  moek::P2PArgs a;
+  if (int rc = p2p_args(a, peer, world, rank, mcap, H, top_k, err)) return rc;
+  if (M < 0 || M > mcap || (M && (!pos || !out))) return fail(MOEK_ERR_ARG, "moek_b200: EP unpack bad arguments");
+  return cuda_status(moek::launch_ep_unpack_p2p(a, pos, M, static_cast<__nv_bfloat16*>(out), (cudaStream_t)stream),
+                     "ep unpack launch");
+}
+
+MOEK_API int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap,
+                                int32_t H, int32_t I, int32_t local_experts, int32_t top_k, const void* w13,
+                                const uint8_t* sp13, const float* g13, const int32_t* exc_off13,
+                                const int32_t* exc_ent13, const void* w2, const uint8_t* sp2, const float* g2,
+                                const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                                int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state,
+                                int64_t state_ints, int32_t* err, void* stream) {
+  moek::P2PArgs a;
+  if (int rc = p2p_args(a, peer, world, rank, mcap, H, top_k, err)) return rc;
+  if (!own) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_p2p needs this rank's exchange block");
+  const int32_t R = world * mcap;
+  if (R == 0) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_p2p needs mcap > 0");
+  const uint8_t* blk = static_cast<const uint8_t*>(own);
+  moek::LayerParams p;
+  if (int rc = layer_params(p, blk + a.lay.x, R, H, I, local_experts, reinterpret_cast<const int32_t*>(blk + a.lay.ids),
+                            reinterpret_cast<const float*>(blk + a.lay.w), top_k, w13, sp13, g13, exc_off13, exc_ent13,
+                            w2, sp2, g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down, workspace, workspace_bytes,
+                            state, state_ints, err, true))
+    return rc;
+  p.ep_peer = peer;
+  p.ep_recv_flags = reinterpret_cast<const int*>(blk + a.lay.flags);
+  p.ep_back_off = a.lay.back;
+  p.ep_flags_off = a.lay.flags;
+  p.ep_world = world;
+  p.ep_rank = rank;
+  p.ep_mcap = mcap;
+  return cuda_status(moek::launch_layer(p, layer_block_rows(R), sm_count(), (cudaStream_t)stream),
+                     "moe_layer_p2p launch");
 }
 
 MOEK_API int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int32_t N, int32_t gate_up,

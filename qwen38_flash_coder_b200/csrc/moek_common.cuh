@@ -92,6 +92,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// ------------------------------------------------------------------------------ flags shared with other GPUs
+// int32 flags in peer-visible memory (CUDA IPC): system-scope acquire loads and release stores, bounded waits.
+__device__ __forceinline__ int ld_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool wait_flag(const int* p, int want, uint64_t deadline, int* err) {
+  for (uint32_t i = 0;; i++) {
+    if (ld_sys(p) == want) return true;
+    if ((i & 63) == 63 && globaltimer() > deadline) {
+      report(err, MOEK_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ bulk copies
 // Non-tensor bulk copy global -> this CTA's shared memory, completion counted on an mbarrier (no multicast).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -6,7 +6,8 @@
 // same gate_up / SwiGLU / down kernels on the rows it received, sums each row's local slots in fp32 and sends the
 // partial row back; the source rank adds the returned partials in rank order and rounds once to bf16. The byte
 // movement between ranks is NCCL's (all-to-allv through torch.distributed on the caller's stream); these kernels do
-// the index work and the row copies on each rank's own memory:
+// the index work and the row copies on each rank's own memory (the fixed-capacity exchange can instead run over peer
+// memory with this file's own kernels: the section "peer-memory exchange" below):
 //
 //   ep_plan     one CTA: for every destination rank, the position of each token in that rank's send segment
 //               (ascending token order, -1 when nothing goes there), the per-rank row counts and their offsets.
@@ -19,6 +20,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <algorithm>
 
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
@@ -169,6 +172,231 @@ cudaError_t launch_ep_unpack(const float* back, const int32_t* pos, const int32_
   const int64_t n = (int64_t)M * H;
   if (n == 0) return cudaSuccess;
   ep_unpack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(back, pos, offsets, M, H, world, out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------- peer-memory exchange (fixed capacity)
+// Every rank holds one exchange block (P2PLayout), shared by CUDA IPC; the kernels below write straight into the
+// peers' blocks over NVLink (plain stores, no multicast) and hand segments over with system-scope flags:
+//   dispatch  CTAs (d, g), G per destination d: reset my back flag d (its last reader, my previous unpack, is done),
+//             wait until d's receive flag for me is 0 (d's previous unpack is done, so d has finished reading what I
+//             sent last time), place my tokens in d's segment for me (ascending token order, as moek_ep_plan), copy
+//             rows g, g + G, ... with their slot ids (local id, or -1 for slots owned elsewhere) and router weights,
+//             mark the unused rows as having no valid slot; the last CTA of d fences and raises d's receive flag.
+//   wait      my receive flags all 1 (bounded); the whole-layer kernel does this wait itself.
+//   combine   CTAs (s, g): for the rows of receive segment s, the fp32 sum (slot order) of the row's local slots into
+//             s's back segment for me; the last CTA of s fences and raises s's back flag for me. No wait is needed
+//             before writing: s raised my receive flag after its previous unpack had read that back segment.
+//   unpack    wait until my back flags are all 1, clear my receive flags (this layer's readers of the receive
+//             segments, the local layer or combine, have completed), out[t] = bf16(sum over ranks d in order of
+//             back segment d's row for t).
+// Every wait is bounded by the caller's deadline; on expiry the kernel records MOEK_DEV_TIMEOUT and stops waiting.
+constexpr int P2P_THREADS = 256;
+
+__device__ __forceinline__ int* p2p_flags(const P2PArgs& q, int r) {
+  return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[r]) + q.lay.flags);
+}
+// The last of `n` arrivals on a self-resetting counter (one thread per CTA calls it, after its writes and a fence).
+__device__ __forceinline__ bool last_arrival(int* ctr, int n) {
+  if (n == 1) return true;
+  if (atomicAdd(ctr, 1) != n - 1) return false;
+  *ctr = 0;
+  return true;
+}
+
+__global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q, const uint4* __restrict__ x,
+                                                                      const int32_t* __restrict__ ids,
+                                                                      const float* __restrict__ topk_w, int M, int E,
+                                                                      int G, int32_t* __restrict__ pos) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int spos[EP_P2P_MAXM];
+  __shared__ int wcnt[P2P_THREADS / 32];
+  __shared__ int ok;
+  const int d = blockIdx.x / G, g = blockIdx.x - d * G, per = E / q.world, k = q.k;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int* my_flags = p2p_flags(q, q.rank);
+  int* d_flags = p2p_flags(q, d);
+  if (tid == 0) {
+    if (g == 0) my_flags[q.world + d] = 0;  // my back segment d is free again
+    ok = wait_flag(d_flags + q.rank, 0, globaltimer() + q.timeout_ns, q.err);
+  }
+  int count = 0;  // rows of mine that go to d
+  for (int t0 = 0; t0 < M; t0 += P2P_THREADS) {
+    const int t = t0 + tid;
+    bool has = false;
+    if (t < M)
+      for (int j = 0; j < k; j++) {
+        const int e = ids[(int64_t)t * k + j];
+        has |= e >= 0 && e < E && e / per == d;
+      }
+    const uint32_t b = __ballot_sync(0xffffffffu, has);
+    if (lane == 0) wcnt[warp] = __popc(b);
+    __syncthreads();
+    int before = count, chunk = 0;
+    for (int w = 0; w < P2P_THREADS / 32; w++) {
+      if (w < warp) before += wcnt[w];
+      chunk += wcnt[w];
+    }
+    if (t < M) spos[t] = has ? before + __popc(b & ((1u << lane) - 1u)) : -1;
+    count += chunk;
+    __syncthreads();  // wcnt is rewritten by the next chunk
+  }
+  __syncthreads();  // ok (also when M is 0)
+  if (g == 0)
+    for (int t = tid; t < M; t += P2P_THREADS) pos[(int64_t)t * q.world + d] = spos[t];
+  if (!ok) return;
+  uint8_t* blk = reinterpret_cast<uint8_t*>(q.peer[d]);
+  const int64_t row0 = (int64_t)q.rank * q.mcap;  // my segment in d's receive buffers
+  const int H16 = q.H / 8;
+  uint4* seg_x = reinterpret_cast<uint4*>(blk + q.lay.x) + row0 * H16;
+  int32_t* seg_ids = reinterpret_cast<int32_t*>(blk + q.lay.ids) + row0 * k;
+  float* seg_w = reinterpret_cast<float*>(blk + q.lay.w) + row0 * k;
+  for (int t = g; t < M; t += G) {
+    const int p = spos[t];
+    if (p < 0) continue;
+    uint4* dst = seg_x + (int64_t)p * H16;
+    const uint4* src = x + (int64_t)t * H16;
+    for (int c = tid; c < H16; c += P2P_THREADS) dst[c] = src[c];
+    if (tid < k) {
+      const int e = ids[(int64_t)t * k + tid];
+      const bool mine = e >= 0 && e < E && e / per == d;
+      seg_ids[(int64_t)p * k + tid] = mine ? e - d * per : -1;
+      seg_w[(int64_t)p * k + tid] = mine ? topk_w[(int64_t)t * k + tid] : 0.f;
+    }
+  }
+  for (int i = g * P2P_THREADS + tid; i < (q.mcap - count) * k; i += G * P2P_THREADS) {  // rows no token uses
+    seg_ids[(int64_t)count * k + i] = -1;
+    seg_w[(int64_t)count * k + i] = 0.f;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    int* ctr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[q.rank]) + q.lay.ctr) + d;
+    if (last_arrival(ctr, G)) {
+      __threadfence_system();
+      st_sys(d_flags + q.rank, 1);
+    }
+  }
+}
+
+__global__ void ep_wait_kernel(const int* __restrict__ flags, int world, int* err, uint64_t timeout_ns) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint64_t deadline = globaltimer() + timeout_ns;
+  for (int s = threadIdx.x; s < world; s += blockDim.x) wait_flag(flags + s, 1, deadline, err);
+}
+
+__global__ void __launch_bounds__(P2P_THREADS) ep_combine_p2p_kernel(P2PArgs q, const float* __restrict__ rows,
+                                                                     int E_local, int G) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int s = blockIdx.x / G, g = blockIdx.x - s * G, k = q.k;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(q.peer[q.rank]);
+  const int32_t* rid = reinterpret_cast<const int32_t*>(mine + q.lay.ids);
+  float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(q.peer[s]) + q.lay.back) +
+                (int64_t)q.rank * q.mcap * q.H;  // my segment in s's back buffer
+  const int H4 = q.H / 4;
+  for (int p = g; p < q.mcap; p += G) {
+    const int64_t r = (int64_t)s * q.mcap + p;  // the row's index in my receive buffers (and in rows)
+    bool any = false;
+    for (int j = 0; j < k; j++) any |= rid[r * k + j] >= 0 && rid[r * k + j] < E_local;
+    if (!any) continue;  // an unused row
+    for (int c = threadIdx.x; c < H4; c += P2P_THREADS) {
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < k; j++) {
+        const int e = rid[r * k + j];
+        if (e < 0 || e >= E_local) continue;
+        const float4 v = reinterpret_cast<const float4*>(rows + (r * k + j) * q.H)[c];
+        o.x += v.x;
+        o.y += v.y;
+        o.z += v.z;
+        o.w += v.w;
+      }
+      reinterpret_cast<float4*>(back + (int64_t)p * q.H)[c] = o;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    int* ctr = reinterpret_cast<int*>(mine + q.lay.ctr) + q.world + s;
+    if (last_arrival(ctr, G)) {
+      __threadfence_system();
+      st_sys(p2p_flags(q, s) + q.world + q.rank, 1);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, const int32_t* __restrict__ pos, int M,
+                                                                    __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int ok;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(q.peer[q.rank]);
+  int* my_flags = reinterpret_cast<int*>(mine + q.lay.flags);
+  if (threadIdx.x < 32) {
+    bool good = true;
+    const uint64_t deadline = globaltimer() + q.timeout_ns;
+    for (int s = threadIdx.x; s < q.world; s += 32) good &= wait_flag(my_flags + q.world + s, 1, deadline, q.err);
+    good = __all_sync(0xffffffffu, good);
+    if (threadIdx.x == 0) ok = good;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x < q.world) st_sys(my_flags + threadIdx.x, 0);  // the senders may write again
+  if (!ok) return;
+  const float4* back = reinterpret_cast<const float4*>(mine + q.lay.back);
+  const int H4 = q.H / 4;
+  for (int64_t i = (int64_t)blockIdx.x * P2P_THREADS + threadIdx.x; i < (int64_t)M * H4;
+       i += (int64_t)gridDim.x * P2P_THREADS) {
+    const int64_t t = i / H4;
+    const int c = (int)(i - t * H4);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < q.world; d++) {
+      const int p = pos[t * q.world + d];
+      if (p < 0) continue;
+      const float4 v = __ldcg(back + ((int64_t)d * q.mcap + p) * H4 + c);
+      o.x += v.x;
+      o.y += v.y;
+      o.z += v.z;
+      o.w += v.w;
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&lo);
+    w.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(out)[i] = w;
+  }
+}
+
+static int p2p_split(int rows) { return rows <= 8 ? 1 : rows <= 64 ? (rows + 7) / 8 : 8; }  // CTAs per peer
+
+cudaError_t launch_ep_dispatch_p2p(const P2PArgs& a, const __nv_bfloat16* x, const int32_t* ids, const float* topk_w,
+                                   int M, int E, int32_t* pos, cudaStream_t st) {
+  const int G = p2p_split(M);
+  cudaError_t e = launch_pdl(ep_dispatch_p2p_kernel, dim3(a.world * G), dim3(P2P_THREADS), 0, st, a,
+                             reinterpret_cast<const uint4*>(x), ids, topk_w, M, E, G, pos);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait(const int* flags, int world, int* err, uint64_t timeout_ns, cudaStream_t st) {
+  cudaError_t e = launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, flags, world, err, timeout_ns);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine_p2p(const P2PArgs& a, const float* rows, int E_local, cudaStream_t st) {
+  const int G = p2p_split(a.mcap);
+  cudaError_t e = launch_pdl(ep_combine_p2p_kernel, dim3(a.world * G), dim3(P2P_THREADS), 0, st, a, rows, E_local, G);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_unpack_p2p(const P2PArgs& a, const int32_t* pos, int M, __nv_bfloat16* out, cudaStream_t st) {
+  const int64_t n4 = (int64_t)M * a.H / 4;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n4 + P2P_THREADS - 1) / P2P_THREADS, 1184));
+  cudaError_t e = launch_pdl(ep_unpack_p2p_kernel, dim3(grid), dim3(P2P_THREADS), 0, st, a, pos, M, out);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -73,9 +73,17 @@ struct LayerParams {
   int* err;                // device error word
   uint64_t timeout_ns;
   int M, top_k, num_ids, E, H, I;
-  int off_cnt1, off_rcnt, off_ready, off_cnt2, off_tok, off_epoch, off_done;  // int offsets into ctr
+  int off_cnt1, off_rcnt, off_ready, off_cnt2, off_tok, off_epoch, off_done, off_ep;  // int offsets into ctr
+  // Expert-parallel receive side (ep_peer non-null, out and out_rows null): x / ids / tw are this rank's receive
+  // buffers of the peer-memory exchange (row s * ep_mcap + p came from rank s), the kernel waits for the receive
+  // flags before routing, and each row's fp32 sum of its local slots goes to row ep_rank * ep_mcap + p of rank s's
+  // back buffer; once every row is written, rank s's back flag for this rank is raised.
+  const uint64_t* ep_peer;   // [ep_world] device table: base of each rank's exchange block
+  const int* ep_recv_flags;  // this rank's flags [0, ep_world)
+  int64_t ep_back_off, ep_flags_off;  // byte offsets of the back buffer and the flags in an exchange block
+  int ep_world, ep_rank, ep_mcap;
 };
-cudaError_t launch_layer(const LayerParams& p, int max_rows, int sms, cudaStream_t st);
+cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, cudaStream_t st);  // rows per block: 8/16/32
 
 // moek_router.cu: softmax -> top-k -> optional renormalisation (dtype 0 = fp32 logits, 1 = bf16)
 cudaError_t launch_router_topk(const void* logits, int dtype, int M, int E, int k, int renorm, int32_t* ids,
@@ -108,6 +116,40 @@ cudaError_t launch_combine_bf16(const __nv_bfloat16* rows, int m, int N, int top
 
 // moek_ep.cu: expert-parallel dispatch plan, row packing, partial combine and ordered unpack
 constexpr int EP_MAX_WORLD = 32;
+constexpr int EP_P2P_MAXM = 1024;  // tokens per rank and call of the peer-memory exchange
+// The exchange block of the fixed-capacity peer-memory EP path, the same layout on every rank (R = world x mcap rows;
+// segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent): byte offsets of the received bf16 rows [R, H], their
+// local expert ids int32 [R, k] (-1: slot owned elsewhere or unused row) and router weights fp32 [R, k], the returned
+// fp32 partial rows [R, H] (segment d = what rank d returned for this rank's tokens), the flags int32 [2 world]
+// ([s]: rank s wrote receive segment s; [world + d]: rank d wrote back segment d) and arrival counters int32 [2 world].
+struct P2PLayout {
+  int64_t x, ids, w, back, flags, ctr, total;
+};
+__host__ __device__ inline int64_t up256(int64_t b) { return (b + 255) / 256 * 256; }
+__host__ __device__ inline P2PLayout p2p_layout(int world, int mcap, int H, int k) {
+  const int64_t R = (int64_t)world * mcap;
+  P2PLayout l;
+  l.x = 0;
+  l.ids = l.x + up256(R * H * 2);
+  l.w = l.ids + up256(R * k * 4);
+  l.back = l.w + up256(R * k * 4);
+  l.flags = l.back + up256(R * H * 4);
+  l.ctr = l.flags + up256(2 * world * 4);
+  l.total = l.ctr + up256(2 * world * 4);
+  return l;
+}
+struct P2PArgs {  // peer-memory exchange of the fixed-capacity EP path (moek_ep.cu)
+  const uint64_t* peer;  // [world] device table: base of each rank's exchange block (CUDA IPC mappings)
+  P2PLayout lay;
+  int world, rank, mcap, H, k;
+  int* err;
+  uint64_t timeout_ns;
+};
+cudaError_t launch_ep_dispatch_p2p(const P2PArgs& a, const __nv_bfloat16* x, const int32_t* ids, const float* topk_w,
+                                   int M, int E, int32_t* pos, cudaStream_t st);
+cudaError_t launch_ep_wait(const int* flags, int world, int* err, uint64_t timeout_ns, cudaStream_t st);
+cudaError_t launch_ep_combine_p2p(const P2PArgs& a, const float* rows, int E_local, cudaStream_t st);
+cudaError_t launch_ep_unpack_p2p(const P2PArgs& a, const int32_t* pos, int M, __nv_bfloat16* out, cudaStream_t st);
 cudaError_t launch_ep_plan(const int32_t* ids, int M, int k, int E, int world, int32_t* pos, int32_t* counts,
                            int32_t* offsets, cudaStream_t st);
 cudaError_t launch_ep_pack(const __nv_bfloat16* x, const int32_t* ids, const float* topk_w, const int32_t* pos,

@@ -9,7 +9,9 @@
 //
 //   routing   every CTA sorts the batch's (expert, slot) keys in shared memory at start-up: blocks = the distinct
 //             valid experts in ascending order, each with its slots in ascending order (moe_align's order,
-//             files/mbx_moek.cu:32-140); no global workspace and no separate launch.
+//             files/mbx_moek.cu:32-140), an expert with more than XR slots cut into blocks of XR (its weights are
+//             then streamed once per block: XR <= 32 keeps two CTAs on every SM for any batch); no global
+//             workspace and no separate launch.
 //   units     gate_up units (block, 256-row item, k-split) and then down units (block, item, k-split), dealt
 //             round-robin over the CTAs in that order: a CTA runs its gate_up units first, and the CTAs that got
 //             fewer of those start streaming down weights early.
@@ -68,7 +70,7 @@ struct Cfg {
   static constexpr int X_OFF = LSTAGE + PAIR_BYTES;
   static constexpr int SC_OFF = X_OFF + XR * X_STRIDE;
   static constexpr int SLOT = SC_OFF + SC_BYTES;
-  static constexpr int NS = XR <= 16 ? 4 : 3;  // two CTAs per SM up to XR = 32
+  static constexpr int NS = XR <= 16 ? 4 : 3;  // ring slots: two CTAs per SM (XR <= 32)
   static constexpr int META_OFF = NS * SLOT;
   static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
   static constexpr int LUT_OFF = IDS_OFF + MAXU * XR * 4;
@@ -77,7 +79,8 @@ struct Cfg {
   static constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
   static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
   static constexpr int T = XR / 8;
-  static constexpr int MINB = XR <= 32 ? 2 : 1;
+  static constexpr int MINB = 2;
+  static_assert(XR <= 32, "two CTAs per SM");
   static_assert(2 * LAYER_MAXIDS * 4 <= SLOT, "routing scratch fits in ring slot 0");
 };
 
@@ -124,6 +127,13 @@ __device__ __forceinline__ bool wait_stamp(const int* stamp, int want, uint64_t 
   }
 }
 
+// Raise, on every rank s, s's back flag for this rank (all of this rank's returned rows are written).
+__device__ __forceinline__ void ep_signal(const LayerParams& p) {
+  for (int s = 0; s < p.ep_world; s++)
+    st_sys(reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(p.ep_peer[s]) + p.ep_flags_off) + p.ep_world + p.ep_rank,
+           1);
+}
+
 __device__ __forceinline__ void decode_unit(const LayerParams& p, int64_t u, int64_t U1, int& ph, int& blk, int& item,
                                             int& ks) {
   ph = u >= U1 ? 1 : 0;
@@ -146,7 +156,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   int* srow = reinterpret_cast<int*>(smem + C::ROUTE_OFF);
   int* bexp = srow + LAYER_MAXIDS;
   int* bstart = bexp + LAYER_MAXIDS;
-  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);  // [0] blocks, [1] valid slots, [2] abort
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);  // [0] blocks, [1] valid slots, [2] abort,
+                                                                              // [3] rows returned (expert-parallel)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::NS;
   uint64_t* scaled = empty + C::NS;
@@ -158,6 +169,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   if (tid == 0) {
     misc[1] = 0;
     misc[2] = 0;
+    misc[3] = 0;
     for (int i = 0; i < C::NS; i++) {
       mbar_init(full + i, 2);  // the producer's and the act warp's arrivals (each with its byte count)
       mbar_init(empty + i, NCW);
@@ -173,6 +185,15 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
   const int n = p.num_ids, k = p.top_k;
+  if (p.ep_peer) {  // expert-parallel: wait until every sender's rows, ids and weights are in the receive buffers
+    if (warp == 0) {
+      bool good = true;
+      for (int s = lane; s < p.ep_world; s += 32) good &= wait_flag(p.ep_recv_flags + s, 1, deadline, p.err);
+      if (!__all_sync(0xffffffffu, good) && lane == 0) misc[2] = 1;
+    }
+    __syncthreads();
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the bulk copies below read what the peers wrote
+  }
 
   // ------------------------------------------------------------------------------------------------- routing
   {
@@ -192,19 +213,28 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       for (int j = 0; j < n; j++) r += key[j] < ki;
       skey[r] = ki;
     }
+    if (p.ep_peer)  // rows with at least one valid slot: the rows this rank returns
+      for (int t = tid; t < p.M; t += THREADS) {
+        bool any = false;
+        for (int j = 0; j < k; j++) any |= key[t * k + j] != 0xFFFFFFFFu;
+        if (any) atomicAdd(const_cast<int*>(misc + 3), 1);
+      }
     __syncthreads();
     const int nvalid = misc[1];
-    if (warp == 0) {  // blocks: a block starts where the expert changes
-      int base = 0;
+    if (warp == 0) {  // blocks: one starts where the expert changes, and after every XR rows of the same expert
+      int base = 0, run0 = 0;  // run0: where the expert run that reaches into this chunk started
       for (int p0 = 0; p0 < nvalid; p0 += 32) {
         const int pos = p0 + lane;
         uint32_t kv = 0;
-        bool head = false;
+        bool ehead = false;
         if (pos < nvalid) {
           kv = skey[pos];
-          head = pos == 0 || (skey[pos - 1] >> 9) != (kv >> 9);
+          ehead = pos == 0 || (skey[pos - 1] >> 9) != (kv >> 9);
           srow[pos] = (int)(kv & 511u);
         }
+        const uint32_t eh = __ballot_sync(0xffffffffu, ehead) & (0xffffffffu >> (31 - lane));  // at lanes <= mine
+        const int rs = eh ? p0 + 31 - __clz(eh) : run0;  // start of my expert's run
+        const bool head = pos < nvalid && (pos - rs) % XR == 0;
         const uint32_t hb = __ballot_sync(0xffffffffu, head);
         if (head) {
           const int bi = base + __popc(hb & ((1u << lane) - 1u));
@@ -212,6 +242,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           bexp[bi] = (int)(kv >> 9);
         }
         base += __popc(hb);
+        run0 = __shfl_sync(0xffffffffu, rs, 31);
       }
       if (lane == 0) {
         bstart[base] = nvalid;
@@ -220,7 +251,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
     }
     __syncthreads();
   }
-  const int nblk = misc[0];
+  const int nblk = *abort_flag ? 0 : misc[0];
+  const int ep_rows = misc[3];
+  if (p.ep_peer && ep_rows == 0 && !*abort_flag && blockIdx.x == 0 && tid == 0)
+    ep_signal(p);  // nothing to return: release the senders' waits at once
 
   // tokens with no valid slot get a zero output row (nothing else writes them)
   if (blockIdx.x == 0 && p.out && warp < NCW) {
@@ -628,6 +662,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         __syncwarp();
         // each row's token: the arrival that completes the token's valid slots for (item, warp) adds them in order
         const int col = 256 * item + 32 * warp + lane;
+        int pieces = 0;  // expert-parallel: (token, item, warp) sums written to the senders' back buffers
         for (int row = 0; row < nv; row++) {
           const int tk = ids[row] / k;
           const int ej = lane < k ? p.ids[tk * k + lane] : -1;
@@ -645,7 +680,26 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             if (ejs < 0 || ejs >= p.E) continue;
             o += __ldcg(rows + (int64_t)(tk * k + sl) * H + col);
           }
-          p.out[(int64_t)tk * H + col] = __float2bfloat16_rn(o);
+          if (p.ep_peer) {  // fp32 partial of the row into its sender's back buffer, over NVLink
+            const int s = tk / p.ep_mcap, pr = tk - s * p.ep_mcap;
+            float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peer[s]) + p.ep_back_off);
+            back[((int64_t)p.ep_rank * p.ep_mcap + pr) * H + col] = o;
+            pieces++;
+          } else {
+            p.out[(int64_t)tk * H + col] = __float2bfloat16_rn(o);
+          }
+        }
+        if (pieces) {  // the arrival that completes every returned row raises the senders' back flags
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence_system();
+            const int want = ep_rows * p.m[1].nt * NCW;
+            if (atomicAdd(p.ctr + p.off_ep, pieces) + pieces == want) {
+              p.ctr[p.off_ep] = 0;
+              __threadfence_system();
+              ep_signal(p);
+            }
+          }
         }
       }
       __syncwarp();
@@ -682,11 +736,10 @@ static cudaError_t launch_xr(const LayerParams& p, int sms, cudaStream_t st) {
 
 }  // namespace dl
 
-cudaError_t launch_layer(const LayerParams& p, int max_rows, int sms, cudaStream_t st) {
-  if (max_rows <= 8) return dl::launch_xr<8>(p, sms, st);
-  if (max_rows <= 16) return dl::launch_xr<16>(p, sms, st);
-  if (max_rows <= 32) return dl::launch_xr<32>(p, sms, st);
-  return dl::launch_xr<96>(p, sms, st);
+cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, cudaStream_t st) {
+  if (block_rows <= 8) return dl::launch_xr<8>(p, sms, st);
+  if (block_rows <= 16) return dl::launch_xr<16>(p, sms, st);
+  return dl::launch_xr<32>(p, sms, st);
 }
 
 }  // namespace moek

@@ -1,4 +1,5 @@
-"""Expert parallelism: the routed experts split over the ranks of a process group, tokens exchanged with NCCL.
+"""Expert parallelism: the routed experts split over the ranks of a process group, tokens exchanged with NCCL or,
+for fixed-capacity decode batches, over peer memory by this build's own kernels (``PeerExchange``).
 
 The reference runs on one GPU and rejects vLLM's ``expert_map`` (files/mbx_moek.py:248-255). This module adds the
 expert-parallel form of the same layer for 2/4/8 GPUs of one node, one process per GPU:
@@ -129,6 +130,106 @@ class CudaBackend:
         return out
 
 
+class _DeviceBuffer:
+    """A raw device range seen by torch (``__cuda_array_interface__``), without copying or owning it."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2}
+
+
+class PeerExchange:
+    """Fixed-capacity exchange blocks in every rank's memory, shared by CUDA IPC (plain peer loads and stores over
+    NVLink, no multicast objects), for ``ep_moe(..., capacity=True, peer=...)``: each rank's rows, slot ids and router
+    weights are written straight into the owners' receive segments (``moek_ep_dispatch_p2p``), the owners' fp32
+    partial rows straight back into the senders' back segments (by the whole-layer kernel itself,
+    ``moek_moe_layer_p2p``, or by ``moek_ep_combine_p2p`` after the multi-launch path), and flags hand each segment
+    over. Every rank of ``group`` builds it together (one all_gather of the IPC handles) for up to ``mcap`` tokens per
+    call of ``top_k`` slots and hidden size ``hidden``; ``close()`` (collective) releases it."""
+
+    def __init__(self, group, mcap: int, hidden: int, top_k: int, device):
+        import ctypes
+
+        self.group, self.mcap, self.hidden, self.top_k = group, mcap, hidden, top_k
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        offs = (ctypes.c_int64 * 7)()
+        call("moek_ep_p2p_layout", self.world, mcap, hidden, top_k, offs)
+        self.layout = dict(zip(("x", "ids", "w", "back", "flags", "ctr", "total"), list(offs)))
+        own = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            call("moek_ipc_malloc", self.layout["total"], ctypes.byref(own))
+            handle = (ctypes.c_char * 64)()
+            call("moek_ipc_handle", own, handle)
+        self.own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        bases, self.opened = [], []
+        with torch.cuda.device(device):
+            for r in range(self.world):
+                if r == self.rank:
+                    bases.append(self.own)
+                    continue
+                ptr = ctypes.c_void_p()
+                call("moek_ipc_open", (ctypes.c_char * 64).from_buffer_copy(handles[r]), ctypes.byref(ptr))
+                self.opened.append(ptr.value)
+                bases.append(ptr.value)
+        self.peer = torch.tensor(bases, dtype=torch.int64, device=device)
+        rows, lay = self.world * mcap, self.layout
+        view = lambda off, shape, typestr: torch.as_tensor(_DeviceBuffer(self.own + off, shape, typestr),
+                                                           device=device)
+        self.recv_x = view(lay["x"], (rows, hidden), "<i2").view(torch.bfloat16)
+        self.recv_ids = view(lay["ids"], (rows, top_k), "<i4")
+        self.recv_w = view(lay["w"], (rows, top_k), "<f4")
+        self.back = view(lay["back"], (rows, hidden), "<f4")
+        self.flags = self.own + lay["flags"]
+        self.err = ops.error_word(device)
+        self.device = device
+
+    def close(self):
+        """Collective: every rank unmaps its peers' blocks, then frees its own once all ranks have unmapped."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for ptr in self.opened:
+                call("moek_ipc_close", ptr)
+            dist.barrier(group=self.group)
+            call("moek_ipc_free", self.own)
+        self.own, self.opened = None, []
+
+
+def _ep_moe_peer(x, layer: EPLayer, w, ids32, px: PeerExchange, be) -> torch.Tensor:
+    """The fixed-capacity layer over peer memory (``PeerExchange``): no collective library call. Three launches when
+    the received rows fit the whole-layer kernel (dispatch, layer, unpack), else dispatch, wait, the local layer's
+    kernels, combine, unpack. With ``be.record`` a list, a copy of the received batch (rows, slot metadata as in
+    ``CudaBackend.local``, metadata row stride) is appended to it, taken before the unpack lets the senders write
+    again."""
+    m, hid = x.shape
+    k = ids32.shape[1]
+    dev = x.device
+    if m > px.mcap or k != px.top_k or hid != px.hidden:
+        raise MoekError(f"moek_b200: the peer exchange holds {px.mcap} tokens of {px.top_k} slots and width "
+                        f"{px.hidden} (call: {m}, {k}, {hid})")
+    st = ops._stream(dev)
+    head = (ops._ptr(px.peer), px.world, px.rank, px.mcap, hid, k)
+    pos = torch.empty((m, px.world), dtype=torch.int32, device=dev)
+    call("moek_ep_dispatch_p2p", *head, ops._ptr(x), ops._ptr(ids32), ops._ptr(w), m, layer.num_experts,
+         ops._ptr(pos), ops._ptr(px.err), st)
+    if getattr(be, "record", None) is not None:
+        call("moek_ep_wait", px.flags, px.world, ops._ptr(px.err), st)
+        be.record.append((px.recv_x.clone(), torch.cat([px.recv_ids, px.recv_w.view(torch.int32)], 1), 2 * k))
+    if ops.layer_p2p_fits(px.world * px.mcap, k):
+        ops.layer_p2p(px, layer.prep)
+    else:
+        call("moek_ep_wait", px.flags, px.world, ops._ptr(px.err), st)
+        rows = ops.moe_rows(px.recv_x, layer.prep, px.recv_w, px.recv_ids)
+        call("moek_ep_combine_p2p", *head, ops._ptr(rows), layer.local_experts, ops._ptr(px.err), st)
+    out = torch.empty((m, hid), dtype=torch.bfloat16, device=dev)
+    call("moek_ep_unpack_p2p", *head, ops._ptr(pos), m, ops._ptr(out), ops._ptr(px.err), st)
+    return out
+
+
 def meta_columns(top_k: int) -> int:
     """bf16 columns that hold a row's 2 * top_k int32 of slot metadata in a merged send buffer (a multiple of 8, so
     rows stay 16-byte aligned)."""
@@ -139,14 +240,16 @@ _OFFSETS: dict = {}
 
 
 def ep_moe(hidden_states: torch.Tensor, layer: EPLayer, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
-           group=None, backend=None, capacity: bool = False) -> torch.Tensor:
+           group=None, backend=None, capacity: bool = False, peer: PeerExchange = None) -> torch.Tensor:
     """This rank's tokens through the expert-parallel layer: bf16 [M, H], the same result as ``ops.fused_moe`` on
     one GPU holding all experts (up to the order of fp32 additions). ``topk_ids`` are global expert ids.
 
     ``capacity=False``: all-to-allv with exact row counts (the counts cross to the host once per call).
     ``capacity=True``: every rank reserves M rows for every destination (M = this call's token count, the same on
     all ranks), so the exchange has fixed sizes and no host synchronisation; unused rows carry invalid slot ids and
-    are skipped by the kernels. Suited to decode batches, where the rows are few and the latency matters.
+    are skipped by the kernels. Suited to decode batches, where the rows are few and the latency matters. With
+    ``peer`` (a ``PeerExchange`` of this group), the fixed-capacity exchange runs over peer memory instead of NCCL:
+    rows, ids, weights and partials are written straight into the other ranks' blocks by this build's kernels.
 
     Every rank of ``group`` must call this for the same layer with the same mode (the collectives pair up in call
     order)."""
@@ -159,6 +262,8 @@ def ep_moe(hidden_states: torch.Tensor, layer: EPLayer, topk_weights: torch.Tens
     k = topk_ids.shape[1]
     ids32 = topk_ids.to(torch.int32).contiguous()
     w = topk_weights.float().contiguous()
+    if capacity and peer is not None:
+        return _ep_moe_peer(x, layer, w, ids32, peer, be)
     pos, counts, offsets = be.plan(ids32, layer.num_experts, world)
     if capacity:
         key = (m, world, pos.device)

@@ -208,7 +208,7 @@ LAYER_MAXIDS = 512  # routed slots per whole-layer call (moek_layer.cu)
 
 
 def _decode_path(m: int, top_k: int) -> bool:
-    return m <= min(DECODE_MAX_M, 96) and m * top_k <= LAYER_MAXIDS
+    return m <= DECODE_MAX_M and m * top_k <= LAYER_MAXIDS
 
 
 def _layer_splits(hidden: int, inter: int):
@@ -236,8 +236,24 @@ def _layer_state(dev, E: int, hidden: int, inter: int) -> torch.Tensor:
     return _BUF[key]
 
 
+_ROWS_SET = False
+
+
+def _layer_rows_knob():
+    """MOEK_B200_LAYER_ROWS (8, 16 or 32): rows per block of the whole-layer kernel instead of the automatic
+    choice (moek_set_layer_block_rows), read once."""
+    global _ROWS_SET
+    if not _ROWS_SET:
+        env = os.environ.get("MOEK_B200_LAYER_ROWS")
+        if env:
+            call("moek_set_layer_block_rows", int(env))
+        _ROWS_SET = True
+
+
 def _layer_kernel(x, layer, tw, ids32, m, top_k, output, rows):
     import ctypes
+
+    _layer_rows_knob()
 
     a, b = layer.w13, layer.w2
     hidden, inter = a.K, b.K
@@ -251,6 +267,32 @@ def _layer_kernel(x, layer, tw, ids32, m, top_k, output, rows):
          _ptr(a.g), _ptr(a.exc_off), _ptr(a.exc_ent), _ptr(b.w), _ptr(b.sp), _ptr(b.g), _ptr(b.exc_off),
          _ptr(b.exc_ent), ns1, ns2, _ptr(ws), ws.numel(), _ptr(st), st.numel(), _ptr(error_word(dev)),
          _ptr(output), _ptr(rows), _stream(dev))
+
+
+def layer_p2p_fits(rows: int, top_k: int) -> bool:
+    """Whether ``rows`` received rows of ``top_k`` slots fit the whole-layer kernel (``layer_p2p``)."""
+    return 0 < rows and rows * top_k <= LAYER_MAXIDS
+
+
+def layer_p2p(px, layer: PreparedLayer):
+    """The whole-layer kernel on a peer exchange's receive segments (``ep.PeerExchange``): waits for the senders'
+    flags, and writes each row's fp32 partial straight into its sender's back segment (moek_moe_layer_p2p)."""
+    import ctypes
+
+    _layer_rows_knob()
+    a, b = layer.w13, layer.w2
+    hidden, inter = a.K, b.K
+    dev = px.recv_x.device
+    rows, k = px.world * px.mcap, px.top_k
+    ns1, ns2 = _layer_splits(hidden, inter)
+    wsb = ctypes.c_size_t(0)
+    call("moek_layer_workspace_bytes", rows, k, hidden, inter, ns1, ns2, 0, ctypes.byref(wsb))
+    ws = _scratch("layer_ws", wsb.value, torch.uint8, dev)
+    st = _layer_state(dev, layer.E, hidden, inter)
+    call("moek_moe_layer_p2p", _ptr(px.peer), px.own, px.world, px.rank, px.mcap, hidden, inter, layer.E, k,
+         _ptr(a.w), _ptr(a.sp), _ptr(a.g), _ptr(a.exc_off), _ptr(a.exc_ent), _ptr(b.w), _ptr(b.sp), _ptr(b.g),
+         _ptr(b.exc_off), _ptr(b.exc_ent), ns1, ns2, _ptr(ws), ws.numel(), _ptr(st), st.numel(), _ptr(px.err),
+         _stream(dev))
 
 
 def _splits(k: int, units_per_split: int, grid: int) -> int:

@@ -73,3 +73,32 @@ def test_layer_entry_points_reject_bad_arguments():
     assert lib.moek_moe_layer(*args) == 1 and b"null pointer" in lib.moek_last_error()
     args[18] = 3  # 3 splits do not cut 16 runs
     assert lib.moek_moe_layer(*args) == 1 and b"k-splits" in lib.moek_last_error()
+
+
+def test_peer_exchange_layout_and_argument_checks():
+    """The exchange block layout (x, ids, w, back, flags, counters, total; 256-byte aligned sections) and the
+    argument checks of the peer-exchange entry points (no device call is reached)."""
+    lib = _lib.lib()
+    offs = (ctypes.c_int64 * 7)()
+    world, mcap, H, k = 2, 8, 2048, 5
+    assert lib.moek_ep_p2p_layout(world, mcap, H, k, offs) == 0
+    up = lambda b: (b + 255) // 256 * 256
+    R = world * mcap
+    want = [0]
+    for size in (R * H * 2, R * k * 4, R * k * 4, R * H * 4, 2 * world * 4, 2 * world * 4):
+        want.append(want[-1] + up(size))
+    assert list(offs) == want
+    assert lib.moek_ep_p2p_layout(world, 1025, H, k, offs) == 1  # more than 1024 tokens per rank
+    assert lib.moek_ep_p2p_layout(33, mcap, H, k, offs) == 1  # more ranks than supported
+    fake = ctypes.c_void_p(256)  # never dereferenced: every call below fails its argument checks first
+    assert lib.moek_ep_dispatch_p2p(None, 2, 0, 8, H, k, fake, fake, fake, 4, 64, fake, fake, None) == 1
+    assert lib.moek_ep_dispatch_p2p(fake, 2, 2, 8, H, k, fake, fake, fake, 4, 64, fake, fake, None) == 1  # rank
+    assert lib.moek_ep_dispatch_p2p(fake, 2, 0, 8, H, k, fake, fake, fake, 9, 64, fake, fake, None) == 1  # M > mcap
+    assert lib.moek_ep_dispatch_p2p(fake, 2, 0, 8, H, k, fake, fake, fake, 4, 63, fake, fake, None) == 1  # E % world
+    assert lib.moek_ep_unpack_p2p(fake, 2, 0, 8, H, k, None, 4, fake, fake, None) == 1
+    assert lib.moek_ep_combine_p2p(fake, 2, 0, 8, H, k, fake, 0, fake, None) == 1
+    args = [fake, None, 2, 0, 8, H, 512, 256, k] + [fake] * 10 + [2, 1, fake, 1 << 30, fake, 1 << 20, fake, None]
+    assert lib.moek_moe_layer_p2p(*args) == 1 and b"exchange block" in lib.moek_last_error()
+    args[1], args[4] = fake, 60  # 120 received rows of 5 slots: more than the whole-layer kernel takes
+    assert lib.moek_moe_layer_p2p(*args) == 3 and b"decode batches" in lib.moek_last_error()
+    assert lib.moek_set_layer_block_rows(24) == 1 and lib.moek_set_layer_block_rows(0) == 0

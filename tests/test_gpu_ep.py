@@ -108,6 +108,85 @@ def test_ep_one_rank_equals_fused_moe(m, capacity):
     assert (out != ref).float().mean() < 0.01  # only the odd output lands on the other side of a bf16 rounding
 
 
+@pytest.mark.parametrize("m,mcap", [(8, 8), (5, 8), (100, 128)])
+def test_ep_peer_exchange_one_rank(m, mcap):
+    """The peer-memory exchange on a one-rank group (the block shared with itself): equal to the NCCL fixed-capacity
+    path bit for bit, repeatable (the flags reset themselves), also when replayed as a CUDA graph. mcap 8: the
+    whole-layer kernel reads the receive segment and returns the partials itself (three launches); mcap 128: more
+    slots than it takes, so the local layer's kernels run between a wait and the combine kernel."""
+    import torch.distributed as dist
+
+    from qwen38_flash_coder_b200 import ep, ops, synth
+
+    E = 64
+    w13, w2 = synth.make_layer(E, 2048, 512, 23, device=DEV)
+    layer = ep.EPLayer(w13, w2, E, 1, 0)
+    x = synth.activations(m, 2048, 23, device=DEV)
+    ids, wts = synth.route_zipf(m, E, 5, 23, device=DEV)
+    _single_rank_group()
+    try:
+        px = ep.PeerExchange(None, mcap, 2048, 5, DEV)
+        assert ops.layer_p2p_fits(mcap, 5) == (mcap * 5 <= 512)
+        ref = ep.ep_moe(x, layer, wts, ids, capacity=True)
+        outs = [ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px) for _ in range(3)]
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px)
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(g):
+            gout = ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px)
+        for _ in range(3):
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(gout, ref)
+        del g
+        px.close()
+    finally:
+        dist.destroy_process_group()
+    ops.check_device_errors(DEV)
+    for o in outs:
+        assert torch.equal(o, ref)
+
+
+def test_ep_peer_layer_wait_expires():
+    """The whole-layer kernel on a receive segment that no sender fills: its bounded wait on the receive flag runs
+    out, it records MOEK_DEV_TIMEOUT, writes nothing and returns (the context stays usable); after the error is
+    cleared the exchange works again."""
+    import torch.distributed as dist
+
+    from qwen38_flash_coder_b200 import _lib, ep, ops, synth
+
+    E, m = 64, 8
+    w13, w2 = synth.make_layer(E, 2048, 512, 29, device=DEV)
+    layer = ep.EPLayer(w13, w2, E, 1, 0)
+    x = synth.activations(m, 2048, 29, device=DEV)
+    ids, wts = synth.route_zipf(m, E, 5, 29, device=DEV)
+    _single_rank_group()
+    try:
+        px = ep.PeerExchange(None, m, 2048, 5, DEV)
+        ref = ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px)
+        torch.cuda.synchronize()
+        back = px.back.clone()
+        _lib.call("moek_set_wait_timeout_ns", 20_000_000)  # 20 ms
+        try:
+            ops.layer_p2p(px, layer.prep)  # the receive flag is 0: nothing was dispatched
+            torch.cuda.synchronize()
+        finally:
+            _lib.call("moek_set_wait_timeout_ns", 2_000_000_000)
+        with pytest.raises(ops.MoekError, match="timed out"):
+            ops.check_device_errors(DEV)
+        assert torch.equal(px.back, back)  # nothing was returned
+        again = ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px)
+        torch.cuda.synchronize()
+        ops.check_device_errors(DEV)
+        assert torch.equal(again, ref)
+        px.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _two_gpu_rank(rank, port, q):
     import torch.distributed as dist
 
@@ -131,10 +210,17 @@ def _two_gpu_rank(rank, port, q):
         x2 = synth.activations(m2, 2048, 60 + rank, device=dev)
         ids2, wts2 = synth.route_zipf(m2, E, 5, 60 + rank, device=dev)
         out2 = ep.ep_moe(x2, layer, wts2, ids2, capacity=True)
+        # the same fixed-capacity batch over peer memory (96 received rows: the whole-layer kernel returns the
+        # partials over NVLink): identical to the NCCL exchange, call after call
+        px = ep.PeerExchange(None, m2, 2048, 5, dev)
+        peer_outs = [ep.ep_moe(x2, layer, wts2, ids2, capacity=True, peer=px) for _ in range(3)]
         ref = ops.fused_moe(x, full.prep, wts, ids)
         ref2 = ops.fused_moe(x2, full.prep, wts2, ids2)
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
+        px.close()
+        if not all(torch.equal(o, out2) for o in peer_outs):
+            raise AssertionError("peer-memory exchange differs from the NCCL exchange")
         rel, raw, net = moe_ref.check(out.cpu(), ref.float().cpu())
         rel2, raw2, net2 = moe_ref.check(out2.cpu(), ref2.float().cpu())
         q.put((rank, "ok", (max(rel, rel2), max(net, net2))))
