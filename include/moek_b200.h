@@ -143,8 +143,9 @@ int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M, int32_t
  * zero it again). Calls that share a state buffer must be ordered (one stream). */
 int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n);
 
-/* Scratch bytes of one call: act, k-split partials and the fp32 slot rows (rows_out != 0: the caller's out_rows
- * receives the rows and no top-k sum is formed). Contents need not be preserved between calls. */
+/* Scratch bytes of one call: act, k-split partials (room for one split per 128-k stage, whatever the splits asked
+ * for) and the fp32 slot rows (rows_out != 0: the caller's out_rows receives the rows and no top-k sum is formed).
+ * Contents need not be preserved between calls. */
 int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t nsplit_gate,
                                int32_t nsplit_down, int32_t rows_out, size_t* bytes);
 
@@ -155,12 +156,18 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  *   x       bf16 [M, H]; M * top_k <= 512 (decode batches; larger ones take the moek_gemm path).
  *   w13/sp13/g13/exc_off13/exc_ent13  gate_up in the tiled formats above (N = 2I, K = H); w2.. likewise (N = H,
  *           K = I). H % 256 == 0, I % 128 == 0, both <= 4096.
- *   nsplit_gate, nsplit_down  k-splits per 256-row item; (K/64/nsplit) even.
+ *   nsplit_gate, nsplit_down  k-splits per 256-row item; (K/64/nsplit) even. When the units would spill a few
+ *           items past a whole number of waves of the grid, those items get a finer split (see
+ *           moek_set_layer_tail_split), which changes the order of the fp32 partial sums only.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
 /* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: the batch's size up to 16, else 32).
  * An expert with more routed slots than that is cut into several blocks, its weights streamed once per block.
  * Process-wide; a tuning knob with no effect on the results. */
 int moek_set_layer_block_rows(int32_t rows);
+/* Whether the whole-layer kernel may cut the items past its last whole wave of units into finer k-splits (on != 0,
+ * the default) so that a phase ends soon after its last full wave. Process-wide tuning knob; it changes only the
+ * order of fp32 partial sums. */
+int moek_set_layer_tail_split(int32_t on);
 
 int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
                    const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13, const float* g13,

@@ -11,6 +11,7 @@ SIGNATURES = {
     "moek_version": (ctypes.c_int, []),
     "moek_set_wait_timeout_ns": (ctypes.c_int, [_U64]),
     "moek_set_layer_block_rows": (ctypes.c_int, [_I32]),
+    "moek_set_layer_tail_split": (ctypes.c_int, [_I32]),
     "moek_align_workspace_bytes": (ctypes.c_int, [_I64, _I32, ctypes.POINTER(ctypes.c_size_t)]),
     "moek_align": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P, ctypes.c_size_t, _P]),
     "moek_align_noalloc": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P]),

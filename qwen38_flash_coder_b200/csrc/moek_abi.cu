@@ -240,10 +240,13 @@ static LayerLayout layer_layout(int32_t E, int32_t H, int32_t I) {
   l.total = l.tok + (int64_t)moek::LAYER_MAXIDS * nt2 * 8;
   return l;
 }
-static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, int32_t ns1, int32_t ns2, bool rows) {
+// Workspace: act, then k-split partials for up to one split per 128-k stage (the kernel may cut the items past its
+// last whole wave of units that finely, whatever the caller's split), then the fp32 slot rows.
+static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, bool rows) {
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  return up(num_ids * I * 2) + (ns1 > 1 ? up((int64_t)ns1 * num_ids * 2 * I * 4) : 0) +
-         (ns2 > 1 ? up((int64_t)ns2 * num_ids * H * 4) : 0) + (rows ? up(num_ids * (int64_t)H * 4) : 0);
+  const int64_t nst1 = H / 128, nst2 = I / 128;
+  return up(num_ids * I * 2) + (nst1 > 1 ? up(nst1 * num_ids * 2 * I * 4) : 0) +
+         (nst2 > 1 ? up(nst2 * num_ids * H * 4) : 0) + (rows ? up(num_ids * (int64_t)H * 4) : 0);
 }
 
 MOEK_API int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n) {
@@ -256,7 +259,7 @@ MOEK_API int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int
                                         int32_t nsplit_down, int32_t rows_out, size_t* bytes) {
   if (!bytes || M < 0 || top_k <= 0 || H <= 0 || I <= 0 || nsplit_gate < 1 || nsplit_down < 1)
     return fail(MOEK_ERR_ARG, "moek_b200: bad layer workspace query");
-  *bytes = (size_t)layer_ws_bytes((int64_t)M * top_k, H, I, nsplit_gate, nsplit_down, !rows_out);
+  *bytes = (size_t)layer_ws_bytes((int64_t)M * top_k, H, I, !rows_out);
   return MOEK_OK;
 }
 
@@ -266,6 +269,12 @@ MOEK_API int moek_set_layer_block_rows(int32_t rows) {
   if (rows != 0 && rows != 8 && rows != 16 && rows != 32)
     return fail(MOEK_ERR_ARG, "moek_b200: layer block rows must be 8, 16, 32 or 0 (automatic), got %d", rows);
   g_layer_rows = rows;
+  return MOEK_OK;
+}
+// Whether the whole-layer kernel may give the items past its last whole wave of units a finer k-split (default on).
+static int g_layer_tail = 1;
+MOEK_API int moek_set_layer_tail_split(int32_t on) {
+  g_layer_tail = on ? 1 : 0;
   return MOEK_OK;
 }
 static int layer_block_rows(int M) {
@@ -300,7 +309,7 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   const LayerLayout lay = layer_layout(E, H, I);
   if (state_ints < lay.total)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer state needs %lld int32 (zeroed once)", (long long)lay.total);
-  const int64_t ws = layer_ws_bytes(num_ids, H, I, nsplit_gate, nsplit_down, rows_ws);
+  const int64_t ws = layer_ws_bytes(num_ids, H, I, rows_ws);
   if ((int64_t)workspace_bytes < ws || !workspace)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer needs %lld workspace bytes", (long long)ws);
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
@@ -308,13 +317,13 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   p = moek::LayerParams{};
   p.act = reinterpret_cast<__nv_bfloat16*>(wp);
   wp += up(num_ids * I * 2);
-  if (nsplit_gate > 1) {
+  if (nst1 > 1) {
     p.part1 = reinterpret_cast<float*>(wp);
-    wp += up((int64_t)nsplit_gate * num_ids * 2 * I * 4);
+    wp += up((int64_t)nst1 * num_ids * 2 * I * 4);
   }
-  if (nsplit_down > 1) {
+  if (nst2 > 1) {
     p.part2 = reinterpret_cast<float*>(wp);
-    wp += up((int64_t)nsplit_down * num_ids * H * 4);
+    wp += up((int64_t)nst2 * num_ids * H * 4);
   }
   if (rows_ws) p.rows = reinterpret_cast<float*>(wp);
   const moek::LayerMat m1{static_cast<const uint8_t*>(w13), sp13, g13, exc_off13,
@@ -338,6 +347,7 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   p.off_epoch = 0;
   p.off_done = 1;
   p.off_ep = 2;
+  p.tail = g_layer_tail;
   p.off_cnt1 = (int)lay.cnt1;
   p.off_rcnt = (int)lay.rcnt;
   p.off_ready = (int)lay.ready;

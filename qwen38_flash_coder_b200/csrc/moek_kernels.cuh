@@ -64,8 +64,8 @@ struct LayerParams {
   const int32_t* ids;      // [M * top_k] expert per slot (outside [0, E): not routed)
   const float* tw;         // [M * top_k] router weights
   __nv_bfloat16* act;      // workspace [num_ids, I]
-  float* part1;            // workspace [nsplit_gate, num_ids, 2I] (nsplit_gate > 1)
-  float* part2;            // workspace [nsplit_down, num_ids, H] (nsplit_down > 1)
+  float* part1;            // workspace [H / 128, num_ids, 2I]: k-split partials of gate_up (H > 128)
+  float* part2;            // workspace [I / 128, num_ids, H]: k-split partials of down (I > 128)
   float* rows;             // workspace [num_ids, H]: weighted fp32 slot rows before the top-k sum
   float* out_rows;         // caller's fp32 rows [num_ids, H] instead of the top-k sum (or null)
   __nv_bfloat16* out;      // caller's bf16 [M, H] top-k sums (or null)
@@ -82,6 +82,7 @@ struct LayerParams {
   const int* ep_recv_flags;  // this rank's flags [0, ep_world)
   int64_t ep_back_off, ep_flags_off;  // byte offsets of the back buffer and the flags in an exchange block
   int ep_world, ep_rank, ep_mcap;
+  int tail;  // 1: items past the last whole wave of units may use a finer k-split (up to one per stage)
 };
 cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, cudaStream_t st);  // rows per block: 8/16/32
 

@@ -14,7 +14,8 @@
 //             workspace and no separate launch.
 //   units     gate_up units (block, 256-row item, k-split) and then down units (block, item, k-split), dealt
 //             round-robin over the CTAs in that order: a CTA runs its gate_up units first, and the CTAs that got
-//             fewer of those start streaming down weights early.
+//             fewer of those start streaming down weights early. Items beyond the last whole wave of units get a
+//             finer k-split (PhasePlan), so that a phase does not end with a few CTAs running one more long unit.
 //   producer  warp 8: per 64-k stage, the 8 KB of packed codes (lane 0) and the 1056-byte packed-scale run pair
 //             (lane 1) by bulk copy (cp.async.bulk, no multicast) into a ring slot. It never waits on another CTA:
 //             the weights of every unit are known once the routing is.
@@ -63,7 +64,39 @@ constexpr int MAXU = 32;        // units per metadata round
 
 struct UnitMeta {
   int ph, blk, item, ks, e, nv, flags;  // ph: 0 = gate_up, 1 = down; flags: 2 = block has more rows than XR
+  int st0, st1, ns;                     // the unit's stages [st0, st1) of its item, the item's k-split count
 };
+
+// Units of one phase: items (block, 256-row item) in order, each cut into k-splits. The first ni_main items use the
+// caller's split; when those units would spill a few items past a whole number of waves of the grid, the remaining
+// items use the finest whole-stage split that still fits them in one more wave, so the phase ends about one short
+// unit after the last full wave instead of one full unit (the idea of stream-K, with no fix-up beyond the split-k
+// arrivals the kernel has anyway).
+struct PhasePlan {
+  int ni_main, s_main, s_tail;
+  int64_t u_main, u_total;
+};
+__device__ __forceinline__ PhasePlan plan_phase(const LayerMat& m, int nblk, int grid, bool tail) {
+  PhasePlan q;
+  const int ni = nblk * m.nt;
+  q.s_main = q.s_tail = m.nsplit;
+  q.ni_main = ni;
+  const int64_t main_units = (int64_t)ni * m.nsplit;
+  if (tail && main_units > grid) {
+    const int nim = (int)(main_units / grid * grid / m.nsplit);
+    const int rem = ni - nim;
+    int st = m.nsplit;
+    for (int s = m.nsplit + 1; s <= m.nstage; s++)
+      if (m.nstage % s == 0 && (int64_t)rem * s <= grid) st = s;
+    if (rem > 0 && st > m.nsplit) {
+      q.ni_main = nim;
+      q.s_tail = st;
+    }
+  }
+  q.u_main = (int64_t)q.ni_main * q.s_main;
+  q.u_total = q.u_main + (int64_t)(ni - q.ni_main) * q.s_tail;
+  return q;
+}
 
 template <int XR>
 struct Cfg {
@@ -134,16 +167,29 @@ __device__ __forceinline__ void ep_signal(const LayerParams& p) {
            1);
 }
 
-__device__ __forceinline__ void decode_unit(const LayerParams& p, int64_t u, int64_t U1, int& ph, int& blk, int& item,
-                                            int& ks) {
-  ph = u >= U1 ? 1 : 0;
-  const LayerMat& m = p.m[ph];
-  const int64_t v = ph ? u - U1 : u;
-  const int per = m.nt * m.nsplit;
-  blk = (int)(v / per);
-  const int rem = (int)(v - (int64_t)blk * per);
-  item = rem / m.nsplit;
-  ks = rem - item * m.nsplit;
+__device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePlan& q0, const PhasePlan& q1, int64_t u,
+                                            UnitMeta& um) {
+  um.ph = u >= q0.u_total ? 1 : 0;
+  const LayerMat& m = p.m[um.ph];
+  const PhasePlan& q = um.ph ? q1 : q0;
+  const int64_t v = um.ph ? u - q0.u_total : u;
+  int ii;
+  if (v < q.u_main) {
+    ii = (int)(v / q.s_main);
+    um.ks = (int)(v - (int64_t)ii * q.s_main);
+    um.ns = q.s_main;
+  } else {
+    const int64_t w = v - q.u_main;
+    const int t = (int)(w / q.s_tail);
+    ii = q.ni_main + t;
+    um.ks = (int)(w - (int64_t)t * q.s_tail);
+    um.ns = q.s_tail;
+  }
+  um.blk = ii / m.nt;
+  um.item = ii - um.blk * m.nt;
+  const int su = m.nstage / um.ns;
+  um.st0 = um.ks * su;
+  um.st1 = um.st0 + su;
 }
 
 template <int XR>
@@ -265,8 +311,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
     }
   }
 
-  const int64_t U1 = (int64_t)nblk * p.m[0].nt * p.m[0].nsplit;
-  const int64_t U = U1 + (int64_t)nblk * p.m[1].nt * p.m[1].nsplit;
+  const PhasePlan plan0 = plan_phase(p.m[0], nblk, gridDim.x, p.tail),
+                  plan1 = plan_phase(p.m[1], nblk, gridDim.x, p.tail);
+  const int64_t U = plan0.u_total + plan1.u_total;
   const int n_mine = U > blockIdx.x ? (int)((U - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
   const int rounds = (n_mine + MAXU - 1) / MAXU;
 
@@ -278,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, abort_flag)) break;
       for (int i = lane; i < nu; i += 32) {
         UnitMeta& m = meta[i];
-        decode_unit(p, blockIdx.x + (int64_t)(u0 + i) * gridDim.x, U1, m.ph, m.blk, m.item, m.ks);
+        decode_unit(p, plan0, plan1, blockIdx.x + (int64_t)(u0 + i) * gridDim.x, m);
         m.e = bexp[m.blk];
         const int b0 = bstart[m.blk], cnt = bstart[m.blk + 1] - b0;
         m.nv = min(cnt, XR);
@@ -289,9 +336,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       mbar_arrive(mfull);  // units, experts and rows published
       for (int ci = 0; ci < nu && ok; ci++) {
         const LayerMat& mt = p.m[meta[ci].ph];
-        const int e = meta[ci].e, item = meta[ci].item, ks = meta[ci].ks;
-        const int su = mt.nstage / mt.nsplit;
-        for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
+        const int e = meta[ci].e, item = meta[ci].item;
+        for (int st = meta[ci].st0; st < meta[ci].st1; st++, g++) {
           const int slot = g % C::NS;
           if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag)) {
             ok = false;
@@ -319,11 +365,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
       for (int ci = 0; ci < nu && ok; ci++) {
         const UnitMeta& m = meta[ci];
-        const LayerMat& mt = p.m[m.ph];
-        const int su = mt.nstage / mt.nsplit, nv = m.nv;
+        const int nv = m.nv;
         const int* ids = mids + ci * XR;
         int ready_item = -1;
-        for (int st = m.ks * su; st < (m.ks + 1) * su; st++, g++) {
+        for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag)) {
             ok = false;
@@ -378,8 +423,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       auto fetch = [&](int ui) {  // loads only; consumed one unit later
         const UnitMeta& m = meta[ui];
         const LayerMat& mt = p.m[m.ph];
-        const int nruns = mt.nstage / mt.nsplit;
-        const int64_t key0 = ((int64_t)m.e * mt.nt + m.item) * mt.nstage + (int64_t)m.ks * nruns;
+        const int nruns = m.st1 - m.st0;
+        const int64_t key0 = ((int64_t)m.e * mt.nt + m.item) * mt.nstage + m.st0;
         ro_n = lane < nruns ? mt.exc_off[key0 + lane] : 0;
         end_n = mt.exc_off[key0 + nruns];
         g_n = mt.G[m.e];
@@ -388,7 +433,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       for (int ui = 0; ui < nu && ok; ui++) {
         const UnitMeta& m = meta[ui];
         const LayerMat& mt = p.m[m.ph];
-        const int su = mt.nstage / mt.nsplit;
+        const int su = m.st1 - m.st0;
         const int o0 = __shfl_sync(0xffffffffu, ro_n, 0);
         const int ro = ro_n - o0, cnt = end_n - o0;
         const float gsc = g_n;
@@ -400,7 +445,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
         kq++;
         const int r0g = m.ph == 0 ? m.item : 2 * m.item;  // global run index of the pair's first run
-        for (int st = m.ks * su; st < (m.ks + 1) * su; st++, g++) {
+        for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, abort_flag)) {
             ok = false;
@@ -427,7 +472,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           }
           __syncwarp();
           // this stage's run: entries [eo0, eo1) of the unit's list overwrite their bytes
-          const int rr = st - m.ks * su;
+          const int rr = st - m.st0;
           const int eo0 = __shfl_sync(0xffffffffu, ro, rr);
           const int eo1 = rr + 1 < su ? __shfl_sync(0xffffffffu, ro, rr + 1) : cnt;
           auto patch = [&](uint32_t en) {
@@ -458,8 +503,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       for (int ui = 0; ui < nu && have_meta; ui++) {
         const UnitMeta& m = meta[ui];
         const LayerMat& mt = p.m[m.ph];
-        const int ph = m.ph, item = m.item, ks = m.ks, nv = m.nv, blk = m.blk;
-        const int su = mt.nstage / mt.nsplit;
+        const int ph = m.ph, item = m.item, ks = m.ks, nv = m.nv, blk = m.blk, ns = m.ns;
         const int* ids = mids + ui * XR;
         if ((m.flags & 2) && tid == 0) report(p.err, MOEK_DEV_TOO_MANY_ROWS);
         // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
@@ -476,7 +520,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 #pragma unroll
             for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
         bool ok = true;
-        for (int st = ks * su; st < (ks + 1) * su; st++, g++) {
+        for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
           if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag) ||
@@ -531,7 +575,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         const int N = mt.N;
         if (ph == 0) {
           const int nt1 = mt.nt;
-          bool complete = mt.nsplit == 1;
+          bool complete = ns == 1;
           if (complete) {  // gate row and up row + 128 share the column: act straight from the accumulators
 #pragma unroll
             for (int t = 0; t < C::T; t++) {
@@ -569,7 +613,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             int* cn = p.ctr + p.off_cnt1 + ((int64_t)blk * nt1 + item) * NCW + warp;
             if (lane == 0) old = atomicAdd(cn, 1);
             old = __shfl_sync(0xffffffffu, old, 0);
-            complete = old == mt.nsplit - 1;
+            complete = old == ns - 1;
             if (complete) {  // every split of (block, item, warp) is in: add them in split order
               if (lane == 0) *cn = 0;
               __threadfence();
@@ -577,7 +621,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
                 const int row = idx >> 4, col = 128 * item + 16 * warp + (idx & 15);
                 const float* pr = p.part1 + (int64_t)ids[row] * N;
                 float gs = 0.f, us = 0.f;
-                for (int s2 = 0; s2 < mt.nsplit; s2++) {
+                for (int s2 = 0; s2 < ns; s2++) {
                   gs += __ldcg(pr + (int64_t)s2 * n * N + col);
                   us += __ldcg(pr + (int64_t)s2 * n * N + I + col);
                 }
@@ -602,7 +646,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         // down: weighted fp32 rows of (block, item), then the token sums
         const int nt2 = mt.nt;
         float* rows = p.out_rows ? p.out_rows : p.rows;
-        bool complete = mt.nsplit == 1;
+        bool complete = ns == 1;
         if (complete) {
 #pragma unroll
           for (int t = 0; t < C::T; t++) {
@@ -643,7 +687,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           int* cn = p.ctr + p.off_cnt2 + ((int64_t)blk * nt2 + item) * NCW + warp;
           if (lane == 0) old = atomicAdd(cn, 1);
           old = __shfl_sync(0xffffffffu, old, 0);
-          complete = old == mt.nsplit - 1;
+          complete = old == ns - 1;
           if (complete) {
             if (lane == 0) *cn = 0;
             __threadfence();
@@ -652,7 +696,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               const int id = ids[row];
               const float* pr = p.part2 + (int64_t)id * N + col;
               float s = 0.f;
-              for (int s2 = 0; s2 < mt.nsplit; s2++) s += __ldcg(pr + (int64_t)s2 * n * N);
+              for (int s2 = 0; s2 < ns; s2++) s += __ldcg(pr + (int64_t)s2 * n * N);
               rows[(int64_t)id * H + col] = p.tw[id] * s;
             }
           }

@@ -241,12 +241,16 @@ _ROWS_SET = False
 
 def _layer_rows_knob():
     """MOEK_B200_LAYER_ROWS (8, 16 or 32): rows per block of the whole-layer kernel instead of the automatic
-    choice (moek_set_layer_block_rows), read once."""
+    choice (moek_set_layer_block_rows); MOEK_B200_LAYER_TAIL=0: no finer k-split for the items past the last whole
+    wave of units (moek_set_layer_tail_split). Read once."""
     global _ROWS_SET
     if not _ROWS_SET:
         env = os.environ.get("MOEK_B200_LAYER_ROWS")
         if env:
             call("moek_set_layer_block_rows", int(env))
+        env = os.environ.get("MOEK_B200_LAYER_TAIL")
+        if env:
+            call("moek_set_layer_tail_split", int(env))
         _ROWS_SET = True
 
 
