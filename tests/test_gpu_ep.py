@@ -210,8 +210,9 @@ def _two_gpu_rank(rank, port, q):
         x2 = synth.activations(m2, 2048, 60 + rank, device=dev)
         ids2, wts2 = synth.route_zipf(m2, E, 5, 60 + rank, device=dev)
         out2 = ep.ep_moe(x2, layer, wts2, ids2, capacity=True)
-        # the same fixed-capacity batch over peer memory (96 received rows: the whole-layer kernel returns the
-        # partials over NVLink): identical to the NCCL exchange, call after call
+        # the same fixed-capacity batch over peer memory: 96 received rows, so the whole-layer kernel reads them in
+        # place and returns the partials over NVLink (the NCCL path above runs the tcgen05 GEMMs on them, a different
+        # fp32 order); the same bits call after call, and the same gate against the one-GPU layer
         px = ep.PeerExchange(None, m2, 2048, 5, dev)
         peer_outs = [ep.ep_moe(x2, layer, wts2, ids2, capacity=True, peer=px) for _ in range(3)]
         ref = ops.fused_moe(x, full.prep, wts, ids)
@@ -219,11 +220,15 @@ def _two_gpu_rank(rank, port, q):
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
         px.close()
-        if not all(torch.equal(o, out2) for o in peer_outs):
-            raise AssertionError("peer-memory exchange differs from the NCCL exchange")
+        if not all(torch.equal(o, peer_outs[0]) for o in peer_outs[1:]):
+            raise AssertionError("peer-memory exchange not repeatable")
+        rel_pn, _, _ = moe_ref.check(peer_outs[0].cpu(), out2.float().cpu())
+        if rel_pn > 2e-3:
+            raise AssertionError(f"peer-memory exchange differs from the NCCL exchange: rel {rel_pn:.2e}")
         rel, raw, net = moe_ref.check(out.cpu(), ref.float().cpu())
         rel2, raw2, net2 = moe_ref.check(out2.cpu(), ref2.float().cpu())
-        q.put((rank, "ok", (max(rel, rel2), max(net, net2))))
+        rel3, raw3, net3 = moe_ref.check(peer_outs[0].cpu(), ref2.float().cpu())
+        q.put((rank, "ok", (max(rel, rel2, rel3), max(net, net2, net3))))
         dist.destroy_process_group()
     except Exception as exc:
         q.put((rank, "error", repr(exc)))
