@@ -118,4 +118,8 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOEK_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden.py <checkout of the reference project> "
+                 "(or set MOEK_REFERENCE_ROOT)")
+    main(root)
