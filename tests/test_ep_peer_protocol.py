@@ -27,85 +27,119 @@ class Violation(AssertionError):
 
 
 class State:
-    def __init__(self, world):
+    """Flags, arrival counters and the generation (layer number) of each part of each segment: part g of receive
+    segment s on rank r is what CTA g of rank s's dispatch wrote; part j of back segment d is what piece j of rank
+    d's layer (or CTA j of its combine) returned."""
+
+    def __init__(self, world, parts):
         w = range(world)
-        self.world = world
-        self.recv_flag = [[0] * world for _ in w]  # [owner][sender]
-        self.back_flag = [[0] * world for _ in w]  # [owner][returner]
-        self.recv_gen = [[0] * world for _ in w]
-        self.recv_read = [[0] * world for _ in w]
-        self.back_gen = [[0] * world for _ in w]
-        self.back_read = [[0] * world for _ in w]
+        self.world, self.parts = world, parts
+        grid = lambda: [[0] * world for _ in w]
+        self.recv_flag, self.back_flag = grid(), grid()  # [owner][sender], [owner][returner]
+        self.disp_ctr, self.comb_ctr, self.piece_ctr = grid(), grid(), [0] * world
+        seg = lambda: [[[0] * parts for _ in w] for _ in w]
+        self.recv_gen, self.recv_read, self.back_gen, self.back_read = seg(), seg(), seg(), seg()
 
 
 def _program(st: State, r: int, layers: int, fused: bool, plant: str):
-    """Rank r's kernels, each a list of sub-tasks (concurrent CTAs), each a list of steps. A step is ("wait", cond)
-    or ("do", action)."""
-    W = st.world
+    """Rank r's kernels, each a list of sub-tasks (concurrent CTAs or warps), each a list of steps. A step is
+    ("wait", cond) or ("do", action)."""
+    W, G = st.world, st.parts
+    do = lambda f: ("do", f)
     kernels = []
     for L in range(1, layers + 1):
-        # dispatch: CTA d resets my back flag d, waits for d's receive flag for me to be 0, writes, raises it
+        # dispatch: CTA (d, g); g = 0 resets my back flag d; each waits for d's receive flag for me to be 0, writes
+        # its part; the last of the G arrivals (a self-resetting counter) raises d's receive flag for me
         dispatch = []
         for d in range(W):
-            steps = []
-            if plant != "dispatch_no_reset":
-                steps.append(("do", lambda d=d: st.back_flag[r].__setitem__(d, 0)))
-            if plant != "dispatch_no_wait":
-                steps.append(("wait", lambda d=d: st.recv_flag[d][r] == 0))
+            for g in range(G):
+                steps = []
+                if g == 0 and plant != "dispatch_no_reset":
+                    steps.append(do(lambda d=d: st.back_flag[r].__setitem__(d, 0)))
+                if plant != "dispatch_no_wait":
+                    steps.append(("wait", lambda d=d: st.recv_flag[d][r] == 0))
 
-            def write(d=d, L=L):
-                if st.recv_read[d][r] != L - 1:
-                    raise Violation(f"rank {r} overwrote rank {d}'s receive segment before layer {L - 1} was read")
-                st.recv_gen[d][r] = L
+                def write(d=d, g=g, L=L):
+                    if st.recv_read[d][r][g] != L - 1:
+                        raise Violation(f"rank {r} overwrote rank {d}'s receive segment before layer {L - 1} was read")
+                    st.recv_gen[d][r][g] = L
 
-            steps.append(("do", write))
-            steps.append(("do", lambda d=d: st.recv_flag[d].__setitem__(r, 1)))
-            dispatch.append(steps)
+                def arrive(d=d):
+                    st.disp_ctr[r][d] += 1
+                    if st.disp_ctr[r][d] == G:
+                        st.disp_ctr[r][d] = 0
+                        st.recv_flag[d][r] = 1
+
+                steps += [do(write), do(arrive)]
+                dispatch.append(steps)
         kernels.append(dispatch)
 
-        def read_all(L=L):
-            for s in range(W):
-                if st.recv_gen[r][s] != L:
-                    raise Violation(f"rank {r} read a stale receive segment {s} in layer {L}")
-                st.recv_read[r][s] = L
+        def read(s, g, L=L):
+            if st.recv_gen[r][s][g] != L:
+                raise Violation(f"rank {r} read a stale receive segment {s} in layer {L}")
+            st.recv_read[r][s][g] = L
 
-        def return_to(s, L=L):
-            if st.back_read[s][r] != L - 1:
+        def return_part(s, j, L=L):
+            if st.back_read[s][r][j] != L - 1:
                 raise Violation(f"rank {r} overwrote rank {s}'s back segment before layer {L - 1} was read")
-            st.back_gen[s][r] = L
+            st.back_gen[s][r][j] = L
+
+        def raise_all():
+            for s in range(W):
+                st.back_flag[s][r] = 1
 
         recv_ready = ("wait", lambda: all(st.recv_flag[r][s] == 1 for s in range(W)))
+        read_all = [do(lambda s=s, g=g, f=read: f(s, g)) for s in range(W) for g in range(G)]
         if fused:
-            # the whole-layer kernel: wait, route + compute (reads every segment), return every row, then raise
-            # every sender's back flag (the arrival that completes the last row)
-            steps = [recv_ready, ("do", read_all)]
-            returns = [("do", lambda s=s, f=return_to: f(s)) for s in range(W)]
-            raises = [("do", lambda s=s: st.back_flag[s].__setitem__(r, 1)) for s in range(W)]
-            steps += raises + returns if plant == "layer_signals_before_return" else returns + raises
-            kernels.append([steps])
+            # the whole-layer kernel: every CTA waits for the receive flags and routes (reads every segment); each
+            # piece (a row's sum for one item) goes back to its sender; the arrival that completes the last piece
+            # raises every sender's back flag (the kernel's other case, nothing to return, raises them right after
+            # the wait and is not modelled)
+            def piece_arrive():
+                st.piece_ctr[r] += 1
+                if st.piece_ctr[r] == W * G:
+                    st.piece_ctr[r] = 0
+                    raise_all()
+
+            pieces = []
+            for s in range(W):
+                for j in range(G):
+                    steps = [recv_ready] + read_all + [do(lambda s=s, j=j, f=return_part: f(s, j))]
+                    pieces.append(steps + ([] if plant == "layer_signals_before_return" else [do(piece_arrive)]))
+            if plant == "layer_signals_before_return":
+                pieces.append([recv_ready, do(raise_all)])
+            kernels.append(pieces)
         else:
             kernels.append([[recv_ready]])  # ep_wait
-            kernels.append([[("do", read_all)]])  # the local layer's kernels
-            raise_back = lambda s: ("do", lambda: st.back_flag[s].__setitem__(r, 1))
-            # combine: CTA s returns segment s and raises s's back flag
-            kernels.append([[("do", lambda s=s, f=return_to: f(s)), raise_back(s)] for s in range(W)])
+            kernels.append([read_all])  # the local layer's kernels
 
-        # unpack: wait for every back flag, clear my receive flags (CTA 0), read the back segments (other CTAs)
-        def read_back(L=L):
-            for d in range(W):
-                if st.back_gen[r][d] != L:
-                    raise Violation(f"rank {r} read a stale back segment {d} in layer {L}")
-                st.back_read[r][d] = L
+            def comb_arrive(s):
+                st.comb_ctr[r][s] += 1
+                if st.comb_ctr[r][s] == G:
+                    st.comb_ctr[r][s] = 0
+                    st.back_flag[s][r] = 1
 
-        back_ready = ("wait", lambda: all(st.back_flag[r][d] == 1 for d in range(W)))
-        clear = [("do", lambda s=s: st.recv_flag[r].__setitem__(s, 0)) for s in range(W)]
-        unpack = [[back_ready] + clear, ([] if plant == "unpack_no_wait" else [back_ready]) + [("do", read_back)]]
+            # combine: CTA (s, j) returns part j of segment s; the last of the G arrivals raises s's back flag
+            kernels.append([[do(lambda s=s, j=j, f=return_part: f(s, j)), do(lambda s=s: comb_arrive(s))]
+                            for s in range(W) for j in range(G)])
+
+        # unpack: every CTA waits for the back flags; CTA 0 clears my receive flags; the CTAs read the back segments
+        def read_back(d, j, L=L):
+            if st.back_gen[r][d][j] != L:
+                raise Violation(f"rank {r} read a stale back segment {d} in layer {L}")
+            st.back_read[r][d][j] = L
+
+        back_ready = [] if plant == "unpack_no_wait" else [("wait", lambda: all(st.back_flag[r][d] == 1
+                                                                               for d in range(W)))]
+        clear = [do(lambda s=s: st.recv_flag[r].__setitem__(s, 0)) for s in range(W)]
+        unpack = [back_ready + clear] + [back_ready + [do(lambda d=d, j=j, f=read_back: f(d, j))]
+                                         for d in range(W) for j in range(G)]
         kernels.append(unpack)
     return kernels
 
 
-def run_schedule(world, layers, fused, seed, plant=""):
-    st = State(world)
+def run_schedule(world, layers, fused, seed, plant="", parts=1):
+    st = State(world, parts)
     rng = random.Random(seed)
     progs = [_program(st, r, layers, fused, plant) for r in range(world)]
     kidx = [0] * world
@@ -136,11 +170,14 @@ def run_schedule(world, layers, fused, seed, plant=""):
                 pcs[r] = [0] * len(progs[r][kidx[r]])
 
 
+@pytest.mark.parametrize("parts", [1, 3])
 @pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
-def test_protocol_progress_and_freshness(world, fused):
-    for seed in range(300 if world <= 4 else 60):
-        run_schedule(world, layers=6, fused=fused, seed=1000 * world + seed)
+def test_protocol_progress_and_freshness(world, fused, parts):
+    """parts: CTAs per peer in dispatch and combine, and pieces per sender in the whole-layer kernel."""
+    n = (200 if world <= 4 else 30) // parts
+    for seed in range(n):
+        run_schedule(world, layers=5, fused=fused, seed=1000 * world + seed, parts=parts)
 
 
 @pytest.mark.parametrize("plant", ["dispatch_no_wait", "dispatch_no_reset", "layer_signals_before_return",
@@ -150,7 +187,7 @@ def test_planted_mistakes_are_caught(plant):
     caught = 0
     for seed in range(400):
         try:
-            run_schedule(2, layers=4, fused=True, seed=seed, plant=plant)
+            run_schedule(2, layers=4, fused=True, seed=seed, plant=plant, parts=2)
         except Violation:
             caught += 1
     assert caught > 0, plant
