@@ -208,6 +208,8 @@ def _ep_moe_peer(x, layer: EPLayer, w, ids32, px: PeerExchange, be) -> torch.Ten
     m, hid = x.shape
     k = ids32.shape[1]
     dev = x.device
+    if x.dtype != torch.bfloat16:
+        raise MoekError(f"moek_b200: hidden states must be bf16 (got {x.dtype})")
     if m > px.mcap or k != px.top_k or hid != px.hidden:
         raise MoekError(f"moek_b200: the peer exchange holds {px.mcap} tokens of {px.top_k} slots and width "
                         f"{px.hidden} (call: {m}, {k}, {hid})")
@@ -263,6 +265,9 @@ def ep_moe(hidden_states: torch.Tensor, layer: EPLayer, topk_weights: torch.Tens
     ids32 = topk_ids.to(torch.int32).contiguous()
     w = topk_weights.float().contiguous()
     if capacity and peer is not None:
+        if peer.world != world or peer.rank != dist.get_rank(group):
+            raise MoekError(f"moek_b200: the peer exchange was built for rank {peer.rank} of {peer.world}, this call "
+                            f"is rank {dist.get_rank(group)} of {world}")
         return _ep_moe_peer(x, layer, w, ids32, peer, be)
     pos, counts, offsets = be.plan(ids32, layer.num_experts, world)
     if capacity:

@@ -146,3 +146,32 @@ def test_owned_experts_and_errors():
     assert ep.owned_experts(512, 8, 3) == (192, 256)
     with pytest.raises(MoekError):
         ep.owned_experts(10, 4, 0)
+
+
+def test_peer_exchange_call_checks_on_host():
+    """ep_moe's peer-memory path rejects, before any device call, an exchange built for another process group,
+    hidden states that are not bf16, and a batch beyond the exchange's capacity (one gloo rank on the CPU)."""
+    import types
+
+    import torch.distributed as dist
+
+    from qwen38_flash_coder_b200 import ep
+    from qwen38_flash_coder_b200._lib import MoekError
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        layer = types.SimpleNamespace(world=1, num_experts=8, local_experts=8, prep=None)
+        ids = torch.zeros((4, 2), dtype=torch.int32)
+        w = torch.full((4, 2), 0.5)
+        x = torch.zeros((4, 64), dtype=torch.bfloat16)
+        other = types.SimpleNamespace(world=2, rank=0, mcap=8, top_k=2, hidden=64)
+        with pytest.raises(MoekError, match="built for rank 0 of 2"):
+            ep.ep_moe(x, layer, w, ids, capacity=True, peer=other)
+        px = types.SimpleNamespace(world=1, rank=0, mcap=2, top_k=2, hidden=64)
+        with pytest.raises(MoekError, match="bf16"):
+            ep.ep_moe(x.float(), layer, w, ids, capacity=True, peer=px)
+        with pytest.raises(MoekError, match="holds 2 tokens"):
+            ep.ep_moe(x, layer, w, ids, capacity=True, peer=px)
+    finally:
+        dist.destroy_process_group()
