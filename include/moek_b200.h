@@ -160,7 +160,7 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  *           items past a whole number of waves of the grid, those items get a finer split (see
  *           moek_set_layer_tail_split), which changes the order of the fp32 partial sums only.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
-/* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: the batch's size up to 16, else 32).
+/* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: 8 up to M = 8, else 16).
  * An expert with more routed slots than that is cut into several blocks, its weights streamed once per block.
  * Process-wide; a tuning knob with no effect on the results. */
 int moek_set_layer_block_rows(int32_t rows);

@@ -263,7 +263,10 @@ MOEK_API int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int
   return MOEK_OK;
 }
 
-// Rows per block of the whole-layer kernel (8, 16 or 32): the batch's size up to 16, else 32, unless set.
+// Rows per block of the whole-layer kernel (8, 16 or 32): 8 up to M = 8, else 16, unless set. Above 16 rows, a hot
+// expert's block costs up to four times a cold one's per unit and units are dealt round-robin: on B200 at M = 32 with
+// Zipf routing the slowest CTA ended at 133 us with 32-row blocks and at 105 us with 16-row blocks (the weights of an
+// expert with more than 16 slots are then streamed twice).
 static int g_layer_rows = 0;
 MOEK_API int moek_set_layer_block_rows(int32_t rows) {
   if (rows != 0 && rows != 8 && rows != 16 && rows != 32)
@@ -279,7 +282,7 @@ MOEK_API int moek_set_layer_tail_split(int32_t on) {
 }
 static int layer_block_rows(int M) {
   if (g_layer_rows) return g_layer_rows;
-  return M <= 8 ? 8 : M <= 16 ? 16 : 32;
+  return M <= 8 ? 8 : 16;
 }
 
 // Checks and parameters shared by moek_moe_layer and moek_moe_layer_p2p (rows_ws: the fp32 slot rows live in the

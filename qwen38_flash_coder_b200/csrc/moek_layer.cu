@@ -73,28 +73,27 @@ struct UnitMeta {
 // unit after the last full wave instead of one full unit (the idea of stream-K, with no fix-up beyond the split-k
 // arrivals the kernel has anyway).
 struct PhasePlan {
-  int ni_main, s_main, s_tail;
-  int64_t u_main, u_total;
+  int ni_main, s_main, s_tail, u_main, u_total;  // at most 512 blocks x 16 items x 32 splits: 32-bit
 };
 __device__ __forceinline__ PhasePlan plan_phase(const LayerMat& m, int nblk, int grid, bool tail) {
   PhasePlan q;
   const int ni = nblk * m.nt;
   q.s_main = q.s_tail = m.nsplit;
   q.ni_main = ni;
-  const int64_t main_units = (int64_t)ni * m.nsplit;
+  const int main_units = ni * m.nsplit;
   if (tail && main_units > grid) {
-    const int nim = (int)(main_units / grid * grid / m.nsplit);
+    const int nim = main_units / grid * grid / m.nsplit;
     const int rem = ni - nim;
     int st = m.nsplit;
     for (int s = m.nsplit + 1; s <= m.nstage; s++)
-      if (m.nstage % s == 0 && (int64_t)rem * s <= grid) st = s;
+      if (m.nstage % s == 0 && rem * s <= grid) st = s;
     if (rem > 0 && st > m.nsplit) {
       q.ni_main = nim;
       q.s_tail = st;
     }
   }
-  q.u_main = (int64_t)q.ni_main * q.s_main;
-  q.u_total = q.u_main + (int64_t)(ni - q.ni_main) * q.s_tail;
+  q.u_main = q.ni_main * q.s_main;
+  q.u_total = q.u_main + (ni - q.ni_main) * q.s_tail;
   return q;
 }
 
@@ -109,7 +108,8 @@ struct Cfg {
   static constexpr int LUT_OFF = IDS_OFF + MAXU * XR * 4;
   static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 4;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
   static constexpr int MISC_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;
-  static constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
+  static constexpr int PLAN_OFF = MISC_OFF + 16;  // the two phase plans
+  static constexpr int BAR_OFF = (PLAN_OFF + 2 * (int)sizeof(PhasePlan) + 7) / 8 * 8;
   static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
   static constexpr int T = XR / 8;
   static constexpr int MINB = 2;
@@ -167,22 +167,22 @@ __device__ __forceinline__ void ep_signal(const LayerParams& p) {
            1);
 }
 
-__device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePlan& q0, const PhasePlan& q1, int64_t u,
+__device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePlan& q0, const PhasePlan& q1, int u,
                                             UnitMeta& um) {
   um.ph = u >= q0.u_total ? 1 : 0;
   const LayerMat& m = p.m[um.ph];
   const PhasePlan& q = um.ph ? q1 : q0;
-  const int64_t v = um.ph ? u - q0.u_total : u;
+  const int v = um.ph ? u - q0.u_total : u;
   int ii;
   if (v < q.u_main) {
-    ii = (int)(v / q.s_main);
-    um.ks = (int)(v - (int64_t)ii * q.s_main);
+    ii = v / q.s_main;
+    um.ks = v - ii * q.s_main;
     um.ns = q.s_main;
   } else {
-    const int64_t w = v - q.u_main;
-    const int t = (int)(w / q.s_tail);
+    const int w = v - q.u_main;
+    const int t = w / q.s_tail;
     ii = q.ni_main + t;
-    um.ks = (int)(w - (int64_t)t * q.s_tail);
+    um.ks = w - t * q.s_tail;
     um.ns = q.s_tail;
   }
   um.blk = ii / m.nt;
@@ -293,6 +293,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       if (lane == 0) {
         bstart[base] = nvalid;
         misc[0] = base;
+        const int nb = *abort_flag ? 0 : base;  // the plans, once per CTA (every thread reads them after the barrier)
+        PhasePlan* pl = reinterpret_cast<PhasePlan*>(smem + C::PLAN_OFF);
+        pl[0] = plan_phase(p.m[0], nb, gridDim.x, p.tail);
+        pl[1] = plan_phase(p.m[1], nb, gridDim.x, p.tail);
       }
     }
     __syncthreads();
@@ -302,19 +306,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   if (p.ep_peer && ep_rows == 0 && !*abort_flag && blockIdx.x == 0 && tid == 0)
     ep_signal(p);  // nothing to return: release the senders' waits at once
 
-  // tokens with no valid slot get a zero output row (nothing else writes them)
-  if (blockIdx.x == 0 && p.out && warp < NCW) {
-    for (int t = warp; t < p.M; t += NCW) {
-      const int e = lane < k ? p.ids[t * k + lane] : -1;
-      if (__any_sync(0xffffffffu, e >= 0 && e < p.E)) continue;
-      for (int c = lane; c < p.H; c += 32) p.out[(int64_t)t * p.H + c] = __float2bfloat16_rn(0.f);
-    }
-  }
 
-  const PhasePlan plan0 = plan_phase(p.m[0], nblk, gridDim.x, p.tail),
-                  plan1 = plan_phase(p.m[1], nblk, gridDim.x, p.tail);
-  const int64_t U = plan0.u_total + plan1.u_total;
-  const int n_mine = U > blockIdx.x ? (int)((U - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  const PhasePlan plan0 = reinterpret_cast<const PhasePlan*>(smem + C::PLAN_OFF)[0],
+                  plan1 = reinterpret_cast<const PhasePlan*>(smem + C::PLAN_OFF)[1];
+  const int U = plan0.u_total + plan1.u_total;
+  const int n_mine = U > (int)blockIdx.x ? (U - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int rounds = (n_mine + MAXU - 1) / MAXU;
 
   if (warp == W_PROD) {  // ------------------------------------------------------------------------- producer
@@ -325,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, abort_flag)) break;
       for (int i = lane; i < nu; i += 32) {
         UnitMeta& m = meta[i];
-        decode_unit(p, plan0, plan1, blockIdx.x + (int64_t)(u0 + i) * gridDim.x, m);
+        decode_unit(p, plan0, plan1, (int)blockIdx.x + (u0 + i) * (int)gridDim.x, m);
         m.e = bexp[m.blk];
         const int b0 = bstart[m.blk], cnt = bstart[m.blk + 1] - b0;
         m.nv = min(cnt, XR);
@@ -748,6 +744,16 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(mempty);
+    }
+  }
+
+  // tokens with no valid slot get a zero output row (nothing else writes them): the last CTA, which has the fewest
+  // units, once its own work is done, so that no CTA starts streaming late
+  if (blockIdx.x == gridDim.x - 1 && p.out && warp < NCW) {
+    for (int t = warp; t < p.M; t += NCW) {
+      const int e = lane < k ? p.ids[t * k + lane] : -1;
+      if (__any_sync(0xffffffffu, e >= 0 && e < p.E)) continue;
+      for (int c = lane; c < p.H; c += 32) p.out[(int64_t)t * p.H + c] = __float2bfloat16_rn(0.f);
     }
   }
 
