@@ -45,9 +45,13 @@ METRIC = "routed-MoE layer µs & HBM GB/s (M=8,32); TFLOP/s (M=6912); 1/2/4/8 GP
 H, I, E, TOPK = 2048, 512, 512, 5
 FLOPS_PER_ROW = 2 * 3 * H * I  # gate + up + down per (token, slot) row
 
-# DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu --set full capture each (layer 0):
-# profiles/moek_layer_kernel_decode8.md and profiles/moek_prefill_kernel_prefill6912.md (gate_up launch)
-TRAFFIC = {"decode8": 64_508_928, "prefill": 696_396_544}
+# DRAM bytes (read + write) of one launch of the roofline kernel, dram__bytes_read.sum + dram__bytes_write.sum of
+# layer 0's launch in one ncu capture of this file's own command with the kernels named below; not measured by the
+# run that prints them (the capture's command and date travel with the figure as "traffic_source").
+TRAFFIC = {
+    "decode8": (64_508_928, "ncu capture, moek_layer_kernel<8> of the 44 us build (before the dequant rework)"),
+    "prefill": (696_396_544, "ncu capture, moek_prefill_kernel gate_up launch (fp32-row down epilogue build)"),
+}
 
 WORKLOADS = {
     "decode8": dict(m=8, route="uniform", unit="GB/s", desc="decode verify M=8 (1 stream x block 8), uniform routing"),
@@ -219,6 +223,19 @@ def timed(fn, steps, barrier):
     return e0.elapsed_time(e1) / steps
 
 
+def gate_stats(out, ref):
+    """(rel-L2, net max-abs / rms) of a bf16 result against a reference: the parity gate's two figures, the max-abs
+    taken beyond half a bf16 ulp of the reference (the rounding of the output itself)."""
+    import torch
+
+    o, r = out.float(), ref.float()
+    rel = float((o - r).norm() / r.norm().clamp_min(1e-30))
+    rms = float(r.pow(2).mean().sqrt().clamp_min(1e-30))
+    half_ulp = torch.pow(2.0, torch.floor(torch.log2(r.abs().clamp_min(2.0 ** -126))) - 8)
+    net = float(((o - r).abs() - half_ulp).clamp_min(0).max()) / rms if o.numel() else 0.0
+    return rel, net
+
+
 def over_ranks(v, world, dev, op="max"):
     """The max (or sum) of a per-rank number over all ranks."""
     import torch
@@ -238,10 +255,12 @@ def cpu_baseline(layers, name, budget_s=12.0):
 
     from oracle import moe_ref
 
+    from qwen38_flash_coder_b200 import ops
+
     torch.set_num_threads(os.cpu_count())
     wl = WORKLOADS[name]
     sample_m = min(wl["m"], 256)
-    amount, tot, n = 0.0, 0.0, 0
+    amount, tot, n, checks = 0.0, 0.0, 0, []
     while n < len(layers) and (tot < budget_s or n == 0):
         w13, w2 = layers[n]["ckpt"]
         x = layers[n]["x"][name][:sample_m]
@@ -254,16 +273,22 @@ def cpu_baseline(layers, name, budget_s=12.0):
         c13, c2, cid = cpu(w13), cpu(w2), remap[ids.long()].cpu().numpy()
         xc, wc = x.cpu(), wts.cpu().numpy()
         t1 = time.perf_counter()
-        moe_ref.reference(xc, cid, wc, c13, c2)
+        ref = moe_ref.reference(xc, cid, wc, c13, c2)
         tot += time.perf_counter() - t1
+        # the oracle as the checker: this build's output for the same tokens must be inside the gate
+        got = ops.fused_moe(x, layers[n]["prep"], wts, ids)
+        checks.append(moe_ref.check(got.cpu(), ref))
         if wl["unit"] == "GB/s":
             amount += touched_bytes(layers[n]["prep"], ids, sample_m)[0] / 1e9
         else:
             amount += sample_m * TOPK * FLOPS_PER_ROW / 1e12
         n += 1
+    rel, net = max(c[0] for c in checks), max(c[2] for c in checks)
+    parity = {"vs": "the fp32 oracle (oracle/moe_ref.py) on the sampled tokens", "rel_l2": rel, "net_maxabs": net,
+              "gate": "rel-L2 <= 5e-3, net max-abs <= 2e-2 * rms", "ok": bool(rel <= 5e-3 and net <= 2e-2)}
     return {"value": round(amount / tot, 6), "unit": wl["unit"], "cores": os.cpu_count(), "kind": "port",
             "sample": f"{n} layer(s) x {sample_m} tokens of this workload (touched experts only), torch-CPU oracle "
-                      f"(oracle/moe_ref.py), {tot:.1f} s of compute"}
+                      f"(oracle/moe_ref.py), {tot:.1f} s of compute"}, parity
 
 
 def measure(name, layers, a, dev, world, barrier, headline):
@@ -308,7 +333,7 @@ def measure(name, layers, a, dev, world, barrier, headline):
     pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pp):
         peaks = json.load(open(pp))
-    traffic = TRAFFIC.get(name)
+    traffic, traffic_src = TRAFFIC.get(name, (None, None))
     if wl["unit"] == "GB/s":  # the whole-layer kernel: every touched expert's gate_up and down bytes, x, out
         gb = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] for L in layers) / nl
         peak = peaks.get("hbm_gbs", 6650.0)
@@ -316,8 +341,8 @@ def measure(name, layers, a, dev, world, barrier, headline):
         roof = {"kernel": "moek_layer_kernel (whole decode layer, one launch)", "bound": "hbm",
                 "achieved": round(achieved, 1), "peak": peak,
                 "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
-                "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic, "bytes_per_launch": int(gb),
-                "avg_launch_us": round(kern_us["layer"], 2)}
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+                "bytes_per_launch": int(gb), "avg_launch_us": round(kern_us["layer"], 2)}
     else:
         flops = m * TOPK * 2 * H * 2 * I  # gate + up rows of real tokens
         peak = peaks.get("bf16_tflops_sustained", 1400.0)
@@ -325,7 +350,8 @@ def measure(name, layers, a, dev, world, barrier, headline):
         roof = {"kernel": "moek_prefill_kernel (gate_up, tcgen05)", "bound": "tensor", "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": "of measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
                 if "bf16_tflops_sustained" in peaks else "of fallback", "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic, "flops_per_launch": flops}
+                "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+                "flops_per_launch": flops}
     if "gate_gemm" in kern_us:
         roof["avg_launch_us"] = round(kern_us["gate_gemm"], 2)
         roof["down_gemm_avg_us"] = round(kern_us["down_gemm"], 2)
@@ -408,9 +434,9 @@ def main():
 
     results = {n: measure(n, layers, a, dev, world, barrier, headline=(n == a.workload)) for n in names}
     head = results.pop(a.workload)
-    cpu = None
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline(layers[:3], a.workload)
+        cpu, parity = cpu_baseline(layers[:3], a.workload)
     if world > 1:
         torch.distributed.barrier()
     if rank == 0:
@@ -428,7 +454,7 @@ def main():
             "e2e": head["e2e"], "clocks": head["clocks"],
             "gpu_launches": head["gpu_launches_per_step"] * a.steps,
             "eager_ms_per_step": head["eager_ms_per_step"],
-            "workloads": results,
+            "workloads": results, "parity": parity,
         }
         if "touched_experts_per_layer" in head:
             line["touched_experts_per_layer"] = head["touched_experts_per_layer"]
@@ -453,7 +479,7 @@ def ep_main(a, rank, world, dev):
     import torch
     import torch.distributed as dist
 
-    from qwen38_flash_coder_b200 import ep, ops, synth
+    from qwen38_flash_coder_b200 import ep, ops, prep, synth
 
     names = ["decode8"] if a.only else ["decode8", "decode64", "prefill"]
     layers, touched_bytes_all = [], []
@@ -469,10 +495,33 @@ def ep_main(a, rank, world, dev):
             entry["x"][n] = synth.activations(m, H, seed, device=dev)
             entry["route"][n] = route(m, seed, EP_WORKLOADS[n]["route"], dev)
         layers.append(entry)
+    # parity: one more seeded layer, held whole (all 512 experts) on every rank besides its EP shard, so that every
+    # rank can compare its tokens' expert-parallel output with the one-GPU layer before anything is timed
+    pw13, pw2 = synth.make_layer(E, H, I, 977, device=dev)
+    par_full = prep.PreparedLayer(pw13, pw2)
+    par_ep = ep.EPLayer(ep.shard_checkpoint(pw13, E, world, rank), ep.shard_checkpoint(pw2, E, world, rank), E,
+                        world, rank)
+    del pw13, pw2
     torch.cuda.empty_cache()
+    parity = {}
 
     def barrier():
         dist.barrier()
+
+    def check_parity(name, wl, px):
+        """ep.ep_moe on this rank's seeded tokens against ops.fused_moe of the same tokens on this GPU with every
+        expert; the worst rank's figures."""
+        seed = 100000 * rank + 99
+        x = synth.activations(wl["m"], H, seed, device=dev)
+        ids, wts = route(wl["m"], seed, wl["route"], dev)
+        got = ep.ep_moe(x, par_ep, wts, ids, capacity=wl["capacity"], peer=px)
+        ref = ops.fused_moe(x, par_full, wts, ids)
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        rel, net = gate_stats(got, ref)
+        rel, net = over_ranks(rel, world, dev), over_ranks(net, world, dev)
+        parity[name] = {"rel_l2": rel, "net_maxabs": net, "ok": bool(rel <= 5e-3 and net <= 2e-2),
+                        "exchange": "peer memory" if px is not None else "NCCL"}
 
     def local_touched_bytes(entry, name):
         """Bytes of this rank's experts that any rank's tokens touch in this layer (each streamed once by its
@@ -500,6 +549,8 @@ def ep_main(a, rank, world, dev):
             for e in layers:
                 ids, wts = e["route"][name]
                 ep.ep_moe(e["x"][name], e["layer"], wts, ids, backend=be, capacity=wl["capacity"], peer=px)
+
+        check_parity(name, wl, px)
 
         for _ in range(max(3, a.warmup)):
             step()
@@ -631,8 +682,13 @@ def ep_main(a, rank, world, dev):
             "us_per_layer": head["us_per_layer"], "roofline": head["roofline"], "cpu_baseline": None,
             "e2e": head["e2e"], "clocks": head["clocks"],
             "gpu_launches": head["gpu_launches_per_step"] * a.steps, "launch": head["launch"], "workloads": results,
+            "parity": {"vs": "ops.fused_moe on one GPU holding all 512 experts, the same tokens (every rank its own; "
+                             "worst rank)", "gate": "rel-L2 <= 5e-3, net max-abs <= 2e-2 * rms",
+                       "ok": all(v["ok"] for v in parity.values()), "workloads": parity},
         }
         print(json.dumps(line), flush=True)
+    if not all(v["ok"] for v in parity.values()):
+        raise SystemExit(f"expert-parallel output outside the parity gate: {parity}")
 
 
 def reference_arm(a, rank, world):

@@ -31,7 +31,7 @@ enum {
 };
 
 /* Device-side error codes written to the error word (cnt[0] of moek_gemm); 0 means none. */
-enum { MOEK_DEV_TIMEOUT = 1, MOEK_DEV_BAD_EXPERT = 2, MOEK_DEV_TOO_MANY_ROWS = 3 };
+enum { MOEK_DEV_TIMEOUT = 1, MOEK_DEV_BAD_EXPERT = 2, MOEK_DEV_TOO_MANY_ROWS = 3, MOEK_DEV_BAD_INPUT = 4 };
 
 /* Last error message of the calling thread (empty if none). No reference counterpart (the reference raised
  * c10::Error from TORCH_CHECK, files/mbx_moek.cu:727-755). */
@@ -39,6 +39,22 @@ const char* moek_last_error(void);
 
 /* ABI version of this header (1). */
 int moek_version(void);
+
+/* Build flags of the loaded library: bit 0 = MOEK_TRACE (timeline stamps), bit 1 = MOEK_DEBUG_CHECKS (every index
+ * taken from an input is range-checked before use; a bad one records MOEK_DEV_BAD_INPUT and the access is skipped).
+ * No reference counterpart (the reference's trace flag is a compile-time switch of its kernel, files/mbx_moek.cu:
+ * 152-160). */
+int moek_build_flags(void);
+/* MOEK_TRACE builds: copy the %globaltimer stamps [1024 CTAs][64 slots] (uint64, nanoseconds; 0 = not reached) of the
+ * last launches of one kernel family to host memory dst (bytes <= 512 KiB are copied). kind 0: the whole-layer
+ * kernel (0 start, 1 after the dependent-launch wait, 2 expert-parallel flags seen, 3 routing done, 4 first weight
+ * copy issued, 5 consumers done, 6 end, 7 unit count; per unit u < 16 of the CTA: 8 + 3u first stage ready, 9 + 3u
+ * last stage done, 10 + 3u finished; 56-63: the first four act waits, start and end); kind 1: the tcgen05 GEMM (0 start,
+ * 1 after the wait, 6 end; per unit: 8 + 3u first MMA, 9 + 3u last MMA issued, 10 + 3u accumulator drained);
+ * kind 2: the peer-exchange kernels (dispatch: 0 start, 1 destination free, 2 rows written, 3 flag raised; unpack:
+ * 8 start, 9 partials ready, 10 done). Other builds return MOEK_ERR_UNSUPPORTED. moek_trace_clear zeroes them. */
+int moek_trace_read(int32_t kind, void* dst, size_t bytes);
+int moek_trace_clear(void);
 
 /* Bound on every device-side wait (default 2 s). After it a kernel records MOEK_DEV_TIMEOUT and returns instead of
  * hanging. No reference counterpart (its waits are unbounded, files/mbx_moek.cu:87-93). */
@@ -66,8 +82,10 @@ int moek_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int3
  * 1024 indices is a fixed 512 KiB array inside the library, held on every GPU that loads the library until the
  * process exits, and shared by all calls on that GPU: calls that overlap on the GPU (two streams at once) race on
  * it, so serialise them. It keeps the last call's contents, and nothing in it needs to start at zero (every call
- * writes what it reads). The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
- * caches it; make that first call before any stream capture on that device. */
+ * writes what it reads). The first call on a device with more than 1024 indices looks up the array's device address
+ * (cudaGetSymbolAddress) and caches it; make that first call before any stream capture on that device (calls of up to
+ * 1024 indices use no scratch and look nothing up). The cached address belongs to the device's primary context: after
+ * cudaDeviceReset on that device, do not call this entry point again in the same process. */
 int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
                        int32_t* sorted_ids, int64_t sorted_len, int32_t* expert_ids, int64_t expert_len,
                        int32_t* num_post_pad, void* stream);
@@ -78,11 +96,11 @@ int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_exper
  *   A       bf16: gate_up: hidden states [M, K] (row id / top_k); down: act [num_ids, K] (row id, top_k = 1).
  *   S       must be NULL (plain Marlin scales go with Marlin's untiled weight layout, which this build does not use);
  *           tiled must be 1.
- *   mode    0: the tcgen05 path for large batches (block_m <= 128, K <= 4096, nsplit 1): gate_up writes act bf16
- *           [num_ids, N/2] = bf16(silu(g) * u) to out; down writes the fp32 rows topk_w[id] * sum to part
- *           [num_ids, N] (finish with moek_combine).
- *           1: as 0, but act is kept in moe_align's sorted order: gate_up writes act row sorted position (out holds
- *           sorted_len rows) and down reads A by sorted position, one 128-row tile per stage instead of a gather.
+ *   mode    0, 1: the reference's output contract (files/mbx_moek.cu:620-647; the kit's prefill call,
+ *           files/mbx_moek.py:276-283), on this build's tcgen05 path (block_m <= 128, K <= 4096, nsplit 1; the
+ *           reference's item-counter and stream-k schedules are one schedule here): gate_up writes act bf16
+ *           [num_ids, N/2] = bf16(silu(g) * u) to out; down writes dout bf16 [num_ids, N] = bf16(topk_w[id] * sum)
+ *           to out. part is unused.
  *           2: split-k; the kernel writes fp32 partial sums part[nsplit][num_ids][N] (gate_up: gate at column c, up
  *           at N/2 + c) and moek_split_epilogue finishes (the reference's mode 2).
  *           3: the epilogue is fused. nsplit 1: gate_up writes act bf16 [num_ids, N/2] = bf16(silu(g) * u) to out;
@@ -92,7 +110,11 @@ int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_exper
  *           (part holds (nsplit + 1) * num_ids * N floats) and the arrival that completes a token's valid slots
  *           writes out bf16 [num_ids/combine_k, N] = their sum in slot order (slots whose topk_ids entry is outside
  *           [0, E) are left out).
- *           (The reference's own modes 0/1, its atomic item counter and stream-k, are not available.)
+ *           4: the tcgen05 path with fp32 rows: gate_up as mode 0; down writes the fp32 rows topk_w[id] * sum to
+ *           part [num_ids, N] (finish with moek_combine), out unused.
+ *           5: as 4, but act is kept in moe_align's sorted order: gate_up writes act row sorted position (out holds
+ *           sorted_len rows) and down reads A by sorted position, one 128-row tile per stage instead of a gather.
+ *           Modes 3-5 are this build's own; other values are rejected with MOEK_ERR_UNSUPPORTED.
  *   nsplit  K/64/nsplit must be even (whole packed-scale runs), K/128/nsplit <= 32.
  *   cnt     int32, zero-filled before the first call; cnt[0] is the device error word (MOEK_DEV_*), cnt[1..] the
  *           split counters (mode 3, nsplit > 1: 1 + max_blocks * N/256 entries, down + (num_ids/combine_k) * N/256,
@@ -168,6 +190,12 @@ int moek_set_layer_block_rows(int32_t rows);
  * the default) so that a phase ends soon after its last full wave. Process-wide tuning knob; it changes only the
  * order of fp32 partial sums. */
 int moek_set_layer_tail_split(int32_t on);
+/* Whether the whole-layer kernel is launched as a cooperative grid (on != 0, the default). Its down units wait
+ * (bounded) on gate_up units of other CTAs, so all of its CTAs must be resident at once; a cooperative launch makes
+ * the runtime start the grid only when they all are, also while kernels of other streams hold part of the GPU
+ * (with on = 0 such a stream could hold CTAs back past the wait bound and the layer would end in MOEK_DEV_TIMEOUT).
+ * Process-wide. No reference counterpart (the reference's kernels do not wait across CTAs). */
+int moek_set_layer_cooperative(int32_t on);
 
 int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const int32_t* topk_ids,
                    const float* topk_w, int32_t top_k, const void* w13, const uint8_t* sp13, const float* g13,

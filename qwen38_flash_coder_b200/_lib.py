@@ -1,8 +1,11 @@
-"""ctypes binding of libmoek_b200.so (include/moek_b200.h). Loading fails loudly: there is no fallback path."""
+"""ctypes binding of libmoek_b200.so (include/moek_b200.h). Loading fails loudly: there is no fallback path.
+
+``MOEK_B200_LIB=trace`` or ``=debug`` loads the instrumented build of the same kernels instead (``build.py``): the
+timeline stamps of ``qwen38_flash_coder_b200.trace``, or the input-index checks."""
 import ctypes
 import os
 
-from .build import LIB
+from .build import lib_path
 
 _P, _I32, _I64, _U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64
 
@@ -12,6 +15,7 @@ SIGNATURES = {
     "moek_set_wait_timeout_ns": (ctypes.c_int, [_U64]),
     "moek_set_layer_block_rows": (ctypes.c_int, [_I32]),
     "moek_set_layer_tail_split": (ctypes.c_int, [_I32]),
+    "moek_set_layer_cooperative": (ctypes.c_int, [_I32]),
     "moek_align_workspace_bytes": (ctypes.c_int, [_I64, _I32, ctypes.POINTER(ctypes.c_size_t)]),
     "moek_align": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P, ctypes.c_size_t, _P]),
     "moek_align_noalloc": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _P, _P]),
@@ -41,6 +45,9 @@ SIGNATURES = {
     "moek_ep_unpack_p2p": (ctypes.c_int, [_P] + [_I32] * 5 + [_P, _I32, _P, _P, _P]),
     "moek_moe_layer_p2p": (ctypes.c_int, [_P, _P] + [_I32] * 7 + [_P] * 10 + [_I32, _I32, _P, ctypes.c_size_t, _P,
                                                                               _I64, _P, _P]),
+    "moek_build_flags": (ctypes.c_int, []),
+    "moek_trace_read": (ctypes.c_int, [_I32, _P, ctypes.c_size_t]),
+    "moek_trace_clear": (ctypes.c_int, []),
 }
 
 _lib = None
@@ -50,13 +57,22 @@ class MoekError(RuntimeError):
     pass
 
 
+def variant() -> str:
+    v = os.environ.get("MOEK_B200_LIB", "")
+    if v not in ("", "trace", "debug"):
+        raise ImportError(f"moek_b200: MOEK_B200_LIB={v!r}: the variants are trace and debug")
+    return v
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB):
-            raise ImportError(f"moek_b200: {LIB} is missing; build it with `python -m qwen38_flash_coder_b200.build`"
-                              " (nvcc, sm_100a). There is no fallback implementation.")
-        h = ctypes.CDLL(LIB)
+        path = lib_path(variant())
+        if not os.path.exists(path):
+            raise ImportError(f"moek_b200: {path} is missing; build it with `python -m qwen38_flash_coder_b200.build"
+                              f"{' --variant=' + variant() if variant() else ''}` (nvcc, sm_100a). There is no "
+                              "fallback implementation.")
+        h = ctypes.CDLL(path)
         for name, (res, args) in SIGNATURES.items():
             f = getattr(h, name)
             f.restype, f.argtypes = res, args

@@ -60,6 +60,37 @@ MOEK_API const char* moek_last_error(void) { return g_msg; }
 
 MOEK_API int moek_version(void) { return 1; }
 
+MOEK_API int moek_build_flags(void) {
+  int f = 0;
+#ifdef MOEK_TRACE
+  f |= 1;
+#endif
+#ifdef MOEK_DEBUG_CHECKS
+  f |= 2;
+#endif
+  return f;
+}
+
+// Timeline stamps (MOEK_TRACE builds): kind 0 = the whole-layer kernel, 1 = the tcgen05 GEMM, 2 = the EP peer
+// exchange kernels; dst is host memory of `bytes` (at most 1024 CTAs x 64 slots x 8 bytes are copied).
+MOEK_API int moek_trace_read(int32_t kind, void* dst, size_t bytes) {
+  if (!dst || kind < 0 || kind > 2) return fail(MOEK_ERR_ARG, "moek_b200: trace_read needs kind 0-2 and a buffer");
+  cudaError_t e = kind == 0 ? moek::trace_copy_layer(dst, bytes, 0)
+                : kind == 1 ? moek::trace_copy_prefill(dst, bytes, 0)
+                            : moek::trace_copy_ep(dst, bytes, 0);
+  if (e == cudaErrorNotSupported)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: this library was built without MOEK_TRACE (use the trace variant)");
+  return cuda_status(e, "trace_read");
+}
+MOEK_API int moek_trace_clear(void) {
+  cudaError_t e = moek::trace_copy_layer(nullptr, 0, 1);
+  if (e == cudaErrorNotSupported)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: this library was built without MOEK_TRACE (use the trace variant)");
+  if (e == cudaSuccess) e = moek::trace_copy_prefill(nullptr, 0, 1);
+  if (e == cudaSuccess) e = moek::trace_copy_ep(nullptr, 0, 1);
+  return cuda_status(e, "trace_clear");
+}
+
 MOEK_API int moek_set_wait_timeout_ns(uint64_t ns) {
   if (ns == 0) return fail(MOEK_ERR_ARG, "moek_b200: the wait timeout must be positive");
   g_timeout_ns = ns;
@@ -114,16 +145,26 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
     return fail(MOEK_ERR_ARG, "moek_b200: moe_gemm null pointer");
   if (!gate_up && top_k != 1) return fail(MOEK_ERR_ARG, "moek_b200: down reads one activation row per id (top_k 1)");
   if (top_k <= 0) return fail(MOEK_ERR_ARG, "moek_b200: top_k must be positive");
-  if (mode < 0 || mode > 3)
-    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (0-3)", mode);
-  if (mode <= 1) {  // tcgen05 path: whole K per unit, direct epilogue; mode 1: act rows in moe_align's sorted order
-    if (K / 128 > 32) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: mode 0 supports K <= 4096 (got %d)", K);
+  if (mode < 0 || mode > 5)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_gemm mode %d is not available in this build (0-5)", mode);
+  // tcgen05 path, whole K per unit, direct epilogue. 0/1: the reference's output contract (gate_up: act to out; down:
+  // bf16 rows bf16(topk_w * sum) to out); 4: down writes fp32 rows to part; 5: as 4 with act in sorted order.
+  const bool tc = mode == 0 || mode == 1 || mode == 4 || mode == 5;
+  if (tc) {
+    const bool kit = mode <= 1;
+    if (K / 128 > 32) return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: mode %d supports K <= 4096 (got %d)", mode, K);
+    if (nsplit != 1) return fail(MOEK_ERR_ARG, "moek_b200: mode %d takes whole K per unit (nsplit 1, got %d)", mode,
+                                 nsplit);
     if (block_m > moek::prefill_block_m())
-      return fail(MOEK_ERR_ARG, "moek_b200: mode 0 takes moe_align blocks of <= %d rows (got %d)",
+      return fail(MOEK_ERR_ARG, "moek_b200: mode %d takes moe_align blocks of <= %d rows (got %d)", mode,
                   moek::prefill_block_m(), block_m);
-    if (gate_up ? !out : (!topk_w || !part || part_len < (int64_t)num_ids * N))
-      return fail(MOEK_ERR_ARG, "moek_b200: mode 0 gate_up writes act to out; down writes fp32 rows to part "
-                                "(num_ids * N floats) and needs topk_w");
+    if (gate_up && !out) return fail(MOEK_ERR_ARG, "moek_b200: mode %d gate_up writes act to out", mode);
+    if (!gate_up && kit && (!topk_w || !out))
+      return fail(MOEK_ERR_ARG, "moek_b200: mode %d down writes bf16(topk_w * sum) rows to out and needs topk_w",
+                  mode);
+    if (!gate_up && !kit && (!topk_w || !part || part_len < (int64_t)num_ids * N))
+      return fail(MOEK_ERR_ARG, "moek_b200: mode %d down writes fp32 rows to part (num_ids * N floats) and needs "
+                                "topk_w", mode);
     if (!cnt || cnt_len < 1) return fail(MOEK_ERR_ARG, "moek_b200: cnt[0] is the device error word");
     moek::GemmParams p{};
     p.A = static_cast<const __nv_bfloat16*>(A);
@@ -151,8 +192,10 @@ MOEK_API int moek_gemm(const void* A, const void* W, const void* S, const float*
                                           (num_ids + block_m - 1) / block_m + std::min<int64_t>(E, num_ids));
     p.gate_up = gate_up ? 1 : 0;
     p.mode = mode;
-    // mode 1 down reads A (act) by sorted position: sorted_len rows; otherwise A rows are tokens (num_ids / top_k)
-    p.a_rows = (mode == 1 && !gate_up) ? (int)sorted_len : std::max(1, num_ids / top_k);
+    p.sorted_act = mode == 5 ? 1 : 0;
+    p.down_bf16 = kit && !gate_up ? 1 : 0;
+    // sorted-order down reads A (act) by sorted position: sorted_len rows; otherwise A rows are tokens
+    p.a_rows = (p.sorted_act && !gate_up) ? (int)sorted_len : std::max(1, num_ids / top_k);
     return cuda_status(moek::launch_prefill(p, sm_count(), (cudaStream_t)stream), "moe_gemm (tcgen05) launch");
   }
   const int nstage = K / moek::BK;
@@ -280,6 +323,13 @@ MOEK_API int moek_set_layer_tail_split(int32_t on) {
   g_layer_tail = on ? 1 : 0;
   return MOEK_OK;
 }
+// Whether the whole-layer kernel is launched as a cooperative grid (default on): its down units wait on gate_up
+// units of other CTAs, so every CTA must be resident at once; a cooperative launch makes the runtime guarantee it.
+static int g_layer_coop = 1;
+MOEK_API int moek_set_layer_cooperative(int32_t on) {
+  g_layer_coop = on ? 1 : 0;
+  return MOEK_OK;
+}
 static int layer_block_rows(int M) {
   if (g_layer_rows) return g_layer_rows;
   return M <= 8 ? 8 : 16;
@@ -376,7 +426,7 @@ MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int3
   if (out && out_rows) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer writes either out (bf16 sums) or out_rows");
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_rows = out_rows;
-  return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), (cudaStream_t)stream),
+  return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), g_layer_coop, (cudaStream_t)stream),
                      "moe_layer launch");
 }
 
@@ -488,7 +538,7 @@ MOEK_API int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t w
   p.ep_world = world;
   p.ep_rank = rank;
   p.ep_mcap = mcap;
-  return cuda_status(moek::launch_layer(p, layer_block_rows(R), sm_count(), (cudaStream_t)stream),
+  return cuda_status(moek::launch_layer(p, layer_block_rows(R), sm_count(), g_layer_coop, (cudaStream_t)stream),
                      "moe_layer_p2p launch");
 }
 

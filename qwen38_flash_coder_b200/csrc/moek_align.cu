@@ -310,8 +310,8 @@ extern "C" __attribute__((visibility("default"))) int moek_align_noalloc(
                      (long long)sorted_len, (long long)need, (long long)expert_len);
   if ((sorted_len && !sorted_ids) || (expert_len && !expert_ids) || !num_post_pad || (numel && !topk_ids))
     return set_error(1, "moek_b200: moe_align_noalloc null pointer");
-  int32_t* scratch = nullptr;
-  cudaError_t e = noalloc_scratch(&scratch);
+  int32_t* scratch = nullptr;  // a single-tile call (numel <= AT) needs no scratch and looks nothing up
+  cudaError_t e = numel > AT ? noalloc_scratch(&scratch) : cudaSuccess;
   if (e != cudaSuccess)
     return set_error(2, "moek_b200: moe_align_noalloc scratch lookup: %s", cudaGetErrorString(e));
   e = launch_align(topk_ids, numel, num_experts, block_size, sorted_ids, sorted_len, expert_ids, expert_len,

@@ -40,6 +40,57 @@ constexpr int STAGES_PER_RUN = KG * 16 / BK; // 2
 constexpr int MOEK_DEV_TIMEOUT = 1;
 constexpr int MOEK_DEV_BAD_EXPERT = 2;
 constexpr int MOEK_DEV_TOO_MANY_ROWS = 3;
+constexpr int MOEK_DEV_BAD_INPUT = 4;  // an input index out of range (checked in MOEK_DEBUG_CHECKS builds)
+
+__device__ __forceinline__ uint64_t globaltimer();
+__device__ __forceinline__ void report(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ----------------------------------------------------------------------------------------- timeline stamps
+// Built with -DMOEK_TRACE, a kernel writes %globaltimer stamps of its phases: MOEK_TR(slot) stores the time in
+// g_moek_trace[blockIdx.x][slot] (CTAs and slots beyond the array are not recorded), MOEK_TR_VAL stores a value.
+// Each translation unit has its own array (a static __device__ array defined here), read back by that unit's
+// trace_copy_* function (moek_trace_read). Without the flag the macros are empty.
+constexpr int MOEK_TRACE_CTAS = 1024, MOEK_TRACE_SLOTS = 64;
+#ifdef MOEK_TRACE
+static __device__ unsigned long long g_moek_trace[MOEK_TRACE_CTAS][MOEK_TRACE_SLOTS];
+#define MOEK_TR_VAL(slot, v)                                                      \
+  do {                                                                            \
+    if (blockIdx.x < (unsigned)moek::MOEK_TRACE_CTAS && (slot) < moek::MOEK_TRACE_SLOTS) \
+      moek::g_moek_trace[blockIdx.x][(slot)] = (unsigned long long)(v);          \
+  } while (0)
+#define MOEK_TR(slot) MOEK_TR_VAL(slot, moek::globaltimer())
+#define MOEK_TRACE_COPY_FN(name)                                                                      \
+  cudaError_t name(void* dst, size_t bytes, int clear) {                                              \
+    if (bytes > sizeof(g_moek_trace)) bytes = sizeof(g_moek_trace);                                   \
+    cudaError_t e = dst ? cudaMemcpyFromSymbol(dst, g_moek_trace, bytes) : cudaSuccess;              \
+    if (e == cudaSuccess && clear) {                                                                  \
+      void* a = nullptr;                                                                              \
+      e = cudaGetSymbolAddress(&a, g_moek_trace);                                                     \
+      if (e == cudaSuccess) e = cudaMemset(a, 0, sizeof(g_moek_trace));                               \
+    }                                                                                                 \
+    return e;                                                                                         \
+  }
+#else
+#define MOEK_TR_VAL(slot, v) \
+  do {                       \
+  } while (0)
+#define MOEK_TR(slot) \
+  do {                \
+  } while (0)
+#define MOEK_TRACE_COPY_FN(name) \
+  cudaError_t name(void*, size_t, int) { return cudaErrorNotSupported; }
+#endif
+
+// ------------------------------------------------------------------------------------------ input checks
+// Built with -DMOEK_DEBUG_CHECKS, MOEK_CHECK(cond, err) is false (after recording MOEK_DEV_BAD_INPUT) when an index
+// taken from an input is out of range, and the caller skips the access; otherwise it is always true.
+#ifdef MOEK_DEBUG_CHECKS
+#define MOEK_CHECK(cond, err) ((cond) ? true : (moek::report((err), moek::MOEK_DEV_BAD_INPUT), false))
+#else
+#define MOEK_CHECK(cond, err) true
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -48,9 +99,6 @@ __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
-}
-__device__ __forceinline__ void report(int* err, int code) {
-  if (err) atomicCAS(err, 0, code);
 }
 
 // Programmatic dependent launch: wait until the grid this one depends on has completed and its memory is visible

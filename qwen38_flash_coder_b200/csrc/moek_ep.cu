@@ -210,6 +210,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
                                                                       int G, int32_t* __restrict__ pos) {
   pdl_wait();
   pdl_launch_dependents();
+  if (threadIdx.x == 0) MOEK_TR(0);
   __shared__ int spos[EP_P2P_MAXM];
   __shared__ int wcnt[P2P_THREADS / 32];
   __shared__ int ok;
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
   if (tid == 0) {
     if (g == 0) my_flags[q.world + d] = 0;  // my back segment d is free again
     ok = wait_flag(d_flags + q.rank, 0, globaltimer() + q.timeout_ns, q.err);
+    MOEK_TR(1);
   }
   int count = 0;  // rows of mine that go to d
   for (int t0 = 0; t0 < M; t0 += P2P_THREADS) {
@@ -271,11 +273,13 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
   }
   __syncthreads();
   if (tid == 0) {
+    MOEK_TR(2);
     __threadfence_system();
     int* ctr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[q.rank]) + q.lay.ctr) + d;
     if (last_arrival(ctr, G)) {
       __threadfence_system();
       st_sys(d_flags + q.rank, 1);
+      MOEK_TR(3);
     }
   }
 }
@@ -331,6 +335,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
                                                                     __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_launch_dependents();
+  if (threadIdx.x == 0) MOEK_TR(8);
   __shared__ int ok;
   uint8_t* mine = reinterpret_cast<uint8_t*>(q.peer[q.rank]);
   int* my_flags = reinterpret_cast<int*>(mine + q.lay.flags);
@@ -340,6 +345,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
     for (int s = threadIdx.x; s < q.world; s += 32) good &= wait_flag(my_flags + q.world + s, 1, deadline, q.err);
     good = __all_sync(0xffffffffu, good);
     if (threadIdx.x == 0) ok = good;
+    if (threadIdx.x == 0) MOEK_TR(9);
   }
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x < q.world) st_sys(my_flags + threadIdx.x, 0);  // the senders may write again
@@ -366,7 +372,11 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
     w.y = *reinterpret_cast<uint32_t*>(&hi);
     reinterpret_cast<uint2*>(out)[i] = w;
   }
+  __syncthreads();
+  if (threadIdx.x == 0) MOEK_TR(10);
 }
+
+MOEK_TRACE_COPY_FN(trace_copy_ep)
 
 static int p2p_split(int rows) { return rows <= 8 ? 1 : rows <= 64 ? (rows + 7) / 8 : 8; }  // CTAs per peer
 

@@ -26,6 +26,28 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Launch as a cooperative grid (every CTA resident at once, or the launch fails instead of running), with
+// programmatic stream serialisation as well when the runtime accepts both attributes together (pdl = 1). Kernels
+// whose CTAs wait on one another use this: the co-residency their waits rely on is then guaranteed, also when other
+// kernels hold part of the GPU.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int pdl,
+                        Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 struct GemmParams {
   const __nv_bfloat16* A;  // gate_up: hidden [M, K]; down: act [num_ids, K]
   const uint8_t* W;        // tiled codes [E, N/256, K/64, 8 KB]
@@ -44,8 +66,10 @@ struct GemmParams {
   void* out;                // mode 3: gate_up -> act bf16 [num_ids, N/2]; down (split) -> bf16 [M, N] top-k sums
   uint64_t timeout_ns;
   int num_ids, N, K, E, a_div, block_m, nsplit, max_blocks;
-  int a_rows;  // tcgen05 path: rows of A (x: num_ids / a_div; mode 1 down: the sorted act rows)
+  int a_rows;  // tcgen05 path: rows of A (x: num_ids / a_div; sorted-order down: the sorted act rows)
   int gate_up, mode, combine_k;
+  int sorted_act;  // tcgen05 path: act rows at their position in moe_align's sorted order (moek_gemm mode 5)
+  int down_bf16;   // tcgen05 path, down: bf16 rows topk_w * sum into out (modes 0/1) instead of fp32 rows into part
 };
 
 // moek_layer.cu: the whole decode-regime layer in one persistent kernel
@@ -84,11 +108,18 @@ struct LayerParams {
   int ep_world, ep_rank, ep_mcap;
   int tail;  // 1: items past the last whole wave of units may use a finer k-split (up to one per stage)
 };
-cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, cudaStream_t st);  // rows per block: 8/16/32
+// rows per block: 8/16/32; coop: cooperative launch (every CTA resident together, the default)
+cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, int coop, cudaStream_t st);
 
 // moek_router.cu: softmax -> top-k -> optional renormalisation (dtype 0 = fp32 logits, 1 = bf16)
 cudaError_t launch_router_topk(const void* logits, int dtype, int M, int E, int k, int renorm, int32_t* ids,
                                float* weights, int32_t* tok_idx, cudaStream_t st);
+
+// Timeline stamps of MOEK_TRACE builds (moek_common.cuh): copy up to `bytes` of a translation unit's stamp array
+// [CTA][slot] to host memory (dst may be null) and optionally zero it; cudaErrorNotSupported without MOEK_TRACE.
+cudaError_t trace_copy_layer(void* dst, size_t bytes, int clear);
+cudaError_t trace_copy_prefill(void* dst, size_t bytes, int clear);
+cudaError_t trace_copy_ep(void* dst, size_t bytes, int clear);
 
 // moek_abi.cu: record the calling thread's error message (read back by moek_last_error) and return code
 int set_error(int code, const char* fmt, ...);

@@ -39,12 +39,15 @@
 //
 // Co-residency: a down unit may wait on a gate_up unit of any CTA, and every CTA runs all of its gate_up units
 // before any down unit, so the grid makes progress whenever all its CTAs are resident at once: the launcher sizes
-// the grid to the occupancy the kernel reaches (cudaOccupancyMaxActiveBlocksPerMultiprocessor x SMs).
+// the grid to the occupancy the kernel reaches (cudaOccupancyMaxActiveBlocksPerMultiprocessor x SMs) and launches it
+// as a cooperative grid, so that the runtime starts it only with every CTA resident, also while kernels of other
+// streams hold part of the GPU.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
@@ -226,8 +229,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  if (tid == 0) MOEK_TR(0);
   pdl_wait();  // x, routing and weights of the previous kernels; the workspace of the previous launch
   pdl_launch_dependents();
+  if (tid == 0) MOEK_TR(1);
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
   const int n = p.num_ids, k = p.top_k;
@@ -236,6 +241,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       bool good = true;
       for (int s = lane; s < p.ep_world; s += 32) good &= wait_flag(p.ep_recv_flags + s, 1, deadline, p.err);
       if (!__all_sync(0xffffffffu, good) && lane == 0) misc[2] = 1;
+      if (lane == 0) MOEK_TR(2);
     }
     __syncthreads();
     asm volatile("fence.proxy.async.global;" ::: "memory");  // the bulk copies below read what the peers wrote
@@ -303,6 +309,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   }
   const int nblk = *abort_flag ? 0 : misc[0];
   const int ep_rows = misc[3];
+  if (tid == 0) MOEK_TR(3);
   if (p.ep_peer && ep_rows == 0 && !*abort_flag && blockIdx.x == 0 && tid == 0)
     ep_signal(p);  // nothing to return: release the senders' waits at once
 
@@ -312,6 +319,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   const int U = plan0.u_total + plan1.u_total;
   const int n_mine = U > (int)blockIdx.x ? (U - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int rounds = (n_mine + MAXU - 1) / MAXU;
+  if (tid == 0) MOEK_TR_VAL(7, n_mine);
 
   if (warp == W_PROD) {  // ------------------------------------------------------------------------- producer
     uint32_t g = 0;
@@ -345,6 +353,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           if (lane == 0) {  // the two consecutive 64-k blocks of the stage
             const int64_t wi = (((int64_t)e * mt.nt + item) * mt.nstage + st) * 2;
             bulk_g2s(dst, mt.W + wi * STAGE_BYTES, LSTAGE, full + slot);
+            if (g == 0) MOEK_TR(4);
           } else if (lane == 1) {
             const int64_t si = ((int64_t)e * mt.nt + item) * mt.nstage + st;
             bulk_g2s(dst + LSTAGE, mt.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
@@ -356,6 +365,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   } else if (warp == W_ACT) {  // ----------------------------------------------------------------------- act warp
     uint32_t g = 0;
     bool ok = true;
+    int n_wait = 0;  // act waits so far (the first four are stamped in MOEK_TRACE builds)
     for (int r = 0; r < rounds && ok; r++) {
       const int nu = min(MAXU, n_mine - r * MAXU);
       if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
@@ -379,10 +389,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           } else {  // act rows: columns [128 st, 128 st + 128) are gate_up item st's (ITEM_COLS / 2 act columns)
             const int need = st;
             if (need != ready_item) {
+              if (lane == 0 && n_wait < 4) MOEK_TR(56 + 2 * n_wait);
               if (!wait_stamp(p.ctr + p.off_ready + m.blk * p.m[0].nt + need, epoch + 1, deadline, p.err,
                               abort_flag)) {
                 ok = false;
               }
+              if (lane == 0 && n_wait < 4) MOEK_TR(57 + 2 * n_wait);
+              n_wait++;
               ok = __all_sync(0xffffffffu, ok);
               if (!ok) break;
               ready_item = need;
@@ -473,6 +486,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           const int eo1 = rr + 1 < su ? __shfl_sync(0xffffffffu, ro, rr + 1) : cnt;
           auto patch = [&](uint32_t en) {
             const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+            if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r0g + 1), p.err)) return;
             const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
             tb[row * 8 + kg] = (uint8_t)(en >> 24);
           };
@@ -516,6 +530,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 #pragma unroll
             for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
         bool ok = true;
+        const int tu = r * MAXU + ui;  // the unit's index among this CTA's (timeline stamps)
         for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
@@ -524,6 +539,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             ok = false;
             continue;  // stay in step with the other roles' counters
           }
+          if (tid == 0 && st == m.st0 && tu < 16) MOEK_TR(8 + 3 * tu);
 #pragma unroll
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
@@ -565,6 +581,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         }
         ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
         if (!ok) continue;
+        if (tid == 0 && tu < 16) MOEK_TR(9 + 3 * tu);
 
         // ------------------------------------------------------------------------------------------ finishing
         // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
@@ -637,6 +654,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               }
             }
           }
+          if (tid == 0 && tu < 16) MOEK_TR(10 + 3 * tu);
           continue;
         }
         // down: weighted fp32 rows of (block, item), then the token sums
@@ -697,6 +715,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             }
           }
         }
+        if (tid == 0 && tu < 16) MOEK_TR(10 + 3 * tu);
         if (!complete || p.out_rows) continue;
         __threadfence();
         __syncwarp();
@@ -745,6 +764,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       __syncwarp();
       if (lane == 0) mbar_arrive(mempty);
     }
+    if (tid == 0) MOEK_TR(5);
   }
 
   // tokens with no valid slot get a zero output row (nothing else writes them): the last CTA, which has the fewest
@@ -759,6 +779,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 
   // ------------------------------------------------------------------------------------------------ teardown
   __syncthreads();
+  if (tid == 0) MOEK_TR(6);
   if (tid == 0) {  // the last CTA to finish advances the launch epoch of the ready stamps
     __threadfence();
     if (atomicAdd(p.ctr + p.off_done, 1) == (int)gridDim.x - 1) {
@@ -770,7 +791,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 }
 
 template <int XR>
-static cudaError_t launch_xr(const LayerParams& p, int sms, cudaStream_t st) {
+static cudaError_t launch_xr(const LayerParams& p, int sms, int coop, cudaStream_t st) {
   using C = Cfg<XR>;
   cudaError_t e = cudaFuncSetAttribute(moek_layer_kernel<XR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
@@ -779,17 +800,35 @@ static cudaError_t launch_xr(const LayerParams& p, int sms, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorLaunchOutOfResources;
   const int grid = std::min(occ, C::MINB) * sms;  // every CTA resident at once (down units wait on gate_up units)
-  e = launch_pdl(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, p);
+  if (!coop) {
+    e = launch_pdl(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, p);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
+  // cooperative: the runtime guarantees that all CTAs are resident together (down units wait on gate_up units of
+  // other CTAs), whatever else runs on the GPU. With programmatic serialisation too where the runtime takes both;
+  // if it refuses the pair (a launch-configuration error, reported before anything runs), cooperative alone.
+  static std::atomic<int> coop_pdl{1};
+  if (coop_pdl.load(std::memory_order_relaxed)) {
+    e = launch_coop(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, 1, p);
+    if (e == cudaSuccess) return cudaGetLastError();
+    if (e != cudaErrorInvalidValue && e != cudaErrorNotSupported) return e;
+    cudaGetLastError();
+    coop_pdl.store(0, std::memory_order_relaxed);
+  }
+  e = launch_coop(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, 0, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 }  // namespace dl
 
-cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, cudaStream_t st) {
-  if (block_rows <= 8) return dl::launch_xr<8>(p, sms, st);
-  if (block_rows <= 16) return dl::launch_xr<16>(p, sms, st);
-  return dl::launch_xr<32>(p, sms, st);
+MOEK_TRACE_COPY_FN(trace_copy_layer)
+
+cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, int coop, cudaStream_t st) {
+  if (block_rows <= 8) return dl::launch_xr<8>(p, sms, coop, st);
+  if (block_rows <= 16) return dl::launch_xr<16>(p, sms, coop, st);
+  return dl::launch_xr<32>(p, sms, coop, st);
 }
 
 }  // namespace moek

@@ -39,9 +39,11 @@
 //   epilogue  = warps 24-31 (lane quarter = warp % 4; two warps per quarter take alternate 8-column chunks, so the
 //               accumulator is drained twice as fast and the next unit's MMAs wait less): tcgen05.ld 8 columns at a
 //               time; gate_up writes act = bf16(silu(gate) * up) (gate row r and its up partner are lane r of halves
-//               0 and 1), down writes the fp32 rows topk_w * acc that moek_combine sums over the top-k slots.
-//   mode 1    = gate_up writes act at the row's position in moe_align's sorted order instead of its id, so that the
-//               down GEMM loads a block's rows as one 128-row TMA tile per stage instead of gathering them.
+//               0 and 1), down writes the fp32 rows topk_w * acc that moek_combine sums over the top-k slots, or
+//               (down_bf16: the kit's moe_gemm mode 0 contract) the bf16 rows bf16(topk_w * acc) into out.
+//   sorted    = (sorted_act) gate_up writes act at the row's position in moe_align's sorted order instead of its
+//               id, so that the down GEMM loads a block's rows as one 128-row TMA tile per stage instead of
+//               gathering them.
 //
 // Every wait is bounded (%globaltimer); on expiry the CTA raises an abort flag, every role skips its remaining work
 // in step, and TMEM is freed before the kernel returns.
@@ -278,8 +280,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) MOEK_TR(0);
   pdl_wait();  // sorted ids, experts and activations come from the previous kernels
   pdl_launch_dependents();
+  if (tid == 0) MOEK_TR(1);
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int nblocks = min(p.num_post_pad[0] / p.block_m, p.max_blocks);
   const int64_t nunits = (int64_t)nblocks * nt;
@@ -323,6 +327,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < BMP / 32; j++) {  // all loads first, then the ballots
         const int r = lane + 32 * j;
         ids[j] = r < p.block_m ? p.sorted_ids[(int64_t)ui.blk * p.block_m + r] : p.num_ids;
+        if (!MOEK_CHECK(ids[j] >= 0 && ids[j] <= p.num_ids, p.err)) ids[j] = p.num_ids;
       }
 #pragma unroll
       for (int j = 0; j < BMP / 32; j++) nv += __popc(__ballot_sync(0xffffffffu, ids[j] < p.num_ids));
@@ -340,6 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
+        if (warp == W_MMA && lane == 0 && st == 0 && un < 16) MOEK_TR(8 + 3 * un);
         if (lane == 0) {
           const uint32_t b0 = smem_u32(smem + B_OFF + b * B_BYTES);
           const uint32_t a0 = tmem + A_COL0 + a * A_SLOT_COLS;
@@ -354,6 +360,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           umma_commit(B.aempty + a);  // the A and B slots may be refilled once these MMAs completed
           umma_commit(B.bempty + b);
           if (st == nstage - 1) umma_commit(B.accfull);
+          if (warp == W_MMA && st == nstage - 1 && un < 16) MOEK_TR(9 + 3 * un);
         }
         __syncwarp();
       }
@@ -364,7 +371,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     int* rowc = reinterpret_cast<int*>(smem + IDS_OFF) + (warp - W_LOAD) * BMP;  // each loader warp its own copy
     const int lw = warp - W_LOAD;                // gathers lw, lw + NLOAD, ... of a stage are this warp's
     const int rows_a = p.a_rows;  // rows of A; a coordinate of rows_a reads zeros
-    const bool tile_rows = p.mode == 1 && !p.gate_up;  // act in sorted order: the block's rows are contiguous
+    const bool tile_rows = p.sorted_act && !p.gate_up;  // act in sorted order: the block's rows are contiguous
     uint32_t g = 0;
     for (int64_t u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, u, nt);
@@ -375,7 +382,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int j = 0; j < BMP / 32; j++) {
         const int r = lane + 32 * j;
-        const int id = r < p.block_m ? p.sorted_ids[row0 + r] : p.num_ids;
+        int id = r < p.block_m ? p.sorted_ids[row0 + r] : p.num_ids;
+        if (!MOEK_CHECK(id >= 0 && id <= p.num_ids, p.err)) id = p.num_ids;
         rowc[r] = id < p.num_ids ? id / p.a_div : rows_a;
       }
 #pragma unroll
@@ -483,6 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int eo1 = rn + 1 < nb ? __shfl_sync(0xffffffffu, ro, rn + 1) : cnt;
         auto patch = [&](uint32_t en) {
           const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
+          if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r0g + 1), p.err)) return;
           if ((kg >> 2) != (st & 1)) return;
           const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
           reinterpret_cast<uint8_t*>(tbl)[row * 4 + (kg & 3)] = (uint8_t)(en >> 24);
@@ -565,6 +574,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < 4; j++) {
         const int r = lane + 32 * j;
         ids[j] = r < p.block_m ? p.sorted_ids[row0 + r] : p.num_ids;
+        if (!MOEK_CHECK(ids[j] >= 0 && ids[j] <= p.num_ids, p.err)) ids[j] = p.num_ids;
         nv += __popc(__ballot_sync(0xffffffffu, ids[j] < p.num_ids));
         wts[j] = (!p.gate_up && ids[j] < p.num_ids) ? p.topk_w[ids[j]] : 0.f;
       }
@@ -591,27 +601,35 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < 8; j++) {
           if (c0 + j >= nv) break;
           const int id = __shfl_sync(0xffffffffu, ids[jj], l0 + j);
-          if (p.gate_up) {  // mode 1: act row = the row's sorted position, else its id
-            const int64_t arow = p.mode == 1 ? row0 + c0 + j : (int64_t)id;
+          if (p.gate_up) {  // sorted order: act row = the row's sorted position, else its id
+            const int64_t arow = p.sorted_act ? row0 + c0 + j : (int64_t)id;
             static_cast<__nv_bfloat16*>(p.out)[arow * I + 128 * ui.item + row] =
                 __float2bfloat16_rn(silu_fast(v0[j]) * v1[j]);
           } else {
             const float w = __shfl_sync(0xffffffffu, wts[jj], l0 + j);
-            float* orow = p.part + (int64_t)id * p.N + 256 * ui.item;
-            orow[row] = w * v0[j];
-            orow[128 + row] = w * v1[j];
+            if (p.down_bf16) {  // the kit's dout row: bf16(topk_w * sum)
+              __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (int64_t)id * p.N + 256 * ui.item;
+              orow[row] = __float2bfloat16_rn(w * v0[j]);
+              orow[128 + row] = __float2bfloat16_rn(w * v1[j]);
+            } else {
+              float* orow = p.part + (int64_t)id * p.N + 256 * ui.item;
+              orow[row] = w * v0[j];
+              orow[128 + row] = w * v1[j];
+            }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(B.accempty);
+      if (warp == EPI0 && lane == 0 && un < 16) MOEK_TR(10 + 3 * un);
       un++;
     }
   }
   // ------------------------------------------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) MOEK_TR(6);
   if (warp == W_MMA) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
@@ -619,6 +637,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 }  // namespace pf
+
+MOEK_TRACE_COPY_FN(trace_copy_prefill)
 
 int prefill_block_m() { return pf::BMP; }
 
@@ -645,8 +665,8 @@ cudaError_t launch_prefill(const GemmParams& p, int sms, cudaStream_t st) {
   CUtensorMap tmap;
   const cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)std::max(1, p.a_rows)};
   const cuuint64_t strides[1] = {(cuuint64_t)p.K * 2};
-  // gathered rows: a 1-row box (tile::gather4); mode 1 down: the block's 128 consecutive rows in one box
-  const cuuint32_t box[2] = {BK, (p.mode == 1 && !p.gate_up) ? (cuuint32_t)pf::BMP : 1u}, estr[2] = {1, 1};
+  // gathered rows: a 1-row box (tile::gather4); sorted-order down: the block's 128 consecutive rows in one box
+  const cuuint32_t box[2] = {BK, (p.sorted_act && !p.gate_up) ? (cuuint32_t)pf::BMP : 1u}, estr[2] = {1, 1};
   if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(p.A), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)

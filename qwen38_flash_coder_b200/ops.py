@@ -57,7 +57,7 @@ def check_device_errors(dev) -> None:
             if key[0] == "layer_state" and key[1] == torch.device(dev):
                 t.zero_()
         names = {1: "a bounded wait timed out", 2: "an expert id out of range", 3: "a block with more rows than "
-                 "max_rows"}
+                 "max_rows", 4: "an input index out of range (debug checks)"}
         raise MoekError(f"moek_b200: device error {code}: {names.get(code, 'unknown')}")
 
 
@@ -105,8 +105,14 @@ def moe_gemm(A, W, S, G, sorted_ids, expert_ids, num_post_pad, topk_w, out, top_
              exc_ent, ws, cnt, mode: int, nsplit: int, part, order: int = 0, tiled: bool = True, *,
              block_m: int = BM, max_rows: int = 0) -> None:
     """The kit's moe_gemm argument list (files/mbx_moek.cu:717-721). ``ws`` and ``order`` are accepted and unused;
-    ``S`` must be empty (packed scales only); ``cnt``'s first int32 receives device error codes. Only mode 2 (split-k
-    partials into ``part``) exists; ``out`` and ``topk_w`` are finished by ``moe_split_epilogue``."""
+    ``S`` must be empty (packed scales only); ``cnt``'s first int32 receives device error codes.
+
+    Modes with the reference's meaning: 0 and 1 (the kit's prefill call, files/mbx_moek.py:276-283; the reference's
+    item counter and stream-k schedules are one tcgen05 schedule here): gate_up writes act bf16 [num_ids, N/2] to
+    ``out``, down writes dout bf16 [num_ids, N] = bf16(topk_w * sum) to ``out``; 2 (the kit's decode call): split-k
+    fp32 partials into ``part``, finished by ``moe_split_epilogue``. This build's own modes: 3 (split-k with fused
+    epilogues), 4 (tcgen05, down writes fp32 rows topk_w * sum to ``part`` for ``combine``), 5 (as 4, act rows in
+    moe_align's sorted order)."""
     _need_cuda(A, W, G, sorted_ids, SP, part)
     if S is not None and S.numel():
         raise MoekError("moek_b200: plain Marlin scales are not supported; pass the packed SP")
@@ -242,7 +248,8 @@ _ROWS_SET = False
 def _layer_rows_knob():
     """MOEK_B200_LAYER_ROWS (8, 16 or 32): rows per block of the whole-layer kernel instead of the automatic
     choice (moek_set_layer_block_rows); MOEK_B200_LAYER_TAIL=0: no finer k-split for the items past the last whole
-    wave of units (moek_set_layer_tail_split). Read once."""
+    wave of units (moek_set_layer_tail_split); MOEK_B200_LAYER_COOP=0: a plain launch instead of a cooperative one
+    (moek_set_layer_cooperative). Read once."""
     global _ROWS_SET
     if not _ROWS_SET:
         env = os.environ.get("MOEK_B200_LAYER_ROWS")
@@ -251,6 +258,9 @@ def _layer_rows_knob():
         env = os.environ.get("MOEK_B200_LAYER_TAIL")
         if env:
             call("moek_set_layer_tail_split", int(env))
+        env = os.environ.get("MOEK_B200_LAYER_COOP")
+        if env:
+            call("moek_set_layer_cooperative", int(env))
         _ROWS_SET = True
 
 
@@ -399,13 +409,13 @@ def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
     sid, eid, npad = moe_align_block_size(ids32, BM_PREFILL, layer.E)
     part = _scratch("part", num_ids * b.N, torch.float32, dev) if rows_k is None else \
         torch.empty((num_ids, b.N), dtype=torch.float32, device=dev)
-    # mode 1: act rows in moe_align's sorted order (row = position in sorted_ids), so the down GEMM reads each block's
+    # mode 5: act rows in moe_align's sorted order (row = position in sorted_ids), so the down GEMM reads each block's
     # rows as one tile instead of gathering them
     act = torch.empty((sid.numel(), a.N // 2), dtype=torch.bfloat16, device=dev)
     _timed("gate_gemm", lambda: _gemm(x, a, sid, eid, npad, num_ids, top_k, True, cnt, 1, part, rows, act, tw, ids32,
-                                      top_k, mode=1, block_m=BM_PREFILL))
+                                      top_k, mode=5, block_m=BM_PREFILL))
     _timed("down_gemm", lambda: _gemm(act, b, sid, eid, npad, num_ids, 1, False, cnt, 1, part, rows, None, tw, ids32,
-                                      top_k, mode=1, block_m=BM_PREFILL))
+                                      top_k, mode=5, block_m=BM_PREFILL))
     if rows_k is not None:
         return part
     call("moek_combine", _ptr(part), 1, _ptr(output), m, b.N, top_k, _stream(dev))

@@ -102,3 +102,22 @@ def test_peer_exchange_layout_and_argument_checks():
     args[1], args[4] = fake, 60  # 120 received rows of 5 slots: more than the whole-layer kernel takes
     assert lib.moek_moe_layer_p2p(*args) == 3 and b"decode batches" in lib.moek_last_error()
     assert lib.moek_set_layer_block_rows(24) == 1 and lib.moek_set_layer_block_rows(0) == 0
+
+
+@pytest.mark.parametrize("variant,flag", [("trace", 1), ("debug", 2)])
+def test_instrumented_builds_export_the_same_symbols(variant, flag):
+    """The trace and debug builds (build.py variants) export every declared function and report their flag; the
+    product build reports none and refuses trace reads."""
+    from qwen38_flash_coder_b200 import build
+
+    path = build.lib_path(variant)
+    if not os.path.exists(path):
+        build.build(variant=variant)
+    h = ctypes.CDLL(path)
+    missing = [n for n in declared() if not hasattr(h, n)]
+    assert not missing, missing
+    assert h.moek_build_flags() == flag
+    lib = _lib.lib()
+    assert lib.moek_build_flags() == 0
+    buf = ctypes.create_string_buffer(64)
+    assert lib.moek_trace_read(0, buf, 64) == 3  # MOEK_ERR_UNSUPPORTED without MOEK_TRACE

@@ -46,3 +46,30 @@ def test_install_routes_vllm_functions():
 
     moek.install()
     _check(mu.prepare_nvfp4_moe_layer_for_marlin, mm.fused_marlin_moe)
+
+
+@pytest.mark.parametrize("t", [1, 5, 8, 12, 13, 31, 128, 700, 6912])
+def test_serve_path_sweep(t):
+    """The serving call path across batch sizes, as the reference's serve_path harness drives it
+    (bench/moek/serve_path.py:19-27: T in {1, 5, 8, 12, 13, 31, 128, 700, 6912}, keyword arguments, vLLM's own
+    prepare_nvfp4_moe_layer_for_marlin and fused_marlin_moe after install()): every size against the fp32 oracle
+    within the parity gate (the reference compares with Marlin, which does not run here)."""
+    from oracle import moe_ref
+
+    mm = pytest.importorskip("vllm.model_executor.layers.fused_moe.experts.marlin_moe")
+    import vllm.model_executor.layers.quantization.utils.marlin_utils_fp4 as mu
+
+    moek.install()
+    e = 128
+    w13, w2 = synth.make_layer(e, 2048, 512, 40, device=DEV)
+    out = mu.prepare_nvfp4_moe_layer_for_marlin(None, w13[0], w13[1], w13[2], w2[0], w2[1], w2[2], True)
+    x = (synth.activations(t, 2048, t, device=DEV).float() * 0.5).to(torch.bfloat16)
+    ids, wts = synth.route_softmax(t, e, 5, t, device=DEV)
+    y = mm.fused_marlin_moe(hidden_states=x, w1=out[0], w2=out[3], bias1=None, bias2=None, w1_scale=out[1],
+                            w2_scale=out[4], topk_weights=wts, topk_ids=ids, quant_type_id=0, global_scale1=out[2],
+                            global_scale2=out[5])
+    ops.check_device_errors(DEV)
+    ck = lambda mat: (mat[0].cpu().numpy(), mat[1].view(torch.uint8).cpu().numpy(), mat[2].cpu().numpy())
+    ref = moe_ref.reference(x.cpu(), ids.cpu().numpy(), wts.cpu().numpy(), ck(w13), ck(w2))
+    ok, stats = moe_ref.within_gate(y.cpu(), ref)
+    assert ok, (t, stats)

@@ -126,3 +126,30 @@ def test_layer_kernel_sub_blocks(monkeypatch, m, e):
     for o in outs[:1] + tails:
         ok, stats = moe_ref.within_gate(o.cpu(), ref)
         assert ok, stats
+
+
+def test_layer_kernel_beside_other_streams():
+    """The whole-layer kernel's CTAs wait on one another, so it is launched as a cooperative grid: with large GEMMs
+    occupying the GPU from another stream, every call still completes within the default 2 s wait bound and gives the
+    same bits as a call on an idle GPU."""
+    w13, w2 = synth.make_layer(64, 2048, 512, 31, device=DEV)
+    layer = prep.PreparedLayer(w13, w2)
+    m = 8
+    x = synth.activations(m, 2048, 31, device=DEV)
+    ids, wts = synth.route_softmax(m, 64, 5, 31, device=DEV)
+    ref = ops.fused_moe(x, layer, wts, ids)
+    torch.cuda.synchronize()
+    a = torch.randn((8192, 8192), device=DEV, dtype=torch.bfloat16)
+    side, main = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    with torch.cuda.stream(side):
+        for _ in range(8):
+            a = a @ a
+            a = a / a.abs().amax().clamp_min(1.0)
+    with torch.cuda.stream(main):
+        for _ in range(20):
+            outs.append(ops.fused_moe(x, layer, wts, ids))
+    torch.cuda.synchronize()
+    ops.check_device_errors(DEV)
+    for o in outs:
+        assert torch.equal(o, ref)

@@ -192,3 +192,60 @@ def test_empty_batch():
     out = ops.fused_moe(torch.empty((0, 2048), dtype=torch.bfloat16, device=DEV), layer,
                         torch.empty((0, 5), device=DEV), torch.empty((0, 5), dtype=torch.int32, device=DEV))
     assert out.shape == (0, 2048)
+
+
+@pytest.mark.parametrize("m", [17, 300])
+def test_kit_prefill_call_mode0(m):
+    """The kit's prefill sequence with its own argument lists (files/mbx_moek.py:266-289, ``split = False``): moe_align
+    with block 96, moe_gemm mode 0 for gate_up (act into ``out``) and for down (dout = bf16(topk_w * sum) rows into
+    ``out``), then torch.sum over the top-k slots. dout rows are checked against the oracle's fp32 slot rows, the
+    summed output against the oracle's layer; mode 1 (the reference's stream-k schedule) writes the same bits."""
+    e, k, hid, inter = 64, 5, 2048, 512
+    w13, w2 = synth.make_layer(e, hid, inter, 21, device=DEV)
+    layer = prep.PreparedLayer(w13, w2)
+    x = synth.activations(m, hid, 21, device=DEV)
+    ids, wts = synth.route_softmax(m, e, k, 21, device=DEV)
+    sid, eid, npad = ops.moe_align_block_size(ids, 96, e, None, ignore_invalid_experts=True)
+    a, b = layer.w13, layer.w2
+    none = torch.empty(0, dtype=torch.uint8, device=DEV)
+    ws = torch.empty(2 * 148 * 96 * 256, dtype=torch.float32, device=DEV)
+    cnt = torch.zeros(1 << 16, dtype=torch.int32, device=DEV)
+    part = torch.empty(5 * 12 * 8 * 2560, dtype=torch.float32, device=DEV)  # the kit's split buffer, unused here
+    tw = wts.reshape(-1)
+    douts = []
+    for mode in (0, 1):
+        act = torch.empty((m * k, inter), dtype=torch.bfloat16, device=DEV)
+        dout = torch.empty((m * k, hid), dtype=torch.bfloat16, device=DEV)
+        ops.moe_gemm(x, a.w, none, a.g, sid, eid, npad, a.g, act, k, True, a.sp, a.exc_off, a.exc_ent, ws, cnt, mode,
+                     1, part, 0, True)
+        ops.moe_gemm(act, b.w, none, b.g, sid, eid, npad, tw, dout, 1, False, b.sp, b.exc_off, b.exc_ent, ws, cnt,
+                     mode, 1, part, 0, True)
+        torch.cuda.synchronize()
+        assert int(cnt[0]) == 0
+        douts.append(dout)
+    assert torch.equal(douts[0], douts[1])
+    dout = douts[0]
+    rows = moe_ref.slot_rows(x.cpu(), _np(ids), _np(wts), _ckpt(w13), _ckpt(w2))
+    ok, stats = moe_ref.within_gate(dout.float().cpu(), rows)
+    assert ok, stats
+    out = torch.sum(dout.view(-1, k, hid), dim=1)
+    ref = moe_ref.reference(x.cpu(), _np(ids), _np(wts), _ckpt(w13), _ckpt(w2))
+    rel, _, _ = moe_ref.check(out.cpu(), ref)
+    assert rel <= REL, rel
+
+
+def test_gemm_mode_errors():
+    """Modes outside 0-5 and split-k requests on the whole-K tcgen05 modes are rejected before any launch."""
+    w13, w2 = synth.make_layer(8, 2048, 512, 22, device=DEV)
+    a = prep.PreparedLayer(w13, w2).w13
+    m, k = 4, 5
+    x = synth.activations(m, 2048, 22, device=DEV)
+    ids, _ = synth.route_softmax(m, 8, k, 22, device=DEV)
+    sid, eid, npad = ops.moe_align_block_size(ids, 96, 8)
+    act = torch.empty((m * k, 512), dtype=torch.bfloat16, device=DEV)
+    part = torch.empty(8 * m * k * 1024, dtype=torch.float32, device=DEV)
+    cnt = torch.zeros(8, dtype=torch.int32, device=DEV)
+    for mode, nsplit in ((6, 1), (-1, 1), (0, 2), (1, 4)):
+        with pytest.raises(ops.MoekError):
+            ops.moe_gemm(x, a.w, None, a.g, sid, eid, npad, a.g, act, k, True, a.sp, a.exc_off, a.exc_ent, None,
+                         cnt, mode, nsplit, part, 0, True)

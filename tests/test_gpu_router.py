@@ -56,3 +56,17 @@ def test_router_then_layer_matches_oracle_chain():
     ref = moe_ref.reference(x.cpu(), rids, rw, cpu(w13), cpu(w2))
     ok, stats = moe_ref.within_gate(out.cpu(), ref)
     assert ok, stats
+
+
+def test_router_matches_vllm_golden():
+    """The router kernel against vLLM's own grouped_topk (one group, softmax) on the golden's seeded logits
+    (tests/golden/make_router_golden.py): ids exact, weights to fp32 rounding."""
+    import os
+
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "router_golden.npz")))
+    for n in sorted({k[: -len("_meta")] for k in g if k.endswith("_meta")}):
+        m, e, k, renorm = (int(v) for v in g[f"{n}_meta"])
+        w, ids = ops.router_topk(torch.from_numpy(g[f"{n}_logits"]).to(DEV), k, bool(renorm))
+        order = np.argsort(-g[f"{n}_w"], axis=1, kind="stable")
+        assert np.array_equal(ids.cpu().numpy(), np.take_along_axis(g[f"{n}_ids"], order, 1)), n
+        assert np.allclose(w.cpu().numpy(), np.take_along_axis(g[f"{n}_w"], order, 1), rtol=4e-6, atol=1e-9), n

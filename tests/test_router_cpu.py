@@ -36,3 +36,26 @@ def test_router_entry_rejects_bad_arguments():
     assert lib.moek_router_topk(None, 0, 4, 64, 33, 1, None, None, None, None) == 1  # top_k > 32
     assert lib.moek_router_topk(None, 0, 4, 64, 5, 1, None, None, None, None) == 1  # null pointers
     assert lib.moek_router_topk(None, 0, 0, 64, 5, 1, None, None, None, None) == 0  # empty batch
+
+
+def _golden_cases():
+    import os
+
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "router_golden.npz")))
+    names = sorted({k[: -len("_meta")] for k in g if k.endswith("_meta")})
+    for n in names:
+        m, e, k, renorm = (int(v) for v in g[f"{n}_meta"])
+        order = np.argsort(-g[f"{n}_w"], axis=1, kind="stable")  # vLLM's torch path leaves the top_k unsorted
+        yield n, g[f"{n}_logits"], k, bool(renorm), np.take_along_axis(g[f"{n}_ids"], order, 1), \
+            np.take_along_axis(g[f"{n}_w"], order, 1)
+
+
+def test_oracle_matches_vllm_golden():
+    """The router oracle against vLLM's own grouped_topk (one group, softmax) run on seeded logits
+    (tests/golden/make_router_golden.py): ids exact, weights to fp32 rounding."""
+    cases = list(_golden_cases())
+    assert len(cases) == 6
+    for name, logits, k, renorm, gids, gw in cases:
+        ids, w, _ = router.topk_softmax(logits, k, renorm)
+        assert np.array_equal(ids, gids), name
+        assert np.allclose(w, gw, rtol=4e-6, atol=1e-9), name
