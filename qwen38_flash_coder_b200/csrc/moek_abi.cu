@@ -72,7 +72,7 @@ MOEK_API int moek_build_flags(void) {
 }
 
 // Timeline stamps (MOEK_TRACE builds): kind 0 = the whole-layer kernel, 1 = the tcgen05 GEMM, 2 = the EP peer
-// exchange kernels; dst is host memory of `bytes` (at most 1024 CTAs x 64 slots x 8 bytes are copied).
+// exchange kernels; dst is host memory of `bytes` (at most 1024 CTAs x 128 slots x 8 bytes are copied).
 MOEK_API int moek_trace_read(int32_t kind, void* dst, size_t bytes) {
   if (!dst || kind < 0 || kind > 2) return fail(MOEK_ERR_ARG, "moek_b200: trace_read needs kind 0-2 and a buffer");
   cudaError_t e = kind == 0 ? moek::trace_copy_layer(dst, bytes, 0)
@@ -379,10 +379,17 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
     wp += up((int64_t)nst2 * num_ids * H * 4);
   }
   if (rows_ws) p.rows = reinterpret_cast<float*>(wp);
+  auto divs = [](int n) {
+    uint64_t m = 0;
+    for (int s = 1; s <= n && s < 64; s++)
+      if (n % s == 0) m |= 1ull << s;
+    return m;
+  };
   const moek::LayerMat m1{static_cast<const uint8_t*>(w13), sp13, g13, exc_off13,
-                          reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1, nsplit_gate};
+                          reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1, nsplit_gate,
+                          divs(nst1)};
   const moek::LayerMat m2{static_cast<const uint8_t*>(w2), sp2, g2, exc_off2,
-                          reinterpret_cast<const uint32_t*>(exc_ent2), H, I, H / 256, nst2, nsplit_down};
+                          reinterpret_cast<const uint32_t*>(exc_ent2), H, I, H / 256, nst2, nsplit_down, divs(nst2)};
   p.m[0] = m1;
   p.m[1] = m2;
   p.x = static_cast<const __nv_bfloat16*>(x);
@@ -533,6 +540,7 @@ MOEK_API int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t w
     return rc;
   p.ep_peer = peer;
   p.ep_recv_flags = reinterpret_cast<const int*>(blk + a.lay.flags);
+  p.ep_call = reinterpret_cast<const int*>(blk + a.lay.ctr) + 2 * world;
   p.ep_back_off = a.lay.back;
   p.ep_flags_off = a.lay.flags;
   p.ep_world = world;

@@ -2,8 +2,9 @@
 //
 // Weight decode. A tiled weight word holds 8 E2M1 codes (sign = bit 3) of 8 consecutive k of one output column,
 // bit-scattered at load time (prep.CODE_BITS) so that the bf16 pairs come out with few integer ops: codes 0 and 1
-// already have their signs at bits 15 / 31 and their three magnitude bits at 8..6 / 24..22, codes 2-3 and 4-5 sit 3
-// and 6 bits lower (one shift each), codes 6-7 use the remaining bits (three shifts). A code's sign at bit 15 and its
+// already have their signs at bits 15 / 31 and their three magnitude bits at 8..6 / 24..22, codes 2-3 and 4-5 hold
+// that pattern rotated left by 4 and 10 bits (one funnel-shift rotate and one mask each), codes 6-7 hold their
+// mantissa bits rotated by 14 and the other bits by 6 (two rotates, two masks). A code's sign at bit 15 and its
 // three magnitude bits at 8..6 of a bf16 give exactly e2m1 * 2^-126 (exponent field = the code's exponent, top
 // mantissa bit = its mantissa bit; code 1 becomes the subnormal 2^-127). That value D is exact, and the weight the
 // reference's oracle uses, bf16(e2m1 * s * gs) with s the E4M3 block scale and gs the expert's fp32 global scale
@@ -52,7 +53,7 @@ __device__ __forceinline__ void report(int* err, int code) {
 // g_moek_trace[blockIdx.x][slot] (CTAs and slots beyond the array are not recorded), MOEK_TR_VAL stores a value.
 // Each translation unit has its own array (a static __device__ array defined here), read back by that unit's
 // trace_copy_* function (moek_trace_read). Without the flag the macros are empty.
-constexpr int MOEK_TRACE_CTAS = 1024, MOEK_TRACE_SLOTS = 64;
+constexpr int MOEK_TRACE_CTAS = 1024, MOEK_TRACE_SLOTS = 128;
 #ifdef MOEK_TRACE
 static __device__ unsigned long long g_moek_trace[MOEK_TRACE_CTAS][MOEK_TRACE_SLOTS];
 #define MOEK_TR_VAL(slot, v)                                                      \
@@ -174,9 +175,9 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void fp4_pairs(uint32_t q, uint32_t* d) {
   constexpr uint32_t P = 0x81C081C0u;  // sign and magnitude bits of a bf16 pair
   d[0] = q & P;
-  d[1] = (q << 3) & P;
-  d[2] = (q << 6) & P;
-  d[3] = ((q >> 6) & 0x01800180u) | ((q >> 4) & 0x00400040u) | ((q << 4) & 0x80008000u);
+  d[1] = __funnelshift_r(q, q, 4) & P;
+  d[2] = __funnelshift_r(q, q, 10) & P;
+  d[3] = (__funnelshift_r(q, q, 14) & 0x00400040u) | (__funnelshift_r(q, q, 6) & 0x81808180u);
 }
 // S0E5M3 byte -> fp32 value (s * sf * 2^7)
 __device__ __forceinline__ float s0e5m3_to_f32(uint32_t b) {

@@ -177,24 +177,34 @@ cudaError_t launch_ep_unpack(const float* back, const int32_t* pos, const int32_
 
 // ------------------------------------------------------------------------- peer-memory exchange (fixed capacity)
 // Every rank holds one exchange block (P2PLayout), shared by CUDA IPC; the kernels below write straight into the
-// peers' blocks over NVLink (plain stores, no multicast) and hand segments over with system-scope flags:
-//   dispatch  CTAs (d, g), G per destination d: reset my back flag d (its last reader, my previous unpack, is done),
-//             wait until d's receive flag for me is 0 (d's previous unpack is done, so d has finished reading what I
-//             sent last time), place my tokens in d's segment for me (ascending token order, as moek_ep_plan), copy
-//             rows g, g + G, ... with their slot ids (local id, or -1 for slots owned elsewhere) and router weights,
-//             mark the unused rows as having no valid slot; the last CTA of d fences and raises d's receive flag.
-//   wait      my receive flags all 1 (bounded); the whole-layer kernel does this wait itself.
+// peers' blocks over NVLink (plain stores, no multicast) and hand segments over with system-scope flags that carry
+// the call number c (every rank counts its completed calls in its own block; the current call is that count + 1), so
+// no flag is ever reset and no kernel waits before writing:
+//   dispatch  CTAs (d, g), G per destination d: place my tokens in d's segment for me (ascending token order, as
+//             moek_ep_plan), copy rows g, g + G, ... with their slot ids (local id, or -1 for slots owned elsewhere)
+//             and router weights, mark the unused rows as having no valid slot; the last CTA of d fences and sets
+//             d's receive flag for me to c. No wait is needed before writing: d had finished reading my previous
+//             rows before it returned my partials of call c - 1, and my own unpack of call c - 1 (earlier on my
+//             stream) waited for those.
+//   wait      my receive flags all c (bounded); the whole-layer kernel does this wait itself.
 //   combine   CTAs (s, g): for the rows of receive segment s, the fp32 sum (slot order) of the row's local slots into
-//             s's back segment for me; the last CTA of s fences and raises s's back flag for me. No wait is needed
-//             before writing: s raised my receive flag after its previous unpack had read that back segment.
-//   unpack    wait until my back flags are all 1, clear my receive flags (this layer's readers of the receive
-//             segments, the local layer or combine, have completed), out[t] = bf16(sum over ranks d in order of
-//             back segment d's row for t).
-// Every wait is bounded by the caller's deadline; on expiry the kernel records MOEK_DEV_TIMEOUT and stops waiting.
+//             s's back segment for me; the last CTA of s fences and sets s's back flag for me to c. No wait is
+//             needed before writing: s sent call c's rows after its unpack of call c - 1 had read that back segment.
+//   unpack    wait until my back flags are all c, out[t] = bf16(sum over ranks d in order of back segment d's row
+//             for t); the last CTA to finish advances my completed-call count to c.
+// Every wait is bounded by the caller's deadline; on expiry the kernel records MOEK_DEV_TIMEOUT and stops waiting (the
+// counts of the ranks may then disagree: build the exchange again).
 constexpr int P2P_THREADS = 256;
 
 __device__ __forceinline__ int* p2p_flags(const P2PArgs& q, int r) {
   return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[r]) + q.lay.flags);
+}
+// This rank's completed-call count ([2 world] of its counters) and the unpack's arrival counter ([2 world + 1]).
+__device__ __forceinline__ int* p2p_call(const P2PArgs& q) {
+  return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[q.rank]) + q.lay.ctr) + 2 * q.world;
+}
+__device__ __forceinline__ int current_call(const P2PArgs& q) {
+  return *reinterpret_cast<volatile int*>(p2p_call(q)) + 1;
 }
 // The last of `n` arrivals on a self-resetting counter (one thread per CTA calls it, after its writes and a fence).
 __device__ __forceinline__ bool last_arrival(int* ctr, int n) {
@@ -213,16 +223,10 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
   if (threadIdx.x == 0) MOEK_TR(0);
   __shared__ int spos[EP_P2P_MAXM];
   __shared__ int wcnt[P2P_THREADS / 32];
-  __shared__ int ok;
   const int d = blockIdx.x / G, g = blockIdx.x - d * G, per = E / q.world, k = q.k;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int* my_flags = p2p_flags(q, q.rank);
+  const int call = current_call(q);
   int* d_flags = p2p_flags(q, d);
-  if (tid == 0) {
-    if (g == 0) my_flags[q.world + d] = 0;  // my back segment d is free again
-    ok = wait_flag(d_flags + q.rank, 0, globaltimer() + q.timeout_ns, q.err);
-    MOEK_TR(1);
-  }
   int count = 0;  // rows of mine that go to d
   for (int t0 = 0; t0 < M; t0 += P2P_THREADS) {
     const int t = t0 + tid;
@@ -244,10 +248,9 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
     count += chunk;
     __syncthreads();  // wcnt is rewritten by the next chunk
   }
-  __syncthreads();  // ok (also when M is 0)
+  __syncthreads();  // spos (also when M is 0)
   if (g == 0)
     for (int t = tid; t < M; t += P2P_THREADS) pos[(int64_t)t * q.world + d] = spos[t];
-  if (!ok) return;
   uint8_t* blk = reinterpret_cast<uint8_t*>(q.peer[d]);
   const int64_t row0 = (int64_t)q.rank * q.mcap;  // my segment in d's receive buffers
   const int H16 = q.H / 8;
@@ -278,17 +281,19 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
     int* ctr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[q.rank]) + q.lay.ctr) + d;
     if (last_arrival(ctr, G)) {
       __threadfence_system();
-      st_sys(d_flags + q.rank, 1);
+      st_sys(d_flags + q.rank, call);
       MOEK_TR(3);
     }
   }
 }
 
-__global__ void ep_wait_kernel(const int* __restrict__ flags, int world, int* err, uint64_t timeout_ns) {
+__global__ void ep_wait_kernel(const int* __restrict__ flags, const int* __restrict__ calls, int world, int* err,
+                               uint64_t timeout_ns) {
   pdl_wait();
   pdl_launch_dependents();
   const uint64_t deadline = globaltimer() + timeout_ns;
-  for (int s = threadIdx.x; s < world; s += blockDim.x) wait_flag(flags + s, 1, deadline, err);
+  const int call = *reinterpret_cast<const volatile int*>(calls) + 1;
+  for (int s = threadIdx.x; s < world; s += blockDim.x) wait_flag(flags + s, call, deadline, err);
 }
 
 __global__ void __launch_bounds__(P2P_THREADS) ep_combine_p2p_kernel(P2PArgs q, const float* __restrict__ rows,
@@ -296,6 +301,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_combine_p2p_kernel(P2PArgs q, 
   pdl_wait();
   pdl_launch_dependents();
   const int s = blockIdx.x / G, g = blockIdx.x - s * G, k = q.k;
+  const int call = current_call(q);
   uint8_t* mine = reinterpret_cast<uint8_t*>(q.peer[q.rank]);
   const int32_t* rid = reinterpret_cast<const int32_t*>(mine + q.lay.ids);
   float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(q.peer[s]) + q.lay.back) +
@@ -326,7 +332,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_combine_p2p_kernel(P2PArgs q, 
     int* ctr = reinterpret_cast<int*>(mine + q.lay.ctr) + q.world + s;
     if (last_arrival(ctr, G)) {
       __threadfence_system();
-      st_sys(p2p_flags(q, s) + q.world + q.rank, 1);
+      st_sys(p2p_flags(q, s) + q.world + q.rank, call);
     }
   }
 }
@@ -339,16 +345,16 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
   __shared__ int ok;
   uint8_t* mine = reinterpret_cast<uint8_t*>(q.peer[q.rank]);
   int* my_flags = reinterpret_cast<int*>(mine + q.lay.flags);
+  const int call = current_call(q);
   if (threadIdx.x < 32) {
     bool good = true;
     const uint64_t deadline = globaltimer() + q.timeout_ns;
-    for (int s = threadIdx.x; s < q.world; s += 32) good &= wait_flag(my_flags + q.world + s, 1, deadline, q.err);
+    for (int s = threadIdx.x; s < q.world; s += 32) good &= wait_flag(my_flags + q.world + s, call, deadline, q.err);
     good = __all_sync(0xffffffffu, good);
     if (threadIdx.x == 0) ok = good;
     if (threadIdx.x == 0) MOEK_TR(9);
   }
   __syncthreads();
-  if (blockIdx.x == 0 && threadIdx.x < q.world) st_sys(my_flags + threadIdx.x, 0);  // the senders may write again
   if (!ok) return;
   const float4* back = reinterpret_cast<const float4*>(mine + q.lay.back);
   const int H4 = q.H / 4;
@@ -373,7 +379,13 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
     reinterpret_cast<uint2*>(out)[i] = w;
   }
   __syncthreads();
-  if (threadIdx.x == 0) MOEK_TR(10);
+  if (threadIdx.x == 0) {  // every CTA has read `call`: the last one to finish completes the call
+    MOEK_TR(10);
+    if (last_arrival(p2p_call(q) + 1, gridDim.x)) {
+      __threadfence();
+      *p2p_call(q) = call;
+    }
+  }
 }
 
 MOEK_TRACE_COPY_FN(trace_copy_ep)
@@ -390,7 +402,9 @@ cudaError_t launch_ep_dispatch_p2p(const P2PArgs& a, const __nv_bfloat16* x, con
 }
 
 cudaError_t launch_ep_wait(const int* flags, int world, int* err, uint64_t timeout_ns, cudaStream_t st) {
-  cudaError_t e = launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, flags, world, err, timeout_ns);
+  // the completed-call count sits after the flags and the 2 world arrival counters (p2p_layout)
+  const int* calls = flags + up256(2 * world * 4) / 4 + 2 * world;
+  cudaError_t e = launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, flags, calls, world, err, timeout_ns);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -81,6 +81,7 @@ struct LayerMat {                  // one weight matrix in this build's layout (
   const int32_t* exc_off;
   const uint32_t* exc_ent;
   int N, K, nt, nstage, nsplit;  // nt = N / 256 items, nstage = K / 128, nsplit = k-splits per item
+  uint64_t divmask;              // bit s set when s divides nstage (the whole-stage k-splits)
 };
 struct LayerParams {
   LayerMat m[2];  // 0 = gate_up, 1 = down
@@ -104,6 +105,7 @@ struct LayerParams {
   // back buffer; once every row is written, rank s's back flag for this rank is raised.
   const uint64_t* ep_peer;   // [ep_world] device table: base of each rank's exchange block
   const int* ep_recv_flags;  // this rank's flags [0, ep_world)
+  const int* ep_call;        // this rank's completed-call counter (the current call is *ep_call + 1)
   int64_t ep_back_off, ep_flags_off;  // byte offsets of the back buffer and the flags in an exchange block
   int ep_world, ep_rank, ep_mcap;
   int tail;  // 1: items past the last whole wave of units may use a finer k-split (up to one per stage)
@@ -153,7 +155,9 @@ constexpr int EP_P2P_MAXM = 1024;  // tokens per rank and call of the peer-memor
 // segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent): byte offsets of the received bf16 rows [R, H], their
 // local expert ids int32 [R, k] (-1: slot owned elsewhere or unused row) and router weights fp32 [R, k], the returned
 // fp32 partial rows [R, H] (segment d = what rank d returned for this rank's tokens), the flags int32 [2 world]
-// ([s]: rank s wrote receive segment s; [world + d]: rank d wrote back segment d) and arrival counters int32 [2 world].
+// ([s]: the call number whose rows rank s wrote into receive segment s; [world + d]: the call number whose partials
+// rank d wrote into back segment d) and counters int32 [2 world + 2] (arrival counters; [2 world] = the number of
+// calls this rank has completed, advanced by its unpack; [2 world + 1] = the unpack's arrival counter).
 struct P2PLayout {
   int64_t x, ids, w, back, flags, ctr, total;
 };
@@ -167,7 +171,7 @@ __host__ __device__ inline P2PLayout p2p_layout(int world, int mcap, int H, int 
   l.back = l.w + up256(R * k * 4);
   l.flags = l.back + up256(R * H * 4);
   l.ctr = l.flags + up256(2 * world * 4);
-  l.total = l.ctr + up256(2 * world * 4);
+  l.total = l.ctr + up256((2 * world + 2) * 4);
   return l;
 }
 struct P2PArgs {  // peer-memory exchange of the fixed-capacity EP path (moek_ep.cu)

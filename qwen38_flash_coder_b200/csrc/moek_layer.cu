@@ -62,7 +62,8 @@ constexpr int LBK = 2 * BK;                  // k per pipeline stage: one packed
 constexpr int LSTAGE = 2 * STAGE_BYTES;      // 16 KB of packed codes per (item, stage): one bulk copy
 constexpr int X_STRIDE = LBK * 2 + 16;       // bytes per activation row in a slot (+16: conflict-free reads)
 constexpr int SC_BYTES = ITEM_COLS * KG;     // scale table of a stage: one byte per (weight row, k-group)
-constexpr int NLUT = 8;         // per-unit (B | R) tables in flight (the scale warp runs at most 4 units ahead)
+constexpr int NLUT = 4;  // per-unit {B B, R R} tables in flight: a unit's table is written once its first stage has
+                         // landed, when the consumers have released every stage of the unit NLUT units before
 constexpr int MAXU = 32;        // units per metadata round
 
 struct UnitMeta {
@@ -87,9 +88,11 @@ __device__ __forceinline__ PhasePlan plan_phase(const LayerMat& m, int nblk, int
   if (tail && main_units > grid) {
     const int nim = main_units / grid * grid / m.nsplit;
     const int rem = ni - nim;
-    int st = m.nsplit;
-    for (int s = m.nsplit + 1; s <= m.nstage; s++)
-      if (m.nstage % s == 0 && rem * s <= grid) st = s;
+    int st = m.nsplit;  // the finest whole-stage split (a divisor of nstage, precomputed) that fits the grid
+    for (uint64_t dm = m.divmask >> (m.nsplit + 1) << (m.nsplit + 1); dm; dm &= dm - 1) {
+      const int s = __ffsll((long long)dm) - 1;
+      if (rem * s <= grid) st = s;
+    }
     if (rem > 0 && st > m.nsplit) {
       q.ni_main = nim;
       q.s_tail = st;
@@ -109,7 +112,7 @@ struct Cfg {
   static constexpr int META_OFF = NS * SLOT;
   static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
   static constexpr int LUT_OFF = IDS_OFF + MAXU * XR * 4;
-  static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 4;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
+  static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 8;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
   static constexpr int MISC_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;
   static constexpr int PLAN_OFF = MISC_OFF + 16;  // the two phase plans
   static constexpr int BAR_OFF = (PLAN_OFF + 2 * (int)sizeof(PhasePlan) + 7) / 8 * 8;
@@ -121,7 +124,7 @@ struct Cfg {
 };
 
 __device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -163,11 +166,12 @@ __device__ __forceinline__ bool wait_stamp(const int* stamp, int want, uint64_t 
   }
 }
 
-// Raise, on every rank s, s's back flag for this rank (all of this rank's returned rows are written).
-__device__ __forceinline__ void ep_signal(const LayerParams& p) {
+// Raise, on every rank s, s's back flag for this rank to this call's number (all of this rank's returned rows are
+// written).
+__device__ __forceinline__ void ep_signal(const LayerParams& p, int call) {
   for (int s = 0; s < p.ep_world; s++)
     st_sys(reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(p.ep_peer[s]) + p.ep_flags_off) + p.ep_world + p.ep_rank,
-           1);
+           call);
 }
 
 __device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePlan& q0, const PhasePlan& q1, int u,
@@ -201,7 +205,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   extern __shared__ __align__(128) uint8_t smem[];
   UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);
   int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::LUT_OFF);
+  uint2* lut = reinterpret_cast<uint2*>(smem + C::LUT_OFF);  // per unit: scale byte -> {B B, R R} (moek_common.cuh)
   int* srow = reinterpret_cast<int*>(smem + C::ROUTE_OFF);
   int* bexp = srow + LAYER_MAXIDS;
   int* bstart = bexp + LAYER_MAXIDS;
@@ -234,12 +238,21 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   pdl_launch_dependents();
   if (tid == 0) MOEK_TR(1);
   const uint64_t deadline = globaltimer() + p.timeout_ns;
-  const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
   const int n = p.num_ids, k = p.top_k;
+  // the routing loads first (each thread's at most two ids: n <= 512 < 2 x THREADS); expert-parallel receive buffers
+  // are read only after their flags (below)
+  int e_in[2] = {-1, -1};
+  if (!p.ep_peer) {
+    if (tid < n) e_in[0] = p.ids[tid];
+    if (tid + THREADS < n) e_in[1] = p.ids[tid + THREADS];
+  }
+  const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
+  // expert-parallel: this exchange call's number (the flags carry it, so they never need resetting)
+  const int ep_call = p.ep_peer ? *reinterpret_cast<volatile const int*>(p.ep_call) + 1 : 0;
   if (p.ep_peer) {  // expert-parallel: wait until every sender's rows, ids and weights are in the receive buffers
     if (warp == 0) {
       bool good = true;
-      for (int s = lane; s < p.ep_world; s += 32) good &= wait_flag(p.ep_recv_flags + s, 1, deadline, p.err);
+      for (int s = lane; s < p.ep_world; s += 32) good &= wait_flag(p.ep_recv_flags + s, ep_call, deadline, p.err);
       if (!__all_sync(0xffffffffu, good) && lane == 0) misc[2] = 1;
       if (lane == 0) MOEK_TR(2);
     }
@@ -251,28 +264,40 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   {
     uint32_t* key = reinterpret_cast<uint32_t*>(smem);  // scratch in ring slot 0: nothing is copied there yet
     uint32_t* skey = key + LAYER_MAXIDS;
-    for (int i = tid; i < n; i += THREADS) {
-      const int e = p.ids[i];
-      const bool v = e >= 0 && e < p.E;
-      key[i] = v ? ((uint32_t)e << 9) | (uint32_t)i : 0xFFFFFFFFu;
-      if (v) atomicAdd(const_cast<int*>(misc + 1), 1);
+    const int n4 = (n + 3) & ~3;  // keys padded to whole uint4 with 0xFFFFFFFF (above every valid key)
+    uint32_t kk[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int i = tid + h * THREADS;
+      if (p.ep_peer && i < n) e_in[h] = p.ids[i];
+      const bool v = i < n && e_in[h] >= 0 && e_in[h] < p.E;
+      kk[h] = v ? ((uint32_t)e_in[h] << 9) | (uint32_t)i : 0xFFFFFFFFu;
+      if (i < n4) key[i] = kk[h];
     }
-    __syncthreads();
-    for (int i = tid; i < n; i += THREADS) {  // rank of each valid key among all keys (they are distinct)
-      const uint32_t ki = key[i];
-      if (ki == 0xFFFFFFFFu) continue;
+    const int nvalid = __syncthreads_count(kk[0] != 0xFFFFFFFFu) + __syncthreads_count(kk[1] != 0xFFFFFFFFu);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {  // rank of each valid key among all keys (they are distinct): 4 keys per load
+      if (kk[h] == 0xFFFFFFFFu) continue;
       int r = 0;
-      for (int j = 0; j < n; j++) r += key[j] < ki;
-      skey[r] = ki;
-    }
-    if (p.ep_peer)  // rows with at least one valid slot: the rows this rank returns
-      for (int t = tid; t < p.M; t += THREADS) {
-        bool any = false;
-        for (int j = 0; j < k; j++) any |= key[t * k + j] != 0xFFFFFFFFu;
-        if (any) atomicAdd(const_cast<int*>(misc + 3), 1);
+      for (int j = 0; j < n4; j += 4) {
+        const uint4 q = *reinterpret_cast<const uint4*>(key + j);
+        r += (q.x < kk[h]) + (q.y < kk[h]) + (q.z < kk[h]) + (q.w < kk[h]);
       }
+      skey[r] = kk[h];
+    }
+    if (p.ep_peer) {  // rows with at least one valid slot: the rows this rank returns (p.M * k <= 512)
+      int rows = 0;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int t = tid + h * THREADS;
+        bool any = false;
+        if (t < p.M)
+          for (int j = 0; j < k; j++) any |= key[t * k + j] != 0xFFFFFFFFu;
+        rows += __syncthreads_count(any);
+      }
+      if (tid == 0) misc[3] = rows;
+    }
     __syncthreads();
-    const int nvalid = misc[1];
     if (warp == 0) {  // blocks: one starts where the expert changes, and after every XR rows of the same expert
       int base = 0, run0 = 0;  // run0: where the expert run that reaches into this chunk started
       for (int p0 = 0; p0 < nvalid; p0 += 32) {
@@ -311,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   const int ep_rows = misc[3];
   if (tid == 0) MOEK_TR(3);
   if (p.ep_peer && ep_rows == 0 && !*abort_flag && blockIdx.x == 0 && tid == 0)
-    ep_signal(p);  // nothing to return: release the senders' waits at once
+    ep_signal(p, ep_call);  // nothing to return: release the senders' waits at once
 
 
   const PhasePlan plan0 = reinterpret_cast<const PhasePlan*>(smem + C::PLAN_OFF)[0],
@@ -449,16 +474,23 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         const uint32_t* eg = mt.exc_ent + o0;
         const uint32_t ex0 = lane < cnt ? eg[lane] : 0u, ex1 = lane + 32 < cnt ? eg[lane + 32] : 0u;
         if (ui + 1 < nu) fetch(ui + 1);
-        uint32_t* lt = lut + (kq % NLUT) * 256;
-#pragma unroll
-        for (int j = 0; j < 8; j++) lt[lane + 32 * j] = scale_word(lane + 32 * j, gsc);
+        uint2* lt = lut + (kq % NLUT) * 256;
         kq++;
         const int r0g = m.ph == 0 ? m.item : 2 * m.item;  // global run index of the pair's first run
+        const int r1g = m.ph == 0 ? mt.nt + m.item : r0g + 1;  // and of its second (gate_up: the up rows' run)
         for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, abort_flag)) {
             ok = false;
             break;
+          }
+          if (lane == 0 && r == 0 && ui == 0 && st - m.st0 < 16) MOEK_TR(96 + st - m.st0);
+          if (st == m.st0) {  // the unit's table: its slot's previous unit is done (the first stage has landed)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              const ScaleBR br = scale_br(lane + 32 * j, gsc);
+              lt[lane + 32 * j] = make_uint2(br.b2, br.r2);
+            }
           }
           const uint8_t* runp = smem + slot * C::SLOT + LSTAGE + run * RUN_BYTES;
           uint8_t* tb = smem + slot * C::SLOT + C::SC_OFF;
@@ -486,7 +518,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           const int eo1 = rr + 1 < su ? __shfl_sync(0xffffffffu, ro, rr + 1) : cnt;
           auto patch = [&](uint32_t en) {
             const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-            if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r0g + 1), p.err)) return;
+            if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r1g), p.err)) return;
             const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
             tb[row * 8 + kg] = (uint8_t)(en >> 24);
           };
@@ -519,38 +551,54 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
         const int G0 = ph == 0 ? warp : 2 * warp, G1 = ph == 0 ? warp + 8 : 2 * warp + 1;
         const int slot00 = 16 * G0 + gq, slot10 = 16 * G1 + gq;
-        const uint32_t* lt = lut + (kq % NLUT) * 256;
+        const uint2* lt = lut + (kq % NLUT) * 256;
         kq++;
         const int ntile = (nv + 7) >> 3;
-        float acc[2][C::T][4];
+        // independent accumulator chains per tile: (64-k half of the stage, gate/up or row group) for one-tile blocks,
+        // summed at the end of the unit, so that consecutive MMAs rarely wait on each other; (row group) for larger
+        // blocks, which have the tiles' chains already (and no registers to spare: 80 per thread at two CTAs per SM)
+        constexpr int NH = C::T == 1 ? 2 : 1;
+        float acc[NH][2][C::T][4];
 #pragma unroll
-        for (int i = 0; i < 2; i++)
+        for (int h = 0; h < NH; h++)
 #pragma unroll
-          for (int t = 0; t < C::T; t++)
+          for (int i = 0; i < 2; i++)
 #pragma unroll
-            for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
+            for (int t = 0; t < C::T; t++)
+#pragma unroll
+              for (int v = 0; v < 4; v++) acc[h][i][t][v] = 0.f;
         bool ok = true;
         const int tu = r * MAXU + ui;  // the unit's index among this CTA's (timeline stamps)
         for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
+          if (tid == 0 && tu == 0 && st - m.st0 < 16) MOEK_TR(64 + 2 * (st - m.st0));
           if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag) ||
               !wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
             ok = false;
             continue;  // stay in step with the other roles' counters
           }
           if (tid == 0 && st == m.st0 && tu < 16) MOEK_TR(8 + 3 * tu);
+          if (tid == 0 && tu == 0 && st - m.st0 < 16) MOEK_TR(65 + 2 * (st - m.st0));
 #pragma unroll
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
           const uint8_t* sx = smem + slot * C::SLOT + C::X_OFF + hf * BK * 2;
           const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + 4 * hf + c;  // byte (k-group) of each row
-          const uint32_t s0a = lt[sc[slot00 * 8]], s0b = lt[sc[(slot00 + 8) * 8]], s1a = lt[sc[slot10 * 8]],
-                         s1b = lt[sc[(slot10 + 8) * 8]];
+          const uint2 s0a = lt[sc[slot00 * 8]], s0b = lt[sc[(slot00 + 8) * 8]], s1a = lt[sc[slot10 * 8]],
+                      s1b = lt[sc[(slot10 + 8) * 8]];
+          // the tiles' activation fragments of this half, shared by both row groups (loaded once here for one-tile
+          // blocks; larger blocks load them next to their MMAs, to keep registers free)
+          uint4 xf[C::T][2];
+          if constexpr (C::T == 1) {
+            const uint8_t* xr = sx + gq * X_STRIDE + c * 32;
+            xf[0][0] = *reinterpret_cast<const uint4*>(xr);
+            xf[0][1] = *reinterpret_cast<const uint4*>(xr + 16);
+          }
 #pragma unroll
           for (int i = 0; i < 2; i++) {
-            const uint32_t wa = i ? s1a : s0a, wb = i ? s1b : s0b;
-            const ScaleBR sa{prmt_b(wa, 0x1010), prmt_b(wa, 0x3232)}, sbv{prmt_b(wb, 0x1010), prmt_b(wb, 0x3232)};
+            const uint2 wa = i ? s1a : s0a, wb = i ? s1b : s0b;
+            const ScaleBR sa{wa.x, wa.y}, sbv{wb.x, wb.y};
             const uint8_t* wr = sw + (16 * (i ? G1 : G0) + gq) * 32 + w_off;
             const uint2 qa = *reinterpret_cast<const uint2*>(wr), qb = *reinterpret_cast<const uint2*>(wr + 8 * 32);
             uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
@@ -565,26 +613,37 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 #pragma unroll
             for (int t = 0; t < C::T; t++) {
               if (t < ntile) {
-                const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
-                const uint4 x0 = *reinterpret_cast<const uint4*>(xr);
-                const uint4 x1 = *reinterpret_cast<const uint4*>(xr + 16);
-                mma_16816(acc[i][t], A0, x0.x, x0.y);
-                mma_16816(acc[i][t], A1, x0.z, x0.w);
-                mma_16816(acc[i][t], A2, x1.x, x1.y);
-                mma_16816(acc[i][t], A3, x1.z, x1.w);
+                if constexpr (C::T > 1) {
+                  const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
+                  xf[t][0] = *reinterpret_cast<const uint4*>(xr);
+                  xf[t][1] = *reinterpret_cast<const uint4*>(xr + 16);
+                }
+                mma_16816(acc[hf % NH][i][t], A0, xf[t][0].x, xf[t][0].y);
+                mma_16816(acc[hf % NH][i][t], A1, xf[t][0].z, xf[t][0].w);
+                mma_16816(acc[hf % NH][i][t], A2, xf[t][1].x, xf[t][1].y);
+                mma_16816(acc[hf % NH][i][t], A3, xf[t][1].z, xf[t][1].w);
               }
             }
           }
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(empty + slot);
+          if (tid == 0 && tu == 0 && st - m.st0 < 16) MOEK_TR(112 + st - m.st0);
         }
         ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
         if (!ok) continue;
         if (tid == 0 && tu < 16) MOEK_TR(9 + 3 * tu);
+        if constexpr (NH == 2) {
+#pragma unroll
+          for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int t = 0; t < C::T; t++)
+#pragma unroll
+              for (int v = 0; v < 4; v++) acc[0][i][t][v] += acc[NH - 1][i][t][v];
+        }
 
         // ------------------------------------------------------------------------------------------ finishing
-        // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
+        // acc[0][i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
         const int N = mt.N;
         if (ph == 0) {
           const int nt1 = mt.nt;
@@ -600,7 +659,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 #pragma unroll
                 for (int h = 0; h < 2; h++)
                   p.act[(int64_t)ids[row] * I + 128 * item + slot00 + 8 * h] =
-                      __float2bfloat16_rn(silu(acc[0][t][2 * h + v]) * acc[1][t][2 * h + v]);
+                      __float2bfloat16_rn(silu(acc[0][0][t][2 * h + v]) * acc[0][1][t][2 * h + v]);
               }
             }
           } else {
@@ -615,8 +674,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
                 float* prow = base + (int64_t)ids[row] * N;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                  prow[128 * item + slot00 + 8 * h] = acc[0][t][2 * h + v];
-                  prow[I + 128 * item + slot00 + 8 * h] = acc[1][t][2 * h + v];
+                  prow[128 * item + slot00 + 8 * h] = acc[0][0][t][2 * h + v];
+                  prow[I + 128 * item + slot00 + 8 * h] = acc[0][1][t][2 * h + v];
                 }
               }
             }
@@ -673,8 +732,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               const float w = p.tw[id];
 #pragma unroll
               for (int h = 0; h < 2; h++) {
-                rows[(int64_t)id * H + 256 * item + slot00 + 8 * h] = w * acc[0][t][2 * h + v];
-                rows[(int64_t)id * H + 256 * item + slot10 + 8 * h] = w * acc[1][t][2 * h + v];
+                rows[(int64_t)id * H + 256 * item + slot00 + 8 * h] = w * acc[0][0][t][2 * h + v];
+                rows[(int64_t)id * H + 256 * item + slot10 + 8 * h] = w * acc[0][1][t][2 * h + v];
               }
             }
           }
@@ -690,8 +749,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               float* prow = base + (int64_t)ids[row] * N + 256 * item;
 #pragma unroll
               for (int h = 0; h < 2; h++) {
-                prow[slot00 + 8 * h] = acc[0][t][2 * h + v];
-                prow[slot10 + 8 * h] = acc[1][t][2 * h + v];
+                prow[slot00 + 8 * h] = acc[0][0][t][2 * h + v];
+                prow[slot10 + 8 * h] = acc[0][1][t][2 * h + v];
               }
             }
           }
@@ -756,7 +815,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             if (atomicAdd(p.ctr + p.off_ep, pieces) + pieces == want) {
               p.ctr[p.off_ep] = 0;
               __threadfence_system();
-              ep_signal(p);
+              ep_signal(p, ep_call);
             }
           }
         }

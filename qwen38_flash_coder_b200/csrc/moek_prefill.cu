@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t u_next = next_valid(u + gridDim.x);
       if (u_next < nunits) fetch(u_next);
       const int r0g = p.gate_up ? ui.item : 2 * ui.item;
+      const int r1g = p.gate_up ? nt + ui.item : r0g + 1;  // the pair's second run (gate_up: the up rows' run)
       // the (B | R) table of this expert, once the dequant warps finished the unit that used this buffer last
       if (un >= 2 && !wait_warp(B.lutempty + lb, ((un >> 1) - 1) & 1, deadline, p.err, abort_flag)) break;
 #pragma unroll
@@ -491,7 +492,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int eo1 = rn + 1 < nb ? __shfl_sync(0xffffffffu, ro, rn + 1) : cnt;
         auto patch = [&](uint32_t en) {
           const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
-          if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r0g + 1), p.err)) return;
+          if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r1g), p.err)) return;
           if ((kg >> 2) != (st & 1)) return;
           const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
           reinterpret_cast<uint8_t*>(tbl)[row * 4 + (kg & 3)] = (uint8_t)(en >> 24);

@@ -16,9 +16,10 @@ Output, per matrix:
   row r holds the item's row r over the stage's 64 k as 8 words, word w = the 8 consecutive k ``64s + 8w + i``
   (i = 0..7), so words 2c and 2c + 1 are k-group c (one scale). Inside a word the 4 bits of code i (m, e0, e1, sign
   = bits 0..3 of the E2M1 code) sit at bit positions ``CODE_BITS[i]``: codes 0 and 1 exactly where a bf16 pair wants
-  them (sign at 15 / 31, e1 e0 m at 8..6 / 24..22, which makes the pair e2m1 * 2^-126), codes 2-3 and 4-5 three and
-  six bits lower, codes 6-7 in the bits left over; the decode of a word into its four bf16 pairs (k, k+1) is then
-  one mask, two shift-and-masks and one three-part gather (moek_common.cuh). The row's two 16-byte halves are swapped when
+  them (sign at 15 / 31, e1 e0 m at 8..6 / 24..22, which makes the pair e2m1 * 2^-126), codes 2-3 and 4-5 that
+  pattern rotated left by 4 and 10 bits, codes 6-7 their mantissa bits rotated by 14 and the rest by 6 (the four
+  rotations tile the 32 bits); the decode of a word into its four bf16 pairs (k, k+1) is then one mask, two
+  rotate-and-masks and one two-part gather, nine integer operations (moek_common.cuh). The row's two 16-byte halves are swapped when
   bit 2 of r is set, so that 8 threads reading 16 bytes of 8 consecutive rows, or 32 lanes reading 8 bytes
   (k-group c of rows g and g + 8, the A operand of mma.sync m16n8k16), hit distinct shared-memory banks. Item rows
   0..127 are gate rows ``128t + r`` and 128..255 the matching up rows ``I + 128t + r - 128`` (gate_up), or rows
@@ -29,8 +30,8 @@ import torch
 KG = 8
 RUN = 16 + KG * 64  # 528: packed bytes per (expert, run of 8 k-groups, 128 positions)
 # bit positions (m, e0, e1, sign) of code i of a word's 8 consecutive k
-CODE_BITS = ((6, 7, 8, 15), (22, 23, 24, 31), (3, 4, 5, 12), (19, 20, 21, 28), (0, 1, 2, 9), (16, 17, 18, 25),
-             (10, 13, 14, 11), (26, 29, 30, 27))
+CODE_BITS = ((6, 7, 8, 15), (22, 23, 24, 31), (10, 11, 12, 19), (26, 27, 28, 3), (16, 17, 18, 25), (0, 1, 2, 9),
+             (20, 13, 14, 21), (4, 29, 30, 5))
 
 
 def _spread_table(device) -> torch.Tensor:

@@ -17,7 +17,7 @@ import statistics
 
 import numpy as np
 
-CTAS, SLOTS = 1024, 64
+CTAS, SLOTS = 1024, 128
 
 LAYER_PHASES = {0: "start", 1: "after dependent-launch wait", 2: "EP flags seen", 3: "routing done",
                 4: "first weight copy issued", 5: "consumers done", 6: "end"}
@@ -64,6 +64,18 @@ def summarize(t: np.ndarray, kind: int) -> dict:
                              "end": row[2]})
     if kind == 0:
         out["units_per_cta"] = (int(np.median(t[:, 7])), int(t[:, 7].max()))
+        stages = []  # the first unit's stages (consumer warp 0): data wait, compute, and when the scale warp got them
+        for s in range(16):
+            w0, w1, sc, end = t[:, 64 + 2 * s], t[:, 65 + 2 * s], t[:, 96 + s], t[:, 112 + s]
+            ok = (w0 > 0) & (w1 > 0) & (end > 0)
+            if not ok.any():
+                break
+            med = lambda v: round(float(np.median(v)) / 1e3, 2)
+            sok = ok & (sc > 0)
+            stages.append({"stage": s, "ctas": int(ok.sum()), "ready_at": med(w1[ok] - t0),
+                           "wait": med(w1[ok] - w0[ok]), "compute": med(end[ok] - w1[ok]),
+                           "scale_lead": med(w1[sok] - sc[sok]) if sok.any() else None})
+        out["unit0_stages"] = stages
         waits = []
         for j in range(4):
             a, b = t[:, 56 + 2 * j], t[:, 57 + 2 * j]
@@ -122,6 +134,9 @@ def main():
             f = lambda v: f"{v[0]:7.2f}/{v[1]:7.2f}" if v else "      -"
             print(f"  unit {u['unit']:2d} ({u['ctas']:4d} CTAs): first ready {f(u['first_ready'])}  last stage "
                   f"{f(u['last_stage'])}  end {f(u['end'])}  (median/max us)")
+        for s in r.get("unit0_stages", []):
+            print(f"  unit 0 stage {s['stage']:2d}: ready at {s['ready_at']:7.2f} us (waited {s['wait']:5.2f}), compute "
+                  f"{s['compute']:5.2f} us, scale warp had the data {s['scale_lead']} us before (median over CTAs)")
         if "act_wait_us" in r:
             print(f"  act waits: median {r['act_wait_us'][0]} us, max {r['act_wait_us'][1]} us ({r['act_wait_us'][2]})")
 

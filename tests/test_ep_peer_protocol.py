@@ -11,11 +11,14 @@ segments, runs every rank's program under many random schedules (sequentially co
 - freshness: every read of a receive or back segment sees the data of the current layer;
 - no overwrite: nobody writes a segment before its reader has consumed the previous layer's data.
 
+The flags carry the call (layer) number L instead of 0/1, so nothing resets them and dispatch writes without
+waiting: a sender dispatches call L only after its own unpack of call L - 1 has seen every owner's back flag for
+L - 1, which each owner raised after it had read the sender's rows of L - 1.
+
 It checks the protocol's logic, not the memory ordering of the CUDA code (the kernels publish with fences and
-system-scope release stores and read after acquire loads). Planted mistakes (a missing wait, a missing reset, a flag
-raised before its data is written) must be caught, so the checker is known to bite. Clearing the receive flags at the
-start of unpack is safe: unpack starts only after the layer's readers have completed (stream order), and a sender
-cannot dispatch the next layer before its own unpack has seen this rank's back flag anyway.
+system-scope release stores and read after acquire loads). Planted mistakes (a flag raised before its data is
+written, a back flag raised before the partials, an unpack that does not wait or that accepts the previous call's
+flag, a 0/1 flag that is never reset) must be caught, so the checker is known to bite.
 """
 import random
 
@@ -48,30 +51,24 @@ def _program(st: State, r: int, layers: int, fused: bool, plant: str):
     do = lambda f: ("do", f)
     kernels = []
     for L in range(1, layers + 1):
-        # dispatch: CTA (d, g); g = 0 resets my back flag d; each waits for d's receive flag for me to be 0, writes
-        # its part; the last of the G arrivals (a self-resetting counter) raises d's receive flag for me
+        # dispatch: CTA (d, g) writes its part of d's receive segment for me; the last of the G arrivals (a
+        # self-resetting counter) sets d's receive flag for me to this call's number
         dispatch = []
+        mark = (lambda L: 1) if plant == "binary_flags" else (lambda L: L)
         for d in range(W):
             for g in range(G):
-                steps = []
-                if g == 0 and plant != "dispatch_no_reset":
-                    steps.append(do(lambda d=d: st.back_flag[r].__setitem__(d, 0)))
-                if plant != "dispatch_no_wait":
-                    steps.append(("wait", lambda d=d: st.recv_flag[d][r] == 0))
-
                 def write(d=d, g=g, L=L):
                     if st.recv_read[d][r][g] != L - 1:
                         raise Violation(f"rank {r} overwrote rank {d}'s receive segment before layer {L - 1} was read")
                     st.recv_gen[d][r][g] = L
 
-                def arrive(d=d):
+                def arrive(d=d, L=L):
                     st.disp_ctr[r][d] += 1
                     if st.disp_ctr[r][d] == G:
                         st.disp_ctr[r][d] = 0
-                        st.recv_flag[d][r] = 1
+                        st.recv_flag[d][r] = mark(L)
 
-                steps += [do(write), do(arrive)]
-                dispatch.append(steps)
+                dispatch.append([do(arrive), do(write)] if plant == "flag_before_data" else [do(write), do(arrive)])
         kernels.append(dispatch)
 
         def read(s, g, L=L):
@@ -84,18 +81,18 @@ def _program(st: State, r: int, layers: int, fused: bool, plant: str):
                 raise Violation(f"rank {r} overwrote rank {s}'s back segment before layer {L - 1} was read")
             st.back_gen[s][r][j] = L
 
-        def raise_all():
+        def raise_all(L=L):
             for s in range(W):
-                st.back_flag[s][r] = 1
+                st.back_flag[s][r] = mark(L)
 
-        recv_ready = ("wait", lambda: all(st.recv_flag[r][s] == 1 for s in range(W)))
+        recv_ready = ("wait", lambda L=L: all(st.recv_flag[r][s] == mark(L) for s in range(W)))
         read_all = [do(lambda s=s, g=g, f=read: f(s, g)) for s in range(W) for g in range(G)]
         if fused:
             # the whole-layer kernel: every CTA waits for the receive flags and routes (reads every segment); each
             # piece (a row's sum for one item) goes back to its sender; the arrival that completes the last piece
             # raises every sender's back flag (the kernel's other case, nothing to return, raises them right after
             # the wait and is not modelled)
-            def piece_arrive():
+            def piece_arrive(raise_all=raise_all):
                 st.piece_ctr[r] += 1
                 if st.piece_ctr[r] == W * G:
                     st.piece_ctr[r] = 0
@@ -113,27 +110,30 @@ def _program(st: State, r: int, layers: int, fused: bool, plant: str):
             kernels.append([[recv_ready]])  # ep_wait
             kernels.append([read_all])  # the local layer's kernels
 
-            def comb_arrive(s):
+            def comb_arrive(s, L=L):
                 st.comb_ctr[r][s] += 1
                 if st.comb_ctr[r][s] == G:
                     st.comb_ctr[r][s] = 0
-                    st.back_flag[s][r] = 1
+                    st.back_flag[s][r] = mark(L)
 
             # combine: CTA (s, j) returns part j of segment s; the last of the G arrivals raises s's back flag
-            kernels.append([[do(lambda s=s, j=j, f=return_part: f(s, j)), do(lambda s=s: comb_arrive(s))]
+            kernels.append([[do(lambda s=s, j=j, f=return_part: f(s, j)), do(lambda s=s, c=comb_arrive: c(s))]
                             for s in range(W) for j in range(G)])
 
-        # unpack: every CTA waits for the back flags; CTA 0 clears my receive flags; the CTAs read the back segments
+        # unpack: every CTA waits until the back flags carry this call's number, then reads the back segments (the
+        # last CTA advancing the completed-call count is the L + 1 of the next call's closures)
         def read_back(d, j, L=L):
             if st.back_gen[r][d][j] != L:
                 raise Violation(f"rank {r} read a stale back segment {d} in layer {L}")
             st.back_read[r][d][j] = L
 
-        back_ready = [] if plant == "unpack_no_wait" else [("wait", lambda: all(st.back_flag[r][d] == 1
-                                                                               for d in range(W)))]
-        clear = [do(lambda s=s: st.recv_flag[r].__setitem__(s, 0)) for s in range(W)]
-        unpack = [back_ready + clear] + [back_ready + [do(lambda d=d, j=j, f=read_back: f(d, j))]
-                                         for d in range(W) for j in range(G)]
+        if plant == "unpack_no_wait":
+            back_ready = []
+        elif plant == "unpack_accepts_previous":
+            back_ready = [("wait", lambda L=L: all(st.back_flag[r][d] >= L - 1 for d in range(W)))]
+        else:
+            back_ready = [("wait", lambda L=L: all(st.back_flag[r][d] == mark(L) for d in range(W)))]
+        unpack = [back_ready + [do(lambda d=d, j=j, f=read_back: f(d, j))] for d in range(W) for j in range(G)]
         kernels.append(unpack)
     return kernels
 
@@ -180,8 +180,8 @@ def test_protocol_progress_and_freshness(world, fused, parts):
         run_schedule(world, layers=5, fused=fused, seed=1000 * world + seed, parts=parts)
 
 
-@pytest.mark.parametrize("plant", ["dispatch_no_wait", "dispatch_no_reset", "layer_signals_before_return",
-                                   "unpack_no_wait"])
+@pytest.mark.parametrize("plant", ["flag_before_data", "binary_flags", "layer_signals_before_return",
+                                   "unpack_no_wait", "unpack_accepts_previous"])
 def test_planted_mistakes_are_caught(plant):
     """Each planted mistake leads, in some schedule, to a stale read, an overwrite or a deadlock."""
     caught = 0

@@ -1,6 +1,6 @@
 """Expert parallelism on the GPU: the dispatch / combine kernels against the CPU restatement (bit-exact), the whole
-EP layer on a one-rank NCCL group against ops.fused_moe, and, when two GPUs are visible, two NCCL ranks against the
-one-GPU layer. The EP layer adds the same fp32 slot terms as the one-GPU layer, but the one-GPU decode epilogue
+EP layer on a one-rank NCCL group against ops.fused_moe, and, when 2, 4 or 8 GPUs are visible, that many NCCL ranks
+against the one-GPU layer. The EP layer adds the same fp32 slot terms as the one-GPU layer, but the one-GPU decode epilogue
 fuses each router-weight product into its running sum (one rounding) where EP rounds the weighted row first, so the
 two agree to fp32 rounding, not bitwise."""
 import datetime
@@ -111,7 +111,7 @@ def test_ep_one_rank_equals_fused_moe(m, capacity):
 @pytest.mark.parametrize("m,mcap", [(8, 8), (5, 8), (100, 128)])
 def test_ep_peer_exchange_one_rank(m, mcap):
     """The peer-memory exchange on a one-rank group (the block shared with itself): equal to the NCCL fixed-capacity
-    path bit for bit, repeatable (the flags reset themselves), also when replayed as a CUDA graph. mcap 8: the
+    path bit for bit, repeatable (the flags carry the call number), also when replayed as a CUDA graph. mcap 8: the
     whole-layer kernel reads the receive segment and returns the partials itself (three launches); mcap 128: more
     slots than it takes, so the local layer's kernels run between a wait and the combine kernel."""
     import torch.distributed as dist
@@ -171,7 +171,7 @@ def test_ep_peer_layer_wait_expires():
         back = px.back.clone()
         _lib.call("moek_set_wait_timeout_ns", 20_000_000)  # 20 ms
         try:
-            ops.layer_p2p(px, layer.prep)  # the receive flag is 0: nothing was dispatched
+            ops.layer_p2p(px, layer.prep)  # no dispatch raised the receive flag to this call's number
             torch.cuda.synchronize()
         finally:
             _lib.call("moek_set_wait_timeout_ns", 2_000_000_000)
@@ -187,7 +187,7 @@ def test_ep_peer_layer_wait_expires():
         dist.destroy_process_group()
 
 
-def _two_gpu_rank(rank, port, q):
+def _ep_rank(rank, world, port, q):
     import torch.distributed as dist
 
     from oracle import moe_ref
@@ -196,11 +196,12 @@ def _two_gpu_rank(rank, port, q):
     try:
         dev = torch.device("cuda", rank)
         torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
-        E, m = 64, (40 if rank == 0 else 700)  # one rank on the decode path, the other on the tcgen05 path
+        E, m = 64, (40 if rank % 2 == 0 else 700)  # ranks on the decode path and on the tcgen05 path
         w13, w2 = synth.make_layer(E, 2048, 512, 31, device=dev)
-        layer = ep.EPLayer(ep.shard_checkpoint(w13, E, 2, rank), ep.shard_checkpoint(w2, E, 2, rank), E, 2, rank)
+        layer = ep.EPLayer(ep.shard_checkpoint(w13, E, world, rank), ep.shard_checkpoint(w2, E, world, rank), E,
+                           world, rank)
         full = ep.EPLayer(w13, w2, E, 1, 0)
         x = synth.activations(m, 2048, 40 + rank, device=dev)
         ids, wts = synth.route_zipf(m, E, 5, 40 + rank, device=dev)
@@ -210,9 +211,10 @@ def _two_gpu_rank(rank, port, q):
         x2 = synth.activations(m2, 2048, 60 + rank, device=dev)
         ids2, wts2 = synth.route_zipf(m2, E, 5, 60 + rank, device=dev)
         out2 = ep.ep_moe(x2, layer, wts2, ids2, capacity=True)
-        # the same fixed-capacity batch over peer memory: 96 received rows, so the whole-layer kernel reads them in
-        # place and returns the partials over NVLink (the NCCL path above runs the tcgen05 GEMMs on them, a different
-        # fp32 order); the same bits call after call, and the same gate against the one-GPU layer
+        # the same fixed-capacity batch over peer memory: world x 48 received rows (the whole-layer kernel takes up
+        # to 102, so at 2 ranks it reads them in place and returns the partials over NVLink; with more ranks the local
+        # layer's kernels run between a wait and the combine kernel); the same bits call after call, and the same gate
+        # against the one-GPU layer
         px = ep.PeerExchange(None, m2, 2048, 5, dev)
         peer_outs = [ep.ep_moe(x2, layer, wts2, ids2, capacity=True, peer=px) for _ in range(3)]
         ref = ops.fused_moe(x, full.prep, wts, ids)
@@ -234,24 +236,28 @@ def _two_gpu_rank(rank, port, q):
         q.put((rank, "error", repr(exc)))
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_ep_two_ranks_match_one_gpu_layer():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_ranks_match_one_gpu_layer(world):
+    """world NCCL ranks on world GPUs (NVLS off): exact-count and fixed-capacity NCCL exchanges and the peer-memory
+    exchange, every rank's tokens against the one-GPU layer of the same experts."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = pymp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     env = dict(os.environ)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
-        procs = [ctx.Process(target=_two_gpu_rank, args=(r, port, q)) for r in range(2)]
+        procs = [ctx.Process(target=_ep_rank, args=(r, world, port, q)) for r in range(world)]
         for p in procs:
             p.start()
-        res = dict((r, (s, v)) for r, s, v in (q.get(timeout=300) for _ in range(2)))
+        res = dict((r, (s, v)) for r, s, v in (q.get(timeout=300) for _ in range(world)))
         for p in procs:
             p.join(timeout=60)
     finally:
         os.environ.clear()
         os.environ.update(env)
-    for r in range(2):
+    for r in range(world):
         status, val = res[r]
         assert status == "ok", val
         rel, net = val

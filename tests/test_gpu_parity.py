@@ -198,8 +198,10 @@ def test_empty_batch():
 def test_kit_prefill_call_mode0(m):
     """The kit's prefill sequence with its own argument lists (files/mbx_moek.py:266-289, ``split = False``): moe_align
     with block 96, moe_gemm mode 0 for gate_up (act into ``out``) and for down (dout = bf16(topk_w * sum) rows into
-    ``out``), then torch.sum over the top-k slots. dout rows are checked against the oracle's fp32 slot rows, the
-    summed output against the oracle's layer; mode 1 (the reference's stream-k schedule) writes the same bits."""
+    ``out``), then torch.sum over the top-k slots. Mode 1 (the reference's stream-k schedule) writes the same bits;
+    dout is exactly the bf16 rounding of mode 4's fp32 rows (the same sums); dout rows and the summed output are
+    within rel-L2 5e-3 of the oracle (the max-abs bound is the layer output's, not a per-slot row's: rows with a large
+    router weight sit far above the rms of all rows)."""
     e, k, hid, inter = 64, 5, 2048, 512
     w13, w2 = synth.make_layer(e, hid, inter, 21, device=DEV)
     layer = prep.PreparedLayer(w13, w2)
@@ -225,9 +227,17 @@ def test_kit_prefill_call_mode0(m):
         douts.append(dout)
     assert torch.equal(douts[0], douts[1])
     dout = douts[0]
+    act = torch.empty((m * k, inter), dtype=torch.bfloat16, device=DEV)
+    rows32 = torch.empty((m * k, hid), dtype=torch.float32, device=DEV)
+    ops.moe_gemm(x, a.w, none, a.g, sid, eid, npad, a.g, act, k, True, a.sp, a.exc_off, a.exc_ent, ws, cnt, 4, 1,
+                 rows32, 0, True)
+    ops.moe_gemm(act, b.w, none, b.g, sid, eid, npad, tw, dout.clone(), 1, False, b.sp, b.exc_off, b.exc_ent, ws, cnt,
+                 4, 1, rows32, 0, True)
+    torch.cuda.synchronize()
+    assert torch.equal(rows32.to(torch.bfloat16), dout)
     rows = moe_ref.slot_rows(x.cpu(), _np(ids), _np(wts), _ckpt(w13), _ckpt(w2))
-    ok, stats = moe_ref.within_gate(dout.float().cpu(), rows)
-    assert ok, stats
+    rel, _, _ = moe_ref.check(dout.float().cpu(), rows)
+    assert rel <= REL, rel
     out = torch.sum(dout.view(-1, k, hid), dim=1)
     ref = moe_ref.reference(x.cpu(), _np(ids), _np(wts), _ckpt(w13), _ckpt(w2))
     rel, _, _ = moe_ref.check(out.cpu(), ref)

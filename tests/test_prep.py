@@ -125,3 +125,26 @@ def test_unsupported_shapes_raise():
         prep.check_shapes(300, 256, False)
     with pytest.raises(ValueError):
         prep.check_shapes(512, 200, True)
+
+
+def test_device_pair_decode_matches_code_bits():
+    """The device's word decode (moek_common.cuh fp4_pairs: a mask, two rotate-and-masks, a two-part gather),
+    restated here, yields for pair p the codes 2p and 2p + 1 of prep.CODE_BITS at the bf16 positions (sign 15, e1 e0 m
+    at 8..6; the same 16 bits higher for the second code)."""
+    rotr = lambda q, n: ((q >> n) | (q << (32 - n))) & 0xFFFFFFFF
+    P = 0x81C081C0
+
+    def pairs(q):
+        return [q & P, rotr(q, 4) & P, rotr(q, 10) & P, (rotr(q, 14) & 0x00400040) | (rotr(q, 6) & 0x81808180)]
+
+    def place(code):  # m, e0, e1 at 6, 7, 8 and the sign at 15
+        return (code & 7) << 6 | ((code >> 3) & 1) << 15
+
+    flat = [b for bits in prep.CODE_BITS for b in bits]
+    assert sorted(flat) == list(range(32))
+    rng = np.random.default_rng(7)
+    for _ in range(2000):
+        codes = [int(c) for c in rng.integers(0, 16, 8)]
+        q = sum(((c >> b) & 1) << pos for c, bits in zip(codes, prep.CODE_BITS) for b, pos in enumerate(bits))
+        for p, d in enumerate(pairs(q)):
+            assert d == place(codes[2 * p]) | place(codes[2 * p + 1]) << 16
