@@ -266,19 +266,19 @@ MOEK_API int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M
 }
 
 // ------------------------------------------------------------------------------------- whole decode layer
-// Persistent int32 state of moek_moe_layer: [epoch, done, ep, cnt1, rcnt, ready, cnt2, tok]. The layout depends only
-// on (E, H, I), so one zeroed state buffer serves every call of that geometry.
+// Persistent int32 state of moek_moe_layer: [epoch, done, ep, cnt1, ready, cnt2, tok] (ready: one stamp per (block,
+// gate_up item, consumer warp)). The layout depends only on (E, H, I), so one zeroed state buffer serves every call of
+// that geometry.
 struct LayerLayout {
-  int64_t cnt1, rcnt, ready, cnt2, tok, total;
+  int64_t cnt1, ready, cnt2, tok, total;
 };
 static LayerLayout layer_layout(int32_t E, int32_t H, int32_t I) {
   // blocks: at most one per routed slot (an expert with more slots than a block takes spans several)
   const int64_t nbmax = moek::LAYER_MAXIDS, nt1 = 2 * (int64_t)I / 256, nt2 = H / 256;
   LayerLayout l;
   l.cnt1 = 3;
-  l.rcnt = l.cnt1 + nbmax * nt1 * 8;
-  l.ready = l.rcnt + nbmax * nt1;
-  l.cnt2 = l.ready + nbmax * nt1;
+  l.ready = l.cnt1 + nbmax * nt1 * 8;
+  l.cnt2 = l.ready + nbmax * nt1 * 8;
   l.tok = l.cnt2 + nbmax * nt2 * 8;
   l.total = l.tok + (int64_t)moek::LAYER_MAXIDS * nt2 * 8;
   return l;
@@ -409,7 +409,6 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   p.off_ep = 2;
   p.tail = g_layer_tail;
   p.off_cnt1 = (int)lay.cnt1;
-  p.off_rcnt = (int)lay.rcnt;
   p.off_ready = (int)lay.ready;
   p.off_cnt2 = (int)lay.cnt2;
   p.off_tok = (int)lay.tok;

@@ -98,7 +98,7 @@ struct LayerParams {
   int* err;                // device error word
   uint64_t timeout_ns;
   int M, top_k, num_ids, E, H, I;
-  int off_cnt1, off_rcnt, off_ready, off_cnt2, off_tok, off_epoch, off_done, off_ep;  // int offsets into ctr
+  int off_cnt1, off_ready, off_cnt2, off_tok, off_epoch, off_done, off_ep;  // int offsets into ctr
   // Expert-parallel receive side (ep_peer non-null, out and out_rows null): x / ids / tw are this rank's receive
   // buffers of the peer-memory exchange (row s * ep_mcap + p came from rank s), the kernel waits for the receive
   // flags before routing, and each row's fp32 sum of its local slots goes to row ep_rank * ep_mcap + p of rank s's

@@ -20,16 +20,17 @@
 //             (lane 1) by bulk copy (cp.async.bulk, no multicast) into a ring slot. It never waits on another CTA:
 //             the weights of every unit are known once the routing is.
 //   act warp  warp 9: the stage's activation rows. gate_up: the tokens' hidden rows by bulk copy; down: the act rows
-//             of the block, once the gate_up item that produced those act columns is complete in every CTA (a
-//             per-(block, item) ready stamp, acquire-loaded with a bounded wait), by plain loads into the slot.
+//             of the block, once the gate_up item that produced those act columns is complete in every CTA (one
+//             ready stamp per (block, item, consumer warp), acquire-loaded by eight lanes at once with a bounded
+//             wait), by plain loads into the slot.
 //   scales    warp 10: per stage the scale byte of each row x k-group (base + 4-bit offset, then the exceptions),
 //             per unit the (B | R) table of the expert (moek_common.cuh), as in moek_decode.cu.
 //   consumers warps 0-7: the swap-AB mma.sync m16n8k16 of moek_decode.cu (weights = the 16-row A operand, up to 8
 //             tokens = B), fp32 accumulators per unit.
 //   finishing gate_up: with one k-split the lane holds gate and up of the same column and writes
 //             act = bf16(silu(gate) * up); with more, fp32 partials go to the workspace and the warp whose arrival
-//             completes (block, item, warp) adds them in split order. Each warp's completion counts towards the
-//             (block, item) ready stamp. down: partials likewise, then the router weight: fp32 row w * sum; the
+//             completes (block, item, warp) adds them in split order, then releases that warp's ready stamp.
+//             down: partials likewise, then the router weight: fp32 row w * sum; the
 //             arrival that completes a token's valid slots for (item, warp) adds the token's rows in slot order and
 //             rounds once to bf16 (the fp32 oracle's order, bench/moek/problem.py:51-67).
 //
@@ -152,12 +153,20 @@ __device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) 
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
 
-// Bounded wait (every lane) until the stamp reads `want`; the acquire orders the lane's later loads after it.
-__device__ __forceinline__ bool wait_stamp(const int* stamp, int want, uint64_t deadline, int* err,
-                                           volatile int* abort_flag) {
+// Bounded wait of a whole warp until the NCW ready stamps of a (block, item) all read `want`: lane L polls stamp
+// L % NCW (acquire loads, all eight in parallel), then a warp barrier orders every lane's later loads after all the
+// acquires (the consumer warps released their stamps after writing their act columns).
+__device__ __forceinline__ bool wait_stamps(const int* stamps, int want, uint64_t deadline, int* err,
+                                            volatile int* abort_flag) {
+  const int* st = stamps + (threadIdx.x & 31) % NCW;
+  bool seen = false;
   for (uint32_t i = 0;; i++) {
     if (*abort_flag) return false;
-    if (ld_acquire(stamp) == want) return true;
+    if (!seen) seen = ld_acquire(st) == want;
+    if (__all_sync(0xffffffffu, seen)) {
+      __syncwarp();
+      return true;
+    }
     if ((i & 63) == 63 && globaltimer() > deadline) {
       report(err, MOEK_DEV_TIMEOUT);
       *abort_flag = 1;
@@ -415,8 +424,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             const int need = st;
             if (need != ready_item) {
               if (lane == 0 && n_wait < 4) MOEK_TR(56 + 2 * n_wait);
-              if (!wait_stamp(p.ctr + p.off_ready + m.blk * p.m[0].nt + need, epoch + 1, deadline, p.err,
-                              abort_flag)) {
+              if (!wait_stamps(p.ctr + p.off_ready + (m.blk * p.m[0].nt + need) * NCW, epoch + 1, deadline, p.err,
+                               abort_flag)) {
                 ok = false;
               }
               if (lane == 0 && n_wait < 4) MOEK_TR(57 + 2 * n_wait);
@@ -701,17 +710,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               }
             }
           }
-          if (complete) {  // this warp's act columns of (block, item) are written: count towards the ready stamp
+          if (complete) {  // this warp's act columns of (block, item) are written: its ready stamp
             __threadfence();
             __syncwarp();
-            if (lane == 0) {
-              int* rc = p.ctr + p.off_rcnt + (int64_t)blk * nt1 + item;
-              if (atomicAdd(rc, 1) == NCW - 1) {
-                *rc = 0;
-                __threadfence();
-                st_release(p.ctr + p.off_ready + (int64_t)blk * nt1 + item, epoch + 1);
-              }
-            }
+            if (lane == 0) st_release(p.ctr + p.off_ready + ((int64_t)blk * nt1 + item) * NCW + warp, epoch + 1);
           }
           if (tid == 0 && tu < 16) MOEK_TR(10 + 3 * tu);
           continue;
