@@ -5,7 +5,7 @@ Workloads (the reference's configs; synthetic seeded data of those shapes):
 - decode8  (config 2, the headline): a decode verify step, M = 8 tokens per GPU, uniform routing (softmax of N(0,1)
            logits -> top-5 -> renormalise);
 - decode32 (config 3): M = 32 tokens (4 streams x 8), Zipf(1.1) routing over a seeded permutation of the experts;
-- prefill  (config 4): M = 6912 tokens, uniform routing (``--workload prefill_zipf``: the Zipf variant).
+- prefill  (config 4): M = 6912 tokens, uniform routing; prefill_zipf: the same with Zipf(1.1) routing.
 
 Every workload runs on the same 48 layers of 512 experts (hidden 2048, expert intermediate 512, top-5) with
 independent seeded NVFP4 weights (bf16 N(0, 0.02) quantised; 857 MB per layer, 41 GB in HBM). A step runs the 48
@@ -23,8 +23,11 @@ memory and its outputs read back inside the timed region. ``roofline`` = the gat
 bench/moek/problem.py:51-67, restated in oracle/moe_ref.py) on the host cores, same metric and unit.
 Multi-GPU (torchrun, N > 1): the expert-parallel stack (the reference's config 5). The 512 experts of every layer are
 split contiguously over the ranks (each GPU holds 1/N of the 41 GB), each rank brings its own tokens (weak scaling),
-and ``ep.ep_moe`` moves them with NCCL all-to-all: decode M=8 per GPU (the headline, same metric as N=1) and M=64
-Zipf with the fixed-capacity exchange, prefill M=6912 Zipf with exact counts. value = the bytes of the experts the
+and ``ep.ep_moe`` moves them: decode M=8 per GPU (the headline, same metric as N=1) and M=64 Zipf with the
+fixed-capacity exchange over peer memory, prefill M=6912 Zipf per GPU with exact counts over NCCL, and one M=6912
+chunk split over the GPUs (strong scaling). Each EP workload also reports the load-balance ceiling of the contiguous
+expert split (mean over max of the routed rows each rank owns), and before any timing every rank checks its tokens'
+EP output against the one-GPU layer (``parity`` in the line; the run fails outside the gate). value = the bytes of the experts the
 step touched (each streamed once, by its owner) plus every rank's x / output / routing (or the FLOPs of all ranks'
 rows) over the slowest rank's time (CUDA events, max over ranks). The roofline is the local gate_up GEMM on the rows
 one step delivered.
@@ -415,7 +418,8 @@ def main():
             dist.destroy_process_group()
     from qwen38_flash_coder_b200 import prep, synth
 
-    names = [a.workload] + ([] if a.only else [n for n in ("decode8", "decode32", "prefill") if n != a.workload])
+    names = [a.workload] + ([] if a.only else [n for n in ("decode8", "decode32", "prefill", "prefill_zipf")
+                                               if n != a.workload])
     layers = []
     for l in range(a.layers):
         w13, w2 = synth.make_layer(E, H, I, l, device=dev)
@@ -470,7 +474,16 @@ EP_WORKLOADS = {
                      desc="EP decode, M=64 tokens per GPU (8 streams x 8), Zipf(1.1), fixed-capacity exchange"),
     "prefill": dict(m=6912, route="zipf", unit="TFLOP/s", capacity=False,
                     desc="EP prefill chunk, M=6912 tokens per GPU, Zipf(1.1), all-to-allv exchange"),
+    "prefill_strong": dict(m=None, route="zipf", unit="TFLOP/s", capacity=False,
+                           desc="EP prefill, strong scaling: one M=6912 chunk split over the GPUs (6912 / N tokens "
+                                "each), Zipf(1.1), all-to-allv exchange"),
 }
+
+
+def ep_tokens(name, world):
+    """Tokens per rank of an EP workload (the strong-scaling one splits one 6912-token chunk)."""
+    m = EP_WORKLOADS[name]["m"]
+    return m if m is not None else 6912 // world
 
 
 def ep_main(a, rank, world, dev):
@@ -481,7 +494,7 @@ def ep_main(a, rank, world, dev):
 
     from qwen38_flash_coder_b200 import ep, ops, prep, synth
 
-    names = ["decode8"] if a.only else ["decode8", "decode64", "prefill"]
+    names = ["decode8"] if a.only else ["decode8", "decode64", "prefill", "prefill_strong"]
     layers, touched_bytes_all = [], []
     for l in range(a.layers):
         w13, w2 = synth.make_layer(E, H, I, l, device=dev)
@@ -491,7 +504,7 @@ def ep_main(a, rank, world, dev):
         entry = {"layer": L, "x": {}, "route": {}}
         for j, n in enumerate(names):
             seed = 100000 * rank + 100 * l + j
-            m = EP_WORKLOADS[n]["m"]
+            m = ep_tokens(n, world)
             entry["x"][n] = synth.activations(m, H, seed, device=dev)
             entry["route"][n] = route(m, seed, EP_WORKLOADS[n]["route"], dev)
         layers.append(entry)
@@ -512,8 +525,9 @@ def ep_main(a, rank, world, dev):
         """ep.ep_moe on this rank's seeded tokens against ops.fused_moe of the same tokens on this GPU with every
         expert; the worst rank's figures."""
         seed = 100000 * rank + 99
-        x = synth.activations(wl["m"], H, seed, device=dev)
-        ids, wts = route(wl["m"], seed, wl["route"], dev)
+        m = ep_tokens(name, world)
+        x = synth.activations(m, H, seed, device=dev)
+        ids, wts = route(m, seed, wl["route"], dev)
         got = ep.ep_moe(x, par_ep, wts, ids, capacity=wl["capacity"], peer=px)
         ref = ops.fused_moe(x, par_full, wts, ids)
         torch.cuda.synchronize()
@@ -522,6 +536,16 @@ def ep_main(a, rank, world, dev):
         rel, net = over_ranks(rel, world, dev), over_ranks(net, world, dev)
         parity[name] = {"rel_l2": rel, "net_maxabs": net, "ok": bool(rel <= 5e-3 and net <= 2e-2),
                         "exchange": "peer memory" if px is not None else "NCCL"}
+
+    def load_balance(entry, name):
+        """Mean over max of the routed rows each rank owns in this layer (all ranks' tokens): the most that the
+        expert-compute side of a contiguous expert split lets the ranks reach of ideal scaling."""
+        ids = entry["route"][name][0].to(torch.int32)
+        allids = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(allids, ids)
+        g = torch.cat([t.reshape(-1) for t in allids]).long()
+        rows = torch.bincount(g[(g >= 0) & (g < E)] // (E // world), minlength=world).double()
+        return float(rows.mean() / rows.max().clamp_min(1))
 
     def local_touched_bytes(entry, name):
         """Bytes of this rank's experts that any rank's tokens touch in this layer (each streamed once by its
@@ -539,7 +563,7 @@ def ep_main(a, rank, world, dev):
     results = {}
     for name in names:
         wl = EP_WORKLOADS[name]
-        m = wl["m"]
+        m = ep_tokens(name, world)
 
         # fixed-capacity workloads exchange over peer memory (CUDA IPC blocks, this build's kernels) unless asked
         # for NCCL; exact-count workloads use NCCL all-to-allv
@@ -577,7 +601,9 @@ def ep_main(a, rank, world, dev):
         else:
             amount = world * len(layers) * m * TOPK * FLOPS_PER_ROW / 1e12
         res = {"workload": wl["desc"], "value": round(amount / (ms / 1e3), 3), "unit": wl["unit"],
-               "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / len(layers), 2), "clocks": clk,
+               "tokens_per_gpu": m, "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / len(layers), 2),
+               "load_balance_ceiling": round(sum(load_balance(e, name) for e in layers) / len(layers), 4),
+               "clocks": clk,
                "launch": how}
         # the local kernels on the rows one step delivered, replayed alone (this rank): the whole-layer kernel when
         # the received batch is a decode batch, else the tcgen05 gate_up GEMM

@@ -50,7 +50,9 @@ __device__ __forceinline__ void report(int* err, int code) {
 
 // ----------------------------------------------------------------------------------------- timeline stamps
 // Built with -DMOEK_TRACE, a kernel writes %globaltimer stamps of its phases: MOEK_TR(slot) stores the time in
-// g_moek_trace[blockIdx.x][slot] (CTAs and slots beyond the array are not recorded), MOEK_TR_VAL stores a value.
+// g_moek_trace[blockIdx.x][slot] (CTAs and slots beyond the array are not recorded), MOEK_TR_CLK the SM's cycle
+// counter (clock64: fine-grained intervals inside a CTA; %globaltimer may advance in steps of a microsecond),
+// MOEK_TR_VAL a value.
 // Each translation unit has its own array (a static __device__ array defined here), read back by that unit's
 // trace_copy_* function (moek_trace_read). Without the flag the macros are empty.
 constexpr int MOEK_TRACE_CTAS = 1024, MOEK_TRACE_SLOTS = 128;
@@ -62,6 +64,7 @@ static __device__ unsigned long long g_moek_trace[MOEK_TRACE_CTAS][MOEK_TRACE_SL
       moek::g_moek_trace[blockIdx.x][(slot)] = (unsigned long long)(v);          \
   } while (0)
 #define MOEK_TR(slot) MOEK_TR_VAL(slot, moek::globaltimer())
+#define MOEK_TR_CLK(slot) MOEK_TR_VAL(slot, clock64())
 #define MOEK_TRACE_COPY_FN(name)                                                                      \
   cudaError_t name(void* dst, size_t bytes, int clear) {                                              \
     if (bytes > sizeof(g_moek_trace)) bytes = sizeof(g_moek_trace);                                   \
@@ -79,6 +82,9 @@ static __device__ unsigned long long g_moek_trace[MOEK_TRACE_CTAS][MOEK_TRACE_SL
   } while (0)
 #define MOEK_TR(slot) \
   do {                \
+  } while (0)
+#define MOEK_TR_CLK(slot) \
+  do {                    \
   } while (0)
 #define MOEK_TRACE_COPY_FN(name) \
   cudaError_t name(void*, size_t, int) { return cudaErrorNotSupported; }

@@ -388,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             const int64_t wi = (((int64_t)e * mt.nt + item) * mt.nstage + st) * 2;
             bulk_g2s(dst, mt.W + wi * STAGE_BYTES, LSTAGE, full + slot);
             if (g == 0) MOEK_TR(4);
+            if (r == 0 && ci == 0 && st - meta[0].st0 < 8) MOEK_TR_CLK(112 + st - meta[0].st0);
           } else if (lane == 1) {
             const int64_t si = ((int64_t)e * mt.nt + item) * mt.nstage + st;
             bulk_g2s(dst + LSTAGE, mt.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
@@ -420,6 +421,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             __syncwarp();
             for (int rr = lane; rr < nv; rr += 32)
               bulk_g2s(xs + rr * X_STRIDE, p.x + (int64_t)(ids[rr] / k) * p.H + st * LBK, LBK * 2, full + slot);
+            if (lane == 0 && r == 0 && ci == 0 && st - m.st0 < 8) MOEK_TR_CLK(120 + st - m.st0);
           } else {  // act rows: columns [128 st, 128 st + 128) are gate_up item st's (ITEM_COLS / 2 act columns)
             const int need = st;
             if (need != ready_item) {
@@ -493,7 +495,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             ok = false;
             break;
           }
-          if (lane == 0 && r == 0 && ui == 0 && st - m.st0 < 16) MOEK_TR(96 + st - m.st0);
+          if (lane == 0 && r == 0 && ui == 0 && st - m.st0 < 8) MOEK_TR_CLK(96 + st - m.st0);
           if (st == m.st0) {  // the unit's table: its slot's previous unit is done (the first stage has landed)
 #pragma unroll
             for (int j = 0; j < 8; j++) {
@@ -536,6 +538,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           for (int j = max(eo0, 64) + lane; j < eo1; j += 32) patch(eg[j]);  // long lists: the rest from memory
           __syncwarp();
           mbar_arrive(scaled + slot);
+          if (lane == 0 && r == 0 && ui == 0 && st - m.st0 < 8) MOEK_TR_CLK(104 + st - m.st0);
         }
       }
       __syncwarp();
@@ -563,10 +566,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         const uint2* lt = lut + (kq % NLUT) * 256;
         kq++;
         const int ntile = (nv + 7) >> 3;
-        // independent accumulator chains per tile: (64-k half of the stage, gate/up or row group) for one-tile blocks,
-        // summed at the end of the unit, so that consecutive MMAs rarely wait on each other; (row group) for larger
-        // blocks, which have the tiles' chains already (and no registers to spare: 80 per thread at two CTAs per SM)
-        constexpr int NH = C::T == 1 ? 2 : 1;
+        // one accumulator chain per (row group, tile): every block size adds the same terms in the same order, so
+        // the rows per block never change the results (more chains per tile measured no faster: the consumers are
+        // bound by issue slots, not by the MMA chain)
+        constexpr int NH = 1;
         float acc[NH][2][C::T][4];
 #pragma unroll
         for (int h = 0; h < NH; h++)
@@ -581,14 +584,22 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
-          if (tid == 0 && tu == 0 && st - m.st0 < 16) MOEK_TR(64 + 2 * (st - m.st0));
-          if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag) ||
-              !wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
+          const bool stamp = tid == 0 && tu == 0 && st - m.st0 < 8;
+          if (stamp) MOEK_TR_CLK(64 + st - m.st0);
+          if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag)) {
             ok = false;
             continue;  // stay in step with the other roles' counters
           }
-          if (tid == 0 && st == m.st0 && tu < 16) MOEK_TR(8 + 3 * tu);
-          if (tid == 0 && tu == 0 && st - m.st0 < 16) MOEK_TR(65 + 2 * (st - m.st0));
+          if (stamp) MOEK_TR_CLK(72 + st - m.st0);
+          if (!wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
+            ok = false;
+            continue;
+          }
+          if (stamp) MOEK_TR_CLK(80 + st - m.st0);
+          if (tid == 0 && st == m.st0 && tu < 8) {
+            MOEK_TR(8 + 3 * tu);
+            MOEK_TR_VAL(32 + tu, (ph << 28) | (blk << 16) | (item << 8) | ks);
+          }
 #pragma unroll
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
@@ -637,11 +648,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(empty + slot);
-          if (tid == 0 && tu == 0 && st - m.st0 < 16) MOEK_TR(112 + st - m.st0);
+          if (stamp) MOEK_TR_CLK(88 + st - m.st0);
         }
         ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
         if (!ok) continue;
-        if (tid == 0 && tu < 16) MOEK_TR(9 + 3 * tu);
+        if (tid == 0 && tu < 8) MOEK_TR(9 + 3 * tu);
         if constexpr (NH == 2) {
 #pragma unroll
           for (int i = 0; i < 2; i++)
@@ -715,7 +726,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             __syncwarp();
             if (lane == 0) st_release(p.ctr + p.off_ready + ((int64_t)blk * nt1 + item) * NCW + warp, epoch + 1);
           }
-          if (tid == 0 && tu < 16) MOEK_TR(10 + 3 * tu);
+          if (tid == 0 && tu < 8) MOEK_TR(10 + 3 * tu);
           continue;
         }
         // down: weighted fp32 rows of (block, item), then the token sums
@@ -776,7 +787,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             }
           }
         }
-        if (tid == 0 && tu < 16) MOEK_TR(10 + 3 * tu);
+        if (tid == 0 && tu < 8) MOEK_TR(10 + 3 * tu);
         if (!complete || p.out_rows) continue;
         __threadfence();
         __syncwarp();

@@ -18,6 +18,7 @@ import statistics
 import numpy as np
 
 CTAS, SLOTS = 1024, 128
+CLOCK_GHZ = 1.965  # SM clock the cycle stamps are converted at (the B200's maximum, the clock the bench runs at)
 
 LAYER_PHASES = {0: "start", 1: "after dependent-launch wait", 2: "EP flags seen", 3: "routing done",
                 4: "first weight copy issued", 5: "consumers done", 6: "end"}
@@ -51,7 +52,8 @@ def summarize(t: np.ndarray, kind: int) -> dict:
         v = v[v > 0]
         if v.size:
             out["phases"][name] = (round(float(np.median(us(v))), 2), round(float(us(v).max()), 2))
-    for u in range(16):
+    nunit = 8 if kind == 0 else 16
+    for u in range(nunit):
         cols = [t[:, 8 + 3 * u + j] for j in range(3)]
         have = cols[0] > 0
         if not have.any():
@@ -64,18 +66,36 @@ def summarize(t: np.ndarray, kind: int) -> dict:
                              "end": row[2]})
     if kind == 0:
         out["units_per_cta"] = (int(np.median(t[:, 7])), int(t[:, 7].max()))
-        stages = []  # the first unit's stages (consumer warp 0): data wait, compute, and when the scale warp got them
-        for s in range(16):
-            w0, w1, sc, end = t[:, 64 + 2 * s], t[:, 65 + 2 * s], t[:, 96 + s], t[:, 112 + s]
-            ok = (w0 > 0) & (w1 > 0) & (end > 0)
+        stages = []  # the first unit's stages, SM cycles relative to consumer warp 0's wait for stage 0
+        base = t[:, 64]
+        for s_ in range(8):
+            cols = {k: t[:, off + s_] for k, off in (("begin", 64), ("weights", 72), ("scales", 80), ("done", 88),
+                                                    ("scale_warp_in", 96), ("scale_warp_out", 104),
+                                                    ("producer_issue", 112), ("act_issue", 120))}
+            ok = (cols["begin"] > 0) & (cols["done"] > 0) & (base > 0)
             if not ok.any():
                 break
-            med = lambda v: round(float(np.median(v)) / 1e3, 2)
-            sok = ok & (sc > 0)
-            stages.append({"stage": s, "ctas": int(ok.sum()), "ready_at": med(w1[ok] - t0),
-                           "wait": med(w1[ok] - w0[ok]), "compute": med(end[ok] - w1[ok]),
-                           "scale_lead": med(w1[sok] - sc[sok]) if sok.any() else None})
+            med = lambda v: round(float(np.median(v)) / CLOCK_GHZ / 1e3, 2)
+            row = {"stage": s_, "ctas": int(ok.sum())}
+            for k_, v in cols.items():
+                okk = ok & (v > 0)
+                row[k_] = med(v[okk] - base[okk]) if okk.any() else None
+            stages.append(row)
         out["unit0_stages"] = stages
+        ends = t[:, 6]
+        order = np.argsort(-ends)[:4]
+        slow = []
+        for ci in order:
+            units = []
+            for u in range(8):
+                if t[ci, 8 + 3 * u] == 0:
+                    break
+                v = int(t[ci, 32 + u])
+                units.append({"unit": f"{'gd'[v >> 28]}/{(v >> 16) & 0xFFF}/{(v >> 8) & 0xFF}/{v & 0xFF}",
+                              "ready": float(us(t[ci, 8 + 3 * u])), "end": float(us(t[ci, 10 + 3 * u]))
+                              if t[ci, 10 + 3 * u] else float("nan")})
+            slow.append({"cta": int(np.nonzero(live)[0][ci]), "end": float(us(ends[ci])), "units": units})
+        out["slowest"] = slow
         waits = []
         for j in range(4):
             a, b = t[:, 56 + 2 * j], t[:, 57 + 2 * j]
@@ -134,9 +154,20 @@ def main():
             f = lambda v: f"{v[0]:7.2f}/{v[1]:7.2f}" if v else "      -"
             print(f"  unit {u['unit']:2d} ({u['ctas']:4d} CTAs): first ready {f(u['first_ready'])}  last stage "
                   f"{f(u['last_stage'])}  end {f(u['end'])}  (median/max us)")
-        for s in r.get("unit0_stages", []):
-            print(f"  unit 0 stage {s['stage']:2d}: ready at {s['ready_at']:7.2f} us (waited {s['wait']:5.2f}), compute "
-                  f"{s['compute']:5.2f} us, scale warp had the data {s['scale_lead']} us before (median over CTAs)")
+        if r.get("unit0_stages"):
+            keys = ["begin", "weights", "scales", "done", "scale_warp_in", "scale_warp_out", "producer_issue",
+                    "act_issue"]
+            print("  first unit, per stage (us after consumer warp 0 began waiting for stage 0; median over CTAs):")
+            print("    stage " + " ".join(f"{k:>14s}" for k in keys))
+            for s_ in r["unit0_stages"]:
+                print(f"    {s_['stage']:5d} " + " ".join(f"{(s_[k] if s_[k] is not None else float('nan')):14.2f}"
+                                                      for k in keys))
+        slow = r.get("slowest")
+        if slow:
+            print("  slowest CTAs (end us; units as phase/block/item/split: first ready, end):")
+            for cta in slow:
+                print(f"    CTA {cta['cta']:3d} end {cta['end']:7.2f}: " + "; ".join(
+                    f"{u['unit']} {u['ready']:.1f}-{u['end']:.1f}" for u in cta["units"]))
         if "act_wait_us" in r:
             print(f"  act waits: median {r['act_wait_us'][0]} us, max {r['act_wait_us'][1]} us ({r['act_wait_us'][2]})")
 
