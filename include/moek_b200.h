@@ -53,7 +53,8 @@ int moek_build_flags(void);
  * first four act waits, start and end; the first unit's stages s < 8 in SM clock cycles (clock64): 64 + s consumer
  * warp 0 before its waits, 72 + s weights landed, 80 + s scales ready, 88 + s done, 96 + s the scale warp sees the
  * weights, 104 + s it publishes the scales, 112 + s the producer issues the copy, 120 + s the act warp issues its
- * copies); kind 1: the tcgen05 GEMM (0 start,
+ * copies; 39-45 the routing steps in SM clock cycles: start, keys built, counted, ranked, blocks cut, plans made,
+ * published); kind 1: the tcgen05 GEMM (0 start,
  * 1 after the wait, 6 end; per unit: 8 + 3u first MMA, 9 + 3u last MMA issued, 10 + 3u accumulator drained);
  * kind 2: the peer-exchange kernels (dispatch: 0 start, 1 destination free, 2 rows written, 3 flag raised; unpack:
  * 8 start, 9 partials ready, 10 done). Other builds return MOEK_ERR_UNSUPPORTED. moek_trace_clear zeroes them. */

@@ -23,8 +23,9 @@
 //             of the block, once the gate_up item that produced those act columns is complete in every CTA (one
 //             ready stamp per (block, item, consumer warp), acquire-loaded by eight lanes at once with a bounded
 //             wait), by plain loads into the slot.
-//   scales    warp 10: per stage the scale byte of each row x k-group (base + 4-bit offset, then the exceptions),
-//             per unit the (B | R) table of the expert (moek_common.cuh), as in moek_decode.cu.
+//   scales    warp 10: per stage the scale byte of each k-group x run position (base + 4-bit offset, then the
+//             exceptions), in the packed run's own position order; per unit the {B B, R R} table of the expert
+//             (moek_common.cuh).
 //   consumers warps 0-7: the swap-AB mma.sync m16n8k16 of moek_decode.cu (weights = the 16-row A operand, up to 8
 //             tokens = B), fp32 accumulators per unit.
 //   finishing gate_up: with one k-split the lane holds gate and up of the same column and writes
@@ -146,11 +147,6 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
-}
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
 
 // Bounded wait of a whole warp until the NCW ready stamps of a (block, item) all read `want`: lane L polls stamp
@@ -246,6 +242,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   pdl_wait();  // x, routing and weights of the previous kernels; the workspace of the previous launch
   pdl_launch_dependents();
   if (tid == 0) MOEK_TR(1);
+  if (tid == 0) MOEK_TR_CLK(39);
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int n = p.num_ids, k = p.top_k;
   // the routing loads first (each thread's at most two ids: n <= 512 < 2 x THREADS); expert-parallel receive buffers
@@ -283,7 +280,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       kk[h] = v ? ((uint32_t)e_in[h] << 9) | (uint32_t)i : 0xFFFFFFFFu;
       if (i < n4) key[i] = kk[h];
     }
+    if (tid == 0) MOEK_TR_CLK(40);
     const int nvalid = __syncthreads_count(kk[0] != 0xFFFFFFFFu) + __syncthreads_count(kk[1] != 0xFFFFFFFFu);
+    if (tid == 0) MOEK_TR_CLK(41);
 #pragma unroll
     for (int h = 0; h < 2; h++) {  // rank of each valid key among all keys (they are distinct): 4 keys per load
       if (kk[h] == 0xFFFFFFFFu) continue;
@@ -294,6 +293,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       }
       skey[r] = kk[h];
     }
+    if (tid == 0) MOEK_TR_CLK(42);
     if (p.ep_peer) {  // rows with at least one valid slot: the rows this rank returns (p.M * k <= 512)
       int rows = 0;
 #pragma unroll
@@ -331,12 +331,14 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         run0 = __shfl_sync(0xffffffffu, rs, 31);
       }
       if (lane == 0) {
+        MOEK_TR_CLK(43);
         bstart[base] = nvalid;
         misc[0] = base;
         const int nb = *abort_flag ? 0 : base;  // the plans, once per CTA (every thread reads them after the barrier)
         PhasePlan* pl = reinterpret_cast<PhasePlan*>(smem + C::PLAN_OFF);
         pl[0] = plan_phase(p.m[0], nb, gridDim.x, p.tail);
         pl[1] = plan_phase(p.m[1], nb, gridDim.x, p.tail);
+        MOEK_TR_CLK(44);
       }
     }
     __syncthreads();
@@ -344,6 +346,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   const int nblk = *abort_flag ? 0 : misc[0];
   const int ep_rows = misc[3];
   if (tid == 0) MOEK_TR(3);
+  if (tid == 0) MOEK_TR_CLK(45);
   if (p.ep_peer && ep_rows == 0 && !*abort_flag && blockIdx.x == 0 && tid == 0)
     ep_signal(p, ep_call);  // nothing to return: release the senders' waits at once
 
@@ -452,13 +455,12 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   } else if (warp == W_SCALE) {  // -------------------------------------------------------------------- scale warp
     // Per unit: the expert's global scale and the unit's exception offsets (lane j: run j's first entry) and entries
     // (up to 64 held in registers, two per lane), loaded by all lanes at once and one unit ahead, so that no stage
-    // waits on a chain of global loads. Per stage: the slot's scale table, one 8-byte row per weight row (byte kg =
-    // k-group kg), then the run's exceptions. Lane L decodes chunk L % 16 (8 positions) of run L / 16 of the pair.
+    // waits on a chain of global loads. Per stage: the slot's scale table in run-position order, one byte per
+    // (k-group, run, position) at kg * 256 + run * 128 + position (the consumers map their rows to positions), then
+    // the run's exceptions. Lane L decodes chunk L % 16 (8 positions) of run L / 16 of the pair: eight 8-byte stores,
+    // no byte shuffling, so that the single scale warp keeps ahead of the consumers.
     uint32_t g = 0, kq = 0;
     const int run = lane >> 4, ch = lane & 15;
-    int dst[8];  // the rows (item slots) of the lane's 8 positions
-#pragma unroll
-    for (int i = 0; i < 8; i++) dst[i] = run * 128 + position_slot(8 * ch + i);
     bool ok = true;
     for (int r = 0; r < rounds && ok; r++) {
       const int nu = min(MAXU, n_mine - r * MAXU);
@@ -506,21 +508,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           const uint8_t* runp = smem + slot * C::SLOT + LSTAGE + run * RUN_BYTES;
           uint8_t* tb = smem + slot * C::SLOT + C::SC_OFF;
           const uint32_t b4 = runp[ch] * 0x01010101u;
-          uint32_t lo[KG], hi[KG];  // k-group kk's bytes of positions 8 ch + 0..3 and + 4..7
 #pragma unroll
-          for (int kk = 0; kk < KG; kk++) {
+          for (int kk = 0; kk < KG; kk++) {  // k-group kk's bytes of positions 8 ch + 0..3 (low nibbles), + 4..7
             const uint32_t q = *reinterpret_cast<const uint32_t*>(runp + 16 + kk * 64 + ch * 4);
-            lo[kk] = (q & 0x0F0F0F0Fu) + b4;
-            hi[kk] = ((q >> 4) & 0x0F0F0F0Fu) + b4;
-          }
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const uint32_t* src = i < 4 ? lo : hi;
-            const uint32_t bi = i & 3, sel = bi | ((bi + 4) << 4);
-            uint2 row;
-            row.x = prmt2(prmt2(src[0], src[1], sel), prmt2(src[2], src[3], sel), 0x5410);
-            row.y = prmt2(prmt2(src[4], src[5], sel), prmt2(src[6], src[7], sel), 0x5410);
-            *reinterpret_cast<uint2*>(tb + dst[i] * 8) = row;
+            *reinterpret_cast<uint2*>(tb + kk * 256 + run * 128 + 8 * ch) =
+                make_uint2((q & 0x0F0F0F0Fu) + b4, ((q >> 4) & 0x0F0F0F0Fu) + b4);
           }
           __syncwarp();
           // this stage's run: entries [eo0, eo1) of the unit's list overwrite their bytes
@@ -530,8 +522,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           auto patch = [&](uint32_t en) {
             const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
             if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r1g), p.err)) return;
-            const int row = ((ppos >> 7) == r0g ? 0 : 128) + position_slot(ppos & 127);
-            tb[row * 8 + kg] = (uint8_t)(en >> 24);
+            tb[kg * 256 + ((ppos >> 7) == r0g ? 0 : 128) + (ppos & 127)] = (uint8_t)(en >> 24);
           };
           if (lane >= eo0 && lane < eo1) patch(ex0);
           if (lane + 32 >= eo0 && lane + 32 < eo1) patch(ex1);
@@ -563,6 +554,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
         const int G0 = ph == 0 ? warp : 2 * warp, G1 = ph == 0 ? warp + 8 : 2 * warp + 1;
         const int slot00 = 16 * G0 + gq, slot10 = 16 * G1 + gq;
+        // the scale-table offsets (run * 128 + position) of the lane's four rows
+        auto tpos = [](int r) { return (r & 128) + slot_position(r & 127); };
+        const int p00 = tpos(slot00), p01 = tpos(slot00 + 8), p10 = tpos(slot10), p11 = tpos(slot10 + 8);
         const uint2* lt = lut + (kq % NLUT) * 256;
         kq++;
         const int ntile = (nv + 7) >> 3;
@@ -604,9 +598,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
           const uint8_t* sx = smem + slot * C::SLOT + C::X_OFF + hf * BK * 2;
-          const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + 4 * hf + c;  // byte (k-group) of each row
-          const uint2 s0a = lt[sc[slot00 * 8]], s0b = lt[sc[(slot00 + 8) * 8]], s1a = lt[sc[slot10 * 8]],
-                      s1b = lt[sc[(slot10 + 8) * 8]];
+          const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + (4 * hf + c) * 256;  // k-group 4 hf + c
+          const uint2 s0a = lt[sc[p00]], s0b = lt[sc[p01]], s1a = lt[sc[p10]], s1b = lt[sc[p11]];
           // the tiles' activation fragments of this half, shared by both row groups (loaded once here for one-tile
           // blocks; larger blocks load them next to their MMAs, to keep registers free)
           uint4 xf[C::T][2];

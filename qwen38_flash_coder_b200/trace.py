@@ -82,6 +82,14 @@ def summarize(t: np.ndarray, kind: int) -> dict:
                 row[k_] = med(v[okk] - base[okk]) if okk.any() else None
             stages.append(row)
         out["unit0_stages"] = stages
+        # routing, SM cycles from the dependent-launch wait: keys built, counted, ranked, blocks cut, plans, published
+        r0 = t[:, 39]
+        rt = {}
+        for name, sl in (("keys", 40), ("counted", 41), ("ranked", 42), ("blocks", 43), ("plans", 44), ("published", 45)):
+            ok = (r0 > 0) & (t[:, sl] > 0)
+            if ok.any():
+                rt[name] = round(float(np.median(t[ok, sl] - r0[ok])) / CLOCK_GHZ / 1e3, 2)
+        out["routing_us"] = rt
         ends = t[:, 6]
         order = np.argsort(-ends)[:4]
         slow = []
@@ -162,6 +170,9 @@ def main():
             for s_ in r["unit0_stages"]:
                 print(f"    {s_['stage']:5d} " + " ".join(f"{(s_[k] if s_[k] is not None else float('nan')):14.2f}"
                                                       for k in keys))
+        if r.get("routing_us"):
+            print("  routing (us after the dependent-launch wait, median): " +
+                  ", ".join(f"{k} {v}" for k, v in r["routing_us"].items()))
         slow = r.get("slowest")
         if slow:
             print("  slowest CTAs (end us; units as phase/block/item/split: first ready, end):")
