@@ -51,7 +51,7 @@ int moek_build_flags(void);
  * copy issued, 5 consumers done, 6 end, 7 unit count; per unit u < 8 of the CTA: 8 + 3u first stage ready, 9 + 3u
  * last stage done, 10 + 3u finished, 32 + u the unit (phase << 28 | block << 16 | item << 8 | k-split); 56-63: the
  * first four act waits, start and end; the first unit's stages s < 8 in SM clock cycles (clock64): 64 + s consumer
- * warp 0 before its waits, 72 + s weights landed, 80 + s scales ready, 88 + s done, 96 + s the scale warp sees the
+ * warp 0 before its wait, 80 + s data and scales ready, 88 + s done, 96 + s the scale warp sees the
  * weights, 104 + s it publishes the scales, 112 + s the producer issues the copy, 120 + s the act warp issues its
  * copies; 39-45 the routing steps in SM clock cycles: start, keys built, counted, ranked, blocks cut, plans made,
  * published); kind 1: the tcgen05 GEMM (0 start,

@@ -27,7 +27,8 @@
 //             exceptions), in the packed run's own position order; per unit the {B B, R R} table of the expert
 //             (moek_common.cuh).
 //   consumers warps 0-7: the swap-AB mma.sync m16n8k16 of moek_decode.cu (weights = the 16-row A operand, up to 8
-//             tokens = B), fp32 accumulators per unit.
+//             tokens = B), fp32 accumulators per unit; they wait on the scale warp's barrier only (it has waited for
+//             the slot's copies itself).
 //   finishing gate_up: with one k-split the lane holds gate and up of the same column and writes
 //             act = bf16(silu(gate) * up); with more, fp32 partials go to the workspace and the warp whose arrival
 //             completes (block, item, warp) adds them in split order, then releases that warp's ready stamp.
@@ -78,6 +79,18 @@ struct UnitMeta {
 // items use the finest whole-stage split that still fits them in one more wave, so the phase ends about one short
 // unit after the last full wave instead of one full unit (the idea of stream-K, with no fix-up beyond the split-k
 // arrivals the kernel has anyway).
+// v / d for 0 <= v < 2^22 and 1 <= d < 2^10, without the long dependent chain of an integer division: a quotient
+// estimate from the approximate fp32 reciprocal (relative error about 2^-23, so the estimate is off by at most one)
+// and one correction each way. The unit plan and the unit decode divide by runtime values on the start-up path.
+__device__ __forceinline__ int div_small(int v, int d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"((float)d));
+  int q = __float2int_rz((float)v * r);
+  const int rem = v - q * d;
+  q += (rem >= d) - (rem < 0);
+  return q;
+}
+
 struct PhasePlan {
   int ni_main, s_main, s_tail, u_main, u_total;  // at most 512 blocks x 16 items x 32 splits: 32-bit
 };
@@ -88,7 +101,7 @@ __device__ __forceinline__ PhasePlan plan_phase(const LayerMat& m, int nblk, int
   q.ni_main = ni;
   const int main_units = ni * m.nsplit;
   if (tail && main_units > grid) {
-    const int nim = main_units / grid * grid / m.nsplit;
+    const int nim = div_small(div_small(main_units, grid) * grid, m.nsplit);
     const int rem = ni - nim;
     int st = m.nsplit;  // the finest whole-stage split (a divisor of nstage, precomputed) that fits the grid
     for (uint64_t dm = m.divmask >> (m.nsplit + 1) << (m.nsplit + 1); dm; dm &= dm - 1) {
@@ -187,19 +200,19 @@ __device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePla
   const int v = um.ph ? u - q0.u_total : u;
   int ii;
   if (v < q.u_main) {
-    ii = v / q.s_main;
+    ii = div_small(v, q.s_main);
     um.ks = v - ii * q.s_main;
     um.ns = q.s_main;
   } else {
     const int w = v - q.u_main;
-    const int t = w / q.s_tail;
+    const int t = div_small(w, q.s_tail);
     ii = q.ni_main + t;
     um.ks = w - t * q.s_tail;
     um.ns = q.s_tail;
   }
-  um.blk = ii / m.nt;
+  um.blk = div_small(ii, m.nt);
   um.item = ii - um.blk * m.nt;
-  const int su = m.nstage / um.ns;
+  const int su = div_small(m.nstage, um.ns);
   um.st0 = um.ks * su;
   um.st1 = um.st0 + su;
 }
@@ -334,11 +347,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         MOEK_TR_CLK(43);
         bstart[base] = nvalid;
         misc[0] = base;
-        const int nb = *abort_flag ? 0 : base;  // the plans, once per CTA (every thread reads them after the barrier)
-        PhasePlan* pl = reinterpret_cast<PhasePlan*>(smem + C::PLAN_OFF);
-        pl[0] = plan_phase(p.m[0], nb, gridDim.x, p.tail);
-        pl[1] = plan_phase(p.m[1], nb, gridDim.x, p.tail);
-        MOEK_TR_CLK(44);
+      }
+      if (lane < 2) {  // the two phases' plans, once per CTA, one lane each (every thread reads them after the barrier)
+        const int nb = *abort_flag ? 0 : base;
+        reinterpret_cast<PhasePlan*>(smem + C::PLAN_OFF)[lane] = plan_phase(p.m[lane], nb, gridDim.x, p.tail);
+        if (lane == 0) MOEK_TR_CLK(44);
       }
     }
     __syncthreads();
@@ -580,14 +593,12 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           const uint32_t par = (g / C::NS) & 1;
           const bool stamp = tid == 0 && tu == 0 && st - m.st0 < 8;
           if (stamp) MOEK_TR_CLK(64 + st - m.st0);
-          if (!wait_or_abort(full + slot, par, deadline, p.err, abort_flag)) {
-            ok = false;
-            continue;  // stay in step with the other roles' counters
-          }
-          if (stamp) MOEK_TR_CLK(72 + st - m.st0);
+          // one wait: the scale warp arrives on `scaled` only after its own wait on `full` (weights, scales and
+          // activations of the slot landed), so the consumers' acquire of `scaled` orders their reads after those
+          // writes as well
           if (!wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
             ok = false;
-            continue;
+            continue;  // stay in step with the other roles' counters
           }
           if (stamp) MOEK_TR_CLK(80 + st - m.st0);
           if (tid == 0 && st == m.st0 && tu < 8) {

@@ -69,7 +69,7 @@ def summarize(t: np.ndarray, kind: int) -> dict:
         stages = []  # the first unit's stages, SM cycles relative to consumer warp 0's wait for stage 0
         base = t[:, 64]
         for s_ in range(8):
-            cols = {k: t[:, off + s_] for k, off in (("begin", 64), ("weights", 72), ("scales", 80), ("done", 88),
+            cols = {k: t[:, off + s_] for k, off in (("begin", 64), ("scales", 80), ("done", 88),
                                                     ("scale_warp_in", 96), ("scale_warp_out", 104),
                                                     ("producer_issue", 112), ("act_issue", 120))}
             ok = (cols["begin"] > 0) & (cols["done"] > 0) & (base > 0)
@@ -163,7 +163,7 @@ def main():
             print(f"  unit {u['unit']:2d} ({u['ctas']:4d} CTAs): first ready {f(u['first_ready'])}  last stage "
                   f"{f(u['last_stage'])}  end {f(u['end'])}  (median/max us)")
         if r.get("unit0_stages"):
-            keys = ["begin", "weights", "scales", "done", "scale_warp_in", "scale_warp_out", "producer_issue",
+            keys = ["begin", "scales", "done", "scale_warp_in", "scale_warp_out", "producer_issue",
                     "act_issue"]
             print("  first unit, per stage (us after consumer warp 0 began waiting for stage 0; median over CTAs):")
             print("    stage " + " ".join(f"{k:>14s}" for k in keys))

@@ -148,3 +148,18 @@ def test_device_pair_decode_matches_code_bits():
         q = sum(((c >> b) & 1) << pos for c, bits in zip(codes, prep.CODE_BITS) for b, pos in enumerate(bits))
         for p, d in enumerate(pairs(q)):
             assert d == place(codes[2 * p]) | place(codes[2 * p + 1]) << 16
+
+
+def test_device_small_division_restated():
+    """The layer kernel's div_small (fp32 reciprocal estimate of v / d, one correction each way) restated with an
+    fp32 reciprocal of the same accuracy as the hardware's approximate one (relative error 2^-23): exact for every
+    v < 2^22 and d < 2^10 that the unit plan and unit decode use (sampled, plus the extremes)."""
+    rng = np.random.default_rng(3)
+    v = np.concatenate([rng.integers(0, 1 << 22, 200000), np.arange(0, 5000), [(1 << 22) - 1] * 10])
+    d = np.concatenate([rng.integers(1, 1 << 10, 200000), rng.integers(1, 65, 5000), np.arange(1, 11)])
+    for err in (-2.0 ** -23, 0.0, 2.0 ** -23):  # the reciprocal's worst relative errors either way
+        r = (np.float32(1.0) / d.astype(np.float32)) * np.float32(1.0 + err)
+        q = np.trunc(v.astype(np.float32) * r.astype(np.float32)).astype(np.int64)
+        rem = v - q * d
+        q += (rem >= d).astype(np.int64) - (rem < 0).astype(np.int64)
+        assert np.array_equal(q, v // d)
