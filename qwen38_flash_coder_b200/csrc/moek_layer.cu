@@ -147,6 +147,7 @@ __device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t 
 }
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err,
                                               volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;  // the common case: the phase is complete, no shared-memory load first
   if (*abort_flag) return false;
   if (mbar_wait(bar, parity, deadline, err)) return true;
   *abort_flag = 1;
@@ -588,6 +589,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               for (int v = 0; v < 4; v++) acc[h][i][t][v] = 0.f;
         bool ok = true;
         const int tu = r * MAXU + ui;  // the unit's index among this CTA's (timeline stamps)
+        bool ready = false;  // the next stage's scales were seen published while this stage was computed
         for (int st = m.st0; st < m.st1; st++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
@@ -595,11 +597,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           if (stamp) MOEK_TR_CLK(64 + st - m.st0);
           // one wait: the scale warp arrives on `scaled` only after its own wait on `full` (weights, scales and
           // activations of the slot landed), so the consumers' acquire of `scaled` orders their reads after those
-          // writes as well
-          if (!wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
+          // writes as well. Usually the test made during the previous stage already saw the phase complete, and the
+          // stage starts without a wait on its critical path.
+          if (!ready && !wait_or_abort(scaled + slot, par, deadline, p.err, abort_flag)) {
             ok = false;
             continue;  // stay in step with the other roles' counters
           }
+          ready = false;
           if (stamp) MOEK_TR_CLK(80 + st - m.st0);
           if (tid == 0 && st == m.st0 && tu < 8) {
             MOEK_TR(8 + 3 * tu);
@@ -607,6 +611,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           }
 #pragma unroll
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
+          if (hf == 1 && st + 1 < m.st1)  // test the next stage's scales (its latency hides behind this half's math)
+            ready = mbar_test(scaled + (g + 1) % C::NS, ((g + 1) / C::NS) & 1);
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
           const uint8_t* sx = smem + slot * C::SLOT + C::X_OFF + hf * BK * 2;
           const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + (4 * hf + c) * 256;  // k-group 4 hf + c
