@@ -147,12 +147,25 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is incomplete (it wakes when the phase
+// completes), so that a waiting warp does not spin on issue slots the working warps need.
+__device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with the given parity. Returns false (after reporting) once the deadline passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err) {
   if (mbar_try(bar, parity)) return true;
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 255) == 0 && globaltimer() > deadline) {
+  for (;;) {
+    if (mbar_try_suspend(bar, parity, 20000)) return true;
+    if (globaltimer() > deadline) {
       report(err, MOEK_DEV_TIMEOUT);
       return false;
     }
@@ -176,6 +189,7 @@ __device__ __forceinline__ bool wait_flag(const int* p, int want, uint64_t deadl
       report(err, MOEK_DEV_TIMEOUT);
       return false;
     }
+    __nanosleep(64);
   }
 }
 
@@ -221,6 +235,21 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
+}
+// Pair d (codes 2d, 2d + 1) of a tiled word as bf16x2 of e2m1 * 2^-126 (fp4_pairs, one pair).
+template <int D>
+__device__ __forceinline__ uint32_t fp4_pair(uint32_t q) {
+  constexpr uint32_t P = 0x81C081C0u;
+  if constexpr (D == 0) return q & P;
+  if constexpr (D == 1) return __funnelshift_r(q, q, 4) & P;
+  if constexpr (D == 2) return __funnelshift_r(q, q, 10) & P;
+  return (__funnelshift_r(q, q, 14) & 0x00400040u) | (__funnelshift_r(q, q, 6) & 0x81808180u);
+}
+// The oracle's bf16 weights of pair D of a word (dequant_word, one pair).
+template <int D>
+__device__ __forceinline__ uint32_t dequant_pair(uint32_t q, const ScaleBR& s) {
+  const uint32_t d = fp4_pair<D>(q);
+  return bf2_fma(d, s.b2, bf2_mul(d, s.r2));
 }
 // The oracle's bf16 weights for the 8 codes of one word: out[d] = bf16x2 of codes 2d, 2d + 1.
 __device__ __forceinline__ void dequant_word(uint32_t q, const ScaleBR& s, uint32_t* out) {

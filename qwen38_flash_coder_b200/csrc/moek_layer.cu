@@ -51,6 +51,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
@@ -165,7 +166,8 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 
 // Bounded wait of a whole warp until the NCW ready stamps of a (block, item) all read `want`: lane L polls stamp
 // L % NCW (acquire loads, all eight in parallel), then a warp barrier orders every lane's later loads after all the
-// acquires (the consumer warps released their stamps after writing their act columns).
+// acquires (the consumer warps released their stamps after writing their act columns). Between polls the warp sleeps
+// briefly, leaving the issue slots to the consumers.
 __device__ __forceinline__ bool wait_stamps(const int* stamps, int want, uint64_t deadline, int* err,
                                             volatile int* abort_flag) {
   const int* st = stamps + (threadIdx.x & 31) % NCW;
@@ -182,6 +184,7 @@ __device__ __forceinline__ bool wait_stamps(const int* stamps, int want, uint64_
       *abort_flag = 1;
       return false;
     }
+    __nanosleep(32);
   }
 }
 
@@ -631,29 +634,34 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             const ScaleBR sa{wa.x, wa.y}, sbv{wb.x, wb.y};
             const uint8_t* wr = sw + (16 * (i ? G1 : G0) + gq) * 32 + w_off;
             const uint2 qa = *reinterpret_cast<const uint2*>(wr), qb = *reinterpret_cast<const uint2*>(wr + 8 * 32);
-            uint32_t wa0[4], wb0[4], wa1[4], wb1[4];
-            dequant_word(qa.x, sa, wa0);
-            dequant_word(qb.x, sbv, wb0);
-            dequant_word(qa.y, sa, wa1);
-            dequant_word(qb.y, sbv, wb1);
-            const uint32_t A0[4] = {wa0[0], wb0[0], wa0[1], wb0[1]};
-            const uint32_t A1[4] = {wa0[2], wb0[2], wa0[3], wb0[3]};
-            const uint32_t A2[4] = {wa1[0], wb1[0], wa1[1], wb1[1]};
-            const uint32_t A3[4] = {wa1[2], wb1[2], wa1[3], wb1[3]};
+            if constexpr (C::T > 1) {
 #pragma unroll
-            for (int t = 0; t < C::T; t++) {
-              if (t < ntile) {
-                if constexpr (C::T > 1) {
+              for (int t = 0; t < C::T; t++) {
+                if (t < ntile) {
                   const uint8_t* xr = sx + (t * 8 + gq) * X_STRIDE + c * 32;
                   xf[t][0] = *reinterpret_cast<const uint4*>(xr);
                   xf[t][1] = *reinterpret_cast<const uint4*>(xr + 16);
                 }
-                mma_16816(acc[hf % NH][i][t], A0, xf[t][0].x, xf[t][0].y);
-                mma_16816(acc[hf % NH][i][t], A1, xf[t][0].z, xf[t][0].w);
-                mma_16816(acc[hf % NH][i][t], A2, xf[t][1].x, xf[t][1].y);
-                mma_16816(acc[hf % NH][i][t], A3, xf[t][1].z, xf[t][1].w);
               }
             }
+            // four MMAs: MMA j takes pairs 2(j & 1) and 2(j & 1) + 1 of rows g and g + 8 from the first (j < 2) or
+            // second word of the k-group; each A fragment is dequantised straight into its operand registers
+            auto mma_j = [&](auto jc, uint32_t wa, uint32_t wb) {
+              constexpr int J = decltype(jc)::value, P0 = 2 * (J & 1), P1 = P0 + 1;
+              const uint32_t A[4] = {dequant_pair<P0>(wa, sa), dequant_pair<P0>(wb, sbv), dequant_pair<P1>(wa, sa),
+                                     dequant_pair<P1>(wb, sbv)};
+#pragma unroll
+              for (int t = 0; t < C::T; t++) {
+                if (t < ntile) {
+                  const uint4& xv = xf[t][J >> 1];
+                  mma_16816(acc[hf % NH][i][t], A, (J & 1) ? xv.z : xv.x, (J & 1) ? xv.w : xv.y);
+                }
+              }
+            };
+            mma_j(std::integral_constant<int, 0>{}, qa.x, qb.x);
+            mma_j(std::integral_constant<int, 1>{}, qa.x, qb.x);
+            mma_j(std::integral_constant<int, 2>{}, qa.y, qb.y);
+            mma_j(std::integral_constant<int, 3>{}, qa.y, qb.y);
           }
           }
           __syncwarp();
