@@ -147,24 +147,24 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// try_wait that may suspend the thread for up to `hint_ns` while the phase is incomplete (it wakes when the phase
-// completes), so that a waiting warp does not spin on issue slots the working warps need.
-__device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n.reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-      "selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
 // Bounded wait for the phase with the given parity. Returns false (after reporting) once the deadline passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err) {
   if (mbar_try(bar, parity)) return true;
-  for (;;) {
-    if (mbar_try_suspend(bar, parity, 20000)) return true;
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0 && globaltimer() > deadline) {
+      report(err, MOEK_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+// The same wait with a sleep between tests (growing to about 0.25 us), for warps whose wake-up latency is hidden
+// (they run ahead of the warps they feed): waiting warps then leave the issue slots to the working ones.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err) {
+  if (mbar_try(bar, parity)) return true;
+  for (uint32_t ns = 32;; ns = ns < 256 ? 2 * ns : ns) {
+    __nanosleep(ns);
+    if (mbar_try(bar, parity)) return true;
     if (globaltimer() > deadline) {
       report(err, MOEK_DEV_TIMEOUT);
       return false;

@@ -150,7 +150,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, ui
                                               volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;  // the common case: the phase is complete, no shared-memory load first
   if (*abort_flag) return false;
-  if (mbar_wait(bar, parity, deadline, err)) return true;
+  if (mbar_wait_sleep(bar, parity, deadline, err)) return true;
   *abort_flag = 1;
   return false;
 }
@@ -652,7 +652,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
                                      dequant_pair<P1>(wb, sbv)};
 #pragma unroll
               for (int t = 0; t < C::T; t++) {
-                if (t < ntile) {
+                if (C::T == 1 || t < ntile) {  // a unit has at least one row: one-tile blocks need no test
                   const uint4& xv = xf[t][J >> 1];
                   mma_16816(acc[hf % NH][i][t], A, (J & 1) ? xv.z : xv.x, (J & 1) ? xv.w : xv.y);
                 }
