@@ -209,6 +209,20 @@ int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, co
                    int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state, int64_t state_ints,
                    int32_t* err, void* out, float* out_rows, void* stream);
 
+/* The same layer with the router fused into the kernel: replaces, for decode batches, vLLM's fused_topk (scoring
+ * "softmax", vllm/.../router/fused_topk_router.py:69-108) followed by the layer (moek_router_topk then moek_moe_layer:
+ * one launch instead of two). Every CTA routes the M tokens itself from logits [M, E] (fp32, or bf16 when
+ * logits_bf16 != 0): the same softmax, top_k and renormalisation as moek_router_topk, bit for bit; the ids and
+ * weights also go to topk_ids_out / topk_w_out [M, top_k] when those are not NULL. E <= 512; the other arguments as
+ * moek_moe_layer (out is required; the workspace as moek_layer_workspace_bytes with rows_out = 0). */
+int moek_moe_layer_logits(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const void* logits,
+                          int32_t logits_bf16, int32_t top_k, int32_t renormalize, int32_t* topk_ids_out,
+                          float* topk_w_out, const void* w13, const uint8_t* sp13, const float* g13,
+                          const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2, const uint8_t* sp2,
+                          const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                          int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state,
+                          int64_t state_ints, int32_t* err, void* out, void* stream);
+
 /* ---- Expert parallelism. The reference has none (its hook rejects expert_map, files/mbx_moek.py:248-255); these
  * are the dispatch / combine steps around the same GEMMs when the experts are split contiguously over `world` ranks
  * (rank d owns [d * E/world, (d + 1) * E/world)). The all-to-all transfers are the caller's (NCCL). */

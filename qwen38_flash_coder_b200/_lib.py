@@ -28,6 +28,8 @@ SIGNATURES = {
     "moek_layer_workspace_bytes": (ctypes.c_int, [_I32] * 7 + [ctypes.POINTER(ctypes.c_size_t)]),
     "moek_moe_layer": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _I32] + [_P] * 10 + [_I32, _I32, _P,
                                      ctypes.c_size_t, _P, _I64, _P, _P, _P, _P]),
+    "moek_moe_layer_logits": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _I32, _I32, _P, _P] + [_P] * 10 +
+                              [_I32, _I32, _P, ctypes.c_size_t, _P, _I64, _P, _P, _P]),
     "moek_ep_plan": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "moek_ep_pack": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64,
                                     _P]),

@@ -342,7 +342,8 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
                         const uint8_t* sp13, const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13,
                         const void* w2, const uint8_t* sp2, const float* g2, const int32_t* exc_off2,
                         const int32_t* exc_ent2, int32_t nsplit_gate, int32_t nsplit_down, void* workspace,
-                        size_t workspace_bytes, int32_t* state, int64_t state_ints, int32_t* err, bool rows_ws) {
+                        size_t workspace_bytes, int32_t* state, int64_t state_ints, int32_t* err, bool rows_ws,
+                        bool from_logits = false) {
   if (M < 0 || top_k <= 0 || top_k > 32 || E <= 0 || H <= 0 || I <= 0)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer bad sizes (M %d, top_k %d, E %d, H %d, I %d)", M, top_k, E, H, I);
   const int64_t num_ids = (int64_t)M * top_k;
@@ -356,7 +357,8 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   if (nsplit_gate < 1 || nst1 % nsplit_gate || nsplit_down < 1 || nst2 % nsplit_down)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer k-splits (%d, %d) must cut H/128 = %d and I/128 = %d into whole "
                               "runs", nsplit_gate, nsplit_down, H / 128, I / 128);
-  if (!x || !topk_ids || !topk_w || !w13 || !sp13 || !g13 || !exc_off13 || !exc_ent13 || !w2 || !sp2 || !g2 ||
+  if (!x || (!from_logits && (!topk_ids || !topk_w)) || !w13 || !sp13 || !g13 || !exc_off13 || !exc_ent13 || !w2 ||
+      !sp2 || !g2 ||
       !exc_off2 || !exc_ent2 || !state || !err)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer null pointer");
   const LayerLayout lay = layer_layout(E, H, I);
@@ -434,6 +436,34 @@ MOEK_API int moek_moe_layer(const void* x, int32_t M, int32_t H, int32_t I, int3
   p.out_rows = out_rows;
   return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), g_layer_coop, (cudaStream_t)stream),
                      "moe_layer launch");
+}
+
+MOEK_API int moek_moe_layer_logits(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const void* logits,
+                                   int32_t logits_bf16, int32_t top_k, int32_t renormalize, int32_t* topk_ids_out,
+                                   float* topk_w_out, const void* w13, const uint8_t* sp13, const float* g13,
+                                   const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
+                                   const uint8_t* sp2, const float* g2, const int32_t* exc_off2,
+                                   const int32_t* exc_ent2, int32_t nsplit_gate, int32_t nsplit_down, void* workspace,
+                                   size_t workspace_bytes, int32_t* state, int64_t state_ints, int32_t* err, void* out,
+                                   void* stream) {
+  if (M == 0) return MOEK_OK;
+  if (E > 512 || top_k > E)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: the layer's fused router takes E <= 512 and top_k <= E (E %d, top_k "
+                                      "%d); route with moek_router_topk and call moek_moe_layer", E, top_k);
+  if (!logits || !out) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_logits null pointer");
+  moek::LayerParams p;
+  if (int rc = layer_params(p, x, M, H, I, E, nullptr, nullptr, top_k, w13, sp13, g13, exc_off13, exc_ent13, w2, sp2,
+                            g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down, workspace, workspace_bytes, state,
+                            state_ints, err, true, true))
+    return rc;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.logits = logits;
+  p.logits_bf16 = logits_bf16 ? 1 : 0;
+  p.renorm = renormalize ? 1 : 0;
+  p.ids_out = topk_ids_out;
+  p.w_out = topk_w_out;
+  return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), g_layer_coop, (cudaStream_t)stream),
+                     "moe_layer_logits launch");
 }
 
 // ------------------------------------------------------------------------- EP peer-memory exchange (fixed capacity)

@@ -109,6 +109,13 @@ struct LayerParams {
   int64_t ep_back_off, ep_flags_off;  // byte offsets of the back buffer and the flags in an exchange block
   int ep_world, ep_rank, ep_mcap;
   int tail;  // 1: items past the last whole wave of units may use a finer k-split (up to one per stage)
+  // Fused router (logits non-null): every CTA routes the M tokens itself from the router logits [M, E] (fp32, or bf16
+  // when logits_bf16): softmax, top_k, renormalised when renorm; ids and tw are not read, and CTA 0 writes the
+  // routing to ids_out / w_out (when non-null) for the caller.
+  const void* logits;
+  int logits_bf16, renorm;
+  int32_t* ids_out;
+  float* w_out;
 };
 // rows per block: 8/16/32; coop: cooperative launch (every CTA resident together, the default)
 cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, int coop, cudaStream_t st);

@@ -55,6 +55,7 @@
 
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
+#include "moek_route.cuh"
 
 namespace moek {
 namespace dl {
@@ -68,7 +69,7 @@ constexpr int X_STRIDE = LBK * 2 + 16;       // bytes per activation row in a sl
 constexpr int SC_BYTES = ITEM_COLS * KG;     // scale table of a stage: one byte per (weight row, k-group)
 constexpr int NLUT = 4;  // per-unit {B B, R R} tables in flight: a unit's table is written once its first stage has
                          // landed, when the consumers have released every stage of the unit NLUT units before
-constexpr int MAXU = 32;        // units per metadata round
+constexpr int MAXU = 8;         // units per metadata round (a CTA has about U / grid units; more take more rounds)
 
 struct UnitMeta {
   int ph, blk, item, ks, e, nv, flags;  // ph: 0 = gate_up, 1 = down; flags: 2 = block has more rows than XR
@@ -129,7 +130,8 @@ struct Cfg {
   static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
   static constexpr int LUT_OFF = IDS_OFF + MAXU * XR * 4;
   static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 8;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
-  static constexpr int MISC_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;
+  static constexpr int TOK_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;  // the batch's slots: sid[], stw[]
+  static constexpr int MISC_OFF = TOK_OFF + 2 * LAYER_MAXIDS * 4;
   static constexpr int PLAN_OFF = MISC_OFF + 16;  // the two phase plans
   static constexpr int BAR_OFF = (PLAN_OFF + 2 * (int)sizeof(PhasePlan) + 7) / 8 * 8;
   static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
@@ -262,12 +264,40 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   if (tid == 0) MOEK_TR_CLK(39);
   const uint64_t deadline = globaltimer() + p.timeout_ns;
   const int n = p.num_ids, k = p.top_k;
-  // the routing loads first (each thread's at most two ids: n <= 512 < 2 x THREADS); expert-parallel receive buffers
-  // are read only after their flags (below)
+  // the batch's routing in shared memory for the whole kernel (ids and router weights of every slot): loaded first
+  // (each thread's at most two slots: n <= 512 < 2 x THREADS), or computed from the router logits by every CTA (one
+  // warp per token); expert-parallel receive buffers are read only after their flags (below)
+  int* sid = reinterpret_cast<int*>(smem + C::TOK_OFF);
+  float* stw = reinterpret_cast<float*>(sid + LAYER_MAXIDS);
   int e_in[2] = {-1, -1};
-  if (!p.ep_peer) {
-    if (tid < n) e_in[0] = p.ids[tid];
-    if (tid + THREADS < n) e_in[1] = p.ids[tid + THREADS];
+  float w_in[2] = {0.f, 0.f};
+  if (p.logits) {
+    for (int t = warp; t < p.M; t += THREADS / 32) {
+      int es;
+      float ws;
+      if (p.logits_bf16)
+        route_token<16>(static_cast<const __nv_bfloat16*>(p.logits) + (int64_t)t * p.E, p.E, k, p.renorm, es, ws);
+      else
+        route_token<16>(static_cast<const float*>(p.logits) + (int64_t)t * p.E, p.E, k, p.renorm, es, ws);
+      if (lane < k) {
+        sid[t * k + lane] = es;
+        stw[t * k + lane] = ws;
+        if (blockIdx.x == 0 && p.ids_out) p.ids_out[t * k + lane] = es;
+        if (blockIdx.x == 0 && p.w_out) p.w_out[t * k + lane] = ws;
+      }
+    }
+    __syncthreads();
+    if (tid < n) e_in[0] = sid[tid];
+    if (tid + THREADS < n) e_in[1] = sid[tid + THREADS];
+  } else if (!p.ep_peer) {
+    if (tid < n) {
+      e_in[0] = p.ids[tid];
+      w_in[0] = p.tw[tid];
+    }
+    if (tid + THREADS < n) {
+      e_in[1] = p.ids[tid + THREADS];
+      w_in[1] = p.tw[tid + THREADS];
+    }
   }
   const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
   // expert-parallel: this exchange call's number (the flags carry it, so they never need resetting)
@@ -292,7 +322,14 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const int i = tid + h * THREADS;
-      if (p.ep_peer && i < n) e_in[h] = p.ids[i];
+      if (p.ep_peer && i < n) {
+        e_in[h] = p.ids[i];
+        w_in[h] = p.tw[i];
+      }
+      if (i < n && !p.logits) {
+        sid[i] = e_in[h];
+        stw[i] = w_in[h];
+      }
       const bool v = i < n && e_in[h] >= 0 && e_in[h] < p.E;
       kk[h] = v ? ((uint32_t)e_in[h] << 9) | (uint32_t)i : 0xFFFFFFFFu;
       if (i < n4) key[i] = kk[h];
@@ -760,7 +797,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               const int row = t * 8 + 2 * c + v;
               if (row >= nv) continue;
               const int id = ids[row];
-              const float w = p.tw[id];
+              const float w = stw[id];
 #pragma unroll
               for (int h = 0; h < 2; h++) {
                 rows[(int64_t)id * H + 256 * item + slot00 + 8 * h] = w * acc[0][0][t][2 * h + v];
@@ -801,7 +838,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               const float* pr = p.part2 + (int64_t)id * N + col;
               float s = 0.f;
               for (int s2 = 0; s2 < ns; s2++) s += __ldcg(pr + (int64_t)s2 * n * N);
-              rows[(int64_t)id * H + col] = p.tw[id] * s;
+              rows[(int64_t)id * H + col] = stw[id] * s;
             }
           }
         }
@@ -814,7 +851,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         int pieces = 0;  // expert-parallel: (token, item, warp) sums written to the senders' back buffers
         for (int row = 0; row < nv; row++) {
           const int tk = ids[row] / k;
-          const int ej = lane < k ? p.ids[tk * k + lane] : -1;
+          const int ej = lane < k ? sid[tk * k + lane] : -1;
           const int nslots = __popc(__ballot_sync(0xffffffffu, ej >= 0 && ej < p.E));
           int o2 = 0;
           int* tc = p.ctr + p.off_tok + ((int64_t)tk * nt2 + item) * NCW + warp;
@@ -825,7 +862,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           __threadfence();
           float o = 0.f;
           for (int sl = 0; sl < k; sl++) {
-            const int ejs = p.ids[tk * k + sl];
+            const int ejs = sid[tk * k + sl];
             if (ejs < 0 || ejs >= p.E) continue;
             o += __ldcg(rows + (int64_t)(tk * k + sl) * H + col);
           }
@@ -861,7 +898,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   // units, once its own work is done, so that no CTA starts streaming late
   if (blockIdx.x == gridDim.x - 1 && p.out && warp < NCW) {
     for (int t = warp; t < p.M; t += NCW) {
-      const int e = lane < k ? p.ids[t * k + lane] : -1;
+      const int e = lane < k ? sid[t * k + lane] : -1;
       if (__any_sync(0xffffffffu, e >= 0 && e < p.E)) continue;
       for (int c = lane; c < p.H; c += 32) p.out[(int64_t)t * p.H + c] = __float2bfloat16_rn(0.f);
     }

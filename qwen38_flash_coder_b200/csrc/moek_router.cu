@@ -14,22 +14,12 @@
 
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
+#include "moek_route.cuh"
 
 namespace moek {
 
 constexpr int RT_WARPS = 8;
 constexpr int RT_MAXE = 1024;  // experts per row (32 per lane)
-
-template <typename T>
-__device__ __forceinline__ float to_f32(T v);
-template <>
-__device__ __forceinline__ float to_f32<float>(float v) {
-  return v;
-}
-template <>
-__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
-  return __bfloat162float(v);
-}
 
 template <typename T>
 __global__ void __launch_bounds__(RT_WARPS * 32) router_topk_kernel(const T* __restrict__ logits, int M, int E, int k,
@@ -41,63 +31,13 @@ __global__ void __launch_bounds__(RT_WARPS * 32) router_topk_kernel(const T* __r
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * RT_WARPS + (threadIdx.x >> 5);
   if (t >= M) return;
-  const T* row = logits + (int64_t)t * E;
-  // expert e = 32 j + lane in register v[j]
-  constexpr int PER = RT_MAXE / 32;
-  float v[PER];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < PER; j++) {
-    const int e = 32 * j + lane;
-    v[j] = e < E ? to_f32(row[e]) : -INFINITY;
-    mx = fmaxf(mx, v[j]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < PER; j++) {
-    v[j] = 32 * j + lane < E ? expf(v[j] - mx) : 0.f;
-    sum += v[j];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-  for (int j = 0; j < PER; j++) v[j] = 32 * j + lane < E ? v[j] / sum : -1.f;  // taken / absent: -1
-  float wsel = 0.f, wsum = 0.f;
-  int esel = 0;
-  for (int s = 0; s < k; s++) {
-    // the lane's best (largest value, lowest expert on ties: j ascending visits experts in ascending order)
-    float bv = -1.f;
-    int be = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < PER; j++)
-      if (v[j] > bv) {
-        bv = v[j];
-        be = 32 * j + lane;
-      }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    if (lane == s) {  // lane s keeps slot s
-      wsel = bv;
-      esel = be;
-    }
-    wsum += bv;
-#pragma unroll
-    for (int j = 0; j < PER; j++)  // remove the winner (a constant-index select keeps v in registers)
-      if (32 * j + lane == be) v[j] = -1.f;
-  }
+  int esel;
+  float wsel;
+  route_token<RT_MAXE / 32>(logits + (int64_t)t * E, E, k, renorm, esel, wsel);
   if (lane < k) {
     const int64_t o = (int64_t)t * k + lane;
     ids[o] = esel;
-    weights[o] = renorm ? wsel / wsum : wsel;
+    weights[o] = wsel;
     if (tok_idx) tok_idx[o] = lane * M + t;
   }
 }

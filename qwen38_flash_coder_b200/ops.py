@@ -191,11 +191,45 @@ def router_topk(logits: torch.Tensor, top_k: int, renormalize: bool = True, with
 
 
 def fused_moe_from_logits(hidden_states: torch.Tensor, layer: PreparedLayer, router_logits: torch.Tensor,
-                          top_k: int, renormalize: bool = True, output: torch.Tensor = None) -> torch.Tensor:
-    """Router + routed-expert layer: ``fused_moe`` on the router kernel's ids and weights (two launches, the second
-    ordered behind the first by programmatic dependent launch)."""
-    w, ids = router_topk(router_logits, top_k, renormalize)
-    return fused_moe(hidden_states, layer, w, ids, output=output)
+                          top_k: int, renormalize: bool = True, output: torch.Tensor = None,
+                          return_routing: bool = False):
+    """Router + routed-expert layer. Decode batches (the whole-layer kernel's sizes, E <= 512): one launch, the
+    router fused into the layer kernel's routing (moek_moe_layer_logits, the same bits as the router kernel); larger
+    batches: the router kernel, then ``fused_moe`` (two launches). With ``return_routing`` also returns the
+    (weights fp32 [M, k], ids int32 [M, k]) the layer used."""
+    x = hidden_states
+    _need_cuda(x, router_logits)
+    m, hid = x.shape
+    e = router_logits.shape[1]
+    if output is None:
+        output = torch.empty((m, hid), dtype=torch.bfloat16, device=x.device)
+    if (m == 0 or not _decode_path(m, top_k) or e > 512 or x.dtype != torch.bfloat16
+            or os.environ.get("MOEK_B200_DECODE_PATH", "layer") != "layer"):
+        w, ids = router_topk(router_logits, top_k, renormalize)
+        out = fused_moe(x, layer, w, ids, output=output)
+        return (out, (w, ids)) if return_routing else out
+    import ctypes
+
+    _layer_rows_knob()
+    logits = router_logits if router_logits.dtype in (torch.float32, torch.bfloat16) else router_logits.float()
+    logits = logits.contiguous()
+    x = x.contiguous()
+    dev = x.device
+    ids = torch.empty((m, top_k), dtype=torch.int32, device=dev) if return_routing else None
+    w = torch.empty((m, top_k), dtype=torch.float32, device=dev) if return_routing else None
+    a, b = layer.w13, layer.w2
+    hidden, inter = a.K, b.K
+    ns1, ns2 = _layer_splits(hidden, inter)
+    wsb = ctypes.c_size_t(0)
+    call("moek_layer_workspace_bytes", m, top_k, hidden, inter, ns1, ns2, 0, ctypes.byref(wsb))
+    ws = _scratch("layer_ws", wsb.value, torch.uint8, dev)
+    st = _layer_state(dev, layer.E, hidden, inter)
+    _timed("layer", lambda: call(
+        "moek_moe_layer_logits", _ptr(x), m, hidden, inter, layer.E, _ptr(logits), int(logits.dtype == torch.bfloat16),
+        top_k, int(renormalize), _ptr(ids), _ptr(w), _ptr(a.w), _ptr(a.sp), _ptr(a.g), _ptr(a.exc_off),
+        _ptr(a.exc_ent), _ptr(b.w), _ptr(b.sp), _ptr(b.g), _ptr(b.exc_off), _ptr(b.exc_ent), ns1, ns2, _ptr(ws),
+        ws.numel(), _ptr(st), st.numel(), _ptr(error_word(dev)), _ptr(output), _stream(dev)))
+    return (output, (w, ids)) if return_routing else output
 
 
 # ----------------------------------------------------------------------------------------------------- forward

@@ -70,3 +70,25 @@ def test_router_matches_vllm_golden():
         order = np.argsort(-g[f"{n}_w"], axis=1, kind="stable")
         assert np.array_equal(ids.cpu().numpy(), np.take_along_axis(g[f"{n}_ids"], order, 1)), n
         assert np.allclose(w.cpu().numpy(), np.take_along_axis(g[f"{n}_w"], order, 1), rtol=4e-6, atol=1e-9), n
+
+
+@pytest.mark.parametrize("m,e,dtype", [(8, 512, torch.float32), (32, 512, torch.bfloat16), (1, 64, torch.float32),
+                                       (64, 256, torch.float32)])
+def test_layer_with_fused_router(m, e, dtype):
+    """The router fused into the whole-layer kernel (one launch): the routing it reports equals the router kernel's
+    bit for bit, and the output equals router kernel + layer kernel bit for bit and is within the gate of the oracle
+    chain."""
+    w13, w2 = synth.make_layer(e, 2048, 512, 3 + m, device=DEV)
+    layer = prep.PreparedLayer(w13, w2)
+    x = synth.activations(m, 2048, 3 + m, device=DEV)
+    logits = torch.randn((m, e), generator=torch.Generator().manual_seed(m + e)).to(dtype).to(DEV)
+    out, (w, ids) = ops.fused_moe_from_logits(x, layer, logits, 5, return_routing=True)
+    rw, rids = ops.router_topk(logits, 5, True)
+    ref = ops.fused_moe(x, layer, rw, rids)
+    ops.check_device_errors(DEV)
+    assert torch.equal(ids, rids) and torch.equal(w, rw)
+    assert torch.equal(out, ref)
+    oids, ow, _ = router.topk_softmax(logits.float().cpu().numpy(), 5, True)
+    cpu = lambda mm: (mm[0].cpu().numpy(), mm[1].view(torch.uint8).cpu().numpy(), mm[2].cpu().numpy())
+    ok, stats = moe_ref.within_gate(out.cpu(), moe_ref.reference(x.cpu(), oids, ow, cpu(w13), cpu(w2)))
+    assert ok, stats
