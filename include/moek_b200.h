@@ -260,17 +260,19 @@ int moek_ep_unpack(const float* back, const int32_t* pos, const int32_t* offsets
  * with moek_ipc_handle / moek_ipc_open, and passes `peer`, a device array of every rank's block base (its own
  * included). With R = world * mcap rows (segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent),
  * moek_ep_p2p_layout gives the byte offsets of: received rows bf16 [R, H], their local expert ids int32 [R, top_k]
- * (-1: slot owned elsewhere, or unused row), router weights fp32 [R, top_k], returned partials fp32 [R, H], flags
- * int32 [2 world], arrival counters int32 [2 world], and the total. Per layer call, on one stream, every rank runs:
+ * (-1: slot owned elsewhere, or unused row), router weights fp32 [R, top_k], this rank's fp32 partials of the
+ * received rows [R, H] (segment s: those of rank s's rows, which rank s reads over NVLink), flags int32 [2 world],
+ * counters int32 [2 world + 2], and the total. Per layer call, on one stream, every rank runs:
  *   moek_ep_dispatch_p2p (plans the token order itself, writes pos [M, world] for the unpack, and copies rows, ids
  *   and weights straight into the owners' receive segments), then either
- *     moek_moe_layer_p2p (R * top_k <= 512: the whole-layer kernel waits for the receive flags itself and writes
- *     each row's fp32 partial straight into its sender's back segment), or
+ *     moek_moe_layer_p2p (R * top_k <= 512: the whole-layer kernel waits for the receive flags itself, writes each
+ *     row's fp32 partial into its own back buffer and raises the senders' flags), or
  *     moek_ep_wait(own flags), the local layer on the receive rows (fp32 slot rows), moek_ep_combine_p2p,
- *   then moek_ep_unpack_p2p (waits for every rank's partials, sums them in rank order, rounds once to bf16).
- * The flags hand each segment over and back and leave themselves ready for the next call, so the sequence can be
- * captured in a CUDA graph. Waits are bounded (moek_set_wait_timeout_ns) and record MOEK_DEV_TIMEOUT in err.
- * mcap <= 1024 tokens per rank and call. */
+ *   then moek_ep_unpack_p2p (waits for every rank's flag, reads the partials from the owners' back buffers, sums them
+ *   in rank order, rounds once to bf16).
+ * The flags carry the call number, so they never need resetting and the sequence can be captured in a CUDA graph.
+ * Waits are bounded (moek_set_wait_timeout_ns) and record MOEK_DEV_TIMEOUT in err; after one, build the exchange
+ * again. mcap <= 1024 tokens per rank and call, H <= 4096. */
 int moek_ipc_malloc(size_t bytes, void** ptr);
 int moek_ipc_free(void* ptr);
 int moek_ipc_handle(void* ptr, void* handle64);
@@ -287,7 +289,7 @@ int moek_ep_combine_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32
 int moek_ep_unpack_p2p(const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H, int32_t top_k,
                        const int32_t* pos, int32_t M, void* out, int32_t* err, void* stream);
 /* The whole-layer kernel on this rank's receive segments (own = this rank's block), the same arguments as
- * moek_moe_layer otherwise; its rows' fp32 partials go straight to the senders' back segments. */
+ * moek_moe_layer otherwise; its rows' fp32 partials go to this rank's back buffer, where the senders read them. */
 int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap, int32_t H,
                        int32_t I, int32_t local_experts, int32_t top_k, const void* w13, const uint8_t* sp13,
                        const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,

@@ -494,7 +494,7 @@ MOEK_API int moek_ipc_close(void* ptr) { return cuda_status(cudaIpcCloseMemHandl
 static int p2p_args(moek::P2PArgs& a, const uint64_t* peer, int32_t world, int32_t rank, int32_t mcap, int32_t H,
                     int32_t k, int32_t* err) {
   if (!peer || !err || world < 1 || world > moek::EP_MAX_WORLD || rank < 0 || rank >= world || mcap < 0 ||
-      mcap > moek::EP_P2P_MAXM || H <= 0 || H % 8 || k <= 0 || k > 32)
+      mcap > moek::EP_P2P_MAXM || H <= 0 || H % 8 || H > moek::EP_P2P_MAXH || k <= 0 || k > 32)
     return fail(MOEK_ERR_ARG, "moek_b200: EP peer exchange bad arguments (world %d, rank %d, mcap %d, H %d, k %d)",
                 world, rank, mcap, H, k);
   a = moek::P2PArgs{peer, moek::p2p_layout(world, mcap, H, k), world, rank, mcap, H, k, err, g_timeout_ns};
@@ -503,7 +503,7 @@ static int p2p_args(moek::P2PArgs& a, const uint64_t* peer, int32_t world, int32
 
 MOEK_API int moek_ep_p2p_layout(int32_t world, int32_t mcap, int32_t H, int32_t top_k, int64_t* offsets7) {
   if (!offsets7 || world < 1 || world > moek::EP_MAX_WORLD || mcap < 0 || mcap > moek::EP_P2P_MAXM || H <= 0 ||
-      H % 8 || top_k <= 0 || top_k > 32)
+      H % 8 || H > moek::EP_P2P_MAXH || top_k <= 0 || top_k > 32)
     return fail(MOEK_ERR_ARG, "moek_b200: EP peer exchange layout bad arguments (world %d, mcap %d, H %d, k %d)",
                 world, mcap, H, top_k);
   const moek::P2PLayout l = moek::p2p_layout(world, mcap, H, top_k);

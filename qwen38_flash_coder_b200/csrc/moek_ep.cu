@@ -188,10 +188,11 @@ cudaError_t launch_ep_unpack(const float* back, const int32_t* pos, const int32_
 //             stream) waited for those.
 //   wait      my receive flags all c (bounded); the whole-layer kernel does this wait itself.
 //   combine   CTAs (s, g): for the rows of receive segment s, the fp32 sum (slot order) of the row's local slots into
-//             s's back segment for me; the last CTA of s fences and sets s's back flag for me to c. No wait is
-//             needed before writing: s sent call c's rows after its unpack of call c - 1 had read that back segment.
-//   unpack    wait until my back flags are all c, out[t] = bf16(sum over ranks d in order of back segment d's row
-//             for t); the last CTA to finish advances my completed-call count to c.
+//             segment s of my own back buffer; the last CTA of s sets s's back flag for me to c (a release store: my
+//             writes are local, so no system-wide fence is needed first). No wait is needed before writing: s sent
+//             call c's rows after its unpack of call c - 1 had read that segment.
+//   unpack    wait until my back flags are all c, out[t] = bf16(sum over ranks d in order of my segment of d's back
+//             buffer, read over NVLink); the last CTA to finish advances my completed-call count to c.
 // Every wait is bounded by the caller's deadline; on expiry the kernel records MOEK_DEV_TIMEOUT and stops waiting (the
 // counts of the ranks may then disagree: build the exchange again).
 constexpr int P2P_THREADS = 256;
@@ -257,17 +258,37 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
   uint4* seg_x = reinterpret_cast<uint4*>(blk + q.lay.x) + row0 * H16;
   int32_t* seg_ids = reinterpret_cast<int32_t*>(blk + q.lay.ids) + row0 * k;
   float* seg_w = reinterpret_cast<float*>(blk + q.lay.w) + row0 * k;
-  for (int t = g; t < M; t += G) {
-    const int p = spos[t];
-    if (p < 0) continue;
-    uint4* dst = seg_x + (int64_t)p * H16;
-    const uint4* src = x + (int64_t)t * H16;
-    for (int c = tid; c < H16; c += P2P_THREADS) dst[c] = src[c];
-    if (tid < k) {
-      const int e = ids[(int64_t)t * k + tid];
-      const bool mine = e >= 0 && e < E && e / per == d;
-      seg_ids[(int64_t)p * k + tid] = mine ? e - d * per : -1;
-      seg_w[(int64_t)p * k + tid] = mine ? topk_w[(int64_t)t * k + tid] : 0.f;
+  // rows in batches of RB tokens: all of a batch's loads are issued before its stores to the peer, so the copy costs
+  // one load latency per batch, not one per token
+  constexpr int RB = 8;
+  for (int t0 = g; t0 < M; t0 += RB * G) {
+    uint4 v[RB][(EP_P2P_MAXH / 8 + P2P_THREADS - 1) / P2P_THREADS];
+#pragma unroll
+    for (int b = 0; b < RB; b++) {
+      const int t = t0 + b * G;
+      if (t >= M || spos[t] < 0) continue;
+#pragma unroll
+      for (int j = 0; j < (EP_P2P_MAXH / 8 + P2P_THREADS - 1) / P2P_THREADS; j++) {
+        const int c = tid + j * P2P_THREADS;
+        if (c < H16) v[b][j] = x[(int64_t)t * H16 + c];
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < RB; b++) {
+      const int t = t0 + b * G;
+      if (t >= M || spos[t] < 0) continue;
+      const int p = spos[t];
+#pragma unroll
+      for (int j = 0; j < (EP_P2P_MAXH / 8 + P2P_THREADS - 1) / P2P_THREADS; j++) {
+        const int c = tid + j * P2P_THREADS;
+        if (c < H16) seg_x[(int64_t)p * H16 + c] = v[b][j];
+      }
+      if (tid < k) {
+        const int e = ids[(int64_t)t * k + tid];
+        const bool mine = e >= 0 && e < E && e / per == d;
+        seg_ids[(int64_t)p * k + tid] = mine ? e - d * per : -1;
+        seg_w[(int64_t)p * k + tid] = mine ? topk_w[(int64_t)t * k + tid] : 0.f;
+      }
     }
   }
   for (int i = g * P2P_THREADS + tid; i < (q.mcap - count) * k; i += G * P2P_THREADS) {  // rows no token uses
@@ -275,12 +296,11 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_dispatch_p2p_kernel(P2PArgs q,
     seg_w[(int64_t)count * k + i] = 0.f;
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid == 0) {  // one system-scope fence (the CTA's stores to the peer are complete), then the release store
     MOEK_TR(2);
     __threadfence_system();
     int* ctr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(q.peer[q.rank]) + q.lay.ctr) + d;
     if (last_arrival(ctr, G)) {
-      __threadfence_system();
       st_sys(d_flags + q.rank, call);
       MOEK_TR(3);
     }
@@ -304,8 +324,8 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_combine_p2p_kernel(P2PArgs q, 
   const int call = current_call(q);
   uint8_t* mine = reinterpret_cast<uint8_t*>(q.peer[q.rank]);
   const int32_t* rid = reinterpret_cast<const int32_t*>(mine + q.lay.ids);
-  float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(q.peer[s]) + q.lay.back) +
-                (int64_t)q.rank * q.mcap * q.H;  // my segment in s's back buffer
+  float* back = reinterpret_cast<float*>(mine + q.lay.back) +
+                (int64_t)s * q.mcap * q.H;  // s's segment of my back buffer (s reads it over NVLink)
   const int H4 = q.H / 4;
   for (int p = g; p < q.mcap; p += G) {
     const int64_t r = (int64_t)s * q.mcap + p;  // the row's index in my receive buffers (and in rows)
@@ -330,10 +350,7 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_combine_p2p_kernel(P2PArgs q, 
   if (threadIdx.x == 0) {
     __threadfence_system();
     int* ctr = reinterpret_cast<int*>(mine + q.lay.ctr) + q.world + s;
-    if (last_arrival(ctr, G)) {
-      __threadfence_system();
-      st_sys(p2p_flags(q, s) + q.world + q.rank, call);
-    }
+    if (last_arrival(ctr, G)) st_sys(p2p_flags(q, s) + q.world + q.rank, call);
   }
 }
 
@@ -356,7 +373,6 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
   }
   __syncthreads();
   if (!ok) return;
-  const float4* back = reinterpret_cast<const float4*>(mine + q.lay.back);
   const int H4 = q.H / 4;
   for (int64_t i = (int64_t)blockIdx.x * P2P_THREADS + threadIdx.x; i < (int64_t)M * H4;
        i += (int64_t)gridDim.x * P2P_THREADS) {
@@ -366,7 +382,9 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_unpack_p2p_kernel(P2PArgs q, c
     for (int d = 0; d < q.world; d++) {
       const int p = pos[t * q.world + d];
       if (p < 0) continue;
-      const float4 v = __ldcg(back + ((int64_t)d * q.mcap + p) * H4 + c);
+      // owner d's partial of my row p: my segment of d's back buffer, read over NVLink
+      const float4* back = reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(q.peer[d]) + q.lay.back);
+      const float4 v = __ldcg(back + ((int64_t)q.rank * q.mcap + p) * H4 + c);
       o.x += v.x;
       o.y += v.y;
       o.z += v.z;

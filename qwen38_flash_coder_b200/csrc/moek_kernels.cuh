@@ -101,8 +101,9 @@ struct LayerParams {
   int off_cnt1, off_ready, off_cnt2, off_tok, off_epoch, off_done, off_ep;  // int offsets into ctr
   // Expert-parallel receive side (ep_peer non-null, out and out_rows null): x / ids / tw are this rank's receive
   // buffers of the peer-memory exchange (row s * ep_mcap + p came from rank s), the kernel waits for the receive
-  // flags before routing, and each row's fp32 sum of its local slots goes to row ep_rank * ep_mcap + p of rank s's
-  // back buffer; once every row is written, rank s's back flag for this rank is raised.
+  // flags before routing, and each row's fp32 sum of its local slots goes to the same row of this rank's own back
+  // buffer (rank s reads segment s over NVLink); once every row is written, rank s's back flag for this rank is
+  // raised.
   const uint64_t* ep_peer;   // [ep_world] device table: base of each rank's exchange block
   const int* ep_recv_flags;  // this rank's flags [0, ep_world)
   const int* ep_call;        // this rank's completed-call counter (the current call is *ep_call + 1)
@@ -158,12 +159,14 @@ cudaError_t launch_combine_bf16(const __nv_bfloat16* rows, int m, int N, int top
 // moek_ep.cu: expert-parallel dispatch plan, row packing, partial combine and ordered unpack
 constexpr int EP_MAX_WORLD = 32;
 constexpr int EP_P2P_MAXM = 1024;  // tokens per rank and call of the peer-memory exchange
+constexpr int EP_P2P_MAXH = 4096;  // hidden size of the peer-memory exchange
 // The exchange block of the fixed-capacity peer-memory EP path, the same layout on every rank (R = world x mcap rows;
 // segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent): byte offsets of the received bf16 rows [R, H], their
-// local expert ids int32 [R, k] (-1: slot owned elsewhere or unused row) and router weights fp32 [R, k], the returned
-// fp32 partial rows [R, H] (segment d = what rank d returned for this rank's tokens), the flags int32 [2 world]
-// ([s]: the call number whose rows rank s wrote into receive segment s; [world + d]: the call number whose partials
-// rank d wrote into back segment d) and counters int32 [2 world + 2] (arrival counters; [2 world] = the number of
+// local expert ids int32 [R, k] (-1: slot owned elsewhere or unused row) and router weights fp32 [R, k], this rank's
+// fp32 partial rows of the received rows [R, H] (segment s = the partials for rank s's rows, which rank s reads over
+// NVLink), the flags int32 [2 world] ([s]: the call number whose rows rank s wrote into receive segment s; [world + d]:
+// the call number whose partials for this rank rank d has written into its own back buffer) and counters int32
+// [2 world + 2] (arrival counters; [2 world] = the number of
 // calls this rank has completed, advanced by its unpack; [2 world + 1] = the unpack's arrival counter).
 struct P2PLayout {
   int64_t x, ids, w, back, flags, ctr, total;

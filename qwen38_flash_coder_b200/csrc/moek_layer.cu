@@ -867,9 +867,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             o += __ldcg(rows + (int64_t)(tk * k + sl) * H + col);
           }
           if (p.ep_peer) {  // fp32 partial of the row into its sender's back buffer, over NVLink
-            const int s = tk / p.ep_mcap, pr = tk - s * p.ep_mcap;
-            float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peer[s]) + p.ep_back_off);
-            back[((int64_t)p.ep_rank * p.ep_mcap + pr) * H + col] = o;
+            // the row's partial into its sender's segment of this rank's own back buffer (the sender reads it)
+            float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peer[p.ep_rank]) + p.ep_back_off);
+            back[(int64_t)tk * H + col] = o;
             pieces++;
           } else {
             p.out[(int64_t)tk * H + col] = __float2bfloat16_rn(o);
@@ -878,11 +878,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         if (pieces) {  // the arrival that completes every returned row raises the senders' back flags
           __syncwarp();
           if (lane == 0) {
-            __threadfence_system();
+            // the partials are in this GPU's memory: a device-scope release orders them before the arrival, and the
+            // last arrival's system-scope release stores of the flags carry them to the senders
+            __threadfence();
             const int want = ep_rows * p.m[1].nt * NCW;
             if (atomicAdd(p.ctr + p.off_ep, pieces) + pieces == want) {
               p.ctr[p.off_ep] = 0;
-              __threadfence_system();
+              __threadfence();
               ep_signal(p, ep_call);
             }
           }

@@ -142,7 +142,7 @@ class PeerExchange:
     """Fixed-capacity exchange blocks in every rank's memory, shared by CUDA IPC (plain peer loads and stores over
     NVLink, no multicast objects), for ``ep_moe(..., capacity=True, peer=...)``: each rank's rows, slot ids and router
     weights are written straight into the owners' receive segments (``moek_ep_dispatch_p2p``), the owners' fp32
-    partial rows straight back into the senders' back segments (by the whole-layer kernel itself,
+    partial rows into their own back buffers, where the senders read them over NVLink (by the whole-layer kernel itself,
     ``moek_moe_layer_p2p``, or by ``moek_ep_combine_p2p`` after the multi-launch path), and flags hand each segment
     over. Every rank of ``group`` builds it together (one all_gather of the IPC handles) for up to ``mcap`` tokens per
     call of ``top_k`` slots and hidden size ``hidden``; ``close()`` (collective) releases it."""

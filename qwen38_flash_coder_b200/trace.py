@@ -1,6 +1,11 @@
 """Per-CTA timeline of one layer from the MOEK_TRACE build (``libmoek_b200_trace.so``).
 
     MOEK_B200_LIB=trace python -m qwen38_flash_coder_b200.trace [decode8|decode32|prefill] [--layers N]
+    MOEK_B200_LIB=trace torchrun --nproc-per-node N -m qwen38_flash_coder_b200.trace ep_decode8
+
+The ``ep_decode8`` form runs the expert-parallel decode layer (M = 8 tokens per rank, peer-memory exchange) on N
+ranks and prints, per rank, the dispatch, whole-layer and unpack kernels' stamps of one layer call on one time axis
+(the rank's %globaltimer): when each kernel started, when its cross-GPU waits ended and when it finished.
 
 runs the benchmark's layer geometry (E = 512, hidden 2048, expert intermediate 512, top-5; seeded NVFP4 weights and
 routing as bench.py) through ``ops.fused_moe`` eagerly, then reads the %globaltimer stamps of the last launch
@@ -114,9 +119,77 @@ def summarize(t: np.ndarray, kind: int) -> dict:
     return out
 
 
+EP_DISPATCH = {0: "start", 1: "-", 2: "rows written", 3: "flag raised"}
+
+
+def ep_main(a):
+    """The expert-parallel decode layer's kernels on every rank (see the module docstring)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from . import ep, ops, synth
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        m, E = 8, 512
+        layers = []
+        for l in range(a.layers):
+            w13, w2 = synth.make_layer(E, 2048, 512, l, device=dev)
+            L = ep.EPLayer(ep.shard_checkpoint(w13, E, world, rank), ep.shard_checkpoint(w2, E, world, rank), E,
+                           world, rank)
+            x = synth.activations(m, 2048, 1000 * rank + l, device=dev)
+            ids, w = synth.route_softmax(m, E, 5, 1000 * rank + l, device=dev)
+            layers.append((L, x, ids, w))
+            del w13, w2
+        px = ep.PeerExchange(None, m, 2048, 5, dev)
+        for _ in range(3):
+            for L, x, ids, w in layers:
+                ep.ep_moe(x, L, w, ids, capacity=True, peer=px)
+        torch.cuda.synchronize()
+        dist.barrier()
+        clear()
+        torch.cuda.synchronize()
+        dist.barrier()
+        for L, x, ids, w in layers:  # the stamps keep the last layer's launches
+            ep.ep_moe(x, L, w, ids, capacity=True, peer=px)
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        lay, epk = read(0), read(2)
+        px.close()
+        res = {"rank": rank}
+        live = lay[:, 0] > 0
+        d0 = epk[:, 0][epk[:, 0] > 0]
+        t0 = int(min(d0.min() if d0.size else 2 ** 63, lay[live, 0].min() if live.any() else 2 ** 63))
+        us = lambda v: round((float(v) - t0) / 1e3, 2)
+        pick = lambda col: col[col > 0]
+        stats = lambda col: (us(np.median(pick(col))), us(pick(col).max())) if pick(col).size else None
+        res["dispatch"] = {"start": stats(epk[:, 0]), "rows written": stats(epk[:, 2]), "flag raised": stats(epk[:, 3])}
+        res["layer"] = {"start": stats(lay[:, 0]), "flags seen": stats(lay[:, 2]), "routing done": stats(lay[:, 3]),
+                        "end": stats(lay[:, 6])}
+        res["unpack"] = {"start": stats(epk[:, 8]), "partials ready": stats(epk[:, 9]), "done": stats(epk[:, 10])}
+        out = [None] * world
+        dist.all_gather_object(out, res)
+        if rank == 0:
+            if a.json:
+                print(json.dumps(out))
+            else:
+                for r in out:
+                    print(f"rank {r['rank']} (us after its first kernel start; median / max over CTAs):")
+                    for k in ("dispatch", "layer", "unpack"):
+                        print(f"  {k:<9s} " + "; ".join(f"{n} {v[0]}/{v[1]}" for n, v in r[k].items() if v))
+    finally:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("workload", nargs="?", default="decode8", choices=["decode8", "decode32", "prefill"])
+    ap.add_argument("workload", nargs="?", default="decode8", choices=["decode8", "decode32", "prefill",
+                                                                       "ep_decode8"])
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args()
@@ -128,6 +201,8 @@ def main():
 
     if not lib().moek_build_flags() & 1:
         raise SystemExit("moek_b200: load the trace build (MOEK_B200_LIB=trace)")
+    if a.workload == "ep_decode8":
+        return ep_main(a)
     m, kind = {"decode8": (8, "u"), "decode32": (32, "z"), "prefill": (6912, "u")}[a.workload]
     dev = torch.device("cuda", 0)
     layers = []
