@@ -660,8 +660,10 @@ def ep_main(a, rank, world, dev):
         del rec
         rows_local = world * m if wl["capacity"] else m  # received rows per rank (exact counts: about m)
         local = ops.launches_per_layer(rows_local, TOPK) - (0 if ops._decode_path(rows_local, TOPK) else 1)
-        if px is not None and ops.layer_p2p_fits(rows_local, TOPK):
-            per_layer = 3  # dispatch, the whole-layer kernel on the receive segments, unpack
+        fused = px is not None and ops.layer_p2p_fits(rows_local, TOPK)
+        one_launch = fused and os.environ.get("MOEK_B200_EP_FUSED", "1") != "0"
+        if fused:  # the whole-layer kernel dispatching and unpacking itself, or dispatch, that kernel, unpack
+            per_layer = 1 if one_launch else 3
         else:  # plan + pack or dispatch + wait, the local layer's kernels (no top-k sum), partial or combine, unpack
             per_layer = 4 + local
         res["gpu_launches_per_step"] = per_layer * len(layers)
@@ -687,9 +689,10 @@ def ep_main(a, rank, world, dev):
                                                     for x, r, w in zip(hx, hid, hw)),
                           "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
                           "api": "ep.ep_moe with host copies (per rank; value over all ranks)"}
-        fused = px is not None and ops.layer_p2p_fits(rows_local, TOPK)
-        res["exchange"] = ("peer memory (CUDA IPC; " + ("dispatch, whole-layer kernel returning the partials, unpack)"
-                           if fused else "dispatch / combine kernels)") if px is not None else "NCCL")
+        res["exchange"] = ("peer memory (CUDA IPC; " + (
+            "one whole-layer launch: dispatch, layer, partials over NVLink, unpack)" if one_launch else
+            "dispatch, whole-layer kernel returning the partials, unpack)" if fused else "dispatch / combine kernels)")
+            if px is not None else "NCCL")
         if px is not None:
             px.close()
         results[name] = res

@@ -270,6 +270,7 @@ int moek_ep_unpack(const float* back, const int32_t* pos, const int32_t* offsets
  *     moek_ep_wait(own flags), the local layer on the receive rows (fp32 slot rows), moek_ep_combine_p2p,
  *   then moek_ep_unpack_p2p (waits for every rank's flag, reads the partials from the owners' back buffers, sums them
  *   in rank order, rounds once to bf16).
+ * Or, when R * top_k <= 512, the one launch moek_moe_layer_ep, which runs all three steps in the whole-layer kernel.
  * The flags carry the call number, so they never need resetting and the sequence can be captured in a CUDA graph.
  * Waits are bounded (moek_set_wait_timeout_ns) and record MOEK_DEV_TIMEOUT in err; after one, build the exchange
  * again. mcap <= 1024 tokens per rank and call, H <= 4096. */
@@ -296,6 +297,18 @@ int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t world, int
                        const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
                        int32_t nsplit_gate, int32_t nsplit_down, void* workspace, size_t workspace_bytes,
                        int32_t* state, int64_t state_ints, int32_t* err, void* stream);
+/* The whole expert-parallel decode layer in one launch (R * top_k <= 512): the whole-layer kernel dispatches this
+ * rank's M <= mcap tokens (x bf16 [M, H], global expert ids topk_ids [M, top_k], router weights topk_w, experts split
+ * evenly: rank d owns [d E / world, (d + 1) E / world)) as moek_ep_dispatch_p2p does (pos [M, world] is written), runs
+ * the layer on the receive segments as moek_moe_layer_p2p does, and writes out bf16 [M, H] as moek_ep_unpack_p2p
+ * does; the same bits as that three-launch sequence. x and out 16-byte aligned. */
+int moek_moe_layer_ep(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap, int32_t H,
+                      int32_t I, int32_t num_experts, int32_t top_k, const void* x, const int32_t* topk_ids,
+                      const float* topk_w, int32_t M, int32_t* pos, void* out, const void* w13, const uint8_t* sp13,
+                      const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
+                      const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
+                      int32_t nsplit_gate, int32_t nsplit_down, void* workspace, size_t workspace_bytes,
+                      int32_t* state, int64_t state_ints, int32_t* err, void* stream);
 
 #ifdef __cplusplus
 }

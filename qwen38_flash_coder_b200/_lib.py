@@ -47,6 +47,8 @@ SIGNATURES = {
     "moek_ep_unpack_p2p": (ctypes.c_int, [_P] + [_I32] * 5 + [_P, _I32, _P, _P, _P]),
     "moek_moe_layer_p2p": (ctypes.c_int, [_P, _P] + [_I32] * 7 + [_P] * 10 + [_I32, _I32, _P, ctypes.c_size_t, _P,
                                                                               _I64, _P, _P]),
+    "moek_moe_layer_ep": (ctypes.c_int, [_P, _P] + [_I32] * 7 + [_P] * 3 + [_I32] + [_P] * 12 +
+                          [_I32, _I32, _P, ctypes.c_size_t, _P, _I64, _P, _P]),
     "moek_build_flags": (ctypes.c_int, []),
     "moek_trace_read": (ctypes.c_int, [_I32, _P, ctypes.c_size_t]),
     "moek_trace_clear": (ctypes.c_int, []),

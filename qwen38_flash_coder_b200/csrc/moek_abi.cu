@@ -548,20 +548,19 @@ MOEK_API int moek_ep_unpack_p2p(const uint64_t* peer, int32_t world, int32_t ran
                      "ep unpack launch");
 }
 
-MOEK_API int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap,
-                                int32_t H, int32_t I, int32_t local_experts, int32_t top_k, const void* w13,
-                                const uint8_t* sp13, const float* g13, const int32_t* exc_off13,
-                                const int32_t* exc_ent13, const void* w2, const uint8_t* sp2, const float* g2,
-                                const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
-                                int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state,
-                                int64_t state_ints, int32_t* err, void* stream) {
-  moek::P2PArgs a;
+// The receive side of the peer exchange in the whole-layer kernel's parameters (moek_moe_layer_p2p, moek_moe_layer_ep).
+static int layer_p2p_params(moek::LayerParams& p, moek::P2PArgs& a, const uint64_t* peer, const void* own,
+                            int32_t world, int32_t rank, int32_t mcap, int32_t H, int32_t I, int32_t local_experts,
+                            int32_t top_k, const void* w13, const uint8_t* sp13, const float* g13,
+                            const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2, const uint8_t* sp2,
+                            const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                            int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state,
+                            int64_t state_ints, int32_t* err) {
   if (int rc = p2p_args(a, peer, world, rank, mcap, H, top_k, err)) return rc;
   if (!own) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_p2p needs this rank's exchange block");
   const int32_t R = world * mcap;
   if (R == 0) return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_p2p needs mcap > 0");
   const uint8_t* blk = static_cast<const uint8_t*>(own);
-  moek::LayerParams p;
   if (int rc = layer_params(p, blk + a.lay.x, R, H, I, local_experts, reinterpret_cast<const int32_t*>(blk + a.lay.ids),
                             reinterpret_cast<const float*>(blk + a.lay.w), top_k, w13, sp13, g13, exc_off13, exc_ent13,
                             w2, sp2, g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down, workspace, workspace_bytes,
@@ -575,8 +574,59 @@ MOEK_API int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t w
   p.ep_world = world;
   p.ep_rank = rank;
   p.ep_mcap = mcap;
-  return cuda_status(moek::launch_layer(p, layer_block_rows(R), sm_count(), g_layer_coop, (cudaStream_t)stream),
+  return MOEK_OK;
+}
+
+MOEK_API int moek_moe_layer_p2p(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap,
+                                int32_t H, int32_t I, int32_t local_experts, int32_t top_k, const void* w13,
+                                const uint8_t* sp13, const float* g13, const int32_t* exc_off13,
+                                const int32_t* exc_ent13, const void* w2, const uint8_t* sp2, const float* g2,
+                                const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                                int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state,
+                                int64_t state_ints, int32_t* err, void* stream) {
+  moek::P2PArgs a;
+  moek::LayerParams p;
+  if (int rc = layer_p2p_params(p, a, peer, own, world, rank, mcap, H, I, local_experts, top_k, w13, sp13, g13,
+                                exc_off13, exc_ent13, w2, sp2, g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down,
+                                workspace, workspace_bytes, state, state_ints, err))
+    return rc;
+  return cuda_status(moek::launch_layer(p, layer_block_rows(world * mcap), sm_count(), g_layer_coop,
+                                        (cudaStream_t)stream),
                      "moe_layer_p2p launch");
+}
+
+MOEK_API int moek_moe_layer_ep(const uint64_t* peer, const void* own, int32_t world, int32_t rank, int32_t mcap,
+                               int32_t H, int32_t I, int32_t num_experts, int32_t top_k, const void* x,
+                               const int32_t* topk_ids, const float* topk_w, int32_t M, int32_t* pos, void* out,
+                               const void* w13, const uint8_t* sp13, const float* g13, const int32_t* exc_off13,
+                               const int32_t* exc_ent13, const void* w2, const uint8_t* sp2, const float* g2,
+                               const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                               int32_t nsplit_down, void* workspace, size_t workspace_bytes, int32_t* state,
+                               int64_t state_ints, int32_t* err, void* stream) {
+  if (world < 1 || num_experts <= 0 || num_experts % world)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_ep needs the experts split evenly (E %d, world %d)", num_experts,
+                world);
+  if (M < 0 || M > mcap || (M && (!x || !topk_ids || !topk_w || !pos || !out)))
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_ep needs 0 <= M <= mcap (M %d, mcap %d) and its buffers", M, mcap);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_layer_ep needs 16-byte aligned x and out");
+  moek::P2PArgs a;
+  moek::LayerParams p;
+  if (int rc = layer_p2p_params(p, a, peer, own, world, rank, mcap, H, I, num_experts / world, top_k, w13, sp13, g13,
+                                exc_off13, exc_ent13, w2, sp2, g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down,
+                                workspace, workspace_bytes, state, state_ints, err))
+    return rc;
+  p.ep_q = a;
+  p.ep_x = static_cast<const uint4*>(x);
+  p.ep_ids = topk_ids;
+  p.ep_w = topk_w;
+  p.ep_pos = pos;
+  p.ep_out = static_cast<__nv_bfloat16*>(out);
+  p.ep_M = M;
+  p.ep_E = num_experts;
+  return cuda_status(moek::launch_layer(p, layer_block_rows(world * mcap), sm_count(), g_layer_coop,
+                                        (cudaStream_t)stream),
+                     "moe_layer_ep launch");
 }
 
 MOEK_API int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int32_t N, int32_t gate_up,

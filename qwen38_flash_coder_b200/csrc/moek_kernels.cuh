@@ -72,6 +72,41 @@ struct GemmParams {
   int down_bf16;   // tcgen05 path, down: bf16 rows topk_w * sum into out (modes 0/1) instead of fp32 rows into part
 };
 
+// moek_ep.cu / moek_ep.cuh: the fixed-capacity expert-parallel exchange over peer memory
+constexpr int EP_MAX_WORLD = 32;
+constexpr int EP_P2P_MAXM = 1024;  // tokens per rank and call of the peer-memory exchange
+constexpr int EP_P2P_MAXH = 4096;  // hidden size of the peer-memory exchange
+// The exchange block of the fixed-capacity peer-memory EP path, the same layout on every rank (R = world x mcap rows;
+// segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent): byte offsets of the received bf16 rows [R, H], their
+// local expert ids int32 [R, k] (-1: slot owned elsewhere or unused row) and router weights fp32 [R, k], this rank's
+// fp32 partial rows of the received rows [R, H] (segment s = the partials for rank s's rows, which rank s reads over
+// NVLink), the flags int32 [2 world] ([s]: the call number whose rows rank s wrote into receive segment s; [world + d]:
+// the call number whose partials for this rank rank d has written into its own back buffer) and counters int32
+// [2 world + 2] (arrival counters; [2 world] = the number of
+// calls this rank has completed, advanced by its unpack; [2 world + 1] = the unpack's arrival counter).
+struct P2PLayout {
+  int64_t x, ids, w, back, flags, ctr, total;
+};
+__host__ __device__ inline int64_t up256(int64_t b) { return (b + 255) / 256 * 256; }
+__host__ __device__ inline P2PLayout p2p_layout(int world, int mcap, int H, int k) {
+  const int64_t R = (int64_t)world * mcap;
+  P2PLayout l;
+  l.x = 0;
+  l.ids = l.x + up256(R * H * 2);
+  l.w = l.ids + up256(R * k * 4);
+  l.back = l.w + up256(R * k * 4);
+  l.flags = l.back + up256(R * H * 4);
+  l.ctr = l.flags + up256(2 * world * 4);
+  l.total = l.ctr + up256((2 * world + 2) * 4);
+  return l;
+}
+struct P2PArgs {  // peer-memory exchange of the fixed-capacity EP path (moek_ep.cu)
+  const uint64_t* peer;  // [world] device table: base of each rank's exchange block (CUDA IPC mappings)
+  P2PLayout lay;
+  int world, rank, mcap, H, k;
+  int* err;
+  uint64_t timeout_ns;
+};
 // moek_layer.cu: the whole decode-regime layer in one persistent kernel
 constexpr int LAYER_MAXIDS = 512;  // routed slots (tokens x top_k) per call
 struct LayerMat {                  // one weight matrix in this build's layout (gate_up: N = 2I, K = H; down: N = H, K = I)
@@ -109,6 +144,18 @@ struct LayerParams {
   const int* ep_call;        // this rank's completed-call counter (the current call is *ep_call + 1)
   int64_t ep_back_off, ep_flags_off;  // byte offsets of the back buffer and the flags in an exchange block
   int ep_world, ep_rank, ep_mcap;
+  // Fused exchange (ep_x non-null, with ep_peer): the kernel also runs this rank's side of the exchange, so that the
+  // layer is one launch: CTAs [0, world x G) dispatch this rank's ep_M tokens (rows ep_x, global expert ids ep_ids,
+  // router weights ep_w) into the owners' receive segments and write ep_pos [ep_M, world] before the receive wait, and
+  // once the owners' back flags read this call, CTAs unpack ep_out bf16 [ep_M, H] = the owners' partials summed in
+  // rank order; the last CTA to finish completes the call.
+  P2PArgs ep_q;
+  const uint4* ep_x;
+  const int32_t* ep_ids;
+  const float* ep_w;
+  int32_t* ep_pos;
+  __nv_bfloat16* ep_out;
+  int ep_M, ep_E;
   int tail;  // 1: items past the last whole wave of units may use a finer k-split (up to one per stage)
   // Fused router (logits non-null): every CTA routes the M tokens itself from the router logits [M, E] (fp32, or bf16
   // when logits_bf16): softmax, top_k, renormalised when renorm; ids and tw are not read, and CTA 0 writes the
@@ -156,41 +203,8 @@ cudaError_t launch_combine_f32(const float* rows, int m, int N, int top_k, __nv_
 cudaError_t launch_combine_bf16(const __nv_bfloat16* rows, int m, int N, int top_k, __nv_bfloat16* out,
                                 cudaStream_t st);
 
-// moek_ep.cu: expert-parallel dispatch plan, row packing, partial combine and ordered unpack
-constexpr int EP_MAX_WORLD = 32;
-constexpr int EP_P2P_MAXM = 1024;  // tokens per rank and call of the peer-memory exchange
-constexpr int EP_P2P_MAXH = 4096;  // hidden size of the peer-memory exchange
-// The exchange block of the fixed-capacity peer-memory EP path, the same layout on every rank (R = world x mcap rows;
-// segment s = rows [s mcap, (s + 1) mcap), the rows rank s sent): byte offsets of the received bf16 rows [R, H], their
-// local expert ids int32 [R, k] (-1: slot owned elsewhere or unused row) and router weights fp32 [R, k], this rank's
-// fp32 partial rows of the received rows [R, H] (segment s = the partials for rank s's rows, which rank s reads over
-// NVLink), the flags int32 [2 world] ([s]: the call number whose rows rank s wrote into receive segment s; [world + d]:
-// the call number whose partials for this rank rank d has written into its own back buffer) and counters int32
-// [2 world + 2] (arrival counters; [2 world] = the number of
-// calls this rank has completed, advanced by its unpack; [2 world + 1] = the unpack's arrival counter).
-struct P2PLayout {
-  int64_t x, ids, w, back, flags, ctr, total;
-};
-__host__ __device__ inline int64_t up256(int64_t b) { return (b + 255) / 256 * 256; }
-__host__ __device__ inline P2PLayout p2p_layout(int world, int mcap, int H, int k) {
-  const int64_t R = (int64_t)world * mcap;
-  P2PLayout l;
-  l.x = 0;
-  l.ids = l.x + up256(R * H * 2);
-  l.w = l.ids + up256(R * k * 4);
-  l.back = l.w + up256(R * k * 4);
-  l.flags = l.back + up256(R * H * 4);
-  l.ctr = l.flags + up256(2 * world * 4);
-  l.total = l.ctr + up256((2 * world + 2) * 4);
-  return l;
-}
-struct P2PArgs {  // peer-memory exchange of the fixed-capacity EP path (moek_ep.cu)
-  const uint64_t* peer;  // [world] device table: base of each rank's exchange block (CUDA IPC mappings)
-  P2PLayout lay;
-  int world, rank, mcap, H, k;
-  int* err;
-  uint64_t timeout_ns;
-};
+// moek_ep.cu: expert-parallel dispatch plan, row packing, partial combine and ordered unpack (the exchange
+// structures are declared before the whole-layer kernel, which can run the peer exchange itself)
 cudaError_t launch_ep_dispatch_p2p(const P2PArgs& a, const __nv_bfloat16* x, const int32_t* ids, const float* topk_w,
                                    int M, int E, int32_t* pos, cudaStream_t st);
 cudaError_t launch_ep_wait(const int* flags, int world, int* err, uint64_t timeout_ns, cudaStream_t st);

@@ -54,6 +54,7 @@
 #include <type_traits>
 
 #include "moek_common.cuh"
+#include "moek_ep.cuh"
 #include "moek_kernels.cuh"
 #include "moek_route.cuh"
 
@@ -198,6 +199,11 @@ __device__ __forceinline__ void ep_signal(const LayerParams& p, int call) {
            call);
 }
 
+// CTAs per destination of the fused exchange's dispatch: up to one per token, at least one (the flag must be raised)
+__device__ __forceinline__ int ep_dispatch_ctas(const LayerParams& p) {
+  return max(1, min((int)gridDim.x / p.ep_world, p.ep_M));
+}
+
 __device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePlan& q0, const PhasePlan& q1, int u,
                                             UnitMeta& um) {
   um.ph = u >= q0.u_total ? 1 : 0;
@@ -263,6 +269,18 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   if (tid == 0) MOEK_TR(1);
   if (tid == 0) MOEK_TR_CLK(39);
   const uint64_t deadline = globaltimer() + p.timeout_ns;
+  // expert-parallel: this exchange call's number (the flags carry it, so they never need resetting)
+  const int ep_call = p.ep_peer ? *reinterpret_cast<volatile const int*>(p.ep_call) + 1 : 0;
+  if (p.ep_x) {  // fused exchange: CTAs [0, world x G) first send this rank's tokens to their experts' owners
+    const int G = ep_dispatch_ctas(p);
+    if ((int)blockIdx.x < p.ep_world * G) {
+      if (tid == 0) MOEK_TR(48);
+      const int d = blockIdx.x / G;
+      int* spos = reinterpret_cast<int*>(smem);  // scratch in ring slot 0, as the routing's below
+      ep_dispatch_cta<THREADS, 4, 46>(p.ep_q, p.ep_x, p.ep_ids, p.ep_w, p.ep_M, p.ep_E, d, blockIdx.x - d * G, G,
+                                      ep_call, p.ep_pos, spos, spos + LAYER_MAXIDS);
+    }
+  }
   const int n = p.num_ids, k = p.top_k;
   // the batch's routing in shared memory for the whole kernel (ids and router weights of every slot): loaded first
   // (each thread's at most two slots: n <= 512 < 2 x THREADS), or computed from the router logits by every CTA (one
@@ -300,8 +318,6 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
     }
   }
   const int epoch = *reinterpret_cast<volatile const int*>(p.ctr + p.off_epoch);
-  // expert-parallel: this exchange call's number (the flags carry it, so they never need resetting)
-  const int ep_call = p.ep_peer ? *reinterpret_cast<volatile const int*>(p.ep_call) + 1 : 0;
   if (p.ep_peer) {  // expert-parallel: wait until every sender's rows, ids and weights are in the receive buffers
     if (warp == 0) {
       bool good = true;
@@ -906,6 +922,26 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
     }
   }
 
+  // fused exchange: once every owner's partials of this rank's tokens are written, the last CTAs (the ones with the
+  // fewest units) sum them into the output, a slice each
+  if (p.ep_x) {
+    const int total = p.ep_M * (p.H / 4), ncta = min((int)gridDim.x, (total + THREADS - 1) / THREADS);
+    const int cta = (int)gridDim.x - 1 - (int)blockIdx.x;
+    __syncthreads();
+    if (cta < ncta) {
+      bool good = true;
+      if (warp == 0) {
+        const uint64_t until = globaltimer() + p.timeout_ns;
+        for (int s = lane; s < p.ep_world; s += 32)
+          good &= wait_flag(p.ep_recv_flags + p.ep_world + s, ep_call, until, p.err);
+        good = __all_sync(0xffffffffu, good);
+        if (lane == 0) MOEK_TR(49);
+      }
+      if (__syncthreads_and(good)) ep_unpack_slice<THREADS>(p.ep_q, p.ep_pos, p.ep_M, p.ep_out, cta, ncta);
+      if (tid == 0) MOEK_TR(50);
+    }
+  }
+
   // ------------------------------------------------------------------------------------------------ teardown
   __syncthreads();
   if (tid == 0) MOEK_TR(6);
@@ -915,6 +951,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       p.ctr[p.off_done] = 0;
       __threadfence();
       atomicAdd(p.ctr + p.off_epoch, 1);
+      // fused exchange: every CTA has read this call's number and unpacked its slice, so the call is complete
+      if (p.ep_x) *p2p_call(p.ep_q) = ep_call;
     }
   }
 }

@@ -25,6 +25,8 @@ makes the others' next collective raise instead of hanging (tested with gloo ran
 pluggable so that the orchestration can be tested on CPU ranks against the oracle (``tests/test_ep_cpu.py``); the
 default backend is the CUDA kernels, and there is no CPU fallback in it.
 """
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -200,9 +202,10 @@ class PeerExchange:
 
 
 def _ep_moe_peer(x, layer: EPLayer, w, ids32, px: PeerExchange, be) -> torch.Tensor:
-    """The fixed-capacity layer over peer memory (``PeerExchange``): no collective library call. Three launches when
-    the received rows fit the whole-layer kernel (dispatch, layer, unpack), else dispatch, wait, the local layer's
-    kernels, combine, unpack. With ``be.record`` a list, a copy of the received batch (rows, slot metadata as in
+    """The fixed-capacity layer over peer memory (``PeerExchange``): no collective library call. One launch when the
+    received rows fit the whole-layer kernel (it dispatches, computes and unpacks itself; three launches, dispatch,
+    layer, unpack, with ``MOEK_B200_EP_FUSED=0`` or ``be.record``), else dispatch, wait, the local layer's kernels,
+    combine, unpack. With ``be.record`` a list, a copy of the received batch (rows, slot metadata as in
     ``CudaBackend.local``, metadata row stride) is appended to it, taken before the unpack lets the senders write
     again."""
     m, hid = x.shape
@@ -216,12 +219,17 @@ def _ep_moe_peer(x, layer: EPLayer, w, ids32, px: PeerExchange, be) -> torch.Ten
     st = ops._stream(dev)
     head = (ops._ptr(px.peer), px.world, px.rank, px.mcap, hid, k)
     pos = torch.empty((m, px.world), dtype=torch.int32, device=dev)
+    fits = ops.layer_p2p_fits(px.world * px.mcap, k)
+    if fits and getattr(be, "record", None) is None and os.environ.get("MOEK_B200_EP_FUSED", "1") != "0":
+        out = torch.empty((m, hid), dtype=torch.bfloat16, device=dev)
+        ops.layer_ep(px, layer.prep, x, ids32, w, layer.num_experts, pos, out)
+        return out
     call("moek_ep_dispatch_p2p", *head, ops._ptr(x), ops._ptr(ids32), ops._ptr(w), m, layer.num_experts,
          ops._ptr(pos), ops._ptr(px.err), st)
     if getattr(be, "record", None) is not None:
         call("moek_ep_wait", px.flags, px.world, ops._ptr(px.err), st)
         be.record.append((px.recv_x.clone(), torch.cat([px.recv_ids, px.recv_w.view(torch.int32)], 1), 2 * k))
-    if ops.layer_p2p_fits(px.world * px.mcap, k):
+    if fits:
         ops.layer_p2p(px, layer.prep)
     else:
         call("moek_ep_wait", px.flags, px.world, ops._ptr(px.err), st)

@@ -343,6 +343,30 @@ def layer_p2p(px, layer: PreparedLayer):
          _stream(dev))
 
 
+def layer_ep(px, layer: PreparedLayer, x: torch.Tensor, ids32: torch.Tensor, w: torch.Tensor, num_experts: int,
+             pos: torch.Tensor, out: torch.Tensor):
+    """The whole expert-parallel decode layer in one launch (moek_moe_layer_ep): the whole-layer kernel dispatches this
+    rank's tokens ``x`` (global expert ids ``ids32``, router weights ``w``) into the owners' receive segments, runs
+    the layer on its own receive segments as ``layer_p2p`` does, and sums the owners' partials into ``out`` bf16
+    [M, H]; ``pos`` [M, world] receives each token's row in each owner's segment."""
+    import ctypes
+
+    _layer_rows_knob()
+    a, b = layer.w13, layer.w2
+    hidden, inter = a.K, b.K
+    dev = x.device
+    rows, k = px.world * px.mcap, px.top_k
+    ns1, ns2 = _layer_splits(hidden, inter)
+    wsb = ctypes.c_size_t(0)
+    call("moek_layer_workspace_bytes", rows, k, hidden, inter, ns1, ns2, 0, ctypes.byref(wsb))
+    ws = _scratch("layer_ws", wsb.value, torch.uint8, dev)
+    st = _layer_state(dev, layer.E, hidden, inter)
+    call("moek_moe_layer_ep", _ptr(px.peer), px.own, px.world, px.rank, px.mcap, hidden, inter, num_experts, k,
+         _ptr(x), _ptr(ids32), _ptr(w), x.shape[0], _ptr(pos), _ptr(out), _ptr(a.w), _ptr(a.sp), _ptr(a.g),
+         _ptr(a.exc_off), _ptr(a.exc_ent), _ptr(b.w), _ptr(b.sp), _ptr(b.g), _ptr(b.exc_off), _ptr(b.exc_ent), ns1,
+         ns2, _ptr(ws), ws.numel(), _ptr(st), st.numel(), _ptr(px.err), _stream(dev))
+
+
 def _splits(k: int, units_per_split: int, grid: int) -> int:
     """k-split (whole 128-k runs per unit) that balances units over the grid best: the split whose busiest CTA has the
     least work (in stages), preferring fewer splits on ties."""

@@ -1,9 +1,10 @@
 """A model check of the flag protocol of the peer-memory EP exchange, on the CPU.
 
-The protocol lives in csrc/moek_ep.cu (ep_dispatch_p2p_kernel, ep_wait_kernel, ep_combine_p2p_kernel,
-ep_unpack_p2p_kernel) and csrc/moek_layer.cu (the whole-layer kernel's receive-flag wait and ep_signal). Per layer, on
-every rank's stream: dispatch, then either the whole-layer kernel (fused) or wait + local layer + combine, then
-unpack. The kernels of one rank run in stream order; the CTAs of one kernel run concurrently. This test models each
+The protocol lives in csrc/moek_ep.cuh and csrc/moek_ep.cu (dispatch, ep_wait_kernel, ep_combine_p2p_kernel,
+unpack) and csrc/moek_layer.cu (the whole-layer kernel's receive-flag wait and ep_signal). Per layer, on every rank's
+stream: dispatch, then either the whole-layer kernel (fused) or wait + local layer + combine, then unpack; or one
+launch of the whole-layer kernel whose CTAs dispatch, compute and unpack (one). The kernels of one rank run in stream
+order; the CTAs of one kernel run concurrently. This test models each
 kernel as concurrent sub-tasks made of the protocol's waits and actions on the flags and on generation-tagged
 segments, runs every rank's program under many random schedules (sequentially consistent interleavings), and checks:
 
@@ -44,9 +45,10 @@ class State:
         self.recv_gen, self.recv_read, self.back_gen, self.back_read = seg(), seg(), seg(), seg()
 
 
-def _program(st: State, r: int, layers: int, fused: bool, plant: str):
+def _program(st: State, r: int, layers: int, fused, plant: str):
     """Rank r's kernels, each a list of sub-tasks (concurrent CTAs or warps), each a list of steps. A step is
-    ("wait", cond) or ("do", action)."""
+    ("wait", cond) or ("do", action). fused: False (wait, local layer, combine), True (the whole-layer kernel
+    between dispatch and unpack) or "one" (dispatch, layer and unpack as the CTAs of one kernel)."""
     W, G = st.world, st.parts
     do = lambda f: ("do", f)
     kernels = []
@@ -135,6 +137,8 @@ def _program(st: State, r: int, layers: int, fused: bool, plant: str):
             back_ready = [("wait", lambda L=L: all(st.back_flag[r][d] == mark(L) for d in range(W)))]
         unpack = [back_ready + [do(lambda d=d, j=j, f=read_back: f(d, j))] for d in range(W) for j in range(G)]
         kernels.append(unpack)
+        if fused == "one":  # dispatch, layer and unpack: the concurrent CTAs of one launch
+            kernels[-3:] = [kernels[-3] + kernels[-2] + kernels[-1]]
     return kernels
 
 
@@ -171,7 +175,7 @@ def run_schedule(world, layers, fused, seed, plant="", parts=1):
 
 
 @pytest.mark.parametrize("parts", [1, 3])
-@pytest.mark.parametrize("fused", [True, False])
+@pytest.mark.parametrize("fused", [True, False, "one"])
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_protocol_progress_and_freshness(world, fused, parts):
     """parts: CTAs per peer in dispatch and combine, and pieces per sender in the whole-layer kernel."""
@@ -180,14 +184,15 @@ def test_protocol_progress_and_freshness(world, fused, parts):
         run_schedule(world, layers=5, fused=fused, seed=1000 * world + seed, parts=parts)
 
 
+@pytest.mark.parametrize("fused", [True, "one"])
 @pytest.mark.parametrize("plant", ["flag_before_data", "binary_flags", "layer_signals_before_return",
                                    "unpack_no_wait", "unpack_accepts_previous"])
-def test_planted_mistakes_are_caught(plant):
+def test_planted_mistakes_are_caught(plant, fused):
     """Each planted mistake leads, in some schedule, to a stale read, an overwrite or a deadlock."""
     caught = 0
     for seed in range(400):
         try:
-            run_schedule(2, layers=4, fused=True, seed=seed, plant=plant, parts=2)
+            run_schedule(2, layers=4, fused=fused, seed=seed, plant=plant, parts=2)
         except Violation:
             caught += 1
     assert caught > 0, plant

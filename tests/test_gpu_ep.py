@@ -112,8 +112,9 @@ def test_ep_one_rank_equals_fused_moe(m, capacity):
 def test_ep_peer_exchange_one_rank(m, mcap):
     """The peer-memory exchange on a one-rank group (the block shared with itself): equal to the NCCL fixed-capacity
     path bit for bit, repeatable (the flags carry the call number), also when replayed as a CUDA graph. mcap 8: the
-    whole-layer kernel reads the receive segment and returns the partials itself (three launches); mcap 128: more
-    slots than it takes, so the local layer's kernels run between a wait and the combine kernel."""
+    whole-layer kernel dispatches, reads the receive segment, returns the partials and unpacks them itself (one
+    launch; the three-launch sequence, dispatch, layer, unpack, gives the same bits); mcap 128: more slots than it
+    takes, so the local layer's kernels run between a wait and the combine kernel."""
     import torch.distributed as dist
 
     from qwen38_flash_coder_b200 import ep, ops, synth
@@ -129,6 +130,12 @@ def test_ep_peer_exchange_one_rank(m, mcap):
         assert ops.layer_p2p_fits(mcap, 5) == (mcap * 5 <= 512)
         ref = ep.ep_moe(x, layer, wts, ids, capacity=True)
         outs = [ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px) for _ in range(3)]
+        os.environ["MOEK_B200_EP_FUSED"] = "0"
+        try:
+            outs += [ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px) for _ in range(2)]
+        finally:
+            del os.environ["MOEK_B200_EP_FUSED"]
+        outs.append(ep.ep_moe(x, layer, wts, ids, capacity=True, peer=px))
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -217,20 +224,38 @@ def _ep_rank(rank, world, port, q):
         # against the one-GPU layer
         px = ep.PeerExchange(None, m2, 2048, 5, dev)
         peer_outs = [ep.ep_moe(x2, layer, wts2, ids2, capacity=True, peer=px) for _ in range(3)]
+        # a decode batch of 8 tokens a rank: the one-launch layer (dispatch, layer and unpack in the whole-layer
+        # kernel) at every world size here, against the three-launch sequence, which must give the same bits
+        m3 = 8
+        x3 = synth.activations(m3, 2048, 80 + rank, device=dev)
+        ids3, wts3 = synth.route_zipf(m3, E, 5, 80 + rank, device=dev)
+        px3 = ep.PeerExchange(None, m3, 2048, 5, dev)
+        fused3 = [ep.ep_moe(x3, layer, wts3, ids3, capacity=True, peer=px3) for _ in range(3)]
+        os.environ["MOEK_B200_EP_FUSED"] = "0"
+        try:
+            three3 = [ep.ep_moe(x3, layer, wts3, ids3, capacity=True, peer=px3) for _ in range(2)]
+        finally:
+            del os.environ["MOEK_B200_EP_FUSED"]
+        fused3.append(ep.ep_moe(x3, layer, wts3, ids3, capacity=True, peer=px3))
         ref = ops.fused_moe(x, full.prep, wts, ids)
         ref2 = ops.fused_moe(x2, full.prep, wts2, ids2)
+        ref3 = ops.fused_moe(x3, full.prep, wts3, ids3)
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
         px.close()
+        px3.close()
         if not all(torch.equal(o, peer_outs[0]) for o in peer_outs[1:]):
             raise AssertionError("peer-memory exchange not repeatable")
+        if not all(torch.equal(o, fused3[0]) for o in fused3[1:] + three3):
+            raise AssertionError("one-launch EP layer differs from the three-launch sequence or between calls")
+        rel4, _, net4 = moe_ref.check(fused3[0].cpu(), ref3.float().cpu())
         rel_pn, _, _ = moe_ref.check(peer_outs[0].cpu(), out2.float().cpu())
         if rel_pn > 2e-3:
             raise AssertionError(f"peer-memory exchange differs from the NCCL exchange: rel {rel_pn:.2e}")
         rel, raw, net = moe_ref.check(out.cpu(), ref.float().cpu())
         rel2, raw2, net2 = moe_ref.check(out2.cpu(), ref2.float().cpu())
         rel3, raw3, net3 = moe_ref.check(peer_outs[0].cpu(), ref2.float().cpu())
-        q.put((rank, "ok", (max(rel, rel2, rel3), max(net, net2, net3))))
+        q.put((rank, "ok", (max(rel, rel2, rel3, rel4), max(net, net2, net3, net4))))
         dist.destroy_process_group()
     except Exception as exc:
         q.put((rank, "error", repr(exc)))
