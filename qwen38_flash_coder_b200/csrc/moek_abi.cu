@@ -266,30 +266,24 @@ MOEK_API int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M
 }
 
 // ------------------------------------------------------------------------------------- whole decode layer
-// Persistent int32 state of moek_moe_layer: [epoch, done, ep, cnt1, ready, cnt2, tok] (ready: one stamp per (block,
-// gate_up item, consumer warp)). The layout depends only on (E, H, I), so one zeroed state buffer serves every call of
-// that geometry.
+// Persistent int32 state of moek_moe_layer: [epoch, barrier counter, EP arrival counter], then the share exchange
+// flags [LAYER_MAXREM][LAYER_XFLAG_CTAS][consumer warp] (stamped with the launch epoch). The layout depends on
+// nothing, so one zeroed state buffer serves every call of the layer.
 struct LayerLayout {
-  int64_t cnt1, ready, cnt2, tok, total;
+  int64_t xflag, total;
 };
-static LayerLayout layer_layout(int32_t E, int32_t H, int32_t I) {
-  // blocks: at most one per routed slot (an expert with more slots than a block takes spans several)
-  const int64_t nbmax = moek::LAYER_MAXIDS, nt1 = 2 * (int64_t)I / 256, nt2 = H / 256;
+static LayerLayout layer_layout(int32_t, int32_t, int32_t) {
   LayerLayout l;
-  l.cnt1 = 3;
-  l.ready = l.cnt1 + nbmax * nt1 * 8;
-  l.cnt2 = l.ready + nbmax * nt1 * 8;
-  l.tok = l.cnt2 + nbmax * nt2 * 8;
-  l.total = l.tok + (int64_t)moek::LAYER_MAXIDS * nt2 * 8;
+  l.xflag = 3;
+  l.total = l.xflag + (int64_t)moek::LAYER_MAXREM * moek::LAYER_XFLAG_CTAS * moek::LAYER_NCW;
   return l;
 }
-// Workspace: act, then k-split partials for up to one split per 128-k stage (the kernel may cut the items past its
-// last whole wave of units that finely, whatever the caller's split), then the fp32 slot rows.
-static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, bool rows) {
+// Workspace: the split pairs' gate_up partials (LAYER_MAXREM positions x the grid x 32 rows x 256 columns, fp32),
+// then the down partials per k-slice [I / 128, num_ids, H] fp32.
+static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, bool) {
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  const int64_t nst1 = H / 128, nst2 = I / 128;
-  return up(num_ids * I * 2) + (nst1 > 1 ? up(nst1 * num_ids * 2 * I * 4) : 0) +
-         (nst2 > 1 ? up(nst2 * num_ids * H * 4) : 0) + (rows ? up(num_ids * (int64_t)H * 4) : 0);
+  const int64_t grid = std::min<int64_t>(2 * (int64_t)sm_count(), moek::LAYER_XFLAG_CTAS);
+  return up((int64_t)moek::LAYER_MAXREM * grid * 32 * moek::ITEM_COLS * 4) + up((int64_t)(I / 128) * num_ids * H * 4);
 }
 
 MOEK_API int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n) {
@@ -317,14 +311,12 @@ MOEK_API int moek_set_layer_block_rows(int32_t rows) {
   g_layer_rows = rows;
   return MOEK_OK;
 }
-// Whether the whole-layer kernel may give the items past its last whole wave of units a finer k-split (default on).
-static int g_layer_tail = 1;
-MOEK_API int moek_set_layer_tail_split(int32_t on) {
-  g_layer_tail = on ? 1 : 0;
-  return MOEK_OK;
-}
-// Whether the whole-layer kernel is launched as a cooperative grid (default on): its down units wait on gate_up
-// units of other CTAs, so every CTA must be resident at once; a cooperative launch makes the runtime guarantee it.
+// Kept for callers of the earlier unit plan: the pair plan splits the pairs left over after its whole waves itself,
+// so there is nothing to switch.
+MOEK_API int moek_set_layer_tail_split(int32_t) { return MOEK_OK; }
+// Whether the whole-layer kernel is launched as a cooperative grid (default on): the shares of a pair and its grid
+// barrier wait on other CTAs, so every CTA must be resident at once; a cooperative launch makes the runtime
+// guarantee it.
 static int g_layer_coop = 1;
 MOEK_API int moek_set_layer_cooperative(int32_t on) {
   g_layer_coop = on ? 1 : 0;
@@ -370,28 +362,14 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
   uint8_t* wp = static_cast<uint8_t*>(workspace);
   p = moek::LayerParams{};
-  p.act = reinterpret_cast<__nv_bfloat16*>(wp);
-  wp += up(num_ids * I * 2);
-  if (nst1 > 1) {
-    p.part1 = reinterpret_cast<float*>(wp);
-    wp += up((int64_t)nst1 * num_ids * 2 * I * 4);
-  }
-  if (nst2 > 1) {
-    p.part2 = reinterpret_cast<float*>(wp);
-    wp += up((int64_t)nst2 * num_ids * H * 4);
-  }
-  if (rows_ws) p.rows = reinterpret_cast<float*>(wp);
-  auto divs = [](int n) {
-    uint64_t m = 0;
-    for (int s = 1; s <= n && s < 64; s++)
-      if (n % s == 0) m |= 1ull << s;
-    return m;
-  };
+  const int64_t grid = std::min<int64_t>(2 * (int64_t)sm_count(), moek::LAYER_XFLAG_CTAS);
+  p.xpart = reinterpret_cast<float*>(wp);
+  wp += up((int64_t)moek::LAYER_MAXREM * grid * 32 * moek::ITEM_COLS * 4);
+  p.part2 = reinterpret_cast<float*>(wp);
   const moek::LayerMat m1{static_cast<const uint8_t*>(w13), sp13, g13, exc_off13,
-                          reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1, nsplit_gate,
-                          divs(nst1)};
+                          reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1};
   const moek::LayerMat m2{static_cast<const uint8_t*>(w2), sp2, g2, exc_off2,
-                          reinterpret_cast<const uint32_t*>(exc_ent2), H, I, H / 256, nst2, nsplit_down, divs(nst2)};
+                          reinterpret_cast<const uint32_t*>(exc_ent2), H, I, H / 256, nst2};
   p.m[0] = m1;
   p.m[1] = m2;
   p.x = static_cast<const __nv_bfloat16*>(x);
@@ -409,11 +387,7 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   p.off_epoch = 0;
   p.off_done = 1;
   p.off_ep = 2;
-  p.tail = g_layer_tail;
-  p.off_cnt1 = (int)lay.cnt1;
-  p.off_ready = (int)lay.ready;
-  p.off_cnt2 = (int)lay.cnt2;
-  p.off_tok = (int)lay.tok;
+  p.off_xflag = (int)lay.xflag;
   return MOEK_OK;
 }
 

@@ -147,12 +147,33 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+#ifndef MOEK_WAIT_HINT_NS
+#define MOEK_WAIT_HINT_NS 0
+#endif
+// try_wait with a suspend-time hint: the thread is suspended in hardware (issuing nothing) until the phase completes
+// or about `ns` nanoseconds have passed.
+__device__ __forceinline__ bool mbar_try_for(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with the given parity. Returns false (after reporting) once the deadline passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err) {
   if (mbar_try(bar, parity)) return true;
   for (uint32_t i = 1;; i++) {
+#if MOEK_WAIT_HINT_NS > 0
+    if (mbar_try_for(bar, parity, MOEK_WAIT_HINT_NS)) return true;
+    if (globaltimer() > deadline) {
+#else
     if (mbar_try(bar, parity)) return true;
     if ((i & 255) == 0 && globaltimer() > deadline) {
+#endif
       report(err, MOEK_DEV_TIMEOUT);
       return false;
     }
@@ -162,9 +183,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 // (they run ahead of the warps they feed): waiting warps then leave the issue slots to the working ones.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint64_t deadline, int* err) {
   if (mbar_try(bar, parity)) return true;
+#if MOEK_WAIT_HINT_NS > 0
+  for (;;) {
+    if (mbar_try_for(bar, parity, MOEK_WAIT_HINT_NS)) return true;
+#else
   for (uint32_t ns = 32;; ns = ns < 256 ? 2 * ns : ns) {
     __nanosleep(ns);
     if (mbar_try(bar, parity)) return true;
+#endif
     if (globaltimer() > deadline) {
       report(err, MOEK_DEV_TIMEOUT);
       return false;

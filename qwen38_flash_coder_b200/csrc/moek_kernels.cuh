@@ -108,32 +108,32 @@ struct P2PArgs {  // peer-memory exchange of the fixed-capacity EP path (moek_ep
   uint64_t timeout_ns;
 };
 // moek_layer.cu: the whole decode-regime layer in one persistent kernel
-constexpr int LAYER_MAXIDS = 512;  // routed slots (tokens x top_k) per call
+constexpr int LAYER_MAXIDS = 512;      // routed slots (tokens x top_k) per call
+constexpr int LAYER_MAXREM = 2;        // positions of split pairs after the whole waves
+constexpr int LAYER_XFLAG_CTAS = 1024; // CTAs of the grid at most (exchange flags per (position, CTA, warp))
+constexpr int LAYER_NCW = 8;           // consumer warps per CTA
 struct LayerMat {                  // one weight matrix in this build's layout (gate_up: N = 2I, K = H; down: N = H, K = I)
   const uint8_t* W;
   const uint8_t* SP;
   const float* G;
   const int32_t* exc_off;
   const uint32_t* exc_ent;
-  int N, K, nt, nstage, nsplit;  // nt = N / 256 items, nstage = K / 128, nsplit = k-splits per item
-  uint64_t divmask;              // bit s set when s divides nstage (the whole-stage k-splits)
+  int N, K, nt, nstage;  // nt = N / 256 items, nstage = K / 128
 };
 struct LayerParams {
   LayerMat m[2];  // 0 = gate_up, 1 = down
   const __nv_bfloat16* x;  // [M, H]
   const int32_t* ids;      // [M * top_k] expert per slot (outside [0, E): not routed)
   const float* tw;         // [M * top_k] router weights
-  __nv_bfloat16* act;      // workspace [num_ids, I]
-  float* part1;            // workspace [H / 128, num_ids, 2I]: k-split partials of gate_up (H > 128)
-  float* part2;            // workspace [I / 128, num_ids, H]: k-split partials of down (I > 128)
-  float* rows;             // workspace [num_ids, H]: weighted fp32 slot rows before the top-k sum
+  float* xpart;            // workspace [LAYER_MAXREM, grid, 32, 256]: gate_up partials of split pairs
+  float* part2;            // workspace [I / 128, num_ids, H]: down partials per k-slice
   float* out_rows;         // caller's fp32 rows [num_ids, H] instead of the top-k sum (or null)
   __nv_bfloat16* out;      // caller's bf16 [M, H] top-k sums (or null)
-  int* ctr;                // persistent int32 state: counters and ready stamps (zeroed once)
+  int* ctr;                // persistent int32 state: epoch, barrier and arrival counters, exchange flags (zeroed once)
   int* err;                // device error word
   uint64_t timeout_ns;
   int M, top_k, num_ids, E, H, I;
-  int off_cnt1, off_ready, off_cnt2, off_tok, off_epoch, off_done, off_ep;  // int offsets into ctr
+  int off_epoch, off_done, off_ep, off_xflag;  // int offsets into ctr
   // Expert-parallel receive side (ep_peer non-null, out and out_rows null): x / ids / tw are this rank's receive
   // buffers of the peer-memory exchange (row s * ep_mcap + p came from rank s), the kernel waits for the receive
   // flags before routing, and each row's fp32 sum of its local slots goes to the same row of this rank's own back
@@ -156,7 +156,6 @@ struct LayerParams {
   int32_t* ep_pos;
   __nv_bfloat16* ep_out;
   int ep_M, ep_E;
-  int tail;  // 1: items past the last whole wave of units may use a finer k-split (up to one per stage)
   // Fused router (logits non-null): every CTA routes the M tokens itself from the router logits [M, E] (fp32, or bf16
   // when logits_bf16): softmax, top_k, renormalised when renorm; ids and tw are not read, and CTA 0 writes the
   // routing to ids_out / w_out (when non-null) for the caller.

@@ -4,47 +4,43 @@
 // The layer's data is small next to the latencies of a launch: a decode batch touches ~40 experts (about 60 MB of
 // packed weights), which one B200 streams in ~10 us, while a launch boundary costs a few microseconds of pipeline
 // drain and refill. So the steps that the reference runs as separate kernels (files/mbx_moek.py:252-289: moe_align,
-// the gate_up GEMM, SwiGLU, the down GEMM, the top-k sum) run here inside one grid of persistent CTAs (two per SM)
-// that stream the two weight matrices back to back:
+// the gate_up GEMM, SwiGLU, the down GEMM, the top-k sum) run here inside one grid of persistent CTAs (two per SM).
 //
-//   routing   every CTA sorts the batch's (expert, slot) keys in shared memory at start-up: blocks = the distinct
-//             valid experts in ascending order, each with its slots in ascending order (moe_align's order,
-//             files/mbx_moek.cu:32-140), an expert with more than XR slots cut into blocks of XR (its weights are
-//             then streamed once per block: XR <= 32 keeps two CTAs on every SM for any batch); no global
-//             workspace and no separate launch.
-//   units     gate_up units (block, 256-row item, k-split) and then down units (block, item, k-split), dealt
-//             round-robin over the CTAs in that order: a CTA runs its gate_up units first, and the CTAs that got
-//             fewer of those start streaming down weights early. Items beyond the last whole wave of units get a
-//             finer k-split (PhasePlan), so that a phase does not end with a few CTAs running one more long unit.
-//   producer  warp 8: per 64-k stage, the 8 KB of packed codes (lane 0) and the 1056-byte packed-scale run pair
-//             (lane 1) by bulk copy (cp.async.bulk, no multicast) into a ring slot. It never waits on another CTA:
-//             the weights of every unit are known once the routing is.
-//   act warp  warp 9: the stage's activation rows. gate_up: the tokens' hidden rows by bulk copy; down: the act rows
-//             of the block, once the gate_up item that produced those act columns is complete in every CTA (one
-//             ready stamp per (block, item, consumer warp), acquire-loaded by eight lanes at once with a bounded
-//             wait), by plain loads into the slot.
+// Work plan. A block is a run of at most XR routed slots of one expert (moe_align's blocks); a pair is (block,
+// gate_up item t): item t's 256 weight rows (128 gate rows and their up partners) give the block's act columns
+// [128 t, 128 t + 128), which are exactly the k-slice t of the down GEMM. So a pair's work needs no other pair's:
+//   share     the CTAs of a pair (G of them, 1 <= G <= 8) each stream 1/G of item t's k-range (gate_up) and, once
+//             the pair's act is known, 1/G of the down items over k-slice t; with G > 1 the shares exchange their
+//             fp32 gate_up partials through global memory (they run at the same time: a short wait) and each forms
+//             the same act from them in share order;
+//   waves     pairs are dealt to CTAs in whole waves of one CTA each; the pairs left over after the last whole wave
+//             are split over the CTAs (G > 1) in one or two more positions, which run first (all CTAs start
+//             together, so the partners of a split pair arrive together), so that every CTA streams about the same
+//             number of stages and no CTA ever waits for a unit of a later position;
+//   down      each share writes its fp32 partial rows of k-slice t (plain stores); after a grid barrier every CTA sums
+//             a slice of the outputs: per token, per valid slot in slot order, w * (sum of the k-slices in order),
+//             then the slots in order, rounded once to bf16 (the fp32 oracle's order, bench/moek/problem.py:51-67).
+// The plan is a function of the number of blocks and the grid only, so every call with the same routing gives the
+// same bits.
+//
+// Roles of a CTA (per 128-k stage = one 16 KB bulk copy of packed codes + a 1056-byte packed-scale run pair):
+//   producer  warp 8: decodes the CTA's units (the unit list of the plan, two metadata rounds in flight) and issues
+//             the stage copies (cp.async.bulk, no multicast) into a ring slot. It never waits on another CTA.
+//   act warp  warp 9: gate_up stages: the block's hidden rows by bulk copy; down stages read the act buffer in shared
+//             memory and need nothing.
 //   scales    warp 10: per stage the scale byte of each k-group x run position (base + 4-bit offset, then the
-//             exceptions), in the packed run's own position order; per unit the {B B, R R} table of the expert
-//             (moek_common.cuh).
-//   consumers warps 0-7: the swap-AB mma.sync m16n8k16 of moek_decode.cu (weights = the 16-row A operand, up to 8
-//             tokens = B), fp32 accumulators per unit; they wait on the scale warp's barrier only (it has waited for
-//             the slot's copies itself).
-//   finishing gate_up: with one k-split the lane holds gate and up of the same column and writes
-//             act = bf16(silu(gate) * up); with more, fp32 partials go to the workspace and the warp whose arrival
-//             completes (block, item, warp) adds them in split order, then releases that warp's ready stamp.
-//             down: partials likewise, then the router weight: fp32 row w * sum; the
-//             arrival that completes a token's valid slots for (item, warp) adds the token's rows in slot order and
-//             rounds once to bf16 (the fp32 oracle's order, bench/moek/problem.py:51-67).
+//             exceptions); per table change the {B B, R R} table of the expert (moek_common.cuh).
+//   consumers warps 0-7: swap-AB mma.sync m16n8k16 (weights = the 16-row A operand, up to 8 tokens = B), fp32
+//             accumulators per unit.
 //
-// Counters reset themselves (the completing arrival zeroes its counter); ready stamps carry a launch epoch, so the
-// workspace is zeroed once at allocation and never between launches. Every wait is bounded (%globaltimer); a CTA
-// whose wait expires records MOEK_DEV_TIMEOUT and winds down; the workspace must then be zeroed again.
+// Every wait is bounded (%globaltimer); a CTA whose wait expires records MOEK_DEV_TIMEOUT and winds down; the state
+// buffer must then be zeroed again. The exchange flags and the grid barrier carry a launch epoch, so the state is
+// zeroed once at allocation and never between launches.
 //
-// Co-residency: a down unit may wait on a gate_up unit of any CTA, and every CTA runs all of its gate_up units
-// before any down unit, so the grid makes progress whenever all its CTAs are resident at once: the launcher sizes
-// the grid to the occupancy the kernel reaches (cudaOccupancyMaxActiveBlocksPerMultiprocessor x SMs) and launches it
-// as a cooperative grid, so that the runtime starts it only with every CTA resident, also while kernels of other
-// streams hold part of the GPU.
+// Co-residency: the shares of a pair and the grid barrier wait on other CTAs, so the launcher sizes the grid to the
+// occupancy the kernel reaches (cudaOccupancyMaxActiveBlocksPerMultiprocessor x SMs) and launches it as a cooperative
+// grid, so that the runtime starts it only with every CTA resident, also while kernels of other streams hold part of
+// the GPU.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -68,23 +64,26 @@ constexpr int LBK = 2 * BK;                  // k per pipeline stage: one packed
 constexpr int LSTAGE = 2 * STAGE_BYTES;      // 16 KB of packed codes per (item, stage): one bulk copy
 constexpr int X_STRIDE = LBK * 2 + 16;       // bytes per activation row in a slot (+16: conflict-free reads)
 constexpr int SC_BYTES = ITEM_COLS * KG;     // scale table of a stage: one byte per (weight row, k-group)
-constexpr int NLUT = 4;  // per-unit {B B, R R} tables in flight: a unit's table is written once its first stage has
-                         // landed, when the consumers have released every stage of the unit NLUT units before
-constexpr int MAXU = 8;         // units per metadata round (a CTA has about U / grid units; more take more rounds)
+constexpr int NLUT = 4;  // {B B, R R} tables in flight (>= ring slots: a table is rewritten only once the consumers
+                         // have released every stage of the NLUT tables before it; each table spans >= 1 stage)
+constexpr int MAXU = 8;  // units per metadata round; two rounds in flight
+constexpr int LUT_NEW = 1 << 30;  // UnitMeta::lut: the unit starts a new table
 
+// A unit: ph 0 = a gate_up share, item `item`'s 128-k stages [st0, st0 + nst); ph 1 = a down run, items
+// [item, item + nst) each over the 128-k stage st0 (the pair's k-slice). Stage j of a unit is (unit_item(j),
+// unit_kstage(j)).
 struct UnitMeta {
-  int ph, blk, item, ks, e, nv, flags;  // ph: 0 = gate_up, 1 = down; flags: 2 = block has more rows than XR
-  int st0, st1, ns;                     // the unit's stages [st0, st1) of its item, the item's k-split count
+  int ph, blk, item, st0, nst;
+  int e, nv, flags;  // expert, valid rows (<= XR), 2 = block has more rows than XR
+  int lut;           // table index (| LUT_NEW when the scale warp writes it at this unit)
+  int pos, G, s, cta0;  // remainder position (-1: a whole wave), shares of the pair, this share, first CTA
+  __device__ __forceinline__ int unit_item(int j) const { return ph ? item + j : item; }
+  __device__ __forceinline__ int unit_kstage(int j) const { return ph ? st0 : st0 + j; }
 };
 
-// Units of one phase: items (block, 256-row item) in order, each cut into k-splits. The first ni_main items use the
-// caller's split; when those units would spill a few items past a whole number of waves of the grid, the remaining
-// items use the finest whole-stage split that still fits them in one more wave, so the phase ends about one short
-// unit after the last full wave instead of one full unit (the idea of stream-K, with no fix-up beyond the split-k
-// arrivals the kernel has anyway).
 // v / d for 0 <= v < 2^22 and 1 <= d < 2^10, without the long dependent chain of an integer division: a quotient
 // estimate from the approximate fp32 reciprocal (relative error about 2^-23, so the estimate is off by at most one)
-// and one correction each way. The unit plan and the unit decode divide by runtime values on the start-up path.
+// and one correction each way. The plan and the unit decode divide by runtime values on the start-up path.
 __device__ __forceinline__ int div_small(int v, int d) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"((float)d));
@@ -94,31 +93,84 @@ __device__ __forceinline__ int div_small(int v, int d) {
   return q;
 }
 
-struct PhasePlan {
-  int ni_main, s_main, s_tail, u_main, u_total;  // at most 512 blocks x 16 items x 32 splits: 32-bit
+// The pair plan: `nfull` whole waves of one CTA per pair, then up to LAYER_MAXREM positions whose pairs are split
+// over G CTAs each (pairs [first, first + cnt) on CTAs [0, cnt x G)).
+struct PairPlan {
+  int npairs, nfull, nrem;
+  int first[LAYER_MAXREM], cnt[LAYER_MAXREM], G[LAYER_MAXREM];
 };
-__device__ __forceinline__ PhasePlan plan_phase(const LayerMat& m, int nblk, int grid, bool tail) {
-  PhasePlan q;
-  const int ni = nblk * m.nt;
-  q.s_main = q.s_tail = m.nsplit;
-  q.ni_main = ni;
-  const int main_units = ni * m.nsplit;
-  if (tail && main_units > grid) {
-    const int nim = div_small(div_small(main_units, grid) * grid, m.nsplit);
-    const int rem = ni - nim;
-    int st = m.nsplit;  // the finest whole-stage split (a divisor of nstage, precomputed) that fits the grid
-    for (uint64_t dm = m.divmask >> (m.nsplit + 1) << (m.nsplit + 1); dm; dm &= dm - 1) {
-      const int s = __ffsll((long long)dm) - 1;
-      if (rem * s <= grid) st = s;
+__device__ __forceinline__ int fit_shares(int r, int C, int gmax) {  // the most shares per pair r pairs fit in C
+  return max(1, min(gmax, div_small(C, r)));
+}
+// nt1 gate_up items (= down k-slices), nst1 gate_up stages per item, nt2 down items; C CTAs. The pairs left over
+// after the whole waves either all take one position (G shares each, as many as fit), or floor(C / G') of them take
+// G' > G shares and the rest a second position, whichever ends sooner (the longest share: its gate_up stages plus
+// its down items). Written into q (shared memory) by one thread.
+__device__ __forceinline__ void plan_pairs(PairPlan* q, int nblk, int nt1, int nst1, int nt2, int C) {
+  const int npairs = nblk * nt1, nfull = div_small(npairs, C);
+  q->npairs = npairs;
+  q->nfull = nfull;
+  q->nrem = 0;
+  const int gmax = min(8, min(nst1, nt2));
+  const int R = npairs - nfull * C, i0 = nfull * C;
+  if (R > 0) {
+    auto cost = [&](int g) { return div_small(nst1 + g - 1, g) + div_small(nt2 + g - 1, g); };
+    const int G = fit_shares(R, C, gmax);
+    int best = cost(G), gb = 0, nb = 0, g2 = 0;
+    for (int g = G + 1; g <= gmax; g++) {
+      const int n1 = div_small(C, g);
+      if (n1 <= 0 || n1 >= R) continue;
+      const int gg = fit_shares(R - n1, C, gmax), c2 = cost(g) + cost(gg);
+      if (c2 < best) best = c2, gb = g, nb = n1, g2 = gg;
     }
-    if (rem > 0 && st > m.nsplit) {
-      q.ni_main = nim;
-      q.s_tail = st;
+    if (gb) {
+      q->first[0] = i0, q->cnt[0] = nb, q->G[0] = gb;
+      q->first[1] = i0 + nb, q->cnt[1] = R - nb, q->G[1] = g2;
+      q->nrem = 2;
+    } else {
+      q->first[0] = i0, q->cnt[0] = R, q->G[0] = G;
+      q->nrem = 1;
     }
   }
-  q.u_main = q.ni_main * q.s_main;
-  q.u_total = q.u_main + (ni - q.ni_main) * q.s_tail;
-  return q;
+}
+// Units of CTA c: two per remainder position where it holds a share and per whole wave (the gate_up share, then the
+// down run). The split positions come first: their shares wait on one another, and at the start every CTA begins
+// at the same time, so the partners of a pair arrive together.
+__device__ __forceinline__ int cta_units(const PairPlan* q, int c) {
+  int n = 2 * q->nfull;
+  for (int i = 0; i < q->nrem; i++) n += c < q->cnt[i] * q->G[i] ? 2 : 0;
+  return n;
+}
+// Unit j of CTA c (C CTAs).
+__device__ __forceinline__ void cta_unit(const PairPlan* q, int nt1, int nst1, int nt2, int c, int C, int j,
+                                         UnitMeta& u) {
+  int pair = 0, w = j >> 1;
+  u.pos = -1, u.G = 1, u.s = 0, u.cta0 = c;
+  for (int i = 0; i < q->nrem; i++) {
+    const int G = q->G[i];
+    if (c >= q->cnt[i] * G) continue;
+    if (w == 0) {
+      const int pr = div_small(c, G);
+      pair = q->first[i] + pr;
+      u.pos = i, u.G = G, u.s = c - pr * G, u.cta0 = pr * G;
+      break;
+    }
+    w--;
+  }
+  if (u.pos < 0) pair = w * C + c;
+  u.blk = div_small(pair, nt1);
+  const int t = pair - u.blk * nt1;
+  if ((j & 1) == 0) {
+    u.ph = 0;
+    u.item = t;
+    u.st0 = div_small(nst1 * u.s, u.G);
+    u.nst = div_small(nst1 * (u.s + 1), u.G) - u.st0;
+  } else {
+    u.ph = 1;
+    u.item = div_small(nt2 * u.s, u.G);
+    u.nst = div_small(nt2 * (u.s + 1), u.G) - u.item;
+    u.st0 = t;
+  }
 }
 
 template <int XR>
@@ -126,20 +178,22 @@ struct Cfg {
   static constexpr int X_OFF = LSTAGE + PAIR_BYTES;
   static constexpr int SC_OFF = X_OFF + XR * X_STRIDE;
   static constexpr int SLOT = SC_OFF + SC_BYTES;
-  static constexpr int NS = XR <= 16 ? 4 : 3;  // ring slots: two CTAs per SM (XR <= 32)
-  static constexpr int META_OFF = NS * SLOT;
-  static constexpr int IDS_OFF = META_OFF + MAXU * (int)sizeof(UnitMeta);
-  static constexpr int LUT_OFF = IDS_OFF + MAXU * XR * 4;
+  static constexpr int NS = XR <= 8 ? 4 : 3;  // ring slots: two CTAs per SM
+  static constexpr int ACT_OFF = NS * SLOT;   // the pair's act rows [XR, 128] bf16, X_STRIDE apart (down's B operand)
+  static constexpr int META_OFF = ACT_OFF + XR * X_STRIDE;
+  static constexpr int IDS_OFF = META_OFF + 2 * MAXU * (int)sizeof(UnitMeta);
+  static constexpr int LUT_OFF = IDS_OFF + 2 * MAXU * XR * 4;
   static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 8;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
   static constexpr int TOK_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;  // the batch's slots: sid[], stw[]
   static constexpr int MISC_OFF = TOK_OFF + 2 * LAYER_MAXIDS * 4;
-  static constexpr int PLAN_OFF = MISC_OFF + 16;  // the two phase plans
-  static constexpr int BAR_OFF = (PLAN_OFF + 2 * (int)sizeof(PhasePlan) + 7) / 8 * 8;
-  static constexpr int SMEM = BAR_OFF + (3 * NS + 2) * 8;
+  static constexpr int PLAN_OFF = MISC_OFF + 16;
+  static constexpr int BAR_OFF = (PLAN_OFF + (int)sizeof(PairPlan) + 7) / 8 * 8;
+  static constexpr int SMEM = BAR_OFF + (3 * NS + 4) * 8;
   static constexpr int T = XR / 8;
   static constexpr int MINB = 2;
-  static_assert(XR <= 32, "two CTAs per SM");
+  static_assert(XR <= 32, "at most 32 rows per block");
   static_assert(2 * LAYER_MAXIDS * 4 <= SLOT, "routing scratch fits in ring slot 0");
+  static_assert(XR > 16 || 2 * SMEM + 2048 <= 228 * 1024, "two CTAs per SM (32-row blocks: one)");
 };
 
 __device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -166,29 +220,19 @@ __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
-
-// Bounded wait of a whole warp until the NCW ready stamps of a (block, item) all read `want`: lane L polls stamp
-// L % NCW (acquire loads, all eight in parallel), then a warp barrier orders every lane's later loads after all the
-// acquires (the consumer warps released their stamps after writing their act columns). Between polls the warp sleeps
-// briefly, leaving the issue slots to the consumers.
-__device__ __forceinline__ bool wait_stamps(const int* stamps, int want, uint64_t deadline, int* err,
-                                            volatile int* abort_flag) {
-  const int* st = stamps + (threadIdx.x & 31) % NCW;
-  bool seen = false;
-  for (uint32_t i = 0;; i++) {
-    if (*abort_flag) return false;
-    if (!seen) seen = ld_acquire(st) == want;
-    if (__all_sync(0xffffffffu, seen)) {
-      __syncwarp();
-      return true;
-    }
-    if ((i & 63) == 63 && globaltimer() > deadline) {
-      report(err, MOEK_DEV_TIMEOUT);
-      *abort_flag = 1;
-      return false;
-    }
-    __nanosleep(32);
-  }
+// The same barrier, returning whether v was set in any consumer thread (every consumer warp gets the same answer, so
+// they all take the same path through the barriers that follow).
+__device__ __forceinline__ bool consumer_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\n"
+      "setp.ne.u32 p, %1, 0;\n"
+      "bar.red.or.pred q, 1, %2, p;\n"
+      "selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(NCW * 32)
+      : "memory");
+  return r != 0;
 }
 
 // Raise, on every rank s, s's back flag for this rank to this call's number (all of this rank's returned rows are
@@ -204,62 +248,37 @@ __device__ __forceinline__ int ep_dispatch_ctas(const LayerParams& p) {
   return max(1, min((int)gridDim.x / p.ep_world, p.ep_M));
 }
 
-__device__ __forceinline__ void decode_unit(const LayerParams& p, const PhasePlan& q0, const PhasePlan& q1, int u,
-                                            UnitMeta& um) {
-  um.ph = u >= q0.u_total ? 1 : 0;
-  const LayerMat& m = p.m[um.ph];
-  const PhasePlan& q = um.ph ? q1 : q0;
-  const int v = um.ph ? u - q0.u_total : u;
-  int ii;
-  if (v < q.u_main) {
-    ii = div_small(v, q.s_main);
-    um.ks = v - ii * q.s_main;
-    um.ns = q.s_main;
-  } else {
-    const int w = v - q.u_main;
-    const int t = div_small(w, q.s_tail);
-    ii = q.ni_main + t;
-    um.ks = w - t * q.s_tail;
-    um.ns = q.s_tail;
-  }
-  um.blk = div_small(ii, m.nt);
-  um.item = ii - um.blk * m.nt;
-  const int su = div_small(m.nstage, um.ns);
-  um.st0 = um.ks * su;
-  um.st1 = um.st0 + su;
-}
-
 template <int XR>
 __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(LayerParams p) {
   using C = Cfg<XR>;
   extern __shared__ __align__(128) uint8_t smem[];
-  UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);
-  int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);
-  uint2* lut = reinterpret_cast<uint2*>(smem + C::LUT_OFF);  // per unit: scale byte -> {B B, R R} (moek_common.cuh)
+  UnitMeta* meta = reinterpret_cast<UnitMeta*>(smem + C::META_OFF);  // [2][MAXU]
+  int* mids = reinterpret_cast<int*>(smem + C::IDS_OFF);             // [2][MAXU][XR]
+  uint2* lut = reinterpret_cast<uint2*>(smem + C::LUT_OFF);  // per table: scale byte -> {B B, R R} (moek_common.cuh)
   int* srow = reinterpret_cast<int*>(smem + C::ROUTE_OFF);
   int* bexp = srow + LAYER_MAXIDS;
   int* bstart = bexp + LAYER_MAXIDS;
-  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);  // [0] blocks, [1] valid slots, [2] abort,
-                                                                              // [3] rows returned (expert-parallel)
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);  // [0] blocks, [1] valid slots, [2] abort
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::NS;
   uint64_t* scaled = empty + C::NS;
-  uint64_t* mfull = scaled + C::NS;
-  uint64_t* mempty = mfull + 1;
+  uint64_t* mfull = scaled + C::NS;  // [2]
+  uint64_t* mempty = mfull + 2;      // [2]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   volatile int* abort_flag = misc + 2;
 
   if (tid == 0) {
     misc[1] = 0;
     misc[2] = 0;
-    misc[3] = 0;
     for (int i = 0; i < C::NS; i++) {
       mbar_init(full + i, 2);  // the producer's and the act warp's arrivals (each with its byte count)
       mbar_init(empty + i, NCW);
       mbar_init(scaled + i, 32);
     }
-    mbar_init(mfull, 32);
-    mbar_init(mempty, NCW + 2);  // consumers, scale warp, act warp
+    for (int i = 0; i < 2; i++) {
+      mbar_init(mfull + i, 32);
+      mbar_init(mempty + i, NCW + 2);  // consumers, scale warp, act warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -364,18 +383,6 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       skey[r] = kk[h];
     }
     if (tid == 0) MOEK_TR_CLK(42);
-    if (p.ep_peer) {  // rows with at least one valid slot: the rows this rank returns (p.M * k <= 512)
-      int rows = 0;
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int t = tid + h * THREADS;
-        bool any = false;
-        if (t < p.M)
-          for (int j = 0; j < k; j++) any |= key[t * k + j] != 0xFFFFFFFFu;
-        rows += __syncthreads_count(any);
-      }
-      if (tid == 0) misc[3] = rows;
-    }
     __syncthreads();
     if (warp == 0) {  // blocks: one starts where the expert changes, and after every XR rows of the same expert
       int base = 0, run0 = 0;  // run0: where the expert run that reaches into this chunk started
@@ -404,52 +411,65 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         MOEK_TR_CLK(43);
         bstart[base] = nvalid;
         misc[0] = base;
-      }
-      if (lane < 2) {  // the two phases' plans, once per CTA, one lane each (every thread reads them after the barrier)
         const int nb = *abort_flag ? 0 : base;
-        reinterpret_cast<PhasePlan*>(smem + C::PLAN_OFF)[lane] = plan_phase(p.m[lane], nb, gridDim.x, p.tail);
-        if (lane == 0) MOEK_TR_CLK(44);
+        plan_pairs(reinterpret_cast<PairPlan*>(smem + C::PLAN_OFF), nb, p.m[0].nt, p.m[0].nstage, p.m[1].nt,
+                   gridDim.x);
+        MOEK_TR_CLK(44);
       }
     }
     __syncthreads();
   }
-  const int nblk = *abort_flag ? 0 : misc[0];
-  const int ep_rows = misc[3];
   if (tid == 0) MOEK_TR(3);
   if (tid == 0) MOEK_TR_CLK(45);
-  if (p.ep_peer && ep_rows == 0 && !*abort_flag && blockIdx.x == 0 && tid == 0)
-    ep_signal(p, ep_call);  // nothing to return: release the senders' waits at once
 
-
-  const PhasePlan plan0 = reinterpret_cast<const PhasePlan*>(smem + C::PLAN_OFF)[0],
-                  plan1 = reinterpret_cast<const PhasePlan*>(smem + C::PLAN_OFF)[1];
-  const int U = plan0.u_total + plan1.u_total;
-  const int n_mine = U > (int)blockIdx.x ? (U - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const PairPlan* plan = reinterpret_cast<const PairPlan*>(smem + C::PLAN_OFF);
+  const int nt1 = p.m[0].nt, nst1 = p.m[0].nstage, nt2 = p.m[1].nt, nst2 = p.m[1].nstage;
+  const int n_mine = cta_units(plan, blockIdx.x);
   const int rounds = (n_mine + MAXU - 1) / MAXU;
   if (tid == 0) MOEK_TR_VAL(7, n_mine);
+  if (tid == 0) MOEK_TR_CLK(53);
 
   if (warp == W_PROD) {  // ------------------------------------------------------------------------- producer
     uint32_t g = 0;
     bool ok = true;
+    int lut_cur = -1, prev_key = -1;  // the last table index and its (phase, expert)
     for (int r = 0; r < rounds && ok; r++) {
-      const int u0 = r * MAXU, nu = min(MAXU, n_mine - u0);
-      if (r > 0 && !wait_or_abort(mempty, (r - 1) & 1, deadline, p.err, abort_flag)) break;
-      for (int i = lane; i < nu; i += 32) {
-        UnitMeta& m = meta[i];
-        decode_unit(p, plan0, plan1, (int)blockIdx.x + (u0 + i) * (int)gridDim.x, m);
-        m.e = bexp[m.blk];
-        const int b0 = bstart[m.blk], cnt = bstart[m.blk + 1] - b0;
-        m.nv = min(cnt, XR);
-        m.flags = cnt > XR ? 2 : 0;
-        for (int rr = 0; rr < m.nv; rr++) mids[i * XR + rr] = srow[b0 + rr];
+      const int b = r & 1, u0 = r * MAXU, nu = min(MAXU, n_mine - u0);
+      UnitMeta* mb = meta + b * MAXU;
+      int* ib = mids + b * MAXU * XR;
+      if (r >= 2 && !wait_or_abort(mempty + b, ((r - 2) >> 1) & 1, deadline, p.err, abort_flag)) break;
+      UnitMeta um;
+      int key = -1, b0 = 0;
+      if (lane < nu) {
+        cta_unit(plan, nt1, nst1, nt2, blockIdx.x, gridDim.x, u0 + lane, um);
+        um.e = bexp[um.blk];
+        b0 = bstart[um.blk];
+        const int cnt = bstart[um.blk + 1] - b0;
+        um.nv = min(cnt, XR);
+        um.flags = cnt > XR ? 2 : 0;
+        key = (um.ph << 24) | um.e;
       }
+      if (lane == 0 && r == 0) MOEK_TR_CLK(54);
+      // table indices: a new {B B, R R} table wherever (phase, expert) changes from the unit before
+      const int kprev = __shfl_up_sync(0xffffffffu, key, 1);
+      const bool isnew = lane < nu && key != (lane == 0 ? prev_key : kprev);
+      const uint32_t nbits = __ballot_sync(0xffffffffu, isnew);
+      if (lane < nu) {
+        um.lut = (lut_cur + __popc(nbits & ((2u << lane) - 1u))) | (isnew ? LUT_NEW : 0);
+        mb[lane] = um;
+        for (int rr = 0; rr < um.nv; rr++) ib[lane * XR + rr] = srow[b0 + rr];
+      }
+      lut_cur += __popc(nbits);
+      prev_key = __shfl_sync(0xffffffffu, key, nu - 1);
       __syncwarp();
-      mbar_arrive(mfull);  // units, experts and rows published
+      if (lane == 0 && r == 0) MOEK_TR_CLK(55);
+      mbar_arrive(mfull + b);  // units, experts and rows published
       for (int ci = 0; ci < nu && ok; ci++) {
-        const LayerMat& mt = p.m[meta[ci].ph];
-        const int e = meta[ci].e, item = meta[ci].item;
-        for (int st = meta[ci].st0; st < meta[ci].st1; st++, g++) {
-          const int slot = g % C::NS;
+        const UnitMeta& m = mb[ci];
+        const LayerMat& mt = p.m[m.ph];
+        const int e = m.e;
+        for (int j = 0; j < m.nst; j++, g++) {
+          const int slot = g % C::NS, st = m.unit_kstage(j), item = m.unit_item(j);
           if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag)) {
             ok = false;
             break;
@@ -461,7 +481,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             const int64_t wi = (((int64_t)e * mt.nt + item) * mt.nstage + st) * 2;
             bulk_g2s(dst, mt.W + wi * STAGE_BYTES, LSTAGE, full + slot);
             if (g == 0) MOEK_TR(4);
-            if (r == 0 && ci == 0 && st - meta[0].st0 < 8) MOEK_TR_CLK(112 + st - meta[0].st0);
+            if (r == 0 && ci == 0 && j < 8) MOEK_TR_CLK(112 + j);
           } else if (lane == 1) {
             const int64_t si = ((int64_t)e * mt.nt + item) * mt.nstage + st;
             bulk_g2s(dst + LSTAGE, mt.SP + si * PAIR_BYTES, PAIR_BYTES, full + slot);
@@ -473,106 +493,103 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   } else if (warp == W_ACT) {  // ----------------------------------------------------------------------- act warp
     uint32_t g = 0;
     bool ok = true;
-    int n_wait = 0;  // act waits so far (the first four are stamped in MOEK_TRACE builds)
     for (int r = 0; r < rounds && ok; r++) {
-      const int nu = min(MAXU, n_mine - r * MAXU);
-      if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
+      const int b = r & 1, nu = min(MAXU, n_mine - r * MAXU);
+      const UnitMeta* mb = meta + b * MAXU;
+      if (!wait_or_abort(mfull + b, (r >> 1) & 1, deadline, p.err, abort_flag)) break;
       for (int ci = 0; ci < nu && ok; ci++) {
-        const UnitMeta& m = meta[ci];
+        const UnitMeta& m = mb[ci];
         const int nv = m.nv;
-        const int* ids = mids + ci * XR;
-        int ready_item = -1;
-        for (int st = m.st0; st < m.st1; st++, g++) {
-          const int slot = g % C::NS;
+        const int* ids = mids + (b * MAXU + ci) * XR;
+        for (int j = 0; j < m.nst; j++, g++) {
+          const int slot = g % C::NS, st = m.unit_kstage(j);
           if (g >= C::NS && !wait_or_abort(empty + slot, ((g / C::NS) - 1) & 1, deadline, p.err, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* xs = smem + slot * C::SLOT + C::X_OFF;
-          if (m.ph == 0) {  // hidden rows of the block's tokens, 64 k each, by bulk copy
+          if (m.ph == 0) {  // hidden rows of the block's tokens, 128 k each, by bulk copy
+            uint8_t* xs = smem + slot * C::SLOT + C::X_OFF;
             if (lane == 0) mbar_expect_tx(full + slot, nv * LBK * 2);
             __syncwarp();
             for (int rr = lane; rr < nv; rr += 32)
               bulk_g2s(xs + rr * X_STRIDE, p.x + (int64_t)(ids[rr] / k) * p.H + st * LBK, LBK * 2, full + slot);
-            if (lane == 0 && r == 0 && ci == 0 && st - m.st0 < 8) MOEK_TR_CLK(120 + st - m.st0);
-          } else {  // act rows: columns [128 st, 128 st + 128) are gate_up item st's (ITEM_COLS / 2 act columns)
-            const int need = st;
-            if (need != ready_item) {
-              if (lane == 0 && n_wait < 4) MOEK_TR(56 + 2 * n_wait);
-              if (!wait_stamps(p.ctr + p.off_ready + (m.blk * p.m[0].nt + need) * NCW, epoch + 1, deadline, p.err,
-                               abort_flag)) {
-                ok = false;
-              }
-              if (lane == 0 && n_wait < 4) MOEK_TR(57 + 2 * n_wait);
-              n_wait++;
-              ok = __all_sync(0xffffffffu, ok);
-              if (!ok) break;
-              ready_item = need;
-            }
-            for (int idx = lane; idx < nv * 16; idx += 32) {
-              const int rr = idx >> 4, c = idx & 15;
-              const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.act + (int64_t)ids[rr] * p.I + st * LBK) + c);
-              *reinterpret_cast<uint4*>(xs + rr * X_STRIDE + c * 16) = v;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(full + slot);
+            if (lane == 0 && r == 0 && ci == 0 && j < 8) MOEK_TR_CLK(120 + j);
+          } else if (lane == 0) {  // down: the act rows are in shared memory already
+            mbar_arrive(full + slot);
           }
+          __syncwarp();
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(mempty);
+      if (lane == 0) mbar_arrive(mempty + b);
     }
   } else if (warp == W_SCALE) {  // -------------------------------------------------------------------- scale warp
-    // Per unit: the expert's global scale and the unit's exception offsets (lane j: run j's first entry) and entries
-    // (up to 64 held in registers, two per lane), loaded by all lanes at once and one unit ahead, so that no stage
-    // waits on a chain of global loads. Per stage: the slot's scale table in run-position order, one byte per
-    // (k-group, run, position) at kg * 256 + run * 128 + position (the consumers map their rows to positions), then
-    // the run's exceptions. Lane L decodes chunk L % 16 (8 positions) of run L / 16 of the pair: eight 8-byte stores,
-    // no byte shuffling, so that the single scale warp keeps ahead of the consumers.
-    uint32_t g = 0, kq = 0;
+    // Per unit: the expert's global scale and each stage's exception run [a, b) of the kit's list (lane j: stage j's
+    // run), loaded by all lanes at once and one unit ahead, then the unit's entries (up to 64 held in registers, two
+    // per lane, numbered across the unit's runs in stage order), so that no stage waits on a chain of global loads.
+    // Per stage: the slot's scale table in run-position order, one byte per (k-group, run, position) at
+    // kg * 256 + run * 128 + position (the consumers map their rows to positions), then the run's exceptions. Lane L
+    // decodes chunk L % 16 (8 positions) of run L / 16 of the pair: eight 8-byte stores, no byte shuffling, so that
+    // the single scale warp keeps ahead of the consumers.
+    uint32_t g = 0;
     const int run = lane >> 4, ch = lane & 15;
     bool ok = true;
     for (int r = 0; r < rounds && ok; r++) {
-      const int nu = min(MAXU, n_mine - r * MAXU);
-      if (!wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag)) break;
-      int ro_n = 0, end_n = 0;
+      const int b = r & 1, nu = min(MAXU, n_mine - r * MAXU);
+      const UnitMeta* mb = meta + b * MAXU;
+      if (!wait_or_abort(mfull + b, (r >> 1) & 1, deadline, p.err, abort_flag)) break;
+      int ra_n = 0, rb_n = 0;
       float g_n = 0.f;
       auto fetch = [&](int ui) {  // loads only; consumed one unit later
-        const UnitMeta& m = meta[ui];
+        const UnitMeta& m = mb[ui];
         const LayerMat& mt = p.m[m.ph];
-        const int nruns = m.st1 - m.st0;
-        const int64_t key0 = ((int64_t)m.e * mt.nt + m.item) * mt.nstage + m.st0;
-        ro_n = lane < nruns ? mt.exc_off[key0 + lane] : 0;
-        end_n = mt.exc_off[key0 + nruns];
+        if (lane < m.nst) {
+          const int64_t key = ((int64_t)m.e * mt.nt + m.unit_item(lane)) * mt.nstage + m.unit_kstage(lane);
+          ra_n = mt.exc_off[key];
+          rb_n = mt.exc_off[key + 1];
+        } else {
+          ra_n = rb_n = 0;
+        }
         g_n = mt.G[m.e];
       };
       if (nu > 0) fetch(0);
       for (int ui = 0; ui < nu && ok; ui++) {
-        const UnitMeta& m = meta[ui];
+        const UnitMeta& m = mb[ui];
         const LayerMat& mt = p.m[m.ph];
-        const int su = m.st1 - m.st0;
-        const int o0 = __shfl_sync(0xffffffffu, ro_n, 0);
-        const int ro = ro_n - o0, cnt = end_n - o0;
+        const int ra = ra_n, len = rb_n - ra_n;
+        int pre = len;  // exclusive prefix of the runs' lengths: stage j's entries are numbered [pre_j, pre_j + len_j)
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, pre, o);
+          if (lane >= o) pre += v;
+        }
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        pre -= len;
         const float gsc = g_n;
-        const uint32_t* eg = mt.exc_ent + o0;
-        const uint32_t ex0 = lane < cnt ? eg[lane] : 0u, ex1 = lane + 32 < cnt ? eg[lane + 32] : 0u;
+        // entry number L of the unit: in the run of the last stage whose first number is <= L
+        auto entry = [&](int L) -> uint32_t {
+          int a = 0, p0 = 0;
+          for (int jj = 0; jj < m.nst; jj++) {
+            const int pj = __shfl_sync(0xffffffffu, pre, jj), aj = __shfl_sync(0xffffffffu, ra, jj);
+            if (pj <= L) a = aj, p0 = pj;
+          }
+          return L < total ? mt.exc_ent[a + L - p0] : 0u;
+        };
+        const uint32_t ex0 = entry(lane), ex1 = entry(lane + 32);
         if (ui + 1 < nu) fetch(ui + 1);
-        uint2* lt = lut + (kq % NLUT) * 256;
-        kq++;
-        const int r0g = m.ph == 0 ? m.item : 2 * m.item;  // global run index of the pair's first run
-        const int r1g = m.ph == 0 ? mt.nt + m.item : r0g + 1;  // and of its second (gate_up: the up rows' run)
-        for (int st = m.st0; st < m.st1; st++, g++) {
-          const int slot = g % C::NS;
+        uint2* lt = lut + ((m.lut & 0xFFFF) % NLUT) * 256;
+        for (int j = 0; j < m.nst; j++, g++) {
+          const int slot = g % C::NS, item = m.unit_item(j);
           if (!wait_or_abort(full + slot, (g / C::NS) & 1, deadline, p.err, abort_flag)) {
             ok = false;
             break;
           }
-          if (lane == 0 && r == 0 && ui == 0 && st - m.st0 < 8) MOEK_TR_CLK(96 + st - m.st0);
-          if (st == m.st0) {  // the unit's table: its slot's previous unit is done (the first stage has landed)
+          if (lane == 0 && r == 0 && ui == 0 && j < 8) MOEK_TR_CLK(96 + j);
+          if (j == 0 && (m.lut & LUT_NEW)) {  // a new table: its slot's previous table is no longer read
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-              const ScaleBR br = scale_br(lane + 32 * j, gsc);
-              lt[lane + 32 * j] = make_uint2(br.b2, br.r2);
+            for (int jj = 0; jj < 8; jj++) {
+              const ScaleBR br = scale_br(lane + 32 * jj, gsc);
+              lt[lane + 32 * jj] = make_uint2(br.b2, br.r2);
             }
           }
           const uint8_t* runp = smem + slot * C::SLOT + LSTAGE + run * RUN_BYTES;
@@ -585,10 +602,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
                 make_uint2((q & 0x0F0F0F0Fu) + b4, ((q >> 4) & 0x0F0F0F0Fu) + b4);
           }
           __syncwarp();
-          // this stage's run: entries [eo0, eo1) of the unit's list overwrite their bytes
-          const int rr = st - m.st0;
-          const int eo0 = __shfl_sync(0xffffffffu, ro, rr);
-          const int eo1 = rr + 1 < su ? __shfl_sync(0xffffffffu, ro, rr + 1) : cnt;
+          // this stage's run: entries [eo0, eo1) of the unit's numbering overwrite their bytes
+          const int eo0 = __shfl_sync(0xffffffffu, pre, j);
+          const int eo1 = eo0 + __shfl_sync(0xffffffffu, len, j), aj = __shfl_sync(0xffffffffu, ra, j);
+          const int r0g = m.ph == 0 ? item : 2 * item;           // global run index of the pair's first run
+          const int r1g = m.ph == 0 ? mt.nt + item : r0g + 1;    // and of its second (gate_up: the up rows' run)
           auto patch = [&](uint32_t en) {
             const int ppos = en & 0xFFFF, kg = (en >> 16) & 0xFF;
             if (!MOEK_CHECK(kg < KG && ((ppos >> 7) == r0g || (ppos >> 7) == r1g), p.err)) return;
@@ -596,30 +614,30 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           };
           if (lane >= eo0 && lane < eo1) patch(ex0);
           if (lane + 32 >= eo0 && lane + 32 < eo1) patch(ex1);
-          for (int j = max(eo0, 64) + lane; j < eo1; j += 32) patch(eg[j]);  // long lists: the rest from memory
+          for (int L = max(eo0, 64) + lane; L < eo1; L += 32) patch(mt.exc_ent[aj + L - eo0]);  // long runs
           __syncwarp();
           mbar_arrive(scaled + slot);
-          if (lane == 0 && r == 0 && ui == 0 && st - m.st0 < 8) MOEK_TR_CLK(104 + st - m.st0);
+          if (lane == 0 && r == 0 && ui == 0 && j < 8) MOEK_TR_CLK(104 + j);
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(mempty);
+      if (lane == 0) mbar_arrive(mempty + b);
     }
   } else {  // ------------------------------------------------------------------------------------------ consumers
     const int gq = lane >> 2, c = lane & 3;
     const int w_off = ((((c >> 1) ^ (gq >> 2)) & 1) << 4) | ((c & 1) << 3);  // k-group c's bytes in a 32-byte row
-    const int I = p.I, H = p.H;
-    uint32_t g = 0, kq = 0;
+    const int H = p.H;
+    __nv_bfloat16* act_s = reinterpret_cast<__nv_bfloat16*>(smem + C::ACT_OFF);
+    uint32_t g = 0;
     for (int r = 0; r < rounds; r++) {
-      const int nu = min(MAXU, n_mine - r * MAXU);
-      wait_or_abort(mfull, r & 1, deadline, p.err, abort_flag);
-      consumer_sync();
-      const bool have_meta = !*abort_flag;
+      const int b = r & 1, nu = min(MAXU, n_mine - r * MAXU);
+      const UnitMeta* mb = meta + b * MAXU;
+      wait_or_abort(mfull + b, (r >> 1) & 1, deadline, p.err, abort_flag);
+      const bool have_meta = !consumer_sync_or(*abort_flag);
       for (int ui = 0; ui < nu && have_meta; ui++) {
-        const UnitMeta& m = meta[ui];
-        const LayerMat& mt = p.m[m.ph];
-        const int ph = m.ph, item = m.item, ks = m.ks, nv = m.nv, blk = m.blk, ns = m.ns;
-        const int* ids = mids + ui * XR;
+        const UnitMeta& m = mb[ui];
+        const int ph = m.ph, nv = m.nv;
+        const int* ids = mids + (b * MAXU + ui) * XR;
         if ((m.flags & 2) && tid == 0) report(p.err, MOEK_DEV_TOO_MANY_ROWS);
         // the warp's two 16-row groups of the item (gate_up: gate group w and its up partner w + 8)
         const int G0 = ph == 0 ? warp : 2 * warp, G1 = ph == 0 ? warp + 8 : 2 * warp + 1;
@@ -627,30 +645,26 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         // the scale-table offsets (run * 128 + position) of the lane's four rows
         auto tpos = [](int r) { return (r & 128) + slot_position(r & 127); };
         const int p00 = tpos(slot00), p01 = tpos(slot00 + 8), p10 = tpos(slot10), p11 = tpos(slot10 + 8);
-        const uint2* lt = lut + (kq % NLUT) * 256;
-        kq++;
+        const uint2* lt = lut + ((m.lut & 0xFFFF) % NLUT) * 256;
         const int ntile = (nv + 7) >> 3;
-        // one accumulator chain per (row group, tile): every block size adds the same terms in the same order, so
-        // the rows per block never change the results (more chains per tile measured no faster: the consumers are
-        // bound by issue slots, not by the MMA chain)
-        constexpr int NH = 1;
-        float acc[NH][2][C::T][4];
+        // one accumulator chain per (row group, tile) and gate_up share or down item
+        float acc[2][C::T][4];
 #pragma unroll
-        for (int h = 0; h < NH; h++)
+        for (int i = 0; i < 2; i++)
 #pragma unroll
-          for (int i = 0; i < 2; i++)
+          for (int t = 0; t < C::T; t++)
 #pragma unroll
-            for (int t = 0; t < C::T; t++)
-#pragma unroll
-              for (int v = 0; v < 4; v++) acc[h][i][t][v] = 0.f;
+            for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
         bool ok = true;
         const int tu = r * MAXU + ui;  // the unit's index among this CTA's (timeline stamps)
         bool ready = false;  // the next stage's scales were seen published while this stage was computed
-        for (int st = m.st0; st < m.st1; st++, g++) {
+        // down: this share's fp32 partials of k-slice st0, one item per stage (summed after the grid barrier)
+        float* dbase = p.part2 + ((int64_t)m.st0 * n) * H;
+        for (int j = 0; j < m.nst; j++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
-          const bool stamp = tid == 0 && tu == 0 && st - m.st0 < 8;
-          if (stamp) MOEK_TR_CLK(64 + st - m.st0);
+          const bool stamp = tid == 0 && tu == 0 && j < 8;
+          if (stamp) MOEK_TR_CLK(64 + j);
           // one wait: the scale warp arrives on `scaled` only after its own wait on `full` (weights, scales and
           // activations of the slot landed), so the consumers' acquire of `scaled` orders their reads after those
           // writes as well. Usually the test made during the previous stage already saw the phase complete, and the
@@ -660,17 +674,19 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             continue;  // stay in step with the other roles' counters
           }
           ready = false;
-          if (stamp) MOEK_TR_CLK(80 + st - m.st0);
-          if (tid == 0 && st == m.st0 && tu < 8) {
+          if (stamp) MOEK_TR_CLK(80 + j);
+          if (tid == 0 && j == 0 && tu < 8) {
             MOEK_TR(8 + 3 * tu);
-            MOEK_TR_VAL(32 + tu, (ph << 28) | (blk << 16) | (item << 8) | ks);
+            MOEK_TR_VAL(32 + tu, (ph << 28) | (m.blk << 16) | (m.item << 8) | m.s);
           }
+          // B operand rows: gate_up the slot's hidden rows, down the pair's act rows
+          const uint8_t* xrows = ph == 0 ? smem + slot * C::SLOT + C::X_OFF : smem + C::ACT_OFF;
 #pragma unroll
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
-          if (hf == 1 && st + 1 < m.st1)  // test the next stage's scales (its latency hides behind this half's math)
+          if (hf == 1 && j + 1 < m.nst)  // test the next stage's scales (its latency hides behind this half's math)
             ready = mbar_test(scaled + (g + 1) % C::NS, ((g + 1) / C::NS) & 1);
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
-          const uint8_t* sx = smem + slot * C::SLOT + C::X_OFF + hf * BK * 2;
+          const uint8_t* sx = xrows + hf * BK * 2;
           const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + (4 * hf + c) * 256;  // k-group 4 hf + c
           const uint2 s0a = lt[sc[p00]], s0b = lt[sc[p01]], s1a = lt[sc[p10]], s1b = lt[sc[p11]];
           // the tiles' activation fragments of this half, shared by both row groups (loaded once here for one-tile
@@ -707,7 +723,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               for (int t = 0; t < C::T; t++) {
                 if (C::T == 1 || t < ntile) {  // a unit has at least one row: one-tile blocks need no test
                   const uint4& xv = xf[t][J >> 1];
-                  mma_16816(acc[hf % NH][i][t], A, (J & 1) ? xv.z : xv.x, (J & 1) ? xv.w : xv.y);
+                  mma_16816(acc[i][t], A, (J & 1) ? xv.z : xv.x, (J & 1) ? xv.w : xv.y);
                 }
               }
             };
@@ -719,27 +735,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(empty + slot);
-          if (stamp) MOEK_TR_CLK(88 + st - m.st0);
-        }
-        ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
-        if (!ok) continue;
-        if (tid == 0 && tu < 8) MOEK_TR(9 + 3 * tu);
-        if constexpr (NH == 2) {
-#pragma unroll
-          for (int i = 0; i < 2; i++)
-#pragma unroll
-            for (int t = 0; t < C::T; t++)
-#pragma unroll
-              for (int v = 0; v < 4; v++) acc[0][i][t][v] += acc[NH - 1][i][t][v];
-        }
-
-        // ------------------------------------------------------------------------------------------ finishing
-        // acc[0][i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
-        const int N = mt.N;
-        if (ph == 0) {
-          const int nt1 = mt.nt;
-          bool complete = ns == 1;
-          if (complete) {  // gate row and up row + 128 share the column: act straight from the accumulators
+          if (stamp) MOEK_TR_CLK(88 + j);
+          if (ph == 1) {  // this stage's item done: its partial rows, then a fresh accumulator for the next item
+            // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
+            float* base = dbase + 256 * m.unit_item(j);
 #pragma unroll
             for (int t = 0; t < C::T; t++) {
               if (t >= ntile) break;
@@ -747,64 +746,34 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               for (int v = 0; v < 2; v++) {
                 const int row = t * 8 + 2 * c + v;
                 if (row >= nv) continue;
-#pragma unroll
-                for (int h = 0; h < 2; h++)
-                  p.act[(int64_t)ids[row] * I + 128 * item + slot00 + 8 * h] =
-                      __float2bfloat16_rn(silu(acc[0][0][t][2 * h + v]) * acc[0][1][t][2 * h + v]);
-              }
-            }
-          } else {
-            float* base = p.part1 + (int64_t)ks * n * N;
-#pragma unroll
-            for (int t = 0; t < C::T; t++) {
-              if (t >= ntile) break;
-#pragma unroll
-              for (int v = 0; v < 2; v++) {
-                const int row = t * 8 + 2 * c + v;
-                if (row >= nv) continue;
-                float* prow = base + (int64_t)ids[row] * N;
+                float* prow = base + (int64_t)ids[row] * H;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                  prow[128 * item + slot00 + 8 * h] = acc[0][0][t][2 * h + v];
-                  prow[I + 128 * item + slot00 + 8 * h] = acc[0][1][t][2 * h + v];
+                  prow[slot00 + 8 * h] = acc[0][t][2 * h + v];
+                  prow[slot10 + 8 * h] = acc[1][t][2 * h + v];
                 }
               }
             }
-            __threadfence();
-            __syncwarp();
-            int old = 0;
-            int* cn = p.ctr + p.off_cnt1 + ((int64_t)blk * nt1 + item) * NCW + warp;
-            if (lane == 0) old = atomicAdd(cn, 1);
-            old = __shfl_sync(0xffffffffu, old, 0);
-            complete = old == ns - 1;
-            if (complete) {  // every split of (block, item, warp) is in: add them in split order
-              if (lane == 0) *cn = 0;
-              __threadfence();
-              for (int idx = lane; idx < nv * 16; idx += 32) {
-                const int row = idx >> 4, col = 128 * item + 16 * warp + (idx & 15);
-                const float* pr = p.part1 + (int64_t)ids[row] * N;
-                float gs = 0.f, us = 0.f;
-                for (int s2 = 0; s2 < ns; s2++) {
-                  gs += __ldcg(pr + (int64_t)s2 * n * N + col);
-                  us += __ldcg(pr + (int64_t)s2 * n * N + I + col);
-                }
-                p.act[(int64_t)ids[row] * I + col] = __float2bfloat16_rn(silu(gs) * us);
-              }
-            }
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+              for (int t = 0; t < C::T; t++)
+#pragma unroll
+                for (int v = 0; v < 4; v++) acc[i][t][v] = 0.f;
           }
-          if (complete) {  // this warp's act columns of (block, item) are written: its ready stamp
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) st_release(p.ctr + p.off_ready + ((int64_t)blk * nt1 + item) * NCW + warp, epoch + 1);
-          }
+        }
+        const bool good = __all_sync(0xffffffffu, ok) && !*abort_flag;
+        if (tid == 0 && tu < 8) MOEK_TR(9 + 3 * tu);
+        if (ph == 1) {
           if (tid == 0 && tu < 8) MOEK_TR(10 + 3 * tu);
           continue;
         }
-        // down: weighted fp32 rows of (block, item), then the token sums
-        const int nt2 = mt.nt;
-        float* rows = p.out_rows ? p.out_rows : p.rows;
-        bool complete = ns == 1;
-        if (complete) {
+
+        // --------------------------------------------------------------------------- gate_up finishing: the act
+        // the pair's act columns [16 w, 16 w + 16) of this warp into the act buffer
+        // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
+        consumer_sync();  // every warp is done reading the previous pair's act rows
+        if (good && m.G == 1) {  // gate row and up row + 128 share the column: act straight from the accumulators
 #pragma unroll
           for (int t = 0; t < C::T; t++) {
             if (t >= ntile) break;
@@ -812,17 +781,14 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             for (int v = 0; v < 2; v++) {
               const int row = t * 8 + 2 * c + v;
               if (row >= nv) continue;
-              const int id = ids[row];
-              const float w = stw[id];
 #pragma unroll
-              for (int h = 0; h < 2; h++) {
-                rows[(int64_t)id * H + 256 * item + slot00 + 8 * h] = w * acc[0][0][t][2 * h + v];
-                rows[(int64_t)id * H + 256 * item + slot10 + 8 * h] = w * acc[0][1][t][2 * h + v];
-              }
+              for (int h = 0; h < 2; h++)
+                act_s[row * (X_STRIDE / 2) + slot00 + 8 * h] =
+                    __float2bfloat16_rn(silu(acc[0][t][2 * h + v]) * acc[1][t][2 * h + v]);
             }
           }
-        } else {
-          float* base = p.part2 + (int64_t)ks * n * N;
+        } else if (good) {  // G shares: exchange the fp32 partials, every share forms the act from all of them
+          float* mine = p.xpart + ((int64_t)m.pos * gridDim.x + blockIdx.x) * XR * ITEM_COLS;
 #pragma unroll
           for (int t = 0; t < C::T; t++) {
             if (t >= ntile) break;
@@ -830,100 +796,147 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             for (int v = 0; v < 2; v++) {
               const int row = t * 8 + 2 * c + v;
               if (row >= nv) continue;
-              float* prow = base + (int64_t)ids[row] * N + 256 * item;
 #pragma unroll
               for (int h = 0; h < 2; h++) {
-                prow[slot00 + 8 * h] = acc[0][0][t][2 * h + v];
-                prow[slot10 + 8 * h] = acc[0][1][t][2 * h + v];
+                mine[row * ITEM_COLS + slot00 + 8 * h] = acc[0][t][2 * h + v];
+                mine[row * ITEM_COLS + slot10 + 8 * h] = acc[1][t][2 * h + v];
               }
             }
           }
-          __threadfence();
           __syncwarp();
-          int old = 0;
-          int* cn = p.ctr + p.off_cnt2 + ((int64_t)blk * nt2 + item) * NCW + warp;
-          if (lane == 0) old = atomicAdd(cn, 1);
-          old = __shfl_sync(0xffffffffu, old, 0);
-          complete = old == ns - 1;
-          if (complete) {
-            if (lane == 0) *cn = 0;
-            __threadfence();
-            const int col = 256 * item + 32 * warp + lane;  // the warp's 32 output columns: one per lane
-            for (int row = 0; row < nv; row++) {
-              const int id = ids[row];
-              const float* pr = p.part2 + (int64_t)id * N + col;
-              float s = 0.f;
-              for (int s2 = 0; s2 < ns; s2++) s += __ldcg(pr + (int64_t)s2 * n * N);
-              rows[(int64_t)id * H + col] = stw[id] * s;
+          int* flags = p.ctr + p.off_xflag + (int64_t)m.pos * LAYER_XFLAG_CTAS * NCW;
+          // the warp's partials (ordered before lane 0's release by the warp barrier) before its flag
+          if (lane == 0) st_release(flags + blockIdx.x * NCW + warp, epoch + 1);
+          // the partners' partials of this warp's columns (lane s polls share s; bounded)
+          bool seen = lane >= m.G || lane == m.s;
+          for (uint32_t it = 0;; it++) {
+            if (!seen) seen = ld_acquire(flags + (m.cta0 + lane) * NCW + warp) == epoch + 1;
+            if (__all_sync(0xffffffffu, seen)) break;
+            if ((it & 63) == 63 && globaltimer() > deadline) {
+              if (lane == 0) {
+                report(p.err, MOEK_DEV_TIMEOUT);
+                *abort_flag = 1;
+              }
+              break;
+            }
+            __nanosleep(32);
+          }
+          __syncwarp();
+          if (!*abort_flag) {
+            const float* part0 = p.xpart + ((int64_t)m.pos * gridDim.x + m.cta0) * XR * ITEM_COLS;
+            for (int idx = lane; idx < nv * 16; idx += 32) {
+              const int row = idx >> 4, col = 16 * warp + (idx & 15);
+              float gs = 0.f, us = 0.f;
+              for (int s2 = 0; s2 < m.G; s2++) {
+                const float* pr = part0 + ((int64_t)s2 * XR + row) * ITEM_COLS;
+                gs += __ldcg(pr + col);
+                us += __ldcg(pr + ITEM_COLS / 2 + col);
+              }
+              act_s[row * (X_STRIDE / 2) + col] = __float2bfloat16_rn(silu(gs) * us);
             }
           }
         }
+        consumer_sync();  // the act buffer holds the pair's act rows
         if (tid == 0 && tu < 8) MOEK_TR(10 + 3 * tu);
-        if (!complete || p.out_rows) continue;
-        __threadfence();
-        __syncwarp();
-        // each row's token: the arrival that completes the token's valid slots for (item, warp) adds them in order
-        const int col = 256 * item + 32 * warp + lane;
-        int pieces = 0;  // expert-parallel: (token, item, warp) sums written to the senders' back buffers
-        for (int row = 0; row < nv; row++) {
-          const int tk = ids[row] / k;
-          const int ej = lane < k ? sid[tk * k + lane] : -1;
-          const int nslots = __popc(__ballot_sync(0xffffffffu, ej >= 0 && ej < p.E));
-          int o2 = 0;
-          int* tc = p.ctr + p.off_tok + ((int64_t)tk * nt2 + item) * NCW + warp;
-          if (lane == 0) o2 = atomicAdd(tc, 1);
-          o2 = __shfl_sync(0xffffffffu, o2, 0);
-          if (o2 != nslots - 1) continue;
-          if (lane == 0) *tc = 0;
-          __threadfence();
-          float o = 0.f;
-          for (int sl = 0; sl < k; sl++) {
-            const int ejs = sid[tk * k + sl];
-            if (ejs < 0 || ejs >= p.E) continue;
-            o += __ldcg(rows + (int64_t)(tk * k + sl) * H + col);
-          }
-          if (p.ep_peer) {  // fp32 partial of the row into its sender's back buffer, over NVLink
-            // the row's partial into its sender's segment of this rank's own back buffer (the sender reads it)
-            float* back = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peer[p.ep_rank]) + p.ep_back_off);
-            back[(int64_t)tk * H + col] = o;
-            pieces++;
-          } else {
-            p.out[(int64_t)tk * H + col] = __float2bfloat16_rn(o);
-          }
-        }
-        if (pieces) {  // the arrival that completes every returned row raises the senders' back flags
-          __syncwarp();
-          if (lane == 0) {
-            // the partials are in this GPU's memory: a device-scope release orders them before the arrival, and the
-            // last arrival's system-scope release stores of the flags carry them to the senders
-            __threadfence();
-            const int want = ep_rows * p.m[1].nt * NCW;
-            if (atomicAdd(p.ctr + p.off_ep, pieces) + pieces == want) {
-              p.ctr[p.off_ep] = 0;
-              __threadfence();
-              ep_signal(p, ep_call);
-            }
-          }
-        }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(mempty);
+      if (lane == 0) mbar_arrive(mempty + b);
     }
     if (tid == 0) MOEK_TR(5);
   }
 
-  // tokens with no valid slot get a zero output row (nothing else writes them): the last CTA, which has the fewest
-  // units, once its own work is done, so that no CTA starts streaming late
-  if (blockIdx.x == gridDim.x - 1 && p.out && warp < NCW) {
-    for (int t = warp; t < p.M; t += NCW) {
-      const int e = lane < k ? sid[t * k + lane] : -1;
-      if (__any_sync(0xffffffffu, e >= 0 && e < p.E)) continue;
-      for (int c = lane; c < p.H; c += 32) p.out[(int64_t)t * p.H + c] = __float2bfloat16_rn(0.f);
+  // ------------------------------------------------------------------------------------------- grid barrier
+  // every CTA's down partials are written: the last CTA to arrive advances the launch epoch, every CTA waits for it
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(p.ctr + p.off_done, 1) == (int)gridDim.x - 1) {
+      p.ctr[p.off_done] = 0;
+      __threadfence();
+      atomicAdd(p.ctr + p.off_epoch, 1);
+    }
+    for (uint32_t it = 0;; it++) {
+      if (ld_acquire(p.ctr + p.off_epoch) != epoch) break;
+      if ((it & 63) == 63 && globaltimer() > deadline) {
+        report(p.err, MOEK_DEV_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      __nanosleep(64);
+    }
+    MOEK_TR(51);
+    // fused exchange: every CTA has read this call's number, so the call can be recorded as this rank's current one
+    if (p.ep_x && blockIdx.x == 0) *p2p_call(p.ep_q) = ep_call;
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------------------------ the top-k sums, a slice each
+  // out[t] = bf16(sum over valid slots j in order of w_j * (sum over k-slices in order of the down partials)); with
+  // out_rows the weighted slot rows instead; expert-parallel: the fp32 sum into this rank's back buffer. One output
+  // element per thread, the loads of up to 8 slots x 2 k-slices issued together.
+  {
+    float* back = p.ep_peer ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peer[p.ep_rank]) +
+                                                      p.ep_back_off)
+                            : nullptr;
+    const int64_t nout = (int64_t)p.M * p.H, sstride = (int64_t)n * p.H;
+    for (int64_t i = (int64_t)blockIdx.x * THREADS + tid; i < nout; i += (int64_t)gridDim.x * THREADS) {
+      const int tk = (int)(i / p.H), col = (int)(i - (int64_t)tk * p.H);
+      float o = 0.f;
+      for (int j0 = 0; j0 < k; j0 += 8) {
+        bool val[8];
+        float sj[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          const int e = j0 + jj < k ? sid[tk * k + j0 + jj] : -1;
+          val[jj] = e >= 0 && e < p.E;
+          sj[jj] = 0.f;
+        }
+        for (int t0 = 0; t0 < nst2; t0 += 2) {
+          float v[8][2];
+#pragma unroll
+          for (int jj = 0; jj < 8; jj++)
+#pragma unroll
+            for (int u = 0; u < 2; u++)
+              v[jj][u] = val[jj] && t0 + u < nst2
+                             ? __ldcg(p.part2 + (t0 + u) * sstride + (int64_t)(tk * k + j0 + jj) * p.H + col)
+                             : 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 8; jj++)
+#pragma unroll
+            for (int u = 0; u < 2; u++)
+              if (val[jj] && t0 + u < nst2) sj[jj] += v[jj][u];
+        }
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          if (!val[jj]) continue;
+          const int sl = tk * k + j0 + jj;
+          const float y = __fmul_rn(stw[sl], sj[jj]);  // rounded like a stored slot row (no contraction)
+          if (p.out_rows) p.out_rows[(int64_t)sl * p.H + col] = y;
+          o += y;
+        }
+      }
+      if (p.out) p.out[i] = __float2bfloat16_rn(o);
+      if (back) back[i] = o;
+    }
+  }
+  if (tid == 0) MOEK_TR(52);
+
+  if (p.ep_peer) {  // every returned row is written: the last CTA raises the senders' back flags
+    __syncthreads();
+    if (tid == 0) {
+      // the partials are in this GPU's memory: a device-scope release orders them before the arrival, and the last
+      // arrival's system-scope release stores of the flags carry them to the senders
+      __threadfence();
+      if (atomicAdd(p.ctr + p.off_ep, 1) == (int)gridDim.x - 1) {
+        p.ctr[p.off_ep] = 0;
+        __threadfence();
+        ep_signal(p, ep_call);
+      }
     }
   }
 
-  // fused exchange: once every owner's partials of this rank's tokens are written, the last CTAs (the ones with the
-  // fewest units) sum them into the output, a slice each
+  // fused exchange: once every owner's partials of this rank's tokens are written, the last CTAs sum them into the
+  // output, a slice each
   if (p.ep_x) {
     const int total = p.ep_M * (p.H / 4), ncta = min((int)gridDim.x, (total + THREADS - 1) / THREADS);
     const int cta = (int)gridDim.x - 1 - (int)blockIdx.x;
@@ -941,20 +954,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       if (tid == 0) MOEK_TR(50);
     }
   }
-
-  // ------------------------------------------------------------------------------------------------ teardown
-  __syncthreads();
   if (tid == 0) MOEK_TR(6);
-  if (tid == 0) {  // the last CTA to finish advances the launch epoch of the ready stamps
-    __threadfence();
-    if (atomicAdd(p.ctr + p.off_done, 1) == (int)gridDim.x - 1) {
-      p.ctr[p.off_done] = 0;
-      __threadfence();
-      atomicAdd(p.ctr + p.off_epoch, 1);
-      // fused exchange: every CTA has read this call's number and unpacked its slice, so the call is complete
-      if (p.ep_x) *p2p_call(p.ep_q) = ep_call;
-    }
-  }
 }
 
 template <int XR>
@@ -966,15 +966,16 @@ static cudaError_t launch_xr(const LayerParams& p, int sms, int coop, cudaStream
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moek_layer_kernel<XR>, THREADS, C::SMEM);
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorLaunchOutOfResources;
-  const int grid = std::min(occ, C::MINB) * sms;  // every CTA resident at once (down units wait on gate_up units)
+  // every CTA resident at once (shares of a pair and the grid barrier wait on other CTAs)
+  const int grid = std::min(std::min(occ, C::MINB) * sms, LAYER_XFLAG_CTAS);
   if (!coop) {
     e = launch_pdl(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
-  // cooperative: the runtime guarantees that all CTAs are resident together (down units wait on gate_up units of
-  // other CTAs), whatever else runs on the GPU. With programmatic serialisation too where the runtime takes both;
-  // if it refuses the pair (a launch-configuration error, reported before anything runs), cooperative alone.
+  // cooperative: the runtime guarantees that all CTAs are resident together, whatever else runs on the GPU. With
+  // programmatic serialisation too where the runtime takes both; if it refuses the pair (a launch-configuration
+  // error, reported before anything runs), cooperative alone.
   static std::atomic<int> coop_pdl{1};
   if (coop_pdl.load(std::memory_order_relaxed)) {
     e = launch_coop(moek_layer_kernel<XR>, dim3(grid), dim3(THREADS), C::SMEM, st, 1, p);

@@ -90,7 +90,9 @@ def summarize(t: np.ndarray, kind: int) -> dict:
         # routing, SM cycles from the dependent-launch wait: keys built, counted, ranked, blocks cut, plans, published
         r0 = t[:, 39]
         rt = {}
-        for name, sl in (("keys", 40), ("counted", 41), ("ranked", 42), ("blocks", 43), ("plans", 44), ("published", 45)):
+        for name, sl in (("keys", 40), ("counted", 41), ("ranked", 42), ("blocks", 43), ("plans", 44), ("published", 45),
+                         ("units counted", 53), ("producer: units decoded", 54), ("unit rows published", 55),
+                         ("first copy", 112)):
             ok = (r0 > 0) & (t[:, sl] > 0)
             if ok.any():
                 rt[name] = round(float(np.median(t[ok, sl] - r0[ok])) / CLOCK_GHZ / 1e3, 2)

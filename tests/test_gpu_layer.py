@@ -99,9 +99,9 @@ def test_layer_kernel_matches_split_path(monkeypatch):
 @pytest.mark.parametrize("m,e", [(32, 8), (96, 64), (40, 512)])
 def test_layer_kernel_sub_blocks(monkeypatch, m, e):
     """Experts with more routed slots than a block holds are cut into several blocks: every block size (8, 16, 32
-    rows) gives the same bits with the caller's k-splits everywhere (the finer tail split depends on the number of
-    blocks, so it is off for the bit comparison), and every result is within the gate of the oracle (8 experts:
-    about 20 slots per expert at M = 32)."""
+    rows) gives a result within the gate of the oracle (8 experts: about 20 slots per expert at M = 32), the same
+    bits on a repeated call, and results that agree with each other to fp32 summation order (the number of blocks
+    sets how many CTAs share a gate_up item, which changes only the order of its fp32 partial sums)."""
     from qwen38_flash_coder_b200 import _lib
 
     monkeypatch.setattr(ops, "DECODE_MAX_M", 128)  # the whole-layer kernel up to 102 tokens of 5 slots
@@ -109,21 +109,21 @@ def test_layer_kernel_sub_blocks(monkeypatch, m, e):
     layer = prep.PreparedLayer(w13, w2)
     x = synth.activations(m, 2048, 50 + m, device=DEV)
     ids, wts = synth.route_zipf(m, e, 5, 50 + m, device=DEV)
-    outs, tails = [], []
+    outs, again = [], []
     try:
         for rows in (8, 16, 32):
             _lib.call("moek_set_layer_block_rows", rows)
-            tails.append(ops.fused_moe(x, layer, wts, ids))
-            _lib.call("moek_set_layer_tail_split", 0)
             outs.append(ops.fused_moe(x, layer, wts, ids))
-            _lib.call("moek_set_layer_tail_split", 1)
+            again.append(ops.fused_moe(x, layer, wts, ids))
         ops.check_device_errors(DEV)
     finally:
         _lib.call("moek_set_layer_block_rows", 0)
-        _lib.call("moek_set_layer_tail_split", 1)
-    assert all(torch.equal(o, outs[0]) for o in outs[1:])
+    assert all(torch.equal(o, a) for o, a in zip(outs, again))
+    for o in outs[1:]:
+        rel, _, _ = moe_ref.check(o.cpu(), outs[0].float().cpu())
+        assert rel < 2e-3, rel
     ref = _oracle(w13, w2, x, ids, wts)
-    for o in outs[:1] + tails:
+    for o in outs:
         ok, stats = moe_ref.within_gate(o.cpu(), ref)
         assert ok, stats
 
