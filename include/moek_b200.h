@@ -48,10 +48,10 @@ int moek_build_flags(void);
 /* MOEK_TRACE builds: copy the %globaltimer stamps [1024 CTAs][128 slots] (uint64, nanoseconds; 0 = not reached) of
  * the last launches of one kernel family to host memory dst (bytes <= 1 MiB are copied). kind 0: the whole-layer
  * kernel (0 start, 1 after the dependent-launch wait, 2 expert-parallel flags seen, 3 routing done, 4 first weight
- * copy issued, 5 consumers done, 6 end, 7 unit count, 51 grid barrier passed, 52 top-k sums written; per unit u < 8
- * of the CTA: 8 + 3u first stage ready, 9 + 3u last stage done, 10 + 3u finished (gate_up: act in shared memory),
- * 32 + u the unit (phase << 28 | block << 16 | item << 8 | share); the first unit's stages s < 8 in SM clock cycles
- * (clock64): 64 + s consumer warp 0 before its wait, 80 + s data and scales ready, 88 + s done, 96 + s the scale warp
+ * copy issued, 5 consumers done, 6 end, 7 unit count, 47 every role done, 51 grid barrier passed, 52 top-k sums
+ * written; per unit u < 8 of the CTA: 8 + 3u first stage ready, 9 + 3u last stage done, 10 + 3u finished (gate_up:
+ * record published), 32 + u the unit (phase << 28 | block << 16 | item << 8 | first k-stage); the first unit's
+ * stages s < 8 in SM clock cycles (clock64): 64 + s consumer warp 0 before its wait, 80 + s data and scales ready, 88 + s done, 96 + s the scale warp
  * sees the weights, 104 + s it publishes the scales, 112 + s the producer issues the copy, 120 + s the act warp issues
  * its copies; the start-up in SM clock cycles: 39 start, 40 keys built, 41 counted, 42 ranked, 43 blocks cut, 44 plan
  * made, 45 published, 53 units counted, 54 the producer's units decoded, 55 their rows published); kind 1: the
@@ -163,19 +163,21 @@ int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M, int32_t
 
 /* ---- Whole decode layer in one launch. Replaces, for decode batches, the sequence the kit's forward wrap runs
  * (files/mbx_moek.py:236-289: moe_align, gate_up moe_gemm, split epilogue, down moe_gemm, split epilogue + top-k sum)
- * with one persistent kernel: routing in shared memory; per (block, gate_up item) pair, gate_up + SwiGLU into shared
- * memory by one CTA or by G CTAs that exchange fp32 partials, then the down GEMM over that pair's k-slice; after a
- * grid barrier, the router-weighted top-k sums. */
+ * with one persistent kernel: routing in shared memory; the gate_up stages of every (block, gate_up item) pair cut
+ * into equal contiguous ranges, one per CTA, each CTA publishing fp32 partial records; then the down items cut the
+ * same way, each CTA forming a pair's act (SwiGLU) from the pair's records before its down items; after a grid
+ * barrier, the router-weighted top-k sums. */
 
-/* int32 count of the persistent state: launch epoch, barrier and arrival counters, share exchange flags (the
- * arguments are accepted for the geometry but the layout does not depend on them). Zero it once before the first
+/* int32 count of the persistent state: launch epoch, barrier and arrival counters, the gate_up record flags (their
+ * number depends on I only; num_experts and H are accepted for the geometry). Zero it once before the first
  * call; every completed call leaves it valid for the next one (after a device error, zero it again). Calls that share
  * a state buffer must be ordered (one stream). */
 int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n);
 
-/* Scratch bytes of one call: the split pairs' fp32 gate_up partials (two positions x the grid x 32 rows x 256
- * columns) and the fp32 down partials per 128-k slice [I / 128, M * top_k, H]. rows_out is accepted for the earlier
- * layout and changes nothing. Contents need not be preserved between calls. */
+/* Scratch bytes of one call: the fp32 gate_up partial records ((the grid bound 2 x SMs + M * top_k * 2I / 256)
+ * records of block-rows x 256 values, block rows as moek_set_layer_block_rows sets them for this M at the time of the
+ * query and of the call) and the fp32 down partials per 128-k slice [I / 128, M * top_k, H]. rows_out is accepted for
+ * the earlier layout and changes nothing. Contents need not be preserved between calls. */
 int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t nsplit_gate,
                                int32_t nsplit_down, int32_t rows_out, size_t* bytes);
 
@@ -186,19 +188,18 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  *   x       bf16 [M, H]; M * top_k <= 512 (decode batches; larger ones take the moek_gemm path).
  *   w13/sp13/g13/exc_off13/exc_ent13  gate_up in the tiled formats above (N = 2I, K = H); w2.. likewise (N = H,
  *           K = I). H % 256 == 0, I % 128 == 0, both <= 4096.
- *   nsplit_gate, nsplit_down  checked as before (whole 128-k runs) and otherwise unused: the kernel plans its own
- *           split of each gate_up item over 1-8 CTAs from the number of blocks and the grid, which changes only the
+ *   nsplit_gate, nsplit_down  checked as before (whole 128-k runs) and otherwise unused: the kernel cuts the
+ *           gate_up stages over the CTAs itself (from the number of blocks and the grid), which changes only the
  *           order of fp32 partial sums; the same routing always gives the same plan and the same bits.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
 /* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: 8 up to M = 8, else 16).
  * An expert with more routed slots than that is cut into several blocks, its weights streamed once per block.
  * Process-wide; a tuning knob with no effect on the results. */
 int moek_set_layer_block_rows(int32_t rows);
-/* Accepted for callers of the earlier unit plan; no effect (the pair plan splits the pairs left after its whole waves
- * itself). */
+/* Accepted for callers of the earlier unit plan; no effect (the stream-K plan has no tail to split). */
 int moek_set_layer_tail_split(int32_t on);
-/* Whether the whole-layer kernel is launched as a cooperative grid (on != 0, the default). The CTAs that share a
- * gate_up item wait (bounded) on one another's partials and every CTA waits at a grid barrier before the top-k sums,
+/* Whether the whole-layer kernel is launched as a cooperative grid (on != 0, the default). A CTA's down items wait
+ * (bounded) on the gate_up records of other CTAs and every CTA waits at a grid barrier before the top-k sums,
  * so all of its CTAs must be resident at once; a cooperative launch makes the runtime start the grid only when they
  * all are, also while kernels of other streams hold part of the GPU (with on = 0 such a stream could hold CTAs back
  * past the wait bound and the layer would end in MOEK_DEV_TIMEOUT).

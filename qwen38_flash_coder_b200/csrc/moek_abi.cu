@@ -266,24 +266,37 @@ MOEK_API int moek_router_topk(const void* logits, int32_t logits_bf16, int32_t M
 }
 
 // ------------------------------------------------------------------------------------- whole decode layer
-// Persistent int32 state of moek_moe_layer: [epoch, barrier counter, EP arrival counter], then the share exchange
-// flags [LAYER_MAXREM][LAYER_XFLAG_CTAS][consumer warp] (stamped with the launch epoch). The layout depends on
-// nothing, so one zeroed state buffer serves every call of the layer.
+// Persistent int32 state of moek_moe_layer: [epoch, barrier counter, EP arrival counter], then the gate_up record
+// flags [record][consumer warp] (stamped with the launch epoch), for the most records a call of this expert
+// intermediate size can have (layer_max_records at the largest grid and LAYER_MAXIDS slots). One zeroed state buffer
+// serves every call of the layer.
 struct LayerLayout {
   int64_t xflag, total;
 };
-static LayerLayout layer_layout(int32_t, int32_t, int32_t) {
+static LayerLayout layer_layout(int32_t, int32_t, int32_t I) {
   LayerLayout l;
   l.xflag = 3;
-  l.total = l.xflag + (int64_t)moek::LAYER_MAXREM * moek::LAYER_XFLAG_CTAS * moek::LAYER_NCW;
+  l.total = l.xflag + moek::layer_max_records(moek::LAYER_XFLAG_CTAS, moek::LAYER_MAXIDS, I) * moek::LAYER_NCW;
   return l;
 }
-// Workspace: the split pairs' gate_up partials (LAYER_MAXREM positions x the grid x 32 rows x 256 columns, fp32),
-// then the down partials per k-slice [I / 128, num_ids, H] fp32.
-static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, bool) {
+
+// Rows per block of the whole-layer kernel (8, 16 or 32): 8 up to M = 8, else 16, unless set. Above 16 rows, a hot
+// expert's block costs up to four times a cold one's per stage (its rows are more MMA tiles), so 16-row blocks split
+// such an expert into more blocks; the weights of an expert with more than 16 slots are then streamed once per block.
+static int g_layer_rows = 0;
+static int layer_block_rows(int M) {
+  if (g_layer_rows) return g_layer_rows;
+  return M <= 8 ? 8 : 16;
+}
+static int64_t layer_grid_bound() { return std::min<int64_t>(2 * (int64_t)sm_count(), moek::LAYER_XFLAG_CTAS); }
+// Workspace: the gate_up partial records [records][block rows][256] fp32 (record = CTA + pair, sized for the most
+// pairs num_ids slots can form), then the down partials per k-slice [I / 128, num_ids, H] fp32.
+static int64_t layer_rec_bytes(int64_t num_ids, int32_t I, int M) {
+  return moek::layer_max_records(layer_grid_bound(), num_ids, I) * layer_block_rows(M) * moek::ITEM_COLS * 4;
+}
+static int64_t layer_ws_bytes(int64_t num_ids, int32_t H, int32_t I, int M) {
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  const int64_t grid = std::min<int64_t>(2 * (int64_t)sm_count(), moek::LAYER_XFLAG_CTAS);
-  return up((int64_t)moek::LAYER_MAXREM * grid * 32 * moek::ITEM_COLS * 4) + up((int64_t)(I / 128) * num_ids * H * 4);
+  return up(layer_rec_bytes(num_ids, I, M)) + up((int64_t)(I / 128) * num_ids * H * 4);
 }
 
 MOEK_API int moek_layer_state_ints(int32_t num_experts, int32_t H, int32_t I, int64_t* n) {
@@ -296,37 +309,27 @@ MOEK_API int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int
                                         int32_t nsplit_down, int32_t rows_out, size_t* bytes) {
   if (!bytes || M < 0 || top_k <= 0 || H <= 0 || I <= 0 || nsplit_gate < 1 || nsplit_down < 1)
     return fail(MOEK_ERR_ARG, "moek_b200: bad layer workspace query");
-  *bytes = (size_t)layer_ws_bytes((int64_t)M * top_k, H, I, !rows_out);
+  *bytes = (size_t)layer_ws_bytes((int64_t)M * top_k, H, I, M);
   return MOEK_OK;
 }
 
-// Rows per block of the whole-layer kernel (8, 16 or 32): 8 up to M = 8, else 16, unless set. Above 16 rows, a hot
-// expert's block costs up to four times a cold one's per unit and units are dealt round-robin: on B200 at M = 32 with
-// Zipf routing the slowest CTA ended at 133 us with 32-row blocks and at 105 us with 16-row blocks (the weights of an
-// expert with more than 16 slots are then streamed twice).
-static int g_layer_rows = 0;
 MOEK_API int moek_set_layer_block_rows(int32_t rows) {
   if (rows != 0 && rows != 8 && rows != 16 && rows != 32)
     return fail(MOEK_ERR_ARG, "moek_b200: layer block rows must be 8, 16, 32 or 0 (automatic), got %d", rows);
   g_layer_rows = rows;
   return MOEK_OK;
 }
-// Kept for callers of the earlier unit plan: the pair plan splits the pairs left over after its whole waves itself,
-// so there is nothing to switch.
+// Kept for callers of the earlier unit plan: the stream-K plan cuts every CTA's ranges at stage granularity, so
+// there is no tail to split.
 MOEK_API int moek_set_layer_tail_split(int32_t) { return MOEK_OK; }
-// Whether the whole-layer kernel is launched as a cooperative grid (default on): the shares of a pair and its grid
-// barrier wait on other CTAs, so every CTA must be resident at once; a cooperative launch makes the runtime
-// guarantee it.
+// Whether the whole-layer kernel is launched as a cooperative grid (default on): down units wait for the gate_up
+// records of other CTAs and the grid barrier waits for every CTA, so every CTA must be resident at once; a
+// cooperative launch makes the runtime guarantee it.
 static int g_layer_coop = 1;
 MOEK_API int moek_set_layer_cooperative(int32_t on) {
   g_layer_coop = on ? 1 : 0;
   return MOEK_OK;
 }
-static int layer_block_rows(int M) {
-  if (g_layer_rows) return g_layer_rows;
-  return M <= 8 ? 8 : 16;
-}
-
 // Checks and parameters shared by moek_moe_layer and moek_moe_layer_p2p (rows_ws: the fp32 slot rows live in the
 // workspace, i.e. the caller does not take them).
 static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t H, int32_t I, int32_t E,
@@ -356,15 +359,15 @@ static int layer_params(moek::LayerParams& p, const void* x, int32_t M, int32_t 
   const LayerLayout lay = layer_layout(E, H, I);
   if (state_ints < lay.total)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer state needs %lld int32 (zeroed once)", (long long)lay.total);
-  const int64_t ws = layer_ws_bytes(num_ids, H, I, rows_ws);
+  const int64_t ws = layer_ws_bytes(num_ids, H, I, M);
   if ((int64_t)workspace_bytes < ws || !workspace)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_layer needs %lld workspace bytes", (long long)ws);
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
   uint8_t* wp = static_cast<uint8_t*>(workspace);
   p = moek::LayerParams{};
-  const int64_t grid = std::min<int64_t>(2 * (int64_t)sm_count(), moek::LAYER_XFLAG_CTAS);
   p.xpart = reinterpret_cast<float*>(wp);
-  wp += up((int64_t)moek::LAYER_MAXREM * grid * 32 * moek::ITEM_COLS * 4);
+  wp += up(layer_rec_bytes(num_ids, I, M));
+  p.max_records = (int)moek::layer_max_records(layer_grid_bound(), num_ids, I);
   p.part2 = reinterpret_cast<float*>(wp);
   const moek::LayerMat m1{static_cast<const uint8_t*>(w13), sp13, g13, exc_off13,
                           reinterpret_cast<const uint32_t*>(exc_ent13), 2 * I, H, 2 * I / 256, nst1};

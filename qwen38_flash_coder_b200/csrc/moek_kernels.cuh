@@ -109,8 +109,12 @@ struct P2PArgs {  // peer-memory exchange of the fixed-capacity EP path (moek_ep
 };
 // moek_layer.cu: the whole decode-regime layer in one persistent kernel
 constexpr int LAYER_MAXIDS = 512;      // routed slots (tokens x top_k) per call
-constexpr int LAYER_MAXREM = 2;        // positions of split pairs after the whole waves
-constexpr int LAYER_XFLAG_CTAS = 1024; // CTAs of the grid at most (exchange flags per (position, CTA, warp))
+constexpr int LAYER_XFLAG_CTAS = 1024; // CTAs of the grid at most
+// gate_up partial records of one call: one per (CTA, pair) whose ranges meet; record index = CTA + pair, so at most
+// grid + pairs, pairs = blocks x (2I / 256) <= LAYER_MAXIDS x (2I / 256)
+inline int64_t layer_max_records(int64_t grid, int64_t num_ids, int I) {
+  return grid + num_ids * (2 * (int64_t)I / 256);
+}
 constexpr int LAYER_NCW = 8;           // consumer warps per CTA
 struct LayerMat {                  // one weight matrix in this build's layout (gate_up: N = 2I, K = H; down: N = H, K = I)
   const uint8_t* W;
@@ -125,7 +129,7 @@ struct LayerParams {
   const __nv_bfloat16* x;  // [M, H]
   const int32_t* ids;      // [M * top_k] expert per slot (outside [0, E): not routed)
   const float* tw;         // [M * top_k] router weights
-  float* xpart;            // workspace [LAYER_MAXREM, grid, 32, 256]: gate_up partials of split pairs
+  float* xpart;            // workspace [records, XR, 256]: fp32 gate_up partials, record = CTA + pair
   float* part2;            // workspace [I / 128, num_ids, H]: down partials per k-slice
   float* out_rows;         // caller's fp32 rows [num_ids, H] instead of the top-k sum (or null)
   __nv_bfloat16* out;      // caller's bf16 [M, H] top-k sums (or null)
@@ -133,7 +137,8 @@ struct LayerParams {
   int* err;                // device error word
   uint64_t timeout_ns;
   int M, top_k, num_ids, E, H, I;
-  int off_epoch, off_done, off_ep, off_xflag;  // int offsets into ctr
+  int off_epoch, off_done, off_ep, off_xflag;  // int offsets into ctr (xflag: [records][consumer warp])
+  int max_records;                             // records the workspace and the flags hold
   // Expert-parallel receive side (ep_peer non-null, out and out_rows null): x / ids / tw are this rank's receive
   // buffers of the peer-memory exchange (row s * ep_mcap + p came from rank s), the kernel waits for the receive
   // flags before routing, and each row's fp32 sum of its local slots goes to the same row of this rank's own back

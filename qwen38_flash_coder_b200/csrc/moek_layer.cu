@@ -6,28 +6,30 @@
 // drain and refill. So the steps that the reference runs as separate kernels (files/mbx_moek.py:252-289: moe_align,
 // the gate_up GEMM, SwiGLU, the down GEMM, the top-k sum) run here inside one grid of persistent CTAs (two per SM).
 //
-// Work plan. A block is a run of at most XR routed slots of one expert (moe_align's blocks); a pair is (block,
-// gate_up item t): item t's 256 weight rows (128 gate rows and their up partners) give the block's act columns
-// [128 t, 128 t + 128), which are exactly the k-slice t of the down GEMM. So a pair's work needs no other pair's:
-//   share     the CTAs of a pair (G of them, 1 <= G <= 8) each stream 1/G of item t's k-range (gate_up) and, once
-//             the pair's act is known, 1/G of the down items over k-slice t; with G > 1 the shares exchange their
-//             fp32 gate_up partials through global memory (they run at the same time: a short wait) and each forms
-//             the same act from them in share order;
-//   waves     pairs are dealt to CTAs in whole waves of one CTA each; the pairs left over after the last whole wave
-//             are split over the CTAs (G > 1) in one or two more positions, which run first (all CTAs start
-//             together, so the partners of a split pair arrive together), so that every CTA streams about the same
-//             number of stages and no CTA ever waits for a unit of a later position;
-//   down      each share writes its fp32 partial rows of k-slice t (plain stores); after a grid barrier every CTA sums
-//             a slice of the outputs: per token, per valid slot in slot order, w * (sum of the k-slices in order),
-//             then the slots in order, rounded once to bf16 (the fp32 oracle's order, bench/moek/problem.py:51-67).
-// The plan is a function of the number of blocks and the grid only, so every call with the same routing gives the
-// same bits.
+// Work plan (stream-K, two phases). A block is a run of at most XR routed slots of one expert (moe_align's blocks);
+// a pair is (block, gate_up item t): item t's 256 weight rows (128 gate rows and their up partners) give the block's
+// act columns [128 t, 128 t + 128), which are exactly the k-slice t of the down GEMM.
+//   gate_up   the sequence of every pair's 128-k stages (pair-major) is cut into C equal contiguous ranges, one per
+//             CTA; a CTA's range meets a few pairs, and for each it writes its fp32 partial sums (a record: record
+//             index = CTA + pair, unique because both grow along the sequence) and raises one flag per consumer warp
+//             (stamped with the launch epoch). No CTA waits for another in this phase.
+//   down      the sequence of every pair's down items (256 output rows over the pair's k-slice) is cut the same way;
+//             before its first item of a pair a CTA waits for the pair's records (the CTAs whose gate_up ranges met
+//             the pair: at most H / 128 of them), adds them in CTA order and forms the act (SwiGLU, rounded to bf16).
+//             Each item's fp32 partial rows of k-slice t are written with plain stores. A CTA's down pairs are about
+//             the pairs its own gate_up range covered, so the records it waits for are its own and its neighbours',
+//             which finish at about the same time, and the weights of its down items stream in while it waits.
+//   sums      after a grid barrier every CTA sums a slice of the outputs: per token, per valid slot in slot order,
+//             w * (sum of the k-slices in order), then the slots in order, rounded once to bf16 (the fp32 oracle's
+//             order, bench/moek/problem.py:51-67).
+// Every CTA streams the same number of stages (+- 1 per phase), whatever the batch. The plan is a function of the
+// number of blocks and the grid only, so every call with the same routing gives the same bits.
 //
 // Roles of a CTA (per 128-k stage = one 16 KB bulk copy of packed codes + a 1056-byte packed-scale run pair):
 //   producer  warp 8: decodes the CTA's units (the unit list of the plan, two metadata rounds in flight) and issues
 //             the stage copies (cp.async.bulk, no multicast) into a ring slot. It never waits on another CTA.
 //   act warp  warp 9: gate_up stages: the block's hidden rows by bulk copy; down stages read the act buffer in shared
-//             memory and need nothing.
+//             memory (formed by the consumers from the records) and need nothing.
 //   scales    warp 10: per stage the scale byte of each k-group x run position (base + 4-bit offset, then the
 //             exceptions); per table change the {B B, R R} table of the expert (moek_common.cuh).
 //   consumers warps 0-7: swap-AB mma.sync m16n8k16 (weights = the 16-row A operand, up to 8 tokens = B), fp32
@@ -37,7 +39,7 @@
 // buffer must then be zeroed again. The exchange flags and the grid barrier carry a launch epoch, so the state is
 // zeroed once at allocation and never between launches.
 //
-// Co-residency: the shares of a pair and the grid barrier wait on other CTAs, so the launcher sizes the grid to the
+// Co-residency: down units and the grid barrier wait on other CTAs, so the launcher sizes the grid to the
 // occupancy the kernel reaches (cudaOccupancyMaxActiveBlocksPerMultiprocessor x SMs) and launches it as a cooperative
 // grid, so that the runtime starts it only with every CTA resident, also while kernels of other streams hold part of
 // the GPU.
@@ -69,21 +71,21 @@ constexpr int NLUT = 4;  // {B B, R R} tables in flight (>= ring slots: a table 
 constexpr int MAXU = 8;  // units per metadata round; two rounds in flight
 constexpr int LUT_NEW = 1 << 30;  // UnitMeta::lut: the unit starts a new table
 
-// A unit: ph 0 = a gate_up share, item `item`'s 128-k stages [st0, st0 + nst); ph 1 = a down run, items
-// [item, item + nst) each over the 128-k stage st0 (the pair's k-slice). Stage j of a unit is (unit_item(j),
-// unit_kstage(j)).
+// A unit: ph 0 = a gate_up range of pair `pair`: item `item`'s 128-k stages [st0, st0 + nst), written to record
+// `rec`; ph 1 = a down run of pair `pair`: items [item, item + nst) each over the 128-k stage st0 (the pair's k-slice),
+// after the records of CTAs [c0, c1]. Stage j of a unit is (unit_item(j), unit_kstage(j)).
 struct UnitMeta {
   int ph, blk, item, st0, nst;
   int e, nv, flags;  // expert, valid rows (<= XR), 2 = block has more rows than XR
   int lut;           // table index (| LUT_NEW when the scale warp writes it at this unit)
-  int pos, G, s, cta0;  // remainder position (-1: a whole wave), shares of the pair, this share, first CTA
+  int pair, rec, c0, c1;
   __device__ __forceinline__ int unit_item(int j) const { return ph ? item + j : item; }
   __device__ __forceinline__ int unit_kstage(int j) const { return ph ? st0 : st0 + j; }
 };
 
-// v / d for 0 <= v < 2^22 and 1 <= d < 2^10, without the long dependent chain of an integer division: a quotient
+// v / d for 0 <= v < 2^22 and 1 <= d <= 2^10, without the long dependent chain of an integer division: a quotient
 // estimate from the approximate fp32 reciprocal (relative error about 2^-23, so the estimate is off by at most one)
-// and one correction each way. The plan and the unit decode divide by runtime values on the start-up path.
+// and one correction each way.
 __device__ __forceinline__ int div_small(int v, int d) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"((float)d));
@@ -93,85 +95,78 @@ __device__ __forceinline__ int div_small(int v, int d) {
   return q;
 }
 
-// The pair plan: `nfull` whole waves of one CTA per pair, then up to LAYER_MAXREM positions whose pairs are split
-// over G CTAs each (pairs [first, first + cnt) on CTAs [0, cnt x G)).
-struct PairPlan {
-  int npairs, nfull, nrem;
-  int first[LAYER_MAXREM], cnt[LAYER_MAXREM], G[LAYER_MAXREM];
-};
-__device__ __forceinline__ int fit_shares(int r, int C, int gmax) {  // the most shares per pair r pairs fit in C
-  return max(1, min(gmax, div_small(C, r)));
-}
-// nt1 gate_up items (= down k-slices), nst1 gate_up stages per item, nt2 down items; C CTAs. The pairs left over
-// after the whole waves either all take one position (G shares each, as many as fit), or floor(C / G') of them take
-// G' > G shares and the rest a second position, whichever ends sooner (the longest share: its gate_up stages plus
-// its down items). Written into q (shared memory) by one thread.
-__device__ __forceinline__ void plan_pairs(PairPlan* q, int nblk, int nt1, int nst1, int nt2, int C) {
-  const int npairs = nblk * nt1, nfull = div_small(npairs, C);
-  q->npairs = npairs;
-  q->nfull = nfull;
-  q->nrem = 0;
-  const int gmax = min(8, min(nst1, nt2));
-  const int R = npairs - nfull * C, i0 = nfull * C;
-  if (R > 0) {
-    auto cost = [&](int g) { return div_small(nst1 + g - 1, g) + div_small(nt2 + g - 1, g); };
-    const int G = fit_shares(R, C, gmax);
-    int best = cost(G), gb = 0, nb = 0, g2 = 0;
-    for (int g = G + 1; g <= gmax; g++) {
-      const int n1 = div_small(C, g);
-      if (n1 <= 0 || n1 >= R) continue;
-      const int gg = fit_shares(R - n1, C, gmax), c2 = cost(g) + cost(gg);
-      if (c2 < best) best = c2, gb = g, nb = n1, g2 = gg;
-    }
-    if (gb) {
-      q->first[0] = i0, q->cnt[0] = nb, q->G[0] = gb;
-      q->first[1] = i0 + nb, q->cnt[1] = R - nb, q->G[1] = g2;
-      q->nrem = 2;
+// The stream-K plan: S1 = pairs x nst1 gate_up stages cut into C1 = min(C, S1) ranges (so that every range holds at
+// least one stage and at most H / 128 CTAs meet a pair), CTA c < C1's = [floor(c S1 / C1), floor((c + 1) S1 / C1)),
+// CTAs from C1 on have none; S2 = pairs x nt2 down items cut into C ranges the same way. The bounds are evaluated as
+// c q + floor(c r / C) (S = q C + r, c r < 2^20) with the reciprocal-estimate division, so that no thread runs an
+// integer division routine on the start-up path.
+struct SKPlan {
+  int npairs, nt1, nst1, nt2, C;
+  int s1, c1n, q1, r1, q2, r2;
+  __device__ __forceinline__ SKPlan(int nblk, int nt1_, int nst1_, int nt2_, int C_)
+      : npairs(nblk * nt1_), nt1(nt1_), nst1(nst1_), nt2(nt2_), C(C_) {
+    s1 = npairs * nst1;
+    c1n = min(C, s1);
+    q1 = c1n ? div_small(s1, c1n) : 0;
+    r1 = s1 - q1 * c1n;
+    const int s2 = npairs * nt2;
+    q2 = div_small(s2, C);
+    r2 = s2 - q2 * C;
+  }
+  __device__ __forceinline__ int lo1(int c) const {
+    c = min(c, c1n);
+    return c1n ? c * q1 + div_small(c * r1, c1n) : 0;
+  }
+  __device__ __forceinline__ int lo2(int c) const { return c * q2 + div_small(c * r2, C); }
+  // the CTA whose gate_up range holds stage q (q < S1): the largest c with lo1(c) <= q (an fp32 estimate, off by at
+  // most one, then corrected)
+  __device__ __forceinline__ int owner1(int q) const {
+    int c = min(max(__float2int_rz(__fdividef(((float)q + 1.f) * (float)c1n, (float)s1)), 0), c1n - 1);
+    if (c + 1 < c1n && lo1(c + 1) <= q) c++;
+    if (lo1(c) > q) c--;
+    return c;
+  }
+  __device__ __forceinline__ int n_gate(int c) const {
+    const int a = lo1(c), b = lo1(c + 1);
+    return b > a ? div_small(b - 1, nst1) - div_small(a, nst1) + 1 : 0;
+  }
+  __device__ __forceinline__ int n_down(int c) const {
+    const int a = lo2(c), b = lo2(c + 1);
+    return b > a ? div_small(b - 1, nt2) - div_small(a, nt2) + 1 : 0;
+  }
+  __device__ __forceinline__ int units(int c) const { return n_gate(c) + n_down(c); }
+  // unit j of CTA c: its gate_up units (pairs in order), then its down units
+  __device__ __forceinline__ void unit(int c, int j, UnitMeta& u) const {
+    const int ng = n_gate(c);
+    if (j < ng) {
+      const int a = lo1(c), b = lo1(c + 1);
+      const int pr = div_small(a, nst1) + j, s0 = pr * nst1;
+      u.ph = 0;
+      u.pair = pr;
+      u.st0 = max(a - s0, 0);
+      u.nst = min(b - s0, nst1) - u.st0;
+      u.rec = c + pr;
+      u.c0 = u.c1 = c;
     } else {
-      q->first[0] = i0, q->cnt[0] = R, q->G[0] = G;
-      q->nrem = 1;
+      const int a = lo2(c), b = lo2(c + 1);
+      const int pr = div_small(a, nt2) + (j - ng), i0 = pr * nt2;
+      u.ph = 1;
+      u.pair = pr;
+      u.item = max(a - i0, 0);
+      u.nst = min(b - i0, nt2) - u.item;
+      u.rec = -1;
+      u.c0 = owner1(pr * nst1);
+      u.c1 = owner1(pr * nst1 + nst1 - 1);
     }
+    u.blk = pr_blk(u.pair);
+    const int t = u.pair - u.blk * nt1;
+    if (u.ph == 0)
+      u.item = t;
+    else
+      u.st0 = t;
   }
-}
-// Units of CTA c: two per remainder position where it holds a share and per whole wave (the gate_up share, then the
-// down run). The split positions come first: their shares wait on one another, and at the start every CTA begins
-// at the same time, so the partners of a pair arrive together.
-__device__ __forceinline__ int cta_units(const PairPlan* q, int c) {
-  int n = 2 * q->nfull;
-  for (int i = 0; i < q->nrem; i++) n += c < q->cnt[i] * q->G[i] ? 2 : 0;
-  return n;
-}
-// Unit j of CTA c (C CTAs).
-__device__ __forceinline__ void cta_unit(const PairPlan* q, int nt1, int nst1, int nt2, int c, int C, int j,
-                                         UnitMeta& u) {
-  int pair = 0, w = j >> 1;
-  u.pos = -1, u.G = 1, u.s = 0, u.cta0 = c;
-  for (int i = 0; i < q->nrem; i++) {
-    const int G = q->G[i];
-    if (c >= q->cnt[i] * G) continue;
-    if (w == 0) {
-      const int pr = div_small(c, G);
-      pair = q->first[i] + pr;
-      u.pos = i, u.G = G, u.s = c - pr * G, u.cta0 = pr * G;
-      break;
-    }
-    w--;
-  }
-  if (u.pos < 0) pair = w * C + c;
-  u.blk = div_small(pair, nt1);
-  const int t = pair - u.blk * nt1;
-  if ((j & 1) == 0) {
-    u.ph = 0;
-    u.item = t;
-    u.st0 = div_small(nst1 * u.s, u.G);
-    u.nst = div_small(nst1 * (u.s + 1), u.G) - u.st0;
-  } else {
-    u.ph = 1;
-    u.item = div_small(nt2 * u.s, u.G);
-    u.nst = div_small(nt2 * (u.s + 1), u.G) - u.item;
-    u.st0 = t;
-  }
-}
+  __device__ __forceinline__ int pr_blk(int pr) const { return div_small(pr, nt1); }
+};
 
 template <int XR>
 struct Cfg {
@@ -186,12 +181,14 @@ struct Cfg {
   static constexpr int ROUTE_OFF = LUT_OFF + NLUT * 256 * 8;  // srow[MAXIDS], bexp[MAXIDS], bstart[MAXIDS + 1]
   static constexpr int TOK_OFF = ROUTE_OFF + (3 * LAYER_MAXIDS + 1) * 4;  // the batch's slots: sid[], stw[]
   static constexpr int MISC_OFF = TOK_OFF + 2 * LAYER_MAXIDS * 4;
-  static constexpr int PLAN_OFF = MISC_OFF + 16;
-  static constexpr int BAR_OFF = (PLAN_OFF + (int)sizeof(PairPlan) + 7) / 8 * 8;
+  static constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;  // mbarriers: 8-byte aligned
   static constexpr int SMEM = BAR_OFF + (3 * NS + 4) * 8;
   static constexpr int T = XR / 8;
   static constexpr int MINB = 2;
   static_assert(XR <= 32, "at most 32 rows per block");
+  static_assert(BAR_OFF % 8 == 0 && LUT_OFF % 8 == 0 && META_OFF % 4 == 0 && X_OFF % 16 == 0 && ACT_OFF % 16 == 0 &&
+                    SLOT % 16 == 0 && X_STRIDE % 16 == 0,
+                "shared-memory sections aligned for their widest access");
   static_assert(2 * LAYER_MAXIDS * 4 <= SLOT, "routing scratch fits in ring slot 0");
   static_assert(XR > 16 || 2 * SMEM + 2048 <= 228 * 1024, "two CTAs per SM (32-row blocks: one)");
 };
@@ -258,7 +255,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   int* srow = reinterpret_cast<int*>(smem + C::ROUTE_OFF);
   int* bexp = srow + LAYER_MAXIDS;
   int* bstart = bexp + LAYER_MAXIDS;
-  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);  // [0] blocks, [1] valid slots, [2] abort
+  // [0] blocks, [1] valid slots, [2] abort, [3] the blocks the plan covers
+  volatile int* misc = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::NS;
   uint64_t* scaled = empty + C::NS;
@@ -411,9 +409,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         MOEK_TR_CLK(43);
         bstart[base] = nvalid;
         misc[0] = base;
-        const int nb = *abort_flag ? 0 : base;
-        plan_pairs(reinterpret_cast<PairPlan*>(smem + C::PLAN_OFF), nb, p.m[0].nt, p.m[0].nstage, p.m[1].nt,
-                   gridDim.x);
+        misc[3] = *abort_flag ? 0 : base;  // the blocks the plan covers
         MOEK_TR_CLK(44);
       }
     }
@@ -422,9 +418,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   if (tid == 0) MOEK_TR(3);
   if (tid == 0) MOEK_TR_CLK(45);
 
-  const PairPlan* plan = reinterpret_cast<const PairPlan*>(smem + C::PLAN_OFF);
   const int nt1 = p.m[0].nt, nst1 = p.m[0].nstage, nt2 = p.m[1].nt, nst2 = p.m[1].nstage;
-  const int n_mine = cta_units(plan, blockIdx.x);
+  const SKPlan plan(misc[3], nt1, nst1, nt2, (int)gridDim.x);
+  const int n_mine = plan.units(blockIdx.x);
   const int rounds = (n_mine + MAXU - 1) / MAXU;
   if (tid == 0) MOEK_TR_VAL(7, n_mine);
   if (tid == 0) MOEK_TR_CLK(53);
@@ -441,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       UnitMeta um;
       int key = -1, b0 = 0;
       if (lane < nu) {
-        cta_unit(plan, nt1, nst1, nt2, blockIdx.x, gridDim.x, u0 + lane, um);
+        plan.unit(blockIdx.x, u0 + lane, um);
         um.e = bexp[um.blk];
         b0 = bstart[um.blk];
         const int cnt = bstart[um.blk + 1] - b0;
@@ -658,8 +654,66 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
         bool ok = true;
         const int tu = r * MAXU + ui;  // the unit's index among this CTA's (timeline stamps)
         bool ready = false;  // the next stage's scales were seen published while this stage was computed
-        // down: this share's fp32 partials of k-slice st0, one item per stage (summed after the grid barrier)
+        // down: this CTA's fp32 partials of k-slice st0, one item per stage (summed after the grid barrier)
         float* dbase = p.part2 + ((int64_t)m.st0 * n) * H;
+        if (ph == 1) {  // ------------------------------------------------------------- the pair's act from records
+          // every warp is done with the previous unit's operands before the act buffer is rewritten
+          consumer_sync();
+          if (!*abort_flag) {
+            // the records of CTAs [c0, c1] for this warp's act columns [16 w, 16 w + 16) (lane i polls CTA c0 + i;
+            // at most H / 128 <= 32 CTAs meet a pair)
+            const int nrec = m.c1 - m.c0 + 1;
+            const int* flags = p.ctr + p.off_xflag;
+            bool seen = lane >= nrec;
+            for (uint32_t it = 0;; it++) {
+              if (!seen) seen = ld_acquire(flags + (int64_t)(m.c0 + lane + m.pair) * NCW + warp) == epoch + 1;
+              if (__all_sync(0xffffffffu, seen)) break;
+              if ((it & 63) == 63 && globaltimer() > deadline) {
+                if (lane == 0) {
+                  report(p.err, MOEK_DEV_TIMEOUT);
+                  *abort_flag = 1;
+                }
+                break;
+              }
+              __nanosleep(32);
+            }
+            __syncwarp();
+            if (!*abort_flag) {
+              // act = bf16(silu(gate) * up), gate and up the records' sums in CTA order. Lane 4 r + q takes columns
+              // 16 w + 4 q .. + 3 of row r (8 rows per pass): two 16-byte loads per record, two records' loads in
+              // flight before they are added, so a pair costs about one L2 round trip per two records.
+              const float* rec0 = p.xpart + (int64_t)(m.c0 + m.pair) * XR * ITEM_COLS + 16 * warp + 4 * (lane & 3);
+              for (int row = lane >> 2; row < nv; row += 8) {
+                const float* b = rec0 + row * ITEM_COLS;
+                float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = gs;
+                for (int s2 = 0; s2 < nrec; s2 += 2) {
+                  float4 gv[2], uv[2];
+#pragma unroll
+                  for (int u = 0; u < 2; u++) {
+                    if (s2 + u < nrec) {
+                      gv[u] = __ldcg(reinterpret_cast<const float4*>(b + (s2 + u) * XR * ITEM_COLS));
+                      uv[u] = __ldcg(reinterpret_cast<const float4*>(b + (s2 + u) * XR * ITEM_COLS + ITEM_COLS / 2));
+                    }
+                  }
+#pragma unroll
+                  for (int u = 0; u < 2; u++) {
+                    if (s2 + u < nrec) {
+                      gs.x += gv[u].x, gs.y += gv[u].y, gs.z += gv[u].z, gs.w += gv[u].w;
+                      us.x += uv[u].x, us.y += uv[u].y, us.z += uv[u].z, us.w += uv[u].w;
+                    }
+                  }
+                }
+                const __nv_bfloat162 a01 = __floats2bfloat162_rn(silu(gs.x) * us.x, silu(gs.y) * us.y);
+                const __nv_bfloat162 a23 = __floats2bfloat162_rn(silu(gs.z) * us.z, silu(gs.w) * us.w);
+                uint2 pk;
+                pk.x = *reinterpret_cast<const uint32_t*>(&a01);
+                pk.y = *reinterpret_cast<const uint32_t*>(&a23);
+                *reinterpret_cast<uint2*>(act_s + row * (X_STRIDE / 2) + 16 * warp + 4 * (lane & 3)) = pk;
+              }
+            }
+          }
+          consumer_sync();  // the act buffer holds the pair's act rows
+        }
         for (int j = 0; j < m.nst; j++, g++) {
           const int slot = g % C::NS;
           const uint32_t par = (g / C::NS) & 1;
@@ -677,7 +731,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           if (stamp) MOEK_TR_CLK(80 + j);
           if (tid == 0 && j == 0 && tu < 8) {
             MOEK_TR(8 + 3 * tu);
-            MOEK_TR_VAL(32 + tu, (ph << 28) | (m.blk << 16) | (m.item << 8) | m.s);
+            MOEK_TR_VAL(32 + tu, (ph << 28) | (m.blk << 16) | (m.item << 8) | m.st0);
           }
           // B operand rows: gate_up the slot's hidden rows, down the pair's act rows
           const uint8_t* xrows = ph == 0 ? smem + slot * C::SLOT + C::X_OFF : smem + C::ACT_OFF;
@@ -769,26 +823,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           continue;
         }
 
-        // --------------------------------------------------------------------------- gate_up finishing: the act
-        // the pair's act columns [16 w, 16 w + 16) of this warp into the act buffer
-        // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v
-        consumer_sync();  // every warp is done reading the previous pair's act rows
-        if (good && m.G == 1) {  // gate row and up row + 128 share the column: act straight from the accumulators
-#pragma unroll
-          for (int t = 0; t < C::T; t++) {
-            if (t >= ntile) break;
-#pragma unroll
-            for (int v = 0; v < 2; v++) {
-              const int row = t * 8 + 2 * c + v;
-              if (row >= nv) continue;
-#pragma unroll
-              for (int h = 0; h < 2; h++)
-                act_s[row * (X_STRIDE / 2) + slot00 + 8 * h] =
-                    __float2bfloat16_rn(silu(acc[0][t][2 * h + v]) * acc[1][t][2 * h + v]);
-            }
-          }
-        } else if (good) {  // G shares: exchange the fp32 partials, every share forms the act from all of them
-          float* mine = p.xpart + ((int64_t)m.pos * gridDim.x + blockIdx.x) * XR * ITEM_COLS;
+        // ------------------------------------------------------------------ gate_up finishing: this CTA's record
+        // acc[i][t][2h + v] = weight row (16 G_i + g + 8h) x block row 8t + 2c + v; the warp's rows are its act
+        // columns' gate and up rows, so each warp publishes its own columns with its own flag
+        if (good) {
+          float* mine = p.xpart + (int64_t)m.rec * XR * ITEM_COLS;
 #pragma unroll
           for (int t = 0; t < C::T; t++) {
             if (t >= ntile) break;
@@ -798,45 +837,15 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
               if (row >= nv) continue;
 #pragma unroll
               for (int h = 0; h < 2; h++) {
-                mine[row * ITEM_COLS + slot00 + 8 * h] = acc[0][t][2 * h + v];
-                mine[row * ITEM_COLS + slot10 + 8 * h] = acc[1][t][2 * h + v];
+                __stcg(mine + row * ITEM_COLS + slot00 + 8 * h, acc[0][t][2 * h + v]);
+                __stcg(mine + row * ITEM_COLS + slot10 + 8 * h, acc[1][t][2 * h + v]);
               }
             }
           }
           __syncwarp();
-          int* flags = p.ctr + p.off_xflag + (int64_t)m.pos * LAYER_XFLAG_CTAS * NCW;
           // the warp's partials (ordered before lane 0's release by the warp barrier) before its flag
-          if (lane == 0) st_release(flags + blockIdx.x * NCW + warp, epoch + 1);
-          // the partners' partials of this warp's columns (lane s polls share s; bounded)
-          bool seen = lane >= m.G || lane == m.s;
-          for (uint32_t it = 0;; it++) {
-            if (!seen) seen = ld_acquire(flags + (m.cta0 + lane) * NCW + warp) == epoch + 1;
-            if (__all_sync(0xffffffffu, seen)) break;
-            if ((it & 63) == 63 && globaltimer() > deadline) {
-              if (lane == 0) {
-                report(p.err, MOEK_DEV_TIMEOUT);
-                *abort_flag = 1;
-              }
-              break;
-            }
-            __nanosleep(32);
-          }
-          __syncwarp();
-          if (!*abort_flag) {
-            const float* part0 = p.xpart + ((int64_t)m.pos * gridDim.x + m.cta0) * XR * ITEM_COLS;
-            for (int idx = lane; idx < nv * 16; idx += 32) {
-              const int row = idx >> 4, col = 16 * warp + (idx & 15);
-              float gs = 0.f, us = 0.f;
-              for (int s2 = 0; s2 < m.G; s2++) {
-                const float* pr = part0 + ((int64_t)s2 * XR + row) * ITEM_COLS;
-                gs += __ldcg(pr + col);
-                us += __ldcg(pr + ITEM_COLS / 2 + col);
-              }
-              act_s[row * (X_STRIDE / 2) + col] = __float2bfloat16_rn(silu(gs) * us);
-            }
-          }
+          if (lane == 0) st_release(p.ctr + p.off_xflag + (int64_t)m.rec * NCW + warp, epoch + 1);
         }
-        consumer_sync();  // the act buffer holds the pair's act rows
         if (tid == 0 && tu < 8) MOEK_TR(10 + 3 * tu);
       }
       __syncwarp();
@@ -849,11 +858,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   // every CTA's down partials are written: the last CTA to arrive advances the launch epoch, every CTA waits for it
   __syncthreads();
   if (tid == 0) {
+    MOEK_TR(47);
     __threadfence();
     if (atomicAdd(p.ctr + p.off_done, 1) == (int)gridDim.x - 1) {
+      // the last arrival: release the epoch first (the waiting CTAs pass on it), then reset the counter for the next
+      // launch (no CTA of this launch reads it again; stream order makes the reset visible to the next launch)
+      st_release(p.ctr + p.off_epoch, epoch + 1);
       p.ctr[p.off_done] = 0;
-      __threadfence();
-      atomicAdd(p.ctr + p.off_epoch, 1);
     }
     for (uint32_t it = 0;; it++) {
       if (ld_acquire(p.ctr + p.off_epoch) != epoch) break;
@@ -873,37 +884,39 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
   // ------------------------------------------------------------------------------------ the top-k sums, a slice each
   // out[t] = bf16(sum over valid slots j in order of w_j * (sum over k-slices in order of the down partials)); with
   // out_rows the weighted slot rows instead; expert-parallel: the fp32 sum into this rank's back buffer. One output
-  // element per thread, the loads of up to 8 slots x 2 k-slices issued together.
+  // element per thread, the loads of up to 8 slots x 4 k-slices issued together.
   {
     float* back = p.ep_peer ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.ep_peer[p.ep_rank]) +
                                                       p.ep_back_off)
                             : nullptr;
-    const int64_t nout = (int64_t)p.M * p.H, sstride = (int64_t)n * p.H;
-    for (int64_t i = (int64_t)blockIdx.x * THREADS + tid; i < nout; i += (int64_t)gridDim.x * THREADS) {
-      const int tk = (int)(i / p.H), col = (int)(i - (int64_t)tk * p.H);
+    // 32-bit indices: M * H <= 512 x 4096 and (I / 128) x num_ids x H <= 32 x 512 x 4096 < 2^31
+    const int H = p.H, nout = p.M * H, sst = n * H;
+    for (int i = (int)blockIdx.x * THREADS + tid; i < nout; i += (int)gridDim.x * THREADS) {
+      const int tk = i / H, col = i - tk * H;
       float o = 0.f;
       for (int j0 = 0; j0 < k; j0 += 8) {
         bool val[8];
         float sj[8];
+        const float* rp[8];  // the slot's row of k-slice 0 (unused slots read slot 0's row, in bounds, then dropped)
 #pragma unroll
         for (int jj = 0; jj < 8; jj++) {
-          const int e = j0 + jj < k ? sid[tk * k + j0 + jj] : -1;
+          const bool in = j0 + jj < k;
+          const int sl = tk * k + (in ? j0 + jj : 0);
+          const int e = in ? sid[sl] : -1;
           val[jj] = e >= 0 && e < p.E;
           sj[jj] = 0.f;
+          rp[jj] = p.part2 + sl * H + col;
         }
-        for (int t0 = 0; t0 < nst2; t0 += 2) {
-          float v[8][2];
+        for (int t0 = 0; t0 < nst2; t0 += 4) {  // 32 loads in flight (I = 512: every load of a token at once)
+          float v[8][4];
 #pragma unroll
           for (int jj = 0; jj < 8; jj++)
 #pragma unroll
-            for (int u = 0; u < 2; u++)
-              v[jj][u] = val[jj] && t0 + u < nst2
-                             ? __ldcg(p.part2 + (t0 + u) * sstride + (int64_t)(tk * k + j0 + jj) * p.H + col)
-                             : 0.f;
+            for (int u = 0; u < 4; u++) v[jj][u] = __ldcg(rp[jj] + min(t0 + u, nst2 - 1) * sst);
 #pragma unroll
           for (int jj = 0; jj < 8; jj++)
 #pragma unroll
-            for (int u = 0; u < 2; u++)
+            for (int u = 0; u < 4; u++)
               if (val[jj] && t0 + u < nst2) sj[jj] += v[jj][u];
         }
 #pragma unroll
@@ -911,7 +924,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           if (!val[jj]) continue;
           const int sl = tk * k + j0 + jj;
           const float y = __fmul_rn(stw[sl], sj[jj]);  // rounded like a stored slot row (no contraction)
-          if (p.out_rows) p.out_rows[(int64_t)sl * p.H + col] = y;
+          if (p.out_rows) p.out_rows[(int64_t)sl * H + col] = y;
           o += y;
         }
       }

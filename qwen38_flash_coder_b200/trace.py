@@ -26,7 +26,9 @@ CTAS, SLOTS = 1024, 128
 CLOCK_GHZ = 1.965  # SM clock the cycle stamps are converted at (the B200's maximum, the clock the bench runs at)
 
 LAYER_PHASES = {0: "start", 1: "after dependent-launch wait", 2: "EP flags seen", 3: "routing done",
-                4: "first weight copy issued", 5: "consumers done", 6: "end"}
+                4: "first weight copy issued", 5: "consumers done", 47: "every role done (barrier arrival)",
+                51: "grid barrier passed",
+                52: "top-k sums written", 6: "end"}
 GEMM_PHASES = {0: "start", 1: "after dependent-launch wait", 6: "end"}
 
 
@@ -194,6 +196,7 @@ def main():
                                                                        "ep_decode8"])
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--dump", default=None, help="also save every layer's raw stamps [CTA][slot] to this .npy file")
     a = ap.parse_args()
     os.environ.setdefault("MOEK_B200_LIB", "trace")
     import torch
@@ -218,7 +221,7 @@ def main():
         for L, x, ids, w in layers:
             ops.fused_moe(x, L, w, ids)
     torch.cuda.synchronize()
-    res = []
+    res, raw = [], []
     for L, x, ids, w in layers:
         clear()
         torch.cuda.synchronize()
@@ -226,7 +229,10 @@ def main():
         torch.cuda.synchronize()
         ops.check_device_errors(dev)
         k = 0 if a.workload != "prefill" else 1
-        res.append(summarize(read(k), k))
+        raw.append(read(k))
+        res.append(summarize(raw[-1], k))
+    if a.dump:
+        np.save(a.dump, np.stack(raw))
     if a.json:
         print(json.dumps(res))
         return

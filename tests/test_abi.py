@@ -65,9 +65,9 @@ def test_layer_entry_points_reject_bad_arguments():
     assert lib.moek_layer_state_ints(512, 2048, 512, ctypes.byref(n)) == 0 and n.value > 2
     b = ctypes.c_size_t(0)
     assert lib.moek_layer_workspace_bytes(8, 5, 2048, 512, 4, 2, 0, ctypes.byref(b)) == 0
-    # the split pairs' fp32 gate_up partials (2 positions x a grid of 2 x 148 CTAs x 32 rows x 256 columns; no GPU
-    # here, so the SM count is B200's 148) + the down partials per 128-k slice [I / 128, 40, H] fp32
-    assert b.value == 2 * 296 * 32 * 256 * 4 + 4 * 40 * 2048 * 4
+    # the fp32 gate_up records (grid bound 2 x 148 CTAs -- no GPU here, so the SM count is B200's 148 -- plus 40 slots
+    # x 4 gate_up items, each 8 block rows x 256 columns) + the down partials per 128-k slice [I / 128, 40, H] fp32
+    assert b.value == (296 + 40 * 4) * 8 * 256 * 4 + 4 * 40 * 2048 * 4
     args = [None, 200, 2048, 512, 512, None, None, 5] + [None] * 10 + [4, 2, None, 0, None, 0, None, None, None, None]
     assert lib.moek_moe_layer(*args) == 3 and b"decode batches" in lib.moek_last_error()  # M = 200 too large
     args[1] = 8
