@@ -192,7 +192,7 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  *           gate_up stages over the CTAs itself (from the number of blocks and the grid), which changes only the
  *           order of fp32 partial sums; the same routing always gives the same plan and the same bits.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
-/* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: 8 up to M = 8, else 16).
+/* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: 8).
  * An expert with more routed slots than that is cut into several blocks, its weights streamed once per block.
  * Process-wide; a tuning knob with no effect on the results. */
 int moek_set_layer_block_rows(int32_t rows);

@@ -630,6 +630,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
       const UnitMeta* mb = meta + b * MAXU;
       wait_or_abort(mfull + b, (r >> 1) & 1, deadline, p.err, abort_flag);
       const bool have_meta = !consumer_sync_or(*abort_flag);
+      bool pre_seen = false;  // this lane's record flag of the next (down) unit was seen set during this unit
       for (int ui = 0; ui < nu && have_meta; ui++) {
         const UnitMeta& m = mb[ui];
         const int ph = m.ph, nv = m.nv;
@@ -664,7 +665,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
             // at most H / 128 <= 32 CTAs meet a pair)
             const int nrec = m.c1 - m.c0 + 1;
             const int* flags = p.ctr + p.off_xflag;
-            bool seen = lane >= nrec;
+            bool seen = lane >= nrec || pre_seen;
+            pre_seen = false;
             for (uint32_t it = 0;; it++) {
               if (!seen) seen = ld_acquire(flags + (int64_t)(m.c0 + lane + m.pair) * NCW + warp) == epoch + 1;
               if (__all_sync(0xffffffffu, seen)) break;
@@ -739,6 +741,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           for (int hf = 0; hf < 2; hf++) {  // the stage's two 64-k halves: an 8 KB block of codes and 4 k-groups each
           if (hf == 1 && j + 1 < m.nst)  // test the next stage's scales (its latency hides behind this half's math)
             ready = mbar_test(scaled + (g + 1) % C::NS, ((g + 1) / C::NS) & 1);
+          if (hf == 1 && j + 1 == m.nst && ui + 1 < nu && mb[ui + 1].ph == 1) {
+            // the next unit is a down unit: test its records' flags now, so that the load's latency hides behind
+            // this half's math and the unit's prologue usually needs no poll
+            const UnitMeta& mn = mb[ui + 1];
+            pre_seen = lane < mn.c1 - mn.c0 + 1 &&
+                       ld_acquire(p.ctr + p.off_xflag + (int64_t)(mn.c0 + lane + mn.pair) * NCW + warp) == epoch + 1;
+          }
           const uint8_t* sw = smem + slot * C::SLOT + hf * STAGE_BYTES;
           const uint8_t* sx = xrows + hf * BK * 2;
           const uint8_t* sc = smem + slot * C::SLOT + C::SC_OFF + (4 * hf + c) * 256;  // k-group 4 hf + c
