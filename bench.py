@@ -48,12 +48,16 @@ METRIC = "routed-MoE layer µs & HBM GB/s (M=8,32); TFLOP/s (M=6912); 1/2/4/8 GP
 H, I, E, TOPK = 2048, 512, 512, 5
 FLOPS_PER_ROW = 2 * 3 * H * I  # gate + up + down per (token, slot) row
 
-# DRAM bytes (read + write) of one launch of the roofline kernel, dram__bytes_read.sum + dram__bytes_write.sum of
-# layer 0's launch in one ncu capture of this file's own command with the kernels named below; not measured by the
-# run that prints them (the capture's command and date travel with the figure as "traffic_source").
+# DRAM bytes (read + write) of one launch of the roofline kernel: dram__bytes_read.sum + dram__bytes_write.sum of one
+# launch in an ncu capture of this file's own command (given with each figure as "traffic_source"); not measured by
+# the run that prints them.
 TRAFFIC = {
-    "decode8": (64_508_928, "ncu capture, moek_layer_kernel<8> of the 44 us build (before the dequant rework)"),
-    "prefill": (696_396_544, "ncu capture, moek_prefill_kernel gate_up launch (fp32-row down epilogue build)"),
+    "decode8": (68_361_728, "ncu capture of one moek_layer_kernel<8> launch (stream-K plan, 8-row blocks), "
+                            "bench.py --only --workload decode8 --layers 4"),
+    "decode32": (141_612_800, "ncu capture of one moek_layer_kernel<8> launch (stream-K plan, 8-row blocks), "
+                              "bench.py --only --workload decode32 --layers 4"),
+    "prefill": (696_165_888, "ncu capture of one moek_prefill_kernel gate_up launch, "
+                             "bench.py --only --workload prefill --layers 2"),
 }
 
 WORKLOADS = {
