@@ -192,6 +192,48 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  *           gate_up stages over the CTAs itself (from the number of blocks and the grid), which changes only the
  *           order of fp32 partial sums; the same routing always gives the same plan and the same bits.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
+/* ---- The rest of the MoE block at decode sizes: the router gate GEMM and the MXFP8 shared expert, whose fp32 rows
+ * the whole-layer kernel adds to each token's sum before its one bf16 rounding. They replace, for decode batches, the
+ * block's other steps around the routed experts (files/v54/model.py:193-210 subclasses vLLM's
+ * Qwen3NextSparseMoeBlock: vllm/model_executor/models/qwen3_next.py:125-131,193 the gate, qwen2_moe.py:114-122 the
+ * shared expert with its sigmoid gate; the shared expert is MXFP8 in the kit's checkpoint, README.md:38). */
+
+/* logits fp32 [M, E] = x bf16 [M, H] @ w_gate bf16 [E, H]^T (fp32 sums: eight K slices added in order, the same
+ * bits on every call). M <= 64, H % 128 == 0, E % 16 == 0 (else MOEK_ERR_UNSUPPORTED: larger batches are a plain
+ * library GEMM). x and w_gate 4-byte aligned. */
+int moek_router_gate(const void* x, int32_t M, int32_t H, const void* w_gate, int32_t E, float* logits, void* stream);
+
+/* Scratch bytes of moek_shared_expert: act bf16 [M, Is] and the expert gate fp32 [M], each rounded up to 256. */
+int moek_shared_workspace_bytes(int32_t M, int32_t Is, size_t* bytes);
+
+/* rows fp32 [M, H] = sigmoid(x @ w_sg) * (bf16(silu(g) * u) @ W_d^T), [g | u] = x @ W_gu^T in fp32, with MXFP8
+ * weights in the checkpoint layout: w_gu uint8 [2 Is, H] (float8_e4m3fn bytes; gate rows 0..Is-1, then the up rows),
+ * s_gu uint8 [2 Is, H / 32] (E8M0 exponents, one per 32 inputs), w_d uint8 [H, Is], s_d uint8 [H, Is / 32]; w_sg
+ * bf16 [H] (shared_expert_gate). Dequantisation is exact for scale bytes in [10, 134], the supported range (the
+ * Python wrapper rejects others). M <= 64, H % 128 == 0, Is % 128 == 0. */
+int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is, const uint8_t* w_gu, const uint8_t* s_gu,
+                       const uint8_t* w_d, const uint8_t* s_d, const void* w_sg, void* workspace,
+                       size_t workspace_bytes, float* rows, void* stream);
+
+/* Scratch bytes of moek_moe_block: logits fp32 [M, E], the shared rows fp32 [M, H], the shared expert's scratch
+ * (Is > 0) and the whole-layer kernel's workspace. */
+int moek_block_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t E, int32_t Is, size_t* bytes);
+
+/* The whole MoE block for a decode batch (M <= 64 tokens, E <= 512), three or four launches chained with programmatic
+ * dependent launch: moek_router_gate, moek_shared_expert (when Is > 0) and the whole-layer kernel from the logits
+ * (softmax, top_k, renormalised when renormalize != 0; as moek_moe_layer_logits) with the shared rows added:
+ * out bf16 [M, H] = bf16(sum over valid slots j in order of topk_w * down_e(...) + shared row). The routed weights and
+ * the state as moek_moe_layer; the shared expert's tensors as moek_shared_expert (ignored when Is = 0);
+ * topk_ids_out / topk_w_out (may be NULL) receive the routing. No reference counterpart as one call: the reference
+ * runs these steps as separate vLLM layers. */
+int moek_moe_block(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const void* w_gate, int32_t top_k,
+                   int32_t renormalize, int32_t* topk_ids_out, float* topk_w_out, const void* w13, const uint8_t* sp13,
+                   const float* g13, const int32_t* exc_off13, const int32_t* exc_ent13, const void* w2,
+                   const uint8_t* sp2, const float* g2, const int32_t* exc_off2, const int32_t* exc_ent2,
+                   int32_t nsplit_gate, int32_t nsplit_down, int32_t Is, const uint8_t* w_gu, const uint8_t* s_gu,
+                   const uint8_t* w_d, const uint8_t* s_d, const void* w_sg, void* workspace, size_t workspace_bytes,
+                   int32_t* state, int64_t state_ints, int32_t* err, void* out, void* stream);
+
 /* Rows per block of the whole-layer kernel: 8, 16 or 32, or 0 (automatic: 8).
  * An expert with more routed slots than that is cut into several blocks, its weights streamed once per block.
  * Process-wide; a tuning knob with no effect on the results. */

@@ -441,6 +441,117 @@ MOEK_API int moek_moe_layer_logits(const void* x, int32_t M, int32_t H, int32_t 
                      "moe_layer_logits launch");
 }
 
+// ------------------------------------------------------------------ the rest of the MoE block (decode sizes)
+static bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
+
+MOEK_API int moek_router_gate(const void* x, int32_t M, int32_t H, const void* w_gate, int32_t E, float* logits,
+                              void* stream) {
+  if (M < 0 || M > moek::SHARED_MAXM || H <= 0 || H % 128 || E <= 0 || E % 16)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: router_gate takes decode batches of <= %d tokens, H %% 128 == 0 and "
+                                      "E %% 16 == 0 (M %d, H %d, E %d); larger batches are a plain bf16 GEMM",
+                moek::SHARED_MAXM, M, H, E);
+  if (M == 0) return MOEK_OK;
+  if (!x || !w_gate || !logits || !aligned4(x) || !aligned4(w_gate))
+    return fail(MOEK_ERR_ARG, "moek_b200: router_gate null or unaligned pointer");
+  return cuda_status(moek::launch_router_gate(static_cast<const __nv_bfloat16*>(x), M, H,
+                                              static_cast<const __nv_bfloat16*>(w_gate), E, logits,
+                                              (cudaStream_t)stream),
+                     "router_gate launch");
+}
+
+static int64_t shared_ws_bytes(int64_t M, int64_t Is) {
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return up(M * Is * 2) + up(M * 4);
+}
+MOEK_API int moek_shared_workspace_bytes(int32_t M, int32_t Is, size_t* bytes) {
+  if (!bytes || M < 0 || Is < 0) return fail(MOEK_ERR_ARG, "moek_b200: bad shared-expert workspace query");
+  *bytes = (size_t)shared_ws_bytes(M, Is);
+  return MOEK_OK;
+}
+
+MOEK_API int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is, const uint8_t* w_gu,
+                                const uint8_t* s_gu, const uint8_t* w_d, const uint8_t* s_d, const void* w_sg,
+                                void* workspace, size_t workspace_bytes, float* rows, void* stream) {
+  if (M < 0 || M > moek::SHARED_MAXM || H <= 0 || H % 128 || Is <= 0 || Is % 128)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: shared_expert takes decode batches of <= %d tokens, H %% 128 == 0 "
+                                      "and Is %% 128 == 0 (M %d, H %d, Is %d)", moek::SHARED_MAXM, M, H, Is);
+  if (M == 0) return MOEK_OK;
+  if (!x || !w_gu || !s_gu || !w_d || !s_d || !w_sg || !rows || !workspace || !aligned4(x))
+    return fail(MOEK_ERR_ARG, "moek_b200: shared_expert null or unaligned pointer");
+  if ((int64_t)workspace_bytes < shared_ws_bytes(M, Is))
+    return fail(MOEK_ERR_ARG, "moek_b200: shared_expert needs %lld workspace bytes", (long long)shared_ws_bytes(M, Is));
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* wp = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(wp);
+  float* sg = reinterpret_cast<float*>(wp + up((int64_t)M * Is * 2));
+  return cuda_status(moek::launch_shared_expert(static_cast<const __nv_bfloat16*>(x), M, H, Is, w_gu, s_gu, w_d, s_d,
+                                                static_cast<const __nv_bfloat16*>(w_sg), act, sg, rows,
+                                                (cudaStream_t)stream),
+                     "shared_expert launch");
+}
+
+static int64_t block_ws_bytes(int64_t M, int32_t top_k, int32_t H, int32_t I, int32_t E, int32_t Is) {
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return up(M * E * 4) + up(M * H * 4) + (Is > 0 ? shared_ws_bytes(M, Is) : 0) +
+         layer_ws_bytes(M * top_k, H, I, (int)M);
+}
+MOEK_API int moek_block_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t E, int32_t Is,
+                                        size_t* bytes) {
+  if (!bytes || M < 0 || top_k <= 0 || H <= 0 || I <= 0 || E <= 0 || Is < 0)
+    return fail(MOEK_ERR_ARG, "moek_b200: bad MoE block workspace query");
+  *bytes = (size_t)block_ws_bytes(M, top_k, H, I, E, Is);
+  return MOEK_OK;
+}
+
+MOEK_API int moek_moe_block(const void* x, int32_t M, int32_t H, int32_t I, int32_t E, const void* w_gate,
+                            int32_t top_k, int32_t renormalize, int32_t* topk_ids_out, float* topk_w_out,
+                            const void* w13, const uint8_t* sp13, const float* g13, const int32_t* exc_off13,
+                            const int32_t* exc_ent13, const void* w2, const uint8_t* sp2, const float* g2,
+                            const int32_t* exc_off2, const int32_t* exc_ent2, int32_t nsplit_gate,
+                            int32_t nsplit_down, int32_t Is, const uint8_t* w_gu, const uint8_t* s_gu,
+                            const uint8_t* w_d, const uint8_t* s_d, const void* w_sg, void* workspace,
+                            size_t workspace_bytes, int32_t* state, int64_t state_ints, int32_t* err, void* out,
+                            void* stream) {
+  if (M == 0) return MOEK_OK;
+  if (M < 0 || M > moek::SHARED_MAXM || E > 512 || top_k <= 0 || top_k > E || Is < 0)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_block takes decode batches of <= %d tokens, E <= 512 and "
+                                      "0 < top_k <= E (M %d, E %d, top_k %d, Is %d)", moek::SHARED_MAXM, M, E, top_k,
+                Is);
+  if (!out || !workspace) return fail(MOEK_ERR_ARG, "moek_b200: moe_block null pointer");
+  const int64_t need = block_ws_bytes(M, top_k, H, I, E, Is);
+  if ((int64_t)workspace_bytes < need)
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_block needs %lld workspace bytes", (long long)need);
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* wp = static_cast<uint8_t*>(workspace);
+  float* logits = reinterpret_cast<float*>(wp);
+  wp += up((int64_t)M * E * 4);
+  float* rows = reinterpret_cast<float*>(wp);
+  wp += up((int64_t)M * H * 4);
+  const int64_t sws = Is > 0 ? shared_ws_bytes(M, Is) : 0;
+  void* shared_ws = wp;
+  wp += sws;
+  moek::LayerParams p;
+  if (int rc = layer_params(p, x, M, H, I, E, nullptr, nullptr, top_k, w13, sp13, g13, exc_off13, exc_ent13, w2, sp2,
+                            g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down, wp,
+                            workspace_bytes - (size_t)(wp - static_cast<uint8_t*>(workspace)), state, state_ints, err,
+                            true, true))
+    return rc;
+  if (int rc = moek_router_gate(x, M, H, w_gate, E, logits, stream)) return rc;
+  if (Is > 0) {
+    if (int rc = moek_shared_expert(x, M, H, Is, w_gu, s_gu, w_d, s_d, w_sg, shared_ws, (size_t)sws, rows, stream))
+      return rc;
+    p.shared = rows;
+  }
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.logits = logits;
+  p.logits_bf16 = 0;
+  p.renorm = renormalize ? 1 : 0;
+  p.ids_out = topk_ids_out;
+  p.w_out = topk_w_out;
+  return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), g_layer_coop, (cudaStream_t)stream),
+                     "moe_block launch");
+}
+
 // ------------------------------------------------------------------------- EP peer-memory exchange (fixed capacity)
 MOEK_API int moek_ipc_malloc(size_t bytes, void** ptr) {
   if (!ptr || bytes == 0) return fail(MOEK_ERR_ARG, "moek_b200: ipc_malloc needs a size and an output pointer");

@@ -133,6 +133,8 @@ struct LayerParams {
   float* part2;            // workspace [I / 128, num_ids, H]: down partials per k-slice
   float* out_rows;         // caller's fp32 rows [num_ids, H] instead of the top-k sum (or null)
   __nv_bfloat16* out;      // caller's bf16 [M, H] top-k sums (or null)
+  const float* shared;     // fp32 [M, H] rows added to each token's sum before its rounding (the shared expert), or
+                           // null
   int* ctr;                // persistent int32 state: epoch, barrier and arrival counters, exchange flags (zeroed once)
   int* err;                // device error word
   uint64_t timeout_ns;
@@ -171,6 +173,15 @@ struct LayerParams {
 };
 // rows per block: 8/16/32; coop: cooperative launch (every CTA resident together, the default)
 cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, int coop, cudaStream_t st);
+
+// moek_shared.cu: the router gate GEMM and the MXFP8 shared expert at decode sizes (M <= SHARED_MAXM tokens)
+constexpr int SHARED_MAXM = 64;
+cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_bfloat16* wg, int E, float* logits,
+                               cudaStream_t st);
+// act bf16 [M, Is] and sg fp32 [M] are scratch; rows fp32 [M, H] the output
+cudaError_t launch_shared_expert(const __nv_bfloat16* x, int M, int H, int Is, const uint8_t* wgu, const uint8_t* sgu,
+                                 const uint8_t* wd, const uint8_t* sd, const __nv_bfloat16* wsg, __nv_bfloat16* act,
+                                 float* sg, float* rows, cudaStream_t st);
 
 // moek_router.cu: softmax -> top-k -> optional renormalisation (dtype 0 = fp32 logits, 1 = bf16)
 cudaError_t launch_router_topk(const void* logits, int dtype, int M, int E, int k, int renorm, int32_t* ids,

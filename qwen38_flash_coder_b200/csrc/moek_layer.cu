@@ -937,6 +937,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
           o += y;
         }
       }
+      if (p.shared) o += p.shared[i];  // the shared expert's row (the block output = routed + shared)
       if (p.out) p.out[i] = __float2bfloat16_rn(o);
       if (back) back[i] = o;
     }

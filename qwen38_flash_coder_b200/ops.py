@@ -505,3 +505,120 @@ def record_launches(fn) -> list:
         return list(_PROF)
     finally:
         _PROF = None
+
+
+# ------------------------------------------------------------------------------- the rest of the MoE block
+SHARED_MAXM = 64  # decode sizes of the router gate and shared-expert kernels (moek_shared.cu)
+
+
+class SharedExpert:
+    """The block's shared expert in the kit's checkpoint format (MXFP8): w_gu uint8 [2 Is, H] float8_e4m3fn bytes
+    (gate rows, then up rows), s_gu uint8 [2 Is, H / 32] E8M0 exponents, w_d uint8 [H, Is], s_d uint8 [H, Is / 32],
+    and the expert gate w_sg bf16 [H] (vllm/model_executor/models/qwen2_moe.py:114-122). Used as is: the kernels read
+    the checkpoint layout."""
+
+    def __init__(self, w_gu, s_gu, w_d, s_d, w_sg):
+        self.w_gu, self.s_gu = w_gu.contiguous().view(torch.uint8), s_gu.contiguous().view(torch.uint8)
+        self.w_d, self.s_d = w_d.contiguous().view(torch.uint8), s_d.contiguous().view(torch.uint8)
+        self.w_sg = w_sg.contiguous().reshape(-1).to(torch.bfloat16)
+        self.inter = self.w_gu.shape[0] // 2
+        self.hidden = self.w_gu.shape[1]
+        lo = min(int(self.s_gu.min()), int(self.s_d.min()))
+        hi = max(int(self.s_gu.max()), int(self.s_d.max()))
+        if lo < 10 or hi > 134:  # outside, an e4m3 x 2^(s - 127) weight may not be a normal bf16 (see moek_shared.cu)
+            raise MoekError(f"moek_b200: MXFP8 scale exponents must lie in [10, 134] (got [{lo}, {hi}])")
+
+    def dequant(self):
+        """bf16 (exact) weights (W_gu [2 Is, H], W_d [H, Is]) for batches past the decode kernels."""
+        f = lambda q, s: (q.view(torch.float8_e4m3fn).float().view(q.shape[0], -1, 32)
+                          * torch.exp2(s.float() - 127.0)[..., None]).view(q.shape[0], -1).to(torch.bfloat16)
+        return f(self.w_gu, self.s_gu), f(self.w_d, self.s_d)
+
+
+def router_gate(hidden_states: torch.Tensor, w_gate: torch.Tensor) -> torch.Tensor:
+    """Router logits fp32 [M, E] = x @ w_gate^T (the block's gate, vllm/.../qwen3_next.py:125-131,193): this build's
+    kernel for decode batches (M <= 64), a library fp32 GEMM for larger ones."""
+    x = hidden_states
+    _need_cuda(x, w_gate)
+    m, hid = x.shape
+    e = w_gate.shape[0]
+    if m > SHARED_MAXM or e % 16 or hid % 128:
+        return x.float() @ w_gate.float().t()
+    x, w_gate = x.contiguous(), w_gate.contiguous()
+    logits = torch.empty((m, e), dtype=torch.float32, device=x.device)
+    call("moek_router_gate", _ptr(x), m, hid, _ptr(w_gate), e, _ptr(logits), _stream(x.device))
+    return logits
+
+
+def shared_expert(hidden_states: torch.Tensor, shared: SharedExpert) -> torch.Tensor:
+    """fp32 rows [M, H] = sigmoid(x @ w_sg) * down(bf16(silu(gate) * up)) of the MXFP8 shared expert: this build's
+    kernels for decode batches (M <= 64), exact bf16 weights and library fp32 GEMMs for larger ones."""
+    x = hidden_states
+    _need_cuda(x, shared.w_gu)
+    m, hid = x.shape
+    if m > SHARED_MAXM:
+        a, b = shared.dequant()
+        h = x.float() @ a.float().t()
+        act = (torch.nn.functional.silu(h[:, :shared.inter]) * h[:, shared.inter:]).to(torch.bfloat16)
+        return torch.sigmoid(x.float() @ shared.w_sg.float()[:, None]) * (act.float() @ b.float().t())
+    import ctypes
+
+    x = x.contiguous()
+    wsb = ctypes.c_size_t(0)
+    call("moek_shared_workspace_bytes", m, shared.inter, ctypes.byref(wsb))
+    ws = _scratch("shared_ws", wsb.value, torch.uint8, x.device)
+    rows = torch.empty((m, hid), dtype=torch.float32, device=x.device)
+    call("moek_shared_expert", _ptr(x), m, hid, shared.inter, _ptr(shared.w_gu), _ptr(shared.s_gu), _ptr(shared.w_d),
+         _ptr(shared.s_d), _ptr(shared.w_sg), _ptr(ws), ws.numel(), _ptr(rows), _stream(x.device))
+    return rows
+
+
+def moe_block(hidden_states: torch.Tensor, w_gate: torch.Tensor, layer: PreparedLayer, shared: SharedExpert,
+              top_k: int, renormalize: bool = True, output: torch.Tensor = None, return_routing: bool = False):
+    """The MoE block (vllm/model_executor/models/qwen3_next.py:177-204, which the kit's files/v54/model.py:193-210
+    subclasses): router gate -> softmax / top-k -> routed experts, plus the shared expert (``shared`` may be None),
+    out = bf16(sum of the routed slots in slot order + the shared row). Decode batches (M <= 64, E <= 512): one call
+    of moek_moe_block (the gate, the shared expert and the whole-layer kernel, chained on the GPU). Larger batches: the
+    gate and the shared expert as library GEMMs, the routed experts' fp32 slot rows from this build's prefill kernels,
+    added in slot order. With ``return_routing`` also returns (weights fp32 [M, k], ids int32 [M, k])."""
+    x = hidden_states
+    _need_cuda(x, w_gate)
+    m, hid = x.shape
+    e = w_gate.shape[0]
+    if output is None:
+        output = torch.empty((m, hid), dtype=torch.bfloat16, device=x.device)
+    if m == 0:
+        return (output, (None, None)) if return_routing else output
+    if m <= SHARED_MAXM and e <= 512 and e % 16 == 0 and hid % 128 == 0 and _decode_path(m, top_k) and \
+            x.dtype == torch.bfloat16 and (shared is None or shared.inter % 128 == 0):
+        import ctypes
+
+        _layer_rows_knob()
+        x = x.contiguous()
+        a, b = layer.w13, layer.w2
+        hidden, inter = a.K, b.K
+        ns1, ns2 = _layer_splits(hidden, inter)
+        is_ = shared.inter if shared is not None else 0
+        wsb = ctypes.c_size_t(0)
+        call("moek_block_workspace_bytes", m, top_k, hidden, inter, e, is_, ctypes.byref(wsb))
+        ws = _scratch("block_ws", wsb.value, torch.uint8, x.device)
+        st = _layer_state(x.device, layer.E, hidden, inter)
+        ids = torch.empty((m, top_k), dtype=torch.int32, device=x.device) if return_routing else None
+        w = torch.empty((m, top_k), dtype=torch.float32, device=x.device) if return_routing else None
+        sh = [None] * 5 if shared is None else [shared.w_gu, shared.s_gu, shared.w_d, shared.s_d, shared.w_sg]
+        call("moek_moe_block", _ptr(x), m, hidden, inter, e, _ptr(w_gate.contiguous()), top_k, int(renormalize),
+             _ptr(ids), _ptr(w), _ptr(a.w), _ptr(a.sp), _ptr(a.g), _ptr(a.exc_off), _ptr(a.exc_ent), _ptr(b.w),
+             _ptr(b.sp), _ptr(b.g), _ptr(b.exc_off), _ptr(b.exc_ent), ns1, ns2, is_, *[_ptr(t) for t in sh], _ptr(ws),
+             ws.numel(), _ptr(st), st.numel(), _ptr(error_word(x.device)), _ptr(output), _stream(x.device))
+        return (output, (w, ids)) if return_routing else output
+    logits = router_gate(x, w_gate)
+    w, ids = router_topk(logits, top_k, renormalize)
+    rows = moe_rows(x, layer, w, ids).view(m, top_k, hid)
+    valid = ((ids >= 0) & (ids < layer.E)).unsqueeze(-1)
+    acc = torch.zeros((m, hid), dtype=torch.float32, device=x.device)
+    for j in range(top_k):  # slot order, as the oracle (invalid slots' rows hold arbitrary values: left out)
+        acc = acc + torch.where(valid[:, j], rows[:, j], 0.0)
+    if shared is not None:
+        acc = acc + shared_expert(x, shared)
+    output.copy_(acc.to(torch.bfloat16))
+    return (output, (w, ids)) if return_routing else output

@@ -80,3 +80,35 @@ def route_zipf(m: int, num_experts: int, top_k: int, seed: int, s: float = 1.1, 
     ids = torch.multinomial(p.float().expand(m, -1), top_k, replacement=False, generator=g)
     w = torch.softmax(torch.randn((m, top_k), generator=g, dtype=torch.float32), dim=-1)
     return ids.to(torch.int32).to(device), w.float().to(device)
+
+
+def quantize_mxfp8(w: torch.Tensor):
+    """w [N, K] (bf16/fp32) -> (codes uint8 [N, K] = float8_e4m3fn bits, scales uint8 [N, K/32] = E8M0 exponents):
+    per block of 32 along K the smallest power-of-two scale that keeps amax / scale <= 448 (e4m3's largest value, so
+    nothing saturates), elements = w / scale rounded to the nearest e4m3; an all-zero block takes scale 2^0."""
+    n, k = w.shape
+    wf = w.float().reshape(n, k // 32, 32)
+    amax = wf.abs().amax(-1)
+    e = torch.where(amax > 0, torch.ceil(torch.log2(amax.clamp_min(2.0 ** -126) / 448.0)), torch.zeros_like(amax))
+    e = e.clamp(-127, 127)
+    q = (wf / torch.exp2(e)[..., None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8).reshape(n, k), (e + 127).to(torch.uint8)
+
+
+def make_shared(hidden: int, inter: int, seed: int, device="cpu"):
+    """A seeded MXFP8 shared expert (the kit's checkpoint format for it): (w_gu codes [2 inter, hidden] with the gate
+    rows first, its scales [2 inter, hidden / 32], w_d codes [hidden, inter], its scales [hidden, inter / 32],
+    shared_expert_gate bf16 [hidden]); weights bf16 N(0, 0.02), the gate vector N(0, 0.02)."""
+    g = torch.Generator(device="cpu").manual_seed(7_000_000 + seed)
+    w_gu = (torch.randn(2 * inter, hidden, generator=g) * 0.02).to(torch.bfloat16)
+    w_d = (torch.randn(hidden, inter, generator=g) * 0.02).to(torch.bfloat16)
+    w_sg = (torch.randn(hidden, generator=g) * 0.02).to(torch.bfloat16)
+    gu, sgu = quantize_mxfp8(w_gu)
+    d, sd = quantize_mxfp8(w_d)
+    return tuple(t.to(device) for t in (gu, sgu, d, sd, w_sg))
+
+
+def make_router_gate(num_experts: int, hidden: int, seed: int, device="cpu") -> torch.Tensor:
+    """The router gate's bf16 weight [E, hidden], N(0, 0.02) (vLLM's unquantised ReplicatedLinear)."""
+    g = torch.Generator(device="cpu").manual_seed(8_000_000 + seed)
+    return (torch.randn(num_experts, hidden, generator=g) * 0.02).to(torch.bfloat16).to(device)
