@@ -6,6 +6,9 @@ Workloads (the reference's configs; synthetic seeded data of those shapes):
            logits -> top-5 -> renormalise);
 - decode32 (config 3): M = 32 tokens (4 streams x 8), Zipf(1.1) routing over a seeded permutation of the experts;
 - prefill  (config 4): M = 6912 tokens, uniform routing; prefill_zipf: the same with Zipf(1.1) routing.
+- block8   the whole MoE block at M = 8 (the routed layer's neighbours): the router gate GEMM, its
+           softmax / top-5 routing, the routed experts and the MXFP8 shared expert (Is = 512) with its sigmoid gate,
+           through ``ops.moe_block``; GB/s over the touched experts' bytes plus the gate's and the shared expert's.
 
 Every workload runs on the same 48 layers of 512 experts (hidden 2048, expert intermediate 512, top-5) with
 independent seeded NVFP4 weights (bf16 N(0, 0.02) quantised; 857 MB per layer, 41 GB in HBM). A step runs the 48
@@ -65,7 +68,11 @@ WORKLOADS = {
     "decode32": dict(m=32, route="zipf", unit="GB/s", desc="multi-stream decode M=32 (4 x 8), Zipf(1.1) routing"),
     "prefill": dict(m=6912, route="uniform", unit="TFLOP/s", desc="prefill chunk M=6912, uniform routing"),
     "prefill_zipf": dict(m=6912, route="zipf", unit="TFLOP/s", desc="prefill chunk M=6912, Zipf(1.1) routing"),
+    "block8": dict(m=8, route="gate", unit="GB/s",
+                   desc="whole MoE block M=8: router gate GEMM -> softmax top-5 -> routed experts, plus the MXFP8 "
+                        "shared expert (Is = 512) with its sigmoid gate"),
 }
+SHARED_INTER = 512  # the block workload's shared-expert width
 
 
 def parse():
@@ -308,18 +315,27 @@ def measure(name, layers, a, dev, world, barrier, headline):
     m, nl = wl["m"], len(layers)
     outs = [torch.empty((m, H), dtype=torch.bfloat16, device=dev) for _ in range(nl)]
 
+    block = wl["route"] == "gate"
+
     def step():
         for l in range(nl):
             ids, wts = layers[l]["route"][name]
-            ops.fused_moe(layers[l]["x"][name], layers[l]["prep"], wts, ids, output=outs[l])
+            if block:
+                ops.moe_block(layers[l]["x"][name], layers[l]["gate"], layers[l]["prep"], layers[l]["shared"], TOPK,
+                              output=outs[l])
+            else:
+                ops.fused_moe(layers[l]["x"][name], layers[l]["prep"], wts, ids, output=outs[l])
 
     graph = make_graph(step, a.warmup)
     ops.check_device_errors(dev)
     clocks = Clocks(dev)
     ms = timed(graph.replay, a.steps, barrier)
     clk = clocks.stop()
+    extra = 0  # the block's gate and shared-expert bytes per layer (weights, scales, the expert gate)
+    if block:
+        extra = E * H * 2 + 3 * SHARED_INTER * H * (1 + 1 / 32) + H * 2
     if wl["unit"] == "GB/s":
-        amount = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] for L in layers) / 1e9
+        amount = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] + extra for L in layers) / 1e9
     else:
         amount = nl * m * TOPK * FLOPS_PER_ROW / 1e12
     ms = over_ranks(ms, world, dev)
@@ -341,11 +357,15 @@ def measure(name, layers, a, dev, world, barrier, headline):
     if os.path.exists(pp):
         peaks = json.load(open(pp))
     traffic, traffic_src = TRAFFIC.get(name, (None, None))
+    if block:  # the block's three kernels together: the step's own time per layer
+        kern_us["layer"] = ms * 1e3 / nl
     if wl["unit"] == "GB/s":  # the whole-layer kernel: every touched expert's gate_up and down bytes, x, out
-        gb = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] for L in layers) / nl
+        gb = sum(touched_bytes(L["prep"], L["route"][name][0], m)[0] + extra for L in layers) / nl
         peak = peaks.get("hbm_gbs", 6650.0)
         achieved = gb / (kern_us["layer"] / 1e6) / 1e9
-        roof = {"kernel": "moek_layer_kernel (whole decode layer, one launch)", "bound": "hbm",
+        roof = {"kernel": "moek_layer_kernel (whole decode layer, one launch)" if not block else
+                "moek_moe_block (router gate, shared expert, whole layer: three launches, timed together)",
+                "bound": "hbm",
                 "achieved": round(achieved, 1), "peak": peak,
                 "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "of fallback",
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
@@ -364,7 +384,7 @@ def measure(name, layers, a, dev, world, barrier, headline):
         roof["down_gemm_avg_us"] = round(kern_us["down_gemm"], 2)
     res = {"workload": wl["desc"], "value": round(value, 3), "unit": wl["unit"], "ms_per_step": round(ms, 4),
            "us_per_layer": round(ms * 1e3 / nl, 2), "roofline": roof, "clocks": clk,
-           "gpu_launches_per_step": ops.launches_per_layer(m, TOPK) * nl}
+           "gpu_launches_per_step": (4 if block else ops.launches_per_layer(m, TOPK)) * nl}
     if wl["unit"] == "GB/s":
         res["touched_experts_per_layer"] = round(
             sum(touched_bytes(L["prep"], L["route"][name][0], m)[1] for L in layers) / nl, 1)
@@ -422,7 +442,7 @@ def main():
             dist.destroy_process_group()
     from qwen38_flash_coder_b200 import prep, synth
 
-    names = [a.workload] + ([] if a.only else [n for n in ("decode8", "decode32", "prefill", "prefill_zipf")
+    names = [a.workload] + ([] if a.only else [n for n in ("decode8", "decode32", "prefill", "prefill_zipf", "block8")
                                                if n != a.workload])
     layers = []
     for l in range(a.layers):
@@ -433,7 +453,15 @@ def main():
         for j, n in enumerate(names):
             seed = 100000 * rank + 100 * l + j
             L["x"][n] = synth.activations(WORKLOADS[n]["m"], H, seed, device=dev)
-            L["route"][n] = route(WORKLOADS[n]["m"], seed, WORKLOADS[n]["route"], dev)
+            if WORKLOADS[n]["route"] == "gate":  # the block routes itself: its gate and shared expert per layer
+                from qwen38_flash_coder_b200 import ops
+
+                L["gate"] = synth.make_router_gate(E, H, l, device=dev)
+                L["shared"] = ops.SharedExpert(*synth.make_shared(H, SHARED_INTER, l, device=dev))
+                w, ids = ops.router_topk(ops.router_gate(L["x"][n], L["gate"]), TOPK, True)
+                L["route"][n] = (ids, w)
+            else:
+                L["route"][n] = route(WORKLOADS[n]["m"], seed, WORKLOADS[n]["route"], dev)
         layers.append(L)
 
     def barrier():

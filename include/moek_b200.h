@@ -200,8 +200,10 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
 
 /* logits fp32 [M, E] = x bf16 [M, H] @ w_gate bf16 [E, H]^T (fp32 sums: eight K slices added in order, the same
  * bits on every call). M <= 64, H % 128 == 0, E % 16 == 0 (else MOEK_ERR_UNSUPPORTED: larger batches are a plain
- * library GEMM). x and w_gate 4-byte aligned. */
-int moek_router_gate(const void* x, int32_t M, int32_t H, const void* w_gate, int32_t E, float* logits, void* stream);
+ * library GEMM). x and w_gate 16-byte aligned. err: the int32 device error word (MOEK_DEV_TIMEOUT if a weight copy's
+ * bounded wait ran out; may be NULL). */
+int moek_router_gate(const void* x, int32_t M, int32_t H, const void* w_gate, int32_t E, float* logits, int32_t* err,
+                     void* stream);
 
 /* Scratch bytes of moek_shared_expert: act bf16 [M, Is] and the expert gate fp32 [M], each rounded up to 256. */
 int moek_shared_workspace_bytes(int32_t M, int32_t Is, size_t* bytes);
@@ -210,10 +212,11 @@ int moek_shared_workspace_bytes(int32_t M, int32_t Is, size_t* bytes);
  * weights in the checkpoint layout: w_gu uint8 [2 Is, H] (float8_e4m3fn bytes; gate rows 0..Is-1, then the up rows),
  * s_gu uint8 [2 Is, H / 32] (E8M0 exponents, one per 32 inputs), w_d uint8 [H, Is], s_d uint8 [H, Is / 32]; w_sg
  * bf16 [H] (shared_expert_gate). Dequantisation is exact for scale bytes in [10, 134], the supported range (the
- * Python wrapper rejects others). M <= 64, H % 128 == 0, Is % 128 == 0. */
+ * Python wrapper rejects others). M <= 64, H % 128 == 0, Is % 128 == 0; x and the weight and scale pointers
+ * 16-byte aligned. err as moek_router_gate. */
 int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is, const uint8_t* w_gu, const uint8_t* s_gu,
                        const uint8_t* w_d, const uint8_t* s_d, const void* w_sg, void* workspace,
-                       size_t workspace_bytes, float* rows, void* stream);
+                       size_t workspace_bytes, float* rows, int32_t* err, void* stream);
 
 /* Scratch bytes of moek_moe_block: logits fp32 [M, E], the shared rows fp32 [M, H], the shared expert's scratch
  * (Is > 0) and the whole-layer kernel's workspace. */

@@ -24,9 +24,10 @@ SIGNATURES = {
     "moek_split_epilogue": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P]),
     "moek_combine": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _P]),
     "moek_router_topk": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
-    "moek_router_gate": (ctypes.c_int, [_P, _I32, _I32, _P, _I32, _P, _P]),
+    "moek_router_gate": (ctypes.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
     "moek_shared_workspace_bytes": (ctypes.c_int, [_I32, _I32, ctypes.POINTER(ctypes.c_size_t)]),
-    "moek_shared_expert": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P]),
+    "moek_shared_expert": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P,
+                                          _P]),
     "moek_block_workspace_bytes": (ctypes.c_int, [_I32] * 6 + [ctypes.POINTER(ctypes.c_size_t)]),
     "moek_moe_block": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _I32, _P, _P] + [_P] * 10 +
                        [_I32, _I32, _I32] + [_P] * 5 + [_P, ctypes.c_size_t, _P, _I64, _P, _P, _P]),

@@ -442,20 +442,20 @@ MOEK_API int moek_moe_layer_logits(const void* x, int32_t M, int32_t H, int32_t 
 }
 
 // ------------------------------------------------------------------ the rest of the MoE block (decode sizes)
-static bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 MOEK_API int moek_router_gate(const void* x, int32_t M, int32_t H, const void* w_gate, int32_t E, float* logits,
-                              void* stream) {
+                              int32_t* err, void* stream) {
   if (M < 0 || M > moek::SHARED_MAXM || H <= 0 || H % 128 || E <= 0 || E % 16)
     return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: router_gate takes decode batches of <= %d tokens, H %% 128 == 0 and "
                                       "E %% 16 == 0 (M %d, H %d, E %d); larger batches are a plain bf16 GEMM",
                 moek::SHARED_MAXM, M, H, E);
   if (M == 0) return MOEK_OK;
-  if (!x || !w_gate || !logits || !aligned4(x) || !aligned4(w_gate))
+  if (!x || !w_gate || !logits || !aligned16(x) || !aligned16(w_gate))
     return fail(MOEK_ERR_ARG, "moek_b200: router_gate null or unaligned pointer");
   return cuda_status(moek::launch_router_gate(static_cast<const __nv_bfloat16*>(x), M, H,
-                                              static_cast<const __nv_bfloat16*>(w_gate), E, logits,
-                                              (cudaStream_t)stream),
+                                              static_cast<const __nv_bfloat16*>(w_gate), E, logits, g_timeout_ns,
+                                              err, (cudaStream_t)stream),
                      "router_gate launch");
 }
 
@@ -471,12 +471,13 @@ MOEK_API int moek_shared_workspace_bytes(int32_t M, int32_t Is, size_t* bytes) {
 
 MOEK_API int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is, const uint8_t* w_gu,
                                 const uint8_t* s_gu, const uint8_t* w_d, const uint8_t* s_d, const void* w_sg,
-                                void* workspace, size_t workspace_bytes, float* rows, void* stream) {
+                                void* workspace, size_t workspace_bytes, float* rows, int32_t* err, void* stream) {
   if (M < 0 || M > moek::SHARED_MAXM || H <= 0 || H % 128 || Is <= 0 || Is % 128)
     return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: shared_expert takes decode batches of <= %d tokens, H %% 128 == 0 "
                                       "and Is %% 128 == 0 (M %d, H %d, Is %d)", moek::SHARED_MAXM, M, H, Is);
   if (M == 0) return MOEK_OK;
-  if (!x || !w_gu || !s_gu || !w_d || !s_d || !w_sg || !rows || !workspace || !aligned4(x))
+  if (!x || !w_gu || !s_gu || !w_d || !s_d || !w_sg || !rows || !workspace || !aligned16(x) || !aligned16(w_gu) ||
+      !aligned16(s_gu) || !aligned16(w_d) || !aligned16(s_d))
     return fail(MOEK_ERR_ARG, "moek_b200: shared_expert null or unaligned pointer");
   if ((int64_t)workspace_bytes < shared_ws_bytes(M, Is))
     return fail(MOEK_ERR_ARG, "moek_b200: shared_expert needs %lld workspace bytes", (long long)shared_ws_bytes(M, Is));
@@ -485,8 +486,8 @@ MOEK_API int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is,
   __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(wp);
   float* sg = reinterpret_cast<float*>(wp + up((int64_t)M * Is * 2));
   return cuda_status(moek::launch_shared_expert(static_cast<const __nv_bfloat16*>(x), M, H, Is, w_gu, s_gu, w_d, s_d,
-                                                static_cast<const __nv_bfloat16*>(w_sg), act, sg, rows,
-                                                (cudaStream_t)stream),
+                                                static_cast<const __nv_bfloat16*>(w_sg), act, sg, rows, g_timeout_ns,
+                                                err, (cudaStream_t)stream),
                      "shared_expert launch");
 }
 
@@ -536,9 +537,9 @@ MOEK_API int moek_moe_block(const void* x, int32_t M, int32_t H, int32_t I, int3
                             workspace_bytes - (size_t)(wp - static_cast<uint8_t*>(workspace)), state, state_ints, err,
                             true, true))
     return rc;
-  if (int rc = moek_router_gate(x, M, H, w_gate, E, logits, stream)) return rc;
+  if (int rc = moek_router_gate(x, M, H, w_gate, E, logits, err, stream)) return rc;
   if (Is > 0) {
-    if (int rc = moek_shared_expert(x, M, H, Is, w_gu, s_gu, w_d, s_d, w_sg, shared_ws, (size_t)sws, rows, stream))
+    if (int rc = moek_shared_expert(x, M, H, Is, w_gu, s_gu, w_d, s_d, w_sg, shared_ws, (size_t)sws, rows, err, stream))
       return rc;
     p.shared = rows;
   }

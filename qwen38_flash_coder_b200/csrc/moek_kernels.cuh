@@ -177,11 +177,11 @@ cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, int coop
 // moek_shared.cu: the router gate GEMM and the MXFP8 shared expert at decode sizes (M <= SHARED_MAXM tokens)
 constexpr int SHARED_MAXM = 64;
 cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_bfloat16* wg, int E, float* logits,
-                               cudaStream_t st);
+                               uint64_t timeout_ns, int* err, cudaStream_t st);
 // act bf16 [M, Is] and sg fp32 [M] are scratch; rows fp32 [M, H] the output
 cudaError_t launch_shared_expert(const __nv_bfloat16* x, int M, int H, int Is, const uint8_t* wgu, const uint8_t* sgu,
                                  const uint8_t* wd, const uint8_t* sd, const __nv_bfloat16* wsg, __nv_bfloat16* act,
-                                 float* sg, float* rows, cudaStream_t st);
+                                 float* sg, float* rows, uint64_t timeout_ns, int* err, cudaStream_t st);
 
 // moek_router.cu: softmax -> top-k -> optional renormalisation (dtype 0 = fp32 logits, 1 = bf16)
 cudaError_t launch_router_topk(const void* logits, int dtype, int M, int E, int k, int renorm, int32_t* ids,

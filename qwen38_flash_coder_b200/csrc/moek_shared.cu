@@ -4,9 +4,11 @@
 // sigmoid expert gate, MXFP8 in the kit's checkpoint, README.md:38).
 //
 // Both are weight-streaming GEMMs at decode sizes (M <= 64 tokens): the gate reads E x H bf16 (2 MB at E = 512,
-// H = 2048), the shared expert 3 x Is x H e4m3 bytes plus one E8M0 scale per 32 (3.1 MB at Is = 512). So each CTA owns
-// 16 weight rows (the 16-row A operand of mma.sync m16n8k16, tokens as the 8-column B operand), its eight warps split
-// K, and the warps' fp32 partials are added in warp order in shared memory, so every call gives the same bits.
+// H = 2048), the shared expert 3 x Is x H e4m3 bytes plus one E8M0 scale per 32 (3.1 MB at Is = 512). Each CTA owns
+// 16 weight rows (the 16-row A operand of mma.sync m16n8k16, tokens as the 8-column B operand): one thread brings the
+// rows (and their scale rows) into shared memory with bulk copies on one mbarrier (bounded wait), rows padded by 16
+// bytes so that the fragment reads are free of bank conflicts; its eight warps split K, and their fp32 partials are
+// added in warp order, so every call gives the same bits.
 //
 // MXFP8 dequantisation is exact: the e4m3 byte's exponent and mantissa bits placed at bf16 bits 4-10 (sign at 15)
 // are the bf16 value e4m3 x 2^-120 (normal and subnormal e4m3 alike), and one bf16 multiply by 2^(s - 7) (the E8M0
@@ -14,9 +16,10 @@
 // product a normal bf16).
 //
 // Kernels (one launch each, chained with programmatic dependent launch):
-//   router_gate_kernel      logits fp32 [M, E] = x @ W_gate^T
-//   shared_gate_up_kernel   act bf16 [M, Is] = bf16(silu(x @ Wg^T) * (x @ Wu^T)) for 16 act columns per CTA, and
-//                           (CTA 0) the expert gate sg fp32 [M] = sigmoid(x @ w_sg)
+//   router_gate_kernel      logits fp32 [M, E] = x @ W_gate^T, 16 experts per CTA
+//   shared_gate_up_kernel   act bf16 [M, Is] = bf16(silu(x @ Wg^T) * (x @ Wu^T)) for 8 act columns per CTA (its 16
+//                           rows: 8 gate rows then their 8 up rows), and (CTA 0) the expert gate sg fp32 [M] =
+//                           sigmoid(x @ w_sg)
 //   shared_down_kernel      rows fp32 [M, H] = sg * (act @ Wd^T) for 16 output columns per CTA
 // The routed layer adds the rows to each token's fp32 sum before its one bf16 rounding (moek_layer.cu).
 #include <cuda_bf16.h>
@@ -89,39 +92,73 @@ __device__ __forceinline__ void reduce_tile(float (*acc)[4], float* red, int nti
   __syncthreads();
 }
 
+// Bring 16 weight rows of `bytes` bytes (row r from src + row_of[r] * bytes) into shared memory, dst_pitch apart, and,
+// when sdst, their scale rows of `sbytes` bytes as two runs of 8 consecutive rows (from ssrc + row_of[0] * sbytes and
+// ssrc + row_of[8] * sbytes; rows 0-7 and 8-15 are consecutive in the source) to sdst, sbytes apart; then wait
+// (bounded) until everything landed. Sizes and addresses are multiples of 16 bytes (the callers' H, Is % 128 == 0).
+__device__ __forceinline__ bool load_rows(uint8_t* dst, int dst_pitch, const uint8_t* src, int bytes, const int* row_of,
+                                          uint8_t* sdst, const uint8_t* ssrc, int sbytes, uint64_t* bar,
+                                          uint64_t timeout_ns, int* err) {
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(bar, 16 * bytes + (sdst ? 16 * sbytes : 0));
+    for (int r = 0; r < 16; r++) bulk_g2s(dst + r * dst_pitch, src + (int64_t)row_of[r] * bytes, bytes, bar);
+    if (sdst) {
+      bulk_g2s(sdst, ssrc + (int64_t)row_of[0] * sbytes, 8 * sbytes, bar);
+      bulk_g2s(sdst + 8 * sbytes, ssrc + (int64_t)row_of[8] * sbytes, 8 * sbytes, bar);
+    }
+  }
+  return mbar_wait(bar, 0, globaltimer() + timeout_ns, err);
+}
+
 // logits[t][e] = sum_h x[t][h] * Wg[e][h]: CTA = 16 experts, warp w = K slice [w H / 8, (w + 1) H / 8).
 __global__ void __launch_bounds__(THREADS) router_gate_kernel(const __nv_bfloat16* x, int M, int H,
-                                                              const __nv_bfloat16* wg, int E, float* logits) {
+                                                              const __nv_bfloat16* wg, int E, float* logits,
+                                                              uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[NW * 16 * SHARED_MAXM];
+  __shared__ uint64_t bar;
+  __shared__ int row_of[16];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int e0 = blockIdx.x * 16, ntile = (M + 7) >> 3, ks = H / NW, pitch = H * 2 + 16;
+  if (threadIdx.x < 16) row_of[threadIdx.x] = e0 + threadIdx.x;
+  // the weights do not depend on the kernel before: they stream in while it finishes; x may come from it
+  const bool ok = load_rows(smem, pitch, reinterpret_cast<const uint8_t*>(wg), H * 2, row_of, nullptr, nullptr, 0,
+                            &bar, timeout_ns, err);
   pdl_wait();
   pdl_launch_dependents();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
-  const int e0 = blockIdx.x * 16, ntile = (M + 7) >> 3, ks = H / NW;
   float acc[MAXT][4];
 #pragma unroll
   for (int t = 0; t < MAXT; t++)
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[t][i] = 0.f;
-  const __nv_bfloat16* r0 = wg + (int64_t)(e0 + g) * H;
-  const __nv_bfloat16* r1 = r0 + 8 * (int64_t)H;
-  for (int k = warp * ks; k < (warp + 1) * ks; k += 16) {
-    const int kk = k + 2 * c;
-    const uint32_t a[4] = {*reinterpret_cast<const uint32_t*>(r0 + kk), *reinterpret_cast<const uint32_t*>(r1 + kk),
-                           *reinterpret_cast<const uint32_t*>(r0 + kk + 8),
-                           *reinterpret_cast<const uint32_t*>(r1 + kk + 8)};
+  if (ok) {
+    const uint8_t* r0 = smem + g * pitch;
+    const uint8_t* r1 = r0 + 8 * pitch;
+#pragma unroll 2
+    for (int k = warp * ks; k < (warp + 1) * ks; k += 16) {
+      const int kb = 2 * (k + 2 * c);
+      const uint32_t a[4] = {*reinterpret_cast<const uint32_t*>(r0 + kb), *reinterpret_cast<const uint32_t*>(r1 + kb),
+                             *reinterpret_cast<const uint32_t*>(r0 + kb + 16),
+                             *reinterpret_cast<const uint32_t*>(r1 + kb + 16)};
 #pragma unroll
-    for (int t = 0; t < MAXT; t++) {
-      if (t < ntile) {
-        uint32_t b0, b1;
-        b_frag(x, M, H, 8 * t + g, kk, b0, b1);
-        mma_16816(acc[t], a, b0, b1);
+      for (int t = 0; t < MAXT; t++) {
+        if (t < ntile) {
+          uint32_t b0, b1;
+          b_frag(x, M, H, 8 * t + g, k + 2 * c, b0, b1);
+          mma_16816(acc[t], a, b0, b1);
+        }
       }
     }
   }
   reduce_tile(acc, red, ntile, M, [&](int row, int tok, float s) { logits[(int64_t)tok * E + e0 + row] = s; });
 }
 
-// A fragment of 16 MXFP8 rows (r0 = row g, r1 = row g + 8, each row H bytes) at k, scaled: the bf16 weights.
+// A fragment of 16 MXFP8 rows in shared memory (r0 = row g, r1 = row g + 8) at byte kk, scaled: the bf16 weights.
 __device__ __forceinline__ void a_frag_mx(const uint8_t* r0, const uint8_t* r1, int kk, uint32_t f0, uint32_t f1,
                                           uint32_t* a) {
   const uint32_t q0 = *reinterpret_cast<const uint16_t*>(r0 + kk), q1 = *reinterpret_cast<const uint16_t*>(r1 + kk);
@@ -133,45 +170,60 @@ __device__ __forceinline__ void a_frag_mx(const uint8_t* r0, const uint8_t* r1, 
   a[3] = bf2_mul(e4m3x2_pattern(q3), f1);
 }
 
-// act[t][16 b + j] = bf16(silu(gate) * up) for gate row 16 b + j and up row Is + 16 b + j; CTA 0 also sg[t].
-__global__ void __launch_bounds__(THREADS) shared_gate_up_kernel(const __nv_bfloat16* x, int M, int H, int Is,
-                                                                 const uint8_t* wgu, const uint8_t* sgu,
-                                                                 const __nv_bfloat16* wsg, __nv_bfloat16* act,
-                                                                 float* sg) {
-  __shared__ float red[NW * 16 * SHARED_MAXM];
-  __shared__ float gsum[16 * SHARED_MAXM];
-  pdl_wait();
-  pdl_launch_dependents();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
-  const int b = blockIdx.x, ntile = (M + 7) >> 3, ks = H / NW, nsc = H / 32;
-  float accg[MAXT][4], accu[MAXT][4];
-#pragma unroll
-  for (int t = 0; t < MAXT; t++)
-#pragma unroll
-    for (int i = 0; i < 4; i++) accg[t][i] = accu[t][i] = 0.f;
-  const int rg = 16 * b + g, ru = Is + 16 * b + g;  // this lane's gate and up rows (and + 8)
+// The shared expert's 16-row MXFP8 GEMM of one CTA: acc[t] += W[rows] . B[tokens], W rows and scale rows in shared
+// memory (pitch bytes apart; scale rows K / 32 bytes apart), B = bf16 [M, K] in global memory, warp = K slice.
+__device__ __forceinline__ void mx_gemm(const uint8_t* w, int pitch, const uint8_t* sc, const __nv_bfloat16* B, int M,
+                                        int K, int ntile, float (*acc)[4]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3, ks = K / NW, nsc = K / 32;
+  const uint8_t* r0 = w + g * pitch;
+  const uint8_t* r1 = r0 + 8 * pitch;
+#pragma unroll 2
   for (int k = warp * ks; k < (warp + 1) * ks; k += 16) {
-    const int kk = k + 2 * c, sb = k >> 5;
-    uint32_t ag[4], au[4];
-    a_frag_mx(wgu + (int64_t)rg * H, wgu + (int64_t)(rg + 8) * H, kk, e8m0_factor2(sgu[(int64_t)rg * nsc + sb]),
-              e8m0_factor2(sgu[(int64_t)(rg + 8) * nsc + sb]), ag);
-    a_frag_mx(wgu + (int64_t)ru * H, wgu + (int64_t)(ru + 8) * H, kk, e8m0_factor2(sgu[(int64_t)ru * nsc + sb]),
-              e8m0_factor2(sgu[(int64_t)(ru + 8) * nsc + sb]), au);
+    const int kk = k + 2 * c;
+    uint32_t a[4];
+    a_frag_mx(r0, r1, kk, e8m0_factor2(sc[g * nsc + (k >> 5)]), e8m0_factor2(sc[(g + 8) * nsc + (k >> 5)]), a);
 #pragma unroll
     for (int t = 0; t < MAXT; t++) {
       if (t < ntile) {
         uint32_t b0, b1;
-        b_frag(x, M, H, 8 * t + g, kk, b0, b1);
-        mma_16816(accg[t], ag, b0, b1);
-        mma_16816(accu[t], au, b0, b1);
+        b_frag(B, M, K, 8 * t + g, kk, b0, b1);
+        mma_16816(acc[t], a, b0, b1);
       }
     }
   }
-  reduce_tile(accg, red, ntile, M, [&](int row, int tok, float s) { gsum[row * SHARED_MAXM + tok] = s; });
+}
+
+// act[t][8 b + j] = bf16(silu(gate row 8 b + j) * (up row Is + 8 b + j)); CTA 0 also sg[t].
+__global__ void __launch_bounds__(THREADS) shared_gate_up_kernel(const __nv_bfloat16* x, int M, int H, int Is,
+                                                                 const uint8_t* wgu, const uint8_t* sgu,
+                                                                 const __nv_bfloat16* wsg, __nv_bfloat16* act,
+                                                                 float* sg, uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[NW * 16 * SHARED_MAXM];
+  __shared__ uint64_t bar;
+  __shared__ int row_of[16];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x, ntile = (M + 7) >> 3, pitch = H + 16;
+  if (threadIdx.x < 16) row_of[threadIdx.x] = threadIdx.x < 8 ? 8 * b + threadIdx.x : Is + 8 * b + threadIdx.x - 8;
+  uint8_t* sc = smem + 16 * pitch;
+  const bool ok = load_rows(smem, pitch, wgu, H, row_of, sc, sgu, H / 32, &bar, timeout_ns, err);
+  pdl_wait();  // x may come from the kernel before
+  pdl_launch_dependents();
+  float acc[MAXT][4];
+#pragma unroll
+  for (int t = 0; t < MAXT; t++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[t][i] = 0.f;
+  if (ok) mx_gemm(smem, pitch, sc, x, M, H, ntile, acc);
+  // tile rows 0-7 are the gate rows of act columns 8b..8b+7, rows 8-15 their up rows
+  float* gsum = reinterpret_cast<float*>(smem);  // the weights are read: reuse their space for the gate sums
   __syncthreads();
-  reduce_tile(accu, red, ntile, M, [&](int row, int tok, float u) {
-    act[(int64_t)tok * Is + 16 * b + row] = __float2bfloat16_rn(silu(gsum[row * SHARED_MAXM + tok]) * u);
-  });
+  reduce_tile(acc, red, ntile, M, [&](int row, int tok, float s) { gsum[row * SHARED_MAXM + tok] = s; });
+  for (int idx = threadIdx.x; idx < 8 * M; idx += THREADS) {
+    const int j = idx / M, tok = idx - j * M;
+    const float gt = gsum[j * SHARED_MAXM + tok], up = gsum[(j + 8) * SHARED_MAXM + tok];
+    act[(int64_t)tok * Is + 8 * b + j] = __float2bfloat16_rn(silu(gt) * up);
+  }
   if (b == 0) {  // the shared expert's gate: one warp per token, lanes over h, a fixed shuffle order
     for (int t = warp; t < M; t += NW) {
       float s = 0.f;
@@ -187,32 +239,24 @@ __global__ void __launch_bounds__(THREADS) shared_gate_up_kernel(const __nv_bflo
 // rows[t][16 b + j] = sg[t] * sum_i act[t][i] * Wd[16 b + j][i]
 __global__ void __launch_bounds__(THREADS) shared_down_kernel(const __nv_bfloat16* act, int M, int H, int Is,
                                                               const uint8_t* wd, const uint8_t* sd, const float* sg,
-                                                              float* rows) {
+                                                              float* rows, uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[NW * 16 * SHARED_MAXM];
+  __shared__ uint64_t bar;
+  __shared__ int row_of[16];
+  const int b = blockIdx.x, ntile = (M + 7) >> 3, pitch = Is + 16;
+  if (threadIdx.x < 16) row_of[threadIdx.x] = 16 * b + threadIdx.x;
+  uint8_t* sc = smem + 16 * pitch;
+  // the weights do not depend on the kernel before: they are in flight while it finishes
+  const bool ok = load_rows(smem, pitch, wd, Is, row_of, sc, sd, Is / 32, &bar, timeout_ns, err);
   pdl_wait();  // act and sg of the gate_up kernel
   pdl_launch_dependents();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
-  const int b = blockIdx.x, ntile = (M + 7) >> 3, ks = Is / NW, nsc = Is / 32;
   float acc[MAXT][4];
 #pragma unroll
   for (int t = 0; t < MAXT; t++)
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[t][i] = 0.f;
-  const int r = 16 * b + g;
-  for (int k = warp * ks; k < (warp + 1) * ks; k += 16) {
-    const int kk = k + 2 * c, sb = k >> 5;
-    uint32_t a[4];
-    a_frag_mx(wd + (int64_t)r * Is, wd + (int64_t)(r + 8) * Is, kk, e8m0_factor2(sd[(int64_t)r * nsc + sb]),
-              e8m0_factor2(sd[(int64_t)(r + 8) * nsc + sb]), a);
-#pragma unroll
-    for (int t = 0; t < MAXT; t++) {
-      if (t < ntile) {
-        uint32_t b0, b1;
-        b_frag(act, M, Is, 8 * t + g, kk, b0, b1);
-        mma_16816(acc[t], a, b0, b1);
-      }
-    }
-  }
+  if (ok) mx_gemm(smem, pitch, sc, act, M, Is, ntile, acc);
   reduce_tile(acc, red, ntile, M, [&](int row, int tok, float s) {
     rows[(int64_t)tok * H + 16 * b + row] = __fmul_rn(sg[tok], s);
   });
@@ -221,18 +265,28 @@ __global__ void __launch_bounds__(THREADS) shared_down_kernel(const __nv_bfloat1
 }  // namespace sh
 
 cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_bfloat16* wg, int E, float* logits,
-                               cudaStream_t st) {
-  return launch_pdl(sh::router_gate_kernel, dim3(E / 16), dim3(sh::THREADS), 0, st, x, M, H, wg, E, logits);
+                               uint64_t timeout_ns, int* err, cudaStream_t st) {
+  const int smem = 16 * (H * 2 + 16);
+  cudaError_t e = cudaFuncSetAttribute(sh::router_gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(sh::router_gate_kernel, dim3(E / 16), dim3(sh::THREADS), smem, st, x, M, H, wg, E, logits,
+                    timeout_ns, err);
 }
 
 cudaError_t launch_shared_expert(const __nv_bfloat16* x, int M, int H, int Is, const uint8_t* wgu, const uint8_t* sgu,
                                  const uint8_t* wd, const uint8_t* sd, const __nv_bfloat16* wsg, __nv_bfloat16* act,
-                                 float* sg, float* rows, cudaStream_t st) {
-  cudaError_t e = launch_pdl(sh::shared_gate_up_kernel, dim3(Is / 16), dim3(sh::THREADS), 0, st, x, M, H, Is, wgu, sgu,
-                             wsg, act, sg);
+                                 float* sg, float* rows, uint64_t timeout_ns, int* err, cudaStream_t st) {
+  const int smem1 = 16 * (H + 16) + 16 * (H / 32), smem2 = 16 * (Is + 16) + 16 * (Is / 32);
+  cudaError_t e = cudaFuncSetAttribute(sh::shared_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(sh::shared_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
   if (e != cudaSuccess) return e;
-  return launch_pdl(sh::shared_down_kernel, dim3(H / 16), dim3(sh::THREADS), 0, st, static_cast<const __nv_bfloat16*>(act),
-                    M, H, Is, wd, sd, static_cast<const float*>(sg), rows);
+  e = launch_pdl(sh::shared_gate_up_kernel, dim3(Is / 8), dim3(sh::THREADS), smem1, st, x, M, H, Is, wgu, sgu, wsg, act,
+                 sg, timeout_ns, err);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(sh::shared_down_kernel, dim3(H / 16), dim3(sh::THREADS), smem2, st,
+                    static_cast<const __nv_bfloat16*>(act), M, H, Is, wd, sd, static_cast<const float*>(sg), rows,
+                    timeout_ns, err);
 }
 
 }  // namespace moek

@@ -546,7 +546,8 @@ def router_gate(hidden_states: torch.Tensor, w_gate: torch.Tensor) -> torch.Tens
         return x.float() @ w_gate.float().t()
     x, w_gate = x.contiguous(), w_gate.contiguous()
     logits = torch.empty((m, e), dtype=torch.float32, device=x.device)
-    call("moek_router_gate", _ptr(x), m, hid, _ptr(w_gate), e, _ptr(logits), _stream(x.device))
+    call("moek_router_gate", _ptr(x), m, hid, _ptr(w_gate), e, _ptr(logits), _ptr(error_word(x.device)),
+         _stream(x.device))
     return logits
 
 
@@ -569,7 +570,8 @@ def shared_expert(hidden_states: torch.Tensor, shared: SharedExpert) -> torch.Te
     ws = _scratch("shared_ws", wsb.value, torch.uint8, x.device)
     rows = torch.empty((m, hid), dtype=torch.float32, device=x.device)
     call("moek_shared_expert", _ptr(x), m, hid, shared.inter, _ptr(shared.w_gu), _ptr(shared.s_gu), _ptr(shared.w_d),
-         _ptr(shared.s_d), _ptr(shared.w_sg), _ptr(ws), ws.numel(), _ptr(rows), _stream(x.device))
+         _ptr(shared.s_d), _ptr(shared.w_sg), _ptr(ws), ws.numel(), _ptr(rows), _ptr(error_word(x.device)),
+         _stream(x.device))
     return rows
 
 

@@ -46,7 +46,10 @@ def test_block_entry_points_reject_bad_arguments():
     assert lib.moek_shared_workspace_bytes(8, 512, ctypes.byref(b)) == 0 and b.value == 8 * 512 * 2 + 256
     assert lib.moek_block_workspace_bytes(8, 5, 2048, 512, 512, 512, ctypes.byref(b)) == 0 and b.value > 8 * 2048 * 4
     fake = ctypes.c_void_p(256)  # never dereferenced: each call fails its argument checks first
-    assert lib.moek_router_gate(fake, 65, 2048, fake, 512, fake, None) == 3  # M > 64: a library GEMM's job
-    assert lib.moek_router_gate(fake, 8, 2048, fake, 100, fake, None) == 3  # E % 16
-    assert lib.moek_shared_expert(fake, 8, 2048, 500, fake, fake, fake, fake, fake, fake, 1 << 20, fake, None) == 3
-    assert lib.moek_shared_expert(fake, 8, 2048, 512, fake, fake, fake, fake, fake, fake, 16, fake, None) == 1
+    assert lib.moek_router_gate(fake, 65, 2048, fake, 512, fake, None, None) == 3  # M > 64: a library GEMM's job
+    assert lib.moek_router_gate(fake, 8, 2048, fake, 100, fake, None, None) == 3  # E % 16
+    assert lib.moek_router_gate(ctypes.c_void_p(264), 8, 2048, fake, 512, fake, None, None) == 1  # x not 16-aligned
+    args = [fake, 8, 2048, 500, fake, fake, fake, fake, fake, fake, 1 << 20, fake, None, None]
+    assert lib.moek_shared_expert(*args) == 3  # Is % 128
+    args[3], args[10] = 512, 16
+    assert lib.moek_shared_expert(*args) == 1  # workspace too small
