@@ -403,7 +403,11 @@ def measure(name, layers, a, dev, world, barrier, headline):
                 dx[l].copy_(hx[l], non_blocking=True)
                 did[l].copy_(hid[l], non_blocking=True)
                 dw[l].copy_(hw[l], non_blocking=True)
-                ops.fused_moe(dx[l], layers[l]["prep"], dw[l], did[l], output=outs[l])
+                if block:  # the block routes itself: x in, its output out (ids and weights are copied all the same)
+                    ops.moe_block(dx[l], layers[l]["gate"], layers[l]["prep"], layers[l]["shared"], TOPK,
+                                  output=outs[l])
+                else:
+                    ops.fused_moe(dx[l], layers[l]["prep"], dw[l], did[l], output=outs[l])
                 hout[l].copy_(outs[l], non_blocking=True)
 
         eg = make_graph(e2e_step, 2)
@@ -413,7 +417,8 @@ def measure(name, layers, a, dev, world, barrier, headline):
                       "h2d_bytes_per_step": sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4
                                                 for x, r, w in zip(hx, hid, hw)),
                       "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
-                      "api": "ops.fused_moe with host copies, one CUDA graph per step"}
+                      "api": ("ops.moe_block" if block else "ops.fused_moe") + " with host copies, one CUDA graph "
+                             "per step"}
         res["eager_ms_per_step"] = round(over_ranks(timed(step, max(2, a.steps // 4), barrier), world, dev), 4)
     del graph
     return res
