@@ -192,6 +192,28 @@ int moek_layer_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, i
  *           gate_up stages over the CTAs itself (from the number of blocks and the grid), which changes only the
  *           order of fp32 partial sums; the same routing always gives the same plan and the same bits.
  *   err     int32 device error word (MOEK_DEV_*), zero before the call. */
+/* ---- Load-time preparation on the GPU: checkpoint NVFP4 matrices (codes uint8 [E, N, K/2], element 2i in the low
+ * nibble; E4M3 block scales [E, N, K/16]; global scales fp32 [E]) into the kernels' formats. Replaces, at model load,
+ * vLLM's prepare_nvfp4_moe_layer_for_marlin (vllm/.../marlin_utils_fp4.py:288-386: the Marlin repack and scale
+ * processing) plus the kit's codec and tiling (files/mbx_moek.py:61-172), with the same scale bytes. K % 128 == 0,
+ * N % 256 == 0 (gate_up: N/2 % 128 == 0). Order: moek_prep_scales (its workspace from moek_prep_workspace_bytes; it
+ * synchronises the stream twice to read the matrix's largest scale and the exception count back), then
+ * moek_prep_exceptions with the same workspace and an exc_ent of max(1, *n_exc_out) int32; moek_prep_weights any
+ * time. */
+int moek_prep_workspace_bytes(int32_t E, int32_t N, int32_t K, size_t* bytes);
+/* w_out int32 [E, K/16, 2N]: the tiled code words (per (expert, 256-row item, 64-k stage) an 8 KB block). */
+int moek_prep_weights(const uint8_t* codes, int32_t E, int32_t N, int32_t K, int32_t gate_up, int32_t* w_out,
+                      void* stream);
+/* sp_out uint8 [E, N/256, K/128, 1056] (the kit's packed scales, an item's two runs side by side), g_out fp32 [E]
+ * (gs * 2^119 / sf), exc_off_out int32 [E * N/256 * K/128 + 1]; *sf_out the shared power-of-two scale factor,
+ * *n_exc_out the number of exception entries. */
+int moek_prep_scales(const uint8_t* scales, const float* gs, int32_t E, int32_t N, int32_t K, int32_t gate_up,
+                     void* workspace, size_t workspace_bytes, uint8_t* sp_out, float* g_out, int32_t* exc_off_out,
+                     float* sf_out, int64_t* n_exc_out, void* stream);
+/* exc_ent int32 [n_exc]: position | k-group << 16 | scale byte << 24, per (expert, item, run) list in order. */
+int moek_prep_exceptions(const uint8_t* scales, int32_t E, int32_t N, int32_t K, int32_t gate_up, float sf,
+                         const void* workspace, const int32_t* exc_off, int32_t* exc_ent, void* stream);
+
 /* ---- The rest of the MoE block at decode sizes: the router gate GEMM and the MXFP8 shared expert, whose fp32 rows
  * the whole-layer kernel adds to each token's sum before its one bf16 rounding. They replace, for decode batches, the
  * block's other steps around the routed experts (files/v54/model.py:193-210 subclasses vLLM's

@@ -25,6 +25,11 @@ SIGNATURES = {
     "moek_combine": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _P]),
     "moek_router_topk": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "moek_router_gate": (ctypes.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
+    "moek_prep_workspace_bytes": (ctypes.c_int, [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)]),
+    "moek_prep_weights": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P]),
+    "moek_prep_scales": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _I32, _P, ctypes.c_size_t, _P, _P, _P,
+                                        ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int64), _P]),
+    "moek_prep_exceptions": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, ctypes.c_float, _P, _P, _P, _P]),
     "moek_shared_workspace_bytes": (ctypes.c_int, [_I32, _I32, ctypes.POINTER(ctypes.c_size_t)]),
     "moek_shared_expert": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P,
                                           _P]),

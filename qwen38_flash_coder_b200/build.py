@@ -20,7 +20,7 @@ from concurrent.futures import ThreadPoolExecutor
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 SOURCES = ["moek_abi.cu", "moek_align.cu", "moek_decode.cu", "moek_layer.cu", "moek_prefill.cu", "moek_ep.cu",
-           "moek_router.cu", "moek_shared.cu"]
+           "moek_router.cu", "moek_shared.cu", "moek_prep.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden"]
 VARIANTS = {"": [], "trace": ["-DMOEK_TRACE"], "debug": ["-DMOEK_DEBUG_CHECKS"]}

@@ -441,6 +441,84 @@ MOEK_API int moek_moe_layer_logits(const void* x, int32_t M, int32_t H, int32_t 
                      "moe_layer_logits launch");
 }
 
+// ----------------------------------------------------------------------------- load-time weight preparation
+static int prep_shape(int32_t E, int32_t N, int32_t K, int32_t gate_up) {
+  if (E <= 0 || N <= 0 || K <= 0 || K % 128 || N % 256 || (gate_up && (N / 2) % 128))
+    return fail(MOEK_ERR_ARG, "moek_b200: prep needs K %% 128 == 0, N %% 256 == 0 (and N/2 %% 128 == 0 for gate_up) "
+                              "(E %d, N %d, K %d)", E, N, K);
+  return MOEK_OK;
+}
+static int64_t prep_keys(int32_t E, int32_t N, int32_t K) { return (int64_t)E * (N / 256) * (K / 128); }
+static int64_t prep_ws_bytes(int32_t E, int32_t N, int32_t K) {
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return up(prep_keys(E, N, K) * 32 * 4) + up(prep_keys(E, N, K) * 4) + 256;
+}
+
+MOEK_API int moek_prep_workspace_bytes(int32_t E, int32_t N, int32_t K, size_t* bytes) {
+  if (!bytes) return fail(MOEK_ERR_ARG, "moek_b200: prep workspace query needs an output");
+  if (int rc = prep_shape(E, N, K, 0)) return rc;
+  *bytes = (size_t)prep_ws_bytes(E, N, K);
+  return MOEK_OK;
+}
+
+MOEK_API int moek_prep_weights(const uint8_t* codes, int32_t E, int32_t N, int32_t K, int32_t gate_up, int32_t* w_out,
+                               void* stream) {
+  if (int rc = prep_shape(E, N, K, gate_up)) return rc;
+  if (!codes || !w_out || (reinterpret_cast<uintptr_t>(codes) & 3))
+    return fail(MOEK_ERR_ARG, "moek_b200: prep_weights null or unaligned pointer");
+  return cuda_status(moek::launch_prep_weights(codes, E, N, K, gate_up ? 1 : 0, reinterpret_cast<uint32_t*>(w_out),
+                                               (cudaStream_t)stream),
+                     "prep_weights launch");
+}
+
+MOEK_API int moek_prep_scales(const uint8_t* scales, const float* gs, int32_t E, int32_t N, int32_t K, int32_t gate_up,
+                              void* workspace, size_t workspace_bytes, uint8_t* sp_out, float* g_out,
+                              int32_t* exc_off_out, float* sf_out, int64_t* n_exc_out, void* stream) {
+  if (int rc = prep_shape(E, N, K, gate_up)) return rc;
+  if (!scales || !gs || !workspace || !sp_out || !g_out || !exc_off_out || !sf_out || !n_exc_out)
+    return fail(MOEK_ERR_ARG, "moek_b200: prep_scales null pointer");
+  if ((int64_t)workspace_bytes < prep_ws_bytes(E, N, K))
+    return fail(MOEK_ERR_ARG, "moek_b200: prep_scales needs %lld workspace bytes", (long long)prep_ws_bytes(E, N, K));
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  const int64_t nkeys = prep_keys(E, N, K);
+  uint8_t* wp = static_cast<uint8_t*>(workspace);
+  int* cnt = reinterpret_cast<int*>(wp);
+  int* total = reinterpret_cast<int*>(wp + up(nkeys * 32 * 4));
+  unsigned int* mx = reinterpret_cast<unsigned int*>(wp + up(nkeys * 32 * 4) + up(nkeys * 4));
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = moek::launch_prep_scale_max(scales, (int64_t)E * N * (K / 16), mx, st);
+  unsigned int m = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&m, mx, sizeof(m), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_status(e, "prep_scales scale max");
+  // the shared factor: the largest power of two sf with max * 2^7 * sf <= 448 * 2^7 (vllm/.../marlin_utils_fp4.py:
+  // 30-60, _nvfp4_compute_scale_factor); 1 when no scale is positive
+  float sf = 1.0f;
+  if (m) {
+    const float v = (m >> 3) ? ldexpf(1.0f + (m & 7) * 0.125f, (int)(m >> 3) - 7) : ldexpf((float)(m & 7), -9);
+    const float mxv = v * 128.0f, lim = 448.0f * 128.0f;
+    while (mxv < lim && mxv * sf * 2.0f <= lim) sf *= 2.0f;
+  }
+  e = moek::launch_prep_scales(scales, gs, E, N, K, gate_up ? 1 : 0, sf, sp_out, g_out, cnt, total, exc_off_out, st);
+  int n = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&n, exc_off_out + nkeys, sizeof(n), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_status(e, "prep_scales");
+  *sf_out = sf;
+  *n_exc_out = n;
+  return MOEK_OK;
+}
+
+MOEK_API int moek_prep_exceptions(const uint8_t* scales, int32_t E, int32_t N, int32_t K, int32_t gate_up, float sf,
+                                  const void* workspace, const int32_t* exc_off, int32_t* exc_ent, void* stream) {
+  if (int rc = prep_shape(E, N, K, gate_up)) return rc;
+  if (!scales || !workspace || !exc_off || !exc_ent) return fail(MOEK_ERR_ARG, "moek_b200: prep_exceptions null pointer");
+  return cuda_status(moek::launch_prep_exceptions(scales, E, N, K, gate_up ? 1 : 0, sf,
+                                                  static_cast<const int*>(workspace), exc_off, exc_ent,
+                                                  (cudaStream_t)stream),
+                     "prep_exceptions launch");
+}
+
 // ------------------------------------------------------------------ the rest of the MoE block (decode sizes)
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 

@@ -174,6 +174,17 @@ struct LayerParams {
 // rows per block: 8/16/32; coop: cooperative launch (every CTA resident together, the default)
 cudaError_t launch_layer(const LayerParams& p, int block_rows, int sms, int coop, cudaStream_t st);
 
+// moek_prep.cu: load-time conversion of checkpoint NVFP4 matrices (E4M3 scales [E, N, K/16], codes [E, N, K/2])
+cudaError_t launch_prep_scale_max(const uint8_t* scales, int64_t n, unsigned int* out, cudaStream_t st);
+cudaError_t launch_prep_weights(const uint8_t* codes, int E, int N, int K, int gate_up, uint32_t* out,
+                                cudaStream_t st);
+// sp [E, N/256, K/128, 1056], g [E], cnt [nkeys, 32] (the blocks' exclusive prefixes within their list on return),
+// total [nkeys], exc_off [nkeys + 1]; nkeys = E * N/256 * K/128
+cudaError_t launch_prep_scales(const uint8_t* scales, const float* gs, int E, int N, int K, int gate_up, float sf,
+                               uint8_t* sp, float* g, int* cnt, int* total, int* exc_off, cudaStream_t st);
+cudaError_t launch_prep_exceptions(const uint8_t* scales, int E, int N, int K, int gate_up, float sf,
+                                   const int* cnt_prefix, const int* exc_off, int* ent, cudaStream_t st);
+
 // moek_shared.cu: the router gate GEMM and the MXFP8 shared expert at decode sizes (M <= SHARED_MAXM tokens)
 constexpr int SHARED_MAXM = 64;
 cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_bfloat16* wg, int E, float* logits,

@@ -1,4 +1,6 @@
-"""Load-time conversion of checkpoint NVFP4 experts into the kernels' layouts (torch, runs on the weights' device).
+"""Load-time conversion of checkpoint NVFP4 experts into the kernels' layouts: this build's prep kernels on a CUDA
+device (csrc/moek_prep.cu, ``PreparedMatrix``), and the same conversion restated with torch ops below (the CPU path,
+and the kernels' test reference).
 
 Input: the checkpoint tensors vLLM hands to ``prepare_nvfp4_moe_layer_for_marlin`` (vllm/.../marlin_utils_fp4.py:
 288-298): ``weight`` uint8 [E, N, K/2] (element 2i in the low nibble), ``weight_scale`` float8 E4M3 [E, N, K/16],
@@ -189,19 +191,55 @@ def untile_weights(w: torch.Tensor, n: int, gate_up: bool) -> torch.Tensor:
 
 # ------------------------------------------------------------------------------------------------------------- layer
 class PreparedMatrix:
-    """One matrix of a layer in the kernels' format."""
+    """One matrix of a layer in the kernels' format. On a CUDA device the conversion runs in this build's prep
+    kernels (``native``, csrc/moek_prep.cu); elsewhere, or with ``native=False``, in the torch restatement above
+    (the same bytes: tests/test_gpu_prep.py compares the two)."""
 
-    def __init__(self, codes, scales, gs, gate_up: bool):
+    def __init__(self, codes, scales, gs, gate_up: bool, native=None):
         e, n, k2 = codes.shape
         k = 2 * k2
         check_shapes(n, k, gate_up)
         self.gate_up, self.E, self.N, self.K = gate_up, e, n, k
+        if native is None:
+            native = codes.is_cuda
+        if native:
+            self._prepare_native(codes, scales, gs)
+            return
         self.sf = scale_factor(scales)
         sb = marlin_scale_bytes(scales, self.sf)
         packed, self.exc_off, self.exc_ent = pack_scales(sb, gate_up)
         self.sp = tile_scales(packed, n, gate_up)
         self.g = global_scale(gs, self.sf).contiguous()
         self.w = tile_weights(codes, gate_up)
+
+    def _prepare_native(self, codes, scales, gs):
+        import ctypes
+
+        from ._lib import call
+
+        e, n, k, gu = self.E, self.N, self.K, int(self.gate_up)
+        dev = codes.device
+        codes = codes.contiguous()
+        sc = scales.contiguous().view(torch.uint8)
+        gs = gs.float().contiguous()
+        st = torch.cuda.current_stream(dev).cuda_stream
+        wsb = ctypes.c_size_t(0)
+        call("moek_prep_workspace_bytes", e, n, k, ctypes.byref(wsb))
+        ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
+        nkeys = e * (n // 256) * (k // 128)
+        self.sp = torch.empty((e, n // 256, k // 128, 2 * RUN), dtype=torch.uint8, device=dev)
+        self.g = torch.empty(e, dtype=torch.float32, device=dev)
+        self.exc_off = torch.empty(nkeys + 1, dtype=torch.int32, device=dev)
+        sf, nexc = ctypes.c_float(0.0), ctypes.c_int64(0)
+        call("moek_prep_scales", sc.data_ptr(), gs.data_ptr(), e, n, k, gu, ws.data_ptr(), ws.numel(),
+             self.sp.data_ptr(), self.g.data_ptr(), self.exc_off.data_ptr(), ctypes.byref(sf), ctypes.byref(nexc), st)
+        self.sf = float(sf.value)
+        self.exc_ent = torch.zeros(max(1, nexc.value), dtype=torch.int32, device=dev)
+        if nexc.value:
+            call("moek_prep_exceptions", sc.data_ptr(), e, n, k, gu, sf, ws.data_ptr(), self.exc_off.data_ptr(),
+                 self.exc_ent.data_ptr(), st)
+        self.w = torch.empty((e, k // 16, 2 * n), dtype=torch.int32, device=dev)
+        call("moek_prep_weights", codes.data_ptr(), e, n, k, gu, self.w.data_ptr(), st)
 
     def nbytes(self) -> int:
         """Bytes the kernels read for the whole matrix (weights + packed scales + exception lists)."""
@@ -218,9 +256,9 @@ def check_shapes(n: int, k: int, gate_up: bool):
 class PreparedLayer:
     """Both matrices of one routed-expert layer (w13 = gate rows then up rows, w2 = down)."""
 
-    def __init__(self, w13, w2):
-        self.w13 = PreparedMatrix(*w13, gate_up=True)
-        self.w2 = PreparedMatrix(*w2, gate_up=False)
+    def __init__(self, w13, w2, native=None):
+        self.w13 = PreparedMatrix(*w13, gate_up=True, native=native)
+        self.w2 = PreparedMatrix(*w2, gate_up=False, native=native)
         self.E = self.w13.E
         self.hidden = self.w13.K
         self.inter = self.w13.N // 2
