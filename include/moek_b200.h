@@ -240,13 +240,14 @@ int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is, const ui
                        const uint8_t* w_d, const uint8_t* s_d, const void* w_sg, void* workspace,
                        size_t workspace_bytes, float* rows, int32_t* err, void* stream);
 
-/* Scratch bytes of moek_moe_block: logits fp32 [M, E], the shared rows fp32 [M, H], the shared expert's scratch
- * (Is > 0) and the whole-layer kernel's workspace. */
+/* Scratch bytes of moek_moe_block: logits fp32 [M, E], the shared rows fp32 [M, H], the shared expert's scratch,
+ * the routing (ids int32 and weights fp32 [M, top_k]) and the whole-layer kernel's workspace. */
 int moek_block_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t E, int32_t Is, size_t* bytes);
 
-/* The whole MoE block for a decode batch (M <= 64 tokens, E <= 512), three or four launches chained with programmatic
- * dependent launch: moek_router_gate, moek_shared_expert (when Is > 0) and the whole-layer kernel from the logits
- * (softmax, top_k, renormalised when renormalize != 0; as moek_moe_layer_logits) with the shared rows added:
+/* The whole MoE block for a decode batch (M <= 64 tokens, E <= 512, E % 16 == 0, top_k <= 32), three launches chained
+ * with programmatic dependent launch: the router gate GEMM beside the shared expert's gate_up (one grid), the shared
+ * expert's down beside the routing of the logits (softmax, top_k, renormalised when renormalize != 0; the router
+ * kernel's per-token code), then the whole-layer kernel from those ids and weights with the shared rows added:
  * out bf16 [M, H] = bf16(sum over valid slots j in order of topk_w * down_e(...) + shared row). The routed weights and
  * the state as moek_moe_layer; the shared expert's tensors as moek_shared_expert (ignored when Is = 0);
  * topk_ids_out / topk_w_out (may be NULL) receive the routing. No reference counterpart as one call: the reference

@@ -571,7 +571,7 @@ MOEK_API int moek_shared_expert(const void* x, int32_t M, int32_t H, int32_t Is,
 
 static int64_t block_ws_bytes(int64_t M, int32_t top_k, int32_t H, int32_t I, int32_t E, int32_t Is) {
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  return up(M * E * 4) + up(M * H * 4) + (Is > 0 ? shared_ws_bytes(M, Is) : 0) +
+  return up(M * E * 4) + up(M * H * 4) + shared_ws_bytes(M, Is) + 2 * up(M * top_k * 4) +
          layer_ws_bytes(M * top_k, H, I, (int)M);
 }
 MOEK_API int moek_block_workspace_bytes(int32_t M, int32_t top_k, int32_t H, int32_t I, int32_t E, int32_t Is,
@@ -592,11 +592,15 @@ MOEK_API int moek_moe_block(const void* x, int32_t M, int32_t H, int32_t I, int3
                             size_t workspace_bytes, int32_t* state, int64_t state_ints, int32_t* err, void* out,
                             void* stream) {
   if (M == 0) return MOEK_OK;
-  if (M < 0 || M > moek::SHARED_MAXM || E > 512 || top_k <= 0 || top_k > E || Is < 0)
-    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_block takes decode batches of <= %d tokens, E <= 512 and "
-                                      "0 < top_k <= E (M %d, E %d, top_k %d, Is %d)", moek::SHARED_MAXM, M, E, top_k,
-                Is);
-  if (!out || !workspace) return fail(MOEK_ERR_ARG, "moek_b200: moe_block null pointer");
+  if (M < 0 || M > moek::SHARED_MAXM || E > 512 || E % 16 || top_k <= 0 || top_k > 32 || top_k > E || Is < 0 ||
+      Is % 128 || H % 128)
+    return fail(MOEK_ERR_UNSUPPORTED, "moek_b200: moe_block takes decode batches of <= %d tokens, E <= 512 with "
+                                      "E %% 16 == 0, 0 < top_k <= min(E, 32), H %% 128 == 0 and Is %% 128 == 0 (M %d, "
+                                      "E %d, top_k %d, H %d, Is %d)", moek::SHARED_MAXM, M, E, top_k, H, Is);
+  if (!out || !workspace || !x || !w_gate || !aligned16(x) || !aligned16(w_gate) ||
+      (Is > 0 && (!w_gu || !s_gu || !w_d || !s_d || !w_sg || !aligned16(w_gu) || !aligned16(s_gu) ||
+                  !aligned16(w_d) || !aligned16(s_d))))
+    return fail(MOEK_ERR_ARG, "moek_b200: moe_block null or unaligned pointer");
   const int64_t need = block_ws_bytes(M, top_k, H, I, E, Is);
   if ((int64_t)workspace_bytes < need)
     return fail(MOEK_ERR_ARG, "moek_b200: moe_block needs %lld workspace bytes", (long long)need);
@@ -606,27 +610,26 @@ MOEK_API int moek_moe_block(const void* x, int32_t M, int32_t H, int32_t I, int3
   wp += up((int64_t)M * E * 4);
   float* rows = reinterpret_cast<float*>(wp);
   wp += up((int64_t)M * H * 4);
-  const int64_t sws = Is > 0 ? shared_ws_bytes(M, Is) : 0;
-  void* shared_ws = wp;
-  wp += sws;
+  __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(wp);
+  float* sg = reinterpret_cast<float*>(wp + up((int64_t)M * Is * 2));
+  wp += shared_ws_bytes(M, Is);
+  int32_t* ids = topk_ids_out ? topk_ids_out : reinterpret_cast<int32_t*>(wp);
+  wp += up((int64_t)M * top_k * 4);
+  float* tw = topk_w_out ? topk_w_out : reinterpret_cast<float*>(wp);
+  wp += up((int64_t)M * top_k * 4);
   moek::LayerParams p;
-  if (int rc = layer_params(p, x, M, H, I, E, nullptr, nullptr, top_k, w13, sp13, g13, exc_off13, exc_ent13, w2, sp2,
-                            g2, exc_off2, exc_ent2, nsplit_gate, nsplit_down, wp,
+  if (int rc = layer_params(p, x, M, H, I, E, ids, tw, top_k, w13, sp13, g13, exc_off13, exc_ent13, w2, sp2, g2,
+                            exc_off2, exc_ent2, nsplit_gate, nsplit_down, wp,
                             workspace_bytes - (size_t)(wp - static_cast<uint8_t*>(workspace)), state, state_ints, err,
-                            true, true))
+                            true))
     return rc;
-  if (int rc = moek_router_gate(x, M, H, w_gate, E, logits, err, stream)) return rc;
-  if (Is > 0) {
-    if (int rc = moek_shared_expert(x, M, H, Is, w_gu, s_gu, w_d, s_d, w_sg, shared_ws, (size_t)sws, rows, err, stream))
-      return rc;
-    p.shared = rows;
-  }
+  cudaError_t e = moek::launch_block_pre_post(static_cast<const __nv_bfloat16*>(x), M, H, E, Is,
+                                              static_cast<const __nv_bfloat16*>(w_gate), logits, w_gu, s_gu, w_d, s_d,
+                                              static_cast<const __nv_bfloat16*>(w_sg), act, sg, rows, top_k,
+                                              renormalize ? 1 : 0, ids, tw, g_timeout_ns, err, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_status(e, "moe_block gate and shared expert launch");
+  if (Is > 0) p.shared = rows;
   p.out = static_cast<__nv_bfloat16*>(out);
-  p.logits = logits;
-  p.logits_bf16 = 0;
-  p.renorm = renormalize ? 1 : 0;
-  p.ids_out = topk_ids_out;
-  p.w_out = topk_w_out;
   return cuda_status(moek::launch_layer(p, layer_block_rows(M), sm_count(), g_layer_coop, (cudaStream_t)stream),
                      "moe_block launch");
 }

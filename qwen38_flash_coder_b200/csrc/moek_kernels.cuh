@@ -189,6 +189,13 @@ cudaError_t launch_prep_exceptions(const uint8_t* scales, int E, int N, int K, i
 constexpr int SHARED_MAXM = 64;
 cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_bfloat16* wg, int E, float* logits,
                                uint64_t timeout_ns, int* err, cudaStream_t st);
+// The MoE block's two kernels before the whole-layer kernel: [router gate | shared gate_up], then [shared down | the
+// routing of the logits into ids / w (softmax, top k, renormalised when renorm)]; Is = 0: no shared expert
+cudaError_t launch_block_pre_post(const __nv_bfloat16* x, int M, int H, int E, int Is, const __nv_bfloat16* wg,
+                                  float* logits, const uint8_t* wgu, const uint8_t* sgu, const uint8_t* wd,
+                                  const uint8_t* sd, const __nv_bfloat16* wsg, __nv_bfloat16* act, float* sg,
+                                  float* rows, int k, int renorm, int32_t* ids, float* w, uint64_t timeout_ns, int* err,
+                                  cudaStream_t st);
 // act bf16 [M, Is] and sg fp32 [M] are scratch; rows fp32 [M, H] the output
 cudaError_t launch_shared_expert(const __nv_bfloat16* x, int M, int H, int Is, const uint8_t* wgu, const uint8_t* sgu,
                                  const uint8_t* wd, const uint8_t* sd, const __nv_bfloat16* wsg, __nv_bfloat16* act,

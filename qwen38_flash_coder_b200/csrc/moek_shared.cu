@@ -26,8 +26,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "moek_common.cuh"
 #include "moek_kernels.cuh"
+#include "moek_route.cuh"
 
 namespace moek {
 namespace sh {
@@ -115,16 +118,22 @@ __device__ __forceinline__ bool load_rows(uint8_t* dst, int dst_pitch, const uin
   return mbar_wait(bar, 0, globaltimer() + timeout_ns, err);
 }
 
-// logits[t][e] = sum_h x[t][h] * Wg[e][h]: CTA = 16 experts, warp w = K slice [w H / 8, (w + 1) H / 8).
-__global__ void __launch_bounds__(THREADS) router_gate_kernel(const __nv_bfloat16* x, int M, int H,
-                                                              const __nv_bfloat16* wg, int E, float* logits,
-                                                              uint64_t timeout_ns, int* err) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[NW * 16 * SHARED_MAXM];
-  __shared__ uint64_t bar;
-  __shared__ int row_of[16];
+// shared memory of the kernels below besides the dynamic weight rows
+struct Smem {
+  float red[NW * 16 * SHARED_MAXM];
+  uint64_t bar;
+  int row_of[16];
+};
+
+// logits[t][e] = sum_h x[t][h] * Wg[e][h]: CTA cta = 16 experts, warp w = K slice [w H / 8, (w + 1) H / 8).
+__device__ __forceinline__ void router_gate_cta(uint8_t* smem, Smem& S, int cta, const __nv_bfloat16* x, int M, int H,
+                                                const __nv_bfloat16* wg, int E, float* logits, uint64_t timeout_ns,
+                                                int* err) {
+  float* red = S.red;
+  uint64_t& bar = S.bar;
+  int* row_of = S.row_of;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
-  const int e0 = blockIdx.x * 16, ntile = (M + 7) >> 3, ks = H / NW, pitch = H * 2 + 16;
+  const int e0 = cta * 16, ntile = (M + 7) >> 3, ks = H / NW, pitch = H * 2 + 16;
   if (threadIdx.x < 16) row_of[threadIdx.x] = e0 + threadIdx.x;
   // the weights do not depend on the kernel before: they stream in while it finishes; x may come from it
   const bool ok = load_rows(smem, pitch, reinterpret_cast<const uint8_t*>(wg), H * 2, row_of, nullptr, nullptr, 0,
@@ -193,17 +202,16 @@ __device__ __forceinline__ void mx_gemm(const uint8_t* w, int pitch, const uint8
   }
 }
 
-// act[t][8 b + j] = bf16(silu(gate row 8 b + j) * (up row Is + 8 b + j)); CTA 0 also sg[t].
-__global__ void __launch_bounds__(THREADS) shared_gate_up_kernel(const __nv_bfloat16* x, int M, int H, int Is,
-                                                                 const uint8_t* wgu, const uint8_t* sgu,
-                                                                 const __nv_bfloat16* wsg, __nv_bfloat16* act,
-                                                                 float* sg, uint64_t timeout_ns, int* err) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[NW * 16 * SHARED_MAXM];
-  __shared__ uint64_t bar;
-  __shared__ int row_of[16];
+// act[t][8 b + j] = bf16(silu(gate row 8 b + j) * (up row Is + 8 b + j)); CTA b = 0 also sg[t].
+__device__ __forceinline__ void shared_gate_up_cta(uint8_t* smem, Smem& S, int b, const __nv_bfloat16* x, int M, int H,
+                                                   int Is, const uint8_t* wgu, const uint8_t* sgu,
+                                                   const __nv_bfloat16* wsg, __nv_bfloat16* act, float* sg,
+                                                   uint64_t timeout_ns, int* err) {
+  float* red = S.red;
+  uint64_t& bar = S.bar;
+  int* row_of = S.row_of;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int b = blockIdx.x, ntile = (M + 7) >> 3, pitch = H + 16;
+  const int ntile = (M + 7) >> 3, pitch = H + 16;
   if (threadIdx.x < 16) row_of[threadIdx.x] = threadIdx.x < 8 ? 8 * b + threadIdx.x : Is + 8 * b + threadIdx.x - 8;
   uint8_t* sc = smem + 16 * pitch;
   const bool ok = load_rows(smem, pitch, wgu, H, row_of, sc, sgu, H / 32, &bar, timeout_ns, err);
@@ -237,14 +245,13 @@ __global__ void __launch_bounds__(THREADS) shared_gate_up_kernel(const __nv_bflo
 }
 
 // rows[t][16 b + j] = sg[t] * sum_i act[t][i] * Wd[16 b + j][i]
-__global__ void __launch_bounds__(THREADS) shared_down_kernel(const __nv_bfloat16* act, int M, int H, int Is,
-                                                              const uint8_t* wd, const uint8_t* sd, const float* sg,
-                                                              float* rows, uint64_t timeout_ns, int* err) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[NW * 16 * SHARED_MAXM];
-  __shared__ uint64_t bar;
-  __shared__ int row_of[16];
-  const int b = blockIdx.x, ntile = (M + 7) >> 3, pitch = Is + 16;
+__device__ __forceinline__ void shared_down_cta(uint8_t* smem, Smem& S, int b, const __nv_bfloat16* act, int M, int H,
+                                                int Is, const uint8_t* wd, const uint8_t* sd, const float* sg,
+                                                float* rows, uint64_t timeout_ns, int* err) {
+  float* red = S.red;
+  uint64_t& bar = S.bar;
+  int* row_of = S.row_of;
+  const int ntile = (M + 7) >> 3, pitch = Is + 16;
   if (threadIdx.x < 16) row_of[threadIdx.x] = 16 * b + threadIdx.x;
   uint8_t* sc = smem + 16 * pitch;
   // the weights do not depend on the kernel before: they are in flight while it finishes
@@ -262,6 +269,71 @@ __global__ void __launch_bounds__(THREADS) shared_down_kernel(const __nv_bfloat1
   });
 }
 
+__global__ void __launch_bounds__(THREADS) router_gate_kernel(const __nv_bfloat16* x, int M, int H,
+                                                              const __nv_bfloat16* wg, int E, float* logits,
+                                                              uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Smem S;
+  router_gate_cta(smem, S, blockIdx.x, x, M, H, wg, E, logits, timeout_ns, err);
+}
+__global__ void __launch_bounds__(THREADS) shared_gate_up_kernel(const __nv_bfloat16* x, int M, int H, int Is,
+                                                                 const uint8_t* wgu, const uint8_t* sgu,
+                                                                 const __nv_bfloat16* wsg, __nv_bfloat16* act,
+                                                                 float* sg, uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Smem S;
+  shared_gate_up_cta(smem, S, blockIdx.x, x, M, H, Is, wgu, sgu, wsg, act, sg, timeout_ns, err);
+}
+__global__ void __launch_bounds__(THREADS) shared_down_kernel(const __nv_bfloat16* act, int M, int H, int Is,
+                                                              const uint8_t* wd, const uint8_t* sd, const float* sg,
+                                                              float* rows, uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Smem S;
+  shared_down_cta(smem, S, blockIdx.x, act, M, H, Is, wd, sd, sg, rows, timeout_ns, err);
+}
+
+// The MoE block's two kernels before the whole-layer kernel (moek_moe_block): the router gate and the shared
+// expert's gate_up share one grid (CTAs [0, E / 16) the gate, the rest the gate_up); then the shared expert's down and
+// the routing of the logits (softmax, top-k, renormalised: the router kernel's per-token code, one warp per token, in
+// the grid's last CTA), so that the layer kernel reads ids and weights.
+__global__ void __launch_bounds__(THREADS) block_pre_kernel(const __nv_bfloat16* x, int M, int H, int E, int Is,
+                                                            const __nv_bfloat16* wg, float* logits, const uint8_t* wgu,
+                                                            const uint8_t* sgu, const __nv_bfloat16* wsg,
+                                                            __nv_bfloat16* act, float* sg, uint64_t timeout_ns,
+                                                            int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Smem S;
+  const int ng = E / 16;
+  if ((int)blockIdx.x < ng)
+    router_gate_cta(smem, S, blockIdx.x, x, M, H, wg, E, logits, timeout_ns, err);
+  else
+    shared_gate_up_cta(smem, S, blockIdx.x - ng, x, M, H, Is, wgu, sgu, wsg, act, sg, timeout_ns, err);
+}
+__global__ void __launch_bounds__(THREADS) block_post_kernel(const __nv_bfloat16* act, int M, int H, int E, int Is,
+                                                             const uint8_t* wd, const uint8_t* sd, const float* sg,
+                                                             float* rows, const float* logits, int k, int renorm,
+                                                             int32_t* ids, float* w, uint64_t timeout_ns, int* err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Smem S;
+  const int nd = Is > 0 ? H / 16 : 0;
+  if ((int)blockIdx.x < nd) {
+    shared_down_cta(smem, S, blockIdx.x, act, M, H, Is, wd, sd, sg, rows, timeout_ns, err);
+  } else {
+    pdl_wait();  // the logits of the kernel before
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    for (int t = threadIdx.x >> 5; t < M; t += NW) {
+      int es;
+      float ws;
+      route_token<16>(logits + (int64_t)t * E, E, k, renorm, es, ws);
+      if (lane < k) {
+        ids[t * k + lane] = es;
+        w[t * k + lane] = ws;
+      }
+    }
+  }
+}
+
 }  // namespace sh
 
 cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_bfloat16* wg, int E, float* logits,
@@ -271,6 +343,25 @@ cudaError_t launch_router_gate(const __nv_bfloat16* x, int M, int H, const __nv_
   if (e != cudaSuccess) return e;
   return launch_pdl(sh::router_gate_kernel, dim3(E / 16), dim3(sh::THREADS), smem, st, x, M, H, wg, E, logits,
                     timeout_ns, err);
+}
+
+cudaError_t launch_block_pre_post(const __nv_bfloat16* x, int M, int H, int E, int Is, const __nv_bfloat16* wg,
+                                  float* logits, const uint8_t* wgu, const uint8_t* sgu, const uint8_t* wd,
+                                  const uint8_t* sd, const __nv_bfloat16* wsg, __nv_bfloat16* act, float* sg,
+                                  float* rows, int k, int renorm, int32_t* ids, float* w, uint64_t timeout_ns, int* err,
+                                  cudaStream_t st) {
+  const int smem1 = std::max(16 * (H * 2 + 16), Is > 0 ? 16 * (H + 16) + 16 * (H / 32) : 0);
+  const int smem2 = Is > 0 ? 16 * (Is + 16) + 16 * (Is / 32) : 0;
+  cudaError_t e = cudaFuncSetAttribute(sh::block_pre_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(sh::block_post_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(sh::block_pre_kernel, dim3(E / 16 + (Is > 0 ? Is / 8 : 0)), dim3(sh::THREADS), smem1, st, x, M, H,
+                 E, Is, wg, logits, wgu, sgu, wsg, act, sg, timeout_ns, err);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(sh::block_post_kernel, dim3((Is > 0 ? H / 16 : 0) + 1), dim3(sh::THREADS), smem2, st,
+                    static_cast<const __nv_bfloat16*>(act), M, H, E, Is, wd, sd, static_cast<const float*>(sg), rows,
+                    static_cast<const float*>(logits), k, renorm, ids, w, timeout_ns, err);
 }
 
 cudaError_t launch_shared_expert(const __nv_bfloat16* x, int M, int H, int Is, const uint8_t* wgu, const uint8_t* sgu,

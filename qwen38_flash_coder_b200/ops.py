@@ -591,7 +591,7 @@ def moe_block(hidden_states: torch.Tensor, w_gate: torch.Tensor, layer: Prepared
         output = torch.empty((m, hid), dtype=torch.bfloat16, device=x.device)
     if m == 0:
         return (output, (None, None)) if return_routing else output
-    if m <= SHARED_MAXM and e <= 512 and e % 16 == 0 and hid % 128 == 0 and _decode_path(m, top_k) and \
+    if m <= SHARED_MAXM and e <= 512 and e % 16 == 0 and hid % 128 == 0 and top_k <= 32 and _decode_path(m, top_k) and \
             x.dtype == torch.bfloat16 and (shared is None or shared.inter % 128 == 0):
         import ctypes
 
