@@ -900,7 +900,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<XR>::MINB) moek_layer_kernel(Laye
                             : nullptr;
     // 32-bit indices: M * H <= 512 x 4096 and (I / 128) x num_ids x H <= 32 x 512 x 4096 < 2^31
     const int H = p.H, nout = p.M * H, sst = n * H;
-    for (int i = (int)blockIdx.x * THREADS + tid; i < nout; i += (int)gridDim.x * THREADS) {
+    // chunks of 32 consecutive outputs (one coalesced warp access each) dealt over the warps CTA by CTA, so that
+    // every SM takes part, not only the first nout / THREADS CTAs
+    for (int ch = warp * (int)gridDim.x + (int)blockIdx.x; ch * 32 < nout; ch += (int)gridDim.x * (THREADS / 32)) {
+      const int i = ch * 32 + lane;
+      if (i >= nout) continue;
       const int tk = i / H, col = i - tk * H;
       float o = 0.f;
       for (int j0 = 0; j0 < k; j0 += 8) {
