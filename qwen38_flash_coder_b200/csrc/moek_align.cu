@@ -170,12 +170,15 @@ __global__ void __launch_bounds__(AT) align_offsets_kernel(int32_t* __restrict__
   extern __shared__ int sm[];
   int* off = sm;  // [E + 1]
   const int t = threadIdx.x;
-  for (int x = t; x < E; x += AT) {  // per expert: exclusive scan over tiles (in place), total kept in off
+  // per expert: the total over tiles (loads issued 16 tiles at a time, not one dependent round trip per tile)
+  for (int x = t; x < E; x += AT) {
     int s = 0;
-    for (int tl = 0; tl < ntiles; tl++) {
-      const int c = counts[(int64_t)tl * E + x];
-      counts[(int64_t)tl * E + x] = s;
-      s += c;
+    for (int tl0 = 0; tl0 < ntiles; tl0 += 16) {
+      int c[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) c[i] = tl0 + i < ntiles ? counts[(int64_t)(tl0 + i) * E + x] : 0;
+#pragma unroll
+      for (int i = 0; i < 16; i++) s += c[i];
     }
     off[x] = s;
   }
@@ -197,8 +200,20 @@ __global__ void __launch_bounds__(AT) align_offsets_kernel(int32_t* __restrict__
     }
   }
   __syncthreads();
-  for (int x = t; x < E; x += AT)
-    for (int tl = 0; tl < ntiles; tl++) counts[(int64_t)tl * E + x] += off[x];
+  // each (tile, expert) count becomes the expert's padded offset plus the counts of the tiles before it
+  for (int x = t; x < E; x += AT) {
+    int s = off[x];
+    for (int tl0 = 0; tl0 < ntiles; tl0 += 16) {
+      int c[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) c[i] = tl0 + i < ntiles ? counts[(int64_t)(tl0 + i) * E + x] : 0;
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        if (tl0 + i < ntiles) counts[(int64_t)(tl0 + i) * E + x] = s;
+        s += c[i];
+      }
+    }
+  }
   const int total = off[E];
   for (int64_t j = t; j < sorted_len; j += AT) sorted_ids[j] = numel;
   for (int b = t; b < expert_len; b += AT) {
