@@ -98,6 +98,23 @@ def route(m, seed, kind, device):
     return synth.route_softmax(m, E, TOPK, seed, device=device)
 
 
+def pack_inputs(x, ids, w):
+    """One layer's inputs as one byte tensor x | ids | weights (x first, so that it stays 16-byte aligned), so that
+    they cross between host and GPU in one copy."""
+    import torch
+
+    return torch.cat([t.contiguous().view(torch.uint8).reshape(-1) for t in (x, ids, w)])
+
+
+def unpack_inputs(buf, m):
+    """Views (x bf16 [m, H], ids int32 [m, TOPK], weights fp32 [m, TOPK]) of a ``pack_inputs`` buffer."""
+    import torch
+
+    xb, ib = m * H * 2, m * TOPK * 4
+    return (buf[:xb].view(torch.bfloat16).view(m, H), buf[xb:xb + ib].view(torch.int32).view(m, TOPK),
+            buf[xb + ib:xb + 2 * ib].view(torch.float32).view(m, TOPK))
+
+
 def touched_bytes(layer, ids, m):
     """Algorithmic bytes of one layer call: touched experts' streamed bytes + x + out + routing."""
     import torch
@@ -313,7 +330,8 @@ def measure(name, layers, a, dev, world, barrier, headline):
 
     wl = WORKLOADS[name]
     m, nl = wl["m"], len(layers)
-    outs = [torch.empty((m, H), dtype=torch.bfloat16, device=dev) for _ in range(nl)]
+    out_all = torch.empty((nl, m, H), dtype=torch.bfloat16, device=dev)  # every layer's output, one buffer
+    outs = list(out_all.unbind(0))
 
     block = wl["route"] == "gate"
 
@@ -390,35 +408,32 @@ def measure(name, layers, a, dev, world, barrier, headline):
             sum(touched_bytes(L["prep"], L["route"][name][0], m)[1] for L in layers) / nl, 1)
     if headline:
         # e2e: the public API with each step's inputs copied from pinned host memory and its outputs read back
-        hx = [L["x"][name].cpu().pin_memory() for L in layers]
-        hid = [L["route"][name][0].cpu().pin_memory() for L in layers]
-        hw = [L["route"][name][1].cpu().pin_memory() for L in layers]
-        hout = [torch.empty((m, H), dtype=torch.bfloat16).pin_memory() for _ in range(nl)]
-        dx = [torch.empty_like(L["x"][name]) for L in layers]
-        did = [torch.empty_like(L["route"][name][0]) for L in layers]
-        dw = [torch.empty_like(L["route"][name][1]) for L in layers]
+        # one pinned staging buffer per layer holding x | ids | weights, so that a layer's inputs cross to the GPU in
+        # one copy (and its output back in one): x (16-byte aligned) at 0, then the int32 ids and the fp32 weights
+        hin = [pack_inputs(L["x"][name], *L["route"][name]).cpu().pin_memory() for L in layers]
+        hout = torch.empty((nl, m, H), dtype=torch.bfloat16).pin_memory()
+        din = [torch.empty_like(h, device=dev) for h in hin]
+        dx, did, dw = zip(*[unpack_inputs(d, m) for d in din])
 
         def e2e_step():
             for l in range(nl):
-                dx[l].copy_(hx[l], non_blocking=True)
-                did[l].copy_(hid[l], non_blocking=True)
-                dw[l].copy_(hw[l], non_blocking=True)
+                din[l].copy_(hin[l], non_blocking=True)  # the layer's inputs: one copy
                 if block:  # the block routes itself: x in, its output out (ids and weights are copied all the same)
                     ops.moe_block(dx[l], layers[l]["gate"], layers[l]["prep"], layers[l]["shared"], TOPK,
                                   output=outs[l])
                 else:
                     ops.fused_moe(dx[l], layers[l]["prep"], dw[l], did[l], output=outs[l])
-                hout[l].copy_(outs[l], non_blocking=True)
+            hout.copy_(out_all, non_blocking=True)  # the step's results: every layer's output, one copy back
 
         eg = make_graph(e2e_step, 2)
         ems = over_ranks(timed(eg.replay, a.steps, barrier), world, dev)
         del eg
         res["e2e"] = {"value": round(amount / (ems / 1e3), 3), "unit": wl["unit"],
-                      "h2d_bytes_per_step": sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4
-                                                for x, r, w in zip(hx, hid, hw)),
-                      "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
-                      "api": ("ops.moe_block" if block else "ops.fused_moe") + " with host copies, one CUDA graph "
-                             "per step"}
+                      "h2d_bytes_per_step": sum(h.numel() for h in hin),
+                      "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(ems, 4),
+                      "api": ("ops.moe_block" if block else "ops.fused_moe") + " with host copies (one pinned "
+                             "staging copy of each layer's inputs in, every layer's output back in one copy at the "
+                             "step's end), one CUDA graph per step"}
         res["eager_ms_per_step"] = round(over_ranks(timed(step, max(2, a.steps // 4), barrier), world, dev), 4)
     del graph
     return res
@@ -706,24 +721,21 @@ def ep_main(a, rank, world, dev):
         res["gpu_launches_per_step"] = per_layer * len(layers)
         if name == names[0]:
             # e2e: inputs copied from pinned host memory and the outputs read back, every layer, every step
-            hx = [e["x"][name].cpu().pin_memory() for e in layers]
-            hid = [e["route"][name][0].cpu().pin_memory() for e in layers]
-            hw = [e["route"][name][1].cpu().pin_memory() for e in layers]
+            hin = [pack_inputs(e["x"][name], *e["route"][name]).cpu().pin_memory() for e in layers]
             hout = [torch.empty((m, H), dtype=torch.bfloat16).pin_memory() for _ in layers]
+            din = [torch.empty_like(h, device=dev) for h in hin]
 
             def e2e_step():
                 for l, e in enumerate(layers):
-                    dx = hx[l].to(dev, non_blocking=True)
-                    did = hid[l].to(dev, non_blocking=True)
-                    dw = hw[l].to(dev, non_blocking=True)
+                    din[l].copy_(hin[l], non_blocking=True)
+                    dx, did, dw = unpack_inputs(din[l], m)
                     o = ep.ep_moe(dx, e["layer"], dw, did, capacity=wl["capacity"], peer=px)
                     hout[l].copy_(o, non_blocking=True)
 
             e2e_step()
             ems = over_ranks(timed(e2e_step, a.steps, barrier), world, dev)
             res["e2e"] = {"value": round(amount / (ems / 1e3), 3), "unit": wl["unit"],
-                          "h2d_bytes_per_step": sum(x.numel() * 2 + r.numel() * 4 + w.numel() * 4
-                                                    for x, r, w in zip(hx, hid, hw)),
+                          "h2d_bytes_per_step": sum(h.numel() for h in hin),
                           "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
                           "api": "ep.ep_moe with host copies (per rank; value over all ranks)"}
         res["exchange"] = ("peer memory (CUDA IPC; " + (
