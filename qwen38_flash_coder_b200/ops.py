@@ -53,7 +53,7 @@ def check_device_errors(dev) -> None:
     code = int(w[0].item())
     if code:
         w.zero_()  # an aborted launch may also have left split counters behind
-        for key, t in _BUF.items():  # and the whole-layer kernel's counters and ready stamps
+        for key, t in _BUF.items():  # and the whole-layer kernel's counters and record flags
             if key[0] == "layer_state" and key[1] == torch.device(dev):
                 t.zero_()
         names = {1: "a bounded wait timed out", 2: "an expert id out of range", 3: "a block with more rows than "
@@ -252,9 +252,9 @@ def _decode_path(m: int, top_k: int) -> bool:
 
 
 def _layer_splits(hidden: int, inter: int):
-    """k-splits of the whole-layer kernel's gate_up (K = hidden) and down (K = inter) units: 2 and 1 where they cut
-    K into whole 128-k runs (measured best at M = 8 and 32 on B200: every further split costs a partial round trip
-    and an arrival; MOEK_B200_LAYER_SPLITS="g,d" overrides)."""
+    """The (gate_up, down) k-split arguments passed to the whole-layer kernel: 2 and 1 where they cut K into whole
+    128-k runs (MOEK_B200_LAYER_SPLITS="g,d" overrides). The kernel checks them and otherwise plans its own split
+    (stream-K ranges over the CTAs), so they do not change the results."""
     env = os.environ.get("MOEK_B200_LAYER_SPLITS")
     if env:
         g, d = (int(v) for v in env.split(","))
@@ -264,7 +264,7 @@ def _layer_splits(hidden: int, inter: int):
 
 
 def _layer_state(dev, E: int, hidden: int, inter: int) -> torch.Tensor:
-    """Persistent zero-initialised int32 state of the whole-layer kernel (counters and ready stamps) for one layer
+    """Persistent zero-initialised int32 state of the whole-layer kernel (counters and record flags) for one layer
     geometry on one device; calls in one stream share it (concurrent calls on other streams would race)."""
     import ctypes
 
@@ -280,9 +280,9 @@ _ROWS_SET = False
 
 
 def _layer_rows_knob():
-    """MOEK_B200_LAYER_ROWS (8, 16 or 32): rows per block of the whole-layer kernel instead of the automatic
-    choice (moek_set_layer_block_rows); MOEK_B200_LAYER_TAIL=0: no finer k-split for the items past the last whole
-    wave of units (moek_set_layer_tail_split); MOEK_B200_LAYER_COOP=0: a plain launch instead of a cooperative one
+    """MOEK_B200_LAYER_ROWS (8, 16 or 32): rows per block of the whole-layer kernel instead of the automatic 8
+    (moek_set_layer_block_rows); MOEK_B200_LAYER_TAIL: accepted for the earlier plan, no effect
+    (moek_set_layer_tail_split); MOEK_B200_LAYER_COOP=0: a plain launch instead of a cooperative one
     (moek_set_layer_cooperative). Read once."""
     global _ROWS_SET
     if not _ROWS_SET:
