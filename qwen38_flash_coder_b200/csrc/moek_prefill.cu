@@ -83,8 +83,8 @@ constexpr int TBL_BYTES = ITEM_COLS * 4;  // one scale word (4 k-groups) per row
 constexpr int W_SLOT = STAGE_BYTES + PAIR_BYTES + TBL_BYTES;
 constexpr int W_OFF = B_OFF + NB * B_BYTES;
 constexpr int S_REL = STAGE_BYTES, TBL_REL = STAGE_BYTES + PAIR_BYTES;
-constexpr int LUT_OFF = W_OFF + NW * W_SLOT;                     // 2 x 256 (B | R) words (units alternate)
-constexpr int IDS_OFF = LUT_OFF + 2 * 256 * 4;                   // 128 activation rows per loader warp
+constexpr int LUT_OFF = W_OFF + NW * W_SLOT;  // 2 x 256 {B B, R R} word pairs (units alternate; no per-use prmt)
+constexpr int IDS_OFF = LUT_OFF + 2 * 256 * 8;                   // 128 activation rows per loader warp
 constexpr int MISC_OFF = IDS_OFF + NLOAD * BMP * 4;              // tmem base, abort flag
 constexpr int BAR_OFF = (MISC_OFF + 16 + 7) / 8 * 8;
 constexpr int NBARS = 3 * NW + 2 * NB + 2 * NA + 2 + 2;
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   B.accfull = B.aempty + NA;
   B.accempty = B.accfull + 1;
   B.lutempty = B.accempty + 1;
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + LUT_OFF);
+  uint2* lut = reinterpret_cast<uint2*>(smem + LUT_OFF);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + MISC_OFF + 4);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -458,7 +458,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the (B | R) table of this expert, once the dequant warps finished the unit that used this buffer last
       if (un >= 2 && !wait_warp(B.lutempty + lb, ((un >> 1) - 1) & 1, deadline, p.err, abort_flag)) break;
 #pragma unroll
-      for (int j = 0; j < 8; j++) lut[lb * 256 + lane + 32 * j] = scale_word(lane + 32 * j, gsc);
+      for (int j = 0; j < 8; j++) {
+        const ScaleBR br = scale_br(lane + 32 * j, gsc);
+        lut[lb * 256 + lane + 32 * j] = make_uint2(br.b2, br.r2);
+      }
       __syncwarp();
       bool ok = true;
       for (int st = 0; st < nstage; st++, g++) {
@@ -522,7 +525,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (dw == 0 && lane == 0) report(p.err, MOEK_DEV_BAD_EXPERT);
         continue;
       }
-      const uint32_t* lt = lut + (un & 1) * 256;
+      const uint2* lt = lut + (un & 1) * 256;
       for (int st = 0; st < nstage; st++, g++) {
         if ((int)(g & 1) != grp) continue;  // the other group's stage
         const int s = g % NW, a = g % NA;
@@ -541,8 +544,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t v[32];
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
-            const uint32_t lw = lt[(sc >> (8 * kk)) & 0xFF];
-            const ScaleBR sbr{prmt_b(lw, 0x1010), prmt_b(lw, 0x3232)};
+            const uint2 lw = lt[(sc >> (8 * kk)) & 0xFF];
+            const ScaleBR sbr{lw.x, lw.y};
             dequant_word(words[2 * kk], sbr, v + 8 * kk);
             dequant_word(words[2 * kk + 1], sbr, v + 8 * kk + 4);
           }
