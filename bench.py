@@ -59,7 +59,7 @@ TRAFFIC = {
                             "bench.py --only --workload decode8 --layers 4"),
     "decode32": (141_612_800, "ncu capture of one moek_layer_kernel<8> launch (stream-K plan, 8-row blocks), "
                               "bench.py --only --workload decode32 --layers 4"),
-    "prefill": (696_165_888, "ncu capture of one moek_prefill_kernel gate_up launch, "
+    "prefill": (695_998_464, "ncu capture of one moek_prefill_kernel gate_up launch, "
                              "bench.py --only --workload prefill --layers 2"),
 }
 
