@@ -409,15 +409,34 @@ def measure(name, layers, a, dev, world, barrier, headline):
     if headline:
         # e2e: the public API with each step's inputs copied from pinned host memory and its outputs read back
         # one pinned staging buffer per layer holding x | ids | weights, so that a layer's inputs cross to the GPU in
-        # one copy (and its output back in one): x (16-byte aligned) at 0, then the int32 ids and the fp32 weights
-        hin = [pack_inputs(L["x"][name], *L["route"][name]).cpu().pin_memory() for L in layers]
+        # one copy (and its output back in one): x (16-byte aligned) at 0, then the int32 ids and the fp32 weights.
+        # The step's staging buffers sit back to back in one pinned block, and a copy stream moves them in two
+        # copies: the first layer's inputs, then all the others, which cross while the first layer computes. Only
+        # the first two layers wait for a copy; the rest follow each other directly.
+        packed = [pack_inputs(L["x"][name], *L["route"][name]) for L in layers]
+        seg = (packed[0].numel() + 15) // 16 * 16
+        hall = torch.zeros((nl, seg), dtype=torch.uint8).pin_memory()
+        for l in range(nl):
+            hall[l, :packed[l].numel()].copy_(packed[l])
+        hin = [hall[l, :packed[l].numel()] for l in range(nl)]
         hout = torch.empty((nl, m, H), dtype=torch.bfloat16).pin_memory()
-        din = [torch.empty_like(h, device=dev) for h in hin]
+        dall = torch.empty_like(hall, device=dev)
+        din = [dall[l, :packed[l].numel()] for l in range(nl)]
         dx, did, dw = zip(*[unpack_inputs(d, m) for d in din])
+        copy_stream = torch.cuda.Stream(dev)
+        copied = [torch.cuda.Event() for _ in range(2)]
 
         def e2e_step():
+            cur = torch.cuda.current_stream(dev)
+            copy_stream.wait_stream(cur)  # this step's copies start after the previous step's layers read them
+            with torch.cuda.stream(copy_stream):
+                dall[:1].copy_(hall[:1], non_blocking=True)  # the first layer's inputs
+                copied[0].record(copy_stream)
+                dall[1:].copy_(hall[1:], non_blocking=True)  # every other layer's, in one copy
+                copied[1].record(copy_stream)
             for l in range(nl):
-                din[l].copy_(hin[l], non_blocking=True)  # the layer's inputs: one copy
+                if l < 2:
+                    cur.wait_event(copied[l])
                 if block:  # the block routes itself: x in, its output out (ids and weights are copied all the same)
                     ops.moe_block(dx[l], layers[l]["gate"], layers[l]["prep"], layers[l]["shared"], TOPK,
                                   output=outs[l])
@@ -425,15 +444,19 @@ def measure(name, layers, a, dev, world, barrier, headline):
                     ops.fused_moe(dx[l], layers[l]["prep"], dw[l], did[l], output=outs[l])
             hout.copy_(out_all, non_blocking=True)  # the step's results: every layer's output, one copy back
 
+        device_out = out_all.clone()  # the device-resident step's results, to check the copied path against
         eg = make_graph(e2e_step, 2)
         ems = over_ranks(timed(eg.replay, a.steps, barrier), world, dev)
         del eg
+        torch.cuda.synchronize()
         res["e2e"] = {"value": round(amount / (ems / 1e3), 3), "unit": wl["unit"],
-                      "h2d_bytes_per_step": sum(h.numel() for h in hin),
+                      "h2d_bytes_per_step": hall.numel(),
                       "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(ems, 4),
-                      "api": ("ops.moe_block" if block else "ops.fused_moe") + " with host copies (one pinned "
-                             "staging copy of each layer's inputs in, every layer's output back in one copy at the "
-                             "step's end), one CUDA graph per step"}
+                      "api": ("ops.moe_block" if block else "ops.fused_moe") + " with host copies (the step's "
+                             "pinned staging buffers in two copies on a copy stream, the first layer's inputs, then "
+                             "the other layers' while the first computes; every layer's output back in one copy at "
+                             "the step's end), one CUDA graph per step",
+                      "output_equals_device_step": bool(torch.equal(hout, device_out.cpu()))}
         res["eager_ms_per_step"] = round(over_ranks(timed(step, max(2, a.steps // 4), barrier), world, dev), 4)
     del graph
     return res
@@ -721,13 +744,30 @@ def ep_main(a, rank, world, dev):
         res["gpu_launches_per_step"] = per_layer * len(layers)
         if name == names[0]:
             # e2e: inputs copied from pinned host memory and the outputs read back, every layer, every step
-            hin = [pack_inputs(e["x"][name], *e["route"][name]).cpu().pin_memory() for e in layers]
+            # the step's inputs as on one GPU: one pinned block, copied in two on a copy stream (the first layer's,
+            # then the others' while the first computes)
+            packed = [pack_inputs(e["x"][name], *e["route"][name]) for e in layers]
+            seg = (packed[0].numel() + 15) // 16 * 16
+            hall = torch.zeros((len(layers), seg), dtype=torch.uint8).pin_memory()
+            for l, t in enumerate(packed):
+                hall[l, :t.numel()].copy_(t)
             hout = [torch.empty((m, H), dtype=torch.bfloat16).pin_memory() for _ in layers]
-            din = [torch.empty_like(h, device=dev) for h in hin]
+            dall = torch.empty_like(hall, device=dev)
+            din = [dall[l, :t.numel()] for l, t in enumerate(packed)]
+            copy_stream = torch.cuda.Stream(dev)
+            copied = [torch.cuda.Event() for _ in range(2)]
 
             def e2e_step():
+                cur = torch.cuda.current_stream(dev)
+                copy_stream.wait_stream(cur)
+                with torch.cuda.stream(copy_stream):
+                    dall[:1].copy_(hall[:1], non_blocking=True)
+                    copied[0].record(copy_stream)
+                    dall[1:].copy_(hall[1:], non_blocking=True)
+                    copied[1].record(copy_stream)
                 for l, e in enumerate(layers):
-                    din[l].copy_(hin[l], non_blocking=True)
+                    if l < 2:
+                        cur.wait_event(copied[l])
                     dx, did, dw = unpack_inputs(din[l], m)
                     o = ep.ep_moe(dx, e["layer"], dw, did, capacity=wl["capacity"], peer=px)
                     hout[l].copy_(o, non_blocking=True)
@@ -735,9 +775,10 @@ def ep_main(a, rank, world, dev):
             e2e_step()
             ems = over_ranks(timed(e2e_step, a.steps, barrier), world, dev)
             res["e2e"] = {"value": round(amount / (ems / 1e3), 3), "unit": wl["unit"],
-                          "h2d_bytes_per_step": sum(h.numel() for h in hin),
+                          "h2d_bytes_per_step": hall.numel(),
                           "d2h_bytes_per_step": sum(o.numel() * 2 for o in hout), "ms_per_step": round(ems, 4),
-                          "api": "ep.ep_moe with host copies (per rank; value over all ranks)"}
+                          "api": "ep.ep_moe with host copies (per rank: the inputs in two copies on a copy stream, "
+                                 "each layer's output back after it; value over all ranks)"}
         res["exchange"] = ("peer memory (CUDA IPC; " + (
             "one whole-layer launch: dispatch, layer, partials over NVLink, unpack)" if one_launch else
             "dispatch, whole-layer kernel returning the partials, unpack)" if fused else "dispatch / combine kernels)")
