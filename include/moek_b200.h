@@ -151,6 +151,15 @@ int moek_split_epilogue(const float* part, int32_t nsplit, int32_t num_ids, int3
  * 284-289): out bf16 [m, N] = bf16(sum_j rows[t*top_k + j]) in fp32, slot order. rows: fp32 if rows_fp32 else bf16. */
 int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_t m, int32_t N, int32_t top_k, void* stream);
 
+/* Top-k combine over the routed slots: the same sum for routings that leave slots unrouted (an expert map marks the
+ * experts it does not hold with -1, vllm/.../fused_moe/moe_align_block_size.py:11-103, and moe_align skips them; the
+ * oracle leaves such slots out, bench/moek/problem.py:51-67). out bf16 [m, N] = bf16(sum_j rows[t*top_k + j]) over
+ * the slots j whose topk_ids[t*top_k + j] lies in [0, E), in slot order, in fp32; a token with no such slot gets a
+ * zero row. The rows of unrouted slots may hold any value (the down GEMM never writes them); with every slot routed
+ * the result equals moek_combine's bit for bit. rows fp32 [m * top_k, N]. */
+int moek_combine_routed(const float* rows, const int32_t* topk_ids, int32_t E, void* out, int32_t m, int32_t N,
+                        int32_t top_k, void* stream);
+
 /* ---- Router. Replaces vLLM's fused_topk with scoring "softmax" (vllm/.../router/fused_topk_router.py:69-108, the
  * topk_softmax op), the gating step in front of the layer (vllm/.../models/qwen3_next.py:158-165): per token t,
  * p = softmax(logits[t]) in fp32, the top_k largest p (the lowest expert index among equal p, largest first) into

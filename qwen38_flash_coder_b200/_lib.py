@@ -23,6 +23,7 @@ SIGNATURES = {
                                  _P, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _I32, _I32, _I32, _P, _I32, _P]),
     "moek_split_epilogue": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _I32, _P]),
     "moek_combine": (ctypes.c_int, [_P, _I32, _P, _I32, _I32, _I32, _P]),
+    "moek_combine_routed": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _I32, _I32, _P]),
     "moek_router_topk": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "moek_router_gate": (ctypes.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
     "moek_prep_workspace_bytes": (ctypes.c_int, [_I32, _I32, _I32, ctypes.POINTER(ctypes.c_size_t)]),

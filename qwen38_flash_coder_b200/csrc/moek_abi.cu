@@ -836,6 +836,16 @@ MOEK_API int moek_combine(const void* rows, int32_t rows_fp32, void* out, int32_
                      "combine");
 }
 
+MOEK_API int moek_combine_routed(const float* rows, const int32_t* topk_ids, int32_t E, void* out, int32_t m,
+                                 int32_t N, int32_t top_k, void* stream) {
+  if (m == 0) return MOEK_OK;
+  if (!rows || !topk_ids || !out || m < 0 || N <= 0 || top_k <= 0 || E <= 0)
+    return fail(MOEK_ERR_ARG, "moek_b200: routed combine bad arguments");
+  return cuda_status(moek::launch_combine_routed(rows, topk_ids, E, m, N, top_k, static_cast<__nv_bfloat16*>(out),
+                                                 (cudaStream_t)stream),
+                     "routed combine");
+}
+
 // ------------------------------------------------------------------------------------------- expert parallel
 static int ep_world_ok(int32_t E, int32_t world) {
   if (world < 1 || world > moek::EP_MAX_WORLD)

@@ -616,6 +616,58 @@ __global__ void __launch_bounds__(256) moek_combine_f32x4_kernel(const float4* _
   }
 }
 
+// The top-k sum over the routed slots only: a slot whose expert id lies outside [0, E) was not computed (its row
+// holds whatever the buffer held) and is left out, so a token with no routed slot gets a zero row. Every slot's row is
+// loaded (all rows lie inside the buffer) and the ids only choose which ones are added, so the row loads do not wait
+// for the id loads; with every slot routed the additions are the plain combine's, bit for bit.
+__global__ void __launch_bounds__(256) moek_combine_routed_f32x4_kernel(const float4* __restrict__ rows,
+                                                                        const int32_t* __restrict__ ids, int E, int m,
+                                                                        int N4, int top_k, uint2* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t n = (int64_t)m * N4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / N4;
+    const int64_t c = i - t * N4;
+    const float4* r = rows + t * top_k * N4 + c;
+    const int32_t* tid = ids + t * top_k;
+    float4 v[8];
+    int e[8];
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j0 = 0; j0 < top_k; j0 += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (j0 + j < top_k) {
+          e[j] = __ldg(tid + j0 + j);
+          v[j] = __ldcs(r + (int64_t)(j0 + j) * N4);  // read once: do not keep in L2
+        }
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (j0 + j < top_k && e[j] >= 0 && e[j] < E) o.x += v[j].x, o.y += v[j].y, o.z += v[j].z, o.w += v[j].w;
+    }
+    const __nv_bfloat162 a = __floats2bfloat162_rn(o.x, o.y), b = __floats2bfloat162_rn(o.z, o.w);
+    out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  }
+}
+
+// The same, one column per thread (any N or alignment).
+__global__ void moek_combine_routed_f32_kernel(const float* __restrict__ rows, const int32_t* __restrict__ ids, int E,
+                                               int m, int N, int top_k, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)m * N) return;
+  const int64_t t = i / N;
+  const int n = (int)(i - t * N);
+  float o = 0.f;
+  for (int j = 0; j < top_k; j++) {
+    const int e = ids[t * top_k + j];
+    const float v = rows[(t * top_k + j) * N + n];
+    if (e >= 0 && e < E) o += v;
+  }
+  out[i] = __float2bfloat16_rn(o);
+}
+
 // top-k combine of bf16 rows (the reference's torch.sum over dim 1: fp32 accumulation, one rounding)
 __global__ void moek_combine_bf16_kernel(const __nv_bfloat16* __restrict__ rows, int m, int N, int top_k,
                                          __nv_bfloat16* __restrict__ out) {
@@ -691,6 +743,21 @@ cudaError_t launch_combine_f32(const float* rows, int m, int N, int top_k, __nv_
     return cudaGetLastError();
   }
   moek_combine_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, m, N, top_k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_routed(const float* rows, const int32_t* ids, int E, int m, int N, int top_k,
+                                  __nv_bfloat16* out, cudaStream_t st) {
+  const int64_t n = (int64_t)m * N;
+  if (n == 0) return cudaSuccess;
+  if (N % 4 == 0 && ((reinterpret_cast<uintptr_t>(rows) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+    const int64_t n4 = n / 4;
+    const unsigned grid = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+    moek_combine_routed_f32x4_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float4*>(rows), ids, E, m, N / 4,
+                                                           top_k, reinterpret_cast<uint2*>(out));
+    return cudaGetLastError();
+  }
+  moek_combine_routed_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, ids, E, m, N, top_k, out);
   return cudaGetLastError();
 }
 

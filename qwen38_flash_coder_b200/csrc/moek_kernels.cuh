@@ -233,6 +233,9 @@ cudaError_t launch_down_combine(const float* part, int nsplit, int num_ids, int 
 cudaError_t launch_down_rows(const float* part, int nsplit, int num_ids, int N, const float* topk_w, float* dout,
                              cudaStream_t st);
 cudaError_t launch_combine_f32(const float* rows, int m, int N, int top_k, __nv_bfloat16* out, cudaStream_t st);
+// the top-k sum over the slots whose id lies in [0, E) (unrouted slots left out; none routed: a zero row)
+cudaError_t launch_combine_routed(const float* rows, const int32_t* ids, int E, int m, int N, int top_k,
+                                  __nv_bfloat16* out, cudaStream_t st);
 cudaError_t launch_combine_bf16(const __nv_bfloat16* rows, int m, int N, int top_k, __nv_bfloat16* out,
                                 cudaStream_t st);
 

@@ -441,7 +441,8 @@ def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
         return output if rows_k is None else out_rows
     act = torch.empty((num_ids, a.N // 2), dtype=torch.bfloat16, device=dev)
     if m <= DECODE_MAX_M:
-        # split-k GEMM launches (moek_gemm mode 2) and their two epilogue kernels (MOEK_B200_DECODE_PATH=split)
+        # split-k GEMM launches (moek_gemm mode 2) and their two epilogue kernels (MOEK_B200_DECODE_PATH=split); like
+        # the kit's own split epilogue, this path adds every slot's partials, so it expects every id in [0, E)
         sid, eid, npad = moe_align_block_size(ids32, BM, layer.E)
         # split-k with fp32 partials (no cross-CTA synchronisation in the GEMMs), finished by two small
         # deterministic epilogue kernels: SwiGLU -> act, and router weight + top-k sum -> output
@@ -463,7 +464,7 @@ def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
         call("moek_split_epilogue", _ptr(part), ns2, num_ids, b.N, 0, _ptr(tw), top_k, _ptr(dout), 1, st)
         return dout
     # prefill: tcgen05 GEMMs over moe_align blocks of <= 128 rows (the MMA's N), SwiGLU and router weight in their
-    # epilogues, the top-k sum of the fp32 rows in one more kernel
+    # epilogues, the top-k sum of the routed slots' fp32 rows in one more kernel
     sid, eid, npad = moe_align_block_size(ids32, BM_PREFILL, layer.E)
     part = _scratch("part", num_ids * b.N, torch.float32, dev) if rows_k is None else \
         torch.empty((num_ids, b.N), dtype=torch.float32, device=dev)
@@ -476,7 +477,8 @@ def _layer_call(x, layer, topk_weights, topk_ids, output, rows_k):
                                       top_k, mode=5, block_m=BM_PREFILL))
     if rows_k is not None:
         return part
-    call("moek_combine", _ptr(part), 1, _ptr(output), m, b.N, top_k, _stream(dev))
+    # the top-k sum over the routed slots: rows of slots outside [0, E) were never written (moe_align skips them)
+    call("moek_combine_routed", _ptr(part), _ptr(ids32), layer.E, _ptr(output), m, b.N, top_k, _stream(dev))
     return output
 
 

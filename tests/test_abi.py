@@ -46,6 +46,16 @@ def test_version_and_errors_without_gpu():
     assert rc == 1
 
 
+def test_routed_combine_rejects_bad_arguments():
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(256)  # never dereferenced: the argument checks fail first
+    assert lib.moek_combine_routed(fake, fake, 64, fake, 0, 2048, 5, None) == 0  # empty batch: nothing to do
+    assert lib.moek_combine_routed(fake, None, 64, fake, 4, 2048, 5, None) == 1
+    assert b"routed combine" in lib.moek_last_error()
+    assert lib.moek_combine_routed(fake, fake, 0, fake, 4, 2048, 5, None) == 1  # no experts
+    assert lib.moek_combine_routed(fake, fake, 64, fake, 4, 2048, 0, None) == 1  # top_k 0
+
+
 def test_align_workspace_query():
     lib = _lib.lib()
     b = ctypes.c_size_t(7)
