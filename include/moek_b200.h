@@ -110,14 +110,16 @@ int moek_align_noalloc(const int32_t* topk_ids, int64_t numel, int32_t num_exper
  *           2: split-k; the kernel writes fp32 partial sums part[nsplit][num_ids][N] (gate_up: gate at column c, up
  *           at N/2 + c) and moek_split_epilogue finishes (the reference's mode 2).
  *           3: the epilogue is fused. nsplit 1: gate_up writes act bf16 [num_ids, N/2] = bf16(silu(g) * u) to out;
- *           down writes fp32 rows topk_w[id] * sum to part [num_ids, N] (finish with moek_combine). nsplit > 1:
- *           the warp whose arrival completes a (block, item) (counters in cnt[1..]) adds the partials in split
+ *           down writes fp32 rows topk_w[id] * sum to part [num_ids, N] (finish with moek_combine, or with
+ *           moek_combine_routed when some slots are unrouted: their rows are not written). nsplit > 1: the warp
+ *           whose arrival completes a (block, item) (counters in cnt[1..]) adds the partials in split
  *           order; gate_up writes act to out; down writes fp32 rows topk_w * sum to part after the partials
  *           (part holds (nsplit + 1) * num_ids * N floats) and the arrival that completes a token's valid slots
  *           writes out bf16 [num_ids/combine_k, N] = their sum in slot order (slots whose topk_ids entry is outside
  *           [0, E) are left out).
  *           4: the tcgen05 path with fp32 rows: gate_up as mode 0; down writes the fp32 rows topk_w[id] * sum to
- *           part [num_ids, N] (finish with moek_combine), out unused.
+ *           part [num_ids, N] (finish with moek_combine_routed, which leaves out the unrouted slots' unwritten
+ *           rows), out unused.
  *           5: as 4, but act is kept in moe_align's sorted order: gate_up writes act row sorted position (out holds
  *           sorted_len rows) and down reads A by sorted position, one 128-row tile per stage instead of a gather.
  *           Modes 3-5 are this build's own; other values are rejected with MOEK_ERR_UNSUPPORTED.
