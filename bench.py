@@ -30,10 +30,10 @@ and ``ep.ep_moe`` moves them: decode M=8 per GPU (the headline, same metric as N
 fixed-capacity exchange over peer memory, prefill M=6912 Zipf per GPU with exact counts over NCCL, and one M=6912
 chunk split over the GPUs (strong scaling). Each EP workload also reports the load-balance ceiling of the contiguous
 expert split (mean over max of the routed rows each rank owns), and before any timing every rank checks its tokens'
-EP output against the one-GPU layer (``parity`` in the line; the run fails outside the gate). value = the bytes of the experts the
-step touched (each streamed once, by its owner) plus every rank's x / output / routing (or the FLOPs of all ranks'
-rows) over the slowest rank's time (CUDA events, max over ranks). The roofline is the local gate_up GEMM on the rows
-one step delivered.
+EP output against the one-GPU layer (``parity`` in the line; the run fails outside the gate). value = the bytes of the
+experts the step touched (each streamed once, by its owner) plus every rank's x / output / routing (or the FLOPs of
+all ranks' rows) over the slowest rank's time (CUDA events, max over ranks). The roofline is the local gate_up GEMM on
+the rows one step delivered.
 """
 import argparse
 import json

@@ -45,20 +45,20 @@ int moek_version(void);
  * No reference counterpart (the reference's trace flag is a compile-time switch of its kernel, files/mbx_moek.cu:
  * 152-160). */
 int moek_build_flags(void);
-/* MOEK_TRACE builds: copy the %globaltimer stamps [1024 CTAs][128 slots] (uint64, nanoseconds; 0 = not reached) of
- * the last launches of one kernel family to host memory dst (bytes <= 1 MiB are copied). kind 0: the whole-layer
- * kernel (0 start, 1 after the dependent-launch wait, 2 expert-parallel flags seen, 3 routing done, 4 first weight
- * copy issued, 5 consumers done, 6 end, 7 unit count, 47 every role done, 51 grid barrier passed, 52 top-k sums
- * written; per unit u < 8 of the CTA: 8 + 3u first stage ready, 9 + 3u last stage done, 10 + 3u finished (gate_up:
- * record published), 32 + u the unit (phase << 28 | block << 16 | item << 8 | first k-stage); the first unit's
- * stages s < 8 in SM clock cycles (clock64): 64 + s consumer warp 0 before its wait, 80 + s data and scales ready, 88 + s done, 96 + s the scale warp
+/* MOEK_TRACE builds: copy the %globaltimer stamps [1024 CTAs][128 slots] (uint64, nanoseconds; 0 = not reached) of the
+ * last launches of one kernel family to host memory dst (bytes <= 1 MiB are copied). kind 0: the whole-layer kernel (0
+ * start, 1 after the dependent-launch wait, 2 expert-parallel flags seen, 3 routing done, 4 first weight copy issued, 5
+ * consumers done, 6 end, 7 unit count, 47 every role done, 51 grid barrier passed, 52 top-k sums written; per unit u <
+ * 8 of the CTA: 8 + 3u first stage ready, 9 + 3u last stage done, 10 + 3u finished (gate_up: record published), 32 + u
+ * the unit (phase << 28 | block << 16 | item << 8 | first k-stage); the first unit's stages s < 8 in SM clock cycles
+ * (clock64): 64 + s consumer warp 0 before its wait, 80 + s data and scales ready, 88 + s done, 96 + s the scale warp
  * sees the weights, 104 + s it publishes the scales, 112 + s the producer issues the copy, 120 + s the act warp issues
  * its copies; the start-up in SM clock cycles: 39 start, 40 keys built, 41 counted, 42 ranked, 43 blocks cut, 44 plan
- * made, 45 published, 53 units counted, 54 the producer's units decoded, 55 their rows published); kind 1: the
- * tcgen05 GEMM (0 start,
- * 1 after the wait, 6 end; per unit: 8 + 3u first MMA, 9 + 3u last MMA issued, 10 + 3u accumulator drained);
- * kind 2: the peer-exchange kernels (dispatch: 0 start, 1 destination free, 2 rows written, 3 flag raised; unpack:
- * 8 start, 9 partials ready, 10 done). Other builds return MOEK_ERR_UNSUPPORTED. moek_trace_clear zeroes them. */
+ * made, 45 published, 53 units counted, 54 the producer's units decoded, 55 their rows published); kind 1: the tcgen05
+ * GEMM (0 start, 1 after the wait, 6 end; per unit: 8 + 3u first MMA, 9 + 3u last MMA issued, 10 + 3u accumulator
+ * drained); kind 2: the peer-exchange kernels (dispatch: 0 start, 1 destination free, 2 rows written, 3 flag raised;
+ * unpack: 8 start, 9 partials ready, 10 done). Other builds return MOEK_ERR_UNSUPPORTED. moek_trace_clear zeroes
+ * them. */
 int moek_trace_read(int32_t kind, void* dst, size_t bytes);
 int moek_trace_clear(void);
 

@@ -512,7 +512,8 @@ MOEK_API int moek_prep_scales(const uint8_t* scales, const float* gs, int32_t E,
 MOEK_API int moek_prep_exceptions(const uint8_t* scales, int32_t E, int32_t N, int32_t K, int32_t gate_up, float sf,
                                   const void* workspace, const int32_t* exc_off, int32_t* exc_ent, void* stream) {
   if (int rc = prep_shape(E, N, K, gate_up)) return rc;
-  if (!scales || !workspace || !exc_off || !exc_ent) return fail(MOEK_ERR_ARG, "moek_b200: prep_exceptions null pointer");
+  if (!scales || !workspace || !exc_off || !exc_ent)
+    return fail(MOEK_ERR_ARG, "moek_b200: prep_exceptions null pointer");
   return cuda_status(moek::launch_prep_exceptions(scales, E, N, K, gate_up ? 1 : 0, sf,
                                                   static_cast<const int*>(workspace), exc_off, exc_ent,
                                                   (cudaStream_t)stream),
@@ -850,7 +851,8 @@ MOEK_API int moek_combine_routed(const float* rows, const int32_t* topk_ids, int
 static int ep_world_ok(int32_t E, int32_t world) {
   if (world < 1 || world > moek::EP_MAX_WORLD)
     return fail(MOEK_ERR_ARG, "moek_b200: EP world size %d outside [1, %d]", world, moek::EP_MAX_WORLD);
-  if (E <= 0 || E % world) return fail(MOEK_ERR_ARG, "moek_b200: %d experts do not split evenly over %d ranks", E, world);
+  if (E <= 0 || E % world)
+    return fail(MOEK_ERR_ARG, "moek_b200: %d experts do not split evenly over %d ranks", E, world);
   return MOEK_OK;
 }
 
