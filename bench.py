@@ -418,7 +418,6 @@ def measure(name, layers, a, dev, world, barrier, headline):
         hall = torch.zeros((nl, seg), dtype=torch.uint8).pin_memory()
         for l in range(nl):
             hall[l, :packed[l].numel()].copy_(packed[l])
-        hin = [hall[l, :packed[l].numel()] for l in range(nl)]
         hout = torch.empty((nl, m, H), dtype=torch.bfloat16).pin_memory()
         dall = torch.empty_like(hall, device=dev)
         din = [dall[l, :packed[l].numel()] for l in range(nl)]
