@@ -391,7 +391,9 @@ def _sms(dev) -> int:
 
 def fused_moe(hidden_states: torch.Tensor, layer: PreparedLayer, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
               output: torch.Tensor = None) -> torch.Tensor:
-    """One routed-expert layer: out[t] = sum_j w[t, j] * down_e(silu(gate_e(x_t)) * up_e(x_t)), e = topk_ids[t, j]."""
+    """One routed-expert layer: out[t] = sum_j w[t, j] * down_e(silu(gate_e(x_t)) * up_e(x_t)), e = topk_ids[t, j].
+    Slots whose expert id lies outside [0, E) (an expert map's -1) are not routed and add nothing; a token with no
+    routed slot gets a zero row."""
     x = hidden_states
     _need_cuda(x, topk_ids, topk_weights)
     m, hid = x.shape
